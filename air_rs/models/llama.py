@@ -1,0 +1,181 @@
+"""Llama-family transformer on the sm_100a kernels (Llama / Mistral / Qwen2 shapes).
+
+Weights live in HBM in kernel-native formats (``QWeight``); Q/K/V rows are concatenated
+into one matrix and gate/up into another so each layer is five weight streams. The
+decode step (batch <= 8) is
+
+    norm+quant -> QKV GEMV (+RoPE, +paged KV write) -> paged attention (+quant)
+    -> O GEMV (+residual) -> norm+quant -> gate|up GEMV (+SwiGLU) -> quant
+    -> down GEMV (+residual)
+
+which replaces the reference's per-layer candle path (``src/model.rs:460-745``) and its
+host round trips of the KV cache (``src/kv_cache.rs:244-339``). Prefill and large-batch
+decode go through ``linear`` (tcgen05 GEMM) with token-parallel RoPE/KV, SwiGLU and
+residual kernels, and the same paged attention kernel.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Iterable
+
+import torch
+
+from .. import ops
+from ..gguf import GGMLType
+from ..gguf.quants import dequantize
+from .config import ModelConfig, FfnType
+
+
+@dataclass
+class LayerWeights:
+    attn_norm: torch.Tensor
+    wqkv: ops.QWeight
+    wo: ops.QWeight
+    ffn_norm: torch.Tensor
+    wgu: ops.QWeight | None          # [2F, H]: gate rows then up rows
+    wdown: ops.QWeight | None
+    # MoE
+    router: torch.Tensor | None = None      # [E, H] f32
+    experts_gu: list = field(default_factory=list)
+    experts_down: list = field(default_factory=list)
+
+    @property
+    def w_gate(self) -> ops.QWeight:
+        return self.wgu.rows(0, self.wgu.N // 2)
+
+    @property
+    def w_up(self) -> ops.QWeight:
+        return self.wgu.rows(self.wgu.N // 2, self.wgu.N)
+
+
+class LlamaWeights:
+    """Device-resident weights, built from (name, raw, qtype, shape) records."""
+
+    def __init__(self, cfg: ModelConfig, records: Iterable, device, tp_rank: int = 0, tp_size: int = 1):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        pending: dict[str, tuple] = {}
+        self.layers: list[LayerWeights | None] = [None] * cfg.n_layers
+        self.embd = self.out_norm = self.lm_head = None
+        for name, raw, qt, shape in records:
+            pending[name] = (raw, GGMLType(qt), tuple(shape))
+            self._try_build(pending)
+        if self.lm_head is None and "token_embd.weight" in pending:
+            self.lm_head = self._lin_full(*pending["token_embd.weight"])
+        self._try_build(pending, final=True)
+        missing = [i for i, l in enumerate(self.layers) if l is None]
+        if missing or self.embd is None or self.out_norm is None or self.lm_head is None:
+            raise ValueError(f"incomplete checkpoint: layers {missing[:4]}... or globals missing")
+
+    # -- helpers -------------------------------------------------------------
+    def _vec(self, raw, qt, shape):
+        return dequantize(raw.reshape(1, -1), qt).reshape(-1).float().to(self.device)
+
+    def _lin_full(self, raw, qt, shape):
+        return ops.QWeight.from_raw(raw, qt, shape[0], shape[1], self.device)
+
+    def _lin_rows(self, raw, qt, shape, r0, r1):
+        return ops.QWeight.from_raw(raw.reshape(shape[0], -1)[r0:r1], qt, r1 - r0, shape[1], self.device)
+
+    def _lin_cols(self, raw, qt, shape, c0, c1):
+        """Input-dim shard: whole quant blocks of each row (row-parallel TP)."""
+        from ..gguf import BLOCK_GEOMETRY
+        per, nb = BLOCK_GEOMETRY[qt]
+        if c0 % per or c1 % per:
+            raise ValueError(f"TP shard boundary {c0}:{c1} not aligned to {qt.name} block {per}")
+        r = raw.reshape(shape[0], -1)[:, c0 // per * nb: c1 // per * nb]
+        return ops.QWeight.from_raw(r.contiguous(), qt, shape[0], c1 - c0, self.device)
+
+    def _try_build(self, p: dict, final: bool = False):
+        cfg = self.cfg
+        if self.embd is None and "token_embd.weight" in p:
+            self.embd = self._lin_full(*p["token_embd.weight"])
+        if self.out_norm is None and "output_norm.weight" in p:
+            self.out_norm = self._vec(*p.pop("output_norm.weight"))
+        if self.lm_head is None and "output.weight" in p:
+            raw, qt, shape = p.pop("output.weight")
+            self.lm_head = self._shard_rows_tp(raw, qt, shape)
+        for i in range(cfg.n_layers):
+            if self.layers[i] is not None:
+                continue
+            pre = f"blk.{i}."
+            need = ["attn_norm.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight",
+                    "attn_output.weight", "ffn_norm.weight"]
+            if cfg.n_experts:
+                need += ["ffn_gate_inp.weight", "ffn_gate_exps.weight", "ffn_up_exps.weight",
+                         "ffn_down_exps.weight"]
+            else:
+                need += ["ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"]
+            if not all(pre + n in p for n in need):
+                continue
+            g = {n: p.pop(pre + n) for n in need}
+            self.layers[i] = self._build_layer(g)
+
+    def _shard_rows_tp(self, raw, qt, shape):
+        if self.tp_size == 1:
+            return self._lin_full(raw, qt, shape)
+        n = shape[0]
+        per = (n + self.tp_size - 1) // self.tp_size
+        r0, r1 = self.tp_rank * per, min(n, (self.tp_rank + 1) * per)
+        return self._lin_rows(raw, qt, shape, r0, r1)
+
+    def _build_layer(self, g) -> LayerWeights:
+        cfg, tp, rk = self.cfg, self.tp_size, self.tp_rank
+        hd = cfg.head_dim
+        nh_l, nkv_l = cfg.n_heads // tp, max(1, cfg.n_kv_heads // tp)
+        kv_rank = rk * nkv_l // max(1, nkv_l) if cfg.n_kv_heads >= tp else rk * cfg.n_kv_heads // tp
+        q = self._lin_rows(*g["attn_q.weight"], rk * nh_l * hd, (rk + 1) * nh_l * hd)
+        if cfg.n_kv_heads >= tp:
+            k0 = rk * nkv_l * hd
+        else:  # replicate KV heads across ranks that share them
+            k0 = (rk * cfg.n_kv_heads // tp) * hd
+        k = self._lin_rows(*g["attn_k.weight"], k0, k0 + nkv_l * hd)
+        v = self._lin_rows(*g["attn_v.weight"], k0, k0 + nkv_l * hd)
+        del kv_rank
+        wqkv = ops.QWeight.cat([q, k, v])
+        if tp == 1:
+            wo = self._lin_full(*g["attn_output.weight"])
+        else:
+            wo = self._lin_cols(*g["attn_output.weight"], rk * nh_l * hd, (rk + 1) * nh_l * hd)
+        lw = LayerWeights(self._vec(*g["attn_norm.weight"]), wqkv, wo, self._vec(*g["ffn_norm.weight"]),
+                          None, None)
+        F = cfg.intermediate_dim
+        Fl = F // tp
+        if cfg.n_experts:
+            lw.router = dequantize(g["ffn_gate_inp.weight"][0], g["ffn_gate_inp.weight"][1]).reshape(
+                cfg.n_experts, cfg.hidden_dim).float().to(self.device)
+            for name, dst in (("ffn_gate_exps.weight", None),):
+                pass
+            gr, gq, gs = g["ffn_gate_exps.weight"]
+            ur, uq, us = g["ffn_up_exps.weight"]
+            dr, dq, dsh = g["ffn_down_exps.weight"]
+            E = cfg.n_experts
+            gr = gr.reshape(E, F, -1)
+            ur = ur.reshape(E, F, -1)
+            dr = dr.reshape(E, cfg.hidden_dim, -1)
+            for e in range(E):
+                ge = ops.QWeight.from_raw(gr[e], gq, F, cfg.hidden_dim, self.device)
+                ue = ops.QWeight.from_raw(ur[e], uq, F, cfg.hidden_dim, self.device)
+                lw.experts_gu.append(ops.QWeight.cat([ge, ue]))
+                lw.experts_down.append(ops.QWeight.from_raw(dr[e], dq, cfg.hidden_dim, F, self.device))
+        else:
+            gate = self._lin_rows(*g["ffn_gate.weight"], rk * Fl, (rk + 1) * Fl)
+            up = self._lin_rows(*g["ffn_up.weight"], rk * Fl, (rk + 1) * Fl)
+            lw.wgu = ops.QWeight.cat([gate, up])
+            if tp == 1:
+                lw.wdown = self._lin_full(*g["ffn_down.weight"])
+            else:
+                lw.wdown = self._lin_cols(*g["ffn_down.weight"], rk * Fl, (rk + 1) * Fl)
+        return lw
+
+    def nbytes(self) -> int:
+        n = self.embd.nbytes + self.lm_head.nbytes
+        for l in self.layers:
+            n += l.wqkv.nbytes + l.wo.nbytes
+            if l.wgu is not None:
+                n += l.wgu.nbytes + l.wdown.nbytes
+            for e in l.experts_gu + l.experts_down:
+                n += e.nbytes
+        return n

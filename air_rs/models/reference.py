@@ -1,0 +1,256 @@
+"""CPU oracle forward that reproduces the reference's Candle-CPU numerics.
+
+Reference recipe (``src/inference_step.rs:442-514``, ``src/model.rs:460-745``,
+``src/ops.rs``): F16 residual stream and embeddings, RMSNorm computed in F32 and cast
+back to F16, projections run as quantised matmuls on F32 inputs (activations quantised
+to the weight's vec-dot type: Q8_0 for Q8_0 weights, Q8_K for K-quants, integer dot
+products, F32 result), F32 NeoX RoPE with ``inv_freq = 1/theta^(2i/d)``, F32 GQA
+attention with a causal mask only when more than one query, o_proj / FFN outputs cast to
+F16 before the residual add, final norm -> last position -> F32 LM head, repetition
+penalty 1.1 over all tokens (prompt and BOS included) then greedy at T=0.
+
+This is the token-exact oracle for the tiny-Llama CPU configuration and the numerics
+reference for every CUDA kernel test.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..gguf import GGMLType
+from ..gguf.quants import dequantize, unpack_k4_scales
+from .config import ModelConfig
+
+
+def _round_away(x: torch.Tensor) -> torch.Tensor:
+    return torch.sign(x) * torch.floor(x.abs() + 0.5)
+
+
+def quantize_act_q8_0(x: torch.Tensor):
+    """F32 [T, K] -> (int8 codes [T, nb, 32], f16-rounded scales [T, nb])."""
+    xb = x.float().reshape(x.shape[0], -1, 32)
+    amax = xb.abs().amax(-1)
+    d = amax / 127.0
+    inv = torch.where(d > 0, 1.0 / d, torch.zeros_like(d))
+    q = _round_away(xb * inv.unsqueeze(-1)).clamp(-127, 127)
+    return q, d.half().float()
+
+
+def quantize_act_q8_k(x: torch.Tensor):
+    """F32 [T, K] -> Q8_K codes [T, nb, 256] and f32 scales [T, nb] (signed-max rule)."""
+    xb = x.float().reshape(x.shape[0], -1, 256)
+    idx = xb.abs().argmax(-1, keepdim=True)
+    mx = torch.gather(xb, -1, idx).squeeze(-1)
+    iscale = torch.where(mx != 0, -127.0 / mx, torch.zeros_like(mx))
+    q = _round_away(xb * iscale.unsqueeze(-1)).clamp(max=127)
+    d = torch.where(iscale != 0, 1.0 / iscale, torch.zeros_like(iscale))
+    return q, d
+
+
+def qmatmul(x: torch.Tensor, raw: torch.Tensor, qtype: GGMLType, n_out: int) -> torch.Tensor:
+    """Quantised linear layer, F32 in / F32 out, reference vec-dot semantics."""
+    qtype = GGMLType(qtype)
+    T, K = x.shape
+    if qtype == GGMLType.Q8_0:
+        b = raw.reshape(n_out, K // 32, 34)
+        dw = b[..., 0:2].contiguous().view(torch.float16).squeeze(-1).float()
+        qw = b[..., 2:].contiguous().view(torch.int8).float()
+        qx, dx = quantize_act_q8_0(x)
+        sumi = torch.einsum("tbk,nbk->tnb", qx, qw)
+        return (sumi * dx.unsqueeze(1) * dw.unsqueeze(0)).sum(-1)
+    if qtype == GGMLType.Q4_K:
+        b = raw.reshape(n_out, K // 256, 144)
+        d = b[..., 0:2].contiguous().view(torch.float16).squeeze(-1).float()
+        dmin = b[..., 2:4].contiguous().view(torch.float16).squeeze(-1).float()
+        sc, mn = unpack_k4_scales(b[..., 4:16])
+        qs = b[..., 16:].reshape(n_out, K // 256, 4, 32).to(torch.int16)
+        qw = torch.stack([qs & 0xF, qs >> 4], -2).reshape(n_out, K // 256, 8, 32).float()
+        qx, dx = quantize_act_q8_k(x)
+        qx = qx.reshape(T, K // 256, 8, 32)
+        sumi = torch.einsum("tbsk,nbsk->tnbs", qx, qw)           # per sub-block integer dots
+        bsum = qx.sum(-1)                                         # [T, nb, 8]
+        main = (sumi * sc.float().unsqueeze(0)).sum(-1)           # [T, N, nb]
+        mins = torch.einsum("tbs,nbs->tnb", bsum, mn.float())
+        return (dx.unsqueeze(1) * (d.unsqueeze(0) * main - dmin.unsqueeze(0) * mins)).sum(-1)
+    w = dequantize(raw, qtype).reshape(n_out, K)
+    if qtype in (GGMLType.F16, GGMLType.BF16, GGMLType.F32):
+        return x.float() @ w.float().t()
+    return x.float() @ w.t()
+
+
+@dataclass
+class OracleLayer:
+    attn_norm: torch.Tensor
+    wq: tuple
+    wk: tuple
+    wv: tuple
+    wo: tuple
+    ffn_norm: torch.Tensor
+    w_gate: tuple
+    w_up: tuple
+    w_down: tuple
+
+
+class OracleModel:
+    """Reference-numerics Llama-family forward on CPU over GGUF raw tensors."""
+
+    def __init__(self, cfg: ModelConfig, tensors: dict[str, tuple[torch.Tensor, GGMLType, tuple]]):
+        self.cfg = cfg
+        self.t = tensors
+
+        def lin(name):
+            raw, qt, shape = tensors[name]
+            return (raw, qt, shape[0])
+
+        def vec(name):
+            raw, qt, shape = tensors[name]
+            return dequantize(raw.reshape(1, -1), qt).reshape(-1).half()
+
+        self.embd = dequantize(tensors["token_embd.weight"][0], tensors["token_embd.weight"][1]).half()
+        self.layers = []
+        for i in range(cfg.n_layers):
+            p = f"blk.{i}."
+            self.layers.append(OracleLayer(
+                vec(p + "attn_norm.weight"), lin(p + "attn_q.weight"), lin(p + "attn_k.weight"),
+                lin(p + "attn_v.weight"), lin(p + "attn_output.weight"), vec(p + "ffn_norm.weight"),
+                lin(p + "ffn_gate.weight"), lin(p + "ffn_up.weight"), lin(p + "ffn_down.weight")))
+        self.out_norm = vec("output_norm.weight")
+        self.lm_head = lin("output.weight" if "output.weight" in tensors else "token_embd.weight")
+        hd = cfg.head_dim
+        self.inv_freq = 1.0 / torch.pow(torch.tensor(float(cfg.rope_theta)),
+                                        torch.arange(0, hd, 2, dtype=torch.float32) / hd)
+        self.k_cache: list[torch.Tensor | None] = [None] * cfg.n_layers
+        self.v_cache: list[torch.Tensor | None] = [None] * cfg.n_layers
+
+    @classmethod
+    def from_gguf(cls, g) -> "OracleModel":
+        cfg = ModelConfig.from_gguf_metadata(g.metadata)
+        tensors = {n: (g.raw(n), t.qtype, t.torch_shape) for n, t in g.tensors.items()}
+        return cls(cfg, tensors)
+
+    def reset(self):
+        self.k_cache = [None] * self.cfg.n_layers
+        self.v_cache = [None] * self.cfg.n_layers
+
+    def truncate(self, n: int):
+        for i in range(self.cfg.n_layers):
+            if self.k_cache[i] is not None:
+                self.k_cache[i] = self.k_cache[i][:, :n]
+                self.v_cache[i] = self.v_cache[i][:, :n]
+
+    @staticmethod
+    def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+        xf = x.float()
+        y = xf / torch.sqrt((xf * xf).mean(-1, keepdim=True) + eps)
+        return (y * w.float()).to(x.dtype)
+
+    def rope(self, x: torch.Tensor, start: int) -> torch.Tensor:
+        # x [S, H, D] f32, NeoX half split
+        S = x.shape[0]
+        pos = torch.arange(start, start + S, dtype=torch.float32)
+        ang = pos[:, None] * self.inv_freq[None, :]
+        c, s = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+        h = x.shape[-1] // 2
+        x1, x2 = x[..., :h], x[..., h:]
+        return torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], -1)
+
+    def forward(self, ids: list[int], start_pos: int) -> torch.Tensor:
+        """Runs ``ids`` at positions start_pos.. ; returns F32 logits of the last position."""
+        cfg = self.cfg
+        x = self.embd[torch.tensor(ids)]  # [S, H] f16
+        S = x.shape[0]
+        nh, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        for li, L in enumerate(self.layers):
+            h = self.rms_norm(x, L.attn_norm, cfg.rms_norm_eps).float()
+            q = qmatmul(h, L.wq[0], L.wq[1], L.wq[2]).reshape(S, nh, hd)
+            k = qmatmul(h, L.wk[0], L.wk[1], L.wk[2]).reshape(S, nkv, hd)
+            v = qmatmul(h, L.wv[0], L.wv[1], L.wv[2]).reshape(S, nkv, hd)
+            q = self.rope(q, start_pos)
+            k = self.rope(k, start_pos)
+            if self.k_cache[li] is not None:
+                k = torch.cat([self.k_cache[li][0], k], 0)
+                v = torch.cat([self.v_cache[li][0], v], 0)
+            self.k_cache[li] = k.unsqueeze(0)
+            self.v_cache[li] = v.unsqueeze(0)
+            attn = attention_reference(q, k, v, causal=S > 1)
+            o = qmatmul(attn.reshape(S, nh * hd), L.wo[0], L.wo[1], L.wo[2]).to(x.dtype)
+            x = x + o
+            h = self.rms_norm(x, L.ffn_norm, cfg.rms_norm_eps).float()
+            g = qmatmul(h, L.w_gate[0], L.w_gate[1], L.w_gate[2])
+            u = qmatmul(h, L.w_up[0], L.w_up[1], L.w_up[2])
+            a = g / (1.0 + torch.exp(-g)) * u
+            dn = qmatmul(a, L.w_down[0], L.w_down[1], L.w_down[2]).to(x.dtype)
+            x = x + dn
+        x = self.rms_norm(x, self.out_norm, cfg.rms_norm_eps)
+        last = x[-1:].float()
+        return qmatmul(last, self.lm_head[0], self.lm_head[1], self.lm_head[2])[0]
+
+
+def attention_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool,
+                        mask: torch.Tensor | None = None, window: int = 0) -> torch.Tensor:
+    """Dense GQA attention, F32. q [S, H, D], k/v [Skv, Hkv, D] -> [S, H, D].
+
+    Causal rule (``src/ops.rs:762-788``): key j visible to query i iff j <= i + (Skv - S).
+    ``mask`` (optional, [S, Skv] bool) further restricts visibility (tree attention).
+    """
+    S, H, D = q.shape
+    Skv, Hkv, _ = k.shape
+    rep = H // Hkv
+    kk = k.float().repeat_interleave(rep, dim=1)
+    vv = v.float().repeat_interleave(rep, dim=1)
+    s = torch.einsum("shd,thd->hst", q.float(), kk) * (1.0 / math.sqrt(D))
+    vis = torch.ones(S, Skv, dtype=torch.bool)
+    if causal:
+        i = torch.arange(S)[:, None]
+        j = torch.arange(Skv)[None, :]
+        vis = j <= i + (Skv - S)
+        if window > 0:
+            vis = vis & (j > i + (Skv - S) - window)
+    if mask is not None:
+        vis = vis & mask
+    s = s.masked_fill(~vis[None], float("-inf"))
+    p = torch.softmax(s, -1)
+    p = torch.nan_to_num(p, nan=0.0)
+    return torch.einsum("hst,thd->shd", p, vv)
+
+
+def apply_repetition_penalty(logits: torch.Tensor, past: list[int], penalty: float) -> torch.Tensor:
+    """Per occurrence: divide positive logits, multiply negative ones (src/sampler.rs:272-292)."""
+    if penalty == 1.0:
+        return logits
+    out = logits.clone()
+    for t in past:
+        if 0 <= t < out.numel():
+            out[t] = out[t] / penalty if out[t] > 0 else out[t] * penalty
+    return out
+
+
+def greedy_generate(model: OracleModel, prompt_ids: list[int], n_tokens: int, bos_id: int | None,
+                    repetition_penalty: float = 1.1, prefill_chunk: int = 512,
+                    eos_id: int | None = None) -> list[int]:
+    """Reference generate loop (src/inference_step.rs:19-184) at temperature 0."""
+    model.reset()
+    toks = ([bos_id] if bos_id is not None else []) + list(prompt_ids)
+    out: list[int] = []
+    pos = 0
+    # chunked prefill of full 512 chunks, then the remainder (src/inference_step.rs:398-463)
+    if len(toks) > prefill_chunk:
+        n_full = len(toks) // prefill_chunk * prefill_chunk
+        for c in range(0, n_full, prefill_chunk):
+            model.forward(toks[c:c + prefill_chunk], c)
+        pos = n_full
+        if pos == len(toks):
+            model.truncate(pos - 1)
+            pos -= 1
+    logits = model.forward(toks[pos:], pos)
+    while True:
+        lg = apply_repetition_penalty(logits, toks, repetition_penalty)
+        nxt = int(torch.argmax(lg))
+        out.append(nxt)
+        toks.append(nxt)
+        if len(out) >= n_tokens or (eos_id is not None and nxt == eos_id):
+            break
+        logits = model.forward([nxt], len(toks) - 1)
+    return out

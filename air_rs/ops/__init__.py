@@ -1,0 +1,217 @@
+"""Python entry points of the sm_100a kernels (extension module ``air_rs._C``).
+
+Every op here requires CUDA tensors and the compiled extension; there is no silent
+fallback. ``require_ext()`` raises with the build command if the ``.so`` is missing.
+"""
+from __future__ import annotations
+
+import importlib
+import os
+from dataclasses import dataclass
+
+import torch
+
+from ..gguf import GGMLType
+from ..gguf.quants import dequantize
+
+_EXT = None
+_EXT_ERR: Exception | None = None
+
+FMT_Q4K, FMT_Q8_0, FMT_BF16 = 0, 1, 2
+
+# Number of our kernels launched (eager launches + kernels inside replayed CUDA graphs).
+_LAUNCHES = [0]
+
+
+def count_launch(n: int = 1):
+    _LAUNCHES[0] += n
+
+
+def launch_count() -> int:
+    return _LAUNCHES[0]
+
+
+def reset_launch_count():
+    _LAUNCHES[0] = 0
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_QKV_ROPE = 0, 1, 2, 3
+
+
+def pad32(k: int) -> int:
+    return (k + 31) // 32 * 32
+
+
+def require_ext():
+    global _EXT, _EXT_ERR
+    if _EXT is not None:
+        return _EXT
+    try:
+        _EXT = importlib.import_module("air_rs._C")
+    except Exception as e:  # pragma: no cover - depends on build state
+        _EXT_ERR = e
+        raise RuntimeError(
+            "air_rs CUDA extension is not built (air_rs/_C*.so missing or unloadable): "
+            f"{e}. Build it with `python setup.py build_ext --inplace`.") from e
+    return _EXT
+
+
+def ext_available() -> bool:
+    try:
+        require_ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+def ext_path() -> str | None:
+    try:
+        return os.path.abspath(require_ext().__file__)
+    except RuntimeError:
+        return None
+
+
+@dataclass
+class QWeight:
+    """A linear weight [N, K] resident on the device in a kernel-native format.
+
+    fmt FMT_Q4K keeps the raw GGUF Q4_K blocks (144 B / 256 weights, 16-byte aligned
+    rows); FMT_Q8_0 keeps Q8_0 split into int8 codes + f16 scales (the 34-byte GGUF block
+    is not 16-byte aligned); FMT_BF16 holds dense bf16 (F16/BF16/F32 checkpoints and the
+    K-quants without a fused kernel yet are expanded to it at load).
+    """
+    fmt: int
+    data: torch.Tensor
+    scales: torch.Tensor | None
+    N: int
+    K: int
+    qtype: GGMLType
+
+    @property
+    def row_bytes(self) -> int:
+        return self.data.stride(0) * self.data.element_size()
+
+    @property
+    def nbytes(self) -> int:
+        n = self.data.numel() * self.data.element_size()
+        if self.scales is not None:
+            n += self.scales.numel() * self.scales.element_size()
+        return n
+
+    def rows(self, r0: int, r1: int) -> "QWeight":
+        """Row slice (a view; used for fused gate|up and TP shards)."""
+        return QWeight(self.fmt, self.data[r0:r1], None if self.scales is None else self.scales[r0:r1],
+                       r1 - r0, self.K, self.qtype)
+
+    @classmethod
+    def from_raw(cls, raw: torch.Tensor, qtype: GGMLType, N: int, K: int,
+                 device: torch.device | str) -> "QWeight":
+        qtype = GGMLType(qtype)
+        raw = raw.reshape(N, -1)
+        if qtype == GGMLType.Q4_K:
+            return cls(FMT_Q4K, raw.to(device).contiguous(), None, N, K, qtype)
+        if qtype == GGMLType.Q8_0:
+            b = raw.to(device).reshape(N, K // 32, 34)
+            scales = b[..., 0:2].contiguous().view(torch.float16).reshape(N, K // 32)
+            qs = b[..., 2:].contiguous().view(torch.int8).reshape(N, K)
+            return cls(FMT_Q8_0, qs, scales.contiguous(), N, K, qtype)
+        dense = dequantize(raw.to(device), qtype).reshape(N, K).to(torch.bfloat16)
+        Kp = pad32(K)
+        if Kp != K:  # zero columns so the activation's 32-element groups line up
+            dense = torch.nn.functional.pad(dense, (0, Kp - K))
+        return cls(FMT_BF16, dense.contiguous(), None, N, Kp, qtype)
+
+    @staticmethod
+    def cat(ws: list["QWeight"]) -> "QWeight":
+        fmt = ws[0].fmt
+        assert all(w.fmt == fmt and w.K == ws[0].K for w in ws)
+        data = torch.cat([w.data for w in ws], 0).contiguous()
+        scales = None if ws[0].scales is None else torch.cat([w.scales for w in ws], 0).contiguous()
+        return QWeight(fmt, data, scales, sum(w.N for w in ws), ws[0].K, ws[0].qtype)
+
+    def dequantize_bf16(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        ext = require_ext()
+        if out is None:
+            out = torch.empty(self.N, self.K, dtype=torch.bfloat16, device=self.data.device)
+        ext.dequant(self.fmt, self.data, self.scales, self.row_bytes, self.N, self.K, out)
+        count_launch()
+        return out
+
+
+def rmsnorm_quant(x: torch.Tensor | None, w: torch.Tensor | None, eps: float, q: torch.Tensor | None,
+                  ds: torch.Tensor | None, y_bf16: torch.Tensor | None = None,
+                  x_bf16: torch.Tensor | None = None, w_offset: float = 0.0):
+    src = x if x is not None else x_bf16
+    B, K = src.shape
+    require_ext().rmsnorm_quant(x, x_bf16, w, w_offset, eps, B, K, q, ds, y_bf16)
+    count_launch()
+
+
+def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EPI_STORE, *,
+         out_f32=None, out_bf16=None, ld_out: int | None = None, resid=None, w2: QWeight | None = None,
+         rope_cs=None, positions=None, slots=None, kv=None, q_out=None, n_heads=0, n_kv=0,
+         head_dim=0, block_size=0, rot_dim=0, err=None):
+    ld = ld_out if ld_out is not None else w.N
+    require_ext().gemv(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, B, xq, xds, mode, out_f32,
+                       out_bf16, ld, resid, None if w2 is None else w2.data,
+                       None if w2 is None else w2.scales, rope_cs, positions, slots, kv, q_out,
+                       n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err)
+    count_launch()
+
+
+def paged_attention(q, kv, block_tables, ctx_len, out, *, n_rows, n_heads, n_kv, head_dim,
+                    block_size, row_seq=None, tree_base=None, tree_mask=None, window=0, n_splits=1,
+                    split_tokens=1 << 30, scale=None, part_o=None, part_ml=None, out_q=None,
+                    out_ds=None, err=None):
+    scale = scale if scale is not None else head_dim ** -0.5
+    require_ext().paged_attention(q, kv, block_tables, row_seq, ctx_len, tree_base, tree_mask, window,
+                                  n_rows, n_heads, n_kv, head_dim, block_size, n_splits, split_tokens,
+                                  scale, part_o, part_ml, out, out_q, out_ds, err)
+    count_launch(2 if (n_splits > 1 or out_q is not None) else 1)
+
+
+def sample(logits, out_tokens, *, counts=None, count_row=None, mask=None, temperature=None, penalty=None, top_k=None,
+           top_p=None, seed=0, step=None, out_prob=None, B=None, V=None):
+    B = B if B is not None else logits.shape[0]
+    V = V if V is not None else logits.shape[1]
+    require_ext().sampler(logits, B, V, counts, count_row, mask, temperature, penalty, top_k, top_p, seed, step,
+                          out_tokens, out_prob)
+    count_launch(2 if step is not None else 1)
+
+
+def count_tokens(counts, tokens, n: int | None = None, per_row: int = 0, count_row=None):
+    n = n if n is not None else tokens.numel()
+    require_ext().count_tokens(counts, tokens, n, per_row, count_row)
+    count_launch()
+
+
+def embed(w: QWeight, ids: torch.Tensor, out_f32=None, out_bf16=None, mult: float = 1.0, err=None,
+          n: int | None = None):
+    n = n if n is not None else ids.numel()
+    require_ext().embed(w.fmt, w.data, w.scales, w.row_bytes, w.K, ids, n, w.N, out_f32, out_bf16,
+                        mult, err)
+    count_launch()
+
+
+def rope_kv(qkv, T, rope_cs, positions, slots, kv, q_out, *, n_heads, n_kv, head_dim, block_size,
+            rot_dim=None, err=None):
+    require_ext().rope_kv(qkv, T, rope_cs, positions, slots, kv, q_out, n_heads, n_kv, head_dim,
+                          block_size, rot_dim or head_dim, err)
+    count_launch()
+
+
+def swiglu(gu, T, F, out_bf16=None, out_f32=None, ld_out: int | None = None):
+    """out[t, j] = silu(gu[t, j]) * gu[t, F + j] for j < F (out row stride ld_out)."""
+    require_ext().swiglu(gu, T, F, ld_out if ld_out is not None else F, out_bf16, out_f32)
+    count_launch()
+
+
+def residual_add(resid, y, n: int | None = None):
+    require_ext().residual_add(resid, y, n if n is not None else y.numel())
+    count_launch()
+
+
+def rope_table(max_pos: int, rot_dim: int, theta: float, device) -> torch.Tensor:
+    """(cos, sin) table [max_pos, rot_dim/2, 2] f32, inv_freq = 1/theta^(2i/d) in f32."""
+    inv = 1.0 / torch.pow(torch.tensor(float(theta), dtype=torch.float32),
+                          torch.arange(0, rot_dim, 2, dtype=torch.float32) / rot_dim)
+    ang = torch.arange(max_pos, dtype=torch.float32)[:, None] * inv[None, :]
+    return torch.stack([torch.cos(ang), torch.sin(ang)], -1).contiguous().to(device)

@@ -1,0 +1,60 @@
+"""Tensor parallelism (Megatron column/row split) across one process per GPU.
+
+Column-parallel: QKV heads and gate/up rows are split across ranks; row-parallel: O and
+down are split along their input dim in whole quant blocks (the reference dequantises to
+F16 and narrows, ``src/tensor_parallel.rs:104-161``; here shards stay quantised). The
+partial outputs are summed across ranks after O and down (the reference does this over a
+host TCP ring, ``src/model.rs:596-607,728-739``), and the vocab-parallel LM head's logits
+are gathered before sampling.
+
+``TPGroup`` is the NCCL baseline data plane. ``air_rs.parallel.symm.FusedTP`` replaces its
+all-reduce with the fused peer-memory kernel on NVLink.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+class TPGroup:
+    def __init__(self, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world_size = dist.get_world_size(group)
+        self._gather_buf: torch.Tensor | None = None
+
+    def all_reduce_add(self, partial: torch.Tensor, x: torch.Tensor):
+        """x += sum over ranks of partial (fp32)."""
+        dist.all_reduce(partial, group=self.group)
+        x.add_(partial)
+
+    def all_gather_vocab(self, local: torch.Tensor, full: torch.Tensor) -> torch.Tensor:
+        """[B, V_l] shards -> [B, V] (the last shard may be padded)."""
+        B, Vl = local.shape
+        W = self.world_size
+        n = W * B * Vl
+        if self._gather_buf is None or self._gather_buf.numel() < n:
+            self._gather_buf = torch.empty(n, dtype=local.dtype, device=local.device)
+        buf = self._gather_buf[:n].view(W, B, Vl)
+        dist.all_gather_into_tensor(buf, local.contiguous(), group=self.group)
+        V = full.shape[1]
+        full.copy_(buf.permute(1, 0, 2).reshape(B, W * Vl)[:, :V])
+        return full
+
+    def broadcast_obj(self, obj, src: int = 0):
+        lst = [obj]
+        dist.broadcast_object_list(lst, src=src, group=self.group)
+        return lst[0]
+
+
+def init_from_env(backend: str = "nccl") -> TPGroup | None:
+    """Initialise torch.distributed from torchrun's env; None when WORLD_SIZE is 1."""
+    import os
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws <= 1:
+        return None
+    if not dist.is_initialized():
+        if backend == "nccl":
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group(backend=backend)
+    return TPGroup()

@@ -1,0 +1,85 @@
+"""Constructors that wire weights, KV pool, runner and engine together."""
+from __future__ import annotations
+
+import torch
+
+from ..gguf import GGMLType, read_gguf
+from ..models.config import ModelConfig, PRESETS
+from ..models.llama import LlamaWeights
+from ..models.random_init import random_tensors
+from ..tokenizer import Tokenizer
+from .engine import Engine
+from .runner import ModelRunner
+
+VRAM_CAP_FRACTION = 0.80  # reference src/vram_guard.rs:30
+
+
+class VramBudgetError(RuntimeError):
+    pass
+
+
+def kv_bytes_per_block(cfg: ModelConfig, block_size: int, tp_size: int = 1) -> int:
+    nkv = max(1, cfg.n_kv_heads // tp_size)
+    return cfg.n_layers * 2 * nkv * block_size * cfg.head_dim * 2
+
+
+def plan_kv_blocks(cfg: ModelConfig, weights_bytes: int, *, block_size: int, device,
+                   max_batch: int, max_model_len: int, tp_size: int = 1,
+                   kv_fraction: float | None = None, num_blocks: int | None = None) -> int:
+    """KV blocks to allocate: enough for max_batch full-length sequences, capped by the
+    VRAM guard (weights + KV <= 80 % of device memory, src/vram_guard.rs:198-337)."""
+    per = kv_bytes_per_block(cfg, block_size, tp_size)
+    want = max_batch * ((max_model_len + block_size - 1) // block_size) + 16
+    if num_blocks is not None:
+        want = num_blocks
+    if torch.device(device).type != "cuda":
+        return want
+    free, total = torch.cuda.mem_get_info(torch.device(device))
+    cap = int(total * (kv_fraction or VRAM_CAP_FRACTION))
+    used = total - free
+    room = cap - used
+    if room <= per * 64:
+        raise VramBudgetError(f"VRAM guard: weights/other use {used/2**30:.1f} GiB of the "
+                              f"{cap/2**30:.1f} GiB cap; no room for the KV pool")
+    return int(min(want, room // per))
+
+
+def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_model_len=4096,
+                 block_size=16, num_blocks=None, tp=None, seed=0, max_seqs=None) -> ModelRunner:
+    tp_size = tp.world_size if tp is not None else 1
+    tp_rank = tp.rank if tp is not None else 0
+    w = LlamaWeights(cfg, records, device, tp_rank=tp_rank, tp_size=tp_size)
+    nb = plan_kv_blocks(cfg, w.nbytes(), block_size=block_size, device=device, max_batch=max_batch,
+                        max_model_len=max_model_len, tp_size=tp_size, num_blocks=num_blocks)
+    return ModelRunner(cfg, w, num_blocks=nb, block_size=block_size, max_batch=max_batch,
+                       max_model_len=max_model_len, device=device, tp=tp, seed=seed,
+                       max_seqs=max_seqs or max(2 * max_batch + 1, 64))
+
+
+def random_engine(preset: str | ModelConfig = "tiny", qtype: GGMLType = GGMLType.Q4_K, *, seed=0,
+                  device="cuda", max_batch=64, max_model_len=4096, tp=None, num_blocks=None,
+                  **kw) -> Engine:
+    """Random-init model of a named architecture built directly in HBM (no file)."""
+    cfg = PRESETS[preset]() if isinstance(preset, str) else preset
+    recs = random_tensors(cfg, qtype, seed=seed, device=device)
+    runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=max_model_len,
+                          tp=tp, num_blocks=num_blocks, seed=seed)
+    tok = Tokenizer.byte_vocab(cfg.vocab_size, cfg.bos_token_id, cfg.eos_token_id)
+    return Engine(cfg, runner, tok, max_batch=max_batch, **kw)
+
+
+def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None, tp=None,
+                     num_blocks=None, seed=0, **kw) -> Engine:
+    g = read_gguf(path)
+    cfg = ModelConfig.from_gguf_metadata(g.metadata)
+    tok = Tokenizer.from_gguf_metadata(g.metadata)
+    if device is None:
+        device = "cuda" if torch.cuda.is_available() else "cpu"
+    if torch.device(device).type != "cuda":
+        from ..models.reference import OracleModel
+        return Engine(cfg, None, tok, oracle=OracleModel.from_gguf(g), **kw)
+    mml = max_model_len or min(cfg.context_length, 8192)
+    recs = ((n, g.raw(n), t.qtype, t.torch_shape) for n, t in g.tensors.items())
+    runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=mml, tp=tp,
+                          num_blocks=num_blocks, seed=seed)
+    return Engine(cfg, runner, tok, max_batch=max_batch, **kw)

@@ -1,0 +1,503 @@
+"""Inference engine: continuous batching over the paged KV pool.
+
+The reference serves one request at a time with batch 1 (``src/scheduler.rs:36-100``,
+``src/inference_step.rs:19-184``) and keeps its Orca/Sarathi scheduler as unused
+bookkeeping (``src/continuous_batch.rs``). Here the scheduler drives real batched steps:
+waiting requests are admitted while KV blocks and batch slots allow, prompts are
+prefilled in token-budgeted chunks (``prefill_chunk`` = 512 like the reference's
+``PREFILL_CHUNK_SIZE``), and every step decodes all running sequences in one CUDA-graph
+replay of the bucket that fits them. Output processing is pipelined: step k+1 is
+launched before step k's tokens are read back, so the host never idles the GPU.
+
+On a machine without CUDA the engine runs the reference-numerics CPU oracle (batch 1),
+which is the reference's Candle-CPU path.
+"""
+from __future__ import annotations
+
+import dataclasses
+import itertools
+import time
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Callable, Iterable
+
+import torch
+
+from ..models.config import ModelConfig
+from ..metrics import InferenceMetrics
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 512
+    temperature: float = 0.7
+    top_p: float = 0.9
+    top_k: int = 40
+    repetition_penalty: float = 1.1
+    stop_token_ids: tuple[int, ...] = ()
+    ignore_eos: bool = False
+
+
+class FinishReason:
+    STOP = "stop"
+    LENGTH = "length"
+    ERROR = "error"
+    ABORT = "abort"
+
+
+@dataclass
+class Request:
+    rid: int
+    prompt_ids: list[int]
+    params: SamplingParams
+    priority: int = 0
+    seq: int = -1                 # SequenceManager id
+    slot: int = -1                # penalty-count row
+    output_ids: list[int] = field(default_factory=list)
+    prefilled: int = 0            # prompt tokens already in the KV cache
+    finished: str | None = None
+    arrival: float = field(default_factory=time.perf_counter)
+    first_token_time: float | None = None
+    finish_time: float | None = None
+    on_token: Callable | None = None
+    grammar: object | None = None
+
+    @property
+    def num_tokens(self) -> int:
+        return len(self.prompt_ids) + len(self.output_ids)
+
+
+BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+
+
+class Engine:
+    """Batched generation over a ``ModelRunner`` (GPU) or the CPU oracle."""
+
+    def __init__(self, cfg: ModelConfig, runner=None, tokenizer=None, *, oracle=None,
+                 max_batch: int = 64, prefill_chunk: int = 512, max_prefill_tokens: int = 8192,
+                 add_bos: bool = True, eos_id: int | None = None):
+        self.cfg = cfg
+        self.runner = runner
+        self.oracle = oracle
+        self.tokenizer = tokenizer
+        self.max_batch = max_batch if runner is not None else 1
+        self.prefill_chunk = prefill_chunk
+        self.max_prefill_tokens = max_prefill_tokens
+        self.add_bos = add_bos
+        self.eos_id = eos_id if eos_id is not None else cfg.eos_token_id
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self.finished: dict[int, Request] = {}
+        self._rid = itertools.count()
+        self.metrics = InferenceMetrics()
+        self.seqs = None
+        self.free_slots: list[int] = []
+        self.step_count = 0
+        self.h2d_bytes_last_step = 0
+        self.d2h_bytes_last_step = 0
+        if runner is not None:
+            from .. import _host  # native bookkeeping
+            self.seqs = _host.SequenceManager(runner.num_blocks, runner.block_size)
+            # the last penalty-count row is the sink for padding rows of a bucket
+            self.pad_slot = runner.counts.shape[0] - 1
+            self.free_slots = list(range(runner.counts.shape[0] - 1))[::-1]
+            self._pinned: dict[int, dict] = {}
+
+    # ------------------------------------------------------------------ requests
+    def add_request(self, prompt_ids: list[int], params: SamplingParams | None = None, *,
+                    priority: int = 0, on_token: Callable | None = None, grammar=None) -> int:
+        params = params or SamplingParams()
+        ids = list(prompt_ids)
+        if self.add_bos and self.cfg.bos_token_id is not None:
+            ids = [self.cfg.bos_token_id] + ids
+        if self.runner is not None and len(ids) + params.max_tokens > self.runner.max_model_len:
+            raise ValueError(f"prompt ({len(ids)}) + max_tokens ({params.max_tokens}) exceeds "
+                             f"max_model_len {self.runner.max_model_len}")
+        r = Request(next(self._rid), ids, params, priority=priority, on_token=on_token, grammar=grammar)
+        self.waiting.append(r)
+        return r.rid
+
+    def abort(self, rid: int) -> bool:
+        for q in (self.waiting, self.running):
+            for r in list(q):
+                if r.rid == rid:
+                    self._finish(r, FinishReason.ABORT)
+                    if r in self.waiting:
+                        self.waiting.remove(r)
+                    return True
+        return False
+
+    def has_unfinished(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    # ------------------------------------------------------------------ bookkeeping
+    def _finish(self, r: Request, reason: str):
+        if r.finished:
+            return
+        r.finished = reason
+        r.finish_time = time.perf_counter()
+        if r in self.running:
+            self.running.remove(r)
+        if getattr(self, "_defer_free", False):
+            if not hasattr(self, "_deferred"):
+                self._deferred = []
+            self._deferred.append((r.seq, r.slot))
+        else:
+            if self.seqs is not None and r.seq >= 0:
+                self.seqs.free_sequence(r.seq)
+            if r.slot >= 0:
+                self.free_slots.append(r.slot)
+        r.seq = -1
+        r.slot = -1
+        self.finished[r.rid] = r
+
+    def _emit(self, r: Request, tok: int, prob: float = 1.0):
+        if r.finished:
+            return
+        now = time.perf_counter()
+        if r.first_token_time is None:
+            r.first_token_time = now
+            self.metrics.mark_first_token()
+        r.output_ids.append(tok)
+        self.metrics.record_token()
+        if r.grammar is not None:
+            try:
+                r.grammar.push_token(tok)
+            except Exception:
+                pass
+        if r.on_token is not None:
+            r.on_token(r, tok)
+        stop = (not r.params.ignore_eos and (tok == self.eos_id or tok in r.params.stop_token_ids))
+        if r.grammar is not None and getattr(r.grammar, "is_complete", lambda: False)():
+            stop = True
+        if stop:
+            self._finish(r, FinishReason.STOP)
+        elif len(r.output_ids) >= r.params.max_tokens:
+            self._finish(r, FinishReason.LENGTH)
+
+    # ------------------------------------------------------------------ GPU scheduling
+    def _admit(self) -> list[Request]:
+        """Admit waiting requests while batch slots / KV blocks / token budget allow."""
+        admitted = []
+        budget = self.max_prefill_tokens
+        alloc = self.seqs.allocator
+        bs = self.runner.block_size
+        reserve = sum(1 for _ in self.running)  # one growth block per running sequence
+        while self.waiting and len(self.running) + len(admitted) < self.max_batch:
+            r = self.waiting[0]
+            need = (len(r.prompt_ids) + bs - 1) // bs + 1
+            if not alloc.can_allocate(need + reserve) or not self.free_slots:
+                break
+            if len(r.prompt_ids) > budget and admitted:
+                break
+            self.waiting.popleft()
+            r.seq = self.seqs.create_sequence()
+            r.slot = self.free_slots.pop()
+            admitted.append(r)
+            budget -= len(r.prompt_ids)
+        return admitted
+
+    def _prefill(self, reqs: list[Request]):
+        """Chunked prefill of admitted requests; samples their first tokens."""
+        rn = self.runner
+        dev = rn.device
+        pending = list(reqs)
+        for r in pending:
+            rn.reset_counts(r.slot, torch.tensor(r.prompt_ids, dtype=torch.int32))
+        while pending:
+            ids, pos, slots, rows, lasts, done = [], [], [], [], [], []
+            seq_list = []
+            budget = self.max_prefill_tokens
+            for i, r in enumerate(pending):
+                if budget <= 0:
+                    break
+                n_left = len(r.prompt_ids) - r.prefilled
+                n = min(n_left, self.prefill_chunk, budget)
+                if n <= 0:
+                    continue
+                start = r.prefilled
+                sl = self.seqs.append(r.seq, n)
+                seq_list.append(r.seq)
+                ids.extend(r.prompt_ids[start:start + n])
+                pos.extend(range(start, start + n))
+                slots.extend(sl)
+                rows.extend([len(seq_list) - 1] * n)
+                r.prefilled += n
+                budget -= n
+                lasts.append(len(ids) - 1)
+                done.append(r if r.prefilled == len(r.prompt_ids) else None)
+            tab = torch.full((len(seq_list), rn.max_blocks), -1, dtype=torch.int32)
+            self.seqs.fill_table(seq_list, tab)
+            S = len(lasts)
+            pr = [r for r in pending if r.seq in seq_list]
+            sp = [pending[i].params for i in range(len(pending)) if pending[i].seq in seq_list]
+            toks, probs = rn.prefill(
+                torch.tensor(ids, dtype=torch.int32, device=dev),
+                torch.tensor(pos, dtype=torch.int32, device=dev),
+                torch.tensor(slots, dtype=torch.int64, device=dev),
+                torch.tensor(rows, dtype=torch.int32, device=dev),
+                tab.to(dev, non_blocking=True),
+                torch.tensor(lasts, dtype=torch.int64, device=dev),
+                torch.tensor([r.slot for r in pr], dtype=torch.int32, device=dev),
+                torch.tensor([p.temperature for p in sp], dtype=torch.float32, device=dev),
+                torch.tensor([p.repetition_penalty for p in sp], dtype=torch.float32, device=dev),
+                torch.tensor([p.top_k for p in sp], dtype=torch.int32, device=dev),
+                torch.tensor([p.top_p for p in sp], dtype=torch.float32, device=dev),
+            )
+            toks_h = toks.tolist()
+            for r, d, t in zip(pr, done, toks_h):
+                if d is not None:
+                    self.running.append(r)
+                    self._emit(r, t)
+            pending = [r for r in pending if r.prefilled < len(r.prompt_ids)]
+        rn.check_errors()
+
+    def _bucket(self, n: int) -> int:
+        for b in BUCKETS:
+            if b >= n and b <= self.runner.max_batch:
+                return b
+        return self.runner.max_batch
+
+    def _pinned_for(self, B: int):
+        p = self._pinned.get(B)
+        if p is None:
+            rn = self.runner
+            p = {
+                "i32": torch.zeros(3 * B, dtype=torch.int32).pin_memory(),
+                "slots": torch.zeros(B, dtype=torch.int64).pin_memory(),
+                "tab": torch.zeros(B, rn.max_blocks, dtype=torch.int32).pin_memory(),
+                "samp_f": torch.zeros(3 * B, dtype=torch.float32).pin_memory(),
+                "samp_i": torch.zeros(B, dtype=torch.int32).pin_memory(),
+                "tok": torch.zeros(B, dtype=torch.int32).pin_memory(),
+                "members": None,
+            }
+            self._pinned[B] = p
+        return p
+
+    def _launch_decode(self, batch: list[Request]):
+        """Stage inputs (one H2D copy per buffer) and replay the bucket's graph."""
+        rn = self.runner
+        n = len(batch)
+        B = self._bucket(n)
+        si = rn.step_inputs(B)
+        p = self._pinned_for(B)
+        seqs = [r.seq for r in batch] + [-1] * (B - n)
+        slots = self.seqs.step_slots(seqs)
+        i32 = p["i32"]
+        h2d = 0
+        for i, r in enumerate(batch):
+            pos = r.num_tokens - 1
+            i32[i] = pos
+            i32[B + i] = pos + 1
+            i32[2 * B + i] = r.slot
+        for i in range(n, B):
+            i32[i] = 0
+            i32[B + i] = 0
+            i32[2 * B + i] = self.pad_slot
+        p["slots"][:] = torch.tensor(slots, dtype=torch.int64)
+        si.positions.copy_(i32[:B], non_blocking=True)
+        si.ctx_len.copy_(i32[B:2 * B], non_blocking=True)
+        si.count_row.copy_(i32[2 * B:], non_blocking=True)
+        si.slots.copy_(p["slots"], non_blocking=True)
+        h2d += 3 * B * 4 + B * 8
+        members = tuple(r.rid for r in batch)
+        if p["members"] != (members, [r.seq for r in batch]):
+            self.seqs.fill_table(seqs, p["tab"])
+            si.block_tables.copy_(p["tab"], non_blocking=True)
+            h2d += p["tab"].numel() * 4
+            sf, sii = p["samp_f"], p["samp_i"]
+            for i in range(B):
+                pr = batch[min(i, n - 1)].params
+                sf[i], sf[B + i], sf[2 * B + i] = pr.temperature, pr.repetition_penalty, pr.top_p
+                sii[i] = pr.top_k
+            si.temperature.copy_(sf[:B], non_blocking=True)
+            si.penalty.copy_(sf[B:2 * B], non_blocking=True)
+            si.top_p.copy_(sf[2 * B:], non_blocking=True)
+            si.top_k.copy_(sii, non_blocking=True)
+            h2d += 4 * B * 4
+            # ids: last token of each sequence (from the host; after this the graph feeds itself)
+            ids = torch.tensor([r.output_ids[-1] for r in batch] + [0] * (B - n), dtype=torch.int32)
+            si.ids.copy_(ids.pin_memory(), non_blocking=True)
+            h2d += B * 4
+            p["members"] = (members, [r.seq for r in batch])
+        elif self.seqs_changed_blocks(batch):
+            self.seqs.fill_table(seqs, p["tab"])
+            si.block_tables.copy_(p["tab"], non_blocking=True)
+            h2d += p["tab"].numel() * 4
+        rn.decode(B, use_graph=True)
+        p["tok"].copy_(si.tokens, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.h2d_bytes_last_step = h2d
+        self.d2h_bytes_last_step = B * 4
+        return B, p, ev
+
+    def seqs_changed_blocks(self, batch) -> bool:
+        # a new block was opened for some sequence iff its new token starts a block
+        bs = self.runner.block_size
+        return any((r.num_tokens - 1) % bs == 0 for r in batch)
+
+    def step(self) -> list[tuple[int, int]]:
+        """One scheduler iteration; returns the (rid, token) pairs produced."""
+        produced: list[tuple[int, int]] = []
+        if self.runner is None:
+            return self._step_cpu()
+        admitted = self._admit()
+        if admitted:
+            before = {r.rid: len(r.output_ids) for r in admitted}
+            self._prefill(admitted)
+            produced += [(r.rid, r.output_ids[-1]) for r in admitted if len(r.output_ids) > before[r.rid]]
+        batch = [r for r in self.running if r.output_ids and not r.finished]
+        if not batch:
+            return produced
+        B, p, ev = self._launch_decode(batch)
+        ev.synchronize()
+        toks = p["tok"][:len(batch)].tolist()
+        for r, t in zip(batch, toks):
+            self._emit(r, t)
+            produced.append((r.rid, t))
+        self.step_count += 1
+        return produced
+
+    def run_pipelined(self, max_steps: int | None = None) -> int:
+        """Decode loop that launches step k+1 before reading step k's tokens.
+
+        The next step's inputs (positions, slots) do not depend on the sampled values (the
+        graph feeds its own sampled ids forward), so output processing overlaps the GPU.
+        A sequence that stops at step k still rode in step k+1; that extra token is dropped
+        and its KV blocks are freed only after step k+1 has completed.
+        """
+        steps = 0
+        inflight = None
+        while max_steps is None or steps < max_steps:
+            if inflight is None:
+                if self.waiting:
+                    admitted = self._admit()
+                    if admitted:
+                        self._prefill(admitted)
+                batch = [r for r in self.running if not r.finished]
+                if not batch:
+                    if not self.waiting:
+                        break
+                    continue
+                inflight = (batch, *self._launch_decode(batch))
+                continue
+            ib, B, p, ev = inflight
+            chain = (not self.waiting and (max_steps is None or steps + 1 < max_steps) and
+                     all(len(r.output_ids) + 2 <= r.params.max_tokens for r in ib))
+            nxt = None
+            if chain:
+                for r in ib:
+                    r.output_ids.append(-1)   # the in-flight token occupies a position
+                nxt = (ib, *self._launch_decode(ib))
+                for r in ib:
+                    r.output_ids.pop()
+            ev.synchronize()
+            toks = p["tok"][:len(ib)].tolist()
+            for r, t in zip(ib, toks):
+                self._emit_deferred(r, t)
+            steps += 1
+            self.step_count += 1
+            if nxt is not None and any(r.finished for r in ib):
+                _, _, p2, ev2 = nxt
+                ev2.synchronize()
+                toks = p2["tok"][:len(ib)].tolist()
+                for r, t in zip(ib, toks):
+                    self._emit_deferred(r, t)
+                steps += 1
+                self.step_count += 1
+                nxt = None
+            if nxt is None:
+                self._release_deferred()
+            inflight = nxt
+        self._release_deferred()
+        return steps
+
+    def _emit_deferred(self, r: Request, tok: int):
+        """_emit, but KV blocks of a finishing request are freed later (a step may be in flight)."""
+        if r.finished:
+            return
+        self._defer_free = True
+        try:
+            self._emit(r, tok)
+        finally:
+            self._defer_free = False
+
+    def _release_deferred(self):
+        for seq, slot in getattr(self, "_deferred", []):
+            if seq >= 0:
+                self.seqs.free_sequence(seq)
+            if slot >= 0:
+                self.free_slots.append(slot)
+        self._deferred = []
+
+    # ------------------------------------------------------------------ CPU oracle
+    def _step_cpu(self):
+        from ..models.reference import apply_repetition_penalty
+        produced = []
+        if not self.running and self.waiting:
+            r = self.waiting.popleft()
+            self.running.append(r)
+            self.oracle.reset()
+            toks = r.prompt_ids
+            pc = self.prefill_chunk
+            pos = 0
+            if len(toks) > pc:
+                n_full = len(toks) // pc * pc
+                for c in range(0, n_full, pc):
+                    self.oracle.forward(toks[c:c + pc], c)
+                pos = n_full
+                if pos == len(toks):
+                    self.oracle.truncate(pos - 1)
+                    pos -= 1
+            r._logits = self.oracle.forward(toks[pos:], pos)
+        if not self.running:
+            return produced
+        r = self.running[0]
+        lg = apply_repetition_penalty(r._logits, r.prompt_ids + r.output_ids, r.params.repetition_penalty)
+        if r.grammar is not None and hasattr(r.grammar, "apply_to_logits"):
+            lg = r.grammar.apply_to_logits_tensor(lg) if hasattr(r.grammar, "apply_to_logits_tensor") else lg
+        tok = sample_cpu(lg, r.params, self._cpu_gen())
+        self._emit(r, tok)
+        produced.append((r.rid, tok))
+        if not r.finished:
+            r._logits = self.oracle.forward([tok], r.num_tokens - 1)
+        self.step_count += 1
+        return produced
+
+    def _cpu_gen(self):
+        g = getattr(self, "_gen", None)
+        if g is None:
+            g = self._gen = torch.Generator().manual_seed(0)
+        return g
+
+    # ------------------------------------------------------------------ high level
+    def generate_ids(self, prompts: list[list[int]], params: SamplingParams | None = None,
+                     pipelined: bool = False) -> list[list[int]]:
+        rids = [self.add_request(p, params) for p in prompts]
+        if pipelined and self.runner is not None:
+            self.run_pipelined()
+        while self.has_unfinished():
+            self.step()
+        return [self.finished[r].output_ids for r in rids]
+
+
+def sample_cpu(logits: torch.Tensor, p: SamplingParams, gen: torch.Generator) -> int:
+    """Host sampler with the reference's order (src/sampler.rs:83-164)."""
+    if p.temperature <= 1e-6:
+        return int(torch.argmax(logits))
+    probs = torch.softmax(logits.float() / p.temperature, -1)
+    vals, idx = torch.sort(probs, descending=True, stable=True)
+    if 0 < p.top_k < vals.numel():
+        vals, idx = vals[:p.top_k], idx[:p.top_k]
+    if p.top_p < 1.0:
+        c = torch.cumsum(vals, 0)
+        cut = int(torch.searchsorted(c, torch.tensor(p.top_p)).item()) + 1
+        vals, idx = vals[:cut], idx[:cut]
+    total = float(vals.sum())
+    if total <= 0:
+        return int(torch.argmax(probs))
+    r = torch.rand((), generator=gen).item() * total
+    c = torch.cumsum(vals, 0)
+    k = int(torch.searchsorted(c, torch.tensor(r)).item())
+    return int(idx[min(k, idx.numel() - 1)])

@@ -1,0 +1,355 @@
+"""Model runner: one batched forward over the paged KV pool, on the sm_100a kernels.
+
+``decode(B)`` runs one token for B sequences; its buffers are static per batch bucket so
+the whole step (embedding -> layers -> LM head -> sampler) is captured once in a CUDA
+graph and replayed (the reference's graph registry ``src/strix/gpu_direct.rs:1054-1113`` is
+a stub; this one is real). ``prefill`` runs any number of prompt tokens of one or more
+sequences (chunked prefill) through the GEMM path and samples each sequence's next token.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from ..models.config import ModelConfig
+from ..models.llama import LlamaWeights
+
+GEMV_MAX_B = 8
+
+
+def _dev_param(x, dtype, device):
+    return torch.tensor(x, dtype=dtype, device=device)
+
+
+@dataclass
+class StepInputs:
+    """Static per-bucket device inputs of one decode step."""
+    ids: torch.Tensor          # [B] int32 (written by the previous step's sampler)
+    positions: torch.Tensor    # [B] int32
+    slots: torch.Tensor        # [B] int64
+    ctx_len: torch.Tensor      # [B] int32 (= position + 1)
+    block_tables: torch.Tensor  # [B, max_blocks] int32
+    count_row: torch.Tensor    # [B] int32 (sequence slot for penalty counts)
+    temperature: torch.Tensor  # [B] f32
+    penalty: torch.Tensor      # [B] f32
+    top_k: torch.Tensor        # [B] int32
+    top_p: torch.Tensor        # [B] f32
+    tokens: torch.Tensor       # [B] int32 output
+    probs: torch.Tensor        # [B] f32 output (top-1 prob of the filtered nucleus)
+
+
+class ModelRunner:
+    def __init__(self, cfg: ModelConfig, weights: LlamaWeights, *, num_blocks: int,
+                 block_size: int = 16, max_batch: int = 64, max_model_len: int = 4096,
+                 max_seqs: int = 256, max_prefill_tokens: int = 8192, device="cuda", tp=None,
+                 seed: int = 0, use_gemm_kernel: bool = True):
+        self.cfg, self.w = cfg, weights
+        self.device = torch.device(device)
+        self.tp = tp
+        tp_size = tp.world_size if tp is not None else 1
+        self.tp_size = tp_size
+        self.nh = cfg.n_heads // tp_size
+        self.nkv = max(1, cfg.n_kv_heads // tp_size)
+        self.hd = cfg.head_dim
+        self.H = cfg.hidden_dim
+        self.F = cfg.intermediate_dim // tp_size
+        self.Fp = ops.pad32(self.F)  # activation width of the down projection (zero padded)
+        self.V = cfg.vocab_size
+        self.V_l = weights.lm_head.N
+        self.block_size = block_size
+        self.max_batch = max_batch
+        self.max_model_len = max_model_len
+        self.max_blocks = (max_model_len + block_size - 1) // block_size
+        self.num_blocks = num_blocks
+        self.seed = seed
+        self.use_gemm_kernel = use_gemm_kernel
+        dev = self.device
+        L = cfg.n_layers
+        self.kv = torch.zeros(L, num_blocks, 2, self.nkv, block_size, self.hd, dtype=torch.bfloat16, device=dev)
+        rot = self.hd if cfg.partial_rope_factor is None else int(self.hd * cfg.partial_rope_factor)
+        self.rot_dim = rot
+        self.rope_cs = ops.rope_table(max_model_len + 64, rot, cfg.rope_theta, dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.counts = torch.zeros(max_seqs, self.V, dtype=torch.uint8, device=dev)
+        self.step_ctr = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.qkv_dim = (self.nh + 2 * self.nkv) * self.hd
+        B = max_batch
+        kmax = max(self.H, self.Fp, self.nh * self.hd)
+        f32, i8, bf16 = torch.float32, torch.int8, torch.bfloat16
+        # decode workspace (sized for max_batch; buckets use leading slices)
+        self.x = torch.zeros(B, self.H, dtype=f32, device=dev)
+        self.xq = torch.zeros(B, kmax, dtype=i8, device=dev)
+        self.xds = torch.zeros(B, kmax // 32, 2, dtype=f32, device=dev)
+        self.q = torch.zeros(B, self.nh, self.hd, dtype=f32, device=dev)
+        self.attn = torch.zeros(B, self.nh * self.hd, dtype=f32, device=dev)
+        self.h = torch.zeros(B, self.Fp, dtype=f32, device=dev)
+        self.y = torch.zeros(B, self.H, dtype=f32, device=dev)
+        self.logits = torch.zeros(B, self.V_l, dtype=f32, device=dev)
+        self.logits_full = self.logits if tp_size == 1 else torch.zeros(B, self.V, dtype=f32, device=dev)
+        self.max_splits = 32
+        self.part_o = torch.zeros(B * self.nh * self.max_splits * self.hd, dtype=f32, device=dev)
+        self.part_ml = torch.zeros(B * self.nh * self.max_splits * 2, dtype=f32, device=dev)
+        # GEMM-path activations (bf16) for large-batch decode
+        self.xn_b = torch.zeros(B, self.H, dtype=bf16, device=dev)
+        self.qkv_b = torch.zeros(B, self.qkv_dim, dtype=bf16, device=dev)
+        self.attn_b = torch.zeros(B, self.nh * self.hd, dtype=bf16, device=dev)
+        self.gu_b = torch.zeros(B, 2 * self.F, dtype=bf16, device=dev)
+        self.h_b = torch.zeros(B, self.Fp, dtype=bf16, device=dev)
+        self.o_b = torch.zeros(B, self.H, dtype=bf16, device=dev)
+        self.inputs: dict[int, StepInputs] = {}
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: dict[int, int] = {}
+        self._prefill_ws: dict[str, torch.Tensor] = {}
+        self.max_prefill_tokens = max_prefill_tokens
+        self._wscratch = None
+
+    # ------------------------------------------------------------------ inputs
+    def step_inputs(self, B: int) -> StepInputs:
+        si = self.inputs.get(B)
+        if si is None:
+            d = self.device
+            si = StepInputs(
+                ids=torch.zeros(B, dtype=torch.int32, device=d),
+                positions=torch.zeros(B, dtype=torch.int32, device=d),
+                slots=torch.full((B,), -1, dtype=torch.int64, device=d),
+                ctx_len=torch.ones(B, dtype=torch.int32, device=d),
+                block_tables=torch.full((B, self.max_blocks), -1, dtype=torch.int32, device=d),
+                count_row=torch.arange(B, dtype=torch.int32, device=d),
+                temperature=torch.zeros(B, dtype=torch.float32, device=d),
+                penalty=torch.ones(B, dtype=torch.float32, device=d),
+                top_k=torch.zeros(B, dtype=torch.int32, device=d),
+                top_p=torch.ones(B, dtype=torch.float32, device=d),
+                tokens=torch.zeros(B, dtype=torch.int32, device=d),
+                probs=torch.zeros(B, dtype=torch.float32, device=d),
+            )
+            self.inputs[B] = si
+        return si
+
+    def n_splits(self, B: int) -> int:
+        target = 4 * 148
+        return int(max(1, min(self.max_splits, math.ceil(target / max(1, B * self.nkv)))))
+
+    # ------------------------------------------------------------------ linear (GEMM path)
+    def linear(self, x_bf16: torch.Tensor, w: ops.QWeight, out: torch.Tensor) -> torch.Tensor:
+        """out[T, N] = x[T, K] @ W^T for the prefill / large-batch path."""
+        from ..ops import gemm
+        return gemm.linear(x_bf16, w, out, self)
+
+    # ------------------------------------------------------------------ collectives
+    def _reduce_into_residual(self, partial: torch.Tensor, B: int, x: torch.Tensor):
+        """x += all_reduce(partial) across TP ranks (partial: [B, H] f32)."""
+        self.tp.all_reduce_add(partial[:B], x[:B])
+
+    # ------------------------------------------------------------------ decode
+    def _decode_body(self, B: int):
+        cfg, w, si = self.cfg, self.w, self.inputs[B]
+        eps = cfg.rms_norm_eps
+        x, xq, xds = self.x[:B], self.xq[:B], self.xds[:B]
+        ops.embed(w.embd, si.ids, out_f32=x, err=self.err, n=B)
+        gemv_path = B <= GEMV_MAX_B
+        ns = self.n_splits(B)
+        tp = self.tp_size > 1
+        for li, lw in enumerate(w.layers):
+            kv = self.kv[li]
+            if gemv_path:
+                ops.rmsnorm_quant(x, lw.attn_norm, eps, xq, xds)
+                ops.gemv(lw.wqkv, xq, xds, B, ops.EPI_QKV_ROPE, rope_cs=self.rope_cs,
+                         positions=si.positions, slots=si.slots, kv=kv, q_out=self.q[:B],
+                         n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
+                         block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
+            else:
+                ops.rmsnorm_quant(x, lw.attn_norm, eps, None, None, y_bf16=self.xn_b[:B])
+                self.linear(self.xn_b[:B], lw.wqkv, self.qkv_b[:B])
+                ops.rope_kv(self.qkv_b[:B], B, self.rope_cs, si.positions, si.slots, kv, self.q[:B],
+                            n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
+                            block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
+            ops.paged_attention(self.q[:B], kv, si.block_tables, si.ctx_len, self.attn[:B],
+                                n_rows=B, n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
+                                block_size=self.block_size, n_splits=ns, split_tokens=0,
+                                part_o=self.part_o, part_ml=self.part_ml,
+                                out_q=xq if gemv_path else None, out_ds=xds if gemv_path else None,
+                                err=self.err, window=cfg.sliding_window or 0)
+            if gemv_path:
+                if tp:
+                    ops.gemv(lw.wo, xq, xds, B, ops.EPI_STORE, out_f32=self.y[:B])
+                    self._reduce_into_residual(self.y, B, x)
+                else:
+                    ops.gemv(lw.wo, xq, xds, B, ops.EPI_RESIDUAL, resid=x)
+                ops.rmsnorm_quant(x, lw.ffn_norm, eps, xq, xds)
+                self._ffn_gemv(lw, B, x, xq, xds, tp)
+            else:
+                self.attn_b[:B].copy_(self.attn[:B])
+                self.linear(self.attn_b[:B], lw.wo, self.o_b[:B])
+                self._residual(self.o_b, B, x, tp)
+                ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=self.xn_b[:B])
+                self._ffn_gemm(lw, B, x, tp)
+        self._head(B, x, xq, xds, gemv_path)
+
+    def _residual(self, y_b: torch.Tensor, B: int, x: torch.Tensor, tp: bool):
+        if tp:
+            self.y[:B].copy_(y_b[:B])
+            self._reduce_into_residual(self.y, B, x)
+        else:
+            ops.residual_add(x, y_b[:B])
+
+    def _ffn_gemv(self, lw, B, x, xq, xds, tp):
+        if lw.wgu is None:
+            from ..parallel import moe
+            moe.moe_ffn_decode(self, lw, B, x, xq, xds)
+            return
+        ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, out_f32=self.h[:B], ld_out=self.Fp)
+        ops.rmsnorm_quant(self.h[:B], None, 0.0, xq, xds)
+        if tp:
+            ops.gemv(lw.wdown, xq, xds, B, ops.EPI_STORE, out_f32=self.y[:B])
+            self._reduce_into_residual(self.y, B, x)
+        else:
+            ops.gemv(lw.wdown, xq, xds, B, ops.EPI_RESIDUAL, resid=x)
+
+    def _ffn_gemm(self, lw, B, x, tp):
+        if lw.wgu is None:
+            from ..parallel import moe
+            moe.moe_ffn_gemm(self, lw, B, x)
+            return
+        self.linear(self.xn_b[:B], lw.wgu, self.gu_b[:B])
+        ops.swiglu(self.gu_b[:B], B, self.F, out_bf16=self.h_b[:B], ld_out=self.Fp)
+        self.linear(self.h_b[:B], lw.wdown, self.o_b[:B])
+        self._residual(self.o_b, B, x, tp)
+
+    def _head(self, B, x, xq, xds, gemv_path):
+        w, si = self.w, self.inputs[B]
+        if gemv_path:
+            ops.rmsnorm_quant(x, w.out_norm, self.cfg.rms_norm_eps, xq, xds)
+            ops.gemv(w.lm_head, xq, xds, B, ops.EPI_STORE, out_f32=self.logits[:B])
+        else:
+            ops.rmsnorm_quant(x, w.out_norm, self.cfg.rms_norm_eps, None, None, y_bf16=self.xn_b[:B])
+            self.linear(self.xn_b[:B], w.lm_head, self.logits[:B])
+        logits = self.logits[:B]
+        if self.tp_size > 1:
+            logits = self.tp.all_gather_vocab(self.logits[:B], self.logits_full[:B])
+        ops.sample(logits, si.tokens, counts=self.counts, count_row=si.count_row,
+                   temperature=si.temperature, penalty=si.penalty, top_k=si.top_k, top_p=si.top_p,
+                   seed=self.seed, step=self.step_ctr, out_prob=si.probs, B=B, V=self.V)
+        ops.count_tokens(self.counts, si.tokens, n=B, count_row=si.count_row)
+        si.ids.copy_(si.tokens)
+
+    def decode(self, B: int, use_graph: bool = True):
+        """Runs one decode step for the first B rows of the bucket-B inputs."""
+        self.step_inputs(B)
+        if not use_graph:
+            self._decode_body(B)
+            return self.inputs[B]
+        g = self.graphs.get(B)
+        if g is None:
+            s = torch.cuda.Stream(self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(s):
+                self._decode_body(B)  # warm-up outside capture (allocator, lazy init)
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            c0 = ops.launch_count()
+            with torch.cuda.graph(g):
+                self._decode_body(B)
+            self.graph_launches[B] = ops.launch_count() - c0
+            ops.count_launch(-(ops.launch_count() - c0))  # capture itself runs nothing
+            self.graphs[B] = g
+        g.replay()
+        ops.count_launch(self.graph_launches[B])
+        return self.inputs[B]
+
+    # ------------------------------------------------------------------ prefill
+    def _ws(self, name, shape, dtype, zero: bool = False):
+        t = self._prefill_ws.get(name)
+        n = 1
+        for s in shape:
+            n *= s
+        if t is None or t.numel() < n or t.dtype != dtype:
+            t = (torch.zeros if zero else torch.empty)(max(n, 1), dtype=dtype, device=self.device)
+            self._prefill_ws[name] = t
+        return t[:n].view(*shape)
+
+    def prefill(self, ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
+                row_seq: torch.Tensor, block_tables: torch.Tensor, last_rows: torch.Tensor,
+                count_rows: torch.Tensor, temperature, penalty, top_k, top_p):
+        """Prompt tokens of one or more sequences (concatenated, T total).
+
+        row_seq[t] indexes ``block_tables``; last_rows[s] is the row of each sequence's last
+        token, whose logits are sampled. Returns (tokens [S] int32, probs [S] f32).
+        """
+        cfg, w = self.cfg, self.w
+        T = ids.numel()
+        S = last_rows.numel()
+        eps = cfg.rms_norm_eps
+        f32, bf16 = torch.float32, torch.bfloat16
+        x = self._ws("x", (T, self.H), f32)
+        xn = self._ws("xn", (T, self.H), bf16)
+        qkv = self._ws("qkv", (T, self.qkv_dim), bf16)
+        q = self._ws("q", (T, self.nh, self.hd), f32)
+        attn = self._ws("attn", (T, self.nh * self.hd), f32)
+        attn_b = self._ws("attn_b", (T, self.nh * self.hd), bf16)
+        o = self._ws("o", (T, self.H), bf16)
+        gu = self._ws("gu", (T, 2 * self.F), bf16) if self.w.layers[0].wgu is not None else None
+        hb = self._ws("hb", (T, self.Fp), bf16, zero=True)
+        ctx = (positions + 1).to(torch.int32)
+        tp = self.tp_size > 1
+        ops.embed(w.embd, ids, out_f32=x, err=self.err, n=T)
+        for li, lw in enumerate(w.layers):
+            kv = self.kv[li]
+            ops.rmsnorm_quant(x, lw.attn_norm, eps, None, None, y_bf16=xn)
+            self.linear(xn, lw.wqkv, qkv)
+            ops.rope_kv(qkv, T, self.rope_cs, positions, slots, kv, q, n_heads=self.nh, n_kv=self.nkv,
+                        head_dim=self.hd, block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
+            ops.paged_attention(q, kv, block_tables, ctx, attn, n_rows=T, n_heads=self.nh,
+                                n_kv=self.nkv, head_dim=self.hd, block_size=self.block_size,
+                                row_seq=row_seq, n_splits=1, err=self.err,
+                                window=cfg.sliding_window or 0)
+            attn_b.copy_(attn)
+            self.linear(attn_b, lw.wo, o)
+            self._residual_T(o, T, x, tp)
+            ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=xn)
+            if lw.wgu is None:
+                from ..parallel import moe
+                moe.moe_ffn_prefill(self, lw, T, x, xn)
+            else:
+                self.linear(xn, lw.wgu, gu)
+                ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp)
+                self.linear(hb, lw.wdown, o)
+                self._residual_T(o, T, x, tp)
+        xl = x.index_select(0, last_rows.long())
+        xs = self._ws("xs", (S, self.H), bf16)
+        ops.rmsnorm_quant(xl, w.out_norm, eps, None, None, y_bf16=xs)
+        logits = self._ws("logits", (S, self.V_l), f32)
+        self.linear(xs, w.lm_head, logits)
+        if tp:
+            full = self._ws("logits_full", (S, self.V), f32)
+            logits = self.tp.all_gather_vocab(logits, full)
+        toks = torch.zeros(S, dtype=torch.int32, device=self.device)
+        probs = torch.zeros(S, dtype=torch.float32, device=self.device)
+        ops.sample(logits, toks, counts=self.counts, count_row=count_rows, temperature=temperature,
+                   penalty=penalty, top_k=top_k, top_p=top_p, seed=self.seed, step=self.step_ctr,
+                   out_prob=probs, B=S, V=self.V)
+        ops.count_tokens(self.counts, toks, n=S, count_row=count_rows)
+        return toks, probs
+
+    def _residual_T(self, o, T, x, tp):
+        if tp:
+            y = self._ws("y", (T, self.H), torch.float32)
+            y.copy_(o)
+            self.tp.all_reduce_add(y, x)
+        else:
+            ops.residual_add(x, o)
+
+    # ------------------------------------------------------------------ misc
+    def check_errors(self):
+        e = int(self.err.item())
+        if e:
+            self.err.zero_()
+            raise RuntimeError(f"device kernel reported error code {e} (1=index out of range, 2=peer timeout)")
+
+    def reset_counts(self, row: int, prompt_ids: torch.Tensor | None = None):
+        self.counts[row].zero_()
+        if prompt_ids is not None and prompt_ids.numel():
+            cr = torch.full((prompt_ids.numel(),), row, dtype=torch.int32, device=self.device)
+            ops.count_tokens(self.counts, prompt_ids.to(self.device, torch.int32), count_row=cr, per_row=1)

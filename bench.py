@@ -1,0 +1,253 @@
+#!/usr/bin/env python
+"""Headline benchmark: decode tokens/s (device-timed, max over ranks) and p50 TTFT.
+
+Config (from the benchmark spec): Llama-3-8B-shape, random-init N(0, 0.02) weights
+quantised to Q4_K (built directly in HBM), 512-token uniform-random prompts, batch 64,
+paged KV with 16-token blocks, greedy decode, tensor parallel over the N GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch 64] [--impl ours|reference]
+
+A "step" is one decode iteration of the whole batch (batch tokens). W untimed steps, then
+K timed steps between CUDA events (barrier + synchronize on both sides); the weights
+(4.6 GB) and KV cache are far larger than the 126 MB L2, so no flush is needed between
+steps. Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# README row 5 (RTX 3060, 8B Q8, --resident, batch 1): 8-12 tok/s -> midpoint 10.
+BASELINE_TOK_S = 10.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--model", default="llama3-8b")
+    ap.add_argument("--quant", default="Q4_K")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "baseline"])
+    ap.add_argument("--ttft-runs", type=int, default=5)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_unavailable():
+    msg = ("reference (Rust crate, maturin build backend) cannot be installed: "
+           "pip install of /root/reference fails with ModuleNotFoundError: No module named "
+           "'maturin'; no cargo/rustc in the image")
+    print(json.dumps({"impl": "reference", "unavailable": msg}))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_unavailable()
+        return 0
+    if args.impl == "baseline":
+        os.environ["AIR_GEMM_IMPL"] = "baseline"
+    import torch
+    import torch.distributed as dist
+    from air_rs import ops
+    from air_rs.gguf import GGMLType
+    from air_rs.parallel.tp import init_from_env
+    from air_rs.runtime.builder import random_engine
+    from air_rs.runtime.engine import SamplingParams
+
+    tp = init_from_env("nccl")
+    rank = tp.rank if tp else 0
+    world = tp.world_size if tp else 1
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if tp is not None:
+        from air_rs.parallel.symm import maybe_fused_tp
+        tp = maybe_fused_tp(tp, impl=args.impl)
+
+    B, P, K, W = args.batch, args.prompt_len, args.steps, args.warmup
+    max_len = P + 1 + W + K + 8 + (K + 8 if not args.no_e2e else 0)
+    qt = GGMLType[args.quant]
+    t0 = time.time()
+    eng = random_engine(args.model, qt, seed=0, device=dev, max_batch=B, max_model_len=max_len + 64, tp=tp)
+    rn = eng.runner
+    torch.cuda.synchronize()
+    build_s = time.time() - t0
+
+    def barrier():
+        if tp is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    gen = torch.Generator().manual_seed(1234)
+    V = eng.cfg.vocab_size
+    greedy = SamplingParams(max_tokens=10**6, temperature=0.0, repetition_penalty=1.1, ignore_eos=True)
+
+    # ---- p50 TTFT: one 512-token request, prefill + first token, device-timed ----
+    ttfts = []
+    for i in range(args.ttft_runs + 1):
+        ids = torch.randint(0, V, (P,), generator=gen).tolist()
+        rid = eng.add_request(ids, SamplingParams(max_tokens=1, temperature=0.0, ignore_eos=True))
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = eng.waiting[0]
+        adm = eng._admit()
+        eng._prefill(adm)
+        e1.record()
+        barrier()
+        if i > 0:  # first run includes one-time workspace allocation
+            ttfts.append(e0.elapsed_time(e1))
+        assert eng.finished[rid].output_ids
+    ttft_ms = statistics.median(ttfts)
+
+    # ---- decode throughput: B sequences, W warm-up + K timed steps ----
+    for _ in range(B):
+        eng.add_request(torch.randint(0, V, (P,), generator=gen).tolist(), greedy)
+    adm = eng._admit()
+    assert len(adm) == B, f"admitted {len(adm)} of {B}"
+    eng._prefill(adm)
+    batch = [r for r in eng.running if not r.finished]
+
+    def run_steps(n):
+        for _ in range(n):
+            for r in batch:
+                r.output_ids.append(0)  # positions advance; sampled ids stay on the device
+            eng._launch_decode(batch)
+
+    run_steps(W)
+    ops.reset_launch_count()
+    barrier()
+    from air_rs.ops import launch_count
+    with ClockSampler(local) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run_steps(K)
+        e1.record()
+        barrier()
+    ms = e0.elapsed_time(e1)
+    launches = launch_count()
+    rn.check_errors()
+    t = torch.tensor([ms, ttft_ms], device=dev)
+    if tp is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ttft_ms = float(t[0]), float(t[1])
+    tok_s = B * K / (ms / 1e3)
+    for r in batch:
+        eng.abort(r.rid)
+
+    # ---- end-to-end through the public API: H2D inputs + D2H tokens every step ----
+    e2e = None
+    if not args.no_e2e:
+        prompts = [torch.randint(0, V, (P,), generator=gen).tolist() for _ in range(B)]
+        for pids in prompts:
+            eng.add_request(pids, SamplingParams(max_tokens=K + 1, temperature=0.0,
+                                                  repetition_penalty=1.1, ignore_eos=True))
+        eng.step()  # admission + prefill + first decode step
+        barrier()
+        h0 = time.perf_counter()
+        steps = eng.run_pipelined(max_steps=K)
+        barrier()
+        dt = time.perf_counter() - h0
+        tt = torch.tensor([dt], device=dev)
+        if tp is not None:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e = {"value": B * steps / float(tt[0]), "unit": "tokens/s",
+               "h2d_bytes_per_step": eng.h2d_bytes_last_step,
+               "d2h_bytes_per_step": eng.d2h_bytes_last_step,
+               "api": "Engine.add_request + Engine.run_pipelined (pinned H2D inputs, D2H tokens per step)"}
+
+    if rank == 0:
+        out = {
+            "metric": "decode tokens/sec (box, device-timed, max over ranks) at 1/2/4/8 B200; p50 TTFT",
+            "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": round(tok_s / BASELINE_TOK_S, 2), "dtype": "bf16",
+            "data": "synthetic: uniform-random 512-token prompts; random-init N(0,0.02) weights quantised to Q4_K on device",
+            "config": {"model": f"{args.model} ({args.quant})", "global_batch": B, "seq_len": P,
+                       "decode_tokens_timed": K, "parallelism": f"tp{world}", "kv_block": rn.block_size,
+                       "l2": "inputs larger than L2 (4.6 GB weights + KV per step); no flush",
+                       "gemm": "baseline" if args.impl == "baseline" else "ours"},
+            "p50_ttft_ms": round(ttft_ms, 3),
+            "clocks": clk.summary(),
+            "gpu_launches": int(launches),
+            "e2e": e2e,
+            "build_s": round(build_s, 1),
+            "impl": args.impl,
+        }
+        print(json.dumps(out))
+    if tp is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,36 @@
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace air {
+
+// Which keys each query row sees.
+struct AttnRows {
+  const int* row_seq;        // [R] block-table row of each query row (null: r)
+  const int* ctx_len;        // [R] keys [0, ctx) are candidates (causal bound)
+  const int* tree_base;      // [R] first position of the speculative tree region (null: none)
+  const unsigned long long* tree_mask;  // [R] ancestor bitmask over tree positions
+  int window;                // sliding window (0 = none)
+};
+
+struct AttnArgs {
+  const float* q;            // [R, n_heads, head_dim] (RoPE applied, unscaled)
+  const void* kv;            // layer [num_blocks, 2, n_kv, block_size, head_dim] bf16
+  const int* block_tables;   // [n_seqs, max_blocks]
+  int max_blocks;
+  AttnRows rows;
+  int n_rows, n_heads, n_kv, head_dim, block_size;
+  int64_t num_blocks;
+  int n_splits, split_tokens;
+  float scale;
+  float* part_o;             // [R, n_heads, n_splits, head_dim] scratch (n_splits > 1)
+  float2* part_ml;           // [R, n_heads, n_splits]
+  float* out;                // [R, n_heads, head_dim] fp32
+  int8_t* out_q;             // optional Q8A of out
+  float2* out_ds;
+  int* err;
+};
+
+bool launch_paged_attention(const AttnArgs& a, cudaStream_t st);
+
+}  // namespace air

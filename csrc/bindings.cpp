@@ -1,0 +1,203 @@
+// torch <-> kernel adapter for the air_rs CUDA extension (module air_rs._C).
+// Every launch goes to the current torch CUDA stream, so all ops are capturable in CUDA
+// graphs; no op allocates device memory (callers own every buffer, including scratch).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "kernels.h"
+#include "attention.h"
+#include "sampler.h"
+#include "misc.h"
+#include "gemm_tc.h"
+#include "comm.h"
+
+void register_gemm_tc(pybind11::module_& m);
+void register_comm(pybind11::module_& m);
+
+using at::Tensor;
+using c10::optional;
+
+namespace {
+
+template <typename T = void>
+T* ptr(const optional<Tensor>& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+template <typename T = void>
+T* ptr(const Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+void post_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
+}
+
+void rmsnorm_quant(optional<Tensor> x, optional<Tensor> x_bf16, optional<Tensor> w, double w_offset,
+                   double eps, int64_t B, int64_t K, optional<Tensor> q, optional<Tensor> ds,
+                   optional<Tensor> y_bf16) {
+  TORCH_CHECK(K % 32 == 0, "rmsnorm_quant: K must be a multiple of 32");
+  air::launch_rmsnorm_quant(ptr<float>(x), ptr(x_bf16), ptr<float>(w), (float)w_offset, (int)B,
+                            (int)K, (float)eps, ptr<int8_t>(q), ptr<float2>(ds), ptr(y_bf16), stream());
+  post_launch("rmsnorm_quant");
+}
+
+void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, int64_t N, int64_t K,
+          int64_t B, Tensor xq, Tensor xds, int64_t mode, optional<Tensor> out_f32,
+          optional<Tensor> out_bf16, int64_t ld_out, optional<Tensor> resid,
+          optional<Tensor> w2_data, optional<Tensor> w2_scales, optional<Tensor> rope_cs,
+          optional<Tensor> positions, optional<Tensor> slots, optional<Tensor> kv,
+          optional<Tensor> q_out, int64_t n_heads, int64_t n_kv, int64_t head_dim,
+          int64_t block_size, int64_t rot_dim, optional<Tensor> err) {
+  check_cuda(data, "gemv weight");
+  TORCH_CHECK(B >= 1 && B <= 8, "gemv: batch must be in [1, 8]");
+  TORCH_CHECK(K % 32 == 0, "gemv: K must be a multiple of 32");
+  if (fmt == air::kFmtQ4K) TORCH_CHECK(K % 256 == 0 && row_bytes % 16 == 0, "gemv q4k: bad K");
+  air::GemvWeight w{(int)fmt, data.data_ptr(), ptr(scales), row_bytes};
+  air::GemvEpiParams ep{};
+  ep.mode = (int)mode;
+  ep.out_f32 = ptr<float>(out_f32);
+  ep.out_bf16 = ptr(out_bf16);
+  ep.ld_out = ld_out;
+  ep.resid = ptr<float>(resid);
+  ep.w2 = air::GemvWeight{(int)fmt, ptr(w2_data), ptr(w2_scales), row_bytes};
+  ep.rope_cs = ptr<float2>(rope_cs);
+  ep.positions = ptr<int>(positions);
+  ep.slots = ptr<int64_t>(slots);
+  ep.kv_cache = ptr(kv);
+  ep.num_blocks = kv.has_value() ? kv->size(0) : 0;
+  ep.q_out = ptr<float>(q_out);
+  ep.n_heads = (int)n_heads;
+  ep.n_kv = (int)n_kv;
+  ep.head_dim = (int)head_dim;
+  ep.block_size = (int)block_size;
+  ep.rot_dim = (int)rot_dim;
+  ep.err = ptr<int>(err);
+  if (mode == air::kEpiSwiGLU) TORCH_CHECK(ep.w2.data, "gemv swiglu: w2 required");
+  if (mode == air::kEpiResidual) TORCH_CHECK(ep.resid, "gemv residual: resid required");
+  if (mode == air::kEpiQKVRope)
+    TORCH_CHECK(ep.kv_cache && ep.q_out && ep.rope_cs && ep.positions && ep.slots,
+                "gemv qkv: rope/kv/q buffers required");
+  air::launch_gemv(w, (int)N, (int)K, (int)B, ptr<int8_t>(xq), ptr<float2>(xds), ep, stream());
+  post_launch("gemv");
+}
+
+void paged_attention(Tensor q, Tensor kv, Tensor block_tables, optional<Tensor> row_seq,
+                     Tensor ctx_len, optional<Tensor> tree_base, optional<Tensor> tree_mask,
+                     int64_t window, int64_t n_rows, int64_t n_heads, int64_t n_kv, int64_t head_dim,
+                     int64_t block_size, int64_t n_splits, int64_t split_tokens, double scale,
+                     optional<Tensor> part_o, optional<Tensor> part_ml, Tensor out,
+                     optional<Tensor> out_q, optional<Tensor> out_ds, optional<Tensor> err) {
+  check_cuda(q, "q");
+  check_cuda(kv, "kv");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt, "block_tables must be int32");
+  air::AttnArgs a{};
+  a.q = ptr<float>(q);
+  a.kv = kv.data_ptr();
+  a.block_tables = ptr<int>(block_tables);
+  a.max_blocks = (int)block_tables.size(1);
+  a.rows = air::AttnRows{ptr<int>(row_seq), ptr<int>(ctx_len), ptr<int>(tree_base),
+                         ptr<unsigned long long>(tree_mask), (int)window};
+  a.n_rows = (int)n_rows;
+  a.n_heads = (int)n_heads;
+  a.n_kv = (int)n_kv;
+  a.head_dim = (int)head_dim;
+  a.block_size = (int)block_size;
+  a.num_blocks = kv.size(0);
+  a.n_splits = (int)n_splits;
+  a.split_tokens = (int)split_tokens;
+  a.scale = (float)scale;
+  a.part_o = ptr<float>(part_o);
+  a.part_ml = ptr<float2>(part_ml);
+  a.out = ptr<float>(out);
+  a.out_q = ptr<int8_t>(out_q);
+  a.out_ds = ptr<float2>(out_ds);
+  a.err = ptr<int>(err);
+  if (n_splits > 1) TORCH_CHECK(a.part_o && a.part_ml, "paged_attention: split scratch required");
+  TORCH_CHECK(air::launch_paged_attention(a, stream()), "paged_attention: unsupported head_dim/GQA");
+  post_launch("paged_attention");
+}
+
+void sampler(Tensor logits, int64_t B, int64_t V, optional<Tensor> counts, optional<Tensor> count_row,
+             optional<Tensor> mask,
+             optional<Tensor> temperature, optional<Tensor> penalty, optional<Tensor> top_k,
+             optional<Tensor> top_p, int64_t seed, optional<Tensor> step, Tensor out_tokens,
+             optional<Tensor> out_prob) {
+  check_cuda(logits, "logits");
+  air::SamplerArgs a{ptr<uint8_t>(counts), ptr<int>(count_row), ptr<uint32_t>(mask), ptr<float>(temperature),
+                     ptr<float>(penalty), ptr<int>(top_k), ptr<float>(top_p),
+                     (unsigned long long)seed, ptr<long long>(step), ptr<int>(out_tokens),
+                     ptr<float>(out_prob)};
+  air::launch_sampler(ptr<float>(logits), (int)B, (int)V, logits.stride(0), a, stream());
+  post_launch("sampler");
+}
+
+void count_tokens(Tensor counts, Tensor tokens, int64_t n, int64_t per_row,
+                  optional<Tensor> count_row) {
+  air::launch_count_tokens(ptr<uint8_t>(counts), (int)counts.size(1), ptr<int>(tokens), (int)n,
+                           (int)per_row, ptr<int>(count_row), stream());
+  post_launch("count_tokens");
+}
+
+void embed(int64_t fmt, Tensor table, optional<Tensor> scales, int64_t row_bytes, int64_t K,
+           Tensor ids, int64_t n, int64_t vocab, optional<Tensor> out_f32, optional<Tensor> out_bf16,
+           double mult, optional<Tensor> err) {
+  air::launch_embed((int)fmt, table.data_ptr(), ptr(scales), row_bytes, (int)K, ptr<int>(ids), (int)n,
+                    vocab, ptr<float>(out_f32), ptr(out_bf16), (float)mult, ptr<int>(err), stream());
+  post_launch("embed");
+}
+
+void dequant(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, int64_t N, int64_t K,
+             Tensor out) {
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16, "dequant: out must be bf16");
+  air::launch_dequant((int)fmt, w.data_ptr(), ptr(scales), row_bytes, (int)N, (int)K, out.data_ptr(),
+                      stream());
+  post_launch("dequant");
+}
+
+void rope_kv(Tensor qkv, int64_t T, Tensor rope_cs, Tensor positions, Tensor slots, Tensor kv,
+             Tensor q_out, int64_t n_heads, int64_t n_kv, int64_t head_dim, int64_t block_size,
+             int64_t rot_dim, optional<Tensor> err) {
+  air::RopeKvArgs a{ptr<float2>(rope_cs), ptr<int>(positions), ptr<int64_t>(slots), kv.data_ptr(),
+                    ptr<float>(q_out), (int)n_heads, (int)n_kv, (int)head_dim, (int)block_size,
+                    (int)rot_dim, kv.size(0), ptr<int>(err)};
+  air::launch_rope_kv(qkv.data_ptr(), qkv.scalar_type() == at::kBFloat16, (int)T, a, stream());
+  post_launch("rope_kv");
+}
+
+void swiglu(Tensor gu, int64_t T, int64_t F, int64_t ld_out, optional<Tensor> out_bf16,
+            optional<Tensor> out_f32) {
+  air::launch_swiglu(gu.data_ptr(), gu.scalar_type() == at::kBFloat16, (int)T, (int)F, ld_out, ptr(out_bf16),
+                     ptr<float>(out_f32), stream());
+  post_launch("swiglu");
+}
+
+void residual_add(Tensor resid, Tensor y, int64_t n) {
+  air::launch_residual_add(ptr<float>(resid), y.data_ptr(), y.scalar_type() == at::kBFloat16, n, stream());
+  post_launch("residual_add");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "air_rs sm_100a kernels";
+  m.def("rmsnorm_quant", &rmsnorm_quant);
+  m.def("gemv", &gemv);
+  m.def("paged_attention", &paged_attention);
+  m.def("sampler", &sampler);
+  m.def("count_tokens", &count_tokens);
+  m.def("embed", &embed);
+  m.def("dequant", &dequant);
+  m.def("rope_kv", &rope_kv);
+  m.def("swiglu", &swiglu);
+  m.def("residual_add", &residual_add);
+  register_gemm_tc(m);
+  register_comm(m);
+}

@@ -1,0 +1,10 @@
+// air_rs._host: the CPU-side native runtime (no CUDA dependency, so it also loads on
+// machines without a GPU): paged-KV bookkeeping and the batch scheduler core.
+#include <torch/extension.h>
+
+void register_host_kv(pybind11::module_& m);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "air_rs native host runtime";
+  register_host_kv(m);
+}

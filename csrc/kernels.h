@@ -1,0 +1,57 @@
+// Host-side launch API of the air_rs CUDA kernels (no torch headers here, so the .cu
+// files compile quickly; csrc/bindings.cpp adapts these to torch tensors).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace air {
+
+// ---- weight formats understood by the decode GEMVs ----
+enum WeightFormat : int {
+  kFmtQ4K = 0,    // raw GGUF Q4_K blocks, [N, K/256*144] bytes
+  kFmtQ8_0 = 1,   // repacked Q8_0: int8 qs [N, K] + f16 scales [N, K/32]
+  kFmtBF16 = 2,   // dense bf16 [N, K]
+};
+
+enum GemvEpilogue : int {
+  kEpiStore = 0,      // out[b, n] = acc (fp32 or bf16)
+  kEpiResidual = 1,   // resid[b, n] += acc (fp32 residual stream)
+  kEpiSwiGLU = 2,     // out[b, n] = silu(W·x)[n] * (W2·x)[n]
+  kEpiQKVRope = 3,    // rows = [q | k | v]; NeoX RoPE on q,k; k,v written to the paged cache
+};
+
+struct GemvWeight {
+  int fmt;
+  const void* data;      // q4k blocks / q8 qs / bf16 values
+  const void* scales;    // q8_0 f16 scales (else null)
+  int64_t row_bytes;     // bytes per row of `data`
+};
+
+struct GemvEpiParams {
+  int mode;
+  float* out_f32;             // [B, ld_out]
+  void* out_bf16;             // [B, ld_out]
+  int64_t ld_out;
+  float* resid;               // [B, ld_out]
+  // SwiGLU second operand
+  GemvWeight w2;
+  // QKV + RoPE
+  const float2* rope_cs;      // [max_pos, rot_dim/2] (cos, sin)
+  const int* positions;       // [B]
+  const int64_t* slots;       // [B] paged-cache slot (block*block_size + off); <0 = skip
+  void* kv_cache;             // this layer: [num_blocks, 2, n_kv, block_size, head_dim] bf16
+  float* q_out;               // [B, n_heads, head_dim] fp32
+  int n_heads, n_kv, head_dim, block_size, rot_dim;
+  int64_t num_blocks;
+  int* err;
+};
+
+// x: activations quantised by rmsnorm_quant (int8 [B,K] + float2 [B,K/32]).
+void launch_gemv(const GemvWeight& w, int N, int K, int B, const int8_t* xq, const float2* xds,
+                 const GemvEpiParams& ep, cudaStream_t st);
+
+void launch_rmsnorm_quant(const float* x, const void* x_bf16, const float* w, float w_offset,
+                          int B, int K, float eps, int8_t* q, float2* ds, void* y_bf16,
+                          cudaStream_t st);
+
+}  // namespace air

@@ -1,0 +1,26 @@
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace air {
+
+struct SamplerArgs {
+  const uint8_t* counts;          // [S, V] past-occurrence counts (null: no penalty)
+  const int* count_row;           // [B] row of `counts` for each batch row (null: b)
+  const uint32_t* allow_mask;     // [B, ceil(V/32)] grammar allow bits (null: all allowed)
+  const float* temperature;       // [B] (null: greedy)
+  const float* rep_penalty;       // [B]
+  const int* top_k;               // [B]
+  const float* top_p;             // [B]
+  unsigned long long seed;
+  long long* step;                // device step counter (Philox offset), bumped per call
+  int* out_tokens;                // [B]
+  float* out_prob;                // [B] probability of the chosen token's top-1 (optional)
+};
+
+void launch_sampler(const float* logits, int B, int V, int64_t ld, const SamplerArgs& a,
+                    cudaStream_t st);
+void launch_count_tokens(uint8_t* counts, int V, const int* tokens, int n, int per_row,
+                         const int* count_row, cudaStream_t st);
+
+}  // namespace air
