@@ -243,11 +243,20 @@ class ModelRunner:
             return self.inputs[B]
         g = self.graphs.get(B)
         if g is None:
+            # The warm-up run (lazy init outside capture) mutates step state: sampled ids,
+            # penalty counts, the Philox step counter. Snapshot and restore it so the first
+            # real step sees exactly the inputs the host staged.
+            si = self.inputs[B]
+            saved = (si.ids.clone(), self.counts.clone(), self.step_ctr.clone())
             s = torch.cuda.Stream(self.device)
             s.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(s):
-                self._decode_body(B)  # warm-up outside capture (allocator, lazy init)
+                self._decode_body(B)
             torch.cuda.current_stream(self.device).wait_stream(s)
+            si.ids.copy_(saved[0])
+            self.counts.copy_(saved[1])
+            self.step_ctr.copy_(saved[2])
+            del saved
             g = torch.cuda.CUDAGraph()
             c0 = ops.launch_count()
             with torch.cuda.graph(g):

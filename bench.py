@@ -148,7 +148,7 @@ def main():
 
     gen = torch.Generator().manual_seed(1234)
     V = eng.cfg.vocab_size
-    greedy = SamplingParams(max_tokens=10**6, temperature=0.0, repetition_penalty=1.1, ignore_eos=True)
+    greedy = SamplingParams(max_tokens=W + K + 16, temperature=0.0, repetition_penalty=1.1, ignore_eos=True)
 
     # ---- p50 TTFT: one 512-token request, prefill + first token, device-timed ----
     ttfts = []
@@ -171,9 +171,13 @@ def main():
     # ---- decode throughput: B sequences, W warm-up + K timed steps ----
     for _ in range(B):
         eng.add_request(torch.randint(0, V, (P,), generator=gen).tolist(), greedy)
-    adm = eng._admit()
-    assert len(adm) == B, f"admitted {len(adm)} of {B}"
-    eng._prefill(adm)
+    n_adm = 0
+    while eng.waiting:
+        adm = eng._admit()
+        assert adm, "admission stalled"
+        n_adm += len(adm)
+        eng._prefill(adm)
+    assert n_adm == B, f"admitted {n_adm} of {B}"
     batch = [r for r in eng.running if not r.finished]
 
     def run_steps(n):
