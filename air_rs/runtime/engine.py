@@ -258,32 +258,50 @@ class Engine:
                 return b
         return self.runner.max_batch
 
+    STAGING_RING = 4
+
     def _pinned_for(self, B: int):
+        """Per-bucket state: a ring of pinned staging slots, each guarded by an event.
+
+        The host runs ahead of the GPU, so a staging buffer is rewritten only after the
+        event recorded behind its last H2D copies has completed.
+        """
         p = self._pinned.get(B)
         if p is None:
             rn = self.runner
-            p = {
-                "i32": torch.zeros(3 * B, dtype=torch.int32).pin_memory(),
-                "slots": torch.zeros(B, dtype=torch.int64).pin_memory(),
-                "tab": torch.zeros(B, rn.max_blocks, dtype=torch.int32).pin_memory(),
-                "samp_f": torch.zeros(3 * B, dtype=torch.float32).pin_memory(),
-                "samp_i": torch.zeros(B, dtype=torch.int32).pin_memory(),
-                "tok": torch.zeros(B, dtype=torch.int32).pin_memory(),
-                "members": None,
-            }
+            ring = []
+            for _ in range(self.STAGING_RING):
+                ring.append({
+                    "i32": torch.zeros(4 * B, dtype=torch.int32).pin_memory(),
+                    "slots": torch.zeros(B, dtype=torch.int64).pin_memory(),
+                    "tab": torch.zeros(B, rn.max_blocks, dtype=torch.int32).pin_memory(),
+                    "samp_f": torch.zeros(3 * B, dtype=torch.float32).pin_memory(),
+                    "samp_i": torch.zeros(B, dtype=torch.int32).pin_memory(),
+                    "tok": torch.zeros(B, dtype=torch.int32).pin_memory(),
+                    "ev": None,
+                })
+            p = {"ring": ring, "next": 0, "members": None}
             self._pinned[B] = p
         return p
 
     def _launch_decode(self, batch: list[Request]):
-        """Stage inputs (one H2D copy per buffer) and replay the bucket's graph."""
+        """Stage inputs (one H2D copy per buffer) and replay the bucket's graph.
+
+        Returns (B, staging slot, event); the slot's ``tok`` receives the sampled ids once
+        the event completes.
+        """
         rn = self.runner
         n = len(batch)
         B = self._bucket(n)
         si = rn.step_inputs(B)
         p = self._pinned_for(B)
+        st = p["ring"][p["next"]]
+        p["next"] = (p["next"] + 1) % len(p["ring"])
+        if st["ev"] is not None:
+            st["ev"].synchronize()
         seqs = [r.seq for r in batch] + [-1] * (B - n)
         slots = self.seqs.step_slots(seqs)
-        i32 = p["i32"]
+        i32 = st["i32"]
         h2d = 0
         for i, r in enumerate(batch):
             pos = r.num_tokens - 1
@@ -294,18 +312,18 @@ class Engine:
             i32[i] = 0
             i32[B + i] = 0
             i32[2 * B + i] = self.pad_slot
-        p["slots"][:] = torch.tensor(slots, dtype=torch.int64)
+        st["slots"][:] = torch.tensor(slots, dtype=torch.int64)
         si.positions.copy_(i32[:B], non_blocking=True)
         si.ctx_len.copy_(i32[B:2 * B], non_blocking=True)
-        si.count_row.copy_(i32[2 * B:], non_blocking=True)
-        si.slots.copy_(p["slots"], non_blocking=True)
+        si.count_row.copy_(i32[2 * B:3 * B], non_blocking=True)
+        si.slots.copy_(st["slots"], non_blocking=True)
         h2d += 3 * B * 4 + B * 8
-        members = tuple(r.rid for r in batch)
-        if p["members"] != (members, [r.seq for r in batch]):
-            self.seqs.fill_table(seqs, p["tab"])
-            si.block_tables.copy_(p["tab"], non_blocking=True)
-            h2d += p["tab"].numel() * 4
-            sf, sii = p["samp_f"], p["samp_i"]
+        key = (tuple(r.rid for r in batch), tuple(r.seq for r in batch))
+        if p["members"] != key:
+            self.seqs.fill_table(seqs, st["tab"])
+            si.block_tables.copy_(st["tab"], non_blocking=True)
+            h2d += st["tab"].numel() * 4
+            sf, sii = st["samp_f"], st["samp_i"]
             for i in range(B):
                 pr = batch[min(i, n - 1)].params
                 sf[i], sf[B + i], sf[2 * B + i] = pr.temperature, pr.repetition_penalty, pr.top_p
@@ -316,21 +334,23 @@ class Engine:
             si.top_k.copy_(sii, non_blocking=True)
             h2d += 4 * B * 4
             # ids: last token of each sequence (from the host; after this the graph feeds itself)
-            ids = torch.tensor([r.output_ids[-1] for r in batch] + [0] * (B - n), dtype=torch.int32)
-            si.ids.copy_(ids.pin_memory(), non_blocking=True)
+            for i in range(B):
+                i32[3 * B + i] = batch[i].output_ids[-1] if i < n else 0
+            si.ids.copy_(i32[3 * B:], non_blocking=True)
             h2d += B * 4
-            p["members"] = (members, [r.seq for r in batch])
+            p["members"] = key
         elif self.seqs_changed_blocks(batch):
-            self.seqs.fill_table(seqs, p["tab"])
-            si.block_tables.copy_(p["tab"], non_blocking=True)
-            h2d += p["tab"].numel() * 4
+            self.seqs.fill_table(seqs, st["tab"])
+            si.block_tables.copy_(st["tab"], non_blocking=True)
+            h2d += st["tab"].numel() * 4
         rn.decode(B, use_graph=True)
-        p["tok"].copy_(si.tokens, non_blocking=True)
+        st["tok"].copy_(si.tokens, non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()
+        st["ev"] = ev
         self.h2d_bytes_last_step = h2d
         self.d2h_bytes_last_step = B * 4
-        return B, p, ev
+        return B, st, ev
 
     def seqs_changed_blocks(self, batch) -> bool:
         # a new block was opened for some sequence iff its new token starts a block

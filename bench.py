@@ -182,9 +182,9 @@ def main():
 
     def run_steps(n):
         for _ in range(n):
-            for r in batch:
-                r.output_ids.append(0)  # positions advance; sampled ids stay on the device
             eng._launch_decode(batch)
+            for r in batch:
+                r.output_ids.append(0)  # the token sampled on the device; ids stay there
 
     run_steps(W)
     ops.reset_launch_count()
