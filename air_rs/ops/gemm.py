@@ -1,9 +1,10 @@
 """GEMM entry point of the prefill / large-batch path.
 
-``linear`` runs the tcgen05 dequant-fused GEMM (``air_rs._C.gemm_q``) when it supports the
-weight format and shape; the ``baseline`` implementation (dequantise the weight to a bf16
-scratch with our kernel, then a library matmul) exists only as the comparison arm and for
-formats the fused kernel does not cover yet.
+``linear`` runs the tcgen05 dequant-fused GEMM (``air_rs._C.gemm_q``) for Q4_K and bf16
+weights; split-K partials go to a per-device workspace owned here (allocated once, before
+any CUDA-graph capture, and grown only outside capture). The ``baseline`` implementation
+(dequantise to a bf16 scratch with our kernel, then a library matmul) exists as the
+comparison arm (``AIR_GEMM_IMPL=baseline``) and for formats without a fused kernel (Q8_0).
 """
 from __future__ import annotations
 
@@ -11,22 +12,80 @@ import os
 
 import torch
 
-from . import QWeight, require_ext, FMT_BF16, count_launch
+from . import QWeight, require_ext, FMT_BF16, FMT_Q4K, count_launch
 
-_FORCE_BASELINE = os.environ.get("AIR_GEMM_IMPL", "") == "baseline"
-
-
-def tc_supported(w: QWeight, T: int) -> bool:
-    ext = require_ext()
-    return hasattr(ext, "gemm_q") and not _FORCE_BASELINE and w.K % 256 == 0 and w.N % 128 == 0
+GEMM_STORE_F32, GEMM_STORE_BF16, GEMM_RESIDUAL = 0, 1, 2
 
 
-def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None) -> torch.Tensor:
+def _baseline_forced() -> bool:
+    return os.environ.get("AIR_GEMM_IMPL", "") == "baseline"
+
+
+def tc_supported(w: QWeight) -> bool:
+    if _baseline_forced():
+        return False
+    if w.fmt == FMT_Q4K:
+        return w.K % 256 == 0
+    if w.fmt == FMT_BF16:
+        return w.K % 64 == 0
+    return False
+
+
+class _Workspace:
+    """Split-K scratch for one device: fp32 partials + self-resetting tile counters."""
+
+    def __init__(self, device):
+        self.device = device
+        self.ws = torch.zeros(0, dtype=torch.float32, device=device)
+        self.cnt = torch.zeros(0, dtype=torch.int32, device=device)
+
+    def ensure(self, floats: int, counters: int):
+        if self.ws.numel() < floats:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("gemm workspace must be sized before CUDA-graph capture")
+            self.ws = torch.zeros(max(floats, 2 * self.ws.numel()), dtype=torch.float32, device=self.device)
+        if self.cnt.numel() < counters:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("gemm counters must be sized before CUDA-graph capture")
+            self.cnt = torch.zeros(max(counters, 2 * self.cnt.numel(), 1024), dtype=torch.int32,
+                                   device=self.device)
+        return self.ws, self.cnt
+
+
+_WS: dict = {}
+
+
+def workspace(device) -> _Workspace:
+    key = torch.device(device)
+    w = _WS.get(key)
+    if w is None:
+        w = _WS[key] = _Workspace(key)
+    return w
+
+
+def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, residual: bool = False,
+           splits: int | None = None, err: torch.Tensor | None = None) -> torch.Tensor:
+    """out = x @ W^T (or out += x @ W^T when residual, out fp32)."""
     T = x.shape[0]
-    if tc_supported(w, T):
+    if T == 0:
+        return out
+    if tc_supported(w):
         ext = require_ext()
-        ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out)
+        if residual:
+            mode = GEMM_RESIDUAL
+        else:
+            mode = GEMM_STORE_BF16 if out.dtype == torch.bfloat16 else GEMM_STORE_F32
+        s = splits if splits is not None else ext.gemm_q_splits(w.N, w.K, T, w.fmt)
+        ws = cnt = None
+        if s > 1:
+            ws, cnt = workspace(x.device).ensure(ext.gemm_q_workspace(w.N, w.K, T, w.fmt, s),
+                                                 ext.gemm_q_counters(w.N, T))
+        ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out, mode, s, ws, cnt, err)
         count_launch()
+        return out
+    if residual:
+        tmp = linear_baseline(x, w, torch.empty(T, w.N, dtype=torch.float32, device=x.device), runner)
+        out.add_(tmp)
         return out
     return linear_baseline(x, w, out, runner)
 

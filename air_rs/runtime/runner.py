@@ -133,10 +133,20 @@ class ModelRunner:
         return int(max(1, min(self.max_splits, math.ceil(target / max(1, B * self.nkv)))))
 
     # ------------------------------------------------------------------ linear (GEMM path)
-    def linear(self, x_bf16: torch.Tensor, w: ops.QWeight, out: torch.Tensor) -> torch.Tensor:
-        """out[T, N] = x[T, K] @ W^T for the prefill / large-batch path."""
+    def linear(self, x_bf16: torch.Tensor, w: ops.QWeight, out: torch.Tensor,
+               residual: bool = False) -> torch.Tensor:
+        """out[T, N] = x[T, K] @ W^T (out += ... when residual) for the GEMM path."""
         from ..ops import gemm
-        return gemm.linear(x_bf16, w, out, self)
+        return gemm.linear(x_bf16, w, out, self, residual=residual, err=self.err)
+
+    def _proj_into_residual(self, xin, w, x, obuf, tp: bool):
+        """x += xin @ W^T: fused into the GEMM epilogue, or partial + all-reduce under TP."""
+        if tp:
+            T = xin.shape[0]
+            self.linear(xin, w, obuf[:T])
+            self._residual_T(obuf[:T], T, x, tp)
+        else:
+            self.linear(xin, w, x, residual=True)
 
     # ------------------------------------------------------------------ collectives
     def _reduce_into_residual(self, partial: torch.Tensor, B: int, x: torch.Tensor):
@@ -182,8 +192,7 @@ class ModelRunner:
                 self._ffn_gemv(lw, B, x, xq, xds, tp)
             else:
                 self.attn_b[:B].copy_(self.attn[:B])
-                self.linear(self.attn_b[:B], lw.wo, self.o_b[:B])
-                self._residual(self.o_b, B, x, tp)
+                self._proj_into_residual(self.attn_b[:B], lw.wo, x, self.o_b, tp)
                 ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=self.xn_b[:B])
                 self._ffn_gemm(lw, B, x, tp)
         self._head(B, x, xq, xds, gemv_path)
@@ -215,8 +224,7 @@ class ModelRunner:
             return
         self.linear(self.xn_b[:B], lw.wgu, self.gu_b[:B])
         ops.swiglu(self.gu_b[:B], B, self.F, out_bf16=self.h_b[:B], ld_out=self.Fp)
-        self.linear(self.h_b[:B], lw.wdown, self.o_b[:B])
-        self._residual(self.o_b, B, x, tp)
+        self._proj_into_residual(self.h_b[:B], lw.wdown, x, self.o_b, tp)
 
     def _head(self, B, x, xq, xds, gemv_path):
         w, si = self.w, self.inputs[B]
@@ -315,8 +323,7 @@ class ModelRunner:
                                 row_seq=row_seq, n_splits=1, err=self.err,
                                 window=cfg.sliding_window or 0)
             attn_b.copy_(attn)
-            self.linear(attn_b, lw.wo, o)
-            self._residual_T(o, T, x, tp)
+            self._proj_into_residual(attn_b, lw.wo, x, o, tp)
             ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=xn)
             if lw.wgu is None:
                 from ..parallel import moe
@@ -324,8 +331,7 @@ class ModelRunner:
             else:
                 self.linear(xn, lw.wgu, gu)
                 ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp)
-                self.linear(hb, lw.wdown, o)
-                self._residual_T(o, T, x, tp)
+                self._proj_into_residual(hb, lw.wdown, x, o, tp)
         xl = x.index_select(0, last_rows.long())
         xs = self._ws("xs", (S, self.H), bf16)
         ops.rmsnorm_quant(xl, w.out_norm, eps, None, None, y_bf16=xs)

@@ -62,10 +62,10 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
   }
   __syncthreads();
 
-  // split_tokens <= 0: divide this row's context evenly over the splits (multiple of 128),
+  // split_tokens <= 0: divide this row's context evenly over the splits (multiple of 32),
   // so one captured launch serves every context length.
   const int st = split_tokens > 0 ? split_tokens
-                                  : ((ctx + n_splits - 1) / n_splits + 127) / 128 * 128;
+                                  : ((ctx + n_splits - 1) / n_splits + 31) / 32 * 32;
   int t_begin = split * st;
   int t_end = min(ctx, t_begin + st);
   if (rows.window > 0) t_begin = max(t_begin, ctx - rows.window);

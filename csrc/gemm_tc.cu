@@ -1,0 +1,414 @@
+// Dequant-fused tensor-core GEMM for the prefill / batched-decode path (sm_100a):
+//     out[t, n] (op)= sum_k x[t, k] * W[n, k]
+// with W in raw GGUF Q4_K blocks (or dense bf16) and x bf16 activations.
+//
+// Swap-AB tiling: the MMA's M = 128 weight rows, its N = a tile of NT tokens, so small
+// decode batches (16..128 tokens) still fill the 128-row tcgen05 datapath. Per CTA:
+//   warp 0      TMA producer: raw weight box (128 rows x one 256-weight super-block, the
+//               144-byte GGUF blocks copied verbatim) + the matching x boxes (SW128 swizzle)
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer (f32 accumulators in TMEM)
+//   warps 2..5  dequantise the staged Q4_K blocks into bf16 K-major SW128 tiles with packed
+//               bf16x2 arithmetic (the GGUF scale/min math), then run the epilogue
+//               (tcgen05.ld -> store / residual add / split-K reduction).
+// Stages are handed over with mbarriers (TMA complete_tx, tcgen05.commit). Split-K uses a
+// caller-provided fp32 workspace and per-tile arrival counters; the last CTA of a tile
+// reduces the partials and resets its counter, so the scratch needs no clearing per call.
+//
+// Replaces the reference's candle QMatMul GEMM path (src/model.rs:534-536, 591-594,
+// src/ops.rs:594-611 via candle-core's CUDA quantized matmul).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include "common.cuh"
+#include "sm100.cuh"
+#include "gemm_tc.h"
+
+namespace air {
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kThreads = 192;
+constexpr int kRawRowBytes = 144;           // one Q4_K super-block of one row
+constexpr int kRawTile = 128 * kRawRowBytes; // 18432 B (multiple of 1024)
+constexpr int kATile = 128 * 128;            // 128 rows x 64 bf16
+
+template <int NT, int FMT>
+struct Cfg {
+  static constexpr int kChunks = FMT == kFmtQ4K ? 4 : 1;         // 64-wide K chunks per stage
+  static constexpr int kBChunk = NT * 128;                       // NT rows x 128 B
+  static constexpr int kStageBytes = (FMT == kFmtQ4K ? kRawTile : kATile) + kChunks * kBChunk;
+  static constexpr int kABuf = FMT == kFmtQ4K ? 2 * kATile : 0;
+  static constexpr int kBudget = 227 * 1024 - 2048 - 1024;
+  static constexpr int kStages = (kBudget - kABuf) / kStageBytes > 8 ? 8 : (kBudget - kABuf) / kStageBytes;
+  static constexpr int kSmem = 1024 + kStages * kStageBytes + kABuf + 1024;
+  static constexpr int kTmemCols = NT < 32 ? 32 : NT;
+  static_assert(kStages >= 2, "not enough shared memory for two stages");
+};
+
+struct Bars {
+  uint64_t full[8];
+  uint64_t empty[8];
+  uint64_t afull[2];
+  uint64_t aempty[2];
+  uint64_t done;
+  uint32_t tmem;
+  int abort;
+  int last;
+};
+
+__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// One 16-byte output chunk (8 bf16) = s * q - mm for 8 nibbles taken from 2 words.
+__device__ __forceinline__ uint32_t q4_pair(uint32_t t, __nv_bfloat162 s, __nv_bfloat162 negm) {
+  const uint32_t v = (t & 0x000F000Fu) | 0x43004300u;         // bf16x2 (128 + q0, 128 + q1)
+  __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&v);
+  const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
+  b = __hsub2(b, c128);                                          // exact q
+  b = __hfma2(b, s, negm);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+template <int NT, int FMT>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+              GemmArgs a) {
+  using C = Cfg<NT, FMT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* abuf = stages + C::kStages * C::kStageBytes;
+  Bars* bars = reinterpret_cast<Bars*>(abuf + C::kABuf);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * 128, n0 = blockIdx.y * NT;
+  const int split = blockIdx.z, splits = gridDim.z;
+  const int ksteps = FMT == kFmtQ4K ? a.K / 256 : a.K / 64;
+  const int kper = (ksteps + splits - 1) / splits;
+  const int kb0 = split * kper;
+  const int nk = max(0, min(ksteps, kb0 + kper) - kb0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], FMT == kFmtQ4K ? 5 : 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->afull[i], 4);
+      mbar_init(&bars->aempty[i], 1);
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_x);
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint32_t tx = C::kStageBytes;
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::kStages;
+        if (i >= C::kStages && !mbar_wait(&bars->empty[s], ((i / C::kStages) - 1) & 1)) {
+          set_error(a.err, kErrTimeout);
+          bars->abort = 1;
+          break;
+        }
+        if (*(volatile int*)&bars->abort) break;
+        uint8_t* st = stages + s * C::kStageBytes;
+        mbar_expect_tx(&bars->full[s], tx);
+        const int kb = kb0 + i;
+        if (FMT == kFmtQ4K) {
+          tma_load_2d(st, &tm_w, &bars->full[s], kb * kRawRowBytes, m0);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tma_load_2d(st + kRawTile + c * C::kBChunk, &tm_x, &bars->full[s], kb * 256 + 64 * c, n0);
+        } else {
+          tma_load_2d(st, &tm_w, &bars->full[s], kb * 64, m0);
+          tma_load_2d(st + kATile, &tm_x, &bars->full[s], kb * 64, n0);
+        }
+        issued = i + 1;
+      }
+      // never leave the CTA with copies in flight into its shared memory
+      for (int i = max(0, issued - C::kStages); i < issued; ++i)
+        mbar_wait(&bars->full[i % C::kStages], (i / C::kStages) & 1, 1u << 22);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, NT);
+      int g = 0;
+      bool ok = true;
+      for (int i = 0; i < nk && ok; ++i) {
+        const int s = i % C::kStages;
+        if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1)) { ok = false; break; }
+        uint8_t* st = stages + s * C::kStageBytes;
+        for (int c = 0; c < C::kChunks; ++c, ++g) {
+          const uint8_t* A;
+          if (FMT == kFmtQ4K) {
+            const int ab = g & 1;
+            if (!mbar_wait(&bars->afull[ab], (g >> 1) & 1)) { ok = false; break; }
+            A = abuf + ab * kATile;
+          } else {
+            A = st;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(A);
+          const uint64_t bd = sw128_desc(st + (FMT == kFmtQ4K ? kRawTile : kATile) + c * C::kBChunk);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)  // 4 x K16 per 64-wide chunk: +32 B along K
+            mma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i | c | k) != 0 ? 1u : 0u);
+          if (FMT == kFmtQ4K) mma_commit(&bars->aempty[g & 1]);
+        }
+        mma_commit(&bars->empty[s]);
+      }
+      if (!ok) {
+        set_error(a.err, kErrTimeout);
+        bars->abort = 1;
+      }
+      mma_commit(&bars->done);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant (Q4_K)
+    const int t = threadIdx.x - 64;  // weight row within the tile
+    if (FMT == kFmtQ4K) {
+      int g = 0;
+      bool ok = true;
+      for (int i = 0; i < nk && ok; ++i) {
+        const int s = i % C::kStages;
+        if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1)) { ok = false; break; }
+        const uint8_t* rb = stages + s * C::kStageBytes + t * kRawRowBytes;
+        const uint32_t hdr = *reinterpret_cast<const uint32_t*>(rb);
+        const float d = __half2float(__ushort_as_half((unsigned short)(hdr & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr >> 16)));
+        for (int c = 0; c < 4; ++c, ++g) {
+          const int ab = g & 1;
+          if (g >= 2 && !mbar_wait(&bars->aempty[ab], ((g >> 1) - 1) & 1)) { ok = false; break; }
+          int sl, ml, sh, mh;
+          q4k_scale_min(rb + 4, 2 * c, sl, ml);
+          q4k_scale_min(rb + 4, 2 * c + 1, sh, mh);
+          const __nv_bfloat162 s_lo = __float2bfloat162_rn(d * (float)sl);
+          const __nv_bfloat162 m_lo = __float2bfloat162_rn(-dmin * (float)ml);
+          const __nv_bfloat162 s_hi = __float2bfloat162_rn(d * (float)sh);
+          const __nv_bfloat162 m_hi = __float2bfloat162_rn(-dmin * (float)mh);
+          const uint4 qa = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
+          const uint4 qb = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
+          const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          uint8_t* arow = abuf + ab * kATile + t * 128;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            // bytes 8cc .. 8cc+7: low nibbles -> k = 8cc.., high nibbles -> k = 32 + 8cc..
+            const uint32_t t0 = __byte_perm(w[2 * cc], 0, 0x4140), t1 = __byte_perm(w[2 * cc], 0, 0x4342);
+            const uint32_t t2 = __byte_perm(w[2 * cc + 1], 0, 0x4140), t3 = __byte_perm(w[2 * cc + 1], 0, 0x4342);
+            uint4 lo, hi;
+            lo.x = q4_pair(t0, s_lo, m_lo);
+            lo.y = q4_pair(t1, s_lo, m_lo);
+            lo.z = q4_pair(t2, s_lo, m_lo);
+            lo.w = q4_pair(t3, s_lo, m_lo);
+            hi.x = q4_pair(t0 >> 4, s_hi, m_hi);
+            hi.y = q4_pair(t1 >> 4, s_hi, m_hi);
+            hi.z = q4_pair(t2 >> 4, s_hi, m_hi);
+            hi.w = q4_pair(t3 >> 4, s_hi, m_hi);
+            *reinterpret_cast<uint4*>(arow + ((cc ^ (t & 7)) << 4)) = lo;
+            *reinterpret_cast<uint4*>(arow + (((cc + 4) ^ (t & 7)) << 4)) = hi;
+          }
+          fence_proxy_async_smem();  // generic-proxy stores -> visible to tcgen05 (async proxy)
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->afull[ab]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->empty[s]);
+      }
+      if (!ok) {
+        set_error(a.err, kErrTimeout);
+        bars->abort = 1;
+      }
+    }
+    // ------------------------------------------------------------ epilogue
+    const bool done_ok = mbar_wait(&bars->done, 0);
+    tc_fence_after();
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int m = 32 * q + lane;     // weight row within the tile
+    const int mg = m0 + m;
+    const bool valid = done_ok && !(*(volatile int*)&bars->abort) && nk > 0;
+    if (!done_ok) set_error(a.err, kErrTimeout);
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    if (splits > 1) {
+      float* part = a.ws + ((size_t)tile * splits + split) * NT * 128;
+#pragma unroll 1
+      for (int j = 0; j < NT / 16; ++j) {
+        float v[16];
+        if (valid) tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 16 * j, v);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) part[(16 * j + e) * 128 + m] = valid ? v[e] : 0.f;
+      }
+      __threadfence();
+      named_sync_epi();
+      if (threadIdx.x == 64) {
+        const int old = atomicAdd(&a.counters[tile], 1);
+        bars->last = (old == splits - 1);
+      }
+      named_sync_epi();
+      if (!bars->last) goto finish;
+      __threadfence();
+      if (threadIdx.x == 64) a.counters[tile] = 0;  // self-cleaning for the next call
+    }
+    if (mg < a.N) {
+#pragma unroll 1
+      for (int j = 0; j < NT / 16; ++j) {
+        float v[16];
+        if (splits > 1) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = 0.f;
+          for (int sp = 0; sp < splits; ++sp) {
+            const float* part = a.ws + ((size_t)tile * splits + sp) * NT * 128;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] += __ldcg(part + (16 * j + e) * 128 + m);
+          }
+        } else if (valid) {
+          tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 16 * j, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int n = n0 + 16 * j + e;
+          if (n < a.T) {
+            const size_t o = (size_t)n * a.ldo + mg;
+            if (a.mode == kGemmStoreF32) static_cast<float*>(a.out)[o] = v[e];
+            else if (a.mode == kGemmStoreBF16) static_cast<__nv_bfloat16*>(a.out)[o] = f2bf(v[e]);
+            else static_cast<float*>(a.out)[o] += v[e];
+          }
+        }
+      }
+    }
+  finish:;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64_t inner, uint64_t outer,
+               uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+               CUtensorMapSwizzle swz) {
+  auto fn = get_encode();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NT, int FMT>
+const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
+                     dim3 grid, cudaStream_t st) {
+  using C = Cfg<NT, FMT>;
+  CUtensorMap tw, tx;
+  bool ok;
+  if (FMT == kFmtQ4K)
+    ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)w_row_bytes, (uint64_t)a.N,
+                   (uint64_t)w_row_bytes, kRawRowBytes, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  else
+    ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, (uint64_t)a.K, (uint64_t)a.N,
+                   (uint64_t)w_row_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok) return "cuTensorMapEncodeTiled failed for the weight operand";
+  if (!encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)a.K, (uint64_t)a.T,
+                 (uint64_t)ldx * 2, 64, NT, CU_TENSOR_MAP_SWIZZLE_128B))
+    return "cuTensorMapEncodeTiled failed for the activation operand";
+  static bool attr = false;
+  if (!attr) {
+    if (cudaFuncSetAttribute(gemm_q_kernel<NT, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+        cudaSuccess)
+      return "cudaFuncSetAttribute(max dynamic smem) failed";
+    attr = true;
+  }
+  gemm_q_kernel<NT, FMT><<<grid, kThreads, C::kSmem, st>>>(tw, tx, a);
+  return nullptr;
+}
+
+}  // namespace
+
+int gemm_q_token_tile(int T) {
+  if (T <= 16) return 16;
+  if (T <= 32) return 32;
+  if (T <= 64) return 64;
+  return 128;
+}
+
+int gemm_q_splits(int N, int K, int T, int fmt) {
+  const int nt = gemm_q_token_tile(T);
+  const int tiles = ((N + 127) / 128) * ((T + nt - 1) / nt);
+  const int ksteps = fmt == kFmtQ4K ? K / 256 : K / 64;
+  int s = (148 + tiles - 1) / tiles;
+  s = s < 1 ? 1 : s;
+  const int max_s = ksteps / 2 > 0 ? ksteps / 2 : 1;  // at least two K-steps per split
+  return s > max_s ? max_s : s;
+}
+
+size_t gemm_q_workspace_floats(int N, int K, int T, int fmt, int splits) {
+  const int nt = gemm_q_token_tile(T);
+  const size_t tiles = (size_t)((N + 127) / 128) * ((T + nt - 1) / nt);
+  return splits > 1 ? tiles * splits * nt * 128 : 0;
+}
+
+size_t gemm_q_counters(int N, int T) {
+  const int nt = gemm_q_token_tile(T);
+  return (size_t)((N + 127) / 128) * ((T + nt - 1) / nt);
+}
+
+const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
+                          const GemmArgs& a, cudaStream_t st) {
+  if (a.K % (fmt == kFmtQ4K ? 256 : 64)) return "gemm_q: K must be a multiple of 256 (Q4_K) or 64 (bf16)";
+  if (fmt != kFmtQ4K && fmt != kFmtBF16) return "gemm_q: weight format not supported by the tensor-core path";
+  if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16 || w_row_bytes % 16 ||
+      (ldx * 2) % 16)
+    return "gemm_q: operands must be 16-byte aligned with 16-byte-multiple row strides";
+  const int nt = gemm_q_token_tile(a.T);
+  dim3 grid((a.N + 127) / 128, (a.T + nt - 1) / nt, a.splits);
+  if (a.splits > 1 && (!a.ws || !a.counters)) return "gemm_q: split-K needs workspace and counters";
+  if (fmt == kFmtQ4K) {
+    switch (nt) {
+      case 16: return launch_t<16, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 32: return launch_t<32, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 64: return launch_t<64, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
+      default: return launch_t<128, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
+    }
+  }
+  switch (nt) {
+    case 16: return launch_t<16, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
+    case 32: return launch_t<32, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
+    case 64: return launch_t<64, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
+    default: return launch_t<128, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
+  }
+}
+
+}  // namespace air

@@ -1,3 +1,30 @@
 #pragma once
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
+#include "kernels.h"
+
+namespace air {
+
+enum GemmMode : int { kGemmStoreF32 = 0, kGemmStoreBF16 = 1, kGemmResidualF32 = 2 };
+
+struct GemmArgs {
+  int N, K, T;          // weight rows, reduction length, tokens
+  int mode;             // GemmMode
+  void* out;            // [T, ldo] (f32 or bf16)
+  int64_t ldo;
+  int splits;           // split-K factor (1 = none)
+  float* ws;            // split-K partials: gemm_q_workspace_floats() floats
+  int* counters;        // gemm_q_counters() ints, zero before first use (self-resetting)
+  int* err;
+};
+
+int gemm_q_token_tile(int T);
+int gemm_q_splits(int N, int K, int T, int fmt);
+size_t gemm_q_workspace_floats(int N, int K, int T, int fmt, int splits);
+size_t gemm_q_counters(int N, int T);
+// Returns nullptr on success, else an error message (nothing was launched).
+const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
+                          const GemmArgs& a, cudaStream_t st);
+
+}  // namespace air

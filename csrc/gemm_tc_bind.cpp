@@ -1,3 +1,56 @@
 #include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
 #include "gemm_tc.h"
-void register_gemm_tc(pybind11::module_& m) {}
+
+using at::Tensor;
+using c10::optional;
+
+namespace {
+
+void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, int64_t N, int64_t K,
+            Tensor x, Tensor out, int64_t mode, int64_t splits, optional<Tensor> ws,
+            optional<Tensor> counters, optional<Tensor> err) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2, "gemm_q: x must be 2-D bf16 CUDA");
+  TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "gemm_q: rows must be contiguous");
+  TORCH_CHECK(x.size(1) == K, "gemm_q: x has ", x.size(1), " columns, expected K=", K);
+  if (mode == air::kGemmStoreBF16) {
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16, "gemm_q: out must be bf16");
+  } else {
+    TORCH_CHECK(out.scalar_type() == at::kFloat, "gemm_q: out must be f32");
+  }
+  air::GemmArgs a{};
+  a.N = (int)N;
+  a.K = (int)K;
+  a.T = (int)x.size(0);
+  a.mode = (int)mode;
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.splits = (int)std::max<int64_t>(1, splits);
+  if (a.splits > 1) {
+    TORCH_CHECK(ws.has_value() && counters.has_value(), "gemm_q: split-K needs ws and counters");
+    TORCH_CHECK((size_t)ws->numel() >= air::gemm_q_workspace_floats(a.N, a.K, a.T, (int)fmt, a.splits),
+                "gemm_q: workspace too small");
+    TORCH_CHECK((size_t)counters->numel() >= air::gemm_q_counters(a.N, a.T), "gemm_q: counters too small");
+    a.ws = ws->data_ptr<float>();
+    a.counters = counters->data_ptr<int>();
+  }
+  a.err = err.has_value() ? err->data_ptr<int>() : nullptr;
+  const char* e = air::launch_gemm_q((int)fmt, w.data_ptr(), row_bytes, x.data_ptr(), x.stride(0), a,
+                                     at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(e == nullptr, e ? e : "");
+  cudaError_t ce = cudaGetLastError();
+  TORCH_CHECK(ce == cudaSuccess, "gemm_q launch: ", cudaGetErrorString(ce));
+}
+
+}  // namespace
+
+void register_gemm_tc(pybind11::module_& m) {
+  m.def("gemm_q", &gemm_q);
+  m.def("gemm_q_splits", [](int64_t N, int64_t K, int64_t T, int64_t fmt) {
+    return air::gemm_q_splits((int)N, (int)K, (int)T, (int)fmt);
+  });
+  m.def("gemm_q_workspace", [](int64_t N, int64_t K, int64_t T, int64_t fmt, int64_t splits) {
+    return (int64_t)air::gemm_q_workspace_floats((int)N, (int)K, (int)T, (int)fmt, (int)splits);
+  });
+  m.def("gemm_q_counters", [](int64_t N, int64_t T) { return (int64_t)air::gemm_q_counters((int)N, (int)T); });
+}

@@ -1,0 +1,48 @@
+"""tcgen05 dequant-fused GEMM vs a plain PyTorch fp32 reference."""
+import pytest
+import torch
+
+from air_rs import ops
+from air_rs.gguf import GGMLType, quantize, dequantize
+from air_rs.ops import gemm
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _w(N, K, qt, seed):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(N, K, generator=g) * 0.02
+    raw = quantize(w, qt)
+    wd = dequantize(raw, qt).reshape(N, K)
+    return ops.QWeight.from_raw(raw, qt, N, K, DEV), wd
+
+
+@pytest.mark.parametrize("qt", [GGMLType.Q4_K, GGMLType.BF16])
+@pytest.mark.parametrize("N,K,T,splits", [(128, 256, 1, 1), (384, 512, 5, 1), (256, 1024, 64, None),
+                                          (256, 2048, 64, 4), (512, 1024, 200, None), (4096, 4096, 16, None)])
+def test_gemm_q_store(qt, N, K, T, splits):
+    w, wd = _w(N, K, qt, 1)
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(T, K, generator=g).bfloat16()
+    ref = x.float() @ wd.bfloat16().float().t()
+    out = torch.zeros(T, N, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    gemm.linear(x.to(DEV), w, out, splits=splits, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    torch.testing.assert_close(out.cpu(), ref, rtol=2e-2, atol=2e-3)
+    outb = torch.zeros(T, N, dtype=torch.bfloat16, device=DEV)
+    gemm.linear(x.to(DEV), w, outb, splits=splits)
+    torch.testing.assert_close(outb.float().cpu(), ref, rtol=2e-2, atol=4e-3)
+
+
+def test_gemm_q_residual_and_repeat():
+    N, K, T = 512, 4096, 64
+    w, wd = _w(N, K, GGMLType.Q4_K, 3)
+    x = (torch.randn(T, K) * 0.5).bfloat16()
+    ref = x.float() @ wd.bfloat16().float().t()
+    resid = torch.ones(T, N, device=DEV)
+    for i in range(3):  # the split-K counters must reset themselves between calls
+        gemm.linear(x.to(DEV), w, resid, residual=True)
+    torch.testing.assert_close(resid.cpu(), 1 + 3 * ref, rtol=2e-2, atol=5e-3)
