@@ -42,11 +42,11 @@ class LayerWeights:
 
     @property
     def w_gate(self) -> ops.QWeight:
-        return self.wgu.rows(0, self.wgu.N // 2)
+        return self.wgu.part(0)
 
     @property
     def w_up(self) -> ops.QWeight:
-        return self.wgu.rows(self.wgu.N // 2, self.wgu.N)
+        return self.wgu.part(1)
 
 
 class LlamaWeights:

@@ -69,14 +69,31 @@ def ext_path() -> str | None:
         return None
 
 
+TILE_ROWS = 128
+
+
+def _q4k_tile(raw: torch.Tensor, N: int, K: int) -> torch.Tensor:
+    """Row-major GGUF Q4_K blocks [N, K/256*144] -> tiled device layout
+    [ceil(N/128), K/256, 128, 144] (rows zero-padded to whole tiles)."""
+    nsb = K // 256
+    tiles = (N + TILE_ROWS - 1) // TILE_ROWS
+    blocks = raw.reshape(N, nsb, 144)
+    if tiles * TILE_ROWS != N:
+        blocks = torch.cat([blocks, blocks.new_zeros(tiles * TILE_ROWS - N, nsb, 144)], 0)
+    return blocks.view(tiles, TILE_ROWS, nsb, 144).permute(0, 2, 1, 3).contiguous()
+
+
 @dataclass
 class QWeight:
     """A linear weight [N, K] resident on the device in a kernel-native format.
 
-    fmt FMT_Q4K keeps the raw GGUF Q4_K blocks (144 B / 256 weights, 16-byte aligned
-    rows); FMT_Q8_0 keeps Q8_0 split into int8 codes + f16 scales (the 34-byte GGUF block
-    is not 16-byte aligned); FMT_BF16 holds dense bf16 (F16/BF16/F32 checkpoints and the
-    K-quants without a fused kernel yet are expanded to it at load).
+    FMT_Q4K keeps the GGUF Q4_K blocks (144 B per 256 weights) byte-for-byte but groups
+    them as [N/128 tiles][K/256][128 rows][144 B], so a 128-row x 256-weight tile is one
+    contiguous 18 KB copy for the TMA engine (rows padded to whole tiles). FMT_Q8_0 splits
+    the 34-byte GGUF block into int8 codes + f16 scales (row-major). FMT_BF16 is dense bf16
+    (F16/BF16/F32 checkpoints and K-quants without a fused kernel are expanded to it).
+    ``parts`` records the row offsets of concatenated weights (e.g. gate|up), which start
+    on tile boundaries for Q4_K.
     """
     fmt: int
     data: torch.Tensor
@@ -84,9 +101,12 @@ class QWeight:
     N: int
     K: int
     qtype: GGMLType
+    parts: tuple = ()
 
     @property
     def row_bytes(self) -> int:
+        if self.fmt == FMT_Q4K:
+            return self.K // 256 * 144
         return self.data.stride(0) * self.data.element_size()
 
     @property
@@ -97,9 +117,18 @@ class QWeight:
         return n
 
     def rows(self, r0: int, r1: int) -> "QWeight":
-        """Row slice (a view; used for fused gate|up and TP shards)."""
+        """Row slice (a view; fused gate|up halves and tensor-parallel shards)."""
+        if self.fmt == FMT_Q4K:
+            if r0 % TILE_ROWS:
+                raise ValueError(f"Q4_K row slice must start on a {TILE_ROWS}-row tile (got {r0})")
+            t0, t1 = r0 // TILE_ROWS, (r1 + TILE_ROWS - 1) // TILE_ROWS
+            return QWeight(self.fmt, self.data[t0:t1], None, r1 - r0, self.K, self.qtype)
         return QWeight(self.fmt, self.data[r0:r1], None if self.scales is None else self.scales[r0:r1],
                        r1 - r0, self.K, self.qtype)
+
+    def part(self, i: int) -> "QWeight":
+        off, n = self.parts[i]
+        return self.rows(off, off + n)
 
     @classmethod
     def from_raw(cls, raw: torch.Tensor, qtype: GGMLType, N: int, K: int,
@@ -107,17 +136,17 @@ class QWeight:
         qtype = GGMLType(qtype)
         raw = raw.reshape(N, -1)
         if qtype == GGMLType.Q4_K:
-            return cls(FMT_Q4K, raw.to(device).contiguous(), None, N, K, qtype)
+            return cls(FMT_Q4K, _q4k_tile(raw.to(device), N, K), None, N, K, qtype, ((0, N),))
         if qtype == GGMLType.Q8_0:
             b = raw.to(device).reshape(N, K // 32, 34)
             scales = b[..., 0:2].contiguous().view(torch.float16).reshape(N, K // 32)
             qs = b[..., 2:].contiguous().view(torch.int8).reshape(N, K)
-            return cls(FMT_Q8_0, qs, scales.contiguous(), N, K, qtype)
+            return cls(FMT_Q8_0, qs, scales.contiguous(), N, K, qtype, ((0, N),))
         dense = dequantize(raw.to(device), qtype).reshape(N, K).to(torch.bfloat16)
         Kp = pad32(K)
         if Kp != K:  # zero columns so the activation's 32-element groups line up
             dense = torch.nn.functional.pad(dense, (0, Kp - K))
-        return cls(FMT_BF16, dense.contiguous(), None, N, Kp, qtype)
+        return cls(FMT_BF16, dense.contiguous(), None, N, Kp, qtype, ((0, N),))
 
     @staticmethod
     def cat(ws: list["QWeight"]) -> "QWeight":
@@ -125,7 +154,12 @@ class QWeight:
         assert all(w.fmt == fmt and w.K == ws[0].K for w in ws)
         data = torch.cat([w.data for w in ws], 0).contiguous()
         scales = None if ws[0].scales is None else torch.cat([w.scales for w in ws], 0).contiguous()
-        return QWeight(fmt, data, scales, sum(w.N for w in ws), ws[0].K, ws[0].qtype)
+        parts, off = [], 0
+        for w in ws:
+            parts.append((off, w.N))
+            off += (w.data.shape[0] * TILE_ROWS) if fmt == FMT_Q4K else w.N
+        N = parts[-1][0] + parts[-1][1]
+        return QWeight(fmt, data, scales, N, ws[0].K, ws[0].qtype, tuple(parts))
 
     def dequantize_bf16(self, out: torch.Tensor | None = None) -> torch.Tensor:
         ext = require_ext()
@@ -198,9 +232,10 @@ def rope_kv(qkv, T, rope_cs, positions, slots, kv, q_out, *, n_heads, n_kv, head
     count_launch()
 
 
-def swiglu(gu, T, F, out_bf16=None, out_f32=None, ld_out: int | None = None):
-    """out[t, j] = silu(gu[t, j]) * gu[t, F + j] for j < F (out row stride ld_out)."""
-    require_ext().swiglu(gu, T, F, ld_out if ld_out is not None else F, out_bf16, out_f32)
+def swiglu(gu, T, F, out_bf16=None, out_f32=None, ld_out: int | None = None, up_off: int | None = None):
+    """out[t, j] = silu(gu[t, j]) * gu[t, up_off + j] for j < F (out row stride ld_out)."""
+    require_ext().swiglu(gu, T, F, up_off if up_off is not None else F, ld_out if ld_out is not None else F,
+                         out_bf16, out_f32)
     count_launch()
 
 

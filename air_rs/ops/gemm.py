@@ -25,7 +25,7 @@ def tc_supported(w: QWeight) -> bool:
     if _baseline_forced():
         return False
     if w.fmt == FMT_Q4K:
-        return w.K % 256 == 0
+        return w.K % 256 == 0 and w.data.dim() == 4
     if w.fmt == FMT_BF16:
         return w.K % 64 == 0
     return False
@@ -38,6 +38,8 @@ class _Workspace:
         self.device = device
         self.ws = torch.zeros(0, dtype=torch.float32, device=device)
         self.cnt = torch.zeros(0, dtype=torch.int32, device=device)
+        # error word for callers that pass none (bounded waits report into it)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
 
     def ensure(self, floats: int, counters: int):
         if self.ws.numel() < floats:
@@ -64,7 +66,8 @@ def workspace(device) -> _Workspace:
 
 
 def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, residual: bool = False,
-           splits: int | None = None, err: torch.Tensor | None = None) -> torch.Tensor:
+           splits: int | None = None, err: torch.Tensor | None = None,
+           dbg: torch.Tensor | None = None) -> torch.Tensor:
     """out = x @ W^T (or out += x @ W^T when residual, out fp32)."""
     T = x.shape[0]
     if T == 0:
@@ -80,7 +83,9 @@ def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, resid
         if s > 1:
             ws, cnt = workspace(x.device).ensure(ext.gemm_q_workspace(w.N, w.K, T, w.fmt, s),
                                                  ext.gemm_q_counters(w.N, T))
-        ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out, mode, s, ws, cnt, err)
+        if err is None:
+            err = workspace(x.device).err
+        ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out, mode, s, ws, cnt, err, dbg)
         count_launch()
         return out
     if residual:

@@ -96,7 +96,10 @@ class ModelRunner:
         self.xn_b = torch.zeros(B, self.H, dtype=bf16, device=dev)
         self.qkv_b = torch.zeros(B, self.qkv_dim, dtype=bf16, device=dev)
         self.attn_b = torch.zeros(B, self.nh * self.hd, dtype=bf16, device=dev)
-        self.gu_b = torch.zeros(B, 2 * self.F, dtype=bf16, device=dev)
+        l0 = weights.layers[0]
+        self.gu_w = l0.wgu.N if l0.wgu is not None else 2 * self.F   # gate|up GEMM width
+        self.up_off = l0.wgu.parts[1][0] if l0.wgu is not None else self.F
+        self.gu_b = torch.zeros(B, self.gu_w, dtype=bf16, device=dev)
         self.h_b = torch.zeros(B, self.Fp, dtype=bf16, device=dev)
         self.o_b = torch.zeros(B, self.H, dtype=bf16, device=dev)
         self.inputs: dict[int, StepInputs] = {}
@@ -223,7 +226,7 @@ class ModelRunner:
             moe.moe_ffn_gemm(self, lw, B, x)
             return
         self.linear(self.xn_b[:B], lw.wgu, self.gu_b[:B])
-        ops.swiglu(self.gu_b[:B], B, self.F, out_bf16=self.h_b[:B], ld_out=self.Fp)
+        ops.swiglu(self.gu_b[:B], B, self.F, out_bf16=self.h_b[:B], ld_out=self.Fp, up_off=self.up_off)
         self._proj_into_residual(self.h_b[:B], lw.wdown, x, self.o_b, tp)
 
     def _head(self, B, x, xq, xds, gemv_path):
@@ -307,7 +310,7 @@ class ModelRunner:
         attn = self._ws("attn", (T, self.nh * self.hd), f32)
         attn_b = self._ws("attn_b", (T, self.nh * self.hd), bf16)
         o = self._ws("o", (T, self.H), bf16)
-        gu = self._ws("gu", (T, 2 * self.F), bf16) if self.w.layers[0].wgu is not None else None
+        gu = self._ws("gu", (T, self.gu_w), bf16) if self.w.layers[0].wgu is not None else None
         hb = self._ws("hb", (T, self.Fp), bf16, zero=True)
         ctx = (positions + 1).to(torch.int32)
         tp = self.tp_size > 1
@@ -330,7 +333,7 @@ class ModelRunner:
                 moe.moe_ffn_prefill(self, lw, T, x, xn)
             else:
                 self.linear(xn, lw.wgu, gu)
-                ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp)
+                ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp, up_off=self.up_off)
                 self._proj_into_residual(hb, lw.wdown, x, o, tp)
         xl = x.index_select(0, last_rows.long())
         xs = self._ws("xs", (S, self.H), bf16)

@@ -172,9 +172,10 @@ void rope_kv(Tensor qkv, int64_t T, Tensor rope_cs, Tensor positions, Tensor slo
   post_launch("rope_kv");
 }
 
-void swiglu(Tensor gu, int64_t T, int64_t F, int64_t ld_out, optional<Tensor> out_bf16,
+void swiglu(Tensor gu, int64_t T, int64_t F, int64_t up_off, int64_t ld_out, optional<Tensor> out_bf16,
             optional<Tensor> out_f32) {
-  air::launch_swiglu(gu.data_ptr(), gu.scalar_type() == at::kBFloat16, (int)T, (int)F, ld_out, ptr(out_bf16),
+  air::launch_swiglu(gu.data_ptr(), gu.scalar_type() == at::kBFloat16, (int)T, (int)F, gu.stride(0), up_off,
+                     ld_out, ptr(out_bf16),
                      ptr<float>(out_f32), stream());
   post_launch("swiglu");
 }

@@ -111,3 +111,12 @@ AIR_DEVICE void q4k_scale_min(const uint8_t* sc12, int j, int& sc, int& m) {
 }
 
 }  // namespace air
+
+namespace air {
+// Q4_K device layout ("tiled"): [ceil(N/128)][K/256][128 rows][144 B]. The 144-byte GGUF
+// block is unchanged; rows are grouped 128 at a time per super-block column so one
+// 128-row x 256-weight tile is 18 KB of contiguous memory (one bulk copy).
+AIR_DEVICE const uint8_t* q4k_block(const uint8_t* base, int64_t r, int sb, int nsb) {
+  return base + (((((r >> 7) * nsb + sb) << 7) + (r & 127)) * 144);
+}
+}  // namespace air

@@ -7,7 +7,7 @@
 //   warp 0      TMA producer: raw weight box (128 rows x one 256-weight super-block, the
 //               144-byte GGUF blocks copied verbatim) + the matching x boxes (SW128 swizzle)
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer (f32 accumulators in TMEM)
-//   warps 2..5  dequantise the staged Q4_K blocks into bf16 K-major SW128 tiles with packed
+//   warps 2..9  dequantise the staged Q4_K blocks into bf16 K-major SW128 tiles with packed
 //               bf16x2 arithmetic (the GGUF scale/min math), then run the epilogue
 //               (tcgen05.ld -> store / residual add / split-K reduction).
 // Stages are handed over with mbarriers (TMA complete_tx, tcgen05.commit). Split-K uses a
@@ -21,6 +21,8 @@
 #include "common.cuh"
 #include "sm100.cuh"
 #include "gemm_tc.h"
+#include <stdlib.h>
+#include <string.h>
 
 namespace air {
 
@@ -28,17 +30,18 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 192;
+constexpr int kDqWarps = 8;                     // dequant + epilogue warps
+constexpr int kThreads = 64 + 32 * kDqWarps;
 constexpr int kRawRowBytes = 144;           // one Q4_K super-block of one row
 constexpr int kRawTile = 128 * kRawRowBytes; // 18432 B (multiple of 1024)
 constexpr int kATile = 128 * 128;            // 128 rows x 64 bf16
 
-template <int NT, int FMT>
+template <int NT, int FMT, int NA>
 struct Cfg {
   static constexpr int kChunks = FMT == kFmtQ4K ? 4 : 1;         // 64-wide K chunks per stage
   static constexpr int kBChunk = NT * 128;                       // NT rows x 128 B
   static constexpr int kStageBytes = (FMT == kFmtQ4K ? kRawTile : kATile) + kChunks * kBChunk;
-  static constexpr int kABuf = FMT == kFmtQ4K ? 2 * kATile : 0;
+  static constexpr int kABuf = FMT == kFmtQ4K ? NA * kATile : 0;
   static constexpr int kBudget = 227 * 1024 - 2048 - 1024;
   static constexpr int kStages = (kBudget - kABuf) / kStageBytes > 8 ? 8 : (kBudget - kABuf) / kStageBytes;
   static constexpr int kSmem = 1024 + kStages * kStageBytes + kABuf + 1024;
@@ -49,15 +52,15 @@ struct Cfg {
 struct Bars {
   uint64_t full[8];
   uint64_t empty[8];
-  uint64_t afull[2];
-  uint64_t aempty[2];
+  uint64_t afull[4];
+  uint64_t aempty[4];
   uint64_t done;
   uint32_t tmem;
   int abort;
   int last;
 };
 
-__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kDqWarps) : "memory"); }
 
 // One 16-byte output chunk (8 bf16) = s * q - mm for 8 nibbles taken from 2 words.
 __device__ __forceinline__ uint32_t q4_pair(uint32_t t, __nv_bfloat162 s, __nv_bfloat162 negm) {
@@ -69,11 +72,11 @@ __device__ __forceinline__ uint32_t q4_pair(uint32_t t, __nv_bfloat162 s, __nv_b
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
-template <int NT, int FMT>
+template <int NT, int FMT, int NA>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
               GemmArgs a) {
-  using C = Cfg<NT, FMT>;
+  using C = Cfg<NT, FMT, NA>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -91,10 +94,10 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], FMT == kFmtQ4K ? 5 : 1);
+      mbar_init(&bars->empty[s], FMT == kFmtQ4K ? kDqWarps + 1 : 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->afull[i], 4);
+    for (int i = 0; i < NA; ++i) {
+      mbar_init(&bars->afull[i], kDqWarps);
       mbar_init(&bars->aempty[i], 1);
     }
     mbar_init(&bars->done, 1);
@@ -102,7 +105,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tm_w);
+    if (FMT != kFmtQ4K) prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_x);
   }
   if (warp == 1) tmem_alloc(&bars->tmem, C::kTmemCols);
@@ -110,6 +113,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
+  long long* dbg = (a.dbg && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) ? a.dbg : nullptr;
+  if (dbg && threadIdx.x == 0) dbg[225] = clock64();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -118,17 +123,19 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       int issued = 0;
       for (int i = 0; i < nk; ++i) {
         const int s = i % C::kStages;
-        if (i >= C::kStages && !mbar_wait(&bars->empty[s], ((i / C::kStages) - 1) & 1)) {
+        if (i >= C::kStages && !mbar_wait(&bars->empty[s], ((i / C::kStages) - 1) & 1, a.err)) {
           set_error(a.err, kErrTimeout);
           bars->abort = 1;
           break;
         }
         if (*(volatile int*)&bars->abort) break;
         uint8_t* st = stages + s * C::kStageBytes;
+        if (dbg && i < 32) dbg[i] = clock64();
         mbar_expect_tx(&bars->full[s], tx);
         const int kb = kb0 + i;
         if (FMT == kFmtQ4K) {
-          tma_load_2d(st, &tm_w, &bars->full[s], kb * kRawRowBytes, m0);
+          // tiled Q4_K: the 128-row x 256-weight tile is 18 KB contiguous -> one bulk copy
+          bulk_load(st, a.wq + ((size_t)blockIdx.x * ksteps + kb) * kRawTile, kRawTile, &bars->full[s]);
 #pragma unroll
           for (int c = 0; c < 4; ++c)
             tma_load_2d(st + kRawTile + c * C::kBChunk, &tm_x, &bars->full[s], kb * 256 + 64 * c, n0);
@@ -140,7 +147,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       }
       // never leave the CTA with copies in flight into its shared memory
       for (int i = max(0, issued - C::kStages); i < issued; ++i)
-        mbar_wait(&bars->full[i % C::kStages], (i / C::kStages) & 1, 1u << 22);
+        mbar_wait(&bars->full[i % C::kStages], (i / C::kStages) & 1, a.err, 50ull * 1000 * 1000);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -150,13 +157,13 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
         const int s = i % C::kStages;
-        if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1)) { ok = false; break; }
+        if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1, a.err)) { ok = false; break; }
         uint8_t* st = stages + s * C::kStageBytes;
         for (int c = 0; c < C::kChunks; ++c, ++g) {
           const uint8_t* A;
           if (FMT == kFmtQ4K) {
-            const int ab = g & 1;
-            if (!mbar_wait(&bars->afull[ab], (g >> 1) & 1)) { ok = false; break; }
+            const int ab = g % NA;
+            if (!mbar_wait(&bars->afull[ab], (g / NA) & 1, a.err)) { ok = false; break; }
             A = abuf + ab * kATile;
           } else {
             A = st;
@@ -167,7 +174,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
 #pragma unroll
           for (int k = 0; k < 4; ++k)  // 4 x K16 per 64-wide chunk: +32 B along K
             mma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (i | c | k) != 0 ? 1u : 0u);
-          if (FMT == kFmtQ4K) mma_commit(&bars->aempty[g & 1]);
+          if (FMT == kFmtQ4K) mma_commit(&bars->aempty[g % NA]);
         }
         mma_commit(&bars->empty[s]);
       }
@@ -179,51 +186,59 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
     }
   } else {
     // ------------------------------------------------------------ dequant (Q4_K)
-    const int t = threadIdx.x - 64;  // weight row within the tile
+    // Thread = (weight row t, nibble half hf): hf = 0 expands the low nibbles (sub-blocks
+    // 0,2,4,6 of the super-block), hf = 1 the high nibbles (1,3,5,7). Scales are decoded once
+    // per stage; per 64-wide chunk a thread turns 32 code bytes into 32 bf16 with 3 ops per
+    // pair: PRMT places two nibbles under a 0x43 exponent byte (= 128 + q, exact), HSUB2
+    // removes the 128, HFMA2 applies d*sc and -dmin*m.
+    const int t = (threadIdx.x - 64) & 127;
+    const int hf = (threadIdx.x - 64) >> 7;   // warp-uniform
     if (FMT == kFmtQ4K) {
       int g = 0;
       bool ok = true;
+      const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
       for (int i = 0; i < nk && ok; ++i) {
         const int s = i % C::kStages;
-        if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1)) { ok = false; break; }
+        if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1, a.err)) { ok = false; break; }
         const uint8_t* rb = stages + s * C::kStageBytes + t * kRawRowBytes;
         const uint32_t hdr = *reinterpret_cast<const uint32_t*>(rb);
         const float d = __half2float(__ushort_as_half((unsigned short)(hdr & 0xFFFF)));
         const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr >> 16)));
+        __nv_bfloat162 sv[4], mv[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          int sc, mn;
+          q4k_scale_min(rb + 4, 2 * c + hf, sc, mn);
+          sv[c] = __float2bfloat162_rn(d * (float)sc);
+          mv[c] = __float2bfloat162_rn(-dmin * (float)mn);
+        }
+#pragma unroll
         for (int c = 0; c < 4; ++c, ++g) {
-          const int ab = g & 1;
-          if (g >= 2 && !mbar_wait(&bars->aempty[ab], ((g >> 1) - 1) & 1)) { ok = false; break; }
-          int sl, ml, sh, mh;
-          q4k_scale_min(rb + 4, 2 * c, sl, ml);
-          q4k_scale_min(rb + 4, 2 * c + 1, sh, mh);
-          const __nv_bfloat162 s_lo = __float2bfloat162_rn(d * (float)sl);
-          const __nv_bfloat162 m_lo = __float2bfloat162_rn(-dmin * (float)ml);
-          const __nv_bfloat162 s_hi = __float2bfloat162_rn(d * (float)sh);
-          const __nv_bfloat162 m_hi = __float2bfloat162_rn(-dmin * (float)mh);
+          const int ab = g % NA;
+          if (g >= NA && !mbar_wait(&bars->aempty[ab], ((g / NA) - 1) & 1, a.err)) { ok = false; break; }
+          if (dbg && threadIdx.x == 64 && g < 64) dbg[96 + g] = clock64();
           const uint4 qa = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
           const uint4 qb = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
-          const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) w[k] = hf ? (w[k] >> 4) & 0x0F0F0F0Fu : w[k] & 0x0F0F0F0Fu;
           uint8_t* arow = abuf + ab * kATile + t * 128;
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
-            // bytes 8cc .. 8cc+7: low nibbles -> k = 8cc.., high nibbles -> k = 32 + 8cc..
-            const uint32_t t0 = __byte_perm(w[2 * cc], 0, 0x4140), t1 = __byte_perm(w[2 * cc], 0, 0x4342);
-            const uint32_t t2 = __byte_perm(w[2 * cc + 1], 0, 0x4140), t3 = __byte_perm(w[2 * cc + 1], 0, 0x4342);
-            uint4 lo, hi;
-            lo.x = q4_pair(t0, s_lo, m_lo);
-            lo.y = q4_pair(t1, s_lo, m_lo);
-            lo.z = q4_pair(t2, s_lo, m_lo);
-            lo.w = q4_pair(t3, s_lo, m_lo);
-            hi.x = q4_pair(t0 >> 4, s_hi, m_hi);
-            hi.y = q4_pair(t1 >> 4, s_hi, m_hi);
-            hi.z = q4_pair(t2 >> 4, s_hi, m_hi);
-            hi.w = q4_pair(t3 >> 4, s_hi, m_hi);
-            *reinterpret_cast<uint4*>(arow + ((cc ^ (t & 7)) << 4)) = lo;
-            *reinterpret_cast<uint4*>(arow + (((cc + 4) ^ (t & 7)) << 4)) = hi;
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t v = __byte_perm(w[2 * cc + (e >> 1)], 0x43434343u, (e & 1) ? 0x4342 : 0x4140);
+              __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&v);
+              b = __hfma2(__hsub2(b, c128), sv[c], mv[c]);
+              o[e] = *reinterpret_cast<uint32_t*>(&b);
+            }
+            *reinterpret_cast<uint4*>(arow + (((cc + 4 * hf) ^ (t & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
           fence_proxy_async_smem();  // generic-proxy stores -> visible to tcgen05 (async proxy)
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->afull[ab]);
+          if (dbg && threadIdx.x == 64 && g < 64) dbg[160 + g] = clock64();
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->empty[s]);
@@ -234,18 +249,23 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       }
     }
     // ------------------------------------------------------------ epilogue
-    const bool done_ok = mbar_wait(&bars->done, 0);
+    const bool done_ok = mbar_wait(&bars->done, 0, a.err);
+    if (dbg && threadIdx.x == 64) dbg[224] = clock64();
     tc_fence_after();
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int m = 32 * q + lane;     // weight row within the tile
+    const int jh = (warp - 2) >> 2;  // the kDqWarps/4 warps of a quarter split the column groups
+    constexpr int kJW = kDqWarps / 4;
     const int mg = m0 + m;
-    const bool valid = done_ok && !(*(volatile int*)&bars->abort) && nk > 0;
+    // warp-uniform: every tcgen05.ld below must be executed by all 32 lanes or none
+    const bool valid = __all_sync(0xffffffffu, done_ok && !(*(volatile int*)&bars->abort) && nk > 0);
     if (!done_ok) set_error(a.err, kErrTimeout);
     const int tile = blockIdx.y * gridDim.x + blockIdx.x;
     if (splits > 1) {
       float* part = a.ws + ((size_t)tile * splits + split) * NT * 128;
 #pragma unroll 1
       for (int j = 0; j < NT / 16; ++j) {
+        if ((j % kJW) != jh) continue;
         float v[16];
         if (valid) tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 16 * j, v);
 #pragma unroll
@@ -262,9 +282,10 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       __threadfence();
       if (threadIdx.x == 64) a.counters[tile] = 0;  // self-cleaning for the next call
     }
-    if (mg < a.N) {
+    {  // all lanes stay in: tcgen05.ld is warp-collective; rows >= N are masked at the store
 #pragma unroll 1
       for (int j = 0; j < NT / 16; ++j) {
+        if ((j % kJW) != jh) continue;
         float v[16];
         if (splits > 1) {
 #pragma unroll
@@ -283,7 +304,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int n = n0 + 16 * j + e;
-          if (n < a.T) {
+          if (n < a.T && mg < a.N) {
             const size_t o = (size_t)n * a.ldo + mg;
             if (a.mode == kGemmStoreF32) static_cast<float*>(a.out)[o] = v[e];
             else if (a.mode == kGemmStoreBF16) static_cast<__nv_bfloat16*>(a.out)[o] = f2bf(v[e]);
@@ -328,16 +349,18 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT, int FMT>
-const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
-                     dim3 grid, cudaStream_t st) {
-  using C = Cfg<NT, FMT>;
+template <int NT, int FMT, int NA>
+const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
+                      dim3 grid, cudaStream_t st) {
+  using C = Cfg<NT, FMT, NA>;
   CUtensorMap tw, tx;
   bool ok;
-  if (FMT == kFmtQ4K)
-    ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)w_row_bytes, (uint64_t)a.N,
-                   (uint64_t)w_row_bytes, kRawRowBytes, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
-  else
+  GemmArgs b = a;
+  b.wq = static_cast<const uint8_t*>(w);
+  if (FMT == kFmtQ4K) {
+    memset(&tw, 0, sizeof(tw));  // unused: the tiled Q4_K operand is fetched with bulk copies
+    ok = true;
+  } else
     ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, (uint64_t)a.K, (uint64_t)a.N,
                    (uint64_t)w_row_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok) return "cuTensorMapEncodeTiled failed for the weight operand";
@@ -346,13 +369,34 @@ const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, cons
     return "cuTensorMapEncodeTiled failed for the activation operand";
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(gemm_q_kernel<NT, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+    if (cudaFuncSetAttribute(gemm_q_kernel<NT, FMT, NA>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
         cudaSuccess)
       return "cudaFuncSetAttribute(max dynamic smem) failed";
     attr = true;
   }
-  gemm_q_kernel<NT, FMT><<<grid, kThreads, C::kSmem, st>>>(tw, tx, a);
+  gemm_q_kernel<NT, FMT, NA><<<grid, kThreads, C::kSmem, st>>>(tw, tx, b);
   return nullptr;
+}
+
+// Number of dequantised A buffers in flight between the dequant warps and the MMA issuer.
+int a_buffers() {
+  static int na = 0;
+  if (!na) {
+    const char* e = getenv("AIR_GEMM_NA");
+    na = (e && atoi(e) == 2) ? 2 : 4;
+  }
+  return na;
+}
+
+template <int NT, int FMT>
+const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
+                     dim3 grid, cudaStream_t st) {
+  if constexpr (FMT == kFmtQ4K && NT == 128) {
+    return launch_na<NT, FMT, 2>(a, w, w_row_bytes, x, ldx, grid, st);
+  } else {
+    if (FMT == kFmtQ4K && a_buffers() == 2) return launch_na<NT, FMT, 2>(a, w, w_row_bytes, x, ldx, grid, st);
+    return launch_na<NT, FMT, 4>(a, w, w_row_bytes, x, ldx, grid, st);
+  }
 }
 
 }  // namespace

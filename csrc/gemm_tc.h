@@ -17,6 +17,9 @@ struct GemmArgs {
   float* ws;            // split-K partials: gemm_q_workspace_floats() floats
   int* counters;        // gemm_q_counters() ints, zero before first use (self-resetting)
   int* err;
+  long long* dbg;
+  const uint8_t* wq;    // weight base (filled by launch_gemm_q)
+       // optional per-phase clock64 stamps of CTA (0,0,0) (profiling aid)
 };
 
 int gemm_q_token_tile(int T);

@@ -53,14 +53,14 @@ AIR_DEVICE float h2f_bits(uint32_t bits16) {
 
 // Q4_K: a lane owns half-blocks (128 weights = 16 B header + 64 B codes).
 template <int MAXB>
-AIR_DEVICE void dot2_q4k(const uint8_t* __restrict__ row0, const uint8_t* __restrict__ row1, int K,
-                         int nB, const int8_t* __restrict__ xq, const float2* __restrict__ xds,
-                         float (&acc)[2][MAXB]) {
+AIR_DEVICE void dot2_q4k(const uint8_t* __restrict__ base0, int64_t r0, const uint8_t* __restrict__ base1,
+                         int64_t r1, int K, int nB, const int8_t* __restrict__ xq,
+                         const float2* __restrict__ xds, float (&acc)[2][MAXB]) {
   const int lane = threadIdx.x & 31;
-  const int nhb = K / 128;
+  const int nhb = K / 128, nsb = K / 256;
   for (int hb = lane; hb < nhb; hb += 32) {
     const int blk = hb >> 1, h = hb & 1;
-    const uint8_t* bp[2] = {row0 + (size_t)blk * 144, row1 + (size_t)blk * 144};
+    const uint8_t* bp[2] = {q4k_block(base0, r0, blk, nsb), q4k_block(base1, r1, blk, nsb)};
     uint4 hd[2], qv[2][4];
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -182,8 +182,8 @@ AIR_DEVICE void dot2(const GemvWeight& wa, int64_t ra, const GemvWeight& wb, int
 #pragma unroll
     for (int b = 0; b < MAXB; ++b) acc[r][b] = 0.f;
   if (FMT == kFmtQ4K) {
-    dot2_q4k<MAXB>(static_cast<const uint8_t*>(wa.data) + ra * wa.row_bytes,
-                   static_cast<const uint8_t*>(wb.data) + rb * wb.row_bytes, K, nB, xq, xds, acc);
+    dot2_q4k<MAXB>(static_cast<const uint8_t*>(wa.data), ra, static_cast<const uint8_t*>(wb.data), rb, K,
+                   nB, xq, xds, acc);
   } else if (FMT == kFmtQ8_0) {
     dot2_q8_0<MAXB>(static_cast<const int8_t*>(wa.data) + ra * (int64_t)K,
                     static_cast<const int8_t*>(wb.data) + rb * (int64_t)K,

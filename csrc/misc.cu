@@ -13,10 +13,14 @@ AIR_DEVICE float h2f(const uint8_t* p) {
 }
 
 // Dequantise element range [k0, k0+32) of a GGUF row of format fmt into f.
-AIR_DEVICE void dequant32(int fmt, const uint8_t* row, const void* scales_row, int k0, float* f) {
+// Row r of a weight: Q4_K uses the tiled device layout (base + r), other formats row-major.
+AIR_DEVICE void dequant32(int fmt, const uint8_t* base, int64_t r, int64_t row_bytes, const void* scales,
+                          int K, int k0, float* f) {
+  const uint8_t* row = base + r * row_bytes;
+  const void* scales_row = scales ? static_cast<const __half*>(scales) + r * (K / 32) : nullptr;
   if (fmt == kFmtQ4K) {
     const int blk = k0 >> 8, sub = (k0 >> 5) & 7;
-    const uint8_t* bp = row + (size_t)blk * 144;
+    const uint8_t* bp = q4k_block(base, r, blk, K / 256);
     const float d = h2f(bp), dmin = h2f(bp + 2);
     int sc, m;
     q4k_scale_min(bp + 4, sub, sc, m);
@@ -46,11 +50,9 @@ __global__ void embed_kernel(int fmt, const uint8_t* __restrict__ table, const v
   const int t = blockIdx.x;
   int id = ids[t];
   if (id < 0 || id >= vocab) { set_error(err, kErrBounds); id = 0; }
-  const uint8_t* row = table + (size_t)id * row_bytes;
-  const void* srow = scales ? static_cast<const __half*>(scales) + (size_t)id * (K / 32) : nullptr;
   for (int g = threadIdx.x; g < K / 32; g += blockDim.x) {
     float f[32];
-    dequant32(fmt, row, srow, g * 32, f);
+    dequant32(fmt, table, id, row_bytes, scales, K, g * 32, f);
 #pragma unroll
     for (int l = 0; l < 32; ++l) {
       const size_t o = (size_t)t * K + g * 32 + l;
@@ -67,9 +69,8 @@ __global__ void dequant_kernel(int fmt, const uint8_t* __restrict__ w, const voi
   if (g >= groups) return;
   const int64_t r = g / (K / 32);
   const int k0 = (int)(g % (K / 32)) * 32;
-  const void* srow = scales ? static_cast<const __half*>(scales) + r * (K / 32) : nullptr;
   float f[32];
-  dequant32(fmt, w + r * row_bytes, srow, k0, f);
+  dequant32(fmt, w, r, row_bytes, scales, K, k0, f);
   uint4* o = reinterpret_cast<uint4*>(out + r * K + k0);
 #pragma unroll
   for (int i = 0; i < 4; ++i) o[i] = f32_to_bf16x8(f + 8 * i);
@@ -116,14 +117,15 @@ __global__ void rope_kv_kernel(const TIn* __restrict__ qkv, int T, RopeKvArgs a)
 
 // out[t, j] = silu(gu[t, j]) * gu[t, F + j]   (gate/up concatenated along columns)
 template <typename TIn>
-__global__ void swiglu_kernel(const TIn* __restrict__ gu, int T, int F, int64_t ld_out,
+__global__ void swiglu_kernel(const TIn* __restrict__ gu, int T, int F, int64_t ld_in, int64_t up_off,
+                              int64_t ld_out,
                               __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)T * F) return;
   const int64_t t = idx / F, j = idx % F;
   float g, u;
-  if constexpr (sizeof(TIn) == 4) { g = gu[t * 2 * F + j]; u = gu[t * 2 * F + F + j]; }
-  else { g = bf2f(gu[t * 2 * F + j]); u = bf2f(gu[t * 2 * F + F + j]); }
+  if constexpr (sizeof(TIn) == 4) { g = gu[t * ld_in + j]; u = gu[t * ld_in + up_off + j]; }
+  else { g = bf2f(gu[t * ld_in + j]); u = bf2f(gu[t * ld_in + up_off + j]); }
   const float v = g / (1.f + __expf(-g)) * u;
   if (out_bf16) out_bf16[t * ld_out + j] = f2bf(v);
   if (out_f32) out_f32[t * ld_out + j] = v;
@@ -162,13 +164,13 @@ void launch_rope_kv(const void* qkv, bool bf16_in, int T, const RopeKvArgs& a, c
   else rope_kv_kernel<float><<<grid, 256, 0, st>>>((const float*)qkv, T, a);
 }
 
-void launch_swiglu(const void* gu, bool bf16_in, int T, int F, int64_t ld_out, void* out_bf16,
-                   float* out_f32, cudaStream_t st) {
+void launch_swiglu(const void* gu, bool bf16_in, int T, int F, int64_t ld_in, int64_t up_off,
+                   int64_t ld_out, void* out_bf16, float* out_f32, cudaStream_t st) {
   const int64_t n = (int64_t)T * F;
   if (n <= 0) return;
   const unsigned grid = (unsigned)((n + 255) / 256);
-  if (bf16_in) swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)gu, T, F, ld_out, (__nv_bfloat16*)out_bf16, out_f32);
-  else swiglu_kernel<float><<<grid, 256, 0, st>>>((const float*)gu, T, F, ld_out, (__nv_bfloat16*)out_bf16, out_f32);
+  if (bf16_in) swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, out_f32);
+  else swiglu_kernel<float><<<grid, 256, 0, st>>>((const float*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, out_f32);
 }
 
 void launch_residual_add(float* resid, const void* y, bool bf16_in, int64_t n, cudaStream_t st) {

@@ -22,8 +22,8 @@ void launch_embed(int fmt, const void* table, const void* scales, int64_t row_by
 void launch_dequant(int fmt, const void* w, const void* scales, int64_t row_bytes, int N, int K,
                     void* out, cudaStream_t st);
 void launch_rope_kv(const void* qkv, bool bf16_in, int T, const RopeKvArgs& a, cudaStream_t st);
-void launch_swiglu(const void* gu, bool bf16_in, int T, int F, int64_t ld_out, void* out_bf16,
-                   float* out_f32, cudaStream_t st);
+void launch_swiglu(const void* gu, bool bf16_in, int T, int F, int64_t ld_in, int64_t up_off,
+                   int64_t ld_out, void* out_bf16, float* out_f32, cudaStream_t st);
 void launch_residual_add(float* resid, const void* y, bool bf16_in, int64_t n, cudaStream_t st);
 
 }  // namespace air

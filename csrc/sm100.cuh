@@ -1,6 +1,6 @@
 // Thin inline-PTX wrappers for the sm_100a features used by the tensor-core kernels:
 // mbarriers with bounded waits, TMA (cp.async.bulk.tensor) loads, tcgen05 MMA / TMEM.
-// Written from the public PTX ISA; every wait has an iteration cap so a kernel can never
+// Written from the public PTX ISA; every wait has a wall-time cap so a kernel can never
 // spin forever (it records an error code and returns instead).
 #pragma once
 #include <cuda_runtime.h>
@@ -37,11 +37,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false (and the caller must stop) after `limit` polls.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = 1u << 26) {
-  for (uint32_t i = 0; i < limit; ++i)
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on an mbarrier phase. Gives up (returns false; the caller records an error
+// and winds down) after `limit_ns` of wall time, or as soon as any CTA of the grid has
+// raised the error word `abort_flag`, so a broken pipeline can never spin for long.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const int* abort_flag,
+                                          uint64_t limit_ns = 200ull * 1000 * 1000) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-  return false;
+    if ((i & 127) == 0) {
+      if (abort_flag && *(volatile const int*)abort_flag != 0) return false;
+      if (global_ns() - t0 > limit_ns) return false;
+    }
+  }
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

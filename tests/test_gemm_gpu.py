@@ -20,7 +20,8 @@ def _w(N, K, qt, seed):
 
 @pytest.mark.parametrize("qt", [GGMLType.Q4_K, GGMLType.BF16])
 @pytest.mark.parametrize("N,K,T,splits", [(128, 256, 1, 1), (384, 512, 5, 1), (256, 1024, 64, None),
-                                          (256, 2048, 64, 4), (512, 1024, 200, None), (4096, 4096, 16, None)])
+                                          (256, 2048, 64, 4), (512, 1024, 200, None), (4096, 4096, 16, None),
+                                          (200, 512, 33, None), (1456, 256, 33, 1)])
 def test_gemm_q_store(qt, N, K, T, splits):
     w, wd = _w(N, K, qt, 1)
     g = torch.Generator().manual_seed(2)
@@ -31,10 +32,11 @@ def test_gemm_q_store(qt, N, K, T, splits):
     gemm.linear(x.to(DEV), w, out, splits=splits, err=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    torch.testing.assert_close(out.cpu(), ref, rtol=2e-2, atol=2e-3)
+    tol = 1e-2 * float(ref.abs().max())  # A is rounded to bf16 after the GGUF scale math
+    torch.testing.assert_close(out.cpu(), ref, rtol=2e-2, atol=tol)
     outb = torch.zeros(T, N, dtype=torch.bfloat16, device=DEV)
     gemm.linear(x.to(DEV), w, outb, splits=splits)
-    torch.testing.assert_close(outb.float().cpu(), ref, rtol=2e-2, atol=4e-3)
+    torch.testing.assert_close(outb.float().cpu(), ref, rtol=2e-2, atol=2 * tol)
 
 
 def test_gemm_q_residual_and_repeat():
@@ -45,4 +47,4 @@ def test_gemm_q_residual_and_repeat():
     resid = torch.ones(T, N, device=DEV)
     for i in range(3):  # the split-K counters must reset themselves between calls
         gemm.linear(x.to(DEV), w, resid, residual=True)
-    torch.testing.assert_close(resid.cpu(), 1 + 3 * ref, rtol=2e-2, atol=5e-3)
+    torch.testing.assert_close(resid.cpu(), 1 + 3 * ref, rtol=2e-2, atol=3e-2 * float(ref.abs().max()))
