@@ -12,6 +12,7 @@
 // KV layer layout: [num_blocks, 2 (K,V), n_kv, block_size, head_dim] bf16.
 #include "common.cuh"
 #include "attention.h"
+#include <stdlib.h>
 
 namespace air {
 
@@ -19,6 +20,8 @@ namespace {
 
 constexpr int kD = 128;          // head_dim supported by the fast path (64 also instantiated)
 constexpr int kWarps = 4;
+constexpr int kTPW = 16;            // keys per warp per iteration (4 per pass, 8 lanes per key)
+constexpr int kNI = kTPW / 4;
 
 template <int D>
 struct Frag;  // per-lane slice sizes for a head dim
@@ -62,10 +65,10 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
   }
   __syncthreads();
 
-  // split_tokens <= 0: divide this row's context evenly over the splits (multiple of 32),
+  // split_tokens <= 0: divide this row's context evenly over the splits (multiple of kTPW),
   // so one captured launch serves every context length.
   const int st = split_tokens > 0 ? split_tokens
-                                  : ((ctx + n_splits - 1) / n_splits + 31) / 32 * 32;
+                                  : ((ctx + n_splits - 1) / n_splits + kTPW - 1) / kTPW * kTPW;
   int t_begin = split * st;
   int t_end = min(ctx, t_begin + st);
   if (rows.window > 0) t_begin = max(t_begin, ctx - rows.window);
@@ -84,33 +87,65 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
   const size_t blk_stride = 2 * kv_stride;
 
   const int grp = lane >> 3, gl = lane & 7;   // QK phase: 4 tokens per pass, 8 lanes per token
-  for (int c0 = t_begin + warp * 32; c0 < t_end; c0 += kWarps * 32) {
-    // ---- scores for tokens c0 .. c0+31: s[i][g] for token c0 + 4*i + grp ----
-    float s[8][G];
+  constexpr int KU = D / 64;                   // uint4 of K per lane per token
+  for (int c0 = t_begin + warp * kTPW; c0 < t_end; c0 += kWarps * kTPW) {
+    // ---- issue every K and V load of this 32-token chunk before any math ----
+    uint4 kreg[kNI][KU];
+    uint2 vreg[kNI][4];   // [i][gg]: V slice of token c0 + 4i + gg
+    bool kval[kNI];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < kNI; ++i) {
       const int t = c0 + 4 * i + grp;
-      const bool vis = key_visible(t, rows, r, ctx);
-      float part[G];
+      kval[i] = false;
 #pragma unroll
-      for (int g = 0; g < G; ++g) part[g] = 0.f;
-      if (t < ctx) {
+      for (int u = 0; u < KU; ++u) kreg[i][u] = make_uint4(0, 0, 0, 0);
+      if (t < t_end) {
         const int b = bt[t / block_size];
         if (b < 0 || b >= num_blocks) {
           set_error(err, kErrBounds);
         } else {
-          const __nv_bfloat16* kp = kv + (size_t)b * blk_stride + h * head_stride +
-                                    (size_t)(t % block_size) * D + gl * (D / 8);
+          kval[i] = true;
+          const uint4* kp = reinterpret_cast<const uint4*>(
+              kv + (size_t)b * blk_stride + h * head_stride + (size_t)(t % block_size) * D + gl * (D / 8));
 #pragma unroll
-          for (int u = 0; u < D / 64; ++u) {
-            float kf[8];
-            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(kp) + u), kf);
+          for (int u = 0; u < KU; ++u) kreg[i][u] = __ldg(kp + u);
+        }
+      }
+    }
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
+    for (int i = 0; i < kNI; ++i) {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) part[g] += kf[e] * q_s[g][gl * (D / 8) + u * 8 + e];
-            }
+      for (int gg = 0; gg < 4; ++gg) {
+        const int t = c0 + 4 * i + gg;
+        vreg[i][gg] = make_uint2(0, 0);
+        if (t < t_end) {
+          const int b = bt[t / block_size];
+          if (b >= 0 && b < num_blocks) {
+            const __nv_bfloat16* vp = kv + (size_t)b * blk_stride + kv_stride + h * head_stride +
+                                      (size_t)(t % block_size) * D + lane * DL;
+            if (DL == 4) vreg[i][gg] = __ldg(reinterpret_cast<const uint2*>(vp));
+            else vreg[i][gg].x = *reinterpret_cast<const uint32_t*>(vp);
           }
+        }
+      }
+    }
+    // ---- scores for tokens c0 .. c0+kTPW-1: s[i][g] for token c0 + 4*i + grp ----
+    float s[kNI][G];
+#pragma unroll
+    for (int i = 0; i < kNI; ++i) {
+      const int t = c0 + 4 * i + grp;
+      const bool vis = kval[i] && key_visible(t, rows, r, ctx);
+      float part[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) part[g] = 0.f;
+#pragma unroll
+      for (int u = 0; u < KU; ++u) {
+        float kf[8];
+        bf16x8_to_f32(kreg[i][u], kf);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) part[g] += kf[e] * q_s[g][gl * (D / 8) + u * 8 + e];
         }
       }
 #pragma unroll
@@ -123,18 +158,18 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
       }
     }
     // ---- online softmax ----
-    float p[8][G];
+    float p[kNI][G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float mx = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx = fmaxf(mx, s[i][g]);
+      for (int i = 0; i < kNI; ++i) mx = fmaxf(mx, s[i][g]);
       mx = warp_max(mx);
       const float mnew = fmaxf(m[g], mx);
       const float alpha = (mnew == -INFINITY) ? 1.f : __expf(m[g] - mnew);
       float sum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < kNI; ++i) {
         p[i][g] = (s[i][g] == -INFINITY) ? 0.f : __expf(s[i][g] - mnew);
         sum += p[i][g];
       }
@@ -145,37 +180,22 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
 #pragma unroll
       for (int j = 0; j < DL; ++j) acc[g][j] *= alpha;
     }
-    // ---- o += p · V ----
+    // ---- o += p . V (V already in registers; invisible / absent tokens have p = 0) ----
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < kNI; ++i) {
 #pragma unroll
       for (int gg = 0; gg < 4; ++gg) {
-        const int t = c0 + 4 * i + gg;
         float pv[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) pv[g] = __shfl_sync(0xffffffffu, p[i][g], gg * 8);
-        if (t < ctx) {
-          const int b = bt[t / block_size];
-          if (b >= 0 && b < num_blocks) {
-            const __nv_bfloat16* vp = kv + (size_t)b * blk_stride + kv_stride + h * head_stride +
-                                      (size_t)(t % block_size) * D + lane * DL;
-            float vf[DL];
-            if (DL == 4) {
-              const uint2 u = __ldg(reinterpret_cast<const uint2*>(vp));
-              const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
-              float2 a = __bfloat1622float2(hh[0]), bb = __bfloat1622float2(hh[1]);
-              vf[0] = a.x; vf[1] = a.y; vf[2 % DL] = bb.x; vf[3 % DL] = bb.y;
-            } else {
-              const __nv_bfloat162 u = *reinterpret_cast<const __nv_bfloat162*>(vp);
-              float2 a = __bfloat1622float2(u);
-              vf[0] = a.x; vf[1 % DL] = a.y;
-            }
+        float vf[4];
+        const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&vreg[i][gg]);
+        const float2 a0 = __bfloat1622float2(hh[0]), a1 = __bfloat1622float2(hh[1]);
+        vf[0] = a0.x; vf[1] = a0.y; vf[2] = a1.x; vf[3] = a1.y;
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
+        for (int g = 0; g < G; ++g) {
 #pragma unroll
-              for (int j = 0; j < DL; ++j) acc[g][j] += pv[g] * vf[j];
-            }
-          }
+          for (int j = 0; j < DL; ++j) acc[g][j] += pv[g] * vf[j];
         }
       }
     }
@@ -262,6 +282,8 @@ attn_quant_kernel(const float* __restrict__ out, int n_heads, int8_t* __restrict
 template <int D, int G>
 void launch_dg(const AttnArgs& a, cudaStream_t st) {
   dim3 grid(a.n_kv, a.n_rows, a.n_splits);
+  static const bool simt = getenv("AIR_ATTN_SIMT") != nullptr;
+  if (!(D == 128 && !simt && launch_paged_attention_mma(a, st)))
   paged_attn_kernel<D, G><<<grid, kWarps * 32, 0, st>>>(
       a.q, (const __nv_bfloat16*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_heads, a.n_kv,
       a.block_size, a.num_blocks, a.n_splits, a.split_tokens, a.scale, a.part_o, a.part_ml,

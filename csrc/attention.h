@@ -32,5 +32,7 @@ struct AttnArgs {
 };
 
 bool launch_paged_attention(const AttnArgs& a, cudaStream_t st);
+// tensor-core main pass (head_dim 128, group <= 8); false if the shape is not covered
+bool launch_paged_attention_mma(const AttnArgs& a, cudaStream_t st);
 
 }  // namespace air
