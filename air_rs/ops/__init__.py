@@ -184,10 +184,20 @@ def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EP
          rope_cs=None, positions=None, slots=None, kv=None, q_out=None, n_heads=0, n_kv=0,
          head_dim=0, block_size=0, rot_dim=0, err=None):
     ld = ld_out if ld_out is not None else w.N
-    require_ext().gemv(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, B, xq, xds, mode, out_f32,
-                       out_bf16, ld, resid, None if w2 is None else w2.data,
-                       None if w2 is None else w2.scales, rope_cs, positions, slots, kv, q_out,
-                       n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err)
+    ext = require_ext()
+    splits, ws, cnt = 1, None, None
+    if w.fmt == FMT_Q4K:
+        from .gemm import workspace
+        wsp = workspace(xq.device)
+        if err is None:
+            err = wsp.err
+        splits = ext.gemv_tiled_splits(w.N, w.K, mode)
+        if splits > 1:
+            ws, cnt = wsp.ensure(ext.gemv_tiled_workspace(w.N, splits, mode), ext.gemv_tiled_counters(w.N))
+    ext.gemv(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, B, xq, xds, mode, out_f32,
+             out_bf16, ld, resid, None if w2 is None else w2.data,
+             None if w2 is None else w2.scales, rope_cs, positions, slots, kv, q_out,
+             n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err, splits, ws, cnt)
     count_launch()
 
 

@@ -6,6 +6,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "kernels.h"
+#include "gemv_tiled.h"
 #include "attention.h"
 #include "sampler.h"
 #include "misc.h"
@@ -55,7 +56,8 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
           optional<Tensor> w2_data, optional<Tensor> w2_scales, optional<Tensor> rope_cs,
           optional<Tensor> positions, optional<Tensor> slots, optional<Tensor> kv,
           optional<Tensor> q_out, int64_t n_heads, int64_t n_kv, int64_t head_dim,
-          int64_t block_size, int64_t rot_dim, optional<Tensor> err) {
+          int64_t block_size, int64_t rot_dim, optional<Tensor> err, int64_t splits,
+          optional<Tensor> ws, optional<Tensor> counters) {
   check_cuda(data, "gemv weight");
   TORCH_CHECK(B >= 1 && B <= 8, "gemv: batch must be in [1, 8]");
   TORCH_CHECK(K % 32 == 0, "gemv: K must be a multiple of 32");
@@ -85,7 +87,24 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
   if (mode == air::kEpiQKVRope)
     TORCH_CHECK(ep.kv_cache && ep.q_out && ep.rope_cs && ep.positions && ep.slots,
                 "gemv qkv: rope/kv/q buffers required");
-  air::launch_gemv(w, (int)N, (int)K, (int)B, ptr<int8_t>(xq), ptr<float2>(xds), ep, stream());
+  if (fmt == air::kFmtQ4K) TORCH_CHECK(data.dim() == 4, "gemv q4k: expects the tiled device layout");
+  // the tiled kernel handles every Q4_K case except the QKV epilogue of head_dim != 128
+  if (fmt == air::kFmtQ4K && !(mode == air::kEpiQKVRope && head_dim != 128)) {
+    TORCH_CHECK(data.dim() == 4, "gemv q4k: expects the tiled device layout [N/128, K/256, 128, 144]");
+    TORCH_CHECK(ep.err, "gemv q4k: an error word is required (bounded waits report into it)");
+    const int s = (int)std::max<int64_t>(1, splits);
+    if (s > 1) {
+      TORCH_CHECK(ws.has_value() && counters.has_value(), "gemv q4k: split-K needs ws and counters");
+      TORCH_CHECK((size_t)ws->numel() >= air::gemv_tiled_workspace_floats((int)N, s, (int)mode), "gemv: ws too small");
+      TORCH_CHECK((size_t)counters->numel() >= air::gemv_tiled_counters((int)N), "gemv: counters too small");
+    }
+    air::GemvTiledScratch sc{ptr<float>(ws), ptr<int>(counters)};
+    const char* e = air::launch_gemv_tiled(w, (int)N, (int)K, (int)B, ptr<int8_t>(xq), ptr<float2>(xds), ep, sc,
+                                           s, stream());
+    TORCH_CHECK(e == nullptr, e ? e : "");
+  } else {
+    air::launch_gemv(w, (int)N, (int)K, (int)B, ptr<int8_t>(xq), ptr<float2>(xds), ep, stream());
+  }
   post_launch("gemv");
 }
 
@@ -191,6 +210,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "air_rs sm_100a kernels";
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("gemv", &gemv);
+  m.def("gemv_tiled_splits", [](int64_t N, int64_t K, int64_t mode) { return air::gemv_tiled_splits((int)N, (int)K, (int)mode); });
+  m.def("gemv_tiled_workspace", [](int64_t N, int64_t splits, int64_t mode) {
+    return (int64_t)air::gemv_tiled_workspace_floats((int)N, (int)splits, (int)mode); });
+  m.def("gemv_tiled_counters", [](int64_t N) { return (int64_t)air::gemv_tiled_counters((int)N); });
   m.def("paged_attention", &paged_attention);
   m.def("sampler", &sampler);
   m.def("count_tokens", &count_tokens);

@@ -153,7 +153,7 @@ def test_paged_decode_attention(splits, G):
     lens = [1, 37, 300, 1000]
     kv, bt, dense = _paged_setup(lens, nkv, d, bs)
     R = len(lens)
-    q = torch.randn(R, nh, d)
+    q = torch.randn(R, nh, d, generator=torch.Generator().manual_seed(5))
     out = torch.zeros(R, nh, d, device=DEV)
     part_o = torch.zeros(R * nh * splits * d, device=DEV)
     part_ml = torch.zeros(R * nh * splits * 2, device=DEV)
@@ -162,7 +162,8 @@ def test_paged_decode_attention(splits, G):
                         n_splits=splits, split_tokens=0, part_o=part_o, part_ml=part_ml)
     for i, l in enumerate(lens):
         ref = attention_reference(q[i:i + 1], dense[i][0], dense[i][1], causal=False)[0]
-        torch.testing.assert_close(out[i].cpu(), ref, rtol=2e-3, atol=2e-3)
+        # tensor-core path: Q and P enter the MMA as bf16
+        torch.testing.assert_close(out[i].cpu(), ref, rtol=1e-2, atol=8e-3)
 
 
 def test_paged_prefill_causal_and_tree():
