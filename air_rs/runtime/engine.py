@@ -243,6 +243,7 @@ class Engine:
                 torch.tensor([p.repetition_penalty for p in sp], dtype=torch.float32, device=dev),
                 torch.tensor([p.top_k for p in sp], dtype=torch.int32, device=dev),
                 torch.tensor([p.top_p for p in sp], dtype=torch.float32, device=dev),
+                mask=self._grammar_masks(pr, rn),
             )
             toks_h = toks.tolist()
             for r, d, t in zip(pr, done, toks_h):
@@ -343,6 +344,15 @@ class Engine:
             self.seqs.fill_table(seqs, st["tab"])
             si.block_tables.copy_(st["tab"], non_blocking=True)
             h2d += st["tab"].numel() * 4
+        gm = self._grammar_masks(batch, rn, B)
+        if gm is not None:
+            si.mask.copy_(gm)
+            self._mask_dirty = True
+            h2d += gm.numel() * 4
+        elif getattr(self, "_mask_dirty", False):
+            for m in rn.inputs.values():
+                m.mask.fill_(-1)
+            self._mask_dirty = False
         rn.decode(B, use_graph=True)
         st["tok"].copy_(si.tokens, non_blocking=True)
         ev = torch.cuda.Event()
@@ -351,6 +361,18 @@ class Engine:
         self.h2d_bytes_last_step = h2d
         self.d2h_bytes_last_step = B * 4
         return B, st, ev
+
+    def _grammar_masks(self, reqs, rn, B: int | None = None):
+        """[B, ceil(V/32)] allow-bits for the sampler, or None when no request is constrained."""
+        if not any(r.grammar is not None for r in reqs):
+            return None
+        words = (rn.V + 31) // 32
+        m = torch.full((B or len(reqs), words), -1, dtype=torch.int32)
+        for i, r in enumerate(reqs):
+            if r.grammar is not None:
+                bm = r.grammar.step_bitmask()
+                m[i, : bm.numel()] = bm[:words]
+        return m.to(rn.device)
 
     def seqs_changed_blocks(self, batch) -> bool:
         # a new block was opened for some sequence iff its new token starts a block
@@ -404,6 +426,7 @@ class Engine:
                 continue
             ib, B, p, ev = inflight
             chain = (not self.waiting and (max_steps is None or steps + 1 < max_steps) and
+                     all(r.grammar is None for r in ib) and
                      all(len(r.output_ids) + 2 <= r.params.max_tokens for r in ib))
             nxt = None
             if chain:
@@ -475,8 +498,8 @@ class Engine:
             return produced
         r = self.running[0]
         lg = apply_repetition_penalty(r._logits, r.prompt_ids + r.output_ids, r.params.repetition_penalty)
-        if r.grammar is not None and hasattr(r.grammar, "apply_to_logits"):
-            lg = r.grammar.apply_to_logits_tensor(lg) if hasattr(r.grammar, "apply_to_logits_tensor") else lg
+        if r.grammar is not None:
+            lg = r.grammar.apply_to_logits(lg.clone())
         tok = sample_cpu(lg, r.params, self._cpu_gen())
         self._emit(r, tok)
         produced.append((r.rid, tok))

@@ -39,6 +39,7 @@ class StepInputs:
     top_p: torch.Tensor        # [B] f32
     tokens: torch.Tensor       # [B] int32 output
     probs: torch.Tensor        # [B] f32 output (top-1 prob of the filtered nucleus)
+    mask: torch.Tensor         # [B, ceil(V/32)] int32 grammar allow-bits (all ones = no constraint)
 
 
 class ModelRunner:
@@ -127,6 +128,7 @@ class ModelRunner:
                 top_p=torch.ones(B, dtype=torch.float32, device=d),
                 tokens=torch.zeros(B, dtype=torch.int32, device=d),
                 probs=torch.zeros(B, dtype=torch.float32, device=d),
+                mask=torch.full((B, (self.V + 31) // 32), -1, dtype=torch.int32, device=d),
             )
             self.inputs[B] = si
         return si
@@ -240,7 +242,7 @@ class ModelRunner:
         logits = self.logits[:B]
         if self.tp_size > 1:
             logits = self.tp.all_gather_vocab(self.logits[:B], self.logits_full[:B])
-        ops.sample(logits, si.tokens, counts=self.counts, count_row=si.count_row,
+        ops.sample(logits, si.tokens, counts=self.counts, count_row=si.count_row, mask=si.mask,
                    temperature=si.temperature, penalty=si.penalty, top_k=si.top_k, top_p=si.top_p,
                    seed=self.seed, step=self.step_ctr, out_prob=si.probs, B=B, V=self.V)
         ops.count_tokens(self.counts, si.tokens, n=B, count_row=si.count_row)
@@ -292,7 +294,7 @@ class ModelRunner:
 
     def prefill(self, ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                 row_seq: torch.Tensor, block_tables: torch.Tensor, last_rows: torch.Tensor,
-                count_rows: torch.Tensor, temperature, penalty, top_k, top_p):
+                count_rows: torch.Tensor, temperature, penalty, top_k, top_p, mask=None):
         """Prompt tokens of one or more sequences (concatenated, T total).
 
         row_seq[t] indexes ``block_tables``; last_rows[s] is the row of each sequence's last
@@ -345,7 +347,7 @@ class ModelRunner:
             logits = self.tp.all_gather_vocab(logits, full)
         toks = torch.zeros(S, dtype=torch.int32, device=self.device)
         probs = torch.zeros(S, dtype=torch.float32, device=self.device)
-        ops.sample(logits, toks, counts=self.counts, count_row=count_rows, temperature=temperature,
+        ops.sample(logits, toks, counts=self.counts, count_row=count_rows, mask=mask, temperature=temperature,
                    penalty=penalty, top_k=top_k, top_p=top_p, seed=self.seed, step=self.step_ctr,
                    out_prob=probs, B=S, V=self.V)
         ops.count_tokens(self.counts, toks, n=S, count_row=count_rows)

@@ -142,12 +142,41 @@ class Tokenizer:
             return bs.decode("utf-8", errors="replace")
         return raw.replace("▁", " ")
 
+    @staticmethod
+    def _byte_piece(tok: str) -> int | None:
+        """SentencePiece byte-fallback token ``<0xNN>`` -> NN (else None)."""
+        if len(tok) == 6 and tok.startswith("<0x") and tok.endswith(">"):
+            try:
+                return int(tok[3:5], 16)
+            except ValueError:
+                return None
+        return None
+
     def decode(self, ids: list[int]) -> str:
-        raw = "".join(self.id_to_token[i] for i in ids if 0 <= i < len(self.id_to_token))
-        return self._raw_to_text(raw)
+        toks = [self.id_to_token[i] for i in ids if 0 <= i < len(self.id_to_token)]
+        if self.is_byte_level:
+            return self._raw_to_text("".join(toks))
+        # byte-fallback pieces are reassembled into UTF-8 (the reference prints them verbatim)
+        out, pending = [], bytearray()
+        for t in toks:
+            b = self._byte_piece(t)
+            if b is not None:
+                pending.append(b)
+                continue
+            if pending:
+                out.append(pending.decode("utf-8", errors="replace"))
+                pending = bytearray()
+            out.append(t.replace("▁", " "))
+        if pending:
+            out.append(pending.decode("utf-8", errors="replace"))
+        return "".join(out)
 
     def decode_token(self, i: int) -> str:
         raw = self.id_to_token[i] if 0 <= i < len(self.id_to_token) else "<unk>"
+        if not self.is_byte_level:
+            b = self._byte_piece(raw)
+            if b is not None:
+                return chr(b) if b < 0x80 else bytes([b]).decode("latin-1")
         return self._raw_to_text(raw)
 
     def token_texts(self) -> list[str]:
