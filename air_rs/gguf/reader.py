@@ -10,6 +10,7 @@ from __future__ import annotations
 import mmap
 import os
 import struct
+import warnings
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -193,5 +194,7 @@ def read_gguf(path: str | os.PathLike) -> GGUFFile:
         if abs_off + nb > len(mm):
             raise GGUFError(f"{path}: tensor {name} extends past end of file")
         tensors[name] = TensorInfo(name, dims, qt, abs_off, nb)
-    buf = torch.frombuffer(memoryview(mm), dtype=torch.uint8) if len(mm) else torch.empty(0, dtype=torch.uint8)
+    with warnings.catch_warnings():  # read-only mapping: tensors are views we never write
+        warnings.simplefilter("ignore", UserWarning)
+        buf = torch.frombuffer(memoryview(mm), dtype=torch.uint8) if len(mm) else torch.empty(0, dtype=torch.uint8)
     return GGUFFile(path, version, metadata, tensors, alignment, data_offset, mm, buf)

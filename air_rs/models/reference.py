@@ -156,6 +156,17 @@ class OracleModel:
         x1, x2 = x[..., :h], x[..., h:]
         return torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], -1)
 
+    def hidden(self, ids: list[int]) -> torch.Tensor:
+        """Final-norm hidden states [S, H] (F32) of a fresh sequence; the KV cache is reset."""
+        self.reset()
+        self._want_hidden = True
+        try:
+            self.forward(ids, 0)
+            return self._hidden
+        finally:
+            self._want_hidden = False
+            self.reset()
+
     def forward(self, ids: list[int], start_pos: int) -> torch.Tensor:
         """Runs ``ids`` at positions start_pos.. ; returns F32 logits of the last position."""
         cfg = self.cfg
@@ -184,6 +195,8 @@ class OracleModel:
             dn = qmatmul(a, L.w_down[0], L.w_down[1], L.w_down[2]).to(x.dtype)
             x = x + dn
         x = self.rms_norm(x, self.out_norm, cfg.rms_norm_eps)
+        if getattr(self, "_want_hidden", False):
+            self._hidden = x.float()
         last = x[-1:].float()
         return qmatmul(last, self.lm_head[0], self.lm_head[1], self.lm_head[2])[0]
 

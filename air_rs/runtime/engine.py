@@ -514,6 +514,34 @@ class Engine:
             g = self._gen = torch.Generator().manual_seed(0)
         return g
 
+    # ------------------------------------------------------------------ embeddings
+    def embed(self, ids: list[int]) -> list[float]:
+        """Mean-pooled final-norm hidden state of a prompt (``/v1/embeddings``).
+
+        The reference returns a hash of the input bytes here (``src/api.rs:770-780``); this is
+        the model's representation.
+        """
+        ids = ([self.cfg.bos_token_id] if self.add_bos else []) + list(ids)
+        if self.runner is None:
+            return self.oracle.hidden(ids).mean(0).tolist()
+        rn = self.runner
+        dev = rn.device
+        seq = self.seqs.create_sequence()
+        try:
+            slots = self.seqs.append(seq, len(ids))
+            tab = torch.full((1, rn.max_blocks), -1, dtype=torch.int32)
+            self.seqs.fill_table([seq], tab)
+            T = len(ids)
+            h = rn.prefill(torch.tensor(ids, dtype=torch.int32, device=dev),
+                           torch.arange(T, dtype=torch.int32, device=dev),
+                           torch.tensor(slots, dtype=torch.int64, device=dev),
+                           torch.zeros(T, dtype=torch.int32, device=dev), tab.to(dev),
+                           torch.tensor([T - 1], dtype=torch.int64, device=dev), None, None, None, None,
+                           None, return_hidden=True)
+            return h.mean(0).tolist()
+        finally:
+            self.seqs.free_sequence(seq)
+
     # ------------------------------------------------------------------ high level
     def generate_ids(self, prompts: list[list[int]], params: SamplingParams | None = None,
                      pipelined: bool = False) -> list[list[int]]:

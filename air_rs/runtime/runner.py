@@ -294,7 +294,8 @@ class ModelRunner:
 
     def prefill(self, ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                 row_seq: torch.Tensor, block_tables: torch.Tensor, last_rows: torch.Tensor,
-                count_rows: torch.Tensor, temperature, penalty, top_k, top_p, mask=None):
+                count_rows: torch.Tensor, temperature, penalty, top_k, top_p, mask=None,
+                return_hidden: bool = False):
         """Prompt tokens of one or more sequences (concatenated, T total).
 
         row_seq[t] indexes ``block_tables``; last_rows[s] is the row of each sequence's last
@@ -337,6 +338,10 @@ class ModelRunner:
                 self.linear(xn, lw.wgu, gu)
                 ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp, up_off=self.up_off)
                 self._proj_into_residual(hb, lw.wdown, x, o, tp)
+        if return_hidden:  # final-norm hidden states of every row (embeddings)
+            hn = self._ws("hn", (T, self.H), bf16)
+            ops.rmsnorm_quant(x, w.out_norm, eps, None, None, y_bf16=hn)
+            return hn.float()
         xl = x.index_select(0, last_rows.long())
         xs = self._ws("xs", (S, self.H), bf16)
         ops.rmsnorm_quant(xl, w.out_norm, eps, None, None, y_bf16=xs)

@@ -1,0 +1,101 @@
+"""REST server: routes, SSE streaming, error envelope, auth, rate limit, metrics (CPU)."""
+import json
+
+import pytest
+from fastapi.testclient import TestClient
+
+from air_rs.serve.app import create_app
+from air_rs.serve.dispatcher import EngineDispatcher, MockDispatcher
+from air_rs.serve.openai import LatencyHistogram, RateLimiter
+
+
+@pytest.fixture()
+def client():
+    return TestClient(create_app(MockDispatcher("mock"), "mock"))
+
+
+def test_chat_completion(client):
+    r = client.post("/v1/chat/completions", json={"model": "mock", "messages": [{"role": "user", "content": "hi"}]})
+    assert r.status_code == 200
+    body = r.json()
+    assert body["object"] == "chat.completion"
+    assert body["choices"][0]["message"]["content"] == "Hello, world!"
+    assert body["choices"][0]["finish_reason"] == "stop"
+    assert body["usage"]["completion_tokens"] == 4
+
+
+def test_chat_stream_sse(client):
+    with client.stream("POST", "/chat/completions",
+                       json={"messages": [{"role": "user", "content": "hi"}], "stream": True}) as r:
+        lines = [l for l in r.iter_lines() if l.startswith("data: ")]
+    assert lines[-1] == "data: [DONE]"
+    chunks = [json.loads(l[6:]) for l in lines[:-1]]
+    assert chunks[0]["choices"][0]["delta"]["role"] == "assistant"
+    assert "".join(c["choices"][0]["delta"].get("content", "") for c in chunks) == "Hello, world!"
+    assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
+
+
+def test_completions_length_and_models(client):
+    r = client.post("/v1/completions", json={"prompt": "x", "max_tokens": 2})
+    assert r.json()["choices"][0]["finish_reason"] == "length"
+    assert r.json()["choices"][0]["text"] == "Hello,"
+    assert client.get("/v1/models").json()["data"][0]["id"] == "mock"
+    assert client.get("/models/mock").status_code == 200
+    r = client.get("/v1/models/nope")
+    assert r.status_code == 404 and r.json()["error"]["code"] == "model_not_found"
+
+
+def test_errors_envelope(client):
+    r = client.post("/v1/chat/completions", json={"messages": []})
+    assert r.status_code == 400 and r.json()["error"]["type"] == "invalid_request_error"
+    r = client.post("/v1/completions", json={"prompt": "x", "temperature": 9})
+    assert r.status_code == 400
+    r = client.post("/v1/chat/completions", json={"model": "other", "messages": [{"role": "user", "content": "x"}]})
+    assert r.status_code == 404
+
+
+def test_embeddings_responses_health_metrics(client):
+    r = client.post("/v1/embeddings", json={"input": ["ab", "abc"]})
+    assert [d["embedding"][0] for d in r.json()["data"]] == [2.0, 3.0]
+    r = client.post("/v1/responses", json={"input": "hi", "instructions": "be nice"})
+    assert r.json()["output_text"] == "Hello, world!" and r.json()["status"] == "completed"
+    h = client.get("/health").json()
+    assert h["status"] == "ok" and h["requests_served"] >= 1
+    m = client.get("/metrics").text
+    assert "air_requests_total" in m and "air_ttft_ms_bucket" in m
+
+
+def test_auth_and_rate_limit():
+    c = TestClient(create_app(MockDispatcher("mock"), "mock", api_keys=["sk-1"], rate_limit=(0.0001, 2)))
+    body = {"prompt": "x"}
+    assert c.post("/v1/completions", json=body).status_code == 401
+    hdr = {"Authorization": "Bearer sk-1"}
+    assert c.post("/v1/completions", json=body, headers=hdr).status_code == 200
+    assert c.post("/v1/completions", json=body, headers=hdr).status_code == 200
+    assert c.post("/v1/completions", json=body, headers=hdr).status_code == 429
+
+
+def test_rate_limiter_refill_and_histogram():
+    rl = RateLimiter(rate=1.0, burst=1)
+    assert rl.allow("a", 0.0) and not rl.allow("a", 0.5) and rl.allow("a", 1.6)
+    h = LatencyHistogram()
+    for v in range(1, 101):
+        h.record(float(v))
+    assert h.percentile(50) == 50.0 and h.percentile(99) == 99.0
+
+
+def test_engine_dispatcher_cpu(tmp_path):
+    from air_rs.gguf import GGMLType
+    from air_rs.models.config import tiny_llama
+    from air_rs.models.random_init import write_random_gguf
+    from air_rs.runtime.builder import engine_from_gguf
+    p = write_random_gguf(str(tmp_path / "t.gguf"), tiny_llama(), GGMLType.Q8_0)
+    d = EngineDispatcher(engine_from_gguf(p, device="cpu"), "tiny")
+    try:
+        c = TestClient(create_app(d, "tiny"))
+        r = c.post("/v1/completions", json={"prompt": "ab", "max_tokens": 4, "temperature": 0})
+        assert r.status_code == 200 and r.json()["usage"]["completion_tokens"] >= 1
+        e = c.post("/v1/embeddings", json={"input": "abc"}).json()["data"][0]["embedding"]
+        assert len(e) == 256
+    finally:
+        d.shutdown()
