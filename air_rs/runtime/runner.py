@@ -295,7 +295,9 @@ class ModelRunner:
     def prefill(self, ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                 row_seq: torch.Tensor, block_tables: torch.Tensor, last_rows: torch.Tensor,
                 count_rows: torch.Tensor, temperature, penalty, top_k, top_p, mask=None,
-                return_hidden: bool = False):
+                return_hidden: bool = False, tree_base: torch.Tensor | None = None,
+                tree_mask: torch.Tensor | None = None, return_logits: bool = False,
+                ctx_len: torch.Tensor | None = None):
         """Prompt tokens of one or more sequences (concatenated, T total).
 
         row_seq[t] indexes ``block_tables``; last_rows[s] is the row of each sequence's last
@@ -315,7 +317,8 @@ class ModelRunner:
         o = self._ws("o", (T, self.H), bf16)
         gu = self._ws("gu", (T, self.gu_w), bf16) if self.w.layers[0].wgu is not None else None
         hb = self._ws("hb", (T, self.Fp), bf16, zero=True)
-        ctx = (positions + 1).to(torch.int32)
+        # keys [0, ctx) are candidates; tree rows pass their own bound (slot-based, not position)
+        ctx = ctx_len if ctx_len is not None else (positions + 1).to(torch.int32)
         tp = self.tp_size > 1
         ops.embed(w.embd, ids, out_f32=x, err=self.err, n=T)
         for li, lw in enumerate(w.layers):
@@ -327,7 +330,7 @@ class ModelRunner:
             ops.paged_attention(q, kv, block_tables, ctx, attn, n_rows=T, n_heads=self.nh,
                                 n_kv=self.nkv, head_dim=self.hd, block_size=self.block_size,
                                 row_seq=row_seq, n_splits=1, err=self.err,
-                                window=cfg.sliding_window or 0)
+                                window=cfg.sliding_window or 0, tree_base=tree_base, tree_mask=tree_mask)
             attn_b.copy_(attn)
             self._proj_into_residual(attn_b, lw.wo, x, o, tp)
             ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=xn)
@@ -350,6 +353,8 @@ class ModelRunner:
         if tp:
             full = self._ws("logits_full", (S, self.V), f32)
             logits = self.tp.all_gather_vocab(logits, full)
+        if return_logits:
+            return logits[:, : self.V].clone()
         toks = torch.zeros(S, dtype=torch.int32, device=self.device)
         probs = torch.zeros(S, dtype=torch.float32, device=self.device)
         ops.sample(logits, toks, counts=self.counts, count_row=count_rows, mask=mask, temperature=temperature,
