@@ -33,7 +33,7 @@ def launch_count() -> int:
 
 def reset_launch_count():
     _LAUNCHES[0] = 0
-EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_QKV_ROPE = 0, 1, 2, 3
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_QKV_ROPE, EPI_PEER_PUSH = 0, 1, 2, 3, 4
 
 
 def pad32(k: int) -> int:
@@ -182,7 +182,7 @@ def rmsnorm_quant(x: torch.Tensor | None, w: torch.Tensor | None, eps: float, q:
 def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EPI_STORE, *,
          out_f32=None, out_bf16=None, ld_out: int | None = None, resid=None, w2: QWeight | None = None,
          rope_cs=None, positions=None, slots=None, kv=None, q_out=None, n_heads=0, n_kv=0,
-         head_dim=0, block_size=0, rot_dim=0, err=None):
+         head_dim=0, block_size=0, rot_dim=0, err=None, push_meta=None):
     ld = ld_out if ld_out is not None else w.N
     ext = require_ext()
     splits, ws, cnt = 1, None, None
@@ -197,7 +197,7 @@ def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EP
     ext.gemv(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, B, xq, xds, mode, out_f32,
              out_bf16, ld, resid, None if w2 is None else w2.data,
              None if w2 is None else w2.scales, rope_cs, positions, slots, kv, q_out,
-             n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err, splits, ws, cnt)
+             n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err, splits, ws, cnt, push_meta)
     count_launch()
 
 

@@ -144,10 +144,16 @@ class ModelRunner:
         from ..ops import gemm
         return gemm.linear(x_bf16, w, out, self, residual=residual, err=self.err)
 
-    def _proj_into_residual(self, xin, w, x, obuf, tp: bool):
-        """x += xin @ W^T: fused into the GEMM epilogue, or partial + all-reduce under TP."""
-        if tp:
-            T = xin.shape[0]
+    def _proj_into_residual(self, xin, w, x, obuf, tp: bool, peer=None):
+        """x += xin @ W^T: fused into the GEMM epilogue, or partial + all-reduce under TP.
+
+        With a peer communicator the partial is pushed to every rank instead and the sum
+        happens in the next ``_norm`` (decode only)."""
+        T = xin.shape[0]
+        if peer is not None:
+            self.linear(xin, w, self.y[:T])
+            peer.push(self.y[:T], T)
+        elif tp:
             self.linear(xin, w, obuf[:T])
             self._residual_T(obuf[:T], T, x, tp)
         else:
@@ -158,25 +164,51 @@ class ModelRunner:
         """x += all_reduce(partial) across TP ranks (partial: [B, H] f32)."""
         self.tp.all_reduce_add(partial[:B], x[:B])
 
+    def _peer(self, B: int):
+        """The fused peer-memory all-reduce for a decode batch of B rows, if any."""
+        peer = getattr(self.tp, "peer", None) if self.tp_size > 1 else None
+        return peer if peer is not None and peer.fits(B, self.H) else None
+
+    def _row_parallel(self, w, xq, xds, B: int, x, peer):
+        """Decode GEMV of a row-parallel projection: x += sum over ranks of xq @ W^T."""
+        if peer is not None:
+            if w.fmt == ops.FMT_Q4K:
+                peer.push_gemv(w, xq, xds, B, err=self.err)
+            else:
+                ops.gemv(w, xq, xds, B, ops.EPI_STORE, out_f32=self.y[:B])
+                peer.push(self.y[:B], B)
+        elif self.tp_size > 1:
+            ops.gemv(w, xq, xds, B, ops.EPI_STORE, out_f32=self.y[:B])
+            self._reduce_into_residual(self.y, B, x)
+        else:
+            ops.gemv(w, xq, xds, B, ops.EPI_RESIDUAL, resid=x)
+
+    def _norm(self, x, w, B: int, xq=None, xds=None, y_bf16=None, peer=None):
+        """RMSNorm(+quant) of the residual stream; first completes a pending peer reduce."""
+        if peer is not None and peer.pending:
+            peer.reduce_norm(x[:B], w, self.cfg.rms_norm_eps, xq, xds, y_bf16, B)
+        else:
+            ops.rmsnorm_quant(x[:B], w, self.cfg.rms_norm_eps, xq, xds, y_bf16=y_bf16)
+
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int):
         cfg, w, si = self.cfg, self.w, self.inputs[B]
-        eps = cfg.rms_norm_eps
         x, xq, xds = self.x[:B], self.xq[:B], self.xds[:B]
         ops.embed(w.embd, si.ids, out_f32=x, err=self.err, n=B)
         gemv_path = B <= GEMV_MAX_B
         ns = self.n_splits(B)
         tp = self.tp_size > 1
+        peer = self._peer(B)
         for li, lw in enumerate(w.layers):
             kv = self.kv[li]
             if gemv_path:
-                ops.rmsnorm_quant(x, lw.attn_norm, eps, xq, xds)
+                self._norm(x, lw.attn_norm, B, xq, xds, peer=peer)
                 ops.gemv(lw.wqkv, xq, xds, B, ops.EPI_QKV_ROPE, rope_cs=self.rope_cs,
                          positions=si.positions, slots=si.slots, kv=kv, q_out=self.q[:B],
                          n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
                          block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
             else:
-                ops.rmsnorm_quant(x, lw.attn_norm, eps, None, None, y_bf16=self.xn_b[:B])
+                self._norm(x, lw.attn_norm, B, y_bf16=self.xn_b[:B], peer=peer)
                 self.linear(self.xn_b[:B], lw.wqkv, self.qkv_b[:B])
                 ops.rope_kv(self.qkv_b[:B], B, self.rope_cs, si.positions, si.slots, kv, self.q[:B],
                             n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
@@ -188,19 +220,15 @@ class ModelRunner:
                                 out_q=xq if gemv_path else None, out_ds=xds if gemv_path else None,
                                 err=self.err, window=cfg.sliding_window or 0)
             if gemv_path:
-                if tp:
-                    ops.gemv(lw.wo, xq, xds, B, ops.EPI_STORE, out_f32=self.y[:B])
-                    self._reduce_into_residual(self.y, B, x)
-                else:
-                    ops.gemv(lw.wo, xq, xds, B, ops.EPI_RESIDUAL, resid=x)
-                ops.rmsnorm_quant(x, lw.ffn_norm, eps, xq, xds)
-                self._ffn_gemv(lw, B, x, xq, xds, tp)
+                self._row_parallel(lw.wo, xq, xds, B, x, peer)
+                self._norm(x, lw.ffn_norm, B, xq, xds, peer=peer)
+                self._ffn_gemv(lw, B, x, xq, xds, tp, peer)
             else:
                 self.attn_b[:B].copy_(self.attn[:B])
-                self._proj_into_residual(self.attn_b[:B], lw.wo, x, self.o_b, tp)
-                ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=self.xn_b[:B])
-                self._ffn_gemm(lw, B, x, tp)
-        self._head(B, x, xq, xds, gemv_path)
+                self._proj_into_residual(self.attn_b[:B], lw.wo, x, self.o_b, tp, peer)
+                self._norm(x, lw.ffn_norm, B, y_bf16=self.xn_b[:B], peer=peer)
+                self._ffn_gemm(lw, B, x, tp, peer)
+        self._head(B, x, xq, xds, gemv_path, peer)
 
     def _residual(self, y_b: torch.Tensor, B: int, x: torch.Tensor, tp: bool):
         if tp:
@@ -209,35 +237,31 @@ class ModelRunner:
         else:
             ops.residual_add(x, y_b[:B])
 
-    def _ffn_gemv(self, lw, B, x, xq, xds, tp):
+    def _ffn_gemv(self, lw, B, x, xq, xds, tp, peer=None):
         if lw.wgu is None:
             from ..parallel import moe
             moe.moe_ffn_decode(self, lw, B, x, xq, xds)
             return
         ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, out_f32=self.h[:B], ld_out=self.Fp)
         ops.rmsnorm_quant(self.h[:B], None, 0.0, xq, xds)
-        if tp:
-            ops.gemv(lw.wdown, xq, xds, B, ops.EPI_STORE, out_f32=self.y[:B])
-            self._reduce_into_residual(self.y, B, x)
-        else:
-            ops.gemv(lw.wdown, xq, xds, B, ops.EPI_RESIDUAL, resid=x)
+        self._row_parallel(lw.wdown, xq, xds, B, x, peer)
 
-    def _ffn_gemm(self, lw, B, x, tp):
+    def _ffn_gemm(self, lw, B, x, tp, peer=None):
         if lw.wgu is None:
             from ..parallel import moe
             moe.moe_ffn_gemm(self, lw, B, x)
             return
         self.linear(self.xn_b[:B], lw.wgu, self.gu_b[:B])
         ops.swiglu(self.gu_b[:B], B, self.F, out_bf16=self.h_b[:B], ld_out=self.Fp, up_off=self.up_off)
-        self._proj_into_residual(self.h_b[:B], lw.wdown, x, self.o_b, tp)
+        self._proj_into_residual(self.h_b[:B], lw.wdown, x, self.o_b, tp, peer)
 
-    def _head(self, B, x, xq, xds, gemv_path):
+    def _head(self, B, x, xq, xds, gemv_path, peer=None):
         w, si = self.w, self.inputs[B]
         if gemv_path:
-            ops.rmsnorm_quant(x, w.out_norm, self.cfg.rms_norm_eps, xq, xds)
+            self._norm(x, w.out_norm, B, xq, xds, peer=peer)
             ops.gemv(w.lm_head, xq, xds, B, ops.EPI_STORE, out_f32=self.logits[:B])
         else:
-            ops.rmsnorm_quant(x, w.out_norm, self.cfg.rms_norm_eps, None, None, y_bf16=self.xn_b[:B])
+            self._norm(x, w.out_norm, B, y_bf16=self.xn_b[:B], peer=peer)
             self.linear(self.xn_b[:B], w.lm_head, self.logits[:B])
         logits = self.logits[:B]
         if self.tp_size > 1:
@@ -373,6 +397,9 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ misc
     def check_errors(self):
+        peer = getattr(self.tp, "peer", None) if self.tp_size > 1 else None
+        if peer is not None:
+            peer.check()
         e = int(self.err.item())
         if e:
             self.err.zero_()

@@ -130,7 +130,9 @@ def main():
     dev = torch.device("cuda", local)
     if tp is not None:
         from air_rs.parallel.symm import maybe_fused_tp
-        tp = maybe_fused_tp(tp, impl=args.impl)
+        from air_rs.models.config import PRESETS
+        tp = maybe_fused_tp(tp, impl="nccl" if args.impl == "baseline" else "ours", max_rows=args.batch,
+                            hidden=PRESETS[args.model]().hidden_dim, device=dev)
 
     B, P, K, W = args.batch, args.prompt_len, args.steps, args.warmup
     max_len = P + 1 + W + K + 8 + (K + 8 if not args.no_e2e else 0)
@@ -238,7 +240,9 @@ def main():
             "config": {"model": f"{args.model} ({args.quant})", "global_batch": B, "seq_len": P,
                        "decode_tokens_timed": K, "parallelism": f"tp{world}", "kv_block": rn.block_size,
                        "l2": "inputs larger than L2 (4.6 GB weights + KV per step); no flush",
-                       "gemm": "baseline" if args.impl == "baseline" else "ours"},
+                       "gemm": "baseline" if args.impl == "baseline" else "ours",
+                       "tp_allreduce": ("none" if world == 1 else
+                                        "nccl" if args.impl == "baseline" else "fused peer-memory push/reduce")},
             "p50_ttft_ms": round(ttft_ms, 3),
             "clocks": clk.summary(),
             "gpu_launches": int(launches),

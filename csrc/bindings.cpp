@@ -15,6 +15,7 @@
 
 void register_gemm_tc(pybind11::module_& m);
 void register_comm(pybind11::module_& m);
+air::PeerPush peer_push_from_meta(const at::Tensor& meta);
 
 using at::Tensor;
 using c10::optional;
@@ -57,7 +58,7 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
           optional<Tensor> positions, optional<Tensor> slots, optional<Tensor> kv,
           optional<Tensor> q_out, int64_t n_heads, int64_t n_kv, int64_t head_dim,
           int64_t block_size, int64_t rot_dim, optional<Tensor> err, int64_t splits,
-          optional<Tensor> ws, optional<Tensor> counters) {
+          optional<Tensor> ws, optional<Tensor> counters, optional<Tensor> push_meta) {
   check_cuda(data, "gemv weight");
   TORCH_CHECK(B >= 1 && B <= 8, "gemv: batch must be in [1, 8]");
   TORCH_CHECK(K % 32 == 0, "gemv: K must be a multiple of 32");
@@ -83,6 +84,12 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
   ep.rot_dim = (int)rot_dim;
   ep.err = ptr<int>(err);
   if (mode == air::kEpiSwiGLU) TORCH_CHECK(ep.w2.data, "gemv swiglu: w2 required");
+  if (mode == air::kEpiPeerPush) {
+    TORCH_CHECK(push_meta.has_value() && fmt == air::kFmtQ4K, "gemv peer push: Q4_K tiled weights and push meta");
+    ep.push = peer_push_from_meta(*push_meta);
+    TORCH_CHECK(B * ld_out <= ep.push.slot_elems && (N + 127) / 128 <= ep.push.max_tiles,
+                "gemv peer push: output exceeds the receive slot");
+  }
   if (mode == air::kEpiResidual) TORCH_CHECK(ep.resid, "gemv residual: resid required");
   if (mode == air::kEpiQKVRope)
     TORCH_CHECK(ep.kv_cache && ep.q_out && ep.rope_cs && ep.positions && ep.slots,

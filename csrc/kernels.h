@@ -18,6 +18,25 @@ enum GemvEpilogue : int {
   kEpiResidual = 1,   // resid[b, n] += acc (fp32 residual stream)
   kEpiSwiGLU = 2,     // out[b, n] = silu(W·x)[n] * (W2·x)[n]
   kEpiQKVRope = 3,    // rows = [q | k | v]; NeoX RoPE on q,k; k,v written to the paged cache
+  kEpiPeerPush = 4,   // tensor-parallel partial: stored into every rank's receive slot over
+                      // NVLink, then one flag per 128-row tile (see comm.h)
+};
+
+constexpr int kMaxPeers = 8;
+
+// Producer side of the fused tensor-parallel all-reduce. Every rank owns one receive
+// buffer, mapped into every peer process:
+//   flags [world][max_tiles] int32 (epoch values)  |  data [2][world][slot_elems] f32
+// A producer writes its [B, ld] partial into slot (parity, its rank) of every rank's
+// buffer, then stores flag[its rank][tile] = epoch + 1 (release, system scope) for each
+// 128-row output tile. `epoch` is the local collective counter, advanced by the consumer
+// (reduce_rmsnorm_quant) once all of its CTAs have read it.
+struct PeerPush {
+  float* data[kMaxPeers];     // per destination rank: its receive data base (mapped here)
+  int* flags[kMaxPeers];      // per destination rank: its flag base
+  const int* epoch;           // this rank's collective counter
+  int64_t slot_elems;
+  int world, rank, max_tiles;
 };
 
 struct GemvWeight {
@@ -44,6 +63,7 @@ struct GemvEpiParams {
   int n_heads, n_kv, head_dim, block_size, rot_dim;
   int64_t num_blocks;
   int* err;
+  PeerPush push;              // kEpiPeerPush
 };
 
 // x: activations quantised by rmsnorm_quant (int8 [B,K] + float2 [B,K/32]).
