@@ -56,5 +56,8 @@ def init_from_env(backend: str = "nccl") -> TPGroup | None:
     if not dist.is_initialized():
         if backend == "nccl":
             torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        dist.init_process_group(backend=backend)
+        from datetime import timedelta
+        # a lost rank ends the others' next collective with an error instead of a long hang
+        timeout = timedelta(seconds=float(os.environ.get("AIR_PG_TIMEOUT_S", "300")))
+        dist.init_process_group(backend=backend, timeout=timeout)
     return TPGroup()

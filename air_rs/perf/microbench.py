@@ -1,0 +1,168 @@
+"""Per-kernel microbenchmarks at Llama-3-8B decode / prefill shapes.
+
+``python -m air_rs.perf.microbench [--op gemv|gemm|attn|norm|all] [--name qkv|o|gateup|down|lm]
+[--batch B] [--iters N]`` prints one line per case: device time (CUDA events around a CUDA
+graph of N back-to-back launches, after warm-up), achieved bytes/s or FLOP/s, and the
+fraction of the measured HBM copy bandwidth / cuBLAS bf16 rate (``MEASURED_PEAKS.json`` at
+the repo root when present, else 6.65 TB/s and 1.59 PFLOP/s). Weights rotate over enough
+copies that every launch streams from HBM (working set > L2).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from .. import ops
+from ..gguf import GGMLType
+
+SHAPES = {"qkv": (6144, 4096), "o": (4096, 4096), "gateup": (28672, 4096), "down": (4096, 14336),
+          "lm": (128256, 4096)}
+L2_BYTES = 126e6
+
+
+def peaks() -> tuple[float, float, str]:
+    p = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return d["hbm_gbs"] * 1e9, d["bf16_tflops"] * 1e12, "of measured"
+    except (OSError, KeyError, ValueError):
+        return 6.65e12, 1.59e15, "of fallback"
+
+
+def ev_time(fn, iters: int = 20) -> float:
+    """Mean microseconds per call over a graph of ``iters`` calls."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(iters):
+                fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters * 1e3
+
+
+def _q4k_weights(N: int, K: int, dev, min_bytes: float = 4 * L2_BYTES):
+    """Random Q4_K tiles (valid f16 d/dmin) in enough copies to exceed L2."""
+    nb = K // 256
+    one = N * nb * 144
+    copies = max(1, int(min_bytes // one) + 1)
+    ws = []
+    for _ in range(copies):
+        d = torch.randint(0, 255, (N // 128, nb, 128, 144), dtype=torch.uint8, device=dev)
+        d[..., 0:4] = torch.tensor([0, 0x20, 0, 0x20], dtype=torch.uint8, device=dev)   # d = dmin = 2^-7
+        ws.append(ops.QWeight(ops.FMT_Q4K, d, None, N, K, GGMLType.Q4_K))
+    return ws, one
+
+
+def bench_gemv(name: str, B: int, iters: int, dev):
+    N, K = SHAPES[name]
+    ws, nbytes = _q4k_weights(N, K, dev)
+    xq = torch.randint(-100, 100, (B, K), dtype=torch.int8, device=dev)
+    xds = torch.rand(B, K // 32, 2, device=dev)
+    out = torch.zeros(B, N, device=dev)
+    i = [0]
+
+    def f():
+        w = ws[i[0] % len(ws)]
+        i[0] += 1
+        if name == "gateup":
+            ops.gemv(w.rows(0, N // 2), xq, xds, B, ops.EPI_SWIGLU, w2=w.rows(N // 2, N), out_f32=out, ld_out=N)
+        else:
+            ops.gemv(w, xq, xds, B, ops.EPI_STORE, out_f32=out)
+    us = ev_time(f, iters)
+    return us, nbytes, 2.0 * N * K * B
+
+
+def bench_gemm(name: str, T: int, iters: int, dev):
+    from ..ops import gemm
+    N, K = SHAPES[name]
+    ws, nbytes = _q4k_weights(N, K, dev)
+    x = torch.randn(T, K, device=dev).bfloat16()
+    out = torch.zeros(T, N, device=dev, dtype=torch.bfloat16)
+    i = [0]
+
+    def f():
+        gemm.linear(x, ws[i[0] % len(ws)], out)
+        i[0] += 1
+    us = ev_time(f, iters)
+    return us, nbytes + T * K * 2 + T * N * 2, 2.0 * N * K * T
+
+
+def bench_attn(B: int, ctx: int, iters: int, dev):
+    nkv, nh, d, bs = 8, 32, 128, 16
+    nblk = B * ((ctx + bs - 1) // bs)
+    copies = max(1, int(4 * L2_BYTES // (nblk * 2 * nkv * bs * d * 2)) + 1)
+    kvs = [torch.randn(nblk, 2, nkv, bs, d, device=dev).bfloat16() for _ in range(copies)]
+    bt = torch.arange(nblk, dtype=torch.int32, device=dev).view(B, -1)
+    q = torch.randn(B, nh, d, device=dev)
+    out = torch.zeros(B, nh, d, device=dev)
+    ns = max(1, min(32, -(-4 * 148 // (B * nkv))))
+    po = torch.zeros(B * nh * ns * d, device=dev)
+    pm = torch.zeros(B * nh * ns * 2, device=dev)
+    cl = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    i = [0]
+
+    def f():
+        ops.paged_attention(q, kvs[i[0] % copies], bt, cl, out, n_rows=B, n_heads=nh, n_kv=nkv, head_dim=d,
+                            block_size=bs, n_splits=ns, split_tokens=0, part_o=po, part_ml=pm)
+        i[0] += 1
+    us = ev_time(f, iters)
+    return us, B * ctx * 2 * nkv * d * 2, 4.0 * B * nh * ctx * d
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--op", default="all", choices=["all", "gemv", "gemm", "attn", "norm"])
+    ap.add_argument("--name", default=None, choices=list(SHAPES))
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--ctx", type=int, default=640)
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda")
+    bw, fl, tag = peaks()
+    names = [a.name] if a.name else list(SHAPES)
+
+    def line(kind, desc, us, nbytes, flops):
+        print(f"{kind:5s} {desc:34s} {us:9.1f} us  {nbytes / us / 1e3:7.0f} GB/s ({nbytes / us * 1e6 / bw:5.2f} {tag})"
+              f"  {flops / us / 1e6:7.1f} TFLOP/s ({flops / us * 1e6 / fl:5.3f} {tag})", flush=True)
+
+    if a.op in ("all", "gemv"):
+        for n in names:
+            for B in ([a.batch] if a.batch else [1, 8]):
+                us, nb, f = bench_gemv(n, B, a.iters, dev)
+                line("gemv", f"{n} N={SHAPES[n][0]} K={SHAPES[n][1]} B={B}", us, nb, f)
+    if a.op in ("all", "gemm"):
+        for n in names:
+            for T in ([a.batch] if a.batch else [16, 64, 512]):
+                us, nb, f = bench_gemm(n, T, a.iters, dev)
+                line("gemm", f"{n} N={SHAPES[n][0]} K={SHAPES[n][1]} T={T}", us, nb, f)
+    if a.op in ("all", "attn"):
+        for B in ([a.batch] if a.batch else [1, 64]):
+            us, nb, f = bench_attn(B, a.ctx, a.iters, dev)
+            line("attn", f"decode B={B} ctx={a.ctx}", us, nb, f)
+    if a.op in ("all", "norm"):
+        for K, B in [(4096, 1), (4096, 64), (14336, 8)]:
+            x = torch.randn(B, K, device=dev)
+            w = torch.rand(K, device=dev)
+            q = torch.empty(B, K, dtype=torch.int8, device=dev)
+            ds = torch.empty(B, K // 32, 2, device=dev)
+            us = ev_time(lambda: ops.rmsnorm_quant(x, w, 1e-5, q, ds), a.iters)
+            line("norm", f"rmsnorm_quant K={K} B={B}", us, B * K * 4 + B * K + B * K // 8, 0.0)
+
+
+if __name__ == "__main__":
+    main()

@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference", "baseline"])
     ap.add_argument("--ttft-runs", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                    help="TP all-reduce: fused peer-memory push/reduce, or NCCL (baseline arm)")
     return ap.parse_args()
 
 
@@ -131,7 +133,8 @@ def main():
     if tp is not None:
         from air_rs.parallel.symm import maybe_fused_tp
         from air_rs.models.config import PRESETS
-        tp = maybe_fused_tp(tp, impl="nccl" if args.impl == "baseline" else "ours", max_rows=args.batch,
+        ar_nccl = args.impl == "baseline" or args.allreduce == "nccl"
+        tp = maybe_fused_tp(tp, impl="nccl" if ar_nccl else "ours", max_rows=args.batch,
                             hidden=PRESETS[args.model]().hidden_dim, device=dev)
 
     B, P, K, W = args.batch, args.prompt_len, args.steps, args.warmup
@@ -242,7 +245,8 @@ def main():
                        "l2": "inputs larger than L2 (4.6 GB weights + KV per step); no flush",
                        "gemm": "baseline" if args.impl == "baseline" else "ours",
                        "tp_allreduce": ("none" if world == 1 else
-                                        "nccl" if args.impl == "baseline" else "fused peer-memory push/reduce")},
+                                        "nccl" if (args.impl == "baseline" or args.allreduce == "nccl")
+                                        else "fused peer-memory push/reduce")},
             "p50_ttft_ms": round(ttft_ms, 3),
             "clocks": clk.summary(),
             "gpu_launches": int(launches),
@@ -252,8 +256,25 @@ def main():
         }
         print(json.dumps(out))
     if tp is not None:
+        # Release everything that references the NCCL communicator or a peer's memory
+        # (graphs with captured collectives, IPC mappings) while every rank is still alive,
+        # then leave without tearing the communicator down: the process ends here anyway.
+        torch.cuda.synchronize()
         dist.barrier()
-        dist.destroy_process_group()
+        rn.graphs.clear()
+        del eng, rn
+        import gc
+        gc.collect()
+        torch.cuda.synchronize()
+        peer = getattr(tp, "peer", None)
+        if peer is not None:
+            dist.barrier()
+            peer.close()
+        dist.barrier()
+        torch.cuda.synchronize()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
     return 0
 
 

@@ -7,7 +7,7 @@
 //   warp 0      TMA producer: raw weight box (128 rows x one 256-weight super-block, the
 //               144-byte GGUF blocks copied verbatim) + the matching x boxes (SW128 swizzle)
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer (f32 accumulators in TMEM)
-//   warps 2..9  dequantise the staged Q4_K blocks into bf16 K-major SW128 tiles with packed
+//   warps 2..    (8 or 16 of them) dequantise the staged Q4_K blocks into bf16 K-major SW128 tiles with packed
 //               bf16x2 arithmetic (the GGUF scale/min math), then run the epilogue
 //               (tcgen05.ld -> store / residual add / split-K reduction).
 // Stages are handed over with mbarriers (TMA complete_tx, tcgen05.commit). Split-K uses a
@@ -30,22 +30,23 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kDqWarps = 8;                     // dequant + epilogue warps
-constexpr int kThreads = 64 + 32 * kDqWarps;
 constexpr int kRawRowBytes = 144;           // one Q4_K super-block of one row
 constexpr int kRawTile = 128 * kRawRowBytes; // 18432 B (multiple of 1024)
 constexpr int kATile = 128 * 128;            // 128 rows x 64 bf16
 
-template <int NT, int FMT, int NA>
+template <int NT, int FMT, int NA, bool AT>
 struct Cfg {
   static constexpr int kChunks = FMT == kFmtQ4K ? 4 : 1;         // 64-wide K chunks per stage
   static constexpr int kBChunk = NT * 128;                       // NT rows x 128 B
   static constexpr int kStageBytes = (FMT == kFmtQ4K ? kRawTile : kATile) + kChunks * kBChunk;
-  static constexpr int kABuf = FMT == kFmtQ4K ? NA * kATile : 0;
+  // dequantised A in shared memory (NA 64-wide chunks), unless AT: then it lives in TMEM
+  static constexpr int kABuf = (FMT == kFmtQ4K && !AT) ? NA * kATile : 0;
   static constexpr int kBudget = 227 * 1024 - 2048 - 1024;
   static constexpr int kStages = (kBudget - kABuf) / kStageBytes > 8 ? 8 : (kBudget - kABuf) / kStageBytes;
   static constexpr int kSmem = 1024 + kStages * kStageBytes + kABuf + 1024;
-  static constexpr int kTmemCols = NT < 32 ? 32 : NT;
+  // AT: accumulator in columns [0, 128), three 128-column stage buffers of A at 128, 256, 384
+  static constexpr int kTmemCols = AT ? 512 : (NT < 32 ? 32 : NT);
+  static constexpr int kATmemCol = 128;
   static_assert(kStages >= 2, "not enough shared memory for two stages");
 };
 
@@ -60,7 +61,8 @@ struct Bars {
   int last;
 };
 
-__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kDqWarps) : "memory"); }
+template <int DQ>
+__device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, %0;" ::"n"(32 * DQ) : "memory"); }
 
 // One 16-byte output chunk (8 bf16) = s * q - mm for 8 nibbles taken from 2 words.
 __device__ __forceinline__ uint32_t q4_pair(uint32_t t, __nv_bfloat162 s, __nv_bfloat162 negm) {
@@ -72,11 +74,12 @@ __device__ __forceinline__ uint32_t q4_pair(uint32_t t, __nv_bfloat162 s, __nv_b
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
-template <int NT, int FMT, int NA>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int NT, int FMT, int NA, int DQ, bool AT>
+__global__ void __launch_bounds__(64 + 32 * DQ, 1)
 gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
               GemmArgs a) {
-  using C = Cfg<NT, FMT, NA>;
+  using C = Cfg<NT, FMT, NA, AT>;
+  static_assert(!AT || FMT == kFmtQ4K, "A-in-TMEM path: Q4_K only");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -94,10 +97,10 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], FMT == kFmtQ4K ? kDqWarps + 1 : 1);
+      mbar_init(&bars->empty[s], FMT == kFmtQ4K ? (AT ? 8 : DQ) + 1 : 1);
     }
-    for (int i = 0; i < NA; ++i) {
-      mbar_init(&bars->afull[i], kDqWarps);
+    for (int i = 0; i < (AT ? 3 : NA); ++i) {
+      mbar_init(&bars->afull[i], AT ? 8 : DQ);
       mbar_init(&bars->aempty[i], 1);
     }
     mbar_init(&bars->done, 1);
@@ -114,6 +117,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
   long long* dbg = (a.dbg && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) ? a.dbg : nullptr;
+  // profiling aid (dbg[255], only with a dbg buffer): 1 = skip the dequant math, 2 = skip the MMAs
+  const int dmode = a.dbg ? (int)a.dbg[255] : 0;
   if (dbg && threadIdx.x == 0) dbg[225] = clock64();
 
   if (warp == 0) {
@@ -159,6 +164,23 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         const int s = i % C::kStages;
         if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1, a.err)) { ok = false; break; }
         uint8_t* st = stages + s * C::kStageBytes;
+        if constexpr (AT) {
+          const int ab = i % 3;
+          if (!mbar_wait(&bars->afull[ab], (i / 3) & 1, a.err)) { ok = false; break; }
+          tc_fence_after();
+          if (dbg && i < 64) dbg[32 + i] = clock64();
+          const uint32_t ta = tmem + C::kATmemCol + 128 * ab;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint64_t bd = sw128_desc(st + kRawTile + c * C::kBChunk);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)  // K16 steps: 8 TMEM columns of A, +32 B of B
+              if (dmode != 2) mma_bf16_ts(tmem, ta + 32 * c + 8 * k, bd + 2 * k, idesc, (i | c | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&bars->aempty[ab]);
+          mma_commit(&bars->empty[s]);
+          continue;
+        }
         for (int c = 0; c < C::kChunks; ++c, ++g) {
           const uint8_t* A;
           if (FMT == kFmtQ4K) {
@@ -169,6 +191,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
             A = st;
           }
           tc_fence_after();
+          if (dbg && g < 64) dbg[32 + g] = clock64();
           const uint64_t ad = sw128_desc(A);
           const uint64_t bd = sw128_desc(st + (FMT == kFmtQ4K ? kRawTile : kATile) + c * C::kBChunk);
 #pragma unroll
@@ -186,14 +209,78 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
     }
   } else {
     // ------------------------------------------------------------ dequant (Q4_K)
-    // Thread = (weight row t, nibble half hf): hf = 0 expands the low nibbles (sub-blocks
-    // 0,2,4,6 of the super-block), hf = 1 the high nibbles (1,3,5,7). Scales are decoded once
-    // per stage; per 64-wide chunk a thread turns 32 code bytes into 32 bf16 with 3 ops per
-    // pair: PRMT places two nibbles under a 0x43 exponent byte (= 128 + q, exact), HSUB2
-    // removes the 128, HFMA2 applies d*sc and -dmin*m.
+    // Thread = (weight row t, nibble half hf, code-byte part sub): hf = 0 expands the low
+    // nibbles (sub-blocks 0,2,4,6 of the super-block), hf = 1 the high nibbles (1,3,5,7);
+    // with 16 warps each (row, half) is further split into two 16-byte parts. Scales are
+    // decoded once per stage; per 64-wide chunk a thread turns its code bytes into bf16 with
+    // 3 ops per pair: PRMT places two nibbles under a 0x43 exponent byte (= 128 + q, exact),
+    // HSUB2 removes the 128, HFMA2 applies d*sc and -dmin*m.
+    constexpr int kParts = DQ / 8;             // 1 or 2 code-byte parts per (row, half)
+    constexpr int kWords = 8 / kParts;          // 32-bit code words per thread per chunk
     const int t = (threadIdx.x - 64) & 127;
-    const int hf = (threadIdx.x - 64) >> 7;   // warp-uniform
-    if (FMT == kFmtQ4K) {
+    const int hf = ((threadIdx.x - 64) >> 7) / kParts;   // warp-uniform
+    const int sub = ((threadIdx.x - 64) >> 7) % kParts;
+    if constexpr (AT) {
+      // A in TMEM: warp w owns TMEM lanes 32*(w%4).. (rows), h = which nibble half; per
+      // stage a thread writes 4 chunks x 16 columns of its row (two bf16 per column), then
+      // one wait::st + fence + arrive hands the whole stage to the MMA issuer. With 16
+      // warps, two groups of 8 take alternate stages, so one group's fixed per-stage
+      // latency (shared-memory loads, TMEM store completion) overlaps the other's work;
+      // three TMEM stage buffers let both groups run ahead of the MMA.
+      constexpr int G = DQ / 8;
+      const int grp = (warp - 2) >> 3;
+      const int r = 32 * (warp & 3) + lane;
+      const int h = ((warp - 2) >> 2) & 1;
+      const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
+      bool ok = true;
+      for (int i = grp; i < nk; i += G) {
+        const int s = i % C::kStages;
+        const int ab = i % 3;
+        if (i >= 3 && !mbar_wait(&bars->aempty[ab], ((i / 3) - 1) & 1, a.err)) { ok = false; break; }
+        if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1, a.err)) { ok = false; break; }
+        if (dbg && threadIdx.x == 64 && i < 64) dbg[96 + i] = clock64();
+        const uint8_t* rb = stages + s * C::kStageBytes + r * kRawRowBytes;
+        const uint32_t hdr = *reinterpret_cast<const uint32_t*>(rb);
+        const float d = __half2float(__ushort_as_half((unsigned short)(hdr & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr >> 16)));
+        const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + C::kATmemCol + 128 * ab + 16 * h;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          int sc, mn;
+          q4k_scale_min(rb + 4, 2 * c + h, sc, mn);
+          const __nv_bfloat162 sv = __float2bfloat162_rn(d * (float)sc);
+          const __nv_bfloat162 mv = __float2bfloat162_rn(-dmin * (float)mn);
+          const uint4 qa = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
+          const uint4 qb = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
+          uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          uint32_t o[16];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t wk = h ? (w[k] >> 4) & 0x0F0F0F0Fu : w[k] & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const uint32_t v = __byte_perm(wk, 0x43434343u, e ? 0x4342 : 0x4140);
+              __nv_bfloat162 bv = *reinterpret_cast<const __nv_bfloat162*>(&v);
+              bv = __hfma2(__hsub2(bv, c128), sv, mv);
+              o[2 * k + e] = *reinterpret_cast<uint32_t*>(&bv);
+            }
+          }
+          if (dmode != 1) tmem_st16(ta + 32 * c, o);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bars->afull[ab]);
+          mbar_arrive(&bars->empty[s]);
+        }
+        if (dbg && threadIdx.x == 64 && i < 64) dbg[160 + i] = clock64();
+      }
+      if (!ok) {
+        set_error(a.err, kErrTimeout);
+        bars->abort = 1;
+      }
+    } else if (FMT == kFmtQ4K) {
       int g = 0;
       bool ok = true;
       const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
@@ -217,18 +304,25 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
           const int ab = g % NA;
           if (g >= NA && !mbar_wait(&bars->aempty[ab], ((g / NA) - 1) & 1, a.err)) { ok = false; break; }
           if (dbg && threadIdx.x == 64 && g < 64) dbg[96 + g] = clock64();
-          const uint4 qa = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
-          const uint4 qb = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
-          uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          uint32_t w[kWords];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) w[k] = hf ? (w[k] >> 4) & 0x0F0F0F0Fu : w[k] & 0x0F0F0F0Fu;
+          for (int u = 0; u < kWords / 4; ++u) {
+            const uint4 qv = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c + 16 * (sub + u));
+            w[4 * u] = qv.x;
+            w[4 * u + 1] = qv.y;
+            w[4 * u + 2] = qv.z;
+            w[4 * u + 3] = qv.w;
+          }
+#pragma unroll
+          for (int k = 0; k < kWords; ++k) w[k] = hf ? (w[k] >> 4) & 0x0F0F0F0Fu : w[k] & 0x0F0F0F0Fu;
           uint8_t* arow = abuf + ab * kATile + t * 128;
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
+          for (int c2 = 0; c2 < kWords / 2; ++c2) {
+            const int cc = c2 + sub * (kWords / 2);
             uint32_t o[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const uint32_t v = __byte_perm(w[2 * cc + (e >> 1)], 0x43434343u, (e & 1) ? 0x4342 : 0x4140);
+              const uint32_t v = __byte_perm(w[2 * c2 + (e >> 1)], 0x43434343u, (e & 1) ? 0x4342 : 0x4140);
               __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&v);
               b = __hfma2(__hsub2(b, c128), sv[c], mv[c]);
               o[e] = *reinterpret_cast<uint32_t*>(&b);
@@ -254,8 +348,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
     tc_fence_after();
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int m = 32 * q + lane;     // weight row within the tile
-    const int jh = (warp - 2) >> 2;  // the kDqWarps/4 warps of a quarter split the column groups
-    constexpr int kJW = kDqWarps / 4;
+    const int jh = (warp - 2) >> 2;  // the DQ/4 warps of a quarter split the column groups
+    constexpr int kJW = DQ / 4;
     const int mg = m0 + m;
     // warp-uniform: every tcgen05.ld below must be executed by all 32 lanes or none
     const bool valid = __all_sync(0xffffffffu, done_ok && !(*(volatile int*)&bars->abort) && nk > 0);
@@ -272,12 +366,12 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         for (int e = 0; e < 16; ++e) part[(16 * j + e) * 128 + m] = valid ? v[e] : 0.f;
       }
       __threadfence();
-      named_sync_epi();
+      named_sync_epi<DQ>();
       if (threadIdx.x == 64) {
         const int old = atomicAdd(&a.counters[tile], 1);
         bars->last = (old == splits - 1);
       }
-      named_sync_epi();
+      named_sync_epi<DQ>();
       if (!bars->last) goto finish;
       __threadfence();
       if (threadIdx.x == 64) a.counters[tile] = 0;  // self-cleaning for the next call
@@ -349,10 +443,10 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT, int FMT, int NA>
+template <int NT, int FMT, int NA, int DQ, bool AT = false>
 const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
                       dim3 grid, cudaStream_t st) {
-  using C = Cfg<NT, FMT, NA>;
+  using C = Cfg<NT, FMT, NA, AT>;
   CUtensorMap tw, tx;
   bool ok;
   GemmArgs b = a;
@@ -369,34 +463,41 @@ const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, con
     return "cuTensorMapEncodeTiled failed for the activation operand";
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(gemm_q_kernel<NT, FMT, NA>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+    if (cudaFuncSetAttribute(gemm_q_kernel<NT, FMT, NA, DQ, AT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
         cudaSuccess)
       return "cudaFuncSetAttribute(max dynamic smem) failed";
     attr = true;
   }
-  gemm_q_kernel<NT, FMT, NA><<<grid, kThreads, C::kSmem, st>>>(tw, tx, b);
+  gemm_q_kernel<NT, FMT, NA, DQ, AT><<<grid, 64 + 32 * DQ, C::kSmem, st>>>(tw, tx, b);
   return nullptr;
 }
 
-// Number of dequantised A buffers in flight between the dequant warps and the MMA issuer.
-int a_buffers() {
-  static int na = 0;
-  if (!na) {
-    const char* e = getenv("AIR_GEMM_NA");
-    na = (e && atoi(e) == 2) ? 2 : 4;
+// Q4_K variant: "tmem" (default) keeps the dequantised A operand in tensor memory;
+// AIR_GEMM_A=smem selects the shared-memory A path; AIR_GEMM_DQ=16 doubles the dequant warps.
+int a_path() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("AIR_GEMM_A");
+    const char* q = getenv("AIR_GEMM_DQ");
+    v = (e && strcmp(e, "smem") == 0) ? ((q && atoi(q) == 16) ? 2 : 1) : 0;
   }
-  return na;
+  return v;
 }
 
 template <int NT, int FMT>
 const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
                      dim3 grid, cudaStream_t st) {
-  if constexpr (FMT == kFmtQ4K && NT == 128) {
-    return launch_na<NT, FMT, 2>(a, w, w_row_bytes, x, ldx, grid, st);
-  } else {
-    if (FMT == kFmtQ4K && a_buffers() == 2) return launch_na<NT, FMT, 2>(a, w, w_row_bytes, x, ldx, grid, st);
-    return launch_na<NT, FMT, 4>(a, w, w_row_bytes, x, ldx, grid, st);
+  constexpr int NA = (FMT == kFmtQ4K && NT == 128) ? 2 : 4;
+  if constexpr (FMT == kFmtQ4K) {
+    const int p = a_path();
+    if (p == 0) {
+      const char* e = getenv("AIR_GEMM_DQ");
+      if (e && atoi(e) == 16) return launch_na<NT, FMT, NA, 16, true>(a, w, w_row_bytes, x, ldx, grid, st);
+      return launch_na<NT, FMT, NA, 8, true>(a, w, w_row_bytes, x, ldx, grid, st);
+    }
+    if (p == 2) return launch_na<NT, FMT, NA, 16>(a, w, w_row_bytes, x, ldx, grid, st);
   }
+  return launch_na<NT, FMT, NA, 8>(a, w, w_row_bytes, x, ldx, grid, st);
 }
 
 }  // namespace
@@ -412,7 +513,9 @@ int gemm_q_splits(int N, int K, int T, int fmt) {
   const int nt = gemm_q_token_tile(T);
   const int tiles = ((N + 127) / 128) * ((T + nt - 1) / nt);
   const int ksteps = fmt == kFmtQ4K ? K / 256 : K / 64;
-  int s = (148 + tiles - 1) / tiles;
+  // as many K splits as fit in ONE wave of 148 CTAs (a partial second wave costs a whole
+  // wave of time); more than one wave of tiles already fills the machine
+  int s = 148 / tiles;
   s = s < 1 ? 1 : s;
   const int max_s = ksteps / 2 > 0 ? ksteps / 2 : 1;  // at least two K-steps per split
   return s > max_s ? max_s : s;
