@@ -2,13 +2,14 @@
 all-reduce after the row-parallel O and down projections, ``src/model.rs:596-607,728-739``,
 ``src/distributed.rs``).
 
-Each rank cudaMallocs one receive buffer (``flags | data[2][world][slot]``), exports a CUDA
-IPC handle, and maps every peer's buffer into its own address space. The row-parallel
-projection pushes finished output tiles into every rank's buffer and flags them (the GEMV
-epilogue ``EPI_PEER_PUSH``, or ``peer_push`` after the tcgen05 GEMM); the following RMSNorm
-(``reduce_rmsnorm_quant``) waits on its local flags, sums the partials into the residual
-stream and quantises the normalised row for the next GEMV. All state is device-resident
-(epoch counter, flags), so the sequence is CUDA-graph capturable and replayable.
+Each rank cudaMallocs one receive buffer (``[2 parities][world][slot]`` of 8-byte
+(value, tag) elements), exports a CUDA IPC handle, and maps every peer's buffer into its
+own address space. The row-parallel projection pushes every finished output element into
+every rank's buffer as one tagged 8-byte store (the GEMV epilogue ``EPI_PEER_PUSH``, or
+``peer_push`` after the tcgen05 GEMM); the following RMSNorm (``reduce_rmsnorm_quant``)
+waits per element for this collective's tag in its local buffer, sums the partials into
+the residual stream and quantises the normalised row for the next GEMV. All state is
+device-resident (epoch counter, tags), so the sequence is CUDA-graph capturable.
 
 ``PeerComm.local_group`` builds W communicators on one GPU whose "peer" buffers are local
 allocations: the same kernels run with every rank's data in one process, which is how the
@@ -16,8 +17,6 @@ protocol is tested with fewer GPUs than ranks (producers never wait, so running 
 launches one after another on one stream is always safe).
 """
 from __future__ import annotations
-
-import math
 
 import torch
 import torch.distributed as dist
@@ -30,43 +29,35 @@ DEFAULT_TIMEOUT_S = 2.0
 
 
 class PeerComm:
-    def __init__(self, bases: list[int], rank: int, device, slot_elems: int, max_tiles: int, owned: list,
+    def __init__(self, bases: list[int], rank: int, device, slot_elems: int, owned: list,
                  timeout_s: float = DEFAULT_TIMEOUT_S):
-        ext = ops.require_ext()
         self.world = len(bases)
         if not 1 <= self.world <= MAX_PEERS:
             raise ValueError(f"peer all-reduce supports 1..{MAX_PEERS} ranks")
         self.rank, self.device = rank, torch.device(device)
-        self.slot_elems, self.max_tiles = slot_elems, max_tiles
+        self.slot_elems = slot_elems
         self._owned = owned                       # keeps buffers / IPC mappings alive
-        fb = ext.peer_flags_bytes(self.world, max_tiles)
         self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
-        pm = [0] * 21
-        for r, b in enumerate(bases):
-            pm[r] = b + fb
-            pm[8 + r] = b
-        pm[16], pm[17], pm[18], pm[19], pm[20] = self.epoch.data_ptr(), slot_elems, self.world, rank, max_tiles
+        pm = [0] * 12
+        pm[:len(bases)] = bases
+        pm[8], pm[9], pm[10], pm[11] = self.epoch.data_ptr(), slot_elems, self.world, rank
         self.push_meta = torch.tensor(pm, dtype=torch.int64)
-        me = bases[rank]
-        self.reduce_meta = torch.tensor([me + fb, me, self.epoch.data_ptr(), self.done.data_ptr(),
-                                         self.err.data_ptr(), slot_elems, self.world, max_tiles, max_tiles,
-                                         int(timeout_s * 1e9)], dtype=torch.int64)
+        self.reduce_meta = torch.tensor([bases[rank], self.epoch.data_ptr(), self.done.data_ptr(),
+                                         self.err.data_ptr(), slot_elems, self.world, int(timeout_s * 1e9)],
+                                        dtype=torch.int64)
         self.pending = False
 
     # ----------------------------------------------------------------- construction
-    @staticmethod
-    def _sizes(max_rows: int, hidden: int):
-        return max_rows * hidden, math.ceil(hidden / 128)
 
     @classmethod
     def create(cls, tp: TPGroup, max_rows: int, hidden: int, device, timeout_s: float = DEFAULT_TIMEOUT_S):
         """Collective: every rank of ``tp`` calls this; exchanges IPC handles."""
         ext = ops.require_ext()
         dev = torch.device(device)
-        slot, tiles = cls._sizes(max_rows, hidden)
-        buf = ext.comm_alloc(ext.peer_buffer_bytes(tp.world_size, tiles, slot), dev.index or 0)
+        slot = max_rows * hidden
+        buf = ext.comm_alloc(ext.peer_buffer_bytes(tp.world_size, slot), dev.index or 0)
         handles = [None] * tp.world_size
         dist.all_gather_object(handles, ext.ipc_handle(buf), group=tp.group)
         bases, opened = [], []
@@ -77,7 +68,7 @@ class PeerComm:
                 p = ext.ipc_open(h, dev.index or 0)
                 opened.append(p)
                 bases.append(p)
-        comm = cls(bases, tp.rank, dev, slot, tiles, [buf], timeout_s)
+        comm = cls(bases, tp.rank, dev, slot, [buf], timeout_s)
         comm._opened = opened
         torch.cuda.synchronize(dev)
         dist.barrier(group=tp.group)             # every buffer is zeroed before any push
@@ -88,10 +79,10 @@ class PeerComm:
         """``world`` communicators on one GPU (all buffers local); see the module docstring."""
         ext = ops.require_ext()
         dev = torch.device(device)
-        slot, tiles = cls._sizes(max_rows, hidden)
-        bufs = [ext.comm_alloc(ext.peer_buffer_bytes(world, tiles, slot), dev.index or 0) for _ in range(world)]
+        slot = max_rows * hidden
+        bufs = [ext.comm_alloc(ext.peer_buffer_bytes(world, slot), dev.index or 0) for _ in range(world)]
         bases = [b.data_ptr() for b in bufs]
-        return [cls(bases, r, dev, slot, tiles, bufs, timeout_s) for r in range(world)]
+        return [cls(bases, r, dev, slot, bufs, timeout_s) for r in range(world)]
 
     def close(self):
         ext = ops.require_ext()
@@ -101,7 +92,7 @@ class PeerComm:
 
     # ----------------------------------------------------------------- producer side
     def fits(self, B: int, N: int) -> bool:
-        return B * N <= self.slot_elems and math.ceil(N / 128) <= self.max_tiles
+        return B * N <= self.slot_elems
 
     def push_gemv(self, w: ops.QWeight, xq, xds, B: int, err=None):
         """Row-parallel decode GEMV whose epilogue pushes the partial to every rank."""
@@ -120,8 +111,7 @@ class PeerComm:
         """x += sum of all ranks' pushed partials, then RMSNorm (+ Q8A quantisation)."""
         B = B if B is not None else x.shape[0]
         K = x.shape[1]
-        ops.require_ext().reduce_rmsnorm_quant(self.reduce_meta, x, w, w_offset, eps, B, K, xq, xds, y_bf16,
-                                               math.ceil(K / 128))
+        ops.require_ext().reduce_rmsnorm_quant(self.reduce_meta, x, w, w_offset, eps, B, K, xq, xds, y_bf16)
         ops.count_launch()
         self.pending = False
 

@@ -11,6 +11,21 @@ namespace {
 constexpr int kThreads = 1024;
 constexpr int kMaxPer = 16;   // K <= 16 * 1024
 
+// Wait (bounded) until the element carries this collective's tag; returns its value.
+__device__ __forceinline__ float wait_tagged(const uint2* p, uint32_t tag, int64_t timeout_ns, bool& timed_out) {
+  uint2 v = ld_tagged(p);
+  if (v.y == tag) return __uint_as_float(v.x);
+  const uint64_t t0 = sm100::global_ns();
+  for (uint32_t it = 1;; ++it) {
+    v = ld_tagged(p);
+    if (v.y == tag) return __uint_as_float(v.x);
+    if ((it & 31) == 0 && sm100::global_ns() - t0 > (uint64_t)timeout_ns) {
+      timed_out = true;
+      return 0.f;
+    }
+  }
+}
+
 // Grid (1, B): one CTA per row, so the reduced row can be held in registers between the
 // sum-of-squares pass and the quantisation pass (no other CTA reads x meanwhile).
 __global__ void __launch_bounds__(kThreads)
@@ -20,25 +35,10 @@ reduce_rmsnorm_quant_kernel(PeerReduce r, float* __restrict__ x, const float* __
   __shared__ float red[32];
   const int b = blockIdx.y, t = threadIdx.x;
   const int e = *(volatile const int*)r.epoch;
-  const int par = e & 1;
-  // ---- wait for every rank's flag of every tile (local memory, bounded) ----
-  const int nflags = r.world * r.ntiles;
+  const uint32_t tag = (uint32_t)e + 1u;
+  const uint2* base = r.data + (int64_t)(e & 1) * r.world * r.slot_elems + (int64_t)b * K;
   bool timed_out = false;
-  for (int i = t; i < nflags; i += kThreads) {
-    const int* f = r.flags + (i / r.ntiles) * r.max_tiles + (i % r.ntiles);
-    if (ld_acquire_sys(f) > e) continue;
-    const uint64_t t0 = sm100::global_ns();
-    for (uint32_t it = 1;; ++it) {
-      if (ld_acquire_sys(f) > e) break;
-      if ((it & 63) == 0 && sm100::global_ns() - t0 > (uint64_t)r.timeout_ns) {
-        timed_out = true;
-        break;
-      }
-    }
-  }
-  if (timed_out) set_error(r.err, kErrTimeout);
-  __syncthreads();
-  // ---- x += sum of partials; sum of squares ----
+  // ---- x += sum of partials (each element waits for its tag); sum of squares ----
   float v[kMaxPer];
   float ss = 0.f;
   float* xr = x + (size_t)b * K;
@@ -49,12 +49,13 @@ reduce_rmsnorm_quant_kernel(PeerReduce r, float* __restrict__ x, const float* __
     if (i < K) {
       float s = xr[i];
       for (int src = 0; src < r.world; ++src)
-        s += __ldcg(r.data + ((int64_t)par * r.world + src) * r.slot_elems + (int64_t)b * K + i);
+        s += wait_tagged(base + (int64_t)src * r.slot_elems + i, tag, r.timeout_ns, timed_out);
       xr[i] = s;
       v[j] = s;
       ss += s * s;
     }
   }
+  if (timed_out) set_error(r.err, kErrTimeout);
   float scale = 1.f;
   if (w) {
     ss = block_sum(ss, red);
@@ -91,15 +92,14 @@ reduce_rmsnorm_quant_kernel(PeerReduce r, float* __restrict__ x, const float* __
   }
 }
 
-// One CTA per 128-column tile, all B rows.
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 peer_push_kernel(PeerPush p, const float* __restrict__ src, int B, int N, int64_t ld) {
-  const int tile = blockIdx.x, t = threadIdx.x;
   const int e = *(volatile const int*)p.epoch;
-  const int col = tile * 128 + t;
-  if (col < N)
-    for (int b = 0; b < B; ++b) peer_store(p, e & 1, (int64_t)b * ld + col, __ldcg(src + (int64_t)b * ld + col));
-  peer_signal(p, tile, e);
+  const int64_t n = (int64_t)B * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / N, c = i % N;
+    peer_store(p, e, b * ld + c, __ldcg(src + b * ld + c));
+  }
 }
 
 }  // namespace
@@ -111,7 +111,9 @@ void launch_reduce_rmsnorm_quant(const PeerReduce& r, float* x, const float* w, 
 }
 
 void launch_peer_push(const PeerPush& p, const float* src, int B, int N, int64_t ld, cudaStream_t st) {
-  peer_push_kernel<<<(N + 127) / 128, 128, 0, st>>>(p, src, B, N, ld);
+  const int64_t n = (int64_t)B * N;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4 * 148);
+  peer_push_kernel<<<blocks, 256, 0, st>>>(p, src, B, N, ld);
 }
 
 }  // namespace air

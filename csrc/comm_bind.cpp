@@ -3,8 +3,8 @@
 // export/import between the ranks' processes, and the producer/consumer launches.
 //
 // Pointer tables travel as int64 CPU tensors ("meta"):
-//   push meta  : data[8], flags[8], epoch, slot_elems, world, rank, max_tiles
-//   reduce meta: data, flags, epoch, done, err, slot_elems, world, max_tiles, ntiles, timeout_ns
+//   push meta  : data[8], epoch, slot_elems, world, rank
+//   reduce meta: data, epoch, done, err, slot_elems, world, timeout_ns
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -48,25 +48,20 @@ int64_t ipc_open(const std::string& handle, int64_t device) {
 void ipc_close(int64_t ptr) { ck(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)), "cudaIpcCloseMemHandle"); }
 
 void reduce_rmsnorm_quant(const Tensor& meta, Tensor x, optional<Tensor> w, double w_offset, double eps, int64_t B,
-                          int64_t K, optional<Tensor> q, optional<Tensor> ds, optional<Tensor> y_bf16,
-                          int64_t ntiles) {
-  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 10, "reduce meta");
+                          int64_t K, optional<Tensor> q, optional<Tensor> ds, optional<Tensor> y_bf16) {
+  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 7, "reduce meta");
   TORCH_CHECK(K % 32 == 0 && K <= 16384, "reduce_rmsnorm_quant: K must be a multiple of 32, <= 16384");
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat, "x must be fp32 CUDA");
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat && x.is_contiguous(), "x must be contiguous fp32 CUDA");
   const int64_t* m = meta.data_ptr<int64_t>();
   air::PeerReduce r{};
-  r.data = reinterpret_cast<const float*>(m[0]);
-  r.flags = reinterpret_cast<const int*>(m[1]);
-  r.epoch = reinterpret_cast<int*>(m[2]);
-  r.done = reinterpret_cast<int*>(m[3]);
-  r.err = reinterpret_cast<int*>(m[4]);
-  r.slot_elems = m[5];
-  r.world = (int)m[6];
-  r.max_tiles = (int)m[7];
-  r.ntiles = ntiles > 0 ? (int)ntiles : (int)m[8];
-  r.timeout_ns = m[9];
+  r.data = reinterpret_cast<const uint2*>(m[0]);
+  r.epoch = reinterpret_cast<int*>(m[1]);
+  r.done = reinterpret_cast<int*>(m[2]);
+  r.err = reinterpret_cast<int*>(m[3]);
+  r.slot_elems = m[4];
+  r.world = (int)m[5];
+  r.timeout_ns = m[6];
   TORCH_CHECK(B * K <= r.slot_elems, "reduce_rmsnorm_quant: B*K exceeds the receive slot");
-  TORCH_CHECK(r.ntiles <= r.max_tiles, "reduce_rmsnorm_quant: too many tiles");
   auto p = [](const optional<Tensor>& t) { return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr; };
   air::launch_reduce_rmsnorm_quant(r, x.data_ptr<float>(), static_cast<const float*>(p(w)), (float)w_offset,
                                    (int)B, (int)K, (float)eps, static_cast<int8_t*>(p(q)), static_cast<float2*>(p(ds)),
@@ -77,18 +72,14 @@ void reduce_rmsnorm_quant(const Tensor& meta, Tensor x, optional<Tensor> w, doub
 }  // namespace
 
 air::PeerPush peer_push_from_meta(const Tensor& meta) {
-  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 21, "push meta");
+  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 12, "push meta");
   const int64_t* m = meta.data_ptr<int64_t>();
   air::PeerPush p{};
-  for (int i = 0; i < air::kMaxPeers; ++i) {
-    p.data[i] = reinterpret_cast<float*>(m[i]);
-    p.flags[i] = reinterpret_cast<int*>(m[8 + i]);
-  }
-  p.epoch = reinterpret_cast<const int*>(m[16]);
-  p.slot_elems = m[17];
-  p.world = (int)m[18];
-  p.rank = (int)m[19];
-  p.max_tiles = (int)m[20];
+  for (int i = 0; i < air::kMaxPeers; ++i) p.data[i] = reinterpret_cast<uint2*>(m[i]);
+  p.epoch = reinterpret_cast<const int*>(m[8]);
+  p.slot_elems = m[9];
+  p.world = (int)m[10];
+  p.rank = (int)m[11];
   TORCH_CHECK(p.world >= 1 && p.world <= air::kMaxPeers && p.rank >= 0 && p.rank < p.world, "push meta: world/rank");
   return p;
 }
@@ -98,14 +89,12 @@ void register_comm(pybind11::module_& m) {
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
-  m.def("peer_buffer_bytes", [](int64_t w, int64_t t, int64_t s) { return air::peer_buffer_bytes((int)w, (int)t, s); });
-  m.def("peer_flags_bytes", [](int64_t w, int64_t t) { return air::peer_flags_bytes((int)w, (int)t); });
+  m.def("peer_buffer_bytes", [](int64_t w, int64_t s) { return air::peer_buffer_bytes((int)w, s); });
   m.def("reduce_rmsnorm_quant", &reduce_rmsnorm_quant);
   m.def("peer_push", [](const Tensor& meta, const Tensor& src, int64_t B, int64_t N, int64_t ld) {
     TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kFloat, "peer_push: fp32 CUDA source");
     const air::PeerPush p = peer_push_from_meta(meta);
     TORCH_CHECK(B * ld <= p.slot_elems, "peer_push: B*ld exceeds the receive slot");
-    TORCH_CHECK((N + 127) / 128 <= p.max_tiles, "peer_push: too many tiles");
     air::launch_peer_push(p, src.data_ptr<float>(), (int)B, (int)N, ld, at::cuda::getCurrentCUDAStream());
     ck(cudaGetLastError(), "peer_push");
   });

@@ -13,8 +13,8 @@
 // arrival counter, reset by that CTA) reduces them and runs the fused epilogue:
 //   store / residual add / SwiGLU (gate and up tiles streamed together) /
 //   QKV + NeoX RoPE + paged KV write (a 128-row tile is one head: pairs (i, i+64)) /
-//   tensor-parallel peer push (the tile is stored into every rank's receive buffer over
-//   NVLink and flagged there; comm.h).
+//   tensor-parallel peer push (each element goes to every rank's receive buffer over
+//   NVLink as one tagged 8-byte store; comm.h).
 #include "common.cuh"
 #include "sm100.cuh"
 #include "kernels.h"
@@ -218,10 +218,9 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
 #pragma unroll
       for (int b = 0; b < MAXB; ++b) {
         if (b >= nB) break;
-        peer_store(ep.push, e & 1, (int64_t)b * ep.ld_out + row, acc[0][b]);
+        peer_store(ep.push, e, (int64_t)b * ep.ld_out + row, acc[0][b]);
       }
     }
-    peer_signal(ep.push, tile, e);
     return;
   }
   if (row >= N) return;

@@ -19,24 +19,23 @@ enum GemvEpilogue : int {
   kEpiSwiGLU = 2,     // out[b, n] = silu(W·x)[n] * (W2·x)[n]
   kEpiQKVRope = 3,    // rows = [q | k | v]; NeoX RoPE on q,k; k,v written to the paged cache
   kEpiPeerPush = 4,   // tensor-parallel partial: stored into every rank's receive slot over
-                      // NVLink, then one flag per 128-row tile (see comm.h)
+                      // NVLink as tagged 8-byte elements (see comm.h)
 };
 
 constexpr int kMaxPeers = 8;
 
 // Producer side of the fused tensor-parallel all-reduce. Every rank owns one receive
-// buffer, mapped into every peer process:
-//   flags [world][max_tiles] int32 (epoch values)  |  data [2][world][slot_elems] f32
-// A producer writes its [B, ld] partial into slot (parity, its rank) of every rank's
-// buffer, then stores flag[its rank][tile] = epoch + 1 (release, system scope) for each
-// 128-row output tile. `epoch` is the local collective counter, advanced by the consumer
-// (reduce_rmsnorm_quant) once all of its CTAs have read it.
+// buffer, mapped into every peer process: data [2 parities][world][slot_elems] of 8-byte
+// (value, tag) pairs. A producer writes each element of its [B, ld] partial into slot
+// (parity, its rank) of every rank's buffer as ONE 8-byte store carrying tag = epoch + 1,
+// so a reader that sees the tag also sees the value (no fence, no separate flag: the
+// "low-latency" protocol). `epoch` is the local collective counter, advanced by the
+// consumer (reduce_rmsnorm_quant) once all of its CTAs have read it.
 struct PeerPush {
-  float* data[kMaxPeers];     // per destination rank: its receive data base (mapped here)
-  int* flags[kMaxPeers];      // per destination rank: its flag base
+  uint2* data[kMaxPeers];     // per destination rank: its receive buffer (mapped here)
   const int* epoch;           // this rank's collective counter
   int64_t slot_elems;
-  int world, rank, max_tiles;
+  int world, rank;
 };
 
 struct GemvWeight {
