@@ -204,5 +204,12 @@ def draft_1b() -> ModelConfig:
                        context_length=8192, head_dim=64, eos_token_id=128001, bos_token_id=128000)
 
 
-PRESETS = {"tiny": tiny_llama, "llama3-8b": llama3_8b, "llama3-70b": llama3_70b,
+def tiny_moe() -> ModelConfig:
+    """Tiny Mixtral-style model (4 experts, top-2) for tests."""
+    return ModelConfig(n_layers=2, n_heads=4, n_kv_heads=2, hidden_dim=256, intermediate_dim=256,
+                       vocab_size=4096, rope_theta=10000.0, rms_norm_eps=1e-5, head_dim=64,
+                       variant=ModelVariant.MISTRAL, n_experts=4, moe_top_k=2)
+
+
+PRESETS = {"tiny": tiny_llama, "tiny-moe": tiny_moe, "llama3-8b": llama3_8b, "llama3-70b": llama3_70b,
            "mixtral-8x7b": mixtral_8x7b, "draft-1b": draft_1b}

@@ -88,9 +88,11 @@ class OracleLayer:
     wv: tuple
     wo: tuple
     ffn_norm: torch.Tensor
-    w_gate: tuple
-    w_up: tuple
-    w_down: tuple
+    w_gate: tuple | None
+    w_up: tuple | None
+    w_down: tuple | None
+    router: torch.Tensor | None = None          # [E, H] f32
+    experts: list | None = None                 # per expert (gate, up, down) raw tuples
 
 
 class OracleModel:
@@ -112,10 +114,23 @@ class OracleModel:
         self.layers = []
         for i in range(cfg.n_layers):
             p = f"blk.{i}."
-            self.layers.append(OracleLayer(
+            moe = cfg.n_experts > 0
+            L = OracleLayer(
                 vec(p + "attn_norm.weight"), lin(p + "attn_q.weight"), lin(p + "attn_k.weight"),
                 lin(p + "attn_v.weight"), lin(p + "attn_output.weight"), vec(p + "ffn_norm.weight"),
-                lin(p + "ffn_gate.weight"), lin(p + "ffn_up.weight"), lin(p + "ffn_down.weight")))
+                None if moe else lin(p + "ffn_gate.weight"), None if moe else lin(p + "ffn_up.weight"),
+                None if moe else lin(p + "ffn_down.weight"))
+            if moe:
+                E, F, H = cfg.n_experts, cfg.intermediate_dim, cfg.hidden_dim
+                rr, rq, _ = tensors[p + "ffn_gate_inp.weight"]
+                L.router = dequantize(rr, rq).reshape(E, H).float()
+                stk = {}
+                for nm in ("gate", "up", "down"):
+                    raw, qt, _ = tensors[p + f"ffn_{nm}_exps.weight"]
+                    stk[nm] = (raw.reshape(E, -1), qt)
+                L.experts = [tuple((stk[nm][0][e], stk[nm][1], H if nm == "down" else F)
+                                   for nm in ("gate", "up", "down")) for e in range(E)]
+            self.layers.append(L)
         self.out_norm = vec("output_norm.weight")
         self.lm_head = lin("output.weight" if "output.weight" in tensors else "token_embd.weight")
         hd = cfg.head_dim
@@ -189,16 +204,49 @@ class OracleModel:
             o = qmatmul(attn.reshape(S, nh * hd), L.wo[0], L.wo[1], L.wo[2]).to(x.dtype)
             x = x + o
             h = self.rms_norm(x, L.ffn_norm, cfg.rms_norm_eps).float()
-            g = qmatmul(h, L.w_gate[0], L.w_gate[1], L.w_gate[2])
-            u = qmatmul(h, L.w_up[0], L.w_up[1], L.w_up[2])
-            a = g / (1.0 + torch.exp(-g)) * u
-            dn = qmatmul(a, L.w_down[0], L.w_down[1], L.w_down[2]).to(x.dtype)
+            if L.router is not None:
+                dn = self.moe_ffn(h, L).to(x.dtype)
+            else:
+                g = qmatmul(h, L.w_gate[0], L.w_gate[1], L.w_gate[2])
+                u = qmatmul(h, L.w_up[0], L.w_up[1], L.w_up[2])
+                a = g / (1.0 + torch.exp(-g)) * u
+                dn = qmatmul(a, L.w_down[0], L.w_down[1], L.w_down[2]).to(x.dtype)
             x = x + dn
         x = self.rms_norm(x, self.out_norm, cfg.rms_norm_eps)
         if getattr(self, "_want_hidden", False):
             self._hidden = x.float()
         last = x[-1:].float()
         return qmatmul(last, self.lm_head[0], self.lm_head[1], self.lm_head[2])[0]
+
+
+def compute_routing(logits: torch.Tensor, k: int, normalize: bool = True):
+    """Softmax over experts, top-k (ties to the lower index), optional renormalisation of
+    the selected weights (reference src/moe.rs:163-199). logits [E] -> (ids, weights)."""
+    p = torch.softmax(logits.float(), -1)
+    order = sorted(range(p.numel()), key=lambda e: (-float(p[e]), e))[:k]
+    w = p[order]
+    if normalize and float(w.sum()) > 1e-9:
+        w = w / w.sum()
+    return order, w
+
+
+def _moe_ffn(self, h: torch.Tensor, L) -> torch.Tensor:
+    """Per token: route, run the top-k experts' SwiGLU FFNs, sum weighted (src/moe.rs:250-300)."""
+    cfg = self.cfg
+    logits = h @ L.router.t()
+    out = torch.zeros(h.shape[0], cfg.hidden_dim)
+    for t in range(h.shape[0]):
+        ids, w = compute_routing(logits[t], cfg.moe_top_k, True)
+        for e, we in zip(ids, w):
+            (gr, gq, gn), (ur, uq, un), (dr, dq, dn) = L.experts[e]
+            g = qmatmul(h[t:t + 1], gr, gq, gn)
+            u = qmatmul(h[t:t + 1], ur, uq, un)
+            a = g / (1.0 + torch.exp(-g)) * u
+            out[t] += float(we) * qmatmul(a, dr, dq, dn)[0]
+    return out
+
+
+OracleModel.moe_ffn = _moe_ffn
 
 
 def attention_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool,

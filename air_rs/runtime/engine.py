@@ -21,6 +21,7 @@ from collections import deque
 from dataclasses import dataclass, field
 from typing import Callable, Iterable
 
+import numpy as np
 import torch
 
 from ..models.config import ModelConfig
@@ -281,6 +282,8 @@ class Engine:
                     "tok": torch.zeros(B, dtype=torch.int32).pin_memory(),
                     "ev": None,
                 })
+                ring[-1]["i32_np"] = ring[-1]["i32"].numpy()        # numpy views of the pinned
+                ring[-1]["slots_np"] = ring[-1]["slots"].numpy()    # buffers (vectorised fills)
             p = {"ring": ring, "next": 0, "members": None}
             self._pinned[B] = p
         return p
@@ -303,17 +306,16 @@ class Engine:
         seqs = [r.seq for r in batch] + [-1] * (B - n)
         slots = self.seqs.step_slots(seqs)
         i32 = st["i32"]
+        a32 = st["i32_np"]
         h2d = 0
-        for i, r in enumerate(batch):
-            pos = r.num_tokens - 1
-            i32[i] = pos
-            i32[B + i] = pos + 1
-            i32[2 * B + i] = r.slot
-        for i in range(n, B):
-            i32[i] = 0
-            i32[B + i] = 0
-            i32[2 * B + i] = self.pad_slot
-        st["slots"][:] = torch.tensor(slots, dtype=torch.int64)
+        pos = np.fromiter((len(r.prompt_ids) + len(r.output_ids) - 1 for r in batch), dtype=np.int32, count=n)
+        a32[:n] = pos
+        a32[B:B + n] = pos + 1
+        a32[2 * B:2 * B + n] = np.fromiter((r.slot for r in batch), dtype=np.int32, count=n)
+        a32[n:B] = 0
+        a32[B + n:2 * B] = 0
+        a32[2 * B + n:3 * B] = self.pad_slot
+        st["slots_np"][:] = slots
         si.positions.copy_(i32[:B], non_blocking=True)
         si.ctx_len.copy_(i32[B:2 * B], non_blocking=True)
         si.count_row.copy_(i32[2 * B:3 * B], non_blocking=True)
@@ -325,18 +327,17 @@ class Engine:
             si.block_tables.copy_(st["tab"], non_blocking=True)
             h2d += st["tab"].numel() * 4
             sf, sii = st["samp_f"], st["samp_i"]
-            for i in range(B):
-                pr = batch[min(i, n - 1)].params
-                sf[i], sf[B + i], sf[2 * B + i] = pr.temperature, pr.repetition_penalty, pr.top_p
-                sii[i] = pr.top_k
+            prs = [batch[min(i, n - 1)].params for i in range(B)]
+            sf.numpy()[:] = [q.temperature for q in prs] + [q.repetition_penalty for q in prs] + [q.top_p for q in prs]
+            sii.numpy()[:] = [q.top_k for q in prs]
             si.temperature.copy_(sf[:B], non_blocking=True)
             si.penalty.copy_(sf[B:2 * B], non_blocking=True)
             si.top_p.copy_(sf[2 * B:], non_blocking=True)
             si.top_k.copy_(sii, non_blocking=True)
             h2d += 4 * B * 4
             # ids: last token of each sequence (from the host; after this the graph feeds itself)
-            for i in range(B):
-                i32[3 * B + i] = batch[i].output_ids[-1] if i < n else 0
+            a32[3 * B:3 * B + n] = [r.output_ids[-1] for r in batch]
+            a32[3 * B + n:] = 0
             si.ids.copy_(i32[3 * B:], non_blocking=True)
             h2d += B * 4
             p["members"] = key

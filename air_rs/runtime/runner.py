@@ -221,7 +221,8 @@ class ModelRunner:
                                 err=self.err, window=cfg.sliding_window or 0)
             if gemv_path:
                 self._row_parallel(lw.wo, xq, xds, B, x, peer)
-                self._norm(x, lw.ffn_norm, B, xq, xds, peer=peer)
+                # MoE layers also need the bf16 normalised row for the router
+                self._norm(x, lw.ffn_norm, B, xq, xds, y_bf16=self.xn_b[:B] if lw.wgu is None else None, peer=peer)
                 self._ffn_gemv(lw, B, x, xq, xds, tp, peer)
             else:
                 self.attn_b[:B].copy_(self.attn[:B])

@@ -216,19 +216,25 @@ def main():
     e2e = None
     if not args.no_e2e:
         prompts = [torch.randint(0, V, (P,), generator=gen).tolist() for _ in range(B)]
-        for pids in prompts:
-            eng.add_request(pids, SamplingParams(max_tokens=K + 1, temperature=0.0,
-                                                  repetition_penalty=1.1, ignore_eos=True))
-        eng.step()  # admission + prefill + first decode step
+        # max_tokens leaves room for the admission steps, so all B sequences decode in every
+        # timed step; the value counts the tokens actually emitted
+        rids = [eng.add_request(pids, SamplingParams(max_tokens=K + 64, temperature=0.0,
+                                                     repetition_penalty=1.1, ignore_eos=True))
+                for pids in prompts]
+        while eng.waiting:  # admission + prefill (not part of the decode metric)
+            eng.step()
         barrier()
+        reqs = [r for r in eng.running if r.rid in set(rids)]
+        n0 = sum(len(r.output_ids) for r in reqs)
         h0 = time.perf_counter()
         steps = eng.run_pipelined(max_steps=K)
         barrier()
         dt = time.perf_counter() - h0
+        emitted = sum(len(r.output_ids) for r in reqs) - n0
         tt = torch.tensor([dt], device=dev)
         if tp is not None:
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e = {"value": B * steps / float(tt[0]), "unit": "tokens/s",
+        e2e = {"value": emitted / float(tt[0]), "unit": "tokens/s", "steps": steps, "tokens": emitted,
                "h2d_bytes_per_step": eng.h2d_bytes_last_step,
                "d2h_bytes_per_step": eng.d2h_bytes_last_step,
                "api": "Engine.add_request + Engine.run_pipelined (pinned H2D inputs, D2H tokens per step)"}

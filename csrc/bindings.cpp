@@ -12,6 +12,7 @@
 #include "misc.h"
 #include "gemm_tc.h"
 #include "comm.h"
+#include "moe.h"
 
 void register_gemm_tc(pybind11::module_& m);
 void register_comm(pybind11::module_& m);
@@ -214,6 +215,27 @@ void residual_add(Tensor resid, Tensor y, int64_t n) {
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "air_rs sm_100a kernels";
+  m.def("moe_route", [](Tensor x, int64_t T, Tensor router, int64_t k, bool normalize, Tensor cw,
+                        optional<Tensor> ids, optional<Tensor> wts) {
+    TORCH_CHECK(x.is_cuda() && router.is_cuda() && cw.is_cuda(), "moe_route: CUDA tensors");
+    TORCH_CHECK(router.scalar_type() == torch::kFloat && router.dim() == 2, "moe_route: router fp32 [E, H]");
+    const int E = (int)router.size(0), H = (int)router.size(1);
+    TORCH_CHECK(E <= 256 && k >= 1 && k <= 8 && k <= E, "moe_route: E <= 256, 1 <= k <= 8");
+    TORCH_CHECK(x.size(-1) >= H && x.stride(-1) == 1, "moe_route: x rows");
+    TORCH_CHECK(cw.scalar_type() == torch::kFloat && cw.numel() >= T * E, "moe_route: cw [T, E] fp32");
+    air::launch_moe_route(x.data_ptr(), x.scalar_type() == torch::kBFloat16, x.stride(0), (int)T, H,
+                          router.data_ptr<float>(), E, (int)k, normalize, cw.data_ptr<float>(), ptr<int>(ids),
+                          ptr<float>(wts), stream());
+    post_launch("moe_route");
+  });
+  m.def("moe_combine", [](Tensor x, Tensor y, Tensor cw, int64_t e, int64_t E, int64_t T) {
+    TORCH_CHECK(x.is_cuda() && y.is_cuda() && x.scalar_type() == torch::kFloat && y.scalar_type() == torch::kFloat,
+                "moe_combine: fp32 CUDA");
+    TORCH_CHECK(x.is_contiguous() && y.stride(-1) == 1, "moe_combine: layouts");
+    air::launch_moe_combine(x.data_ptr<float>(), y.data_ptr<float>(), y.stride(0), cw.data_ptr<float>(), (int)e,
+                            (int)E, (int)T, (int)x.size(1), stream());
+    post_launch("moe_combine");
+  });
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("gemv", &gemv);
   m.def("gemv_tiled_splits", [](int64_t N, int64_t K, int64_t mode) { return air::gemv_tiled_splits((int)N, (int)K, (int)mode); });
