@@ -62,6 +62,7 @@ class Request:
     finish_time: float | None = None
     on_token: Callable | None = None
     grammar: object | None = None
+    cached_tokens: int = 0        # prompt tokens served from the prefix cache
 
     @property
     def num_tokens(self) -> int:
@@ -76,7 +77,8 @@ class Engine:
 
     def __init__(self, cfg: ModelConfig, runner=None, tokenizer=None, *, oracle=None,
                  max_batch: int = 64, prefill_chunk: int = 512, max_prefill_tokens: int = 8192,
-                 add_bos: bool = True, eos_id: int | None = None):
+                 add_bos: bool = True, eos_id: int | None = None, prefix_cache: bool = False,
+                 prefix_cache_blocks: int | None = None, kv_swap: bool = True):
         self.cfg = cfg
         self.runner = runner
         self.oracle = oracle
@@ -103,6 +105,12 @@ class Engine:
             self.pad_slot = runner.counts.shape[0] - 1
             self.free_slots = list(range(runner.counts.shape[0] - 1))[::-1]
             self._pinned: dict[int, dict] = {}
+            from ..kv.prefix_cache import RadixCache
+            from ..kv.swap import KvSwapManager
+            self.prefix_cache = (RadixCache(runner.block_size, prefix_cache_blocks or runner.num_blocks // 2,
+                                            self.seqs.allocator) if prefix_cache else None)
+            self.swap = KvSwapManager(runner.kv, self.seqs) if kv_swap else None
+        self.swapped: list[Request] = []      # preempted (KV in host memory), resumed first
 
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt_ids: list[int], params: SamplingParams | None = None, *,
@@ -119,9 +127,12 @@ class Engine:
         return r.rid
 
     def abort(self, rid: int) -> bool:
-        for q in (self.waiting, self.running):
+        for q in (self.waiting, self.running, self.swapped):
             for r in list(q):
                 if r.rid == rid:
+                    if r in self.swapped:
+                        self.swapped.remove(r)
+                        self.swap.drop(r.seq)
                     self._finish(r, FinishReason.ABORT)
                     if r in self.waiting:
                         self.waiting.remove(r)
@@ -129,7 +140,7 @@ class Engine:
         return False
 
     def has_unfinished(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self.swapped)
 
     # ------------------------------------------------------------------ bookkeeping
     def _finish(self, r: Request, reason: str):
@@ -184,19 +195,73 @@ class Engine:
         alloc = self.seqs.allocator
         bs = self.runner.block_size
         reserve = sum(1 for _ in self.running)  # one growth block per running sequence
+        committed = 0
+        self._resume_swapped()
+        if self.swapped:          # preempted requests go first
+            return admitted
         while self.waiting and len(self.running) + len(admitted) < self.max_batch:
             r = self.waiting[0]
-            need = (len(r.prompt_ids) + bs - 1) // bs + 1
-            if not alloc.can_allocate(need + reserve) or not self.free_slots:
+            hit, blocks = 0, []
+            if self.prefix_cache is not None:
+                # keep at least one prompt token to prefill (its logits give the first token)
+                hit, blocks = self.prefix_cache.longest_prefix_match(r.prompt_ids, len(r.prompt_ids) - 1)
+            need = (len(r.prompt_ids) - hit + bs - 1) // bs + 1
+            if not alloc.can_allocate(need + reserve + committed) and self.prefix_cache is not None:
+                self.prefix_cache.evict_until(need + reserve + committed - alloc.num_free_blocks())
+            if not alloc.can_allocate(need + reserve + committed) or not self.free_slots:
                 break
-            if len(r.prompt_ids) > budget and admitted:
+            if len(r.prompt_ids) - hit > budget and admitted:
                 break
             self.waiting.popleft()
-            r.seq = self.seqs.create_sequence()
+            if hit:
+                r.seq = self.seqs.create_with_prefix(blocks, hit)
+                r.prefilled = hit
+                r.cached_tokens = hit
+            else:
+                r.seq = self.seqs.create_sequence()
             r.slot = self.free_slots.pop()
             admitted.append(r)
-            budget -= len(r.prompt_ids)
+            committed += need       # allocated by _prefill, after this loop
+            budget -= len(r.prompt_ids) - hit
         return admitted
+
+    # ------------------------------------------------------------------ preemption (KV host tier)
+    def _blocks_needed(self, batch) -> int:
+        """New KV blocks the next decode step opens (a sequence whose KV fills whole blocks)."""
+        bs = self.runner.block_size
+        return sum(1 for r in batch if self.seqs.num_tokens(r.seq) % bs == 0)
+
+    def _make_room(self, batch: list) -> list:
+        """Preempt the most recently admitted sequences (KV -> pinned host memory) until the
+        next step's new blocks fit; returns the batch that can run."""
+        alloc = self.seqs.allocator
+        need = self._blocks_needed(batch)
+        if need > alloc.num_free_blocks() and self.prefix_cache is not None:
+            self.prefix_cache.evict_until(need - alloc.num_free_blocks())
+        while batch and self._blocks_needed(batch) > alloc.num_free_blocks():
+            if self.swap is None or len(batch) == 1:
+                raise RuntimeError("out of KV blocks and no sequence left to preempt")
+            victim = batch[-1]
+            self.swap.evict(victim.seq)
+            self.running.remove(victim)
+            self.swapped.append(victim)
+            batch = batch[:-1]
+            self.metrics.preemptions = getattr(self.metrics, "preemptions", 0) + 1
+        return batch
+
+    def _resume_swapped(self):
+        """Bring preempted sequences back (oldest first) while their blocks + one fit."""
+        alloc = self.seqs.allocator
+        bs = self.runner.block_size
+        while self.swapped and len(self.running) < self.max_batch:
+            r = self.swapped[0]
+            n = (self.seqs.num_tokens(r.seq) + bs - 1) // bs
+            reserve = len(self.running) + 2
+            if not alloc.can_allocate(n + reserve):
+                break
+            self.swapped.pop(0)
+            self.swap.restore(r.seq)
+            self.running.append(r)
 
     def _prefill(self, reqs: list[Request]):
         """Chunked prefill of admitted requests; samples their first tokens."""
@@ -249,6 +314,9 @@ class Engine:
             toks_h = toks.tolist()
             for r, d, t in zip(pr, done, toks_h):
                 if d is not None:
+                    if self.prefix_cache is not None:
+                        # whole prompt blocks are complete and never written again
+                        self.prefix_cache.insert(r.prompt_ids, self.seqs.block_table(r.seq))
                     self.running.append(r)
                     self._emit(r, t)
             pending = [r for r in pending if r.prefilled < len(r.prompt_ids)]
@@ -393,6 +461,7 @@ class Engine:
         batch = [r for r in self.running if r.output_ids and not r.finished]
         if not batch:
             return produced
+        batch = self._make_room(batch)
         B, p, ev = self._launch_decode(batch)
         ev.synchronize()
         toks = p["tok"][:len(batch)].tolist()
@@ -418,15 +487,21 @@ class Engine:
                     admitted = self._admit()
                     if admitted:
                         self._prefill(admitted)
+                if self.swapped:
+                    self._resume_swapped()
                 batch = [r for r in self.running if not r.finished]
                 if not batch:
-                    if not self.waiting:
+                    if not self.waiting and not self.swapped:
                         break
+                    if self.swapped and not self.waiting:
+                        self._resume_swapped()
                     continue
+                batch = self._make_room(batch)
                 inflight = (batch, *self._launch_decode(batch))
                 continue
             ib, B, p, ev = inflight
-            chain = (not self.waiting and (max_steps is None or steps + 1 < max_steps) and
+            chain = (not self.waiting and not self.swapped and (max_steps is None or steps + 1 < max_steps) and
+                     self._blocks_needed_after(ib) <= self.seqs.allocator.num_free_blocks() and
                      all(r.grammar is None for r in ib) and
                      all(len(r.output_ids) + 2 <= r.params.max_tokens for r in ib))
             nxt = None
@@ -456,6 +531,11 @@ class Engine:
             inflight = nxt
         self._release_deferred()
         return steps
+
+    def _blocks_needed_after(self, batch) -> int:
+        """New blocks the step after the in-flight one opens (one more token per sequence)."""
+        bs = self.runner.block_size
+        return sum(1 for r in batch if self.seqs.num_tokens(r.seq) % bs == 0)
 
     def _emit_deferred(self, r: Request, tok: int):
         """_emit, but KV blocks of a finishing request are freed later (a step may be in flight)."""

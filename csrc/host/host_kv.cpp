@@ -94,6 +94,21 @@ class SequenceManager {
     tables_[id] = Table{};
     return id;
   }
+  // New sequence that starts with `blocks` (full blocks shared from a prefix cache; each
+  // gains a reference) holding n_tokens tokens; later appends open fresh blocks.
+  int64_t create_with_prefix(const std::vector<int64_t>& blocks, int64_t n_tokens) {
+    const int64_t bs = alloc_.block_size();
+    if (n_tokens != (int64_t)blocks.size() * bs)
+      throw std::invalid_argument("create_with_prefix: prefix must be whole blocks");
+    for (int64_t b : blocks) alloc_.check(b);
+    int64_t id = next_++;
+    Table tb;
+    tb.blocks = blocks;
+    tb.num_tokens = n_tokens;
+    for (int64_t b : blocks) alloc_.share(b);
+    tables_[id] = tb;
+    return id;
+  }
   Table& t(int64_t s) {
     auto it = tables_.find(s);
     if (it == tables_.end()) throw std::out_of_range("sequence not found");
@@ -263,6 +278,7 @@ void register_host_kv(py::module_& m) {
       .def(py::init<int64_t, int64_t>(), py::arg("capacity"), py::arg("block_size") = 16)
       .def_property_readonly("allocator", &SequenceManager::allocator, py::return_value_policy::reference_internal)
       .def("create_sequence", &SequenceManager::create)
+      .def("create_with_prefix", &SequenceManager::create_with_prefix)
       .def("has", &SequenceManager::has)
       .def("append", &SequenceManager::append)
       .def("append_token", &SequenceManager::append_token)
