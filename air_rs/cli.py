@@ -20,7 +20,9 @@ from . import __version__
 def _common(p: argparse.ArgumentParser, serve: bool = False):
     p.add_argument("-m", "--model", required=True, help="Path to GGUF model file (or registry alias)")
     p.add_argument("--ctx-size", type=int, default=None, help="Override context length for the KV budget")
-    p.add_argument("--resident", action="store_true", help="Keep all weights in HBM (always true on B200)")
+    p.add_argument("--resident", action="store_true", help="Keep all weights in HBM (the default on B200)")
+    p.add_argument("--stream-weights", action="store_true",
+                   help="S.L.I.P.: keep layer weights in pinned host memory and stream them per forward")
     p.add_argument("--tp", type=int, default=1, help="Tensor-parallel GPUs (default: 1)")
     p.add_argument("--gds", action="store_true", help="Use GPUDirect Storage for weight streaming")
     p.add_argument("--enable-auto-tool-choice", action="store_true")
@@ -102,7 +104,8 @@ def _engine(args, max_batch=64):
     if args.tp > 1:
         tp = init_from_env("nccl")
     path = resolve(args.model)
-    return engine_from_gguf(path, device=args.device, max_batch=max_batch, max_model_len=args.ctx_size, tp=tp)
+    return engine_from_gguf(path, device=args.device, max_batch=max_batch, max_model_len=args.ctx_size, tp=tp,
+                            resident=not getattr(args, "stream_weights", False))
 
 
 def cmd_generate(args) -> int:

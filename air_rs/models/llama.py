@@ -49,12 +49,43 @@ class LayerWeights:
         return self.wgu.part(1)
 
 
+def layer_tensors(lw: "LayerWeights") -> list:
+    """Every tensor of a layer in a fixed order (weights data/scales, norms, router)."""
+    out = [lw.attn_norm, lw.ffn_norm]
+    qws = [lw.wqkv, lw.wo] + ([lw.wgu, lw.wdown] if lw.wgu is not None else []) + list(lw.experts_gu) + \
+        list(lw.experts_down)
+    for q in qws:
+        out.append(q.data)
+        if q.scales is not None:
+            out.append(q.scales)
+    if lw.router is not None:
+        out.append(lw.router)
+    return out
+
+
+def pin_layer(lw: "LayerWeights"):
+    """Move a host-resident layer's tensors into page-locked memory (in place)."""
+    import dataclasses
+    for f in dataclasses.fields(lw):
+        v = getattr(lw, f.name)
+        if isinstance(v, torch.Tensor):
+            setattr(lw, f.name, v.pin_memory())
+        elif isinstance(v, ops.QWeight):
+            setattr(lw, f.name, v.to_device(None, pin=True))
+        elif isinstance(v, list) and v and isinstance(v[0], ops.QWeight):
+            setattr(lw, f.name, [q.to_device(None, pin=True) for q in v])
+
+
 class LlamaWeights:
     """Device-resident weights, built from (name, raw, qtype, shape) records."""
 
-    def __init__(self, cfg: ModelConfig, records: Iterable, device, tp_rank: int = 0, tp_size: int = 1):
+    def __init__(self, cfg: ModelConfig, records: Iterable, device, tp_rank: int = 0, tp_size: int = 1,
+                 layer_device=None):
+        """``layer_device`` (default: ``device``) holds the per-layer weights; ``"cpu"`` keeps
+        them in pinned host memory for layer streaming (S.L.I.P.)."""
         self.cfg = cfg
         self.device = torch.device(device)
+        self.layer_device = torch.device(layer_device) if layer_device is not None else self.device
         self.tp_rank, self.tp_size = tp_rank, tp_size
         pending: dict[str, tuple] = {}
         self.layers: list[LayerWeights | None] = [None] * cfg.n_layers
@@ -111,7 +142,13 @@ class LlamaWeights:
             if not all(pre + n in p for n in need):
                 continue
             g = {n: p.pop(pre + n) for n in need}
-            self.layers[i] = self._build_layer(g)
+            dev, self.device = self.device, self.layer_device
+            try:
+                self.layers[i] = self._build_layer(g)
+            finally:
+                self.device = dev
+            if self.layer_device.type == "cpu" and dev.type == "cuda":
+                pin_layer(self.layers[i])
 
     def _shard_rows_tp(self, raw, qt, shape):
         if self.tp_size == 1:
@@ -169,6 +206,12 @@ class LlamaWeights:
             else:
                 lw.wdown = self._lin_cols(*g["ffn_down.weight"], rk * Fl, (rk + 1) * Fl)
         return lw
+
+    def resident_nbytes(self) -> int:
+        """Bytes on the compute device (layers streamed from host memory excluded)."""
+        if self.layer_device == self.device:
+            return self.nbytes()
+        return self.embd.nbytes + self.lm_head.nbytes
 
     def nbytes(self) -> int:
         n = self.embd.nbytes + self.lm_head.nbytes

@@ -126,6 +126,14 @@ class QWeight:
         return QWeight(self.fmt, self.data[r0:r1], None if self.scales is None else self.scales[r0:r1],
                        r1 - r0, self.K, self.qtype)
 
+    def to_device(self, device, pin: bool = False) -> "QWeight":
+        """Same weight on another device (``device=None, pin=True``: pinned host copy)."""
+        def mv(t):
+            if t is None:
+                return None
+            return t.pin_memory() if pin else t.to(device)
+        return QWeight(self.fmt, mv(self.data), mv(self.scales), self.N, self.K, self.qtype, self.parts)
+
     def part(self, i: int) -> "QWeight":
         off, n = self.parts[i]
         return self.rows(off, off + n)

@@ -45,15 +45,23 @@ def plan_kv_blocks(cfg: ModelConfig, weights_bytes: int, *, block_size: int, dev
 
 
 def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_model_len=4096,
-                 block_size=16, num_blocks=None, tp=None, seed=0, max_seqs=None) -> ModelRunner:
+                 block_size=16, num_blocks=None, tp=None, seed=0, max_seqs=None,
+                 resident: bool = True, stream_slots: int = 2) -> ModelRunner:
+    """``resident=False``: per-layer weights stay in pinned host memory and are streamed
+    through ``stream_slots`` device slots each forward (S.L.I.P. streaming mode)."""
     tp_size = tp.world_size if tp is not None else 1
     tp_rank = tp.rank if tp is not None else 0
-    w = LlamaWeights(cfg, records, device, tp_rank=tp_rank, tp_size=tp_size)
-    nb = plan_kv_blocks(cfg, w.nbytes(), block_size=block_size, device=device, max_batch=max_batch,
-                        max_model_len=max_model_len, tp_size=tp_size, num_blocks=num_blocks)
-    return ModelRunner(cfg, w, num_blocks=nb, block_size=block_size, max_batch=max_batch,
-                       max_model_len=max_model_len, device=device, tp=tp, seed=seed,
-                       max_seqs=max_seqs or max(2 * max_batch + 1, 64))
+    w = LlamaWeights(cfg, records, device, tp_rank=tp_rank, tp_size=tp_size,
+                     layer_device=None if resident else "cpu")
+    streamed = 0 if resident else stream_slots * max(1, w.nbytes() - w.resident_nbytes()) // cfg.n_layers
+    nb = plan_kv_blocks(cfg, w.resident_nbytes() + streamed, block_size=block_size, device=device,
+                        max_batch=max_batch, max_model_len=max_model_len, tp_size=tp_size, num_blocks=num_blocks)
+    rn = ModelRunner(cfg, w, num_blocks=nb, block_size=block_size, max_batch=max_batch,
+                     max_model_len=max_model_len, device=device, tp=tp, seed=seed,
+                     max_seqs=max_seqs or max(2 * max_batch + 1, 64))
+    if not resident:
+        rn.enable_streaming(stream_slots)
+    return rn
 
 
 def random_engine(preset: str | ModelConfig = "tiny", qtype: GGMLType = GGMLType.Q4_K, *, seed=0,
@@ -69,7 +77,7 @@ def random_engine(preset: str | ModelConfig = "tiny", qtype: GGMLType = GGMLType
 
 
 def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None, tp=None,
-                     num_blocks=None, seed=0, **kw) -> Engine:
+                     num_blocks=None, seed=0, resident: bool = True, **kw) -> Engine:
     g = read_gguf(path)
     cfg = ModelConfig.from_gguf_metadata(g.metadata)
     tok = Tokenizer.from_gguf_metadata(g.metadata)
@@ -81,5 +89,5 @@ def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None
     mml = max_model_len or min(cfg.context_length, 8192)
     recs = ((n, g.raw(n), t.qtype, t.torch_shape) for n, t in g.tensors.items())
     runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=mml, tp=tp,
-                          num_blocks=num_blocks, seed=seed)
+                          num_blocks=num_blocks, seed=seed, resident=resident)
     return Engine(cfg, runner, tok, max_batch=max_batch, **kw)

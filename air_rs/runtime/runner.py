@@ -107,8 +107,26 @@ class ModelRunner:
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_launches: dict[int, int] = {}
         self._prefill_ws: dict[str, torch.Tensor] = {}
+        self.streamer = None
         self.max_prefill_tokens = max_prefill_tokens
         self._wscratch = None
+
+    # ------------------------------------------------------------------ layer weights
+    def _layer(self, li: int):
+        """Layer li's weights on the device (resident, or streamed into a slot)."""
+        if self.streamer is not None:
+            return self.streamer.get(li)
+        return self.w.layers[li]
+
+    def _layer_done(self, li: int):
+        if self.streamer is not None:
+            self.streamer.release(li)
+
+    def enable_streaming(self, n_slots: int = 2):
+        """Stream host-resident layers through ``n_slots`` device slots (S.L.I.P.)."""
+        from ..stream.slip import LayerStreamer
+        self.streamer = LayerStreamer(self.w.layers, self.device, n_slots)
+        return self.streamer
 
     # ------------------------------------------------------------------ inputs
     def step_inputs(self, B: int) -> StepInputs:
@@ -199,7 +217,8 @@ class ModelRunner:
         ns = self.n_splits(B)
         tp = self.tp_size > 1
         peer = self._peer(B)
-        for li, lw in enumerate(w.layers):
+        for li in range(len(w.layers)):
+            lw = self._layer(li)
             kv = self.kv[li]
             if gemv_path:
                 self._norm(x, lw.attn_norm, B, xq, xds, peer=peer)
@@ -229,6 +248,7 @@ class ModelRunner:
                 self._proj_into_residual(self.attn_b[:B], lw.wo, x, self.o_b, tp, peer)
                 self._norm(x, lw.ffn_norm, B, y_bf16=self.xn_b[:B], peer=peer)
                 self._ffn_gemm(lw, B, x, tp, peer)
+            self._layer_done(li)
         self._head(B, x, xq, xds, gemv_path, peer)
 
     def _residual(self, y_b: torch.Tensor, B: int, x: torch.Tensor, tp: bool):
@@ -276,7 +296,7 @@ class ModelRunner:
     def decode(self, B: int, use_graph: bool = True):
         """Runs one decode step for the first B rows of the bucket-B inputs."""
         self.step_inputs(B)
-        if not use_graph:
+        if not use_graph or self.streamer is not None:
             self._decode_body(B)
             return self.inputs[B]
         g = self.graphs.get(B)
@@ -346,7 +366,8 @@ class ModelRunner:
         ctx = ctx_len if ctx_len is not None else (positions + 1).to(torch.int32)
         tp = self.tp_size > 1
         ops.embed(w.embd, ids, out_f32=x, err=self.err, n=T)
-        for li, lw in enumerate(w.layers):
+        for li in range(len(w.layers)):
+            lw = self._layer(li)
             kv = self.kv[li]
             ops.rmsnorm_quant(x, lw.attn_norm, eps, None, None, y_bf16=xn)
             self.linear(xn, lw.wqkv, qkv)
@@ -366,6 +387,7 @@ class ModelRunner:
                 self.linear(xn, lw.wgu, gu)
                 ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp, up_off=self.up_off)
                 self._proj_into_residual(hb, lw.wdown, x, o, tp)
+            self._layer_done(li)
         if return_hidden:  # final-norm hidden states of every row (embeddings)
             hn = self._ws("hn", (T, self.H), bf16)
             ops.rmsnorm_quant(x, w.out_norm, eps, None, None, y_bf16=hn)
