@@ -623,6 +623,43 @@ class Engine:
         finally:
             self.seqs.free_sequence(seq)
 
+    def token_logprobs(self, ids: list[int], add_bos: bool | None = None) -> list[float]:
+        """Per-token log-probabilities of ``ids`` under the model, each given everything before
+        it (BOS included when added): one forward over all rows on the GPU, teacher forcing
+        on the CPU oracle. Used by the eval harness."""
+        bos = self.add_bos if add_bos is None else add_bos
+        ids = ([self.cfg.bos_token_id] if bos else []) + list(ids)
+        T = len(ids)
+        if T < 2:
+            return []
+        if self.runner is None:
+            self.oracle.reset()
+            out = []
+            logits = self.oracle.forward(ids[:1], 0)
+            for i in range(1, T):
+                out.append(float(torch.log_softmax(logits.float(), -1)[ids[i]]))
+                logits = self.oracle.forward([ids[i]], i)
+            self.oracle.reset()
+            return out
+        rn = self.runner
+        dev = rn.device
+        seq = self.seqs.create_sequence()
+        try:
+            slots = self.seqs.append(seq, T)
+            tab = torch.full((1, rn.max_blocks), -1, dtype=torch.int32)
+            self.seqs.fill_table([seq], tab)
+            lg = rn.prefill(torch.tensor(ids, dtype=torch.int32, device=dev),
+                            torch.arange(T, dtype=torch.int32, device=dev),
+                            torch.tensor(slots, dtype=torch.int64, device=dev),
+                            torch.zeros(T, dtype=torch.int32, device=dev), tab.to(dev),
+                            torch.arange(T - 1, dtype=torch.int64, device=dev), None, None, None, None,
+                            None, return_logits=True)
+            lp = torch.log_softmax(lg.float(), -1)
+            tgt = torch.tensor(ids[1:], dtype=torch.long, device=dev)
+            return lp.gather(1, tgt[:, None]).squeeze(1).tolist()
+        finally:
+            self.seqs.free_sequence(seq)
+
     # ------------------------------------------------------------------ high level
     def generate_ids(self, prompts: list[list[int]], params: SamplingParams | None = None,
                      pipelined: bool = False) -> list[list[int]]:
