@@ -71,6 +71,13 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--tls-key", default=None)
     s.add_argument("--api-key", action="append", default=None)
     s.add_argument("--model-name", default=None)
+    s.add_argument("--content-safety", action="store_true", help="Screen prompts/outputs with the safety gate")
+    s.add_argument("--modelfile", default=None, help="Modelfile with SYSTEM / PARAMETER defaults")
+    s.add_argument("--enable-prefix-caching", action="store_true", help="Radix prefix cache over KV blocks")
+
+    mc = sub.add_parser("mcp", help="Model Context Protocol server on stdio")
+    _common(mc)
+    mc.add_argument("--model-name", default=None)
 
     b = sub.add_parser("bench", help="Throughput benchmark")
     _common(b)
@@ -161,11 +168,33 @@ def cmd_serve(args) -> int:
     from .serve.dispatcher import EngineDispatcher
     core = _engine(args, max_batch=args.max_num_seqs)
     name = args.model_name or os.path.splitext(os.path.basename(args.model))[0]
+    if args.enable_prefix_caching and core.runner is not None:
+        from .kv.prefix_cache import RadixCache
+        core.prefix_cache = RadixCache(core.runner.block_size, core.runner.num_blocks // 2, core.seqs.allocator)
     d = EngineDispatcher(core, name)
+    safety = None
+    if args.content_safety:
+        from .safety import ContentSafetyGate
+        safety = ContentSafetyGate()
+    mf = None
+    if args.modelfile:
+        from .modelfile import Modelfile
+        mf = Modelfile.load(args.modelfile)
     app = create_app(d, name, api_keys=args.api_key, chat_format=args.chat_template,
-                     reasoning_format=args.reasoning_format, tool_call_parser=args.tool_call_parser)
+                     reasoning_format=args.reasoning_format, tool_call_parser=args.tool_call_parser,
+                     safety=safety, modelfile=mf)
     uvicorn.run(app, host=args.host, port=args.port, ssl_certfile=args.tls_cert, ssl_keyfile=args.tls_key,
                 log_level="info")
+    return 0
+
+
+def cmd_mcp(args) -> int:
+    from .serve.mcp import McpServer
+    core = _engine(args, max_batch=8)
+    srv = McpServer()
+    name = args.model_name or os.path.splitext(os.path.basename(args.model))[0]
+    srv.register_builtin_tools(core.tokenizer, core, name)
+    srv.serve_stdio()
     return 0
 
 
@@ -245,7 +274,8 @@ def main(argv: list[str] | None = None) -> int:
         from .hub import pull
         print(pull(args.repo_id, args.filename, args.alias, args.sha256))
         return 0
-    return {"generate": cmd_generate, "serve": cmd_serve, "bench": cmd_bench, "info": cmd_info}[args.cmd](args)
+    return {"generate": cmd_generate, "serve": cmd_serve, "bench": cmd_bench, "info": cmd_info,
+            "mcp": cmd_mcp}[args.cmd](args)
 
 
 if __name__ == "__main__":

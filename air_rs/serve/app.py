@@ -28,7 +28,10 @@ DEFAULT_TEMPERATURE = 0.7      # reference default_temperature()
 
 def create_app(dispatcher: Dispatcher, model_name: str = "air-rs", *, api_keys: list[str] | None = None,
                rate_limit: tuple[float, int] | None = None, chat_format: str | None = None,
-               reasoning_format: str | None = None, tool_call_parser: str | None = None) -> FastAPI:
+               reasoning_format: str | None = None, tool_call_parser: str | None = None,
+               safety=None, modelfile=None) -> FastAPI:
+    """``safety``: an ``air_rs.safety.ContentSafetyGate`` screening prompts (and completed
+    outputs); ``modelfile``: an ``air_rs.modelfile.Modelfile`` supplying defaults."""
     app = FastAPI(title="air-rs", version=__version__)
     keys = ApiKeyStore(api_keys)
     limiter = RateLimiter(*rate_limit) if rate_limit else None
@@ -58,7 +61,27 @@ def create_app(dispatcher: Dispatcher, model_name: str = "air-rs", *, api_keys: 
         validate_sampling(body)
         return body
 
+    def screen(text: str):
+        if safety is not None and safety.policy.screen_input and safety.should_block(text):
+            raise ApiError(safety.block_reason(safety.check(text)), ApiErrorCode.INVALID_REQUEST,
+                           "content_policy_violation")
+
+    def screen_output(text: str) -> str:
+        if safety is not None and safety.policy.screen_output and safety.should_block(text):
+            raise ApiError(safety.block_reason(safety.check(text)), ApiErrorCode.INVALID_REQUEST,
+                           "content_policy_violation")
+        return text
+
     def config_from(body: dict, prompt: str, max_key: str = "max_tokens") -> GenerateConfig:
+        screen(prompt)
+        if modelfile is not None:
+            mf_cfg = modelfile.apply_to(GenerateConfig(model=model_name, prompt=prompt))
+            prompt = mf_cfg.prompt
+            for k in ("temperature", "top_p", "max_tokens"):
+                if body.get(k) is None and getattr(modelfile, k) is not None:
+                    body = {**body, k: getattr(mf_cfg, k)}
+            if modelfile.stop and not body.get("stop"):
+                body = {**body, "stop": list(modelfile.stop)}
         rf = body.get("response_format") or {}
         return GenerateConfig(
             model=body.get("model") or model_name, prompt=prompt,
@@ -151,6 +174,7 @@ def create_app(dispatcher: Dispatcher, model_name: str = "air-rs", *, api_keys: 
                 return chat_chunk(cid, model, delta)
             return stream(cfg, mk, lambda r: chat_chunk(cid, model, {}, r))
         text, n, reason = await run(cfg)
+        text = screen_output(text)
         msg = {"role": "assistant", "content": text}
         if reasoning_format and reasoning_format != "none":
             tr = strip_think_tags(text)
@@ -182,7 +206,7 @@ def create_app(dispatcher: Dispatcher, model_name: str = "air-rs", *, api_keys: 
         if body.get("stream"):
             return stream(cfg, chunk, lambda r: chunk("", r))
         text, n, reason = await run(cfg)
-        out = chunk(text, reason)
+        out = chunk(screen_output(text), reason)
         out["usage"] = usage(dispatcher.count_tokens(prompt), n)
         return out
 
