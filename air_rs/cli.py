@@ -73,7 +73,6 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--model-name", default=None)
     s.add_argument("--content-safety", action="store_true", help="Screen prompts/outputs with the safety gate")
     s.add_argument("--modelfile", default=None, help="Modelfile with SYSTEM / PARAMETER defaults")
-    s.add_argument("--enable-prefix-caching", action="store_true", help="Radix prefix cache over KV blocks")
 
     mc = sub.add_parser("mcp", help="Model Context Protocol server on stdio")
     _common(mc)
@@ -112,7 +111,8 @@ def _engine(args, max_batch=64):
         tp = init_from_env("nccl")
     path = resolve(args.model)
     return engine_from_gguf(path, device=args.device, max_batch=max_batch, max_model_len=args.ctx_size, tp=tp,
-                            resident=not getattr(args, "stream_weights", False))
+                            resident=not getattr(args, "stream_weights", False),
+                            **({"prefix_cache": True} if getattr(args, "enable_prefix_caching", False) else {}))
 
 
 def cmd_generate(args) -> int:
@@ -168,9 +168,6 @@ def cmd_serve(args) -> int:
     from .serve.dispatcher import EngineDispatcher
     core = _engine(args, max_batch=args.max_num_seqs)
     name = args.model_name or os.path.splitext(os.path.basename(args.model))[0]
-    if args.enable_prefix_caching and core.runner is not None:
-        from .kv.prefix_cache import RadixCache
-        core.prefix_cache = RadixCache(core.runner.block_size, core.runner.num_blocks // 2, core.seqs.allocator)
     d = EngineDispatcher(core, name)
     safety = None
     if args.content_safety:

@@ -111,6 +111,8 @@ class Engine:
                                             self.seqs.allocator) if prefix_cache else None)
             self.swap = KvSwapManager(runner.kv, self.seqs) if kv_swap else None
         self.swapped: list[Request] = []      # preempted (KV in host memory), resumed first
+        if runner is None:
+            self.prefix_cache = self.swap = None
 
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt_ids: list[int], params: SamplingParams | None = None, *,
