@@ -286,6 +286,41 @@ def dequantize_q8_k(raw: torch.Tensor) -> torch.Tensor:
     return _flat(q * d)
 
 
+# ---------------------------------------------------------------------------
+# IQ4 non-linear 4-bit formats: a fixed 16-entry int8 codebook (part of the GGUF format
+# definition) scaled per 32-element block (IQ4_NL) or per 32 within a 256 super-block with
+# 6-bit scales (IQ4_XS)
+# ---------------------------------------------------------------------------
+
+IQ4_NL_VALUES = torch.tensor([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113],
+                             dtype=torch.float32)
+
+
+def _iq4_nibbles(qs: torch.Tensor) -> torch.Tensor:
+    """16 bytes -> 32 codebook values: low nibbles first, then high nibbles."""
+    lo, hi = (qs & 0xF).long(), (qs >> 4).long()
+    return IQ4_NL_VALUES[torch.cat([lo, hi], -1)]
+
+
+def dequantize_iq4_nl(raw: torch.Tensor) -> torch.Tensor:
+    b = _blocks(raw, 18)
+    d = _f16(b[..., 0:2])
+    return _flat(_iq4_nibbles(b[..., 2:18]) * d.unsqueeze(-1))
+
+
+def dequantize_iq4_xs(raw: torch.Tensor) -> torch.Tensor:
+    b = _blocks(raw, 136)
+    d = _f16(b[..., 0:2])
+    sh = b[..., 2].to(torch.int64) | (b[..., 3].to(torch.int64) << 8)
+    sl = b[..., 4:8].to(torch.int64)
+    ib = torch.arange(8)
+    ls = ((sl[..., ib // 2] >> (4 * (ib % 2))) & 0xF) | (((sh[..., None] >> (2 * ib)) & 3) << 4)
+    dl = d.unsqueeze(-1) * (ls.float() - 32.0)                                  # [..., 8]
+    qs = b[..., 8:136].reshape(*b.shape[:-1], 8, 16)
+    v = _iq4_nibbles(qs) * dl.unsqueeze(-1)                                    # [..., 8, 32]
+    return _flat(v.reshape(*b.shape[:-1], 256))
+
+
 def _dense(dtype):
     def f(raw: torch.Tensor) -> torch.Tensor:
         n = torch.tensor([], dtype=dtype).element_size()
@@ -308,6 +343,8 @@ DEQUANT = {
     GGMLType.Q5_K: dequantize_q5_k,
     GGMLType.Q6_K: dequantize_q6_k,
     GGMLType.Q8_K: dequantize_q8_k,
+    GGMLType.IQ4_NL: dequantize_iq4_nl,
+    GGMLType.IQ4_XS: dequantize_iq4_xs,
 }
 
 QUANT = {
