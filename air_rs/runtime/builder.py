@@ -46,7 +46,7 @@ def plan_kv_blocks(cfg: ModelConfig, weights_bytes: int, *, block_size: int, dev
 
 def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_model_len=4096,
                  block_size=16, num_blocks=None, tp=None, seed=0, max_seqs=None,
-                 resident: bool = True, stream_slots: int = 2) -> ModelRunner:
+                 resident: bool = True, stream_slots: int = 2, kv_alloc=None) -> ModelRunner:
     """``resident=False``: per-layer weights stay in pinned host memory and are streamed
     through ``stream_slots`` device slots each forward (S.L.I.P. streaming mode)."""
     tp_size = tp.world_size if tp is not None else 1
@@ -58,7 +58,7 @@ def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_
                         max_batch=max_batch, max_model_len=max_model_len, tp_size=tp_size, num_blocks=num_blocks)
     rn = ModelRunner(cfg, w, num_blocks=nb, block_size=block_size, max_batch=max_batch,
                      max_model_len=max_model_len, device=device, tp=tp, seed=seed,
-                     max_seqs=max_seqs or max(2 * max_batch + 1, 64))
+                     max_seqs=max_seqs or max(2 * max_batch + 1, 64), kv_alloc=kv_alloc)
     if not resident:
         rn.enable_streaming(stream_slots)
     return rn

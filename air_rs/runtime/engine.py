@@ -227,6 +227,25 @@ class Engine:
             budget -= len(r.prompt_ids) - hit
         return admitted
 
+    def _request_for_handoff(self, prompt_ids: list[int], params: SamplingParams | None,
+                             generated: list[int]) -> Request:
+        """Disaggregated decode: a running request whose prompt KV arrives from a prefill
+        engine (``prompt_ids`` already include BOS). Reserves the KV blocks the sender fills."""
+        params = params or SamplingParams()
+        if not self.free_slots:
+            raise RuntimeError("no free sequence slot for a handed-over request")
+        r = Request(next(self._rid), list(prompt_ids), params)
+        r.seq = self.seqs.create_sequence()
+        self.seqs.append(r.seq, len(prompt_ids))
+        r.slot = self.free_slots.pop()
+        r.prefilled = len(prompt_ids)
+        self.runner.reset_counts(r.slot, torch.tensor(list(prompt_ids) + list(generated), dtype=torch.int32))
+        for t in generated:
+            self._emit(r, t)
+        if not r.finished:
+            self.running.append(r)
+        return r
+
     # ------------------------------------------------------------------ preemption (KV host tier)
     def _blocks_needed(self, batch) -> int:
         """New KV blocks the next decode step opens (a sequence whose KV fills whole blocks)."""

@@ -46,7 +46,9 @@ class ModelRunner:
     def __init__(self, cfg: ModelConfig, weights: LlamaWeights, *, num_blocks: int,
                  block_size: int = 16, max_batch: int = 64, max_model_len: int = 4096,
                  max_seqs: int = 256, max_prefill_tokens: int = 8192, device="cuda", tp=None,
-                 seed: int = 0, use_gemm_kernel: bool = True):
+                 seed: int = 0, use_gemm_kernel: bool = True, kv_alloc=None):
+        """``kv_alloc(nbytes) -> uint8 CUDA tensor`` supplies the KV pool's memory (e.g. a
+        cudaMalloc'd buffer exported over CUDA IPC for prefill->decode KV pushes)."""
         self.cfg, self.w = cfg, weights
         self.device = torch.device(device)
         self.tp = tp
@@ -69,7 +71,15 @@ class ModelRunner:
         self.use_gemm_kernel = use_gemm_kernel
         dev = self.device
         L = cfg.n_layers
-        self.kv = torch.zeros(L, num_blocks, 2, self.nkv, block_size, self.hd, dtype=torch.bfloat16, device=dev)
+        kv_shape = (L, num_blocks, 2, self.nkv, block_size, self.hd)
+        if kv_alloc is None:
+            self.kv = torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev)
+        else:
+            n = 1
+            for d_ in kv_shape:
+                n *= d_
+            self._kv_buf = kv_alloc(2 * n)
+            self.kv = self._kv_buf[: 2 * n].view(torch.bfloat16).view(kv_shape)
         rot = self.hd if cfg.partial_rope_factor is None else int(self.hd * cfg.partial_rope_factor)
         self.rot_dim = rot
         self.rope_cs = ops.rope_table(max_model_len + 64, rot, cfg.rope_theta, dev)

@@ -16,6 +16,7 @@
 
 void register_gemm_tc(pybind11::module_& m);
 void register_comm(pybind11::module_& m);
+void register_kv_push(pybind11::module_& m);
 air::PeerPush peer_push_from_meta(const at::Tensor& meta);
 
 using at::Tensor;
@@ -251,5 +252,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu", &swiglu);
   m.def("residual_add", &residual_add);
   register_gemm_tc(m);
+  register_kv_push(m);
   register_comm(m);
 }

@@ -45,6 +45,21 @@ int64_t ipc_open(const std::string& handle, int64_t device) {
   return reinterpret_cast<int64_t>(p);
 }
 
+// Lets kernels on `device` dereference pointers into `peer`'s memory (same process).
+bool enable_peer_access(int64_t device, int64_t peer) {
+  int ok = 0;
+  ck(cudaDeviceCanAccessPeer(&ok, (int)device, (int)peer), "cudaDeviceCanAccessPeer");
+  if (!ok) return false;
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  cudaError_t e = cudaDeviceEnablePeerAccess((int)peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return true;
+  }
+  ck(e, "cudaDeviceEnablePeerAccess");
+  return true;
+}
+
 void ipc_close(int64_t ptr) { ck(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)), "cudaIpcCloseMemHandle"); }
 
 void reduce_rmsnorm_quant(const Tensor& meta, Tensor x, optional<Tensor> w, double w_offset, double eps, int64_t B,
@@ -89,6 +104,7 @@ void register_comm(pybind11::module_& m) {
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
+  m.def("enable_peer_access", &enable_peer_access);
   m.def("peer_buffer_bytes", [](int64_t w, int64_t s) { return air::peer_buffer_bytes((int)w, s); });
   m.def("reduce_rmsnorm_quant", &reduce_rmsnorm_quant);
   m.def("peer_push", [](const Tensor& meta, const Tensor& src, int64_t B, int64_t N, int64_t ld) {
