@@ -80,15 +80,17 @@ class LlamaWeights:
     """Device-resident weights, built from (name, raw, qtype, shape) records."""
 
     def __init__(self, cfg: ModelConfig, records: Iterable, device, tp_rank: int = 0, tp_size: int = 1,
-                 layer_device=None):
+                 layer_device=None, layer_range: tuple[int, int] | None = None):
         """``layer_device`` (default: ``device``) holds the per-layer weights; ``"cpu"`` keeps
         them in pinned host memory for layer streaming (S.L.I.P.)."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.layer_device = torch.device(layer_device) if layer_device is not None else self.device
+        # pipeline stage: only layers [l0, l1) are loaded (indexed from 0 here)
+        self.layer_range = tuple(layer_range) if layer_range is not None else (0, cfg.n_layers)
         self.tp_rank, self.tp_size = tp_rank, tp_size
         pending: dict[str, tuple] = {}
-        self.layers: list[LayerWeights | None] = [None] * cfg.n_layers
+        self.layers: list[LayerWeights | None] = [None] * (self.layer_range[1] - self.layer_range[0])
         self.embd = self.out_norm = self.lm_head = None
         for name, raw, qt, shape in records:
             pending[name] = (raw, GGMLType(qt), tuple(shape))
@@ -128,8 +130,13 @@ class LlamaWeights:
         if self.lm_head is None and "output.weight" in p:
             raw, qt, shape = p.pop("output.weight")
             self.lm_head = self._shard_rows_tp(raw, qt, shape)
+        l0, l1 = self.layer_range
         for i in range(cfg.n_layers):
-            if self.layers[i] is not None:
+            if not l0 <= i < l1:
+                for k in [k for k in p if k.startswith(f"blk.{i}.")]:
+                    del p[k]                 # another pipeline stage's layer
+                continue
+            if self.layers[i - l0] is not None:
                 continue
             pre = f"blk.{i}."
             need = ["attn_norm.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight",
@@ -144,11 +151,11 @@ class LlamaWeights:
             g = {n: p.pop(pre + n) for n in need}
             dev, self.device = self.device, self.layer_device
             try:
-                self.layers[i] = self._build_layer(g)
+                self.layers[i - l0] = self._build_layer(g)
             finally:
                 self.device = dev
             if self.layer_device.type == "cpu" and dev.type == "cuda":
-                pin_layer(self.layers[i])
+                pin_layer(self.layers[i - l0])
 
     def _shard_rows_tp(self, raw, qt, shape):
         if self.tp_size == 1:

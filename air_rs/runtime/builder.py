@@ -46,13 +46,14 @@ def plan_kv_blocks(cfg: ModelConfig, weights_bytes: int, *, block_size: int, dev
 
 def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_model_len=4096,
                  block_size=16, num_blocks=None, tp=None, seed=0, max_seqs=None,
-                 resident: bool = True, stream_slots: int = 2, kv_alloc=None) -> ModelRunner:
+                 resident: bool = True, stream_slots: int = 2, kv_alloc=None,
+                 layer_range: tuple[int, int] | None = None) -> ModelRunner:
     """``resident=False``: per-layer weights stay in pinned host memory and are streamed
     through ``stream_slots`` device slots each forward (S.L.I.P. streaming mode)."""
     tp_size = tp.world_size if tp is not None else 1
     tp_rank = tp.rank if tp is not None else 0
     w = LlamaWeights(cfg, records, device, tp_rank=tp_rank, tp_size=tp_size,
-                     layer_device=None if resident else "cpu")
+                     layer_device=None if resident else "cpu", layer_range=layer_range)
     streamed = 0 if resident else stream_slots * max(1, w.nbytes() - w.resident_nbytes()) // cfg.n_layers
     nb = plan_kv_blocks(cfg, w.resident_nbytes() + streamed, block_size=block_size, device=device,
                         max_batch=max_batch, max_model_len=max_model_len, tp_size=tp_size, num_blocks=num_blocks)

@@ -70,7 +70,7 @@ class ModelRunner:
         self.seed = seed
         self.use_gemm_kernel = use_gemm_kernel
         dev = self.device
-        L = cfg.n_layers
+        L = len(weights.layers)          # this pipeline stage's layers
         kv_shape = (L, num_blocks, 2, self.nkv, block_size, self.hd)
         if kv_alloc is None:
             self.kv = torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev)
@@ -352,11 +352,15 @@ class ModelRunner:
                 count_rows: torch.Tensor, temperature, penalty, top_k, top_p, mask=None,
                 return_hidden: bool = False, tree_base: torch.Tensor | None = None,
                 tree_mask: torch.Tensor | None = None, return_logits: bool = False,
-                ctx_len: torch.Tensor | None = None):
+                ctx_len: torch.Tensor | None = None, hidden_in: torch.Tensor | None = None,
+                return_hidden_out: bool = False):
         """Prompt tokens of one or more sequences (concatenated, T total).
 
         row_seq[t] indexes ``block_tables``; last_rows[s] is the row of each sequence's last
         token, whose logits are sampled. Returns (tokens [S] int32, probs [S] f32).
+        Pipeline stages: ``hidden_in`` [T, H] fp32 replaces the embedding (the previous
+        stage's residual stream) and ``return_hidden_out`` returns the residual stream after
+        this runner's layers instead of sampling.
         """
         cfg, w = self.cfg, self.w
         T = ids.numel()
@@ -375,7 +379,10 @@ class ModelRunner:
         # keys [0, ctx) are candidates; tree rows pass their own bound (slot-based, not position)
         ctx = ctx_len if ctx_len is not None else (positions + 1).to(torch.int32)
         tp = self.tp_size > 1
-        ops.embed(w.embd, ids, out_f32=x, err=self.err, n=T)
+        if hidden_in is not None:
+            x.copy_(hidden_in)
+        else:
+            ops.embed(w.embd, ids, out_f32=x, err=self.err, n=T)
         for li in range(len(w.layers)):
             lw = self._layer(li)
             kv = self.kv[li]
@@ -398,6 +405,8 @@ class ModelRunner:
                 ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp, up_off=self.up_off)
                 self._proj_into_residual(hb, lw.wdown, x, o, tp)
             self._layer_done(li)
+        if return_hidden_out:
+            return x.clone()
         if return_hidden:  # final-norm hidden states of every row (embeddings)
             hn = self._ws("hn", (T, self.H), bf16)
             ops.rmsnorm_quant(x, w.out_norm, eps, None, None, y_bf16=hn)
