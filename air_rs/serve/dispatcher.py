@@ -103,9 +103,12 @@ class MockDispatcher(Dispatcher):
 class EngineDispatcher(Dispatcher):
     """Continuous-batching engine loop on a worker thread."""
 
-    def __init__(self, engine, model_name: str = "air-rs"):
+    def __init__(self, engine, model_name: str = "air-rs", health=None):
+        """``health``: an ``air_rs.parallel.health.Heartbeat`` checked before every step."""
         self.engine = engine               # air_rs.runtime.engine.Engine
         self.model_name = model_name
+        self.health = health
+        self.errors = 0
         self._submit: queue.Queue = queue.Queue()
         self._texts: list[str] | None = None
         self._lock = threading.Lock()
@@ -144,9 +147,12 @@ class EngineDispatcher(Dispatcher):
                     item = None
             if eng.has_unfinished():
                 try:
+                    if self.health is not None:
+                        self.health.check()       # a dead peer rank: fail fast, no collective
                     eng.step()
                 except Exception as e:  # fail every in-flight request, keep serving
-                    for r in list(eng.running) + list(eng.waiting):
+                    self.errors += 1
+                    for r in list(eng.running) + list(eng.waiting) + list(getattr(eng, "swapped", [])):
                         cb = getattr(r, "_on_done", None)
                         eng.abort(r.rid)
                         if cb:
