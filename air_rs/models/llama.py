@@ -39,6 +39,7 @@ class LayerWeights:
     router: torch.Tensor | None = None      # [E, H] f32
     experts_gu: list = field(default_factory=list)
     experts_down: list = field(default_factory=list)
+    expert_ids: list = field(default_factory=list)   # global ids of the local experts
 
     @property
     def w_gate(self) -> ops.QWeight:
@@ -199,7 +200,10 @@ class LlamaWeights:
             gr = gr.reshape(E, F, -1)
             ur = ur.reshape(E, F, -1)
             dr = dr.reshape(E, cfg.hidden_dim, -1)
-            for e in range(E):
+            # expert parallelism: under TP the experts are spread over the ranks (expert e on
+            # rank e % tp); attention stays tensor parallel
+            lw.expert_ids = [e for e in range(E) if e % tp == rk]
+            for e in lw.expert_ids:
                 ge = ops.QWeight.from_raw(gr[e], gq, F, cfg.hidden_dim, self.device)
                 ue = ops.QWeight.from_raw(ur[e], uq, F, cfg.hidden_dim, self.device)
                 lw.experts_gu.append(ops.QWeight.cat([ge, ue]))

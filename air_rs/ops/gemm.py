@@ -67,8 +67,9 @@ def workspace(device) -> _Workspace:
 
 def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, residual: bool = False,
            splits: int | None = None, err: torch.Tensor | None = None,
-           dbg: torch.Tensor | None = None) -> torch.Tensor:
-    """out = x @ W^T (or out += x @ W^T when residual, out fp32)."""
+           dbg: torch.Tensor | None = None, row_count: torch.Tensor | None = None) -> torch.Tensor:
+    """out = x @ W^T (or out += x @ W^T when residual, out fp32). ``row_count`` (device int32)
+    limits the tensor-core path to the first rows (token tiles past it exit at once)."""
     T = x.shape[0]
     if T == 0:
         return out
@@ -85,7 +86,7 @@ def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, resid
                                                  ext.gemm_q_counters(w.N, T))
         if err is None:
             err = workspace(x.device).err
-        ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out, mode, s, ws, cnt, err, dbg)
+        ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out, mode, s, ws, cnt, err, dbg, row_count)
         count_launch()
         return out
     if residual:

@@ -1,13 +1,24 @@
-"""Mixture-of-experts FFN on the GPU runner (reference ``src/moe.rs:163-300``).
+"""Mixture-of-experts FFN on the GPU runner, with expert parallelism (reference
+``src/moe.rs:163-300`` routing + per-token expert loop, ``src/moe.rs:510-536`` EP router).
 
 Routing runs on the device (``moe_route``: fp32 router logits, softmax, top-k, renormalise)
-and produces a dense combine matrix ``cw[T, E]`` (zero for experts a token did not pick), so
-the step stays CUDA-graph capturable with no host round trip. Each expert's SwiGLU FFN then
-runs over the batch with the runner's own kernels (decode GEMV with the fused SwiGLU
-epilogue, or the tcgen05 GEMM path) and ``moe_combine`` adds ``cw[:, e] * y_e`` into the
-residual stream; rows whose weight is zero are skipped there. Every expert's weights are
-streamed once per step — for large batches (the Mixtral config's 128-sequence decode) every
-expert is active anyway.
+into a dense combine matrix ``cw[T, E]`` (zero for experts a token did not pick), so the step
+has no host round trip and stays CUDA-graph capturable.
+
+* Decode GEMV path (B <= 8): each local expert's SwiGLU FFN runs over the batch with the
+  fused GEMV kernels (weights are read once either way) and ``moe_combine`` adds
+  ``cw[:, e] * y_e`` (zero-weight rows skipped).
+* Batched / prefill path: per local expert, ``moe_select`` lists the tokens routed to it,
+  ``moe_gather`` packs their rows, the tcgen05 GEMMs run on that group only (token tiles past
+  the device-side count exit at once — launches keep a fixed shape), and ``moe_scatter``
+  adds the weighted outputs back.
+
+Expert parallelism: under TP the experts are spread over the ranks (expert e on rank
+e % tp) while attention stays tensor parallel, so every rank holds every token's
+activations after the attention all-reduce — the dispatch is a local gather with no
+communication, and the combine is the sum over ranks of each rank's partial expert output,
+done by the same fused peer-memory push / reduce-RMSNorm as the dense row-parallel layers
+(NCCL all-reduce when the peer path is off).
 """
 from __future__ import annotations
 
@@ -26,58 +37,87 @@ def _ensure(rn, name, shape, dtype):
     return t
 
 
-def _check(rn):
-    if rn.tp_size > 1:
-        raise NotImplementedError("MoE layers under tensor parallelism: use expert parallelism")
+def _ids(lw):
+    return lw.expert_ids or list(range(len(lw.experts_gu)))
 
 
-def moe_ffn_decode(rn, lw, B, x, xq, xds):
+def _finish(rn, T, x, partial, peer):
+    """EP combine: partial expert outputs of this rank -> every rank's residual stream."""
+    if rn.tp_size == 1:
+        return
+    if peer is not None:
+        peer.push(partial[:T], T)            # summed by the next reduce-RMSNorm
+    else:
+        rn.tp.all_reduce_add(partial[:T], x[:T])
+
+
+def moe_ffn_decode(rn, lw, B, x, xq, xds, peer=None):
     """GEMV path (B <= 8). Expects ``rn.xn_b[:B]`` = normalised input (bf16) and xq/xds its
     quantised form."""
-    _check(rn)
     ext = ops.require_ext()
-    E = len(lw.experts_gu)
+    E = rn.cfg.n_experts
     cw = _ensure(rn, "moe_cw", (rn.max_batch, E), torch.float32)
     hq = _ensure(rn, "moe_hq", (rn.max_batch, rn.Fp), torch.int8)
     hds = _ensure(rn, "moe_hds", (rn.max_batch, rn.Fp // 32, 2), torch.float32)
     ext.moe_route(rn.xn_b[:B], B, lw.router, rn.cfg.moe_top_k, True, cw[:B], None, None)
     ops.count_launch()
-    for e in range(E):
-        gu, dn = lw.experts_gu[e], lw.experts_down[e]
+    ep = rn.tp_size > 1
+    acc = x
+    if ep:
+        acc = _ensure(rn, "moe_part", (rn.max_batch, rn.H), torch.float32)
+        acc[:B].zero_()
+    for gu, dn, e in zip(lw.experts_gu, lw.experts_down, _ids(lw)):
         ops.gemv(gu.part(0), xq, xds, B, ops.EPI_SWIGLU, w2=gu.part(1), out_f32=rn.h[:B], ld_out=rn.Fp)
         ops.rmsnorm_quant(rn.h[:B], None, 0.0, hq[:B], hds[:B])
         ops.gemv(dn, hq[:B], hds[:B], B, ops.EPI_STORE, out_f32=rn.y[:B])
-        ext.moe_combine(x[:B], rn.y[:B], cw[:B], e, E, B)
+        ext.moe_combine(acc[:B], rn.y[:B], cw[:B], e, E, B)
         ops.count_launch()
+    if ep:
+        _finish(rn, B, x, acc, peer)
 
 
-def _ffn_tokens(rn, lw, T, x, xn, gu_buf, h_buf, y_buf, cw):
+def _ffn_tokens(rn, lw, T, x, xn, bufs, peer=None):
     ext = ops.require_ext()
-    E = len(lw.experts_gu)
+    E = rn.cfg.n_experts
+    cw, idx, wts, cnt, xg, gu_buf, h_buf, y_buf = (bufs[k] for k in ("cw", "idx", "wts", "cnt", "xg", "gu", "h", "y"))
     ext.moe_route(xn[:T], T, lw.router, rn.cfg.moe_top_k, True, cw[:T], None, None)
     ops.count_launch()
-    for e in range(E):
-        gu, dn = lw.experts_gu[e], lw.experts_down[e]
-        rn.linear(xn[:T], gu, gu_buf[:T])
+    ep = rn.tp_size > 1
+    acc = bufs["part"] if ep else x
+    if ep:
+        acc[:T].zero_()
+    for j, (gu, dn, e) in enumerate(zip(lw.experts_gu, lw.experts_down, _ids(lw))):
+        c = cnt[j:j + 1]
+        ext.moe_select(cw[:T], e, T, idx, wts, c)
+        ext.moe_gather(xn[:T], idx, c, T, xg)
+        rn.linear_rows(xg[:T], gu, gu_buf[:T], c)
         ops.swiglu(gu_buf[:T], T, rn.F, out_bf16=h_buf[:T], ld_out=rn.Fp, up_off=gu.parts[1][0])
-        rn.linear(h_buf[:T], dn, y_buf[:T])
-        ext.moe_combine(x[:T], y_buf[:T], cw[:T], e, E, T)
-        ops.count_launch()
+        rn.linear_rows(h_buf[:T], dn, y_buf[:T], c)
+        ext.moe_scatter(acc[:T], y_buf[:T], idx, wts, c, T)
+        ops.count_launch(3)
+    if ep:
+        _finish(rn, T, x, acc, peer)
 
 
-def moe_ffn_gemm(rn, lw, B, x):
+def _bufs(rn, T, prefix, alloc):
+    E = rn.cfg.n_experts
+    return {"cw": alloc(prefix + "cw", (T, E), torch.float32),
+            "idx": alloc(prefix + "idx", (T,), torch.int32),
+            "wts": alloc(prefix + "wts", (T,), torch.float32),
+            "cnt": alloc(prefix + "cnt", (max(1, len(rn.w.layers[0].experts_gu)),), torch.int32),
+            "xg": alloc(prefix + "xg", (T, rn.H), torch.bfloat16),
+            "gu": alloc(prefix + "gu", (T, rn.gu_w), torch.bfloat16),
+            "h": alloc(prefix + "h", (T, rn.Fp), torch.bfloat16),
+            "y": alloc(prefix + "y", (T, rn.H), torch.float32),
+            "part": alloc(prefix + "part", (T, rn.H), torch.float32)}
+
+
+def moe_ffn_gemm(rn, lw, B, x, peer=None):
     """Batched decode (GEMM path): input is ``rn.xn_b[:B]`` (bf16, normalised)."""
-    _check(rn)
-    E = len(lw.experts_gu)
-    cw = _ensure(rn, "moe_cw", (rn.max_batch, E), torch.float32)
-    _ffn_tokens(rn, lw, B, x, rn.xn_b, rn.gu_b, rn.h_b, rn.y, cw)
+    bufs = _bufs(rn, rn.max_batch, "moe_d_", lambda n, s, d: _ensure(rn, n, s, d))
+    _ffn_tokens(rn, lw, B, x, rn.xn_b, bufs, peer)
 
 
 def moe_ffn_prefill(rn, lw, T, x, xn):
-    _check(rn)
-    E = len(lw.experts_gu)
-    cw = rn._ws("moe_cw", (T, E), torch.float32)
-    gu = rn._ws("gu", (T, rn.gu_w), torch.bfloat16)
-    hb = rn._ws("hb", (T, rn.Fp), torch.bfloat16, zero=True)
-    y = rn._ws("moe_y", (T, rn.H), torch.float32)
-    _ffn_tokens(rn, lw, T, x, xn, gu, hb, y, cw)
+    bufs = _bufs(rn, T, "moe_p_", lambda n, s, d: rn._ws(n, s, d, zero=(n.endswith("h"))))
+    _ffn_tokens(rn, lw, T, x, xn, bufs, None)

@@ -58,7 +58,8 @@ class ModelRunner:
         self.nkv = max(1, cfg.n_kv_heads // tp_size)
         self.hd = cfg.head_dim
         self.H = cfg.hidden_dim
-        self.F = cfg.intermediate_dim // tp_size
+        # MoE experts are not split across TP ranks (expert parallelism places whole experts)
+        self.F = cfg.intermediate_dim if cfg.n_experts else cfg.intermediate_dim // tp_size
         self.Fp = ops.pad32(self.F)  # activation width of the down projection (zero padded)
         self.V = cfg.vocab_size
         self.V_l = weights.lm_head.N
@@ -172,6 +173,14 @@ class ModelRunner:
         from ..ops import gemm
         return gemm.linear(x_bf16, w, out, self, residual=residual, err=self.err)
 
+    def linear_rows(self, x_bf16, w: ops.QWeight, out, row_count: torch.Tensor):
+        """``linear`` for the first ``row_count`` (device int32) rows; later rows are left
+        unspecified (routed-expert groups launched for a fixed capacity)."""
+        from ..ops import gemm
+        if gemm.tc_supported(w):
+            return gemm.linear(x_bf16, w, out, self, err=self.err, row_count=row_count)
+        return gemm.linear(x_bf16, w, out, self, err=self.err)
+
     def _proj_into_residual(self, xin, w, x, obuf, tp: bool, peer=None):
         """x += xin @ W^T: fused into the GEMM epilogue, or partial + all-reduce under TP.
 
@@ -271,7 +280,7 @@ class ModelRunner:
     def _ffn_gemv(self, lw, B, x, xq, xds, tp, peer=None):
         if lw.wgu is None:
             from ..parallel import moe
-            moe.moe_ffn_decode(self, lw, B, x, xq, xds)
+            moe.moe_ffn_decode(self, lw, B, x, xq, xds, peer)
             return
         ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, out_f32=self.h[:B], ld_out=self.Fp)
         ops.rmsnorm_quant(self.h[:B], None, 0.0, xq, xds)
@@ -280,7 +289,7 @@ class ModelRunner:
     def _ffn_gemm(self, lw, B, x, tp, peer=None):
         if lw.wgu is None:
             from ..parallel import moe
-            moe.moe_ffn_gemm(self, lw, B, x)
+            moe.moe_ffn_gemm(self, lw, B, x, peer)
             return
         self.linear(self.xn_b[:B], lw.wgu, self.gu_b[:B])
         ops.swiglu(self.gu_b[:B], B, self.F, out_bf16=self.h_b[:B], ld_out=self.Fp, up_off=self.up_off)

@@ -237,6 +237,29 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                             (int)E, (int)T, (int)x.size(1), stream());
     post_launch("moe_combine");
   });
+  m.def("moe_select", [](Tensor cw, int64_t e, int64_t T, Tensor idx, Tensor wts, Tensor count) {
+    TORCH_CHECK(cw.is_cuda() && cw.scalar_type() == torch::kFloat && cw.dim() == 2, "moe_select: cw [T, E] fp32");
+    TORCH_CHECK(idx.numel() >= T && wts.numel() >= T && count.numel() >= 1, "moe_select: buffers");
+    air::launch_moe_select(cw.data_ptr<float>(), (int)e, (int)cw.size(1), (int)T, idx.data_ptr<int>(),
+                           wts.data_ptr<float>(), count.data_ptr<int>(), stream());
+    post_launch("moe_select");
+  });
+  m.def("moe_gather", [](Tensor x, Tensor idx, Tensor count, int64_t cap, Tensor xg) {
+    TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && xg.scalar_type() == torch::kBFloat16 && x.stride(1) == 1,
+                "moe_gather: bf16 rows");
+    const int H = (int)x.size(1);
+    TORCH_CHECK(H % 8 == 0 && x.stride(0) % 8 == 0 && xg.size(1) == H && xg.size(0) >= cap, "moe_gather: shapes");
+    air::launch_moe_gather(x.data_ptr(), x.stride(0), H, idx.data_ptr<int>(), count.data_ptr<int>(), (int)cap,
+                           xg.data_ptr(), stream());
+    post_launch("moe_gather");
+  });
+  m.def("moe_scatter", [](Tensor out, Tensor y, Tensor idx, Tensor wts, Tensor count, int64_t cap) {
+    TORCH_CHECK(out.scalar_type() == torch::kFloat && y.scalar_type() == torch::kFloat && out.is_contiguous(),
+                "moe_scatter: fp32");
+    air::launch_moe_scatter(out.data_ptr<float>(), y.data_ptr<float>(), y.stride(0), (int)out.size(1),
+                            idx.data_ptr<int>(), wts.data_ptr<float>(), count.data_ptr<int>(), (int)cap, stream());
+    post_launch("moe_scatter");
+  });
   m.def("rmsnorm_quant", &rmsnorm_quant);
   m.def("gemv", &gemv);
   m.def("gemv_tiled_splits", [](int64_t N, int64_t K, int64_t mode) { return air::gemv_tiled_splits((int)N, (int)K, (int)mode); });

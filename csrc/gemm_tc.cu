@@ -80,6 +80,9 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
               GemmArgs a) {
   using C = Cfg<NT, FMT, NA, AT>;
   static_assert(!AT || FMT == kFmtQ4K, "A-in-TMEM path: Q4_K only");
+  // routed-expert GEMMs: token tiles beyond the device row count do nothing (uniform per CTA,
+  // before any barrier, TMEM allocation or copy)
+  if (a.row_count != nullptr && (int)blockIdx.y * NT >= __ldg(a.row_count)) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;

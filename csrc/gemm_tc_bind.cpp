@@ -9,7 +9,8 @@ namespace {
 
 void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, int64_t N, int64_t K,
             Tensor x, Tensor out, int64_t mode, int64_t splits, optional<Tensor> ws,
-            optional<Tensor> counters, optional<Tensor> err, optional<Tensor> dbg) {
+            optional<Tensor> counters, optional<Tensor> err, optional<Tensor> dbg,
+            optional<Tensor> row_count) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2, "gemm_q: x must be 2-D bf16 CUDA");
   TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "gemm_q: rows must be contiguous");
   TORCH_CHECK(x.size(1) == K, "gemm_q: x has ", x.size(1), " columns, expected K=", K);
@@ -37,6 +38,7 @@ void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, i
   TORCH_CHECK(err.has_value(), "gemm_q: an error word is required (bounded waits report into it)");
   a.err = err->data_ptr<int>();
   a.dbg = dbg.has_value() ? (long long*)dbg->data_ptr<int64_t>() : nullptr;
+  a.row_count = row_count.has_value() ? row_count->data_ptr<int>() : nullptr;
   const char* e = air::launch_gemm_q((int)fmt, w.data_ptr(), row_bytes, x.data_ptr(), x.stride(0), a,
                                      at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(e == nullptr, e ? e : "");

@@ -70,7 +70,80 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const float* __restric
     x[(int64_t)t * H + h] += c * y[t * ldy + h];
 }
 
+// One CTA: tokens routed to expert e (cw[t, e] > 0) in token order -> idx, wts, *count.
+__global__ void __launch_bounds__(1024)
+moe_select_kernel(const float* __restrict__ cw, int e, int E, int T, int* __restrict__ idx,
+                  float* __restrict__ wts, int* __restrict__ count) {
+  __shared__ int warp_tot[32];
+  __shared__ int base;
+  if (threadIdx.x == 0) base = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    const float w = t < T ? cw[(int64_t)t * E + e] : 0.f;
+    const bool sel = w > 0.f;
+    const unsigned m = __ballot_sync(0xffffffffu, sel);
+    if (lane == 0) warp_tot[warp] = __popc(m);
+    __syncthreads();
+    int off = base;
+    for (int k = 0; k < warp; ++k) off += warp_tot[k];
+    if (sel) {
+      const int p = off + __popc(m & ((1u << lane) - 1));
+      idx[p] = t;
+      wts[p] = w;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int s = 0;
+      for (int k = 0; k < (int)(blockDim.x >> 5); ++k) s += warp_tot[k];
+      base += s;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *count = base;
+}
+
+// Grid (cap): row i < count copies x[idx[i]] (bf16) into xg[i].
+__global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int H, const int* __restrict__ idx,
+                                  const int* __restrict__ count, __nv_bfloat16* __restrict__ xg) {
+  const int i = blockIdx.x;
+  if (i >= __ldg(count)) return;
+  const uint4* s = reinterpret_cast<const uint4*>(x + (int64_t)idx[i] * ldx);
+  uint4* d = reinterpret_cast<uint4*>(xg + (int64_t)i * H);
+  for (int k = threadIdx.x; k < H / 8; k += blockDim.x) d[k] = s[k];
+}
+
+// Grid (cap): row i < count adds wts[i] * y[i] into out[idx[i]] (one expert per launch, so a
+// token appears at most once).
+__global__ void moe_scatter_kernel(float* __restrict__ out, const float* __restrict__ y, int64_t ldy, int H,
+                                   const int* __restrict__ idx, const float* __restrict__ wts,
+                                   const int* __restrict__ count) {
+  const int i = blockIdx.x;
+  if (i >= __ldg(count)) return;
+  const float w = wts[i];
+  float* o = out + (int64_t)idx[i] * H;
+  const float* yr = y + (int64_t)i * ldy;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) o[k] += w * yr[k];
+}
+
 }  // namespace
+
+void launch_moe_select(const float* cw, int e, int E, int T, int* idx, float* wts, int* count, cudaStream_t st) {
+  moe_select_kernel<<<1, 1024, 0, st>>>(cw, e, E, T, idx, wts, count);
+}
+
+void launch_moe_gather(const void* x, int64_t ldx, int H, const int* idx, const int* count, int cap, void* xg,
+                       cudaStream_t st) {
+  if (cap <= 0) return;
+  moe_gather_kernel<<<cap, 128, 0, st>>>((const __nv_bfloat16*)x, ldx, H, idx, count, (__nv_bfloat16*)xg);
+}
+
+void launch_moe_scatter(float* out, const float* y, int64_t ldy, int H, const int* idx, const float* wts,
+                        const int* count, int cap, cudaStream_t st) {
+  if (cap <= 0) return;
+  moe_scatter_kernel<<<cap, 256, 0, st>>>(out, y, ldy, H, idx, wts, count);
+}
 
 void launch_moe_route(const void* x, bool x_bf16, int64_t ldx, int T, int H, const float* router, int E, int k,
                       bool normalize, float* cw, int* ids, float* wts, cudaStream_t st) {

@@ -15,4 +15,14 @@ void launch_moe_route(const void* x, bool x_bf16, int64_t ldx, int T, int H, con
 void launch_moe_combine(float* x, const float* y, int64_t ldy, const float* cw, int e, int E, int T, int H,
                         cudaStream_t st);
 
+// Routed-expert grouping (per expert e): select the tokens with cw[t, e] > 0 (in token order)
+// into idx / wts / *count; gather their bf16 rows into xg [cap, H]; scatter-add
+// wts[i] * y[i] back into out[idx[i]] (fp32 [T, H]). Kernels past *count do nothing, so the
+// launches have a fixed shape (graph capturable).
+void launch_moe_select(const float* cw, int e, int E, int T, int* idx, float* wts, int* count, cudaStream_t st);
+void launch_moe_gather(const void* x, int64_t ldx, int H, const int* idx, const int* count, int cap, void* xg,
+                       cudaStream_t st);
+void launch_moe_scatter(float* out, const float* y, int64_t ldy, int H, const int* idx, const float* wts,
+                        const int* count, int cap, cudaStream_t st);
+
 }  // namespace air

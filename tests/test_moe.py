@@ -70,3 +70,51 @@ def test_moe_engine_matches_oracle(qt):
     outs = eng.generate_ids(prompts, SamplingParams(max_tokens=6, temperature=0.0, ignore_eos=True))
     _check_near_argmax(oracle, [cfg.bos_token_id] + prompts[0], outs[0])
     runner.check_errors()
+
+
+@pytest.mark.gpu
+def test_moe_select_gather_scatter_kernels():
+    from air_rs import ops
+    ext = ops.require_ext()
+    g = torch.Generator().manual_seed(1)
+    T, E, H = 300, 8, 256
+    cw = torch.zeros(T, E)
+    for t in range(T):
+        e = torch.randperm(E, generator=g)[:2]
+        cw[t, e] = torch.rand(2, generator=g) + 0.1
+    cw = cw.cuda()
+    idx = torch.zeros(T, dtype=torch.int32, device="cuda")
+    wts = torch.zeros(T, device="cuda")
+    cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ext.moe_select(cw, 3, T, idx, wts, cnt)
+    want = torch.nonzero(cw[:, 3].cpu() > 0).flatten()
+    n = int(cnt.item())
+    assert n == want.numel() and idx[:n].cpu().tolist() == want.tolist()
+    torch.testing.assert_close(wts[:n].cpu(), cw[want, 3].cpu())
+    x = torch.randn(T, H, generator=g).cuda().bfloat16()
+    xg = torch.zeros(T, H, device="cuda", dtype=torch.bfloat16)
+    ext.moe_gather(x, idx, cnt, T, xg)
+    assert torch.equal(xg[:n], x[want.cuda()])
+    out = torch.zeros(T, H, device="cuda")
+    y = torch.randn(T, H, generator=g).cuda()
+    ext.moe_scatter(out, y, idx, wts, cnt, T)
+    ref = torch.zeros(T, H)
+    ref[want] = cw[want, 3].cpu()[:, None] * y[:n].cpu()
+    torch.testing.assert_close(out.cpu(), ref)
+
+
+@pytest.mark.gpu
+def test_grouped_gemm_row_count_limits_work():
+    from air_rs import ops
+    from air_rs.ops import gemm
+    from air_rs.gguf import quantize
+    g = torch.Generator().manual_seed(2)
+    N, K, T = 256, 512, 300
+    w = ops.QWeight.from_raw(quantize(torch.randn(N, K, generator=g) * 0.05, GGMLType.Q4_K), GGMLType.Q4_K, N, K, "cuda")
+    x = torch.randn(T, K, generator=g).cuda().bfloat16()
+    full = torch.zeros(T, N, device="cuda")
+    gemm.linear(x, w, full)
+    part = torch.full((T, N), 7.0, device="cuda")
+    gemm.linear(x, w, part, row_count=torch.tensor([40], dtype=torch.int32, device="cuda"))
+    torch.testing.assert_close(part[:40], full[:40])
+    assert torch.all(part[128:] == 7.0)     # token tiles past the count did nothing

@@ -27,10 +27,13 @@ def test_fused_allreduce_matches_nccl(tmp_path):
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = json.loads(out.read_text())
-    for B in (4, 16):
-        a, b = res[f"nccl_B{B}"], res[f"ours_B{B}"]
+    for pre, B in [(p, b) for p in ("", "moe_") for b in (4, 16)]:
+        a, b = res[f"{pre}nccl_B{B}"], res[f"{pre}ours_B{B}"]
         # the first two tokens (prefill + first fused decode step) agree for every sequence;
         # later ones may part at fp32 summation-order near-ties of a random model
-        assert all(x[:2] == y[:2] for x, y in zip(a, b)), (a, b)
+        assert all(x[:2] == y[:2] for x, y in zip(a, b)), (pre, a, b)
         same = sum(x == y for x, y in zip(a, b))
-        assert same >= 0.75 * len(a), (same, len(a))
+        assert same >= 0.75 * len(a), (pre, same, len(a))
+        single = res[f"{pre or 'dense_'}single_B{B}"]
+        # TP / EP against the unsharded model: first token from the same prefill math
+        assert sum(x[:1] == y[:1] for x, y in zip(single, b)) >= 0.75 * len(b), (pre, single, b)

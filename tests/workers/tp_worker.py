@@ -25,6 +25,21 @@ def main(out_path: str):
                       bos_token_id=1, eos_token_id=2)
     g = torch.Generator().manual_seed(7)
     res = {"world": tp0.world_size}
+    moe = ModelConfig(n_layers=2, n_heads=8, n_kv_heads=4, hidden_dim=1024, intermediate_dim=1024,
+                      vocab_size=4096, rope_theta=10000.0, rms_norm_eps=1e-5, head_dim=128,
+                      bos_token_id=1, eos_token_id=2, n_experts=4, moe_top_k=2)
+    for name, mcfg in (("dense", cfg), ("moe", moe)):
+        if name == "moe":
+            cfg = mcfg
+        run_model(res, name, cfg, tp0, dev, g)
+    if tp0.rank == 0:
+        with open(out_path, "w") as f:
+            json.dump(res, f)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
+def run_model(res, name, cfg, tp0, dev, g):
     for B in (4, 16):
         prompts = [torch.randint(3, cfg.vocab_size, (int(l),), generator=g).tolist()
                    for l in torch.randint(5, 40, (B,), generator=g)]
@@ -38,18 +53,18 @@ def main(out_path: str):
             t0 = time.perf_counter()
             eng.generate_ids(prompts, sp)
             torch.cuda.synchronize()
-            res[f"{impl}_B{B}"] = out
-            res[f"{impl}_B{B}_s"] = time.perf_counter() - t0
-            res[f"{impl}_B{B}_logits"] = eng.runner.logits_full[:B].float().cpu().tolist()[0][:64]
+            key = f"{impl}_B{B}" if name == "dense" else f"{name}_{impl}_B{B}"
+            res[key] = out
+            res[key + "_s"] = time.perf_counter() - t0
             if impl == "ours":
                 tp.peer.close()
             del eng
             torch.cuda.empty_cache()
-    if tp0.rank == 0:
-        with open(out_path, "w") as f:
-            json.dump(res, f)
-    torch.distributed.barrier()
-    torch.distributed.destroy_process_group()
+        if tp0.rank == 0:     # the same model on one GPU (no TP / EP)
+            eng = random_engine(cfg, seed=3, device=dev, max_batch=B, max_model_len=256)
+            res[f"{name}_single_B{B}"] = eng.generate_ids(prompts, sp)
+            del eng
+            torch.cuda.empty_cache()
 
 
 if __name__ == "__main__":
