@@ -386,7 +386,7 @@ class PdPair:
         self.timeout_s = timeout_s
         self.metrics = TransferMetrics()
 
-    def submit(self, prompt_ids: list[int], params) -> int:
+    def submit(self, prompt_ids: list[int], params, verify: bool = False) -> int:
         """Prefill on the prefill engine, push its KV into the decode engine, and hand the
         request over (its first token already sampled). Returns the decode-side rid."""
         p, d = self.p, self.d
@@ -415,6 +415,12 @@ class PdPair:
             with torch.cuda.device(d.runner.device):
                 d.abort(dr.rid)
             raise KvTransferError("timeout", f"KV push for request {rid} did not complete")
+        if verify:   # debugging aid: the decode pool now holds exactly the prefill KV
+            a_ = p.runner.kv[:, torch.tensor(src_blocks, device=p.runner.device)].cpu()
+            b_ = d.runner.kv[:, torch.tensor(dst_blocks, device=d.runner.device)].cpu()
+            if not torch.equal(a_, b_):
+                raise KvTransferError("corrupt", f"decode blocks differ from prefill blocks "
+                                                 f"({int((a_ != b_).sum())} elements)")
         self.metrics.record_transfer(len(src_blocks) * d.runner.kv.shape[0] * KvPushLink.block_bytes(
             tuple(d.runner.kv.shape)), time.perf_counter() - t0)
         with torch.cuda.device(p.runner.device):

@@ -100,7 +100,7 @@ def test_device_kv_push_handoff_matches_single_engine():
     g = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, cfg.vocab_size, (int(n),), generator=g).tolist() for n in (37, 12)]
     sp = SamplingParams(max_tokens=16, temperature=0.0, repetition_penalty=1.0, ignore_eos=True)
-    rids = [pair.submit(p, sp) for p in prompts]
+    rids = [pair.submit(p, sp, verify=True) for p in prompts]
     with torch.cuda.device(dec.runner.device):
         while dec.has_unfinished():
             dec.step()
