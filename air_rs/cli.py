@@ -127,10 +127,18 @@ def cmd_generate(args) -> int:
         eng.set_grammar(spec)
     cfg = GenerateConfig(max_tokens=args.max_tokens, temperature=args.temperature, top_p=args.top_p,
                          top_k=args.top_k, repetition_penalty=args.repetition_penalty)
-    if args.model_draft:
+    if (args.model_draft or args.council) and core.runner is not None:
         from .spec.speculative import SpeculativeDecoder
-        draft = _engine(argparse.Namespace(**{**vars(args), "model": args.model_draft}), max_batch=8)
-        sd = SpeculativeDecoder(core, draft, k=args.draft_max)
+        draft = (_engine(argparse.Namespace(**{**vars(args), "model": args.model_draft}), max_batch=8)
+                 if args.model_draft else None)
+        if args.council:
+            from .spec.medusa import CouncilDecoder
+            # voters: the draft model (when given) and the target itself; a draft chain grows
+            # only while their next-token distributions agree within epsilon (JSD)
+            sd = CouncilDecoder(core, [v for v in (draft, core) if v is not None], epsilon=args.epsilon,
+                                k=args.draft_max)
+        else:
+            sd = SpeculativeDecoder(core, draft, k=args.draft_max)
         ids, stats = sd.generate(core.tokenizer.encode(args.prompt), args.max_tokens, temperature=args.temperature)
         text = core.tokenizer.decode(ids)
         if rank0:

@@ -362,7 +362,7 @@ class ModelRunner:
                 return_hidden: bool = False, tree_base: torch.Tensor | None = None,
                 tree_mask: torch.Tensor | None = None, return_logits: bool = False,
                 ctx_len: torch.Tensor | None = None, hidden_in: torch.Tensor | None = None,
-                return_hidden_out: bool = False):
+                return_hidden_out: bool = False, return_final_hidden: bool = False):
         """Prompt tokens of one or more sequences (concatenated, T total).
 
         row_seq[t] indexes ``block_tables``; last_rows[s] is the row of each sequence's last
@@ -429,6 +429,8 @@ class ModelRunner:
             full = self._ws("logits_full", (S, self.V), f32)
             logits = self.tp.all_gather_vocab(logits, full)
         if return_logits:
+            if return_final_hidden:      # (logits, final-norm hidden) of the last rows
+                return logits[:, : self.V].clone(), xs.float().clone()
             return logits[:, : self.V].clone()
         toks = torch.zeros(S, dtype=torch.int32, device=self.device)
         probs = torch.zeros(S, dtype=torch.float32, device=self.device)

@@ -1,0 +1,174 @@
+"""Medusa heads and the CDSC speculative council (reference ``src/medusa_heads.rs``,
+``src/speculative_council.rs``, ``src/async_verifier.rs``).
+
+Both drafters reuse ``SpeculativeDecoder``'s tree verification on the target model (one
+forward over every draft node with ancestor masks, greedy or exact sampled acceptance, KV
+compaction and rollback), so the acceptance statistics are the target's real decisions —
+the reference's council verifier accepted by a hash of the token ids.
+
+* ``MedusaDecoder``: K extra heads on the target's own final hidden state. Head k maps the
+  hidden h_t of the last accepted position to logits for token t+1+k through a residual
+  SiLU block and the target's LM head (``lm(h + silu(W_k h))``); the draft tree takes the
+  top-c tokens of each head as the children of every node of the previous depth (cumulative
+  probability order, capped node count). Heads are random-initialised here (no trained
+  checkpoints offline) and load from a ``.pt`` state dict.
+* ``CouncilDecoder`` (``--council``, ``--epsilon``): several voter drafts (draft engines)
+  propose the next token; the council extends a draft chain only while the voters agree —
+  the Jensen-Shannon divergence of their distributions is at most epsilon — with the
+  argmax of the mean distribution, and stops drafting at the first disagreement.
+"""
+from __future__ import annotations
+
+import math
+import time
+
+import torch
+
+from .eagle2 import DraftNode, DraftTree
+from .speculative import SpeculativeDecoder, _Seq
+
+
+class MedusaHeads:
+    def __init__(self, hidden: int, n_heads: int = 3, device="cuda", seed: int = 0, dtype=torch.float32,
+                 init_scale: float = 0.02):
+        g = torch.Generator().manual_seed(seed)
+        self.W = [(torch.randn(hidden, hidden, generator=g) * init_scale).to(device, dtype) for _ in range(n_heads)]
+        self.n_heads = n_heads
+
+    @classmethod
+    def load(cls, path: str, device="cuda") -> "MedusaHeads":
+        sd = torch.load(path, map_location="cpu")
+        ws = [sd[k] for k in sorted(sd) if k.startswith("head")]
+        obj = cls.__new__(cls)
+        obj.W = [w.to(device, torch.float32) for w in ws]
+        obj.n_heads = len(ws)
+        return obj
+
+    def state_dict(self) -> dict:
+        return {f"head{i}": w.cpu() for i, w in enumerate(self.W)}
+
+    def logits(self, h: torch.Tensor, lm_head_fn) -> list[torch.Tensor]:
+        """h [S, H] final-norm hidden -> per head [S, V] logits."""
+        return [lm_head_fn(h + torch.nn.functional.silu(h @ w.t())) for w in self.W]
+
+
+class MedusaDecoder(SpeculativeDecoder):
+    def __init__(self, target, heads: MedusaHeads, top_c: int = 2, max_nodes: int = 16, eos_id=None):
+        super().__init__(target, None, k=heads.n_heads, max_nodes=max_nodes, eos_id=eos_id)
+        self.heads, self.top_c = heads, top_c
+        self.want_hidden = True
+        self._hidden: dict[int, torch.Tensor] = {}
+        rn = target.runner
+        from ..ops import gemm
+        self._lm = lambda x: gemm.linear(x.to(torch.bfloat16).contiguous(), rn.w.lm_head,
+                                         torch.zeros(x.shape[0], rn.V_l, device=rn.device), rn)[:, : rn.V].float()
+
+    def _prefilled(self, s: _Seq, out):
+        # hidden of the position before the pending token (the prompt's second-to-last)
+        self._hidden[id(s)] = out[1][-1] if isinstance(out, tuple) else None
+
+    def _round(self, active, max_tokens):
+        t0 = time.perf_counter()
+        trees, fed = [], []
+        for s in active:
+            tr = DraftTree(s.tokens[-1], [DraftNode(s.tokens[-1], 1.0, 0, None, 1.0)])
+            h = self._hidden.get(id(s))
+            if h is not None:
+                frontier = [0]
+                for lg in self.heads.logits(h[None], self._lm):
+                    p = torch.softmax(lg[0], -1)
+                    v, ix = torch.topk(p, self.top_c)
+                    nxt = []
+                    for parent in frontier:
+                        for tok, q in zip(ix.tolist(), v.tolist()):
+                            if len(tr.nodes) >= self.builder.max_nodes:
+                                break
+                            tr.nodes.append(DraftNode(tok, q, tr.nodes[parent].depth + 1, parent,
+                                                      tr.nodes[parent].cum_prob * q))
+                            nxt.append(len(tr.nodes) - 1)
+                    frontier = nxt
+            trees.append(tr)
+            fed.append(set())
+        t1 = time.perf_counter()
+        self._verify_commit(active, trees, fed, max_tokens)
+        self.stats.rounds += 1
+        self.stats.draft_ms += (t1 - t0) * 1e3
+        self.stats.verify_ms += (time.perf_counter() - t1) * 1e3
+
+    def _after_verify(self, active, trees, logits, owners):
+        self._owners = owners
+
+    def _accepted(self, si, s, path):
+        # the last accepted node's hidden drives the next round's heads
+        hid = getattr(self, "_verify_hidden", None)
+        if hid is None:
+            return
+        row = [k for k, (sj, i) in enumerate(self._owners) if sj == si and i == path[-1]][0]
+        self._hidden[id(s)] = hid[row]
+
+
+def jsd(dists: list[torch.Tensor]) -> float:
+    """Generalised Jensen-Shannon divergence (nats) of several distributions."""
+    m = torch.stack(dists).mean(0)
+    def kl(p):
+        mask = p > 0
+        return float((p[mask] * (p[mask].log() - m[mask].clamp_min(1e-30).log())).sum())
+    return sum(kl(p) for p in dists) / len(dists)
+
+
+class CouncilDecoder(SpeculativeDecoder):
+    """Consensus drafting over ``voters`` (draft engines sharing the tokenizer)."""
+
+    def __init__(self, target, voters: list, epsilon: float = 0.15, k: int = 4, eos_id=None):
+        super().__init__(target, voters[0], k=k, max_nodes=k + 1, eos_id=eos_id)
+        self.voters, self.epsilon = voters, epsilon
+        self.jsd_history: list[float] = []
+        self._vseq: dict[tuple[int, int], int] = {}
+
+    def _voter_dists(self, vi: int, eng, s: _Seq, chain: list[int]) -> torch.Tensor:
+        """Next-token distribution of voter vi after ``s.tokens + chain`` (its own KV)."""
+        key = (id(s), vi)
+        seq = self._vseq.get(key)
+        ctx = s.tokens + chain
+        if seq is None:
+            seq = self._vseq[key] = eng.seqs.create_sequence()
+        have = eng.seqs.num_tokens(seq)
+        # keep the committed prefix, recompute the rest (chains are short)
+        keep = min(have, len(s.tokens) - 1)
+        eng.seqs.truncate(seq, keep)
+        out = self._plain_prefill(eng, seq, ctx, keep)
+        return torch.softmax(out[0].float() if not isinstance(out, tuple) else out[0][0].float(), -1)
+
+    def _round(self, active, max_tokens):
+        t0 = time.perf_counter()
+        trees, fed = [], []
+        for s in active:
+            tr = DraftTree(s.tokens[-1], [DraftNode(s.tokens[-1], 1.0, 0, None, 1.0)])
+            chain = []
+            for _ in range(self.k):
+                ds = [self._voter_dists(vi, v, s, chain) for vi, v in enumerate(self.voters)]
+                j = jsd(ds)
+                self.jsd_history.append(j)
+                if j > self.epsilon:
+                    break
+                m = torch.stack(ds).mean(0)
+                tok = int(m.argmax())
+                tr.nodes.append(DraftNode(tok, float(m[tok]), len(chain) + 1, len(tr.nodes) - 1, 1.0))
+                chain.append(tok)
+            trees.append(tr)
+            fed.append(set())
+        t1 = time.perf_counter()
+        self._verify_commit(active, trees, fed, max_tokens)
+        self.stats.rounds += 1
+        self.stats.draft_ms += (t1 - t0) * 1e3
+        self.stats.verify_ms += (time.perf_counter() - t1) * 1e3
+
+    def generate_batch(self, prompts, max_tokens, add_bos=True, temperature=0.0, seed=0):
+        d, self.d = self.d, None           # voters keep their own sequences
+        try:
+            return super().generate_batch(prompts, max_tokens, add_bos, temperature, seed)
+        finally:
+            self.d = d
+            for (sid, vi), seq in self._vseq.items():
+                self.voters[vi].seqs.free_sequence(seq)
+            self._vseq.clear()

@@ -74,8 +74,8 @@ class SpeculativeDecoder:
     def __init__(self, target, draft, k: int = 4, top_k: int = DRAFT_TOP_K, tau: float = EXPAND_THRESHOLD,
                  max_nodes: int = 32, eos_id: int | None = None):
         """``target`` / ``draft``: ``air_rs.runtime.engine.Engine`` objects on the GPU."""
-        if target.runner is None or draft.runner is None:
-            raise RuntimeError("speculative decoding needs GPU runners for both models")
+        if target.runner is None or (draft is not None and draft.runner is None):
+            raise RuntimeError("speculative decoding needs GPU runners")
         self.t, self.d = target, draft
         self.k = k
         self.builder = Eagle2Builder(None, tau, top_k, max_depth=k + 1, max_nodes=min(max_nodes, MAX_TREE_NODES))
@@ -102,18 +102,21 @@ class SpeculativeDecoder:
             else torch.tensor(last_rows, dtype=torch.int64, device=dev), None, None, None, None, None,
             tree_base=torch.tensor(col[5], dtype=torch.int32, device=dev),
             tree_mask=torch.tensor(tm, dtype=torch.int64, device=dev),
-            ctx_len=torch.tensor(col[4], dtype=torch.int32, device=dev), return_logits=True)
+            ctx_len=torch.tensor(col[4], dtype=torch.int32, device=dev), return_logits=True,
+            return_final_hidden=getattr(self, "want_hidden", False) and eng is self.t)
 
     def _plain_prefill(self, eng, seq_id, tokens, start):
         """Feed tokens[start:] at positions start.. (no tree; all keys causal)."""
         if not tokens[start:]:
-            return
+            return None
         chunk = 512
+        out = None
         for c in range(start, len(tokens), chunk):
             part = tokens[c:c + chunk]
             slots = eng.seqs.append(seq_id, len(part))
             rows = [(0, tok, c + j, slots[j], c + j + 1, 1 << 30, 0) for j, tok in enumerate(part)]
-            self._forward(eng, rows, [seq_id], last_rows=[len(rows) - 1])
+            out = self._forward(eng, rows, [seq_id], last_rows=[len(rows) - 1])
+        return out
 
     # -- public -------------------------------------------------------------------
     @torch.no_grad()
@@ -130,10 +133,12 @@ class SpeculativeDecoder:
         bos = self.t.cfg.bos_token_id
         for p in prompts:
             toks = ([bos] if add_bos and bos is not None else []) + list(p)
-            s = _Seq(toks, self.t.seqs.create_sequence(), self.d.seqs.create_sequence())
+            s = _Seq(toks, self.t.seqs.create_sequence(), self.d.seqs.create_sequence() if self.d else -1)
             # KV for all but the last (pending) token in both models
-            self._plain_prefill(self.t, s.t_seq, toks[:-1], 0)
-            self._plain_prefill(self.d, s.d_seq, toks[:-1], 0)
+            out = self._plain_prefill(self.t, s.t_seq, toks[:-1], 0)
+            self._prefilled(s, out)
+            if self.d is not None:
+                self._plain_prefill(self.d, s.d_seq, toks[:-1], 0)
             s.d_len = len(toks) - 1
             seqs.append(s)
         try:
@@ -142,7 +147,8 @@ class SpeculativeDecoder:
         finally:
             for s in seqs:
                 self.t.seqs.free_sequence(s.t_seq)
-                self.d.seqs.free_sequence(s.d_seq)
+                if self.d is not None:
+                    self.d.seqs.free_sequence(s.d_seq)
         return [s.out for s in seqs], self.stats
 
     def generate(self, prompt: list[int], max_tokens: int, temperature: float = 0.0, add_bos: bool = True,
@@ -189,6 +195,14 @@ class SpeculativeDecoder:
                 nxt[si].extend(self.builder.add_children(trees[si], node, list(zip(ir, vr))))
             frontier = nxt
         t1 = time.perf_counter()
+        self._verify_commit(active, trees, fed, max_tokens)
+        self.stats.rounds += 1
+        self.stats.draft_ms += (t1 - t0) * 1e3
+        self.stats.verify_ms += (time.perf_counter() - t1) * 1e3
+
+    def _verify_commit(self, active: list[_Seq], trees: list[DraftTree], fed: list[set], max_tokens: int):
+        """Target forward over every tree node, greedy / sampled acceptance, KV compaction of
+        the accepted path and rollback of the rest (target and, when present, draft)."""
         # ---- verify: every node of every tree in one target forward ----
         rows, owners = [], []
         for si, (s, tr) in enumerate(zip(active, trees)):
@@ -200,6 +214,8 @@ class SpeculativeDecoder:
                 rows.append((si, nd.token_id, P + nd.depth, self.t.seqs.slot(s.t_seq, P + i), P + i + 1, P, bits[i]))
                 owners.append((si, i))
         logits = self._forward(self.t, rows, [s.t_seq for s in active])
+        if isinstance(logits, tuple):
+            logits, self._verify_hidden = logits
         if self.temperature > 0:
             pr = torch.softmax(logits.float() / self.temperature, -1)
             tnext = torch.multinomial(pr, 1, generator=self.gen).squeeze(1).tolist()
@@ -208,7 +224,7 @@ class SpeculativeDecoder:
         per_seq = [[0] * len(tr.nodes) for tr in trees]
         for (si, i), tok in zip(owners, tnext):
             per_seq[si][i] = tok
-        t2 = time.perf_counter()
+        self._after_verify(active, trees, logits, owners)
         # ---- accept, compact, roll back ----
         for si, (s, tr) in enumerate(zip(active, trees)):
             P = len(s.tokens) - 1
@@ -221,15 +237,17 @@ class SpeculativeDecoder:
             self.t.seqs.truncate(s.t_seq, P + len(path))
             dst = [self.t.seqs.slot(s.t_seq, P + j) for j in range(len(path))]
             copy_kv_slots(self.t.runner.kv, self.t.runner.block_size, src, dst)
-            # draft: keep the longest prefix of the path that the draft has fed
-            keep = 0
-            while keep < len(path) and path[keep] in fed[si]:
-                keep += 1
-            srcd = [self.d.seqs.slot(s.d_seq, P + i) for i in path[:keep]]
-            self.d.seqs.truncate(s.d_seq, P + keep)
-            dstd = [self.d.seqs.slot(s.d_seq, P + j) for j in range(keep)]
-            copy_kv_slots(self.d.runner.kv, self.d.runner.block_size, srcd, dstd)
-            s.d_len = P + keep
+            self._accepted(si, s, path)
+            if self.d is not None:
+                # draft: keep the longest prefix of the path that the draft has fed
+                keep = 0
+                while keep < len(path) and path[keep] in fed[si]:
+                    keep += 1
+                srcd = [self.d.seqs.slot(s.d_seq, P + i) for i in path[:keep]]
+                self.d.seqs.truncate(s.d_seq, P + keep)
+                dstd = [self.d.seqs.slot(s.d_seq, P + j) for j in range(keep)]
+                copy_kv_slots(self.d.runner.kv, self.d.runner.block_size, srcd, dstd)
+                s.d_len = P + keep
             for tok in new_tokens:
                 if s.done:
                     break
@@ -238,6 +256,13 @@ class SpeculativeDecoder:
                 self.stats.emitted += 1
                 if len(s.out) >= max_tokens or (self.eos_id is not None and tok == self.eos_id):
                     s.done = True
-        self.stats.rounds += 1
-        self.stats.draft_ms += (t1 - t0) * 1e3
-        self.stats.verify_ms += (t2 - t1) * 1e3
+
+    # hooks for drafters that read the target's own hidden states (Medusa)
+    def _prefilled(self, s: _Seq, out):
+        pass
+
+    def _after_verify(self, active, trees, logits, owners):
+        pass
+
+    def _accepted(self, si: int, s: _Seq, path: list[int]):
+        pass

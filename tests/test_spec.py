@@ -1,5 +1,7 @@
 """Speculative decoding: EAGLE-2 tree construction / acceptance on CPU, the tree-verify
 decoder on the GPU (reference tests in ``src/eagle2.rs`` and ``src/speculative.rs``)."""
+import math
+
 import pytest
 import torch
 
@@ -145,3 +147,42 @@ def test_speculative_sampling_runs():
     sd = SpeculativeDecoder(tgt, tgt, k=2, eos_id=-1)
     out, stats = sd.generate([1, 2, 3], max_tokens=16, temperature=0.8, seed=3)
     assert len(out) == 16 and stats.rounds >= 1
+
+
+def test_jsd_properties():
+    from air_rs.spec.medusa import jsd
+    p = torch.tensor([0.5, 0.5, 0.0])
+    q = torch.tensor([0.0, 0.5, 0.5])
+    assert jsd([p, p, p]) == 0.0
+    assert 0 < jsd([p, q]) <= math.log(2) + 1e-6
+
+
+@pytest.mark.gpu
+def test_medusa_and_council_verify_with_target():
+    from air_rs.gguf import GGMLType
+    from air_rs.models.config import tiny_llama
+    from air_rs.models.random_init import random_tensors
+    from air_rs.models.reference import OracleModel
+    from air_rs.runtime.builder import build_runner
+    from air_rs.runtime.engine import Engine
+    from air_rs.spec.medusa import CouncilDecoder, MedusaDecoder, MedusaHeads
+    from test_engine_gpu import _check_near_argmax
+    cfg = tiny_llama()
+    recs = list(random_tensors(cfg, GGMLType.Q8_0, seed=0, device="cpu"))
+    oracle = OracleModel(cfg, {n: (r, q, s) for n, r, q, s in recs})
+    mk = lambda: Engine(cfg, build_runner(cfg, iter(recs), device="cuda", max_batch=8, max_model_len=512,
+                                          num_blocks=128))
+    tgt = mk()
+    prompt = [3, 17, 29, 41, 5, 77]
+    md = MedusaDecoder(tgt, MedusaHeads(cfg.hidden_dim, 3, "cuda"), top_c=2, eos_id=-1)
+    out, st = md.generate(prompt, 16)
+    assert len(out) == 16 and st.rounds >= 1 and st.drafted > 0
+    _check_near_argmax(oracle, [cfg.bos_token_id] + prompt, out, penalty=1.0)
+    used = tgt.seqs.allocator.num_used_blocks()
+    cd = CouncilDecoder(tgt, [mk(), mk()], epsilon=0.05, k=3, eos_id=-1)
+    out, st = cd.generate(prompt, 16)
+    assert len(out) == 16
+    _check_near_argmax(oracle, [cfg.bos_token_id] + prompt, out, penalty=1.0)
+    # identical voters always agree, and they are the target itself: drafts are accepted
+    assert max(cd.jsd_history) < 1e-6 and st.tokens_per_round > 2.0, str(st)
+    assert tgt.seqs.allocator.num_used_blocks() == used
