@@ -253,17 +253,17 @@ class ModelRunner:
                             block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
             ops.paged_attention(self.q[:B], kv, si.block_tables, si.ctx_len, self.attn[:B],
                                 n_rows=B, n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
-                                block_size=self.block_size, n_splits=ns, split_tokens=0,
-                                part_o=self.part_o, part_ml=self.part_ml,
+                                block_size=self.block_size, n_splits=ns if gemv_path else max(2, ns),
+                                split_tokens=0, part_o=self.part_o, part_ml=self.part_ml,
                                 out_q=xq if gemv_path else None, out_ds=xds if gemv_path else None,
-                                err=self.err, window=cfg.sliding_window or 0)
+                                err=self.err, window=cfg.sliding_window or 0,
+                                out_bf16=None if gemv_path else self.attn_b[:B])
             if gemv_path:
                 self._row_parallel(lw.wo, xq, xds, B, x, peer)
                 # MoE layers also need the bf16 normalised row for the router
                 self._norm(x, lw.ffn_norm, B, xq, xds, y_bf16=self.xn_b[:B] if lw.wgu is None else None, peer=peer)
                 self._ffn_gemv(lw, B, x, xq, xds, tp, peer)
             else:
-                self.attn_b[:B].copy_(self.attn[:B])
                 self._proj_into_residual(self.attn_b[:B], lw.wo, x, self.o_b, tp, peer)
                 self._norm(x, lw.ffn_norm, B, y_bf16=self.xn_b[:B], peer=peer)
                 self._ffn_gemm(lw, B, x, tp, peer)

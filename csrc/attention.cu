@@ -236,7 +236,7 @@ template <int D>
 __global__ void __launch_bounds__(D)
 attn_merge_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
                   int n_heads, int n_splits, float* __restrict__ out, int8_t* __restrict__ oq,
-                  float2* __restrict__ ods) {
+                  float2* __restrict__ ods, __nv_bfloat16* __restrict__ ob) {
   const int head = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
   const size_t base = ((size_t)r * n_heads + head) * n_splits;
   float M = -INFINITY;
@@ -251,6 +251,7 @@ attn_merge_kernel(const float* __restrict__ part_o, const float2* __restrict__ p
   const float v = L > 0.f ? O / L : 0.f;
   const size_t o = ((size_t)r * n_heads + head) * D + d;
   if (out) out[o] = v;
+  if (ob) ob[o] = f2bf(v);
   if (oq) {
     const float amax = warp_max(fabsf(v));
     const float dq = amax / 127.f;
@@ -290,7 +291,7 @@ void launch_dg(const AttnArgs& a, cudaStream_t st) {
       a.out, a.err);
   if (a.n_splits > 1) {
     attn_merge_kernel<D><<<dim3(a.n_heads, a.n_rows), D, 0, st>>>(
-        a.part_o, a.part_ml, a.n_heads, a.n_splits, a.out, a.out_q, a.out_ds);
+        a.part_o, a.part_ml, a.n_heads, a.n_splits, a.out, a.out_q, a.out_ds, (__nv_bfloat16*)a.out_bf16);
   } else if (a.out_q) {
     attn_quant_kernel<D><<<dim3(a.n_heads, a.n_rows), D, 0, st>>>(a.out, a.n_heads, a.out_q, a.out_ds);
   }

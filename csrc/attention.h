@@ -27,6 +27,7 @@ struct AttnArgs {
   float2* part_ml;           // [R, n_heads, n_splits]
   float* out;                // [R, n_heads, head_dim] fp32
   int8_t* out_q;             // optional Q8A of out
+  void* out_bf16;            // optional bf16 copy of out (written by the split merge)
   float2* out_ds;
   int* err;
 };

@@ -121,7 +121,8 @@ void paged_attention(Tensor q, Tensor kv, Tensor block_tables, optional<Tensor> 
                      int64_t window, int64_t n_rows, int64_t n_heads, int64_t n_kv, int64_t head_dim,
                      int64_t block_size, int64_t n_splits, int64_t split_tokens, double scale,
                      optional<Tensor> part_o, optional<Tensor> part_ml, Tensor out,
-                     optional<Tensor> out_q, optional<Tensor> out_ds, optional<Tensor> err) {
+                     optional<Tensor> out_q, optional<Tensor> out_ds, optional<Tensor> err,
+                     optional<Tensor> out_bf16) {
   check_cuda(q, "q");
   check_cuda(kv, "kv");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt, "block_tables must be int32");
@@ -146,6 +147,8 @@ void paged_attention(Tensor q, Tensor kv, Tensor block_tables, optional<Tensor> 
   a.out = ptr<float>(out);
   a.out_q = ptr<int8_t>(out_q);
   a.out_ds = ptr<float2>(out_ds);
+  a.out_bf16 = ptr(out_bf16);
+  TORCH_CHECK(!a.out_bf16 || n_splits > 1, "paged_attention: out_bf16 needs the split merge (n_splits > 1)");
   a.err = ptr<int>(err);
   if (n_splits > 1) TORCH_CHECK(a.part_o && a.part_ml, "paged_attention: split scratch required");
   TORCH_CHECK(air::launch_paged_attention(a, stream()), "paged_attention: unsupported head_dim/GQA");

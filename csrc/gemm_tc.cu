@@ -34,7 +34,7 @@ constexpr int kRawRowBytes = 144;           // one Q4_K super-block of one row
 constexpr int kRawTile = 128 * kRawRowBytes; // 18432 B (multiple of 1024)
 constexpr int kATile = 128 * 128;            // 128 rows x 64 bf16
 
-template <int NT, int FMT, int NA, bool AT>
+template <int NT, int FMT, int NA, bool AT, int NACC = 1, int CPS = 1>
 struct Cfg {
   static constexpr int kChunks = FMT == kFmtQ4K ? 4 : 1;         // 64-wide K chunks per stage
   static constexpr int kBChunk = NT * 128;                       // NT rows x 128 B
@@ -44,15 +44,37 @@ struct Cfg {
   static constexpr int kBudget = 227 * 1024 - 2048 - 1024;
   static constexpr int kStages = (kBudget - kABuf) / kStageBytes > 8 ? 8 : (kBudget - kABuf) / kStageBytes;
   static constexpr int kSmem = 1024 + kStages * kStageBytes + kABuf + 1024;
-  // AT: accumulator in columns [0, 128), three 128-column stage buffers of A at 128, 256, 384
-  static constexpr int kTmemCols = AT ? 512 : (NT < 32 ? 32 : NT);
-  static constexpr int kATmemCol = 128;
+  // AT: NACC interleaved accumulators (K steps alternate between them, so consecutive MMAs
+  // do not wait on each other's result) in the low columns, then 128-column stage buffers of
+  // A up to column 512 (three when the accumulators fit in 128 columns, else two)
+  // CPS = 2 (decode shapes): two CTAs per SM, each with half of the shared memory and of
+  // TMEM; A is handed over in half-stage units (two 64-wide chunks, 64 columns)
+  static constexpr int kAccW = NT < 32 ? 32 : NT;
+  static constexpr int kTmemCols = AT ? (CPS == 2 ? 256 : 512) : (NT < 32 ? 32 : NT);
+  static constexpr int kUA = CPS == 2 ? 2 : 4;            // 64-wide chunks per A unit
+  static constexpr int kUPS = 4 / kUA;                    // A units per stage
+  static constexpr int kATmemCol = AT ? (CPS == 2 ? NACC * kAccW : (NACC * kAccW > 128 ? NACC * kAccW : 128)) : 128;
+  static constexpr int kAbufs = AT ? (kTmemCols - kATmemCol) / (32 * kUA) : NA;
+  static_assert(!AT || kAbufs >= 2, "TMEM: not enough room for two A buffers");
+  static_assert(kAbufs <= 4, "A buffer barriers");
   static_assert(kStages >= 2, "not enough shared memory for two stages");
+  // AT: decoupled rings — raw weight tiles (streamed from HBM, as many in flight as fit) and
+  // activation tiles (L2-resident, a short ring), each with its own producer warp
+  static constexpr int kXStage = kChunks * kBChunk;
+  static constexpr int kXStages = (NT >= 64 || CPS == 2) ? 2 : 3;
+  static constexpr int kBudgetAT = CPS == 2 ? 112 * 1024 - 2048 : kBudget;
+  static constexpr int kWStagesRaw = (kBudgetAT - kXStages * kXStage) / kRawTile;
+  static constexpr int kWStages = kWStagesRaw > 12 ? 12 : kWStagesRaw;
+  static constexpr int kSmemAT = 1024 + kWStages * kRawTile + kXStages * kXStage + 1024;
+  static constexpr int kFirstDq = AT ? 3 : 2;       // first dequant/epilogue warp
+  static constexpr int kSmemLaunch = AT ? kSmemAT : kSmem;
 };
 
 struct Bars {
-  uint64_t full[8];
-  uint64_t empty[8];
+  uint64_t full[12];
+  uint64_t empty[12];
+  uint64_t xfull[4];
+  uint64_t xempty[4];
   uint64_t afull[4];
   uint64_t aempty[4];
   uint64_t done;
@@ -60,6 +82,19 @@ struct Bars {
   int abort;
   int last;
 };
+
+// Sum of the NACC interleaved accumulators (kAccW columns apart) for 16 columns.
+template <int ACCW, int NACC>
+__device__ __forceinline__ void load_acc(uint32_t taddr, float (&v)[16]) {
+  tmem_ld16(taddr, v);
+#pragma unroll
+  for (int j = 1; j < NACC; ++j) {
+    float w[16];
+    tmem_ld16(taddr + ACCW * j, w);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] += w[e];
+  }
+}
 
 template <int DQ>
 __device__ __forceinline__ void named_sync_epi() { asm volatile("bar.sync 1, %0;" ::"n"(32 * DQ) : "memory"); }
@@ -74,11 +109,11 @@ __device__ __forceinline__ uint32_t q4_pair(uint32_t t, __nv_bfloat162 s, __nv_b
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
-template <int NT, int FMT, int NA, int DQ, bool AT>
-__global__ void __launch_bounds__(64 + 32 * DQ, 1)
+template <int NT, int FMT, int NA, int DQ, bool AT, int NACC, int CPS>
+__global__ void __launch_bounds__((AT ? 96 : 64) + 32 * DQ, CPS)
 gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
               GemmArgs a) {
-  using C = Cfg<NT, FMT, NA, AT>;
+  using C = Cfg<NT, FMT, NA, AT, NACC, CPS>;
   static_assert(!AT || FMT == kFmtQ4K, "A-in-TMEM path: Q4_K only");
   // routed-expert GEMMs: token tiles beyond the device row count do nothing (uniform per CTA,
   // before any barrier, TMEM allocation or copy)
@@ -87,7 +122,9 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
   uint8_t* abuf = stages + C::kStages * C::kStageBytes;
-  Bars* bars = reinterpret_cast<Bars*>(abuf + C::kABuf);
+  // AT lays out [weight ring][activation ring] instead; the barriers follow whichever layout
+  Bars* bars = reinterpret_cast<Bars*>(AT ? stages + C::kWStages * kRawTile + C::kXStages * C::kXStage
+                                          : abuf + C::kABuf);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * 128, n0 = blockIdx.y * NT;
@@ -98,11 +135,22 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   const int nk = max(0, min(ksteps, kb0 + kper) - kb0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&bars->full[s], 1);
-      mbar_init(&bars->empty[s], FMT == kFmtQ4K ? (AT ? 8 : DQ) + 1 : 1);
+    if constexpr (AT) {
+      for (int s = 0; s < C::kWStages; ++s) {
+        mbar_init(&bars->full[s], 1);
+        mbar_init(&bars->empty[s], 8);        // the dequant group that read the raw tile
+      }
+      for (int s = 0; s < C::kXStages; ++s) {
+        mbar_init(&bars->xfull[s], 1);
+        mbar_init(&bars->xempty[s], 1);       // MMA commit
+      }
+    } else {
+      for (int s = 0; s < C::kStages; ++s) {
+        mbar_init(&bars->full[s], 1);
+        mbar_init(&bars->empty[s], FMT == kFmtQ4K ? DQ + 1 : 1);
+      }
     }
-    for (int i = 0; i < (AT ? 3 : NA); ++i) {
+    for (int i = 0; i < (AT ? C::kAbufs : NA); ++i) {
       mbar_init(&bars->afull[i], AT ? 8 : DQ);
       mbar_init(&bars->aempty[i], 1);
     }
@@ -124,7 +172,46 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   const int dmode = a.dbg ? (int)a.dbg[255] : 0;
   if (dbg && threadIdx.x == 0) dbg[225] = clock64();
 
-  if (warp == 0) {
+  if (AT && (warp == 0 || warp == 2)) {
+    // ------------------------------------------------------------ producers (AT)
+    // warp 0: raw weight tiles into the deep ring; warp 2: activation tiles into the short ring
+    if (lane == 0) {
+      const bool wprod = warp == 0;
+      const int S = wprod ? C::kWStages : C::kXStages;
+      uint64_t* fullb = wprod ? bars->full : bars->xfull;
+      uint64_t* emptyb = wprod ? bars->empty : bars->xempty;
+      uint8_t* ring = wprod ? stages : stages + C::kWStages * kRawTile;
+      const uint32_t bytes = wprod ? kRawTile : C::kXStage;
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % S;
+        if (i >= S && !mbar_wait(&emptyb[s], ((i / S) - 1) & 1, a.err)) {
+          set_error(a.err, kErrTimeout);
+          bars->abort = 1;
+          break;
+        }
+        if (*(volatile int*)&bars->abort) break;
+        uint8_t* st = ring + s * bytes;
+        if (dbg && wprod && i < 32) dbg[i] = clock64();
+        mbar_expect_tx(&fullb[s], bytes);
+        const int kb = kb0 + i;
+        if (wprod) {
+          // the tile as a.wsplit back-to-back bulk copies (more requests in flight per CTA)
+          const uint8_t* src = a.wq + ((size_t)blockIdx.x * ksteps + kb) * kRawTile;
+          const int np = a.wsplit > 0 ? a.wsplit : 1;
+          const uint32_t piece = kRawTile / np;
+          for (int p = 0; p < np; ++p) bulk_load(st + p * piece, src + p * piece, piece, &fullb[s]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            tma_load_2d(st + c * C::kBChunk, &tm_x, &fullb[s], kb * 256 + 64 * c, n0);
+        }
+        issued = i + 1;
+      }
+      for (int i = max(0, issued - S); i < issued; ++i)
+        mbar_wait(&fullb[i % S], (i / S) & 1, a.err, 50ull * 1000 * 1000);
+    }
+  } else if (!AT && warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint32_t tx = C::kStageBytes;
@@ -164,26 +251,38 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       int g = 0;
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
+        if constexpr (AT) {
+          const int xs = i % C::kXStages;
+          if (!mbar_wait(&bars->xfull[xs], (i / C::kXStages) & 1, a.err)) { ok = false; break; }
+          uint8_t* xst = stages + C::kWStages * kRawTile + xs * C::kXStage;
+          for (int u = 0; u < C::kUPS && ok; ++u) {
+            const int g = i * C::kUPS + u;
+            const int ab = g % C::kAbufs;
+            if (!mbar_wait(&bars->afull[ab], (g / C::kAbufs) & 1, a.err)) { ok = false; break; }
+            tc_fence_after();
+            if (dbg && u == 0 && i < 64) dbg[32 + i] = clock64();
+            const uint32_t ta = tmem + C::kATmemCol + 32 * C::kUA * ab;
+#pragma unroll
+            for (int cu = 0; cu < C::kUA; ++cu) {
+              const int c = u * C::kUA + cu;
+              const uint64_t bd = sw128_desc(xst + c * C::kBChunk);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {  // K16 steps: 8 TMEM columns of A, +32 B of B
+                const int j = (4 * c + k) % NACC;       // interleaved accumulators
+                const uint32_t acc = (i == 0 && 4 * c + k < NACC) ? 0u : 1u;
+                if (dmode != 2)
+                  mma_bf16_ts(tmem + C::kAccW * j, ta + 32 * cu + 8 * k, bd + 2 * k, idesc, acc);
+              }
+            }
+            mma_commit(&bars->aempty[ab]);
+          }
+          if (!ok) break;
+          mma_commit(&bars->xempty[xs]);
+          continue;
+        }
         const int s = i % C::kStages;
         if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1, a.err)) { ok = false; break; }
         uint8_t* st = stages + s * C::kStageBytes;
-        if constexpr (AT) {
-          const int ab = i % 3;
-          if (!mbar_wait(&bars->afull[ab], (i / 3) & 1, a.err)) { ok = false; break; }
-          tc_fence_after();
-          if (dbg && i < 64) dbg[32 + i] = clock64();
-          const uint32_t ta = tmem + C::kATmemCol + 128 * ab;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint64_t bd = sw128_desc(st + kRawTile + c * C::kBChunk);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)  // K16 steps: 8 TMEM columns of A, +32 B of B
-              if (dmode != 2) mma_bf16_ts(tmem, ta + 32 * c + 8 * k, bd + 2 * k, idesc, (i | c | k) != 0 ? 1u : 0u);
-          }
-          mma_commit(&bars->aempty[ab]);
-          mma_commit(&bars->empty[s]);
-          continue;
-        }
         for (int c = 0; c < C::kChunks; ++c, ++g) {
           const uint8_t* A;
           if (FMT == kFmtQ4K) {
@@ -231,24 +330,27 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       // latency (shared-memory loads, TMEM store completion) overlaps the other's work;
       // three TMEM stage buffers let both groups run ahead of the MMA.
       constexpr int G = DQ / 8;
-      const int grp = (warp - 2) >> 3;
+      const int grp = (warp - C::kFirstDq) >> 3;
       const int r = 32 * (warp & 3) + lane;
-      const int h = ((warp - 2) >> 2) & 1;
+      const int h = ((warp - C::kFirstDq) >> 2) & 1;
       const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
       bool ok = true;
-      for (int i = grp; i < nk; i += G) {
-        const int s = i % C::kStages;
-        const int ab = i % 3;
-        if (i >= 3 && !mbar_wait(&bars->aempty[ab], ((i / 3) - 1) & 1, a.err)) { ok = false; break; }
-        if (!mbar_wait(&bars->full[s], (i / C::kStages) & 1, a.err)) { ok = false; break; }
-        if (dbg && threadIdx.x == 64 && i < 64) dbg[96 + i] = clock64();
-        const uint8_t* rb = stages + s * C::kStageBytes + r * kRawRowBytes;
+      for (int i = grp; i < nk && ok; i += G) {
+        const int s = i % C::kWStages;
+        if (!mbar_wait(&bars->full[s], (i / C::kWStages) & 1, a.err)) { ok = false; break; }
+        if (dbg && threadIdx.x == 32 * C::kFirstDq && i < 64) dbg[96 + i] = clock64();
+        const uint8_t* rb = stages + s * kRawTile + r * kRawRowBytes;
         const uint32_t hdr = *reinterpret_cast<const uint32_t*>(rb);
         const float d = __half2float(__ushort_as_half((unsigned short)(hdr & 0xFFFF)));
         const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr >> 16)));
-        const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + C::kATmemCol + 128 * ab + 16 * h;
+        const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + C::kATmemCol + 16 * h;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
+          const int g = i * C::kUPS + c / C::kUA;     // A unit of this chunk
+          const int ab = g % C::kAbufs;
+          if (c % C::kUA == 0 && g >= C::kAbufs &&
+              !mbar_wait(&bars->aempty[ab], ((g / C::kAbufs) - 1) & 1, a.err)) { ok = false; break; }
+          const uint32_t ta = tlane + 32 * C::kUA * ab - 32 * (c / C::kUA) * C::kUA;
           int sc, mn;
           q4k_scale_min(rb + 4, 2 * c + h, sc, mn);
           const __nv_bfloat162 sv = __float2bfloat162_rn(d * (float)sc);
@@ -269,15 +371,17 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
             }
           }
           if (dmode != 1) tmem_st16(ta + 32 * c, o);
+          if (c % C::kUA == C::kUA - 1) {           // unit complete: hand it to the MMA issuer
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->afull[ab]);
+          }
         }
-        tmem_wait_st();
-        tc_fence_before();
+        if (!ok) break;
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&bars->afull[ab]);
-          mbar_arrive(&bars->empty[s]);
-        }
-        if (dbg && threadIdx.x == 64 && i < 64) dbg[160 + i] = clock64();
+        if (lane == 0) mbar_arrive(&bars->empty[s]);   // raw tile fully read
+        if (dbg && threadIdx.x == 32 * C::kFirstDq && i < 64) dbg[160 + i] = clock64();
       }
       if (!ok) {
         set_error(a.err, kErrTimeout);
@@ -347,11 +451,11 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
     }
     // ------------------------------------------------------------ epilogue
     const bool done_ok = mbar_wait(&bars->done, 0, a.err);
-    if (dbg && threadIdx.x == 64) dbg[224] = clock64();
+    if (dbg && threadIdx.x == 32 * C::kFirstDq) dbg[224] = clock64();
     tc_fence_after();
     const int q = warp & 3;          // TMEM lane quarter this warp may access
     const int m = 32 * q + lane;     // weight row within the tile
-    const int jh = (warp - 2) >> 2;  // the DQ/4 warps of a quarter split the column groups
+    const int jh = (warp - C::kFirstDq) >> 2;  // the DQ/4 warps of a quarter split the column groups
     constexpr int kJW = DQ / 4;
     const int mg = m0 + m;
     // warp-uniform: every tcgen05.ld below must be executed by all 32 lanes or none
@@ -364,20 +468,20 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       for (int j = 0; j < NT / 16; ++j) {
         if ((j % kJW) != jh) continue;
         float v[16];
-        if (valid) tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 16 * j, v);
+        if (valid) load_acc<C::kAccW, AT ? NACC : 1>(tmem + ((uint32_t)(32 * q) << 16) + 16 * j, v);
 #pragma unroll
         for (int e = 0; e < 16; ++e) part[(16 * j + e) * 128 + m] = valid ? v[e] : 0.f;
       }
       __threadfence();
       named_sync_epi<DQ>();
-      if (threadIdx.x == 64) {
+      if (threadIdx.x == 32 * C::kFirstDq) {
         const int old = atomicAdd(&a.counters[tile], 1);
         bars->last = (old == splits - 1);
       }
       named_sync_epi<DQ>();
       if (!bars->last) goto finish;
       __threadfence();
-      if (threadIdx.x == 64) a.counters[tile] = 0;  // self-cleaning for the next call
+      if (threadIdx.x == 32 * C::kFirstDq) a.counters[tile] = 0;  // self-cleaning for the next call
     }
     {  // all lanes stay in: tcgen05.ld is warp-collective; rows >= N are masked at the store
 #pragma unroll 1
@@ -393,7 +497,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
             for (int e = 0; e < 16; ++e) v[e] += __ldcg(part + (16 * j + e) * 128 + m);
           }
         } else if (valid) {
-          tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + 16 * j, v);
+          load_acc<C::kAccW, AT ? NACC : 1>(tmem + ((uint32_t)(32 * q) << 16) + 16 * j, v);
         } else {
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = 0.f;
@@ -446,10 +550,10 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NT, int FMT, int NA, int DQ, bool AT = false>
+template <int NT, int FMT, int NA, int DQ, bool AT = false, int NACC = 1, int CPS = 1>
 const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
                       dim3 grid, cudaStream_t st) {
-  using C = Cfg<NT, FMT, NA, AT>;
+  using C = Cfg<NT, FMT, NA, AT, NACC, CPS>;
   CUtensorMap tw, tx;
   bool ok;
   GemmArgs b = a;
@@ -466,12 +570,12 @@ const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, con
     return "cuTensorMapEncodeTiled failed for the activation operand";
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(gemm_q_kernel<NT, FMT, NA, DQ, AT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+    if (cudaFuncSetAttribute(gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemLaunch) !=
         cudaSuccess)
       return "cudaFuncSetAttribute(max dynamic smem) failed";
     attr = true;
   }
-  gemm_q_kernel<NT, FMT, NA, DQ, AT><<<grid, 64 + 32 * DQ, C::kSmem, st>>>(tw, tx, b);
+  gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS><<<grid, (AT ? 96 : 64) + 32 * DQ, C::kSmemLaunch, st>>>(tw, tx, b);
   return nullptr;
 }
 
@@ -494,9 +598,16 @@ const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, cons
   if constexpr (FMT == kFmtQ4K) {
     const int p = a_path();
     if (p == 0) {
+      constexpr int NACC = NT <= 64 ? 4 : 2;
       const char* e = getenv("AIR_GEMM_DQ");
-      if (e && atoi(e) == 16) return launch_na<NT, FMT, NA, 16, true>(a, w, w_row_bytes, x, ldx, grid, st);
-      return launch_na<NT, FMT, NA, 8, true>(a, w, w_row_bytes, x, ldx, grid, st);
+      const char* n = getenv("AIR_GEMM_NACC");
+      if (n && atoi(n) == 1) return launch_na<NT, FMT, NA, 8, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
+      if constexpr (NT <= 64) {
+        const char* c2 = getenv("AIR_GEMM_CPS");
+        if (!(c2 && atoi(c2) == 1)) return launch_na<NT, FMT, NA, 8, true, 1, 2>(a, w, w_row_bytes, x, ldx, grid, st);
+      }
+      if (e && atoi(e) == 16) return launch_na<NT, FMT, NA, 16, true, NACC>(a, w, w_row_bytes, x, ldx, grid, st);
+      return launch_na<NT, FMT, NA, 8, true, NACC>(a, w, w_row_bytes, x, ldx, grid, st);
     }
     if (p == 2) return launch_na<NT, FMT, NA, 16>(a, w, w_row_bytes, x, ldx, grid, st);
   }
@@ -516,11 +627,19 @@ int gemm_q_splits(int N, int K, int T, int fmt) {
   const int nt = gemm_q_token_tile(T);
   const int tiles = ((N + 127) / 128) * ((T + nt - 1) / nt);
   const int ksteps = fmt == kFmtQ4K ? K / 256 : K / 64;
-  // as many K splits as fit in ONE wave of 148 CTAs (a partial second wave costs a whole
-  // wave of time); more than one wave of tiles already fills the machine
-  int s = 148 / tiles;
+  // as many K splits as fit in ONE wave (a partial second wave costs a whole wave of time);
+  // the decode variant runs two CTAs per SM, so its wave is 2 x 148 CTAs. More than one wave
+  // of tiles already fills the machine.
+  const char* w = getenv("AIR_GEMM_WAVE");
+  const char* c2 = getenv("AIR_GEMM_CPS");
+  const bool cps2 = fmt == kFmtQ4K && nt <= 64 && a_path() == 0 && !(c2 && atoi(c2) == 1);
+  const int wave = w ? atoi(w) : 148;   // 2 x 148 for the two-CTA variant measured slower on split shapes
+  (void)cps2;
+  int s = wave / tiles;
   s = s < 1 ? 1 : s;
-  const int max_s = ksteps / 2 > 0 ? ksteps / 2 : 1;  // at least two K-steps per split
+  const char* mk = getenv("AIR_GEMM_MINK");
+  const int mink = mk ? atoi(mk) : 2;                     // K-steps per split at least
+  const int max_s = ksteps / mink > 0 ? ksteps / mink : 1;
   return s > max_s ? max_s : s;
 }
 
@@ -535,8 +654,21 @@ size_t gemm_q_counters(int N, int T) {
   return (size_t)((N + 127) / 128) * ((T + nt - 1) / nt);
 }
 
+// Pieces per raw weight tile copy (AIR_GEMM_WSPLIT: 1, 2, 4, 8, 9 or 18; default 1).
+static int wsplit() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("AIR_GEMM_WSPLIT");
+    v = e ? atoi(e) : 1;
+    if (v != 2 && v != 4 && v != 8 && v != 9 && v != 18) v = 1;
+  }
+  return v;
+}
+
 const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
-                          const GemmArgs& a, cudaStream_t st) {
+                          const GemmArgs& a_in, cudaStream_t st) {
+  GemmArgs a = a_in;
+  a.wsplit = wsplit();
   if (a.K % (fmt == kFmtQ4K ? 256 : 64)) return "gemm_q: K must be a multiple of 256 (Q4_K) or 64 (bf16)";
   if (fmt != kFmtQ4K && fmt != kFmtBF16) return "gemm_q: weight format not supported by the tensor-core path";
   if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16 || w_row_bytes % 16 ||

@@ -19,6 +19,7 @@ struct GemmArgs {
   int* err;
   long long* dbg;
   const uint8_t* wq;    // weight base (filled by launch_gemm_q)
+  int wsplit;           // raw weight tile copy split into this many bulk copies (filled in)
   const int* row_count; // optional device count of valid token rows: token tiles at or past it
                         // exit at once (routed-expert GEMMs launched for a capacity)
        // optional per-phase clock64 stamps of CTA (0,0,0) (profiling aid)

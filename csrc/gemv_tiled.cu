@@ -20,6 +20,7 @@
 #include "kernels.h"
 #include "gemv_tiled.h"
 #include "comm.cuh"
+#include <stdlib.h>
 
 namespace air {
 
@@ -66,8 +67,12 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
     issued = i + 1;
     mbar_expect_tx(&bar->full[s], W * kSlab);
     const size_t off = ((size_t)tile * nsb + sb0 + i) * kSlab;
-    bulk_load(slabs + (size_t)(s * W) * kSlab, w1 + off, kSlab, &bar->full[s]);
-    if (DUAL) bulk_load(slabs + (size_t)(s * W + 1) * kSlab, w2 + off, kSlab, &bar->full[s]);
+    const int np = sc.wsplit > 0 ? sc.wsplit : 1;     // split copies: more requests in flight
+    const uint32_t piece = kSlab / np;
+    for (int p = 0; p < np; ++p) {
+      bulk_load(slabs + (size_t)(s * W) * kSlab + p * piece, w1 + off + p * piece, piece, &bar->full[s]);
+      if (DUAL) bulk_load(slabs + (size_t)(s * W + 1) * kSlab + p * piece, w2 + off + p * piece, piece, &bar->full[s]);
+    }
   };
   if (t == 0)
     for (int i = 0; i < min(S, nk); ++i) issue(i);
@@ -288,9 +293,21 @@ size_t gemv_tiled_workspace_floats(int N, int splits, int mode) {
 
 size_t gemv_tiled_counters(int N) { return (N + kRows - 1) / kRows; }
 
+static int gemv_wsplit() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("AIR_GEMV_WSPLIT");
+    v = e ? atoi(e) : 1;
+    if (v != 2 && v != 4 && v != 8 && v != 9 && v != 18) v = 1;
+  }
+  return v;
+}
+
 const char* launch_gemv_tiled(const GemvWeight& w, int N, int K, int B, const int8_t* xq,
-                              const float2* xds, const GemvEpiParams& ep, const GemvTiledScratch& sc,
+                              const float2* xds, const GemvEpiParams& ep, const GemvTiledScratch& sc_in,
                               int splits, cudaStream_t st) {
+  GemvTiledScratch sc = sc_in;
+  if (sc.wsplit <= 0) sc.wsplit = gemv_wsplit();
   if (w.fmt != kFmtQ4K) return "gemv_tiled: Q4_K only";
   if (K % 256) return "gemv_tiled: K must be a multiple of 256";
   if (ep.mode == kEpiQKVRope && ep.head_dim != kRows) return "gemv_tiled: QKV epilogue needs head_dim 128";

@@ -8,6 +8,7 @@ namespace air {
 struct GemvTiledScratch {
   float* ws;        // split-K partials: gemv_tiled_workspace_floats() floats
   int* counters;    // gemv_tiled_counters() ints, zero before first use (self-resetting)
+  int wsplit = 0;   // bulk copies per 18 KB slab (0: launch_gemv_tiled picks)
 };
 
 int gemv_tiled_splits(int N, int K, int mode);
