@@ -38,6 +38,10 @@ def _common(p: argparse.ArgumentParser, serve: bool = False):
     p.add_argument("--ternary", "--bitnet", dest="ternary", action="store_true")
     p.add_argument("--ternary-cdsc", action="store_true")
     p.add_argument("--device", default=None, help="cuda | cpu (default: cuda when available)")
+    p.add_argument("--expert-slots", type=int, default=None,
+                   help="MoE: keep experts in host memory with this many resident in VRAM")
+    p.add_argument("--trace", default=None, metavar="FILE",
+                   help="Record NVTX ranges and host spans; write a Chrome trace to FILE on exit")
 
 
 def build_parser() -> argparse.ArgumentParser:
@@ -112,6 +116,7 @@ def _engine(args, max_batch=64):
     path = resolve(args.model)
     return engine_from_gguf(path, device=args.device, max_batch=max_batch, max_model_len=args.ctx_size, tp=tp,
                             resident=not getattr(args, "stream_weights", False),
+                            expert_slots=getattr(args, "expert_slots", None),
                             **({"prefix_cache": True} if getattr(args, "enable_prefix_caching", False) else {}))
 
 
@@ -275,6 +280,17 @@ def main(argv: list[str] | None = None) -> int:
         build_parser().print_help()
         return 1
     _maybe_relaunch_tp(args, argv)
+    if getattr(args, "trace", None):
+        from .utils import trace
+        trace.enable(True)
+        try:
+            return _dispatch(args)
+        finally:
+            trace.dump_chrome(args.trace)
+    return _dispatch(args)
+
+
+def _dispatch(args) -> int:
     if args.cmd == "pull":
         from .hub import pull
         print(pull(args.repo_id, args.filename, args.alias, args.sha256))

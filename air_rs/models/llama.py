@@ -81,12 +81,14 @@ class LlamaWeights:
     """Device-resident weights, built from (name, raw, qtype, shape) records."""
 
     def __init__(self, cfg: ModelConfig, records: Iterable, device, tp_rank: int = 0, tp_size: int = 1,
-                 layer_device=None, layer_range: tuple[int, int] | None = None):
+                 layer_device=None, layer_range: tuple[int, int] | None = None, expert_device=None):
         """``layer_device`` (default: ``device``) holds the per-layer weights; ``"cpu"`` keeps
-        them in pinned host memory for layer streaming (S.L.I.P.)."""
+        them in pinned host memory for layer streaming (S.L.I.P.). ``expert_device="cpu"`` keeps
+        only the MoE experts in pinned host memory (served through an expert cache)."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.layer_device = torch.device(layer_device) if layer_device is not None else self.device
+        self.expert_device = torch.device(expert_device) if expert_device is not None else None
         # pipeline stage: only layers [l0, l1) are loaded (indexed from 0 here)
         self.layer_range = tuple(layer_range) if layer_range is not None else (0, cfg.n_layers)
         self.tp_rank, self.tp_size = tp_rank, tp_size
@@ -203,11 +205,15 @@ class LlamaWeights:
             # expert parallelism: under TP the experts are spread over the ranks (expert e on
             # rank e % tp); attention stays tensor parallel
             lw.expert_ids = [e for e in range(E) if e % tp == rk]
+            xdev = self.expert_device or self.device
+            pin = xdev.type == "cpu" and self.device.type == "cuda"
             for e in lw.expert_ids:
-                ge = ops.QWeight.from_raw(gr[e], gq, F, cfg.hidden_dim, self.device)
-                ue = ops.QWeight.from_raw(ur[e], uq, F, cfg.hidden_dim, self.device)
-                lw.experts_gu.append(ops.QWeight.cat([ge, ue]))
-                lw.experts_down.append(ops.QWeight.from_raw(dr[e], dq, cfg.hidden_dim, F, self.device))
+                ge = ops.QWeight.from_raw(gr[e], gq, F, cfg.hidden_dim, xdev)
+                ue = ops.QWeight.from_raw(ur[e], uq, F, cfg.hidden_dim, xdev)
+                gu = ops.QWeight.cat([ge, ue])
+                dn = ops.QWeight.from_raw(dr[e], dq, cfg.hidden_dim, F, xdev)
+                lw.experts_gu.append(gu.to_device(None, pin=True) if pin else gu)
+                lw.experts_down.append(dn.to_device(None, pin=True) if pin else dn)
         else:
             gate = self._lin_rows(*g["ffn_gate.weight"], rk * Fl, (rk + 1) * Fl)
             up = self._lin_rows(*g["ffn_up.weight"], rk * Fl, (rk + 1) * Fl)
@@ -221,7 +227,10 @@ class LlamaWeights:
     def resident_nbytes(self) -> int:
         """Bytes on the compute device (layers streamed from host memory excluded)."""
         if self.layer_device == self.device:
-            return self.nbytes()
+            n = self.nbytes()
+            if self.expert_device is not None and self.expert_device != self.device:
+                n -= sum(e.nbytes for l in self.layers for e in l.experts_gu + l.experts_down)
+            return n
         return self.embd.nbytes + self.lm_head.nbytes
 
     def nbytes(self) -> int:

@@ -41,6 +41,15 @@ def _ids(lw):
     return lw.expert_ids or list(range(len(lw.experts_gu)))
 
 
+def _experts(rn, lw, cw, T):
+    """(gate|up, down, global id) of this rank's experts: all of them, or — with host-resident
+    experts behind an expert cache — only those some token picked, made resident on demand."""
+    cache = getattr(rn, "expert_cache", None)
+    if cache is None:
+        return zip(lw.experts_gu, lw.experts_down, _ids(lw))
+    return cache.experts_for(lw, (cw[:T] > 0).any(0).cpu())
+
+
 def _finish(rn, T, x, partial, peer):
     """EP combine: partial expert outputs of this rank -> every rank's residual stream."""
     if rn.tp_size == 1:
@@ -66,7 +75,7 @@ def moe_ffn_decode(rn, lw, B, x, xq, xds, peer=None):
     if ep:
         acc = _ensure(rn, "moe_part", (rn.max_batch, rn.H), torch.float32)
         acc[:B].zero_()
-    for gu, dn, e in zip(lw.experts_gu, lw.experts_down, _ids(lw)):
+    for gu, dn, e in _experts(rn, lw, cw, B):
         ops.gemv(gu.part(0), xq, xds, B, ops.EPI_SWIGLU, w2=gu.part(1), out_f32=rn.h[:B], ld_out=rn.Fp)
         ops.rmsnorm_quant(rn.h[:B], None, 0.0, hq[:B], hds[:B])
         ops.gemv(dn, hq[:B], hds[:B], B, ops.EPI_STORE, out_f32=rn.y[:B])
@@ -86,7 +95,7 @@ def _ffn_tokens(rn, lw, T, x, xn, bufs, peer=None):
     acc = bufs["part"] if ep else x
     if ep:
         acc[:T].zero_()
-    for j, (gu, dn, e) in enumerate(zip(lw.experts_gu, lw.experts_down, _ids(lw))):
+    for j, (gu, dn, e) in enumerate(_experts(rn, lw, cw, T)):
         c = cnt[j:j + 1]
         ext.moe_select(cw[:T], e, T, idx, wts, c)
         ext.moe_gather(xn[:T], idx, c, T, xg)

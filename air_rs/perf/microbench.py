@@ -1,6 +1,11 @@
 """Per-kernel microbenchmarks at Llama-3-8B decode / prefill shapes.
 
-``python -m air_rs.perf.microbench [--op gemv|gemm|attn|norm|all] [--name qkv|o|gateup|down|lm]
+``--op graph`` measures CUDA-graph launch overhead: one decode step of a random-init model
+(``--preset``, default llama3-8b) at batch B run eagerly (every kernel launched from Python)
+and as a replayed graph, device time per step from CUDA events plus host time per step, and
+the number of kernels in the step.
+
+``python -m air_rs.perf.microbench [--op gemv|gemm|attn|norm|graph|all] [--name qkv|o|gateup|down|lm]
 [--batch B] [--iters N]`` prints one line per case: device time (CUDA events around a CUDA
 graph of N back-to-back launches, after warm-up), achieved bytes/s or FLOP/s, and the
 fraction of the measured HBM copy bandwidth / cuBLAS bf16 rate (``MEASURED_PEAKS.json`` at
@@ -124,9 +129,45 @@ def bench_attn(B: int, ctx: int, iters: int, dev):
     return us, B * ctx * 2 * nkv * d * 2, 4.0 * B * nh * ctx * d
 
 
+def bench_graph(preset: str, B: int, iters: int, dev) -> dict:
+    """Eager vs graph-replayed decode step of a random-init model at batch ``B``."""
+    import time
+    from ..runtime.builder import random_engine
+    eng = random_engine(preset, device=dev, max_batch=max(B, 1), max_model_len=1024, num_blocks=B * 64 + 16)
+    rn = eng.runner
+    prompts = [[(7 * i + j) % 200 + 3 for j in range(32)] for i in range(B)]
+    from ..runtime.engine import SamplingParams
+    for p in prompts:
+        eng.add_request(p, SamplingParams(max_tokens=10 ** 6, temperature=0.0, ignore_eos=True))
+    eng.step()                       # prefill + first decode step
+    bucket = eng._bucket(B)
+    out = {"preset": preset, "B": B, "bucket": bucket}
+    for mode in ("eager", "graph"):
+        use_graph = mode == "graph"
+        for _ in range(3):
+            rn.decode(bucket, use_graph=use_graph)
+        torch.cuda.synchronize()
+        c0 = ops.launch_count()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        a.record()
+        for _ in range(iters):
+            rn.decode(bucket, use_graph=use_graph)
+        b.record()
+        host = (time.perf_counter() - t0) / iters * 1e3
+        torch.cuda.synchronize()
+        out[mode] = {"device_ms": a.elapsed_time(b) / iters, "host_ms": host,
+                     "kernels": (ops.launch_count() - c0) // iters}
+    out["graph_speedup"] = out["eager"]["device_ms"] / out["graph"]["device_ms"]
+    for r in list(eng.running):
+        eng.abort(r.rid)
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--op", default="all", choices=["all", "gemv", "gemm", "attn", "norm"])
+    ap.add_argument("--op", default="all", choices=["all", "gemv", "gemm", "attn", "norm", "graph"])
+    ap.add_argument("--preset", default="llama3-8b")
     ap.add_argument("--name", default=None, choices=list(SHAPES))
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=640)
@@ -162,6 +203,14 @@ def main(argv=None):
             ds = torch.empty(B, K // 32, 2, device=dev)
             us = ev_time(lambda: ops.rmsnorm_quant(x, w, 1e-5, q, ds), a.iters)
             line("norm", f"rmsnorm_quant K={K} B={B}", us, B * K * 4 + B * K + B * K // 8, 0.0)
+
+    if a.op == "graph":
+        for B in ([a.batch] if a.batch else [1, 64]):
+            r = bench_graph(a.preset, B, a.iters, dev)
+            e, g = r["eager"], r["graph"]
+            print(f"graph {a.preset} decode B={B}: eager {e['device_ms']:.3f} ms/step (host {e['host_ms']:.3f}), "
+                  f"graph {g['device_ms']:.3f} ms/step (host {g['host_ms']:.3f}), {g['kernels']} kernels/step, "
+                  f"speedup {r['graph_speedup']:.2f}x", flush=True)
 
 
 if __name__ == "__main__":

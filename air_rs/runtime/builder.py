@@ -11,7 +11,7 @@ from ..tokenizer import Tokenizer
 from .engine import Engine
 from .runner import ModelRunner
 
-VRAM_CAP_FRACTION = 0.80  # reference src/vram_guard.rs:30
+from . import vram_guard
 
 
 class VramBudgetError(RuntimeError):
@@ -35,7 +35,7 @@ def plan_kv_blocks(cfg: ModelConfig, weights_bytes: int, *, block_size: int, dev
     if torch.device(device).type != "cuda":
         return want
     free, total = torch.cuda.mem_get_info(torch.device(device))
-    cap = int(total * (kv_fraction or VRAM_CAP_FRACTION))
+    cap = int(total * (kv_fraction or vram_guard.default_fraction()))
     used = total - free
     room = cap - used
     if room <= per * 64:
@@ -47,14 +47,20 @@ def plan_kv_blocks(cfg: ModelConfig, weights_bytes: int, *, block_size: int, dev
 def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_model_len=4096,
                  block_size=16, num_blocks=None, tp=None, seed=0, max_seqs=None,
                  resident: bool = True, stream_slots: int = 2, kv_alloc=None,
-                 layer_range: tuple[int, int] | None = None) -> ModelRunner:
+                 layer_range: tuple[int, int] | None = None, expert_slots: int | None = None) -> ModelRunner:
     """``resident=False``: per-layer weights stay in pinned host memory and are streamed
-    through ``stream_slots`` device slots each forward (S.L.I.P. streaming mode)."""
+    through ``stream_slots`` device slots each forward (S.L.I.P. streaming mode).
+    ``expert_slots``: MoE experts stay in pinned host memory and at most this many are
+    resident at once (expert VRAM scheduler)."""
     tp_size = tp.world_size if tp is not None else 1
     tp_rank = tp.rank if tp is not None else 0
     w = LlamaWeights(cfg, records, device, tp_rank=tp_rank, tp_size=tp_size,
-                     layer_device=None if resident else "cpu", layer_range=layer_range)
+                     layer_device=None if resident else "cpu", layer_range=layer_range,
+                     expert_device="cpu" if expert_slots else None)
     streamed = 0 if resident else stream_slots * max(1, w.nbytes() - w.resident_nbytes()) // cfg.n_layers
+    if expert_slots:
+        l0 = w.layers[0]
+        streamed += expert_slots * (l0.experts_gu[0].nbytes + l0.experts_down[0].nbytes)
     nb = plan_kv_blocks(cfg, w.resident_nbytes() + streamed, block_size=block_size, device=device,
                         max_batch=max_batch, max_model_len=max_model_len, tp_size=tp_size, num_blocks=num_blocks)
     rn = ModelRunner(cfg, w, num_blocks=nb, block_size=block_size, max_batch=max_batch,
@@ -62,23 +68,26 @@ def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_
                      max_seqs=max_seqs or max(2 * max_batch + 1, 64), kv_alloc=kv_alloc)
     if not resident:
         rn.enable_streaming(stream_slots)
+    if expert_slots:
+        rn.enable_expert_cache(expert_slots)
     return rn
 
 
 def random_engine(preset: str | ModelConfig = "tiny", qtype: GGMLType = GGMLType.Q4_K, *, seed=0,
                   device="cuda", max_batch=64, max_model_len=4096, tp=None, num_blocks=None,
-                  **kw) -> Engine:
+                  expert_slots: int | None = None, **kw) -> Engine:
     """Random-init model of a named architecture built directly in HBM (no file)."""
     cfg = PRESETS[preset]() if isinstance(preset, str) else preset
     recs = random_tensors(cfg, qtype, seed=seed, device=device)
     runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=max_model_len,
-                          tp=tp, num_blocks=num_blocks, seed=seed)
+                          tp=tp, num_blocks=num_blocks, seed=seed, expert_slots=expert_slots)
     tok = Tokenizer.byte_vocab(cfg.vocab_size, cfg.bos_token_id, cfg.eos_token_id)
     return Engine(cfg, runner, tok, max_batch=max_batch, **kw)
 
 
 def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None, tp=None,
-                     num_blocks=None, seed=0, resident: bool = True, **kw) -> Engine:
+                     num_blocks=None, seed=0, resident: bool = True, expert_slots: int | None = None,
+                     **kw) -> Engine:
     g = read_gguf(path)
     cfg = ModelConfig.from_gguf_metadata(g.metadata)
     tok = Tokenizer.from_gguf_metadata(g.metadata)
@@ -90,5 +99,5 @@ def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None
     mml = max_model_len or min(cfg.context_length, 8192)
     recs = ((n, g.raw(n), t.qtype, t.torch_shape) for n, t in g.tensors.items())
     runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=mml, tp=tp,
-                          num_blocks=num_blocks, seed=seed, resident=resident)
+                          num_blocks=num_blocks, seed=seed, resident=resident, expert_slots=expert_slots)
     return Engine(cfg, runner, tok, max_batch=max_batch, **kw)

@@ -26,6 +26,7 @@ import torch
 
 from ..models.config import ModelConfig
 from ..metrics import InferenceMetrics
+from ..utils import trace
 
 
 @dataclass
@@ -78,8 +79,10 @@ class Engine:
     def __init__(self, cfg: ModelConfig, runner=None, tokenizer=None, *, oracle=None,
                  max_batch: int = 64, prefill_chunk: int = 512, max_prefill_tokens: int = 8192,
                  add_bos: bool = True, eos_id: int | None = None, prefix_cache: bool = False,
-                 prefix_cache_blocks: int | None = None, kv_swap: bool = True):
+                 prefix_cache_blocks: int | None = None, kv_swap: bool = True,
+                 cuda_graph_batch_sizes: tuple[int, ...] = BUCKETS):
         self.cfg = cfg
+        self.buckets = tuple(sorted(cuda_graph_batch_sizes))
         self.runner = runner
         self.oracle = oracle
         self.tokenizer = tokenizer
@@ -344,7 +347,7 @@ class Engine:
         rn.check_errors()
 
     def _bucket(self, n: int) -> int:
-        for b in BUCKETS:
+        for b in self.buckets:
             if b >= n and b <= self.runner.max_batch:
                 return b
         return self.runner.max_batch
@@ -473,22 +476,27 @@ class Engine:
         """One scheduler iteration; returns the (rid, token) pairs produced."""
         produced: list[tuple[int, int]] = []
         if self.runner is None:
-            return self._step_cpu()
-        admitted = self._admit()
+            with trace.span("cpu_step"):
+                return self._step_cpu()
+        with trace.span("admit"):
+            admitted = self._admit()
         if admitted:
             before = {r.rid: len(r.output_ids) for r in admitted}
-            self._prefill(admitted)
+            with trace.span("prefill"):
+                self._prefill(admitted)
             produced += [(r.rid, r.output_ids[-1]) for r in admitted if len(r.output_ids) > before[r.rid]]
         batch = [r for r in self.running if r.output_ids and not r.finished]
         if not batch:
             return produced
         batch = self._make_room(batch)
-        B, p, ev = self._launch_decode(batch)
-        ev.synchronize()
-        toks = p["tok"][:len(batch)].tolist()
-        for r, t in zip(batch, toks):
-            self._emit(r, t)
-            produced.append((r.rid, t))
+        with trace.span("decode"):
+            B, p, ev = self._launch_decode(batch)
+            ev.synchronize()
+        with trace.span("emit"):
+            toks = p["tok"][:len(batch)].tolist()
+            for r, t in zip(batch, toks):
+                self._emit(r, t)
+                produced.append((r.rid, t))
         self.step_count += 1
         return produced
 
@@ -615,6 +623,35 @@ class Engine:
         if g is None:
             g = self._gen = torch.Generator().manual_seed(0)
         return g
+
+    # ------------------------------------------------------------------ KV session snapshots
+    def snapshot_request(self, rid: int, path) -> "object":
+        """Write a running request's KV (prompt + tokens generated so far, minus the last
+        sampled one, whose KV is written by the next step) to ``path``."""
+        from ..kv import snapshot
+        r = next((x for x in self.running if x.rid == rid), None)
+        if r is None or r.seq < 0 or self.runner is None:
+            raise KeyError(f"request {rid} is not running on the device")
+        if self.seqs.is_swapped(r.seq):
+            raise RuntimeError(f"request {rid} is swapped out")
+        toks = (r.prompt_ids + r.output_ids)[: self.seqs.num_tokens(r.seq)]
+        torch.cuda.current_stream(self.runner.device).synchronize()
+        return snapshot.save(path, self.runner.kv, list(self.seqs.block_table(r.seq)), toks)
+
+    def restore_snapshot(self, path) -> int:
+        """Load a snapshot's whole blocks into the prefix cache; a later request whose prompt
+        starts with those tokens reuses them instead of prefilling. Returns the tokens cached."""
+        from ..kv import snapshot
+        if self.runner is None or self.prefix_cache is None:
+            raise RuntimeError("restoring a KV snapshot needs a device engine with prefix caching")
+        seq, toks, blocks = snapshot.load_into(path, self.runner.kv, self.seqs)
+        try:
+            bs = self.runner.block_size
+            n_full = len(toks) // bs
+            self.prefix_cache.insert(toks[: n_full * bs], blocks[:n_full])
+        finally:
+            self.seqs.free_sequence(seq)
+        return n_full * self.runner.block_size
 
     # ------------------------------------------------------------------ embeddings
     def embed(self, ids: list[int]) -> list[float]:

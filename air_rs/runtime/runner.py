@@ -16,6 +16,7 @@ import torch
 from .. import ops
 from ..models.config import ModelConfig
 from ..models.llama import LlamaWeights
+from ..utils import trace
 
 GEMV_MAX_B = 8
 
@@ -119,6 +120,7 @@ class ModelRunner:
         self.graph_launches: dict[int, int] = {}
         self._prefill_ws: dict[str, torch.Tensor] = {}
         self.streamer = None
+        self.expert_cache = None
         self.max_prefill_tokens = max_prefill_tokens
         self._wscratch = None
 
@@ -132,6 +134,15 @@ class ModelRunner:
     def _layer_done(self, li: int):
         if self.streamer is not None:
             self.streamer.release(li)
+
+    def enable_expert_cache(self, capacity: int):
+        """Serve host-resident MoE experts through ``capacity`` device slots (LRU)."""
+        from .expert_cache import DeviceExpertCache
+        if not any(lw.experts_gu for lw in self.w.layers):
+            raise ValueError("expert cache needs a MoE model")
+        self.expert_cache = DeviceExpertCache(self.w.layers, capacity, self.device)
+        self.graphs.clear()
+        return self.expert_cache
 
     def enable_streaming(self, n_slots: int = 2):
         """Stream host-resident layers through ``n_slots`` device slots (S.L.I.P.)."""
@@ -315,7 +326,7 @@ class ModelRunner:
     def decode(self, B: int, use_graph: bool = True):
         """Runs one decode step for the first B rows of the bucket-B inputs."""
         self.step_inputs(B)
-        if not use_graph or self.streamer is not None:
+        if not use_graph or self.streamer is not None or self.expert_cache is not None:
             self._decode_body(B)
             return self.inputs[B]
         g = self.graphs.get(B)
@@ -393,6 +404,9 @@ class ModelRunner:
         else:
             ops.embed(w.embd, ids, out_f32=x, err=self.err, n=T)
         for li in range(len(w.layers)):
+            _sp = trace.span(f"prefill/layer{li}") if trace.enabled() else None
+            if _sp is not None:
+                _sp.__enter__()
             lw = self._layer(li)
             kv = self.kv[li]
             ops.rmsnorm_quant(x, lw.attn_norm, eps, None, None, y_bf16=xn)
@@ -414,6 +428,8 @@ class ModelRunner:
                 ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp, up_off=self.up_off)
                 self._proj_into_residual(hb, lw.wdown, x, o, tp)
             self._layer_done(li)
+            if _sp is not None:
+                _sp.__exit__(None, None, None)
         if return_hidden_out:
             return x.clone()
         if return_hidden:  # final-norm hidden states of every row (embeddings)

@@ -7,7 +7,19 @@ from __future__ import annotations
 import os
 from dataclasses import dataclass
 
-VRAM_CAP_FRACTION = float(os.environ.get("AIR_VRAM_CAP_FRACTION", "0.80"))
+VRAM_CAP_FRACTION = float(os.environ.get("AIR_VRAM_FRACTION", os.environ.get("AIR_VRAM_CAP_FRACTION", "0.80")))
+
+
+def set_default_fraction(frac: float):
+    """Cap used by later loads (the KV planner and ``VramBudget.check`` defaults)."""
+    global VRAM_CAP_FRACTION
+    if not 0.0 < frac <= 1.0:
+        raise ValueError("VRAM cap fraction must be in (0, 1]")
+    VRAM_CAP_FRACTION = float(frac)
+
+
+def default_fraction() -> float:
+    return VRAM_CAP_FRACTION
 
 
 @dataclass
@@ -39,7 +51,11 @@ class VramBudget:
     total_bytes: int
     free_bytes: int
     estimate_bytes: int
-    cap_fraction: float = VRAM_CAP_FRACTION
+    cap_fraction: float | None = None
+
+    def __post_init__(self):
+        if self.cap_fraction is None:
+            self.cap_fraction = VRAM_CAP_FRACTION
 
     @property
     def cap_bytes(self) -> int:
@@ -65,7 +81,7 @@ class VramBudget:
             return None
 
     @classmethod
-    def check(cls, estimate_bytes: int, device=0, cap_fraction: float = VRAM_CAP_FRACTION,
+    def check(cls, estimate_bytes: int, device=0, cap_fraction: float | None = None,
               mem_get_info=None) -> VramCheckResult:
         q = cls.query(device, mem_get_info)
         if q is None:
