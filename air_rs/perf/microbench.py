@@ -138,7 +138,7 @@ def bench_graph(preset: str, B: int, iters: int, dev) -> dict:
     prompts = [[(7 * i + j) % 200 + 3 for j in range(32)] for i in range(B)]
     from ..runtime.engine import SamplingParams
     for p in prompts:
-        eng.add_request(p, SamplingParams(max_tokens=10 ** 6, temperature=0.0, ignore_eos=True))
+        eng.add_request(p, SamplingParams(max_tokens=900, temperature=0.0, ignore_eos=True))
     eng.step()                       # prefill + first decode step
     bucket = eng._bucket(B)
     out = {"preset": preset, "B": B, "bucket": bucket}
