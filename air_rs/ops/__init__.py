@@ -200,8 +200,7 @@ def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EP
         if err is None:
             err = wsp.err
         splits = ext.gemv_tiled_splits(w.N, w.K, mode)
-        if splits > 1:
-            ws, cnt = wsp.ensure(ext.gemv_tiled_workspace(w.N, splits, mode), ext.gemv_tiled_counters(w.N))
+        ws, cnt = wsp.ensure(ext.gemv_tiled_workspace(w.N, splits, mode), ext.gemv_tiled_counters(w.N))
     ext.gemv(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, B, xq, xds, mode, out_f32,
              out_bf16, ld, resid, None if w2 is None else w2.data,
              None if w2 is None else w2.scales, rope_cs, positions, slots, kv, q_out,

@@ -237,6 +237,7 @@ __global__ void __launch_bounds__(D)
 attn_merge_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
                   int n_heads, int n_splits, float* __restrict__ out, int8_t* __restrict__ oq,
                   float2* __restrict__ ods, __nv_bfloat16* __restrict__ ob) {
+  pdl_trigger();   // a dependent GEMV may start streaming its weights now
   const int head = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
   const size_t base = ((size_t)r * n_heads + head) * n_splits;
   float M = -INFINITY;
@@ -268,6 +269,7 @@ template <int D>
 __global__ void __launch_bounds__(D)
 attn_quant_kernel(const float* __restrict__ out, int n_heads, int8_t* __restrict__ oq,
                   float2* __restrict__ ods) {
+  pdl_trigger();   // a dependent GEMV may start streaming its weights now
   const int head = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
   const size_t o = ((size_t)r * n_heads + head) * D + d;
   const float v = out[o];

@@ -101,11 +101,9 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
     TORCH_CHECK(data.dim() == 4, "gemv q4k: expects the tiled device layout [N/128, K/256, 128, 144]");
     TORCH_CHECK(ep.err, "gemv q4k: an error word is required (bounded waits report into it)");
     const int s = (int)std::max<int64_t>(1, splits);
-    if (s > 1) {
-      TORCH_CHECK(ws.has_value() && counters.has_value(), "gemv q4k: split-K needs ws and counters");
-      TORCH_CHECK((size_t)ws->numel() >= air::gemv_tiled_workspace_floats((int)N, s, (int)mode), "gemv: ws too small");
-      TORCH_CHECK((size_t)counters->numel() >= air::gemv_tiled_counters((int)N), "gemv: counters too small");
-    }
+    TORCH_CHECK(ws.has_value() && counters.has_value(), "gemv q4k: needs ws and counters");
+    TORCH_CHECK((size_t)ws->numel() >= air::gemv_tiled_workspace_floats((int)N, s, (int)mode), "gemv: ws too small");
+    TORCH_CHECK((size_t)counters->numel() >= air::gemv_tiled_counters((int)N), "gemv: counters too small");
     air::GemvTiledScratch sc{ptr<float>(ws), ptr<int>(counters)};
     const char* e = air::launch_gemv_tiled(w, (int)N, (int)K, (int)B, ptr<int8_t>(xq), ptr<float2>(xds), ep, sc,
                                            s, stream());

@@ -32,6 +32,7 @@ __global__ void __launch_bounds__(kThreads)
 reduce_rmsnorm_quant_kernel(PeerReduce r, float* __restrict__ x, const float* __restrict__ w, float w_offset,
                             int K, float eps, int8_t* __restrict__ q, float2* __restrict__ ds,
                             __nv_bfloat16* __restrict__ y_out) {
+  pdl_trigger();   // a dependent GEMV may start streaming its weights now
   __shared__ float red[32];
   const int b = blockIdx.y, t = threadIdx.x;
   const int e = *(volatile const int*)r.epoch;

@@ -94,6 +94,13 @@ AIR_DEVICE uint4 ld_stream(const void* p) {
 
 AIR_DEVICE int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// Programmatic dependent launch. A kernel launched with the programmatic-serialisation
+// attribute may start while its predecessor in the stream still runs; it must call
+// pdl_wait() before touching anything the predecessor writes or reads (a no-op when it was
+// launched normally). pdl_trigger() lets such a successor start early.
+AIR_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+AIR_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 AIR_DEVICE void set_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }

@@ -43,7 +43,11 @@ extern "C" __attribute__((visibility("default"))) int air_gemv_q4k_noalloc(
     cudaStream_t stream) {
   if (!w_tiled || !xq || !xds || !out || N <= 0 || K <= 0 || K % 256 != 0 || B < 1 || B > 8)
     return AIR_NOALLOC_BAD_ARGUMENT;
-  const int splits = air::gemv_tiled_splits(N, K, air::kEpiStore);
+  // grid cap: as many CTAs as the static array has split-K partial slots for
+  const int per_cta = (int)(air::gemv_tiled_workspace_floats(N, 1, air::kEpiStore) * sizeof(float));
+  const int fit = (int)((AIR_NOALLOC_SCRATCH_BYTES - kHeaderBytes) / per_cta);
+  int splits = air::gemv_tiled_splits(N, K, air::kEpiStore);
+  splits = splits < fit ? splits : fit;
   const size_t counters = air::gemv_tiled_counters(N);
   const size_t ws_bytes = air::gemv_tiled_workspace_floats(N, splits, air::kEpiStore) * sizeof(float);
   if (counters > kMaxCounters || kHeaderBytes + ws_bytes > AIR_NOALLOC_SCRATCH_BYTES) return AIR_NOALLOC_TOO_LARGE;

@@ -20,6 +20,7 @@ rmsnorm_quant_kernel(const float* __restrict__ x, const __nv_bfloat16* __restric
                      const float* __restrict__ w, float w_offset, int K, float eps,
                      int8_t* __restrict__ q, float2* __restrict__ ds,
                      __nv_bfloat16* __restrict__ y_out) {
+  pdl_trigger();   // a dependent GEMV may start streaming its weights now
   __shared__ float red[32];
   const int b = blockIdx.y;
   const float* xr = x ? x + (size_t)b * K : nullptr;

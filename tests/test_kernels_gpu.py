@@ -50,6 +50,24 @@ def test_gemv_store(qt, B):
     torch.testing.assert_close(out.cpu(), ref, rtol=2e-3, atol=2e-4)
 
 
+@pytest.mark.parametrize("N,K", [(8192, 3072), (1280, 4096), (128, 256), (1000, 2048), (4096, 14336)])
+@pytest.mark.parametrize("B", [1, 5])
+def test_gemv_q4k_stream_k_shapes(N, K, B):
+    """Persistent GEMV: CTA ranges that start and end inside tiles, tiles completed by one
+    CTA, a single-unit grid, a partial last tile; the same launch twice (self-resetting
+    tile counters)."""
+    w, wd = _qw(N, K, GGMLType.Q4_K)
+    x = _act(B, K)
+    xq = torch.empty(B, K, dtype=torch.int8, device=DEV)
+    xds = torch.empty(B, K // 32, 2, dtype=torch.float32, device=DEV)
+    ops.rmsnorm_quant(x.to(DEV), None, 0.0, xq, xds)
+    ref = _quant_act_ref(x) @ wd.t()
+    for _ in range(2):
+        out = torch.full((B, N), float("nan"), device=DEV)
+        ops.gemv(w, xq, xds, B, ops.EPI_STORE, out_f32=out)
+        torch.testing.assert_close(out.cpu(), ref, rtol=2e-3, atol=float(ref.abs().max()) * 2e-4)
+
+
 def test_rmsnorm_quant_matches():
     B, K = 4, 4096
     x = _act(B, K) * 3
