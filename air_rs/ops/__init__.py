@@ -190,7 +190,7 @@ def rmsnorm_quant(x: torch.Tensor | None, w: torch.Tensor | None, eps: float, q:
 def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EPI_STORE, *,
          out_f32=None, out_bf16=None, ld_out: int | None = None, resid=None, w2: QWeight | None = None,
          rope_cs=None, positions=None, slots=None, kv=None, q_out=None, n_heads=0, n_kv=0,
-         head_dim=0, block_size=0, rot_dim=0, err=None, push_meta=None):
+         head_dim=0, block_size=0, rot_dim=0, err=None, push_meta=None, out_q=None, out_ds=None):
     ld = ld_out if ld_out is not None else w.N
     ext = require_ext()
     splits, ws, cnt = 1, None, None
@@ -204,7 +204,8 @@ def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EP
     ext.gemv(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, B, xq, xds, mode, out_f32,
              out_bf16, ld, resid, None if w2 is None else w2.data,
              None if w2 is None else w2.scales, rope_cs, positions, slots, kv, q_out,
-             n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err, splits, ws, cnt, push_meta)
+             n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err, splits, ws, cnt, push_meta,
+             out_q, out_ds)
     count_launch()
 
 
@@ -223,9 +224,25 @@ def sample(logits, out_tokens, *, counts=None, count_row=None, mask=None, temper
            top_p=None, seed=0, step=None, out_prob=None, B=None, V=None):
     B = B if B is not None else logits.shape[0]
     V = V if V is not None else logits.shape[1]
-    require_ext().sampler(logits, B, V, counts, count_row, mask, temperature, penalty, top_k, top_p, seed, step,
-                          out_tokens, out_prob)
-    count_launch(2 if step is not None else 1)
+    ext = require_ext()
+    part = _sampler_part(logits.device, B, ext.sampler_chunks(V))
+    ext.sampler(logits, B, V, counts, count_row, mask, temperature, penalty, top_k, top_p, seed, step,
+                out_tokens, out_prob, part)
+    count_launch(3 if step is not None else 2)
+
+
+_SAMPLER_PART: dict = {}
+
+
+def _sampler_part(device, B: int, chunks: int) -> torch.Tensor:
+    """Per-device scratch of the sampler's multi-CTA pass (sized before any graph capture)."""
+    need = max(B, 256) * chunks * 4
+    t = _SAMPLER_PART.get(device)
+    if t is None or t.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("sampler scratch must be sized before CUDA-graph capture")
+        t = _SAMPLER_PART[device] = torch.empty(need, dtype=torch.float32, device=device)
+    return t
 
 
 def count_tokens(counts, tokens, n: int | None = None, per_row: int = 0, count_row=None):

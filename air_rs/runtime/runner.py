@@ -99,6 +99,9 @@ class ModelRunner:
         self.q = torch.zeros(B, self.nh, self.hd, dtype=f32, device=dev)
         self.attn = torch.zeros(B, self.nh * self.hd, dtype=f32, device=dev)
         self.h = torch.zeros(B, self.Fp, dtype=f32, device=dev)
+        gb = min(B, GEMV_MAX_B)
+        self.hq = torch.zeros(gb, self.Fp, dtype=i8, device=dev)          # SwiGLU output, Q8A
+        self.hds = torch.zeros(gb, self.Fp // 32, 2, dtype=f32, device=dev)
         self.y = torch.zeros(B, self.H, dtype=f32, device=dev)
         self.logits = torch.zeros(B, self.V_l, dtype=f32, device=dev)
         self.logits_full = self.logits if tp_size == 1 else torch.zeros(B, self.V, dtype=f32, device=dev)
@@ -292,6 +295,12 @@ class ModelRunner:
         if lw.wgu is None:
             from ..parallel import moe
             moe.moe_ffn_decode(self, lw, B, x, xq, xds, peer)
+            return
+        if lw.w_gate.fmt == ops.FMT_Q4K:
+            # SwiGLU product quantised in the GEMV epilogue (no separate quant kernel)
+            hq, hds = self.hq[:B], self.hds[:B]
+            ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, ld_out=self.Fp, out_q=hq, out_ds=hds)
+            self._row_parallel(lw.wdown, hq, hds, B, x, peer)
             return
         ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, out_f32=self.h[:B], ld_out=self.Fp)
         ops.rmsnorm_quant(self.h[:B], None, 0.0, xq, xds)

@@ -68,7 +68,7 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
   // split_tokens <= 0: divide this row's context evenly over the splits (multiple of kTPW),
   // so one captured launch serves every context length.
   const int st = split_tokens > 0 ? split_tokens
-                                  : ((ctx + n_splits - 1) / n_splits + kTPW - 1) / kTPW * kTPW;
+                                  : max(64, ((ctx + n_splits - 1) / n_splits + kTPW - 1) / kTPW * kTPW);
   int t_begin = split * st;
   int t_end = min(ctx, t_begin + st);
   if (rows.window > 0) t_begin = max(t_begin, ctx - rows.window);
@@ -231,6 +231,8 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
   }
 }
 
+constexpr int kMaxMergeSplits = 256;
+
 // Merge split partials; optionally quantise the output rows to int8 per 32 (Q8A).
 template <int D>
 __global__ void __launch_bounds__(D)
@@ -240,12 +242,18 @@ attn_merge_kernel(const float* __restrict__ part_o, const float2* __restrict__ p
   pdl_trigger();   // a dependent GEMV may start streaming its weights now
   const int head = blockIdx.x, r = blockIdx.y, d = threadIdx.x;
   const size_t base = ((size_t)r * n_heads + head) * n_splits;
+  // split statistics staged once (one load per thread) instead of a serial chain per thread
+  __shared__ float2 sml[kMaxMergeSplits];
+  for (int s = d; s < n_splits; s += D) sml[s] = part_ml[base + s];
+  __syncthreads();
   float M = -INFINITY;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[base + s].x);
+  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, sml[s].x);
   float L = 0.f, O = 0.f;
+#pragma unroll 8
   for (int s = 0; s < n_splits; ++s) {
-    const float2 ml = part_ml[base + s];
-    const float f = (ml.x == -INFINITY) ? 0.f : __expf(ml.x - M);
+    const float2 ml = sml[s];
+    if (ml.x == -INFINITY) continue;       // a split that received no keys
+    const float f = __expf(ml.x - M);
     L += ml.y * f;
     O += part_o[(base + s) * D + d] * f;
   }

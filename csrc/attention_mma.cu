@@ -85,7 +85,9 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seq = rows.row_seq ? rows.row_seq[r] : r;
   const int ctx = rows.ctx_len[r];
-  const int st = split_tokens > 0 ? split_tokens : ((ctx + n_splits - 1) / n_splits + kKeys - 1) / kKeys * kKeys;
+  // at least 64 keys per split: shorter splits cost more in fixed work and merge than they save
+  const int st = split_tokens > 0 ? split_tokens
+                                  : max(64, ((ctx + n_splits - 1) / n_splits + kKeys - 1) / kKeys * kKeys);
   int t_begin = split * st;
   const int t_end = min(ctx, t_begin + st);
   if (rows.window > 0) t_begin = max(t_begin, ((ctx - rows.window) / kKeys) * kKeys);

@@ -60,7 +60,8 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
           optional<Tensor> positions, optional<Tensor> slots, optional<Tensor> kv,
           optional<Tensor> q_out, int64_t n_heads, int64_t n_kv, int64_t head_dim,
           int64_t block_size, int64_t rot_dim, optional<Tensor> err, int64_t splits,
-          optional<Tensor> ws, optional<Tensor> counters, optional<Tensor> push_meta) {
+          optional<Tensor> ws, optional<Tensor> counters, optional<Tensor> push_meta,
+          optional<Tensor> out_q, optional<Tensor> out_ds) {
   check_cuda(data, "gemv weight");
   TORCH_CHECK(B >= 1 && B <= 8, "gemv: batch must be in [1, 8]");
   TORCH_CHECK(K % 32 == 0, "gemv: K must be a multiple of 32");
@@ -86,6 +87,16 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
   ep.rot_dim = (int)rot_dim;
   ep.err = ptr<int>(err);
   if (mode == air::kEpiSwiGLU) TORCH_CHECK(ep.w2.data, "gemv swiglu: w2 required");
+  if (out_q.has_value()) {
+    TORCH_CHECK(mode == air::kEpiSwiGLU && fmt == air::kFmtQ4K && out_ds.has_value(),
+                "gemv: quantised output is a SwiGLU epilogue of the tiled Q4_K path");
+    TORCH_CHECK(out_q->dim() == 2 && out_q->size(0) >= B && out_q->size(1) % 32 == 0 && out_q->size(1) >= N &&
+                    out_q->size(1) <= (N + 127) / 128 * 128 && out_q->is_contiguous(),
+                "gemv: out_q must be int8 [>=B, q_k], q_k % 32 == 0, N <= q_k <= N rounded up to 128");
+    ep.out_q = ptr<int8_t>(out_q);
+    ep.out_ds = ptr<float2>(out_ds);
+    ep.q_k = (int)out_q->size(1);
+  }
   if (mode == air::kEpiPeerPush) {
     TORCH_CHECK(push_meta.has_value() && fmt == air::kFmtQ4K, "gemv peer push: Q4_K tiled weights and push meta");
     ep.push = peer_push_from_meta(*push_meta);
@@ -149,6 +160,7 @@ void paged_attention(Tensor q, Tensor kv, Tensor block_tables, optional<Tensor> 
   TORCH_CHECK(!a.out_bf16 || n_splits > 1, "paged_attention: out_bf16 needs the split merge (n_splits > 1)");
   a.err = ptr<int>(err);
   if (n_splits > 1) TORCH_CHECK(a.part_o && a.part_ml, "paged_attention: split scratch required");
+  TORCH_CHECK(n_splits <= 256, "paged_attention: at most 256 splits");
   TORCH_CHECK(air::launch_paged_attention(a, stream()), "paged_attention: unsupported head_dim/GQA");
   post_launch("paged_attention");
 }
@@ -157,12 +169,18 @@ void sampler(Tensor logits, int64_t B, int64_t V, optional<Tensor> counts, optio
              optional<Tensor> mask,
              optional<Tensor> temperature, optional<Tensor> penalty, optional<Tensor> top_k,
              optional<Tensor> top_p, int64_t seed, optional<Tensor> step, Tensor out_tokens,
-             optional<Tensor> out_prob) {
+             optional<Tensor> out_prob, optional<Tensor> part) {
   check_cuda(logits, "logits");
   air::SamplerArgs a{ptr<uint8_t>(counts), ptr<int>(count_row), ptr<uint32_t>(mask), ptr<float>(temperature),
                      ptr<float>(penalty), ptr<int>(top_k), ptr<float>(top_p),
                      (unsigned long long)seed, ptr<long long>(step), ptr<int>(out_tokens),
                      ptr<float>(out_prob)};
+  if (part.has_value()) {
+    TORCH_CHECK(part->dtype() == torch::kFloat32 && part->is_contiguous() &&
+                    (size_t)part->numel() >= (size_t)B * air::sampler_chunks((int)V) * 4,
+                "sampler: part scratch must be float32 [B * sampler_chunks(V) * 4]");
+    a.part = reinterpret_cast<float4*>(part->data_ptr<float>());
+  }
   air::launch_sampler(ptr<float>(logits), (int)B, (int)V, logits.stride(0), a, stream());
   post_launch("sampler");
 }
@@ -269,6 +287,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_tiled_counters", [](int64_t N) { return (int64_t)air::gemv_tiled_counters((int)N); });
   m.def("paged_attention", &paged_attention);
   m.def("sampler", &sampler);
+  m.def("sampler_chunks", [](int64_t V) { return (int64_t)air::sampler_chunks((int)V); });
   m.def("count_tokens", &count_tokens);
   m.def("embed", &embed);
   m.def("dequant", &dequant);

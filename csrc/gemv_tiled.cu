@@ -164,6 +164,25 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
       __syncthreads();                     // xch is reused by the next tile
       return;
     }
+    if (DUAL && TPR == 1 && ep.out_q) {
+      // one warp = 32 consecutive rows = one Q8A group of the next GEMV's input
+      if (tile * kRows + (row_l & ~31) >= ep.q_k) return;       // warp-uniform
+#pragma unroll
+      for (int b = 0; b < MAXB; ++b) {
+        if (b >= nB) break;
+        float v = 0.f;
+        if (row < N) v = acc[0][b] / (1.f + __expf(-acc[0][b])) * acc[1][b];
+        if (ep.out_f32) { if (row < N) ep.out_f32[(size_t)b * ep.ld_out + row] = v; }
+        const float amax = warp_max(fabsf(v));
+        const float dq = amax / 127.f;
+        int qi = dq > 0.f ? __float2int_rn(v / dq) : 0;
+        qi = max(-127, min(127, qi));
+        ep.out_q[(size_t)b * ep.q_k + row] = (int8_t)qi;
+        const int sq = warp_sum_i(qi);
+        if ((t & 31) == 0) ep.out_ds[(size_t)b * (ep.q_k / 32) + row / 32] = make_float2(dq, dq * (float)sq);
+      }
+      return;
+    }
     if (row >= N) return;
     if (ep.mode == kEpiPeerPush) {
       const int e = *(volatile const int*)ep.push.epoch;
@@ -398,7 +417,8 @@ template <int MAXB>
 const char* launch_b(const GemvWeight& w, int N, int K, int B, const int8_t* xq, const float2* xds,
                      const GemvEpiParams& ep, const GemvTiledScratch& sc, int grid, cudaStream_t st) {
   const bool dual = ep.mode == kEpiSwiGLU;
-  const GemvCfg c = gemv_cfg(dual);
+  GemvCfg c = gemv_cfg(dual);
+  if (ep.out_q) c.tpr = 1;          // the quantising epilogue maps one warp to 32 rows
   if (dual)
     return c.tpr == 4 ? launch_t<MAXB, true, 4>(w, N, K, B, xq, xds, ep, sc, grid, c.stages, st)
                       : launch_t<MAXB, true, 1>(w, N, K, B, xq, xds, ep, sc, grid, c.stages, st);

@@ -63,6 +63,11 @@ struct GemvEpiParams {
   int64_t num_blocks;
   int* err;
   PeerPush push;              // kEpiPeerPush
+  // kEpiSwiGLU on the tiled Q4_K path: also (or only) write the product quantised to Q8A
+  // (int8 [B, q_k] + float2 [B, q_k/32]) for the next GEMV; rows N..q_k are zero.
+  int8_t* out_q;
+  float2* out_ds;
+  int q_k;
 };
 
 // x: activations quantised by rmsnorm_quant (int8 [B,K] + float2 [B,K/32]).

@@ -1,5 +1,7 @@
 // Fused on-device sampler: repetition penalty, grammar mask, greedy argmax, temperature,
-// exact top-k (radix select), top-p nucleus and a seeded Philox draw — one CTA per row.
+// exact top-k (radix select), top-p nucleus and a seeded Philox draw — one CTA per row, after
+// a pass that spreads each row's argmax and softmax denominator over many CTAs (one per 1024
+// vocabulary entries), so a greedy step does not stream the vocabulary through one SM.
 //
 // Semantics follow the reference sampler (src/sampler.rs:83-164, 272-292): the penalty
 // divides positive / multiplies negative logits once per past occurrence of a token
@@ -30,6 +32,77 @@ AIR_DEVICE float penalised(float v, int c, float pen) {
   return v > 0.f ? v / f : v * f;
 }
 
+constexpr int kChunk = 1024;          // vocabulary entries per CTA of the partial pass
+constexpr int kPartThreads = 256;
+
+struct RowView {
+  const float* lg;
+  const uint8_t* cnt;
+  const uint32_t* mask;
+  float pen;
+  AIR_DEVICE float value(int i) const {
+    float v = lg[i];
+    if (cnt) v = penalised(v, cnt[i], pen);
+    if (mask && !((mask[i >> 5] >> (i & 31)) & 1u)) v = -INFINITY;
+    return v;
+  }
+};
+
+AIR_DEVICE RowView row_view(const float* logits, int V, int64_t ld, const SamplerArgs& a, int row) {
+  RowView r;
+  r.lg = logits + (size_t)row * ld;
+  r.cnt = a.counts ? a.counts + (size_t)(a.count_row ? a.count_row[row] : row) * V : nullptr;
+  r.mask = a.allow_mask ? a.allow_mask + (size_t)row * ((V + 31) / 32) : nullptr;
+  r.pen = a.rep_penalty ? a.rep_penalty[row] : 1.f;
+  return r;
+}
+
+AIR_DEVICE void argmax_merge(float& best, int& besti, float ov, int oi) {
+  if (ov > best || (ov == best && oi < besti)) { best = ov; besti = oi; }
+}
+
+// Pass over one vocabulary chunk of one row, spread over many CTAs: (max, argmax, and with a
+// temperature the softmax denominator relative to the chunk max) -> part[row][chunk].
+__global__ void __launch_bounds__(kPartThreads)
+sampler_partial_kernel(const float* __restrict__ logits, int V, int64_t ld, SamplerArgs a, int nch) {
+  const int chunk = blockIdx.x, row = blockIdx.y;
+  const RowView rv = row_view(logits, V, ld, a, row);
+  const float temp = a.temperature ? a.temperature[row] : 0.f;
+  const int i0 = chunk * kChunk, i1 = min(V, i0 + kChunk);
+  constexpr int kPer = kChunk / kPartThreads;
+  float v[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = i0 + threadIdx.x + j * kPartThreads;
+    v[j] = i < i1 ? rv.value(i) : -INFINITY;
+  }
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) argmax_merge(best, besti, v[j], i0 + threadIdx.x + j * kPartThreads);
+  __shared__ float red[32];
+  __shared__ int redi[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_merge(best, besti, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, besti, o));
+  if (lane == 0) { red[wid] = best; redi[wid] = besti; }
+  __syncthreads();
+  best = red[0];
+  besti = redi[0];
+  for (int w = 1; w < kPartThreads / 32; ++w) argmax_merge(best, besti, red[w], redi[w]);
+  float z = 0.f;
+  if (temp > 1e-6f && best != -INFINITY) {
+    const float inv_t = 1.f / temp;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (v[j] != -INFINITY) z += __expf((v[j] - best) * inv_t);
+    __syncthreads();
+    z = block_sum(z, red);
+  }
+  if (threadIdx.x == 0) a.part[(size_t)row * nch + chunk] = make_float4(best, __int_as_float(besti), z, 0.f);
+}
+
 __global__ void __launch_bounds__(kThreads)
 sampler_kernel(const float* __restrict__ logits, int V, int64_t ld, SamplerArgs a) {
   const int row = blockIdx.x;
@@ -57,12 +130,20 @@ sampler_kernel(const float* __restrict__ logits, int V, int64_t ld, SamplerArgs 
     return v;
   };
 
-  // ---- pass 1: argmax (lowest index on ties) and max ----
+  // ---- pass 1: argmax (lowest index on ties) and max (from the chunk partials if any) ----
   float best = -INFINITY;
   int besti = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += kThreads) {
-    const float v = value(i);
-    if (v > best || (v == best && i < besti)) { best = v; besti = i; }
+  const int nch = (V + kChunk - 1) / kChunk;
+  if (a.part) {
+    for (int c = threadIdx.x; c < nch; c += kThreads) {
+      const float4 p = a.part[(size_t)row * nch + c];
+      argmax_merge(best, besti, p.x, __float_as_int(p.y));
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += kThreads) {
+      const float v = value(i);
+      if (v > best || (v == best && i < besti)) { best = v; besti = i; }
+    }
   }
   {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -100,9 +181,16 @@ sampler_kernel(const float* __restrict__ logits, int V, int64_t ld, SamplerArgs 
   const float inv_t = 1.f / temp;
   // ---- softmax denominator over the whole vocabulary ----
   float z = 0.f;
-  for (int i = threadIdx.x; i < V; i += kThreads) {
-    const float v = value(i);
-    if (v != -INFINITY) z += __expf((v - best) * inv_t);
+  if (a.part) {
+    for (int c = threadIdx.x; c < nch; c += kThreads) {
+      const float4 p = a.part[(size_t)row * nch + c];
+      if (p.x != -INFINITY) z += p.z * __expf((p.x - best) * inv_t);
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += kThreads) {
+      const float v = value(i);
+      if (v != -INFINITY) z += __expf((v - best) * inv_t);
+    }
   }
   z = block_sum(z, red);
   // ---- exact k-th largest by 4 x 8-bit radix select ----
@@ -223,9 +311,15 @@ __global__ void bump_step_kernel(long long* step) { *step += 1; }
 
 void launch_sampler(const float* logits, int B, int V, int64_t ld, const SamplerArgs& a,
                     cudaStream_t st) {
+  if (a.part) {
+    const int nch = (V + kChunk - 1) / kChunk;
+    sampler_partial_kernel<<<dim3(nch, B), kPartThreads, 0, st>>>(logits, V, ld, a, nch);
+  }
   sampler_kernel<<<B, kThreads, 0, st>>>(logits, V, ld, a);
   if (a.step) bump_step_kernel<<<1, 1, 0, st>>>(a.step);
 }
+
+int sampler_chunks(int V) { return (V + kChunk - 1) / kChunk; }
 
 void launch_count_tokens(uint8_t* counts, int V, const int* tokens, int n, int per_row,
                          const int* count_row, cudaStream_t st) {

@@ -16,7 +16,10 @@ struct SamplerArgs {
   long long* step;                // device step counter (Philox offset), bumped per call
   int* out_tokens;                // [B]
   float* out_prob;                // [B] probability of the chosen token's top-1 (optional)
+  float4* part = nullptr;         // [B, sampler_chunks(V)] scratch for the multi-CTA pass (optional)
 };
+
+int sampler_chunks(int V);
 
 void launch_sampler(const float* logits, int B, int V, int64_t ld, const SamplerArgs& a,
                     cudaStream_t st);

@@ -108,6 +108,30 @@ def test_gemv_residual_and_swiglu():
     torch.testing.assert_close(resid.cpu(), ref, rtol=2e-3, atol=1e-5)
 
 
+@pytest.mark.parametrize("B", [1, 3, 8])
+def test_gemv_swiglu_quantised_epilogue_matches_separate_quant(B):
+    """SwiGLU GEMV writing its product as Q8A (int8 + per-32 scales) equals the GEMV's fp32
+    output quantised by rmsnorm_quant, element for element; padded rows N..q_k are zero."""
+    H, F, Fp = 1024, 1200, 1216
+    wg, _ = _qw(F, H, GGMLType.Q4_K, 6)
+    wu, _ = _qw(F, H, GGMLType.Q4_K, 7)
+    x = _act(B, H, seed=2)
+    xq = torch.empty(B, H, dtype=torch.int8, device=DEV)
+    xds = torch.empty(B, H // 32, 2, dtype=torch.float32, device=DEV)
+    ops.rmsnorm_quant(x.to(DEV), None, 0, xq, xds)
+    h = torch.zeros(B, Fp, device=DEV)
+    ops.gemv(wg, xq, xds, B, ops.EPI_SWIGLU, w2=wu, out_f32=h, ld_out=Fp)
+    rq = torch.empty(B, Fp, dtype=torch.int8, device=DEV)
+    rds = torch.empty(B, Fp // 32, 2, dtype=torch.float32, device=DEV)
+    ops.rmsnorm_quant(h, None, 0, rq, rds)
+    hq = torch.full((B, Fp), 99, dtype=torch.int8, device=DEV)
+    hds = torch.full((B, Fp // 32, 2), float("nan"), device=DEV)
+    ops.gemv(wg, xq, xds, B, ops.EPI_SWIGLU, w2=wu, ld_out=Fp, out_q=hq, out_ds=hds)
+    assert torch.equal(hq.cpu(), rq.cpu())
+    torch.testing.assert_close(hds.cpu(), rds.cpu(), rtol=0, atol=0)
+    assert (hq[:, F:] == 0).all()
+
+
 def _rope_ref(x, pos, theta, d):
     inv = 1.0 / torch.pow(torch.tensor(theta), torch.arange(0, d, 2, dtype=torch.float32) / d)
     ang = pos[:, None].float() * inv[None]
