@@ -5,7 +5,11 @@
 and as a replayed graph, device time per step from CUDA events plus host time per step, and
 the number of kernels in the step.
 
-``python -m air_rs.perf.microbench [--op gemv|gemm|attn|norm|graph|all] [--name qkv|o|gateup|down|lm]
+``--op step`` lists the kernels of one graph-replayed decode step (CUPTI through
+``torch.profiler``: count and device time per kernel over 10 steps) at ``--batch`` rows of
+``--ctx`` context tokens, then the CUDA-event time per step.
+
+``python -m air_rs.perf.microbench [--op gemv|gemm|attn|norm|graph|step|all] [--name qkv|o|gateup|down|lm]
 [--batch B] [--iters N]`` prints one line per case: device time (CUDA events around a CUDA
 graph of N back-to-back launches, after warm-up), achieved bytes/s or FLOP/s, and the
 fraction of the measured HBM copy bandwidth / cuBLAS bf16 rate (``MEASURED_PEAKS.json`` at
@@ -164,9 +168,39 @@ def bench_graph(preset: str, B: int, iters: int, dev) -> dict:
     return out
 
 
+def profile_step(preset: str, B: int, ctx: int, dev) -> str:
+    from torch.profiler import ProfilerActivity, profile
+    from ..runtime.builder import random_engine
+    from ..runtime.engine import SamplingParams
+    eng = random_engine(preset, device=dev, max_batch=max(B, 1), max_model_len=ctx + 1024,
+                        num_blocks=B * ((ctx + 1024) // 16 + 2) + 16)
+    for i in range(B):
+        eng.add_request([(7 * i + j) % 200 + 3 for j in range(ctx)],
+                        SamplingParams(max_tokens=900, temperature=0.0, ignore_eos=True))
+    eng.step()
+    rn, bucket = eng.runner, eng._bucket(B)
+    for _ in range(5):
+        rn.decode(bucket)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(10):
+            rn.decode(bucket)
+        torch.cuda.synchronize()
+    table = prof.key_averages().table(sort_by="cuda_time_total", row_limit=20, max_name_column_width=80)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(20):
+        rn.decode(bucket)
+    b.record()
+    torch.cuda.synchronize()
+    for r in list(eng.running):
+        eng.abort(r.rid)
+    return table + f"\n{preset} decode B={B} ctx={ctx}: {a.elapsed_time(b) / 20:.3f} ms/step (CUDA events, graph replay)"
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--op", default="all", choices=["all", "gemv", "gemm", "attn", "norm", "graph"])
+    ap.add_argument("--op", default="all", choices=["all", "gemv", "gemm", "attn", "norm", "graph", "step"])
     ap.add_argument("--preset", default="llama3-8b")
     ap.add_argument("--name", default=None, choices=list(SHAPES))
     ap.add_argument("--batch", type=int, default=None)
@@ -204,6 +238,8 @@ def main(argv=None):
             us = ev_time(lambda: ops.rmsnorm_quant(x, w, 1e-5, q, ds), a.iters)
             line("norm", f"rmsnorm_quant K={K} B={B}", us, B * K * 4 + B * K + B * K // 8, 0.0)
 
+    if a.op == "step":
+        print(profile_step(a.preset, a.batch or 1, a.ctx, dev), flush=True)
     if a.op == "graph":
         for B in ([a.batch] if a.batch else [1, 64]):
             r = bench_graph(a.preset, B, a.iters, dev)
