@@ -190,7 +190,15 @@ def rmsnorm_quant(x: torch.Tensor | None, w: torch.Tensor | None, eps: float, q:
 def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EPI_STORE, *,
          out_f32=None, out_bf16=None, ld_out: int | None = None, resid=None, w2: QWeight | None = None,
          rope_cs=None, positions=None, slots=None, kv=None, q_out=None, n_heads=0, n_kv=0,
-         head_dim=0, block_size=0, rot_dim=0, err=None, push_meta=None, out_q=None, out_ds=None):
+         head_dim=0, block_size=0, rot_dim=0, err=None, push_meta=None, out_q=None, out_ds=None,
+         norm_w=None, norm_offset: float = 0.0, ss_out=None, ss_in=None, norm_k: int = 0,
+         eps: float = 0.0):
+    """Decode GEMV (batch <= 8) with a fused epilogue ``mode``.
+
+    Fused RMSNorm chain (tiled Q4_K): a residual GEMV given ``norm_w`` also writes the next
+    norm's Q8A input (x * norm_w, quantised per 32) to ``out_q`` / ``out_ds`` and each 32-row
+    group's sum of squares to ``ss_out`` [B, N/32]; a GEMV given ``ss_in`` scales its outputs
+    by rsqrt(sum(ss_in[b]) / norm_k + eps)."""
     ld = ld_out if ld_out is not None else w.N
     ext = require_ext()
     splits, ws, cnt = 1, None, None
@@ -205,7 +213,7 @@ def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EP
              out_bf16, ld, resid, None if w2 is None else w2.data,
              None if w2 is None else w2.scales, rope_cs, positions, slots, kv, q_out,
              n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err, splits, ws, cnt, push_meta,
-             out_q, out_ds)
+             out_q, out_ds, norm_w, norm_offset, ss_out, ss_in, norm_k, eps)
     count_launch()
 
 

@@ -9,6 +9,7 @@ sequences (chunked prefill) through the GEMM path and samples each sequence's ne
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -102,6 +103,10 @@ class ModelRunner:
         gb = min(B, GEMV_MAX_B)
         self.hq = torch.zeros(gb, self.Fp, dtype=i8, device=dev)          # SwiGLU output, Q8A
         self.hds = torch.zeros(gb, self.Fp // 32, 2, dtype=f32, device=dev)
+        # fused-norm decode chain: attention output (Q8A) and per-32-row sums of squares
+        self.aq = torch.zeros(gb, self.nh * self.hd, dtype=i8, device=dev)
+        self.ads = torch.zeros(gb, self.nh * self.hd // 32, 2, dtype=f32, device=dev)
+        self.ss = torch.zeros(gb, self.H // 32, dtype=f32, device=dev)
         self.y = torch.zeros(B, self.H, dtype=f32, device=dev)
         self.logits = torch.zeros(B, self.V_l, dtype=f32, device=dev)
         self.logits_full = self.logits if tp_size == 1 else torch.zeros(B, self.V, dtype=f32, device=dev)
@@ -243,6 +248,8 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int):
+        if B <= GEMV_MAX_B and self.fused_norm_ok():
+            return self._decode_fused(B)
         cfg, w, si = self.cfg, self.w, self.inputs[B]
         x, xq, xds = self.x[:B], self.xq[:B], self.xds[:B]
         ops.embed(w.embd, si.ids, out_f32=x, err=self.err, n=B)
@@ -283,6 +290,62 @@ class ModelRunner:
                 self._ffn_gemm(lw, B, x, tp, peer)
             self._layer_done(li)
         self._head(B, x, xq, xds, gemv_path, peer)
+
+    def fused_norm_ok(self) -> bool:
+        """Decode GEMV chain with the RMSNorms folded into the GEMV epilogues: one GPU, dense
+        layers, every projection in the tiled Q4_K layout, resident weights."""
+        if getattr(self, "_fused_ok", None) is None:
+            q4 = lambda q: q is not None and q.fmt == ops.FMT_Q4K
+            w = self.w
+            self._fused_ok = (self.tp_size == 1 and self.hd == 128 and q4(w.lm_head) and
+                              os.environ.get("AIR_FUSED_NORM", "1") != "0" and
+                              all(lw.wgu is not None and q4(lw.wqkv) and q4(lw.wo) and q4(lw.w_gate) and
+                                  q4(lw.wdown) for lw in w.layers))
+        return self._fused_ok and self.streamer is None
+
+    def _decode_fused(self, B: int):
+        """B <= 8 decode where each residual GEMV (o, down) also emits the next RMSNorm's
+        quantised input and row sums of squares, and the next GEMV applies the 1/rms scale in
+        its epilogue: one norm kernel per step (the first) instead of two per layer."""
+        cfg, w, si = self.cfg, self.w, self.inputs[B]
+        H, eps = self.H, cfg.rms_norm_eps
+        x = self.x[:B]
+        xa = self.xq.view(-1)[: B * H].view(B, H)
+        xda = self.xds.view(-1)[: B * H // 16].view(B, H // 32, 2)
+        aq, ads, hq, hds = self.aq[:B], self.ads[:B], self.hq[:B], self.hds[:B]
+        # one partial-sum buffer suffices: every GEMV writes it only after griddepcontrol.wait,
+        # i.e. after the previous consumer has finished reading it
+        ss = self.ss[:B]
+        ops.embed(w.embd, si.ids, out_f32=x, err=self.err, n=B)
+        ops.rmsnorm_quant(x, w.layers[0].attn_norm, eps, xa, xda)
+        ns = self.n_splits(B)
+        L = len(w.layers)
+        for li in range(L):
+            lw = w.layers[li]
+            kv = self.kv[li]
+            ops.gemv(lw.wqkv, xa, xda, B, ops.EPI_QKV_ROPE, rope_cs=self.rope_cs,
+                     positions=si.positions, slots=si.slots, kv=kv, q_out=self.q[:B],
+                     n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
+                     block_size=self.block_size, rot_dim=self.rot_dim, err=self.err,
+                     ss_in=ss if li > 0 else None, norm_k=H, eps=eps)
+            ops.paged_attention(self.q[:B], kv, si.block_tables, si.ctx_len, self.attn[:B],
+                                n_rows=B, n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
+                                block_size=self.block_size, n_splits=ns, split_tokens=0,
+                                part_o=self.part_o, part_ml=self.part_ml, out_q=aq, out_ds=ads,
+                                err=self.err, window=cfg.sliding_window or 0)
+            ops.gemv(lw.wo, aq, ads, B, ops.EPI_RESIDUAL, resid=x, norm_w=lw.ffn_norm, out_q=xa, out_ds=xda,
+                     ss_out=ss)
+            ops.gemv(lw.w_gate, xa, xda, B, ops.EPI_SWIGLU, w2=lw.w_up, ld_out=self.Fp, out_q=hq, out_ds=hds,
+                     ss_in=ss, norm_k=H, eps=eps)
+            nxt = w.layers[li + 1].attn_norm if li + 1 < L else w.out_norm
+            ops.gemv(lw.wdown, hq, hds, B, ops.EPI_RESIDUAL, resid=x, norm_w=nxt, out_q=xa, out_ds=xda,
+                     ss_out=ss)
+        ops.gemv(w.lm_head, xa, xda, B, ops.EPI_STORE, out_f32=self.logits[:B], ss_in=ss, norm_k=H, eps=eps)
+        ops.sample(self.logits[:B], si.tokens, counts=self.counts, count_row=si.count_row, mask=si.mask,
+                   temperature=si.temperature, penalty=si.penalty, top_k=si.top_k, top_p=si.top_p,
+                   seed=self.seed, step=self.step_ctr, out_prob=si.probs, B=B, V=self.V)
+        ops.count_tokens(self.counts, si.tokens, n=B, count_row=si.count_row)
+        si.ids.copy_(si.tokens)
 
     def _residual(self, y_b: torch.Tensor, B: int, x: torch.Tensor, tp: bool):
         if tp:

@@ -61,7 +61,8 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
           optional<Tensor> q_out, int64_t n_heads, int64_t n_kv, int64_t head_dim,
           int64_t block_size, int64_t rot_dim, optional<Tensor> err, int64_t splits,
           optional<Tensor> ws, optional<Tensor> counters, optional<Tensor> push_meta,
-          optional<Tensor> out_q, optional<Tensor> out_ds) {
+          optional<Tensor> out_q, optional<Tensor> out_ds, optional<Tensor> norm_w, double norm_offset,
+          optional<Tensor> ss_out, optional<Tensor> ss_in, int64_t norm_k, double eps) {
   check_cuda(data, "gemv weight");
   TORCH_CHECK(B >= 1 && B <= 8, "gemv: batch must be in [1, 8]");
   TORCH_CHECK(K % 32 == 0, "gemv: K must be a multiple of 32");
@@ -87,7 +88,27 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
   ep.rot_dim = (int)rot_dim;
   ep.err = ptr<int>(err);
   if (mode == air::kEpiSwiGLU) TORCH_CHECK(ep.w2.data, "gemv swiglu: w2 required");
-  if (out_q.has_value()) {
+  if (norm_w.has_value()) {
+    TORCH_CHECK(mode == air::kEpiResidual && fmt == air::kFmtQ4K && out_q.has_value() && out_ds.has_value() &&
+                    ss_out.has_value() && out_q->size(1) == N && norm_w->numel() >= N &&
+                    ss_out->numel() >= B * (N / 32),
+                "gemv: the fused RMSNorm producer is a residual epilogue of the tiled Q4_K path with "
+                "out_q [B, N], out_ds and ss_out [B, N / 32]");
+    ep.norm_w = ptr<float>(norm_w);
+    ep.norm_offset = (float)norm_offset;
+    ep.ss_out = ptr<float>(ss_out);
+    ep.out_q = ptr<int8_t>(out_q);
+    ep.out_ds = ptr<float2>(out_ds);
+    ep.q_k = (int)N;
+  }
+  if (ss_in.has_value()) {
+    TORCH_CHECK(fmt == air::kFmtQ4K && norm_k > 0 && norm_k % 32 == 0 && ss_in->numel() >= B * (norm_k / 32),
+                "gemv: ss_in (fused RMSNorm partial sums [B, norm_k / 32]) needs the tiled Q4_K path");
+    ep.ss_in = ptr<float>(ss_in);
+    ep.norm_k = (int)norm_k;
+    ep.eps = (float)eps;
+  }
+  if (out_q.has_value() && !norm_w.has_value()) {
     TORCH_CHECK(mode == air::kEpiSwiGLU && fmt == air::kFmtQ4K && out_ds.has_value(),
                 "gemv: quantised output is a SwiGLU epilogue of the tiled Q4_K path");
     TORCH_CHECK(out_q->dim() == 2 && out_q->size(0) >= B && out_q->size(1) % 32 == 0 && out_q->size(1) >= N &&

@@ -35,6 +35,7 @@ constexpr int kMaxStages = 12;
 struct Smem {
   uint64_t full[kMaxStages];
   int last;
+  float scale[8];      // fused RMSNorm: 1/rms of each batch row
 };
 
 // Work range of CTA c: units [c * kper, min((c + 1) * kper, units)), unit = (tile,
@@ -91,6 +92,16 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
   if (t == 0)
     for (int i = 0; i < min(S, nk); ++i) issue(i);
   pdl_wait();
+  if (ep.ss_in) {
+    // 1/rms per batch row from the producer's per-32-row partial sums, in a fixed order
+    const int ng = ep.norm_k / 32, warp = t >> 5, lane = t & 31;
+    for (int b = warp; b < nB; b += (kRows * TPR) >> 5) {
+      float sum = 0.f;
+      for (int g = lane; g < ng; g += 32) sum += __ldcg(ep.ss_in + (size_t)b * ng + g);
+      sum = warp_sum(sum);
+      if (lane == 0) bar->scale[b] = rsqrtf(sum / (float)ep.norm_k + ep.eps);
+    }
+  }
   {
     const int nw = XW == nsb ? nsb : min(nk, XW);
     for (int idx = t; idx < nB * nw * 20; idx += kRows * TPR) {
@@ -120,6 +131,14 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
   // owns batch rows b with b % TPR == c4).
   auto epilogue = [&](int tile) {
     const int row = tile * kRows + row_l;
+    if (ep.ss_in) {
+#pragma unroll
+      for (int b = 0; b < MAXB; ++b) {
+        const float sc = b < nB ? bar->scale[b] : 0.f;
+#pragma unroll
+        for (int u = 0; u < W; ++u) acc[u][b] *= sc;
+      }
+    }
     if (ep.mode == kEpiQKVRope) {
 #pragma unroll
       for (int b = 0; b < MAXB; ++b)
@@ -183,6 +202,32 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
       }
       return;
     }
+    if (TPR == 1 && ep.norm_w) {
+      // residual add + next RMSNorm's Q8A input and sum of squares (one warp = 32 rows)
+#pragma unroll
+      for (int b = 0; b < MAXB; ++b) {
+        if (b >= nB) break;
+        float v = 0.f, y = 0.f;
+        if (row < N) {
+          const size_t o = (size_t)b * ep.ld_out + row;
+          v = ep.resid[o] + acc[0][b];
+          ep.resid[o] = v;
+          y = v * (ep.norm_w[row] + ep.norm_offset);
+        }
+        const float amax = warp_max(fabsf(y));
+        const float dq = amax / 127.f;
+        int qi = dq > 0.f ? __float2int_rn(y / dq) : 0;
+        qi = max(-127, min(127, qi));
+        const float ss = warp_sum(v * v);
+        if (row < ep.q_k) ep.out_q[(size_t)b * ep.q_k + row] = (int8_t)qi;
+        const int sq = warp_sum_i(qi);
+        if ((t & 31) == 0 && row < ep.q_k) {
+          ep.out_ds[(size_t)b * (ep.q_k / 32) + row / 32] = make_float2(dq, dq * (float)sq);
+          ep.ss_out[(size_t)b * (ep.q_k / 32) + row / 32] = ss;
+        }
+      }
+      return;
+    }
     if (row >= N) return;
     if (ep.mode == kEpiPeerPush) {
       const int e = *(volatile const int*)ep.push.epoch;
@@ -242,12 +287,15 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
     // loaded four at a time so the L2 round trips overlap
     const int ua = tile * nsb, ub = ua + nsb;
     const int c_lo = ua / kper, c_hi = (ub - 1) / kper;
+    // every partial (this CTA's own included) is summed in contributor order, so the result
+    // does not depend on which CTA arrived last
+    zero();
     for (int c0 = c_lo; c0 <= c_hi; c0 += 4) {
       float v[4][W][MAXB];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c = c0 + j;
-        const bool use = c <= c_hi && c != cta;
+        const bool use = c <= c_hi;
         const int sl = (c * kper) / nsb == tile ? 0 : 1;
         const float* pp = sc.ws + (((size_t)(use ? c : 0) * 2 + sl) * kRows + row_l) * (W * MAXB);
 #pragma unroll
@@ -324,6 +372,7 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
     __syncthreads();                       // slab s fully consumed by every row
     if (t == 0 && ok && i + S < nk) issue(i + S);
   }
+  if (sc.early_trigger) pdl_trigger();   // a dependent GEMV's weights stream during these tiles
   if (nk > 0) finish_tile(cur_tile, sb_lo, (u_end - 1) / nsb == cur_tile ? (u_end - 1) % nsb + 1 : nsb);
   if (!ok && t == 0)  // never exit with bulk copies still landing in this CTA's shared memory
     for (int i = max(0, issued - S); i < issued; ++i) mbar_wait(&bar->full[i % S], (i / S) & 1, nullptr, 50000000ull);
@@ -418,7 +467,7 @@ const char* launch_b(const GemvWeight& w, int N, int K, int B, const int8_t* xq,
                      const GemvEpiParams& ep, const GemvTiledScratch& sc, int grid, cudaStream_t st) {
   const bool dual = ep.mode == kEpiSwiGLU;
   GemvCfg c = gemv_cfg(dual);
-  if (ep.out_q) c.tpr = 1;          // the quantising epilogue maps one warp to 32 rows
+  if (ep.out_q || ep.norm_w) c.tpr = 1;   // the quantising epilogues map one warp to 32 rows
   if (dual)
     return c.tpr == 4 ? launch_t<MAXB, true, 4>(w, N, K, B, xq, xds, ep, sc, grid, c.stages, st)
                       : launch_t<MAXB, true, 1>(w, N, K, B, xq, xds, ep, sc, grid, c.stages, st);
@@ -459,6 +508,14 @@ const char* launch_gemv_tiled(const GemvWeight& w, int N, int K, int B, const in
                               int splits, cudaStream_t st) {
   GemvTiledScratch sc = sc_in;
   if (sc.wsplit <= 0) sc.wsplit = gemv_wsplit();
+  if (sc.early_trigger < 0) {
+    static int v = -1;
+    if (v < 0) {
+      const char* e = getenv("AIR_PDL_EARLY");
+      v = (e && e[0] == '0') ? 0 : 1;
+    }
+    sc.early_trigger = v;
+  }
   if (w.fmt != kFmtQ4K) return "gemv_tiled: Q4_K only";
   if (K % 256) return "gemv_tiled: K must be a multiple of 256";
   if (ep.mode == kEpiQKVRope && ep.head_dim != kRows) return "gemv_tiled: QKV epilogue needs head_dim 128";

@@ -9,6 +9,7 @@ struct GemvTiledScratch {
   float* ws;        // split-K partials: gemv_tiled_workspace_floats() floats
   int* counters;    // gemv_tiled_counters() ints, zero before first use (self-resetting)
   int wsplit = 0;   // bulk copies per 18 KB slab (0: launch_gemv_tiled picks)
+  int early_trigger = -1;   // release a dependent launch before the epilogue (-1: AIR_PDL_EARLY, default on)
 };
 
 int gemv_tiled_splits(int N, int K, int mode);

@@ -68,6 +68,17 @@ struct GemvEpiParams {
   int8_t* out_q;
   float2* out_ds;
   int q_k;
+  // RMSNorm folded into the decode GEMV chain (tiled Q4_K path). Producer (kEpiResidual with
+  // norm_w): after x += W.h, write Q8A of x * (norm_w + norm_offset) to out_q / out_ds and each
+  // 32-row group's sum of x^2 to ss_out[b][row / 32]. Consumer (ss_in, norm_k = row length):
+  // outputs are scaled by rsqrt(sum(ss_in[b]) / norm_k + eps) before the epilogue (the scale
+  // is linear in the quantised input). Sums are taken in a fixed order (deterministic).
+  const float* norm_w;
+  float norm_offset;
+  float* ss_out;
+  const float* ss_in;
+  int norm_k;
+  float eps;
 };
 
 // x: activations quantised by rmsnorm_quant (int8 [B,K] + float2 [B,K/32]).

@@ -73,3 +73,34 @@ def test_sampling_is_reproducible():
     runner.step_ctr.zero_()
     b = Engine(cfg, runner, max_batch=8).generate_ids([prompt], params)[0]
     assert a == b
+
+
+def _q4k_all_cfg():
+    from air_rs.models.config import ModelConfig
+    # every projection a whole number of Q4_K super-blocks and head_dim 128: the fused-norm chain
+    return ModelConfig(n_layers=3, n_heads=4, n_kv_heads=2, hidden_dim=512, intermediate_dim=1536,
+                       vocab_size=4096, rope_theta=10000.0, rms_norm_eps=1e-5, head_dim=128)
+
+
+@pytest.mark.parametrize("B", [1, 3, 8])
+def test_fused_norm_decode_chain_matches_unfused(B):
+    """RMSNorm folded into the GEMV epilogues (residual GEMV emits the next norm's Q8A input and
+    sum of squares; the next GEMV scales by 1/rms) against the separate-norm chain, and both
+    against the reference-numerics oracle."""
+    cfg = _q4k_all_cfg()
+    recs = list(random_tensors(cfg, GGMLType.Q4_K, seed=3, device="cpu"))
+    oracle = OracleModel(cfg, {n: (r, q, s) for n, r, q, s in recs})
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (int(n),), generator=g).tolist() for n in (17, 40, 5, 23, 9, 31, 12, 8)[:B]]
+    outs = {}
+    for fused in (True, False):
+        rn = build_runner(cfg, iter(recs), device="cuda", max_batch=8, max_model_len=256, num_blocks=256)
+        rn._fused_ok = fused
+        assert rn.fused_norm_ok() == fused
+        eng = Engine(cfg, rn, max_batch=8)
+        outs[fused] = eng.generate_ids(prompts, SamplingParams(max_tokens=16, temperature=0.0, ignore_eos=True))
+        rn.check_errors()
+    for p, o in zip(prompts, outs[True]):
+        _check_near_argmax(oracle, [cfg.bos_token_id] + p, o)
+    same = sum(a == b for x, y in zip(outs[True], outs[False]) for a, b in zip(x, y))
+    assert same >= 0.9 * sum(len(x) for x in outs[True])

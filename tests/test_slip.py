@@ -23,6 +23,7 @@ def test_streaming_matches_resident_and_overlaps():
     for resident in (True, False):
         rn = build_runner(cfg, iter(recs), device="cuda", max_batch=8, max_model_len=256, num_blocks=128,
                           resident=resident)
+        rn._fused_ok = False        # same (separate-norm) decode chain as the streamed runner
         eng = Engine(cfg, rn, max_batch=8)
         outs.append(eng.generate_ids(prompts, sp))
         if not resident:
