@@ -142,12 +142,20 @@ class ModelConfig:
             rd = md.get(f"{arch}.rope.dimension_count")
             if rd:
                 prf = float(rd) / head_dim
+        extra = {}
+        pattern = md.get(f"{arch}.attention.sliding_window_pattern")
+        if sw and pattern and int(pattern) > 1:
+            # local (sliding) layers with every pattern-th layer global, the last one included
+            from .archs.hybrid import HybridAttentionRouter
+            extra["attention_layout"] = HybridAttentionRouter.gemma4(
+                n_layers, int(sw), int(pattern)).windows()
         return cls(n_layers=n_layers, n_heads=n_heads, n_kv_heads=n_kv, hidden_dim=hidden,
                    intermediate_dim=inter, vocab_size=int(vocab), rope_theta=rope,
                    context_length=ctx, rms_norm_eps=float(eps), head_dim=head_dim, arch=arch,
                    variant=variant, norm_type=norm, ffn_type=ffn,
                    sliding_window=int(sw) if sw else None, partial_rope_factor=prf,
-                   n_experts=n_exp, moe_top_k=top_k, eos_token_id=int(eos), bos_token_id=int(bos))
+                   n_experts=n_exp, moe_top_k=top_k, eos_token_id=int(eos), bos_token_id=int(bos),
+                   extra=extra)
 
     def gguf_metadata(self) -> dict[str, Any]:
         a = self.arch

@@ -100,6 +100,8 @@ class OracleModel:
 
     def __init__(self, cfg: ModelConfig, tensors: dict[str, tuple[torch.Tensor, GGMLType, tuple]]):
         self.cfg = cfg
+        from .archs.hybrid import layout_for_config
+        self.windows = layout_for_config(cfg).windows()
         self.t = tensors
 
         def lin(name):
@@ -200,7 +202,7 @@ class OracleModel:
                 v = torch.cat([self.v_cache[li][0], v], 0)
             self.k_cache[li] = k.unsqueeze(0)
             self.v_cache[li] = v.unsqueeze(0)
-            attn = attention_reference(q, k, v, causal=S > 1)
+            attn = attention_reference(q, k, v, causal=S > 1, window=self.windows[li])
             o = qmatmul(attn.reshape(S, nh * hd), L.wo[0], L.wo[1], L.wo[2]).to(x.dtype)
             x = x + o
             h = self.rms_norm(x, L.ffn_norm, cfg.rms_norm_eps).float()
@@ -263,7 +265,7 @@ def attention_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
     vv = v.float().repeat_interleave(rep, dim=1)
     s = torch.einsum("shd,thd->hst", q.float(), kk) * (1.0 / math.sqrt(D))
     vis = torch.ones(S, Skv, dtype=torch.bool)
-    if causal:
+    if causal or window > 0:
         i = torch.arange(S)[:, None]
         j = torch.arange(Skv)[None, :]
         vis = j <= i + (Skv - S)

@@ -90,6 +90,10 @@ class ModelRunner:
         self.counts = torch.zeros(max_seqs, self.V, dtype=torch.uint8, device=dev)
         self.step_ctr = torch.zeros(1, dtype=torch.int64, device=dev)
         self.qkv_dim = (self.nh + 2 * self.nkv) * self.hd
+        from ..models.archs.hybrid import layout_for_config
+        l0 = getattr(weights, "layer_range", (0, cfg.n_layers))[0]
+        # per-layer attention window (0 = whole context): sliding / global interleaving
+        self.layer_window = layout_for_config(cfg).windows()[l0:l0 + len(weights.layers)]
         B = max_batch
         kmax = max(self.H, self.Fp, self.nh * self.hd)
         f32, i8, bf16 = torch.float32, torch.int8, torch.bfloat16
@@ -277,7 +281,7 @@ class ModelRunner:
                                 block_size=self.block_size, n_splits=ns if gemv_path else max(2, ns),
                                 split_tokens=0, part_o=self.part_o, part_ml=self.part_ml,
                                 out_q=xq if gemv_path else None, out_ds=xds if gemv_path else None,
-                                err=self.err, window=cfg.sliding_window or 0,
+                                err=self.err, window=self.layer_window[li],
                                 out_bf16=None if gemv_path else self.attn_b[:B])
             if gemv_path:
                 self._row_parallel(lw.wo, xq, xds, B, x, peer)
@@ -332,7 +336,7 @@ class ModelRunner:
                                 n_rows=B, n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
                                 block_size=self.block_size, n_splits=ns, split_tokens=0,
                                 part_o=self.part_o, part_ml=self.part_ml, out_q=aq, out_ds=ads,
-                                err=self.err, window=cfg.sliding_window or 0)
+                                err=self.err, window=self.layer_window[li])
             ops.gemv(lw.wo, aq, ads, B, ops.EPI_RESIDUAL, resid=x, norm_w=lw.ffn_norm, out_q=xa, out_ds=xda,
                      ss_out=ss)
             ops.gemv(lw.w_gate, xa, xda, B, ops.EPI_SWIGLU, w2=lw.w_up, ld_out=self.Fp, out_q=hq, out_ds=hds,
@@ -488,7 +492,7 @@ class ModelRunner:
             ops.paged_attention(q, kv, block_tables, ctx, attn, n_rows=T, n_heads=self.nh,
                                 n_kv=self.nkv, head_dim=self.hd, block_size=self.block_size,
                                 row_seq=row_seq, n_splits=1, err=self.err,
-                                window=cfg.sliding_window or 0, tree_base=tree_base, tree_mask=tree_mask)
+                                window=self.layer_window[li], tree_base=tree_base, tree_mask=tree_mask)
             attn_b.copy_(attn)
             self._proj_into_residual(attn_b, lw.wo, x, o, tp)
             ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=xn)
