@@ -64,6 +64,8 @@ class Request:
     on_token: Callable | None = None
     grammar: object | None = None
     cached_tokens: int = 0        # prompt tokens served from the prefix cache
+    image_embeds: object | None = None   # [N, H] rows that replace the image placeholders
+    image_token_id: int = -1
 
     @property
     def num_tokens(self) -> int:
@@ -119,7 +121,10 @@ class Engine:
 
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt_ids: list[int], params: SamplingParams | None = None, *,
-                    priority: int = 0, on_token: Callable | None = None, grammar=None) -> int:
+                    priority: int = 0, on_token: Callable | None = None, grammar=None,
+                    image_embeds: torch.Tensor | None = None, image_token_id: int = -1) -> int:
+        """``image_embeds`` [N, H] (e.g. ``VisionEncoder.encode`` output in the language model's
+        hidden size) replace, in order, the N prompt tokens equal to ``image_token_id``."""
         params = params or SamplingParams()
         ids = list(prompt_ids)
         if self.add_bos and self.cfg.bos_token_id is not None:
@@ -127,7 +132,16 @@ class Engine:
         if self.runner is not None and len(ids) + params.max_tokens > self.runner.max_model_len:
             raise ValueError(f"prompt ({len(ids)}) + max_tokens ({params.max_tokens}) exceeds "
                              f"max_model_len {self.runner.max_model_len}")
-        r = Request(next(self._rid), ids, params, priority=priority, on_token=on_token, grammar=grammar)
+        if image_embeds is not None:
+            if self.runner is None:
+                raise ValueError("image inputs need a device engine")
+            n_ph = sum(1 for t in ids if t == image_token_id)
+            if n_ph != image_embeds.shape[0] or image_embeds.shape[-1] != self.runner.H:
+                raise ValueError(f"{n_ph} image placeholders for image embeddings of shape "
+                                 f"{tuple(image_embeds.shape)} (hidden {self.runner.H})")
+            image_embeds = image_embeds.to(self.runner.device, torch.float32)
+        r = Request(next(self._rid), ids, params, priority=priority, on_token=on_token, grammar=grammar,
+                    image_embeds=image_embeds, image_token_id=image_token_id)
         self.waiting.append(r)
         return r.rid
 
@@ -207,7 +221,7 @@ class Engine:
         while self.waiting and len(self.running) + len(admitted) < self.max_batch:
             r = self.waiting[0]
             hit, blocks = 0, []
-            if self.prefix_cache is not None:
+            if self.prefix_cache is not None and r.image_embeds is None:
                 # keep at least one prompt token to prefill (its logits give the first token)
                 hit, blocks = self.prefix_cache.longest_prefix_match(r.prompt_ids, len(r.prompt_ids) - 1)
             need = (len(r.prompt_ids) - hit + bs - 1) // bs + 1
@@ -296,7 +310,7 @@ class Engine:
             rn.reset_counts(r.slot, torch.tensor(r.prompt_ids, dtype=torch.int32))
         while pending:
             ids, pos, slots, rows, lasts, done = [], [], [], [], [], []
-            seq_list = []
+            seq_list, img_rows = [], []
             budget = self.max_prefill_tokens
             for i, r in enumerate(pending):
                 if budget <= 0:
@@ -306,6 +320,10 @@ class Engine:
                 if n <= 0:
                     continue
                 start = r.prefilled
+                if r.image_embeds is not None:
+                    ph = [p for p in range(start, start + n) if r.prompt_ids[p] == r.image_token_id]
+                    first = sum(1 for p in range(start) if r.prompt_ids[p] == r.image_token_id)
+                    img_rows.extend((len(ids) + p - start, r, first + k) for k, p in enumerate(ph))
                 sl = self.seqs.append(r.seq, n)
                 seq_list.append(r.seq)
                 ids.extend(r.prompt_ids[start:start + n])
@@ -321,8 +339,14 @@ class Engine:
             S = len(lasts)
             pr = [r for r in pending if r.seq in seq_list]
             sp = [pending[i].params for i in range(len(pending)) if pending[i].seq in seq_list]
+            ids_t = torch.tensor(ids, dtype=torch.int32, device=dev)
+            hidden_in = None
+            if img_rows:      # token embeddings with image placeholders replaced
+                hidden_in = rn.embed_ids(ids_t)
+                for row, r, k in img_rows:
+                    hidden_in[row] = r.image_embeds[k]
             toks, probs = rn.prefill(
-                torch.tensor(ids, dtype=torch.int32, device=dev),
+                ids_t,
                 torch.tensor(pos, dtype=torch.int32, device=dev),
                 torch.tensor(slots, dtype=torch.int64, device=dev),
                 torch.tensor(rows, dtype=torch.int32, device=dev),
@@ -333,12 +357,12 @@ class Engine:
                 torch.tensor([p.repetition_penalty for p in sp], dtype=torch.float32, device=dev),
                 torch.tensor([p.top_k for p in sp], dtype=torch.int32, device=dev),
                 torch.tensor([p.top_p for p in sp], dtype=torch.float32, device=dev),
-                mask=self._grammar_masks(pr, rn),
+                mask=self._grammar_masks(pr, rn), hidden_in=hidden_in,
             )
             toks_h = toks.tolist()
             for r, d, t in zip(pr, done, toks_h):
                 if d is not None:
-                    if self.prefix_cache is not None:
+                    if self.prefix_cache is not None and r.image_embeds is None:
                         # whole prompt blocks are complete and never written again
                         self.prefix_cache.insert(r.prompt_ids, self.seqs.block_table(r.seq))
                     self.running.append(r)

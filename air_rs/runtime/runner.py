@@ -541,6 +541,12 @@ class ModelRunner:
             ops.residual_add(x, o)
 
     # ------------------------------------------------------------------ misc
+    def embed_ids(self, ids: torch.Tensor) -> torch.Tensor:
+        """Token embeddings [T, H] fp32 (the rows prefill starts from)."""
+        out = torch.empty(ids.numel(), self.H, dtype=torch.float32, device=self.device)
+        ops.embed(self.w.embd, ids, out_f32=out, err=self.err, n=ids.numel())
+        return out
+
     def check_errors(self):
         peer = getattr(self.tp, "peer", None) if self.tp_size > 1 else None
         if peer is not None:
