@@ -72,8 +72,10 @@ def copy_kv_slots(kv: torch.Tensor, block_size: int, src: list[int], dst: list[i
 
 class SpeculativeDecoder:
     def __init__(self, target, draft, k: int = 4, top_k: int = DRAFT_TOP_K, tau: float = EXPAND_THRESHOLD,
-                 max_nodes: int = 32, eos_id: int | None = None):
-        """``target`` / ``draft``: ``air_rs.runtime.engine.Engine`` objects on the GPU."""
+                 max_nodes: int = 32, eos_id: int | None = None, adaptive: bool = False, k_max: int = 8):
+        """``target`` / ``draft``: ``air_rs.runtime.engine.Engine`` objects on the GPU.
+        ``adaptive``: the draft depth follows the measured acceptance (``AcceptanceTracker``:
+        longer drafts while most are accepted, shorter when they are not), within [1, k_max]."""
         if target.runner is None or (draft is not None and draft.runner is None):
             raise RuntimeError("speculative decoding needs GPU runners")
         self.t, self.d = target, draft
@@ -81,6 +83,11 @@ class SpeculativeDecoder:
         self.builder = Eagle2Builder(None, tau, top_k, max_depth=k + 1, max_nodes=min(max_nodes, MAX_TREE_NODES))
         self.eos_id = target.eos_id if eos_id is None else eos_id
         self.stats = SpecStats()
+        self.k_max = max(k, k_max)
+        self.tracker = None
+        if adaptive:
+            from .ghost import AcceptanceTracker
+            self.tracker = AcceptanceTracker(draft_k=k)
 
     # -- helpers ----------------------------------------------------------------
     def _forward(self, eng, rows, seq_ids, last_rows=None):
@@ -158,6 +165,10 @@ class SpeculativeDecoder:
 
     def _round(self, active: list[_Seq], max_tokens: int):
         t0 = time.perf_counter()
+        if self.tracker is not None and self.tracker.batch_count():
+            self.k = self.tracker.suggest_k(self.k_max)
+            self.tracker.draft_k = self.k
+            self.builder.max_depth = self.k + 1
         trees: list[DraftTree] = []
         for s in active:
             P = len(s.tokens) - 1
@@ -232,6 +243,9 @@ class SpeculativeDecoder:
             new_tokens = [tr.nodes[i].token_id for i in path[1:]] + [bonus]
             self.stats.drafted += len(tr.nodes) - 1
             self.stats.accepted += len(path) - 1
+            if self.tracker is not None:
+                depth = max((nd.depth for nd in tr.nodes), default=0)
+                self.tracker.report_batch(depth, len(path) - 1)
             # target: accepted nodes -> slots P .. P+len(path)-1
             src = [self.t.seqs.slot(s.t_seq, P + i) for i in path]
             self.t.seqs.truncate(s.t_seq, P + len(path))
