@@ -101,3 +101,26 @@ def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None
     runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=mml, tp=tp,
                           num_blocks=num_blocks, seed=seed, resident=resident, expert_slots=expert_slots)
     return Engine(cfg, runner, tok, max_batch=max_batch, **kw)
+
+
+def engine_from_hf(path: str, *, qtype=GGMLType.Q4_K, device=None, max_batch=64, max_model_len=None, tp=None,
+                   num_blocks=None, seed=0, tokenizer=None, **kw) -> Engine:
+    """Engine from a Hugging Face checkpoint directory (``config.json`` + safetensors or
+    ``.bin``), quantised on load to ``qtype`` (on the GPU when there is one)."""
+    import json
+    import os
+    from ..checkpoint.hf import hf_config, hf_records
+    d = path if os.path.isdir(path) else os.path.dirname(path)
+    cfg = hf_config(json.load(open(os.path.join(d, "config.json"))))
+    if device is None:
+        device = "cuda" if torch.cuda.is_available() else "cpu"
+    tok = tokenizer or Tokenizer.byte_vocab(cfg.vocab_size, cfg.bos_token_id, cfg.eos_token_id)
+    recs = hf_records(path, qtype, device=device, cfg=cfg)
+    if torch.device(device).type != "cuda":
+        from ..models.reference import OracleModel
+        t = {n: (r.cpu(), q, s) for n, r, q, s in recs}
+        return Engine(cfg, None, tok, oracle=OracleModel(cfg, t), **kw)
+    mml = max_model_len or min(cfg.context_length, 8192)
+    runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=mml, tp=tp,
+                          num_blocks=num_blocks, seed=seed)
+    return Engine(cfg, runner, tok, max_batch=max_batch, **kw)
