@@ -86,8 +86,10 @@ def random_engine(preset: str | ModelConfig = "tiny", qtype: GGMLType = GGMLType
 
 
 def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None, tp=None,
-                     num_blocks=None, seed=0, resident: bool = True, expert_slots: int | None = None,
+                     num_blocks=None, seed=0, resident: bool | str = True, expert_slots: int | None = None,
                      **kw) -> Engine:
+    """``resident="auto"``: keep everything in HBM when it fits under the VRAM cap, else
+    stream layers or serve MoE experts from host memory (``runtime.residency.plan_model``)."""
     g = read_gguf(path)
     cfg = ModelConfig.from_gguf_metadata(g.metadata)
     tok = Tokenizer.from_gguf_metadata(g.metadata)
@@ -97,9 +99,19 @@ def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None
         from ..models.reference import OracleModel
         return Engine(cfg, None, tok, oracle=OracleModel.from_gguf(g), **kw)
     mml = max_model_len or min(cfg.context_length, 8192)
+    stream_slots = 2
+    if resident == "auto":
+        # residency plan from the device size and the checkpoint's main weight format
+        from .residency import plan_model
+        qt = next((t.qtype for n, t in g.tensors.items() if n.endswith("attn_q.weight")), GGMLType.Q4_K)
+        total_mb = torch.cuda.get_device_properties(torch.device(device)).total_memory / 2**20
+        plan = plan_model(cfg, qt, total_mb)
+        resident, stream_slots = plan.resident, plan.stream_slots
+        expert_slots = expert_slots or plan.expert_slots
     recs = ((n, g.raw(n), t.qtype, t.torch_shape) for n, t in g.tensors.items())
     runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=mml, tp=tp,
-                          num_blocks=num_blocks, seed=seed, resident=resident, expert_slots=expert_slots)
+                          num_blocks=num_blocks, seed=seed, resident=resident, expert_slots=expert_slots,
+                          stream_slots=stream_slots)
     return Engine(cfg, runner, tok, max_batch=max_batch, **kw)
 
 
