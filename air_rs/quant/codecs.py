@@ -226,3 +226,127 @@ class IsoQuant:
 
     def reconstruct(self, q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
         return (q.float() * s) @ self.R
+
+
+# ---------------------------------------------------------------------------- alt-format detection
+def detect_alt_format(keys) -> str | None:
+    """'exl2' / 'gptq' / 'awq' from a checkpoint's tensor names (reference
+    src/alt_quant.rs detect_format)."""
+    ks = list(keys)
+    has = lambda s: any(s in k for k in ks)
+    if has("q_scale_max") or has("q_groups") or has("q_perm"):
+        return "exl2"
+    if has("qweight") and has("qzeros") and has("scales"):
+        return "gptq"
+    if has(".zeros") and has(".scales") and not has("qzeros"):
+        return "awq"
+    return None
+
+
+# ---------------------------------------------------------------------------- EXL2-style mixed width
+def exl2_pack(q: torch.Tensor, group_bits: list[int]) -> torch.Tensor:
+    """Pack codes q [K, N] (K = 32 * groups; group g holds ``group_bits[g]``-bit codes) into
+    per-column LSB-first uint32 bit streams [words, N]; a code never straddles two words."""
+    K, N = q.shape
+    words = []
+    for c in range(N):
+        stream, buf, used = [], 0, 0
+        for g, b in enumerate(group_bits):
+            for i in range(32):
+                if used + b > 32:
+                    stream.append(buf)
+                    buf, used = 0, 0
+                buf |= (int(q[g * 32 + i, c]) & ((1 << b) - 1)) << used
+                used += b
+        stream.append(buf)
+        words.append(stream)
+    n_words = max(len(w) for w in words)
+    out = torch.zeros(n_words, N, dtype=torch.int64)
+    for c, w in enumerate(words):
+        out[: len(w), c] = torch.tensor(w, dtype=torch.int64)
+    return out.to(torch.int32)
+
+
+def exl2_dequantize(q_weight: torch.Tensor, q_scale: torch.Tensor, q_scale_max: float, q_groups: torch.Tensor,
+                    q_perm: torch.Tensor | None = None) -> torch.Tensor:
+    """Mixed-bit-width groups of 32 rows (reference src/alt_quant.rs Exl2Layer::dequantize):
+    ``q_groups`` = [bits, start] pairs, group scale = q_scale[g, col] * q_scale_max / 256, value =
+    scale * (code - 2^(bits-1)); codes read per column from LSB-first uint32 streams (a code
+    never straddles two words); ``q_perm`` gives the original row of each stored row. The
+    reference broadcasts one column's codes to every column; each column has its own stream
+    here."""
+    groups = q_groups.reshape(-1, 2)[:, 0].tolist()
+    qw = q_weight.to(torch.int64) & 0xFFFFFFFF
+    N = qw.shape[1]
+    K = 32 * len(groups)
+    out = torch.empty(K, N)
+    word = torch.zeros(N, dtype=torch.int64)
+    wi, used = -1, 32
+    sc = q_scale.reshape(len(groups), -1).float() * (q_scale_max / 256.0)
+    for g, b in enumerate(groups):
+        center = float(1 << (b - 1))
+        mask = (1 << b) - 1
+        for i in range(32):
+            if used + b > 32:
+                wi += 1
+                word = qw[wi]
+                used = 0
+            code = (word >> used) & mask
+            used += b
+            out[g * 32 + i] = (code.float() - center) * (sc[g] if sc.shape[1] == N else sc[g, 0])
+    if q_perm is not None:
+        res = torch.empty_like(out)
+        res[q_perm.long()] = out
+        return res
+    return out
+
+
+# ---------------------------------------------------------------------------- Q4_0 tile reorders
+Q4_0_BLOCK = 18
+
+
+def q4_0_tiled_dequantize(raw: torch.Tensor, kind: str) -> torch.Tensor:
+    """Q4_0 blocks (f16 d + 16 bytes of nibbles, low nibble first) whose 32 codes are stored
+    in an ARM tile order (reference src/q4_tiled.rs): '4x4' transposes each 16-code half as a
+    4 x 4 tile; '4x8' and '8x8' keep row-major order. value = (code - 8) * d."""
+    b = raw.reshape(-1, Q4_0_BLOCK)
+    d = b[:, :2].contiguous().view(torch.float16).float()
+    nib = b[:, 2:].long()
+    codes = torch.stack([nib & 0xF, nib >> 4], -1).reshape(-1, 32)
+    if kind == "4x4":
+        codes = codes.reshape(-1, 2, 4, 4).transpose(-1, -2).reshape(-1, 32)
+    elif kind not in ("4x8", "8x8"):
+        raise ValueError(f"unknown Q4_0 tile kind {kind!r}")
+    return ((codes - 8).float() * d).reshape(-1)
+
+
+def q4_0_tile(raw: torch.Tensor, kind: str) -> torch.Tensor:
+    """Inverse of the '4x4' reorder (for tests / writers); other kinds are unchanged."""
+    if kind != "4x4":
+        return raw.clone()
+    b = raw.reshape(-1, Q4_0_BLOCK).clone()
+    nib = b[:, 2:].long()
+    codes = torch.stack([nib & 0xF, nib >> 4], -1).reshape(-1, 2, 4, 4).transpose(-1, -2).reshape(-1, 16, 2)
+    b[:, 2:] = (codes[..., 0] | (codes[..., 1] << 4)).to(torch.uint8)
+    return b.reshape(-1)
+
+
+# ---------------------------------------------------------------------------- PrismML Q1_0 / Q2_0
+def prism_q1_0_dequantize(raw: torch.Tensor) -> torch.Tensor:
+    """128-weight blocks of f16 d + 16 bytes of sign bits (LSB first): +d for 1, -d for 0."""
+    if raw.numel() % 18:
+        raise ValueError("Q1_0 data is not a whole number of 18-byte blocks")
+    b = raw.reshape(-1, 18)
+    d = b[:, :2].contiguous().view(torch.float16).float()
+    bits = (b[:, 2:, None].long() >> torch.arange(8)) & 1
+    return (d * (bits.reshape(-1, 128).float() * 2 - 1)).reshape(-1)
+
+
+def prism_q2_0_dequantize(raw: torch.Tensor) -> torch.Tensor:
+    """128-weight blocks of f16 d + 32 bytes of 2-bit codes (LSB first): (code - 1) * d."""
+    if raw.numel() % 34:
+        raise ValueError("Q2_0 data is not a whole number of 34-byte blocks")
+    b = raw.reshape(-1, 34)
+    d = b[:, :2].contiguous().view(torch.float16).float()
+    codes = (b[:, 2:, None].long() >> (2 * torch.arange(4))) & 3
+    return (d * (codes.reshape(-1, 128).float() - 1)).reshape(-1)
