@@ -36,7 +36,7 @@ def test_qjl_similarity_estimate():
     d, m = 128, 1024
     R = qjl_projection_matrix(m, d, seed=1)
     q = torch.randn(d, generator=g)
-    k = torch.stack([q, -q, torch.randn(d, generator=g), q + 0.3 * torch.randn(d, generator=g)])
+    k = torch.stack([q, -q, torch.randn(d, generator=g), 0.5 * q + 0.1 * torch.randn(d, generator=g)])
     c = QjlKeys.compress(k, R)
     est = c.approx_cos_sim(QjlKeys.query_bits(q[None], R)[0])
     true = torch.nn.functional.cosine_similarity(k, q[None])
