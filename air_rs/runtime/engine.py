@@ -82,8 +82,11 @@ class Engine:
                  max_batch: int = 64, prefill_chunk: int = 512, max_prefill_tokens: int = 8192,
                  add_bos: bool = True, eos_id: int | None = None, prefix_cache: bool = False,
                  prefix_cache_blocks: int | None = None, kv_swap: bool = True,
-                 cuda_graph_batch_sizes: tuple[int, ...] = BUCKETS):
+                 cuda_graph_batch_sizes: tuple[int, ...] = BUCKETS, pressure_control: bool = False):
+        """``pressure_control``: evaluate KV-pool pressure every step and act on it (prefix-cache
+        eviction from Orange, no admissions from Red, preemption at Critical)."""
         self.cfg = cfg
+        self.admit_paused = False
         self.buckets = tuple(sorted(cuda_graph_batch_sizes))
         self.runner = runner
         self.oracle = oracle
@@ -118,6 +121,10 @@ class Engine:
         self.swapped: list[Request] = []      # preempted (KV in host memory), resumed first
         if runner is None:
             self.prefix_cache = self.swap = None
+        self.pressure = None
+        if pressure_control and runner is not None:
+            from .pressure import KvPressureController
+            self.pressure = KvPressureController(self)
 
     # ------------------------------------------------------------------ requests
     def add_request(self, prompt_ids: list[int], params: SamplingParams | None = None, *,
@@ -210,6 +217,10 @@ class Engine:
     def _admit(self) -> list[Request]:
         """Admit waiting requests while batch slots / KV blocks / token budget allow."""
         admitted = []
+        if self.pressure is not None:
+            self.pressure.tick()
+        if self.admit_paused:
+            return admitted
         budget = self.max_prefill_tokens
         alloc = self.seqs.allocator
         bs = self.runner.block_size
@@ -287,8 +298,23 @@ class Engine:
             self.metrics.preemptions = getattr(self.metrics, "preemptions", 0) + 1
         return batch
 
+    def preempt_latest(self) -> bool:
+        """Swap the most recently admitted running request out to host memory."""
+        if self.swap is None or not self.running:
+            return False
+        victim = self.running[-1]
+        if victim.seq < 0 or self.seqs.is_swapped(victim.seq):
+            return False
+        self.swap.evict(victim.seq)
+        self.running.remove(victim)
+        self.swapped.append(victim)
+        self.metrics.preemptions = getattr(self.metrics, "preemptions", 0) + 1
+        return True
+
     def _resume_swapped(self):
         """Bring preempted sequences back (oldest first) while their blocks + one fit."""
+        if self.admit_paused:
+            return
         alloc = self.seqs.allocator
         bs = self.runner.block_size
         while self.swapped and len(self.running) < self.max_batch:
