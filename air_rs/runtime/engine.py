@@ -82,11 +82,13 @@ class Engine:
                  max_batch: int = 64, prefill_chunk: int = 512, max_prefill_tokens: int = 8192,
                  add_bos: bool = True, eos_id: int | None = None, prefix_cache: bool = False,
                  prefix_cache_blocks: int | None = None, kv_swap: bool = True,
-                 cuda_graph_batch_sizes: tuple[int, ...] = BUCKETS, pressure_control: bool = False):
+                 cuda_graph_batch_sizes: tuple[int, ...] = BUCKETS, pressure_control: bool = False,
+                 secure_kv: bool = False):
         """``pressure_control``: evaluate KV-pool pressure every step and act on it (prefix-cache
         eviction from Orange, no admissions from Red, preemption at Critical)."""
         self.cfg = cfg
         self.admit_paused = False
+        self.secure_kv = secure_kv        # zero the KV blocks a finished request frees
         self.buckets = tuple(sorted(cuda_graph_batch_sizes))
         self.runner = runner
         self.oracle = oracle
@@ -182,6 +184,11 @@ class Engine:
             self._deferred.append((r.seq, r.slot))
         else:
             if self.seqs is not None and r.seq >= 0:
+                if self.secure_kv and not self.seqs.is_swapped(r.seq):
+                    from ..utils.security import zero_kv_blocks
+                    alloc = self.seqs.allocator
+                    zero_kv_blocks(self.runner.kv, [b for b in self.seqs.block_table(r.seq)
+                                                    if alloc.ref_count(b) == 1])
                 self.seqs.free_sequence(r.seq)
             if r.slot >= 0:
                 self.free_slots.append(r.slot)
