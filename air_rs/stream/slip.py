@@ -52,7 +52,10 @@ class StreamStats:
     bytes_h2d: int = 0
     copy_ms: float = 0.0
     compute_ms: float = 0.0
+    underruns: int = 0           # layers whose compute waited for their copy
+    stall_ms: float = 0.0        # compute-stream idle time spent waiting on copies
     _pending: list = field(default_factory=list)
+    _last_end: object = None
 
     def overlap_ratio(self, step_ms: float) -> float:
         """Fraction of the shorter of (copy, compute) hidden under the other."""
@@ -133,14 +136,25 @@ class LayerStreamer:
         if st is not None:
             self.stats._pending.append(("compute", st, ev))
 
+    UNDERRUN_MS = 0.02
+
     def collect(self):
-        """Fold finished event pairs into the copy / compute totals (synchronises them)."""
-        for kind, a, b in self.stats._pending:
+        """Fold finished event pairs into the copy / compute totals (synchronises them). A gap
+        between one layer's compute end and the next layer's compute start is time the compute
+        stream spent waiting for a copy (a slot underrun)."""
+        st = self.stats
+        for kind, a, b in st._pending:
             b.synchronize()
             ms = a.elapsed_time(b)
             if kind == "copy":
-                self.stats.copy_ms += ms
+                st.copy_ms += ms
             else:
-                self.stats.compute_ms += ms
-        self.stats._pending.clear()
-        return self.stats
+                st.compute_ms += ms
+                if st._last_end is not None:
+                    gap = st._last_end.elapsed_time(a)
+                    if gap > self.UNDERRUN_MS:
+                        st.underruns += 1
+                        st.stall_ms += gap
+                st._last_end = b
+        st._pending.clear()
+        return st

@@ -32,4 +32,5 @@ def test_streaming_matches_resident_and_overlaps():
             per_layer = sum(t.numel() * t.element_size() for t in rn.streamer.slot_tensors[0])
             assert st.layers_loaded >= cfg.n_layers and st.bytes_h2d == st.layers_loaded * per_layer
             assert st.copy_ms > 0 and st.compute_ms > 0
+            assert st.underruns >= 0 and st.stall_ms >= 0.0
     assert outs[0] == outs[1]
