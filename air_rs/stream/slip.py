@@ -134,7 +134,8 @@ class LayerStreamer:
         self.free[s] = ev
         st = self._compute_start.pop(li, None)
         if st is not None:
-            self.stats._pending.append(("compute", st, ev))
+            # the first layer of a step follows host work (sampling, scheduling): no gap check
+            self.stats._pending.append(("compute0" if li == 0 else "compute", st, ev))
 
     UNDERRUN_MS = 0.02
 
@@ -150,7 +151,7 @@ class LayerStreamer:
                 st.copy_ms += ms
             else:
                 st.compute_ms += ms
-                if st._last_end is not None:
+                if kind == "compute" and st._last_end is not None:
                     gap = st._last_end.elapsed_time(a)
                     if gap > self.UNDERRUN_MS:
                         st.underruns += 1
