@@ -91,6 +91,8 @@ def build_parser() -> argparse.ArgumentParser:
     i = sub.add_parser("info", help="Print model metadata")
     i.add_argument("-m", "--model", required=True)
 
+    dr = sub.add_parser("doctor", help="Report GPUs, driver / CUDA / NCCL, native extension and host")
+    dr.add_argument("--path", default=".", help="Directory whose free disk space to report")
     pl = sub.add_parser("pull", help="Download a GGUF into the local registry")
     pl.add_argument("repo_id")
     pl.add_argument("filename")
@@ -260,6 +262,12 @@ def cmd_info(args) -> int:
     return 0
 
 
+def cmd_doctor(args) -> int:
+    from .utils.backend import detect
+    print(detect(args.path).summary())
+    return 0
+
+
 def main(argv: list[str] | None = None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     # README shortcuts: --run <model> "prompt" / --serve <model> / --interactive <model>
@@ -296,7 +304,7 @@ def _dispatch(args) -> int:
         print(pull(args.repo_id, args.filename, args.alias, args.sha256))
         return 0
     return {"generate": cmd_generate, "serve": cmd_serve, "bench": cmd_bench, "info": cmd_info,
-            "mcp": cmd_mcp}[args.cmd](args)
+            "mcp": cmd_mcp, "doctor": cmd_doctor}[args.cmd](args)
 
 
 if __name__ == "__main__":
