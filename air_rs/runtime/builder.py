@@ -47,7 +47,8 @@ def plan_kv_blocks(cfg: ModelConfig, weights_bytes: int, *, block_size: int, dev
 def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_model_len=4096,
                  block_size=16, num_blocks=None, tp=None, seed=0, max_seqs=None,
                  resident: bool = True, stream_slots: int = 2, kv_alloc=None,
-                 layer_range: tuple[int, int] | None = None, expert_slots: int | None = None) -> ModelRunner:
+                 layer_range: tuple[int, int] | None = None, expert_slots: int | None = None,
+                 resident_layers: int = 0) -> ModelRunner:
     """``resident=False``: per-layer weights stay in pinned host memory and are streamed
     through ``stream_slots`` device slots each forward (S.L.I.P. streaming mode).
     ``expert_slots``: MoE experts stay in pinned host memory and at most this many are
@@ -57,7 +58,8 @@ def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_
     w = LlamaWeights(cfg, records, device, tp_rank=tp_rank, tp_size=tp_size,
                      layer_device=None if resident else "cpu", layer_range=layer_range,
                      expert_device="cpu" if expert_slots else None)
-    streamed = 0 if resident else stream_slots * max(1, w.nbytes() - w.resident_nbytes()) // cfg.n_layers
+    per_layer = max(1, w.nbytes() - w.resident_nbytes()) // max(1, len(w.layers))
+    streamed = 0 if resident else (stream_slots + resident_layers) * per_layer
     if expert_slots:
         l0 = w.layers[0]
         streamed += expert_slots * (l0.experts_gu[0].nbytes + l0.experts_down[0].nbytes)
@@ -67,7 +69,7 @@ def build_runner(cfg: ModelConfig, records, *, device="cuda", max_batch=64, max_
                      max_model_len=max_model_len, device=device, tp=tp, seed=seed,
                      max_seqs=max_seqs or max(2 * max_batch + 1, 64), kv_alloc=kv_alloc)
     if not resident:
-        rn.enable_streaming(stream_slots)
+        rn.enable_streaming(stream_slots, resident_layers)
     if expert_slots:
         rn.enable_expert_cache(expert_slots)
     return rn

@@ -156,10 +156,11 @@ class ModelRunner:
         self.graphs.clear()
         return self.expert_cache
 
-    def enable_streaming(self, n_slots: int = 2):
-        """Stream host-resident layers through ``n_slots`` device slots (S.L.I.P.)."""
+    def enable_streaming(self, n_slots: int = 2, resident_layers: int = 0):
+        """Stream host-resident layers through ``n_slots`` device slots (S.L.I.P.); the first
+        ``resident_layers`` layers are copied to the device once and stay there."""
         from ..stream.slip import LayerStreamer
-        self.streamer = LayerStreamer(self.w.layers, self.device, n_slots)
+        self.streamer = LayerStreamer(self.w.layers, self.device, n_slots, resident=range(resident_layers))
         return self.streamer
 
     # ------------------------------------------------------------------ inputs

@@ -66,12 +66,23 @@ class StreamStats:
 
 
 class LayerStreamer:
-    def __init__(self, host_layers: list[LayerWeights], device, n_slots: int = 2, timing: bool = True):
+    def __init__(self, host_layers: list[LayerWeights], device, n_slots: int = 2, timing: bool = True,
+                 resident=()):
+        """``resident``: layer indices copied to the device once and kept there (partial
+        residency); the other layers cycle through the ``n_slots`` streaming slots."""
         if n_slots < 2:
             raise ValueError("layer streaming needs at least two device slots")
         self.host = host_layers
         self.device = torch.device(device)
         self.n = n_slots
+        self.resident: dict[int, LayerWeights] = {}
+        for li in sorted(set(resident)):
+            lw = _device_clone(host_layers[li], self.device)
+            for dst, src in zip(layer_tensors(lw), layer_tensors(host_layers[li])):
+                dst.copy_(src)
+            self.resident[li] = lw
+        self.streamed = [li for li in range(len(host_layers)) if li not in self.resident]
+        self._pos = {li: i for i, li in enumerate(self.streamed)}
         self.slots = [_device_clone(host_layers[0], self.device) for _ in range(n_slots)]
         self.slot_tensors = [layer_tensors(s) for s in self.slots]
         self.copy_stream = torch.cuda.Stream(self.device)
@@ -83,11 +94,19 @@ class LayerStreamer:
         self._compute_start: dict[int, torch.cuda.Event] = {}
 
     def _slot(self, li: int) -> int:
-        return li % self.n
+        return self._pos[li] % self.n
+
+    def _next_streamed(self, li: int) -> int:
+        """The first streamed layer after li (wrapping to the next step)."""
+        for d in range(1, len(self.host) + 1):
+            nxt = (li + d) % len(self.host)
+            if nxt not in self.resident:
+                return nxt
+        return -1
 
     def prefetch(self, li: int):
         """Issue the host->device copy of layer li into its slot (no-op if already there)."""
-        if li < 0 or li >= len(self.host):
+        if li < 0 or li >= len(self.host) or li in self.resident:
             return
         s = self._slot(li)
         if self.loaded[s] == li:
@@ -112,14 +131,18 @@ class LayerStreamer:
             self.stats._pending.append(("copy", t0, ev))
 
     def get(self, li: int) -> LayerWeights:
-        """Layer li on the device for the compute stream; starts fetching layer li+1."""
+        """Layer li on the device for the compute stream; starts fetching the next streamed
+        layer."""
+        if li in self.resident:
+            self.prefetch(self._next_streamed(li))
+            return self.resident[li]
         self.prefetch(li)
         s = self._slot(li)
         cs = torch.cuda.current_stream(self.device)
         cs.wait_event(self.ready[s])
-        # the next layer's slot is free once the layer that used it last (li+1-n) is done;
-        # after the last layer this starts layer 0 of the next step
-        self.prefetch((li + 1) % len(self.host))
+        # the next streamed layer's slot is free once the layer that used it last is done;
+        # after the last layer this starts the first streamed layer of the next step
+        self.prefetch(self._next_streamed(li))
         if self.timing:
             e = torch.cuda.Event(enable_timing=True)
             e.record(cs)
@@ -128,6 +151,8 @@ class LayerStreamer:
 
     def release(self, li: int):
         """Record that the compute stream has enqueued every kernel reading layer li."""
+        if li in self.resident:
+            return
         s = self._slot(li)
         ev = torch.cuda.Event(enable_timing=self.timing)
         ev.record(torch.cuda.current_stream(self.device))
