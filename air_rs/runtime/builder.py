@@ -101,7 +101,7 @@ def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None
         from ..models.reference import OracleModel
         return Engine(cfg, None, tok, oracle=OracleModel.from_gguf(g), **kw)
     mml = max_model_len or min(cfg.context_length, 8192)
-    stream_slots = 2
+    stream_slots, resident_layers = 2, 0
     if resident == "auto":
         # residency plan from the device size and the checkpoint's main weight format
         from .residency import plan_model
@@ -110,10 +110,11 @@ def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None
         plan = plan_model(cfg, qt, total_mb)
         resident, stream_slots = plan.resident, plan.stream_slots
         expert_slots = expert_slots or plan.expert_slots
+        resident_layers = plan.resident_layers
     recs = ((n, g.raw(n), t.qtype, t.torch_shape) for n, t in g.tensors.items())
     runner = build_runner(cfg, recs, device=device, max_batch=max_batch, max_model_len=mml, tp=tp,
                           num_blocks=num_blocks, seed=seed, resident=resident, expert_slots=expert_slots,
-                          stream_slots=stream_slots)
+                          stream_slots=stream_slots, resident_layers=resident_layers)
     return Engine(cfg, runner, tok, max_batch=max_batch, **kw)
 
 

@@ -135,6 +135,7 @@ class BuildPlan:
     dense_mb: float
     cap_mb: float
     note: str
+    resident_layers: int = 0          # streamed models: leading layers kept on the device
 
 
 def plan_model(cfg, qtype: GGMLType, total_memory_mb: float, kv_mb: float = KV_HOT_TIER_MB,
@@ -159,5 +160,8 @@ def plan_model(cfg, qtype: GGMLType, total_memory_mb: float, kv_mb: float = KV_H
             return BuildPlan(True, 2, slots, total, dense, cap,
                              f"dense layers resident, {slots} of {L * n_exp} experts in device slots")
     layer = (attn + ffn_one * n_exp) / 2**20
-    slots = max(2, min(8, int((room - 2 * V * H * bpw / 2**20) // max(layer, 1e-9))))
-    return BuildPlan(False, slots, None, total, dense, cap, f"layers streamed through {slots} device slots")
+    fit = int((room - 2 * V * H * bpw / 2**20) // max(layer, 1e-9))     # layers that fit on the device
+    slots = 2
+    keep = max(0, min(L - 1, fit - slots))
+    return BuildPlan(False, slots, None, total, dense, cap,
+                     f"{keep} layers resident, {L - keep} streamed through {slots} device slots", keep)
