@@ -1,0 +1,57 @@
+"""Residency scoring, priority I/O engine and residency scheduler (reference
+src/strix/score.rs, io_engine.rs, scheduler.rs tests)."""
+import math
+import os
+
+import pytest
+import torch
+
+from air_rs.stream import strix as S
+
+
+def test_score_components():
+    assert S.urgency(0, 3) > 0.9 and abs(S.urgency(3, 3) - 0.5) < 0.01 and S.urgency(10, 3) < 0.01
+    assert S.urgency(0, 0) == 1.0 and S.urgency(1, 0) == 0.0
+    assert S.predictive(5, 5) == 1.0 and abs(S.predictive(0, 10, 0.1) - math.exp(-1)) < 1e-9
+    assert S.sticky(0) == 0.0 and abs(S.sticky(20) - 1.0) < 1e-9 and 0 < S.sticky(3) < 1
+    assert S.cost(50, 100) == 0.5 and S.cost(500, 100) == 1.0 and S.cost(1, 0) == 0.0
+    w = S.ScoreWeights()
+    assert abs(w.sum() - 1.0) < 1e-9 and S.residency_score(w, 1, 1, 1, 1) == 1.0
+    assert S.IoPriority.from_class(S.TensorClass.A, False) == S.IoPriority.CRITICAL
+    assert S.IoPriority.from_class(S.TensorClass.C, True) == S.IoPriority.HIGH
+    assert S.IoPriority.from_class(S.TensorClass.D, True) == S.IoPriority.LOW
+
+
+def test_io_engine_reads_in_priority_order(tmp_path):
+    p = tmp_path / "blob.bin"
+    data = os.urandom(1 << 16)
+    p.write_bytes(data)
+    eng = S.IoEngine(str(p), capacity=1, workers=1, pin=False, start_paused=True)
+    try:
+        eng.submit(S.IoRequest("first", 0, 4096, S.IoPriority.NORMAL))
+        eng.submit(S.IoRequest("low", 8192, 100, S.IoPriority.LOW))
+        eng.submit(S.IoRequest("crit", 100, 1000, S.IoPriority.CRITICAL))
+        eng.submit(S.IoRequest("bad", len(data) - 10, 100, S.IoPriority.HIGH))
+        assert eng.queued_count() == 4
+        eng.resume()
+        done = eng.wait_all()
+    finally:
+        eng.close()
+    by = {c.tensor_id: c for c in done}
+    assert bytes(by["crit"].data.numpy()) == data[100:1100] and bytes(by["low"].data.numpy()) == data[8192:8292]
+    assert by["bad"].error is not None and by["crit"].error is None
+    order = [c.tensor_id for c in done]
+    assert order == ["crit", "bad", "first", "low"]
+
+
+def test_residency_scheduler_budget_and_window():
+    sch = S.ResidencyScheduler(budget_bytes=300, prefetch_window=1)
+    sch.register(S.TrackedTensor("embd", 100, S.TensorClass.A))
+    for i in range(4):
+        sch.register(S.TrackedTensor(f"l{i}", 100, S.TensorClass.B, layer=i))
+    load, evict = sch.tick(current_layer=0, n_layers=4)
+    assert "embd" in load and {"l0", "l1"} <= set(load) and not evict
+    load, evict = sch.tick(current_layer=2, n_layers=4)
+    assert {"l2", "l3"} & set(load) and evict and sch.tensors[evict[0]].evictions == 1
+    resident = [t.tensor_id for t in sch.tensors.values() if t.resident]
+    assert "embd" in resident and sum(sch.tensors[t].size for t in resident if t != "embd") <= 300
