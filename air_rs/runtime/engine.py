@@ -88,6 +88,7 @@ class Engine:
         eviction from Orange, no admissions from Red, preemption at Critical)."""
         self.cfg = cfg
         self.admit_paused = False
+        self.decode_ms_last = self.decode_ms_ema = None
         self.secure_kv = secure_kv        # zero the KV blocks a finished request frees
         self.buckets = tuple(sorted(cuda_graph_batch_sizes))
         self.runner = runner
@@ -304,6 +305,36 @@ class Engine:
             batch = batch[:-1]
             self.metrics.preemptions = getattr(self.metrics, "preemptions", 0) + 1
         return batch
+
+    def _timing_event(self, i: int):
+        ev = getattr(self, "_tev", None)
+        if ev is None:
+            ev = self._tev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        return ev[i]
+
+    def stats(self) -> dict:
+        """Gauges for monitoring: queue sizes, KV pool use, prefix cache, preemptions, pressure,
+        device time of the last / average decode step, collective bytes per step."""
+        out = {"running": len(self.running), "waiting": len(self.waiting), "swapped": len(self.swapped),
+               "decode_steps": self.step_count, "preemptions": getattr(self.metrics, "preemptions", 0)}
+        if self.runner is None:
+            return out
+        alloc = self.seqs.allocator
+        out.update(kv_blocks_total=alloc.total_blocks(), kv_blocks_used=alloc.num_used_blocks(),
+                   kv_utilization=alloc.num_used_blocks() / max(1, alloc.total_blocks()))
+        if self.prefix_cache is not None:
+            st = self.prefix_cache.stats()
+            out.update(prefix_cache_hit_rate=st.hit_rate, prefix_cache_blocks=st.cached_blocks,
+                       prefix_cache_hit_tokens=st.hit_tokens)
+        if self.pressure is not None:
+            out["kv_pressure_level"] = int(self.pressure.level)
+        if self.decode_ms_ema is not None:
+            out.update(decode_step_device_ms=self.decode_ms_last, decode_step_device_ms_avg=self.decode_ms_ema)
+        rn = self.runner
+        if rn.tp_size > 1:
+            # row-parallel partials cross the links twice per layer (attention output, FFN down)
+            out["tp_collective_bytes_per_row"] = 2 * len(rn.w.layers) * rn.H * 4 * (rn.tp_size - 1)
+        return out
 
     def preempt_latest(self) -> bool:
         """Swap the most recently admitted running request out to host memory."""
@@ -547,8 +578,16 @@ class Engine:
             return produced
         batch = self._make_room(batch)
         with trace.span("decode"):
+            t0 = self._timing_event(0)
+            t0.record()
             B, p, ev = self._launch_decode(batch)
+            t1 = self._timing_event(1)
+            t1.record()
             ev.synchronize()
+            t1.synchronize()
+            ms = t0.elapsed_time(t1)
+            self.decode_ms_last = ms
+            self.decode_ms_ema = ms if self.decode_ms_ema is None else 0.9 * self.decode_ms_ema + 0.1 * ms
         with trace.span("emit"):
             toks = p["tok"][:len(batch)].tolist()
             for r, t in zip(batch, toks):

@@ -264,7 +264,9 @@ def create_app(dispatcher: Dispatcher, model_name: str = "air-rs", *, api_keys: 
                 "requests_served": state["served"]}
 
     async def prometheus():
-        return PlainTextResponse(metrics.render(model_name), media_type="text/plain; version=0.0.4")
+        eng = getattr(dispatcher, "engine", None)
+        gauges = eng.stats() if eng is not None and hasattr(eng, "stats") else None
+        return PlainTextResponse(metrics.render(model_name, gauges), media_type="text/plain; version=0.0.4")
 
     for prefix in ("/v1", ""):
         app.add_api_route(prefix + "/chat/completions", chat_completions, methods=["POST"])

@@ -169,7 +169,8 @@ class PrometheusMetrics:
     latency: LatencyHistogram = field(default_factory=LatencyHistogram)
     start_time: float = field(default_factory=time.time)
 
-    def render(self, model: str = "air-rs") -> str:
+    def render(self, model: str = "air-rs", gauges: dict | None = None) -> str:
+        """Prometheus text; ``gauges`` (engine statistics) are exported as ``air_<name>``."""
         lines = []
 
         def metric(name, kind, help_, value):
@@ -195,4 +196,7 @@ class PrometheusMetrics:
             lines.append(f'{hname}_count{{model="{model}"}} {h.count}')
             for q in (50, 95, 99):
                 lines.append(f'{hname}_p{q}{{model="{model}"}} {h.percentile(q):.3f}')
+        for k, v in sorted((gauges or {}).items()):
+            if isinstance(v, (int, float)) and not isinstance(v, bool):
+                metric(f"air_{k}", "gauge", f"engine {k.replace('_', ' ')}", v)
         return "\n".join(lines) + "\n"

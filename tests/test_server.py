@@ -65,6 +65,13 @@ def test_embeddings_responses_health_metrics(client):
     assert "air_requests_total" in m and "air_ttft_ms_bucket" in m
 
 
+def test_metrics_export_engine_gauges():
+    from air_rs.serve.openai import PrometheusMetrics
+    text = PrometheusMetrics().render("m", {"kv_utilization": 0.25, "running": 3, "flag": True, "name": "x"})
+    assert 'air_kv_utilization{model="m"} 0.25' in text and 'air_running{model="m"} 3' in text
+    assert "air_flag" not in text and "air_name" not in text
+
+
 def test_auth_and_rate_limit():
     c = TestClient(create_app(MockDispatcher("mock"), "mock", api_keys=["sk-1"], rate_limit=(0.0001, 2)))
     body = {"prompt": "x"}
