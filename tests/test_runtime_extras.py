@@ -230,6 +230,8 @@ def test_engine_snapshot_restore_hits_prefix_cache(tmp_path):
     rid = eng.add_request(prompt, SamplingParams(max_tokens=40, temperature=0.0, ignore_eos=True))
     for _ in range(5):
         eng.step()
+    st = eng.stats()
+    assert st["decode_step_device_ms"] > 0 and st["kv_blocks_used"] > 0 and st["running"] == 1
     info = eng.snapshot_request(rid, tmp_path / "r.kv")
     assert info.n_blocks >= 4
     ref = eng.generate_ids([prompt], SamplingParams(max_tokens=6, temperature=0.0, ignore_eos=True))
