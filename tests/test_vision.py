@@ -86,7 +86,8 @@ def test_engine_image_embeddings_replace_placeholders():
     with_ph = [11, ph, ph, 14, 15, ph, 17, 18]
     sub = torch.tensor([12, 13, 16], dtype=torch.int32, device=rn.device)
     img = rn.embed_ids(sub)
-    sp = SamplingParams(max_tokens=8, temperature=0.0, ignore_eos=True)
+    # no repetition penalty: the placeholder ids would count as different past tokens
+    sp = SamplingParams(max_tokens=8, temperature=0.0, repetition_penalty=1.0, ignore_eos=True)
     ref = eng.generate_ids([text], sp)[0]
     rid = eng.add_request(with_ph, sp, image_embeds=img, image_token_id=ph)
     while eng.has_unfinished():
