@@ -292,3 +292,18 @@ def rope_table(max_pos: int, rot_dim: int, theta: float, device) -> torch.Tensor
                           torch.arange(0, rot_dim, 2, dtype=torch.float32) / rot_dim)
     ang = torch.arange(max_pos, dtype=torch.float32)[:, None] * inv[None, :]
     return torch.stack([torch.cos(ang), torch.sin(ang)], -1).contiguous().to(device)
+
+
+def gated_delta(q, k, v, alpha, beta, state=None):
+    """Gated delta rule over a sequence on the GPU: q, k [BH, L, dk] (k L2-normalised), v
+    [BH, L, dv], alpha, beta [BH, L]; ``state`` [BH, dv, dk] is the initial state (zeros when
+    None) and is updated in place. Returns (out [BH, L, dv], state)."""
+    BH, L, dk = q.shape
+    dv = v.shape[-1]
+    if state is None:
+        state = torch.zeros(BH, dv, dk, dtype=torch.float32, device=q.device)
+    out = torch.empty(BH, L, dv, dtype=torch.float32, device=q.device)
+    f = lambda t: t.float().contiguous()
+    require_ext().gated_delta(f(q), f(k), f(v), f(alpha), f(beta), state, out)
+    count_launch()
+    return out, state

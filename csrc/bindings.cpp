@@ -17,6 +17,7 @@
 void register_gemm_tc(pybind11::module_& m);
 void register_comm(pybind11::module_& m);
 void register_kv_push(pybind11::module_& m);
+void register_ssm(pybind11::module_& m);
 air::PeerPush peer_push_from_meta(const at::Tensor& meta);
 
 using at::Tensor;
@@ -317,5 +318,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("residual_add", &residual_add);
   register_gemm_tc(m);
   register_kv_push(m);
+  register_ssm(m);
   register_comm(m);
 }

@@ -2,6 +2,8 @@
 mamba.rs, rwkv.rs, gated_deltanet.rs, yarn.rs, gemma4.rs, ops.rs variants)."""
 import math
 
+import pytest
+
 import torch
 
 from air_rs.models.archs import gemma, mla, rope_ext as R, ssm
@@ -100,3 +102,28 @@ def test_gemma_ops():
     assert ids.tolist() == [[1, 3]] and abs(float(wt.sum()) - 1) < 1e-6
     eo = torch.arange(8.0).reshape(1, 4, 2)
     torch.testing.assert_close(gemma.moe_weighted_sum(eo, ids, wt), (wt[0, 0] * eo[0, 1] + wt[0, 1] * eo[0, 3])[None])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dk,dv", [(128, 64), (64, 128), (128, 8)])
+def test_gated_delta_cuda_kernel_matches_reference(dk, dv):
+    """The sm_100a recurrence kernel against the PyTorch restatement, including a state carried
+    across two calls."""
+    from air_rs import ops
+    g = torch.Generator().manual_seed(dk + dv)
+    BH, L = 3, 37
+    q = torch.randn(BH, L, dk, generator=g)
+    k = torch.nn.functional.normalize(torch.randn(BH, L, dk, generator=g), dim=-1)
+    v = torch.randn(BH, L, dv, generator=g)
+    a = torch.rand(BH, L, generator=g) * 0.5 + 0.5
+    b = torch.rand(BH, L, generator=g)
+    dev = "cuda"
+    out, st = ops.gated_delta(q.to(dev), k.to(dev), v.to(dev), a.to(dev), b.to(dev))
+    o1, s1 = ops.gated_delta(q[:, :20].to(dev), k[:, :20].to(dev), v[:, :20].to(dev), a[:, :20].to(dev), b[:, :20].to(dev))
+    o2, s2 = ops.gated_delta(q[:, 20:].to(dev), k[:, 20:].to(dev), v[:, 20:].to(dev), a[:, 20:].to(dev), b[:, 20:].to(dev), s1)
+    for h in range(BH):
+        ro, rs = ssm.gated_delta_rule_ref(q[h], k[h], v[h], a[h], b[h])
+        torch.testing.assert_close(out[h].cpu(), ro, rtol=1e-4, atol=1e-4)
+        torch.testing.assert_close(st[h].cpu(), rs, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(torch.cat([o1, o2], 1), out, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(s2, st, rtol=1e-5, atol=1e-5)
