@@ -320,8 +320,9 @@ class Engine:
         if self.runner is None:
             return out
         alloc = self.seqs.allocator
-        out.update(kv_blocks_total=alloc.total_blocks(), kv_blocks_used=alloc.num_used_blocks(),
-                   kv_utilization=alloc.num_used_blocks() / max(1, alloc.total_blocks()))
+        total = alloc.total_blocks
+        out.update(kv_blocks_total=total, kv_blocks_used=alloc.num_used_blocks(),
+                   kv_utilization=alloc.num_used_blocks() / max(1, total))
         if self.prefix_cache is not None:
             st = self.prefix_cache.stats()
             out.update(prefix_cache_hit_rate=st.hit_rate, prefix_cache_blocks=st.cached_blocks,

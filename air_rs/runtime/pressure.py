@@ -83,7 +83,7 @@ class KvPressureController:
     def __init__(self, engine, safety_blocks: int = 0):
         self.eng = engine
         alloc = engine.seqs.allocator
-        self.mgr = VramPressureManager(alloc.total_blocks(), safety_blocks)
+        self.mgr = VramPressureManager(alloc.total_blocks, safety_blocks)
         self.level = PressureLevel.GREEN
         self.history: list[PressureLevel] = []
         self.evicted_blocks = 0

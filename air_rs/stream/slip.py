@@ -83,6 +83,7 @@ class LayerStreamer:
             self.resident[li] = lw
         self.streamed = [li for li in range(len(host_layers)) if li not in self.resident]
         self._pos = {li: i for i, li in enumerate(self.streamed)}
+        self._deferred: int | None = None
         self.slots = [_device_clone(host_layers[0], self.device) for _ in range(n_slots)]
         self.slot_tensors = [layer_tensors(s) for s in self.slots]
         self.copy_stream = torch.cuda.Stream(self.device)
@@ -141,8 +142,14 @@ class LayerStreamer:
         cs = torch.cuda.current_stream(self.device)
         cs.wait_event(self.ready[s])
         # the next streamed layer's slot is free once the layer that used it last is done;
-        # after the last layer this starts the first streamed layer of the next step
-        self.prefetch(self._next_streamed(li))
+        # after the last layer this starts the first streamed layer of the next step. When the
+        # next layer maps to this very slot (an odd number of streamed layers wrapping around),
+        # its copy has to wait for this layer's release.
+        nxt = self._next_streamed(li)
+        if nxt >= 0 and self._slot(nxt) == s and nxt != li:
+            self._deferred = nxt
+        else:
+            self.prefetch(nxt)
         if self.timing:
             e = torch.cuda.Event(enable_timing=True)
             e.record(cs)
@@ -157,6 +164,9 @@ class LayerStreamer:
         ev = torch.cuda.Event(enable_timing=self.timing)
         ev.record(torch.cuda.current_stream(self.device))
         self.free[s] = ev
+        if self._deferred is not None:
+            nxt, self._deferred = self._deferred, None
+            self.prefetch(nxt)
         st = self._compute_start.pop(li, None)
         if st is not None:
             # the first layer of a step follows host work (sampling, scheduling): no gap check

@@ -27,6 +27,7 @@ class _Alloc:
     def __init__(self, total, used):
         self.t, self.u = total, used
 
+    @property
     def total_blocks(self):
         return self.t
 
@@ -80,3 +81,15 @@ def test_controller_actions(used, level, paused, evicted, preempt):
     c = KvPressureController(e)
     assert c.tick() == level
     assert e.admit_paused == paused and c.evicted_blocks == evicted and e.preempts == preempt
+
+
+def test_controller_with_native_allocator():
+    from air_rs import _host
+    seqs = _host.SequenceManager(20, 16)
+    e = _Eng(1, 0, 0)
+    e.seqs, e.prefix_cache = seqs, None
+    c = KvPressureController(e)
+    assert c.mgr.budget == 20 and c.tick() == PressureLevel.GREEN
+    s = seqs.create_sequence()
+    seqs.append(s, 16 * 19)
+    assert c.tick() == PressureLevel.CRITICAL and e.admit_paused and e.preempts == 1
