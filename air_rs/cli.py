@@ -115,11 +115,16 @@ def _engine(args, max_batch=64):
     tp = None
     if args.tp > 1:
         tp = init_from_env("nccl")
+    from .config import EngineConfig
+    from .runtime import vram_guard
     path = resolve(args.model)
+    ec = EngineConfig.from_env()          # AIR_* overrides of the engine defaults
+    vram_guard.set_default_fraction(ec.vram_fraction)
     return engine_from_gguf(path, device=args.device, max_batch=max_batch, max_model_len=args.ctx_size, tp=tp,
                             resident=not getattr(args, "stream_weights", False),
-                            expert_slots=getattr(args, "expert_slots", None),
-                            **({"prefix_cache": True} if getattr(args, "enable_prefix_caching", False) else {}))
+                            expert_slots=getattr(args, "expert_slots", None) or ec.expert_slots,
+                            prefix_cache=getattr(args, "enable_prefix_caching", False) or ec.prefix_cache,
+                            kv_swap=ec.kv_swap, pressure_control=ec.pressure_control, secure_kv=ec.secure_kv)
 
 
 def cmd_generate(args) -> int:
@@ -192,7 +197,8 @@ def cmd_serve(args) -> int:
     if args.modelfile:
         from .modelfile import Modelfile
         mf = Modelfile.load(args.modelfile)
-    app = create_app(d, name, api_keys=args.api_key, chat_format=args.chat_template,
+    keys = args.api_key or [k for k in os.environ.get("AIR_API_KEYS", "").split(",") if k] or None
+    app = create_app(d, name, api_keys=keys, chat_format=args.chat_template,
                      reasoning_format=args.reasoning_format, tool_call_parser=args.tool_call_parser,
                      safety=safety, modelfile=mf)
     uvicorn.run(app, host=args.host, port=args.port, ssl_certfile=args.tls_cert, ssl_keyfile=args.tls_key,

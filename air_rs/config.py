@@ -48,6 +48,8 @@ class EngineConfig:
     draft_max: int = 5
     spec_tree: bool = False
     allreduce: str = "peer"             # TP all-reduce: fused peer kernel or "nccl"
+    pressure_control: bool = False      # act on KV-pool pressure (evict cache, pause, preempt)
+    secure_kv: bool = False             # zero KV blocks freed by finished requests
     extra: dict = field(default_factory=dict)
 
     # ------------------------------------------------------------------ env
@@ -92,6 +94,7 @@ class EngineConfig:
     def engine_kwargs(self) -> dict:
         return dict(max_batch=self.max_batch, prefill_chunk=self.prefill_chunk,
                     max_prefill_tokens=self.max_prefill_tokens, prefix_cache=self.prefix_cache,
+                    pressure_control=self.pressure_control, secure_kv=self.secure_kv,
                     kv_swap=self.kv_swap, cuda_graph_batch_sizes=tuple(self.cuda_graph_batch_sizes))
 
     def build(self, tp=None):
