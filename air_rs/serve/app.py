@@ -265,7 +265,12 @@ def create_app(dispatcher: Dispatcher, model_name: str = "air-rs", *, api_keys: 
 
     async def prometheus():
         eng = getattr(dispatcher, "engine", None)
-        gauges = eng.stats() if eng is not None and hasattr(eng, "stats") else None
+        gauges = None
+        if eng is not None and hasattr(eng, "stats"):
+            try:      # read while the engine thread runs; a torn read only skips the gauges
+                gauges = eng.stats()
+            except (RuntimeError, KeyError, ValueError):
+                gauges = None
         return PlainTextResponse(metrics.render(model_name, gauges), media_type="text/plain; version=0.0.4")
 
     for prefix in ("/v1", ""):
