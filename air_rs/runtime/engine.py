@@ -185,12 +185,7 @@ class Engine:
             self._deferred.append((r.seq, r.slot))
         else:
             if self.seqs is not None and r.seq >= 0:
-                if self.secure_kv and not self.seqs.is_swapped(r.seq):
-                    from ..utils.security import zero_kv_blocks
-                    alloc = self.seqs.allocator
-                    zero_kv_blocks(self.runner.kv, [b for b in self.seqs.block_table(r.seq)
-                                                    if alloc.ref_count(b) == 1])
-                self.seqs.free_sequence(r.seq)
+                self._free_seq(r.seq)
             if r.slot >= 0:
                 self.free_slots.append(r.slot)
         r.seq = -1
@@ -673,10 +668,18 @@ class Engine:
         finally:
             self._defer_free = False
 
+    def _free_seq(self, seq: int):
+        """Return a sequence's blocks to the pool (zeroing those it alone held with secure_kv)."""
+        if self.secure_kv and not self.seqs.is_swapped(seq):
+            from ..utils.security import zero_kv_blocks
+            alloc = self.seqs.allocator
+            zero_kv_blocks(self.runner.kv, [b for b in self.seqs.block_table(seq) if alloc.ref_count(b) == 1])
+        self.seqs.free_sequence(seq)
+
     def _release_deferred(self):
         for seq, slot in getattr(self, "_deferred", []):
             if seq >= 0:
-                self.seqs.free_sequence(seq)
+                self._free_seq(seq)
             if slot >= 0:
                 self.free_slots.append(slot)
         self._deferred = []
