@@ -4,7 +4,8 @@ names mapped to the GGUF ones (``model.layers.N.self_attn.q_proj.weight`` ->
 ``blk.N.attn_q.weight`` ...), Mixtral experts stacked into ``ffn_*_exps``, and matrices
 quantised on the way in (on the device given, chunk by chunk) to the requested GGUF type.
 
-Attention projections are kept in Hugging Face order: its rotary embedding rotates the two
+Block-scaled fp8 weights (E4M3 codes with a ``weight_scale_inv`` per 128 x 128 tile) are
+expanded with their scales first. Attention projections are kept in Hugging Face order: its rotary embedding rotates the two
 halves of each head, which is the rotation the kernels apply, so no permutation is needed.
 """
 from __future__ import annotations
@@ -123,6 +124,14 @@ def hf_records(path: str, qtype: GGMLType = GGMLType.Q4_K, device="cpu", cfg: Mo
                 continue                      # rotary caches, biases of other families ...
             gname = f"blk.{mm.group(1)}.{_LAYER[mm.group(2)]}"
         x = src[name]()
+        if x.dtype in (torch.float8_e4m3fn, torch.float8_e5m2):
+            # block-scaled fp8 checkpoints store the tile multipliers beside the weight
+            sname = name[: -len("weight")] + "weight_scale_inv"
+            if sname in src:
+                from ..quant.fp8 import block_dequantize_fp8
+                x = block_dequantize_fp8(x, src[sname]())
+            else:
+                x = x.float()
         if gname.endswith("norm.weight") or gname.endswith("ffn_gate_inp.weight"):
             raw, qt = _quantise(x, GGMLType.F32, device)
         else:

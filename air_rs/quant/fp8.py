@@ -86,3 +86,29 @@ class Fp8Linear:
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return x.float() @ self.dequantize().t()
+
+
+# ---------------------------------------------------------------------------- block-scaled fp8
+FP8_BLOCK = 128
+
+
+def block_quantize_fp8(w: torch.Tensor, block: int = FP8_BLOCK) -> tuple[torch.Tensor, torch.Tensor]:
+    """W [N, K] -> (E4M3 codes [N, K] as torch.float8_e4m3fn, inverse scales [ceil(N/b), ceil(K/b)]):
+    each block x block tile is scaled so its absmax maps to 448 (the E4M3 maximum); the stored
+    scale is the multiplier that restores the tile (the ``weight_scale_inv`` convention of
+    block-scaled fp8 checkpoints)."""
+    N, K = w.shape
+    nb, kb = -(-N // block), -(-K // block)
+    wp = torch.nn.functional.pad(w.float(), (0, kb * block - K, 0, nb * block - N))
+    tiles = wp.reshape(nb, block, kb, block)
+    amax = tiles.abs().amax((1, 3)).clamp_min(1e-12)
+    scale_inv = amax / 448.0
+    q = (tiles / scale_inv[:, None, :, None]).reshape(nb * block, kb * block)[:N, :K]
+    return q.to(torch.float8_e4m3fn), scale_inv
+
+
+def block_dequantize_fp8(q: torch.Tensor, scale_inv: torch.Tensor, block: int = FP8_BLOCK) -> torch.Tensor:
+    """Inverse of ``block_quantize_fp8``: codes [N, K] times the tile scale -> fp32."""
+    N, K = q.shape
+    s = scale_inv.float().repeat_interleave(block, 0)[:N].repeat_interleave(block, 1)[:, :K]
+    return q.float() * s

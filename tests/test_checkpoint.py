@@ -106,3 +106,25 @@ def test_hf_moe_experts_stacked_and_engine_runs(tmp_path):
     eng = engine_from_hf(str(tmp_path), qtype=GGMLType.Q8_0, device="cpu")
     out = eng.generate_ids([[5, 6, 7]], SamplingParams(max_tokens=3, temperature=0.0, ignore_eos=True))
     assert len(out[0]) == 3
+
+
+def test_block_scaled_fp8_weights(tmp_path):
+    from air_rs.quant.fp8 import block_dequantize_fp8, block_quantize_fp8
+    w = torch.randn(300, 260) * 0.05
+    q, si = block_quantize_fp8(w)
+    assert q.dtype == torch.float8_e4m3fn and si.shape == (3, 3)
+    back = block_dequantize_fp8(q, si)
+    assert float((back - w).abs().max()) <= float(w.abs().max()) / 14     # 3 mantissa bits
+    sd, _ = _hf_dir(tmp_path)
+    name = "model.layers.0.mlp.down_proj.weight"
+    q, si = block_quantize_fp8(sd[name])
+    shards = sorted(tmp_path.glob("*.safetensors"))
+    for f in shards:
+        t = load_safetensors(str(f))
+        if name in t:
+            t[name] = q
+            t[name[:-len("weight")] + "weight_scale_inv"] = si
+            save_safetensors(t, str(f))
+    recs = {n: (r, qq, s) for n, r, qq, s in hf_records(str(tmp_path), GGMLType.F32)}
+    raw, qt, shape = recs["blk.0.ffn_down.weight"]
+    torch.testing.assert_close(raw.view(torch.float32).reshape(shape), block_dequantize_fp8(q, si))
