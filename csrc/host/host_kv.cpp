@@ -8,7 +8,13 @@
 // block is opened when the last one is full. Unlike the reference the blocks here back a
 // real HBM pool: CoW / swap return the (src, dst) block ids the engine must copy, and
 // sequences can be truncated (speculative rollback) and swapped out/in (host tier).
+#ifdef AIR_HOST_NO_TORCH
+// sanitizer builds: plain pybind11, without the two tensor-filling helpers
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+#else
 #include <torch/extension.h>
+#endif
 
 #include <deque>
 #include <stdexcept>
@@ -115,6 +121,13 @@ class SequenceManager {
     return it->second;
   }
   bool has(int64_t s) const { return tables_.count(s) != 0; }
+  // A sequence whose block ids are valid device blocks (a swapped-out table keeps the ids of
+  // blocks already returned to the pool, so no operation may read or share them).
+  Table& live(int64_t s) {
+    Table& tb = t(s);
+    if (tb.swapped) throw std::runtime_error("sequence is swapped out");
+    return tb;
+  }
 
   // Appends n tokens; returns their cache slots (block * block_size + offset).
   // Raises (with no state change) if the pool cannot hold them.
@@ -143,13 +156,13 @@ class SequenceManager {
   }
   // slot of an existing position
   int64_t slot(int64_t s, int64_t pos) {
-    Table& tb = t(s);
+    Table& tb = live(s);
     const int64_t bs = alloc_.block_size();
     if (pos < 0 || pos >= tb.num_tokens) throw std::out_of_range("position out of range");
     return tb.blocks[pos / bs] * bs + pos % bs;
   }
   int64_t fork(int64_t parent) {
-    Table& p = t(parent);
+    Table& p = live(parent);
     for (int64_t b : p.blocks) alloc_.share(b);
     int64_t id = next_++;
     Table c;
@@ -167,7 +180,7 @@ class SequenceManager {
   }
   // Copy-on-write of the last block: returns (old, new) (equal when no copy is needed).
   std::pair<int64_t, int64_t> cow_last(int64_t s) {
-    Table& tb = t(s);
+    Table& tb = live(s);
     if (tb.blocks.empty()) return {-1, -1};
     int64_t old = tb.blocks.back();
     int64_t nb = alloc_.cow_write(old);
@@ -177,7 +190,7 @@ class SequenceManager {
   }
   // Keep the first n tokens; frees whole trailing blocks (speculative rollback).
   void truncate(int64_t s, int64_t n) {
-    Table& tb = t(s);
+    Table& tb = live(s);
     if (n >= tb.num_tokens) return;
     const int64_t bs = alloc_.block_size();
     const int64_t keep = (n + bs - 1) / bs;
@@ -221,6 +234,7 @@ class SequenceManager {
     for (int64_t s : seqs) out.push_back(s < 0 ? -1 : append(s, 1)[0]);
     return out;
   }
+#ifndef AIR_HOST_NO_TORCH
   // Dense [B, max_blocks] int32 block table for a batch (-1 padded; seq < 0 = empty row).
   void fill_table(const std::vector<int64_t>& seqs, torch::Tensor tab) {
     TORCH_CHECK(tab.scalar_type() == torch::kInt && tab.dim() == 2 && tab.device().is_cpu(),
@@ -229,19 +243,21 @@ class SequenceManager {
     auto a = tab.accessor<int, 2>();
     const int64_t n = tab.size(1);
     for (int64_t r = 0; r < (int64_t)seqs.size(); ++r) {
-      const std::vector<int64_t>* bl = seqs[r] >= 0 ? &t(seqs[r]).blocks : nullptr;
+      const std::vector<int64_t>* bl = seqs[r] >= 0 ? &live(seqs[r]).blocks : nullptr;
       const int64_t nb = bl ? (int64_t)bl->size() : 0;
       TORCH_CHECK(nb <= n, "block table row too short");
       for (int64_t i = 0; i < n; ++i) a[r][i] = i < nb ? (int)(*bl)[i] : -1;
     }
   }
+#endif
   std::vector<int64_t> blocks(int64_t s) { return t(s).blocks; }
   int64_t num_tokens(int64_t s) { return t(s).num_tokens; }
   bool swapped(int64_t s) { return t(s).swapped; }
   int64_t num_sequences() const { return (int64_t)tables_.size(); }
+#ifndef AIR_HOST_NO_TORCH
   // Fill a dense int32 block-table row (padding -1) for the kernels.
   void fill_row(int64_t s, torch::Tensor row) {
-    Table& tb = t(s);
+    Table& tb = live(s);
     TORCH_CHECK(row.scalar_type() == torch::kInt && row.dim() == 1 && row.device().is_cpu(),
                 "row must be a 1-D int32 CPU tensor");
     auto a = row.accessor<int, 1>();
@@ -249,6 +265,7 @@ class SequenceManager {
     TORCH_CHECK((int64_t)tb.blocks.size() <= n, "block table row too short");
     for (int64_t i = 0; i < n; ++i) a[i] = i < (int64_t)tb.blocks.size() ? (int)tb.blocks[i] : -1;
   }
+#endif
 
  private:
   BlockAllocator alloc_;
@@ -293,7 +310,10 @@ void register_host_kv(py::module_& m) {
       .def("num_tokens", &SequenceManager::num_tokens)
       .def("is_swapped", &SequenceManager::swapped)
       .def("num_sequences", &SequenceManager::num_sequences)
-      .def("fill_row", &SequenceManager::fill_row)
       .def("step_slots", &SequenceManager::step_slots)
-      .def("fill_table", &SequenceManager::fill_table);
+#ifndef AIR_HOST_NO_TORCH
+      .def("fill_row", &SequenceManager::fill_row)
+      .def("fill_table", &SequenceManager::fill_table)
+#endif
+      ;
 }

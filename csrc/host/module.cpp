@@ -1,6 +1,11 @@
 // air_rs._host: the CPU-side native runtime (no CUDA dependency, so it also loads on
 // machines without a GPU): paged-KV bookkeeping and the batch scheduler core.
+#ifdef AIR_HOST_NO_TORCH
+#include <pybind11/pybind11.h>
+#define TORCH_EXTENSION_NAME _host
+#else
 #include <torch/extension.h>
+#endif
 
 void register_host_kv(pybind11::module_& m);
 
