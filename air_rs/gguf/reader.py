@@ -85,6 +85,37 @@ class GGUFFile:
         flat = self._buf[t.offset:t.offset + t.nbytes]
         return flat.view(t.rows, t.nbytes // t.rows)
 
+    def read_parallel(self, names=None, workers: int = 8, pin: bool | None = None) -> dict:
+        """Tensors read with ``workers`` threads of ``pread`` into (pinned) host buffers
+        instead of page faults on the memory map: globals first, then layer by layer, so a
+        cold start from NVMe keeps several requests in flight. Returns name -> uint8
+        ``[rows, row_bytes]`` like ``raw``."""
+        from ..stream.strix import IoEngine, IoPriority, IoRequest
+        names = list(self.tensors) if names is None else list(names)
+
+        def order(n):
+            if n.startswith("blk."):
+                return (1, int(n.split(".")[1]))
+            return (0, 0)
+        eng = IoEngine(self.path, capacity=workers, workers=workers, pin=pin)
+        try:
+            for n in sorted(names, key=order):
+                t = self.tensors[n]
+                pr = IoPriority.CRITICAL if not n.startswith("blk.") else IoPriority.NORMAL
+                eng.submit(IoRequest(n, t.offset, t.nbytes, pr))
+            done = eng.wait_all(timeout=3600.0)
+        finally:
+            eng.close()
+        out = {}
+        for c in done:
+            if c.error:
+                raise OSError(f"reading {c.tensor_id} from {self.path}: {c.error}")
+            t = self.tensors[c.tensor_id]
+            out[c.tensor_id] = c.data.view(t.rows, t.nbytes // t.rows)
+        if len(out) != len(names):
+            raise OSError(f"{len(names) - len(out)} tensors of {self.path} were not read")
+        return out
+
     def dequantize(self, name: str) -> torch.Tensor:
         from .quants import dequantize
         t = self.tensors[name]

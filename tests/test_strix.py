@@ -55,3 +55,16 @@ def test_residency_scheduler_budget_and_window():
     assert {"l2", "l3"} & set(load) and evict and sch.tensors[evict[0]].evictions == 1
     resident = [t.tensor_id for t in sch.tensors.values() if t.resident]
     assert "embd" in resident and sum(sch.tensors[t].size for t in resident if t != "embd") <= 300
+
+
+def test_gguf_read_parallel_matches_memory_map(tmp_path):
+    from air_rs.gguf import GGMLType, read_gguf
+    from air_rs.models.config import tiny_llama
+    from air_rs.models.random_init import write_random_gguf
+    p = tmp_path / "m.gguf"
+    write_random_gguf(str(p), tiny_llama(), GGMLType.Q8_0, seed=0)
+    g = read_gguf(str(p))
+    bufs = g.read_parallel(workers=4, pin=False)
+    assert set(bufs) == set(g.tensors)
+    for n in g.tensors:
+        assert torch.equal(bufs[n], g.raw(n)), n
