@@ -142,10 +142,15 @@ def cmd_generate(args) -> int:
         eng.set_grammar(spec)
     cfg = GenerateConfig(max_tokens=args.max_tokens, temperature=args.temperature, top_p=args.top_p,
                          top_k=args.top_k, repetition_penalty=args.repetition_penalty)
-    if (args.model_draft or args.council) and core.runner is not None:
+    if (args.model_draft or args.council or args.ternary_cdsc) and core.runner is not None:
         from .spec.speculative import SpeculativeDecoder
         draft = (_engine(argparse.Namespace(**{**vars(args), "model": args.model_draft}), max_batch=8)
                  if args.model_draft else None)
+        if draft is None and (args.ternary_cdsc or args.ternary):
+            # self-drafting: the target's own weights, ternarised
+            from .hub import resolve
+            from .spec.ternary_draft import ternary_draft_engine
+            draft = ternary_draft_engine(resolve(args.model), device=str(core.runner.device))
         if args.council:
             from .spec.medusa import CouncilDecoder
             # voters: the draft model (when given) and the target itself; a draft chain grows
