@@ -127,6 +127,7 @@ def _engine(args, max_batch=64):
                             expert_slots=getattr(args, "expert_slots", None) or ec.expert_slots,
                             prefix_cache=getattr(args, "enable_prefix_caching", False) or ec.prefix_cache,
                             kv_swap=ec.kv_swap, pressure_control=ec.pressure_control, secure_kv=ec.secure_kv,
+                            admission=ec.admission,
                             parallel_read=getattr(args, "gds", False))
 
 

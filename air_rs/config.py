@@ -50,6 +50,7 @@ class EngineConfig:
     allreduce: str = "peer"             # TP all-reduce: fused peer kernel or "nccl"
     pressure_control: bool = False      # act on KV-pool pressure (evict cache, pause, preempt)
     secure_kv: bool = False             # zero KV blocks freed by finished requests
+    admission: str = "fifo"             # fifo | priority | arb (harmonic length grouping)
     extra: dict = field(default_factory=dict)
 
     # ------------------------------------------------------------------ env
@@ -78,6 +79,8 @@ class EngineConfig:
             raise ValueError("block_size must be a power of two")
         if not 0.0 < self.vram_fraction <= 1.0:
             raise ValueError("vram_fraction must be in (0, 1]")
+        if self.admission not in ("fifo", "priority", "arb"):
+            raise ValueError("admission must be fifo, priority or arb")
         if self.allreduce not in ("peer", "nccl"):
             raise ValueError("allreduce must be 'peer' or 'nccl'")
         if self.stream_slots < 2:
@@ -95,6 +98,7 @@ class EngineConfig:
         return dict(max_batch=self.max_batch, prefill_chunk=self.prefill_chunk,
                     max_prefill_tokens=self.max_prefill_tokens, prefix_cache=self.prefix_cache,
                     pressure_control=self.pressure_control, secure_kv=self.secure_kv,
+                    admission=self.admission,
                     kv_swap=self.kv_swap, cuda_graph_batch_sizes=tuple(self.cuda_graph_batch_sizes))
 
     def build(self, tp=None):

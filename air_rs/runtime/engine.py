@@ -83,13 +83,17 @@ class Engine:
                  add_bos: bool = True, eos_id: int | None = None, prefix_cache: bool = False,
                  prefix_cache_blocks: int | None = None, kv_swap: bool = True,
                  cuda_graph_batch_sizes: tuple[int, ...] = BUCKETS, pressure_control: bool = False,
-                 secure_kv: bool = False):
+                 secure_kv: bool = False, admission: str = "fifo", arb_ratio: float = 2.0,
+                 max_wait_s: float = 2.0):
         """``pressure_control``: evaluate KV-pool pressure every step and act on it (prefix-cache
         eviction from Orange, no admissions from Red, preemption at Critical)."""
         self.cfg = cfg
         self.admit_paused = False
         self.decode_ms_last = self.decode_ms_ema = None
         self.secure_kv = secure_kv        # zero the KV blocks a finished request frees
+        if admission not in ("fifo", "priority", "arb"):
+            raise ValueError(f"unknown admission policy {admission!r}")
+        self.admission, self.arb_ratio, self.max_wait_s = admission, arb_ratio, max_wait_s
         self.buckets = tuple(sorted(cuda_graph_batch_sizes))
         self.runner = runner
         self.oracle = oracle
@@ -233,7 +237,7 @@ class Engine:
         if self.swapped:          # preempted requests go first
             return admitted
         while self.waiting and len(self.running) + len(admitted) < self.max_batch:
-            r = self.waiting[0]
+            r = self._next_waiting(admitted)
             hit, blocks = 0, []
             if self.prefix_cache is not None and r.image_embeds is None:
                 # keep at least one prompt token to prefill (its logits give the first token)
@@ -245,7 +249,7 @@ class Engine:
                 break
             if len(r.prompt_ids) - hit > budget and admitted:
                 break
-            self.waiting.popleft()
+            self.waiting.remove(r)
             if hit:
                 r.seq = self.seqs.create_with_prefix(blocks, hit)
                 r.prefilled = hit
@@ -300,6 +304,32 @@ class Engine:
             batch = batch[:-1]
             self.metrics.preemptions = getattr(self.metrics, "preemptions", 0) + 1
         return batch
+
+    def _next_waiting(self, admitted: list) -> "Request":
+        """The waiting request the admission policy takes next.
+
+        fifo: oldest first. priority: highest ``priority``, then oldest. arb: harmonic length
+        grouping (reference ``src/batching/arb.rs``): prefer the oldest request whose prompt
+        length is within ``arb_ratio`` of the running batch's median context, so one decode
+        batch keeps similar attention lengths; a request older than ``max_wait_s`` goes first
+        whatever its length (no starvation)."""
+        if self.admission == "fifo" or len(self.waiting) == 1:
+            return self.waiting[0]
+        if self.admission == "priority":
+            return max(self.waiting, key=lambda r: (r.priority, -r.arrival))
+        now = time.perf_counter()
+        oldest = self.waiting[0]
+        if now - oldest.arrival > self.max_wait_s:
+            return oldest
+        lens = sorted(r.num_tokens for r in list(self.running) + list(admitted))
+        if not lens:
+            return oldest
+        med = lens[len(lens) // 2]
+        for r in self.waiting:
+            n = len(r.prompt_ids)
+            if max(n, med) <= self.arb_ratio * max(1, min(n, med)):
+                return r
+        return oldest
 
     def _timing_event(self, i: int):
         ev = getattr(self, "_tev", None)

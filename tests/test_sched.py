@@ -88,3 +88,27 @@ def test_model_mux_round_robin_on_cpu_engines():
     assert sorted(fin) == [("a", ra), ("b", rb)]
     toks = [e.model for e in mux.events if e.kind == MuxEventKind.TOKEN]
     assert toks[:2] == ["a", "b"] and len(toks) == 6
+
+
+def test_engine_admission_policies():
+    import time as _t
+    from air_rs.models.config import tiny_llama
+    from air_rs.runtime.engine import Engine, Request, SamplingParams
+    cfg = tiny_llama()
+    sp = SamplingParams()
+    mk = lambda rid, n, pr=0: Request(rid, list(range(n)), sp, priority=pr)
+    e = Engine(cfg, None, admission="priority")
+    e.waiting.extend([mk(0, 10), mk(1, 10, pr=5), mk(2, 10, pr=5)])
+    assert e._next_waiting([]).rid == 1
+    a = Engine(cfg, None, admission="arb", arb_ratio=2.0, max_wait_s=60.0)
+    a.running = [mk(9, 100)]
+    a.waiting.extend([mk(0, 1000), mk(1, 20), mk(2, 150)])
+    assert a._next_waiting([]).rid == 2            # within 2x of the running context
+    a.waiting[0].arrival = _t.perf_counter() - 120  # starving: goes first
+    assert a._next_waiting([]).rid == 0
+    f = Engine(cfg, None)
+    f.waiting.extend([mk(0, 5), mk(1, 5, pr=9)])
+    assert f._next_waiting([]).rid == 0
+    import pytest
+    with pytest.raises(ValueError):
+        Engine(cfg, None, admission="lifo")
