@@ -60,6 +60,9 @@ class GGMLType(enum.IntEnum):
     F64 = 28
     IQ1_M = 29
     BF16 = 30
+    TQ1_0 = 34
+    TQ2_0 = 35
+    MXFP4 = 39
 
 
 QK_K = 256
@@ -95,6 +98,9 @@ BLOCK_GEOMETRY: dict[GGMLType, tuple[int, int]] = {
     GGMLType.IQ1_M: (256, 56),
     GGMLType.IQ4_NL: (32, 18),
     GGMLType.IQ4_XS: (256, 136),
+    GGMLType.TQ1_0: (256, 54),
+    GGMLType.TQ2_0: (256, 66),
+    GGMLType.MXFP4: (32, 17),
 }
 
 

@@ -36,6 +36,19 @@ def reset_launch_count():
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_QKV_ROPE, EPI_PEER_PUSH = 0, 1, 2, 3, 4
 
 
+_LOWBIT = frozenset({GGMLType.IQ1_S, GGMLType.IQ1_M, GGMLType.IQ2_XXS, GGMLType.IQ2_XS, GGMLType.IQ2_S,
+                     GGMLType.IQ3_XXS, GGMLType.IQ3_S, GGMLType.TQ1_0, GGMLType.TQ2_0, GGMLType.MXFP4})
+
+
+def lowbit_target() -> str:
+    """Device format of sub-4-bit checkpoint tensors: ``q8_0`` (default) or ``bf16``
+    (``AIR_LOWBIT_AS``)."""
+    v = os.environ.get("AIR_LOWBIT_AS", "q8_0").lower()
+    if v not in ("q8_0", "bf16"):
+        raise ValueError(f"AIR_LOWBIT_AS must be q8_0 or bf16, not {v!r}")
+    return v
+
+
 def pad32(k: int) -> int:
     return (k + 31) // 32 * 32
 
@@ -150,6 +163,14 @@ class QWeight:
             scales = b[..., 0:2].contiguous().view(torch.float16).reshape(N, K // 32)
             qs = b[..., 2:].contiguous().view(torch.int8).reshape(N, K)
             return cls(FMT_Q8_0, qs, scales.contiguous(), N, K, qtype, ((0, N),))
+        if qtype in _LOWBIT and K % 32 == 0 and lowbit_target() == "q8_0":
+            # sub-4-bit lattice / ternary / fp4 blocks: decode once, keep them as Q8_0 (8.5 bits,
+            # the native GEMV/GEMM format) instead of 16-bit bf16
+            from ..gguf.quants import quantize_q8_0
+            q8 = quantize_q8_0(dequantize(raw.to(device), qtype).reshape(N, K))
+            w = cls.from_raw(q8, GGMLType.Q8_0, N, K, device)
+            w.qtype = qtype
+            return w
         dense = dequantize(raw.to(device), qtype).reshape(N, K).to(torch.bfloat16)
         Kp = pad32(K)
         if Kp != K:  # zero columns so the activation's 32-element groups line up
