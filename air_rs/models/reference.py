@@ -139,6 +139,7 @@ class OracleModel:
         self.inv_freq = 1.0 / torch.pow(torch.tensor(float(cfg.rope_theta)),
                                         torch.arange(0, hd, 2, dtype=torch.float32) / hd)
         self.k_cache: list[torch.Tensor | None] = [None] * cfg.n_layers
+        self.ffn_hook = None       # callable(layer, ffn_input [S, H], silu(g) * u [S, I]) -> [S, I]
         self.v_cache: list[torch.Tensor | None] = [None] * cfg.n_layers
 
     @classmethod
@@ -212,6 +213,8 @@ class OracleModel:
                 g = qmatmul(h, L.w_gate[0], L.w_gate[1], L.w_gate[2])
                 u = qmatmul(h, L.w_up[0], L.w_up[1], L.w_up[2])
                 a = g / (1.0 + torch.exp(-g)) * u
+                if self.ffn_hook is not None:      # sparsity predictors: observe / mask neurons
+                    a = self.ffn_hook(li, h, a)
                 dn = qmatmul(a, L.w_down[0], L.w_down[1], L.w_down[2]).to(x.dtype)
             x = x + dn
         x = self.rms_norm(x, self.out_norm, cfg.rms_norm_eps)

@@ -25,7 +25,7 @@ import time
 import torch
 
 from .eagle2 import DraftNode, DraftTree
-from .speculative import SpeculativeDecoder, _Seq
+from .speculative import MAX_TREE_NODES, SpeculativeDecoder, _Seq
 
 
 class MedusaHeads:
@@ -53,9 +53,13 @@ class MedusaHeads:
 
 
 class MedusaDecoder(SpeculativeDecoder):
-    def __init__(self, target, heads: MedusaHeads, top_c: int = 2, max_nodes: int = 16, eos_id=None):
+    def __init__(self, target, heads: MedusaHeads, top_c: int = 2, max_nodes: int = 16, eos_id=None,
+                 monitor=None):
         super().__init__(target, None, k=heads.n_heads, max_nodes=max_nodes, eos_id=eos_id)
         self.heads, self.top_c = heads, top_c
+        # optional spec.wavefront.WavefrontHealthMonitor: acceptance per verified path sets
+        # the node budget of the next draft tree
+        self.monitor = monitor
         self.want_hidden = True
         self._hidden: dict[int, torch.Tensor] = {}
         rn = target.runner
@@ -99,6 +103,9 @@ class MedusaDecoder(SpeculativeDecoder):
         self._owners = owners
 
     def _accepted(self, si, s, path):
+        if self.monitor is not None:
+            self.monitor.update(len(path) - 1, self.heads.n_heads)
+            self.builder.max_nodes = min(MAX_TREE_NODES, max(2, self.monitor.current_draft_size))
         # the last accepted node's hidden drives the next round's heads
         hid = getattr(self, "_verify_hidden", None)
         if hid is None:
