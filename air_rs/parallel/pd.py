@@ -32,6 +32,61 @@ HEADER = struct.Struct("<IHI")          # block_id u32, layer u16, data_len u32
 FRAME = struct.Struct("<4sQI")          # magic, seq_id u64, n_blocks u32
 MAGIC = b"AIRK"
 
+# WARP stream framing (reference ``src/warp_protocol.rs``): every message on a TCP stream is
+# [magic "WARP"][version u16][features u64][body_len u32] + body, little endian. The first
+# message of a stream is the handshake [model fingerprint 32 B][name_len u16][name]; a body
+# length of 0 ends the stream. Same major version required; unknown feature bits rejected.
+WARP_MAGIC = b"WARP"
+WARP_VERSION = 0x0101
+WARP_HEADER = struct.Struct("<4sHQI")
+FEAT_LZ4, FEAT_INT8, FEAT_GHOST_PRUNING, FEAT_ASYNC_PIPELINING = 1, 2, 4, 8
+WARP_SUPPORTED = FEAT_INT8 | FEAT_ASYNC_PIPELINING
+
+
+def warp_header(features: int, body_len: int) -> bytes:
+    return WARP_HEADER.pack(WARP_MAGIC, WARP_VERSION, features, body_len)
+
+
+def parse_warp_header(buf: bytes) -> tuple[int, int]:
+    """(features, body_len); raises KvTransferError("protocol") on a bad magic, another
+    major version or feature bits this side cannot decode."""
+    magic, ver, feats, n = WARP_HEADER.unpack(buf)
+    if magic != WARP_MAGIC:
+        raise KvTransferError("protocol", "bad WARP magic")
+    if ver >> 8 != WARP_VERSION >> 8:
+        raise KvTransferError("protocol", f"WARP major version {ver >> 8} != {WARP_VERSION >> 8}")
+    if feats & ~WARP_SUPPORTED:
+        raise KvTransferError("protocol", f"unsupported WARP features {feats & ~WARP_SUPPORTED:#x}")
+    return feats, n
+
+
+def encode_handshake(fingerprint: bytes, name: str) -> bytes:
+    nb = name.encode()
+    return bytes(fingerprint).ljust(32, b"\0")[:32] + struct.pack("<H", len(nb)) + nb
+
+
+def decode_handshake(body: bytes) -> tuple[bytes, str]:
+    if len(body) < 34:
+        raise KvTransferError("protocol", "short WARP handshake")
+    (n,) = struct.unpack_from("<H", body, 32)
+    if len(body) != 34 + n:
+        raise KvTransferError("protocol", "bad WARP handshake length")
+    return body[:32], body[34:].decode(errors="replace")
+
+
+def gguf_fingerprint(path: str) -> bytes:
+    """SHA-256 of a GGUF file's header, metadata and tensor table (everything before the
+    tensor data) plus its size: two nodes serving the same checkpoint agree on it."""
+    import hashlib
+    import os
+    from ..gguf import read_gguf
+    g = read_gguf(path)
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        h.update(f.read(g.data_offset))
+    h.update(struct.pack("<Q", os.path.getsize(path)))
+    return h.digest()
+
 
 @dataclass
 class KvBlock:
@@ -154,11 +209,16 @@ class ShmKvConnector:
 
 
 class TcpKvConnector:
-    """Length-prefixed frames over TCP. ``listen()`` starts the receiver thread."""
+    """KV frames over TCP in WARP framing, after a model-identity handshake. ``listen()``
+    starts the receiver thread."""
     backend_name = "tcp"
 
-    def __init__(self, host: str = "127.0.0.1", port: int = 0):
+    def __init__(self, host: str = "127.0.0.1", port: int = 0, fingerprint: bytes | None = None,
+                 model_name: str = ""):
         self.host, self.port = host, port
+        # this node's model identity; a receiver with one refuses streams from another model
+        self.fingerprint, self.model_name = fingerprint, model_name
+        self.peers: list[tuple[bytes, str]] = []
         self._store: dict[int, list[KvBlock]] = {}
         self._errors: list[KvTransferError] = []
         self._cv = threading.Condition()
@@ -194,13 +254,19 @@ class TcpKvConnector:
     def _serve(self, conn):
         with conn:
             try:
+                _, n = parse_warp_header(self._read_exact(conn, WARP_HEADER.size))
+                fp, name = decode_handshake(self._read_exact(conn, n))
+                if self.fingerprint is not None and fp != bytes(self.fingerprint).ljust(32, b"\0")[:32]:
+                    raise KvTransferError("handshake", f"KV stream from another model ({name!r})")
+                with self._cv:
+                    self.peers.append((fp, name))
                 while True:
                     try:
-                        hdr = self._read_exact(conn, 8)
+                        hdr = self._read_exact(conn, WARP_HEADER.size)
                     except KvTransferError:
                         return
-                    (n,) = struct.unpack("<Q", hdr)
-                    if n == 0xFFFFFFFFFFFFFFFF:          # sentinel: sender done
+                    _, n = parse_warp_header(hdr)
+                    if n == 0:                             # end of stream
                         return
                     seq_id, blocks = decode_frame(self._read_exact(conn, n))
                     with self._cv:
@@ -212,14 +278,17 @@ class TcpKvConnector:
                     self._cv.notify_all()
 
     def send_blocks(self, seq_id: int, blocks: list[KvBlock], target, timeout: float = 2.0,
-                    corrupt: bool = False) -> int:
+                    corrupt: bool = False, features: int = 0) -> int:
+        """``features``: WARP bits of the payload (FEAT_INT8 for ``blocks_from_pool(quantize=True)``)."""
         frame = bytearray(encode_frame(seq_id, blocks))
         if corrupt and len(frame) > FRAME.size + HEADER.size:   # fault injection: flip a payload bit
             frame[FRAME.size + HEADER.size] ^= 0x01
         try:
+            hs = encode_handshake(self.fingerprint or b"", self.model_name)
             with socket.create_connection(target, timeout=timeout) as s:
-                s.sendall(struct.pack("<Q", len(frame)) + bytes(frame))
-                s.sendall(struct.pack("<Q", 0xFFFFFFFFFFFFFFFF))
+                s.sendall(warp_header(0, len(hs)) + hs)
+                s.sendall(warp_header(features, len(frame)) + bytes(frame))
+                s.sendall(warp_header(0, 0))
         except OSError as e:
             raise KvTransferError("io", str(e))
         return len(frame)

@@ -109,3 +109,44 @@ def test_device_kv_push_handoff_matches_single_engine():
         assert len(out) == 16
         _check_near_argmax(oracle, [cfg.bos_token_id] + p, out, penalty=1.0)
     assert pair.metrics.transfers_total == 2 and pre.seqs.allocator.num_used_blocks() == 0
+
+
+def test_warp_header_and_handshake_codec():
+    from air_rs.parallel.pd import (FEAT_INT8, FEAT_LZ4, WARP_HEADER, decode_handshake, encode_handshake,
+                                    parse_warp_header, warp_header)
+    h = warp_header(FEAT_INT8, 1234)
+    assert len(h) == WARP_HEADER.size == 18 and h[:4] == b"WARP"
+    assert parse_warp_header(h) == (FEAT_INT8, 1234)
+    for bad, why in [(b"XARP" + h[4:], "magic"), (h[:4] + (0x0201).to_bytes(2, "little") + h[6:], "major"),
+                     (warp_header(FEAT_LZ4, 5), "unsupported")]:
+        with pytest.raises(KvTransferError, match=why) as e:
+            parse_warp_header(bad)
+        assert e.value.kind == "protocol"
+    assert parse_warp_header(h[:4] + (0x0107).to_bytes(2, "little") + h[6:])[1] == 1234   # minor differs: ok
+    body = encode_handshake(b"\x01" * 32, "llama-3-8b")
+    assert decode_handshake(body) == (b"\x01" * 32, "llama-3-8b")
+    with pytest.raises(KvTransferError):
+        decode_handshake(body[:-1])
+
+
+def test_tcp_connector_rejects_another_models_stream(tmp_path):
+    from air_rs.gguf import GGMLType
+    from air_rs.models.config import tiny_llama
+    from air_rs.models.random_init import write_random_gguf
+    from air_rs.parallel.pd import FEAT_INT8, gguf_fingerprint
+    a, b = tmp_path / "a.gguf", tmp_path / "b.gguf"
+    write_random_gguf(str(a), tiny_llama(), GGMLType.Q8_0, seed=0)
+    write_random_gguf(str(b), tiny_llama(), GGMLType.Q4_K, seed=0)
+    fa, fb = gguf_fingerprint(str(a)), gguf_fingerprint(str(b))
+    assert len(fa) == 32 and fa == gguf_fingerprint(str(a)) and fa != fb
+    rx = TcpKvConnector(fingerprint=fa, model_name="a")
+    port = rx.listen()
+    blocks = blocks_from_pool(_pool(2), [1], quantize=True)
+    TcpKvConnector(fingerprint=fa, model_name="a").send_blocks(1, blocks, ("127.0.0.1", port), features=FEAT_INT8)
+    assert len(rx.recv_blocks(1, len(blocks), timeout=5.0)) == len(blocks)
+    assert rx.peers == [(fa, "a")]
+    TcpKvConnector(fingerprint=fb, model_name="b").send_blocks(2, blocks, ("127.0.0.1", port))
+    with pytest.raises(KvTransferError) as e:
+        rx.recv_blocks(2, len(blocks), timeout=5.0)
+    assert e.value.kind == "handshake" and "'b'" in str(e.value)
+    rx.close()
