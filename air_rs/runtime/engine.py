@@ -783,6 +783,32 @@ class Engine:
             self.seqs.free_sequence(seq)
         return n_full * self.runner.block_size
 
+    def store_prefix(self, model_id: str, rid: int, store, scheme="bf16"):
+        """Keep a running request's KV (as ``snapshot_request`` selects it) in a
+        ``kv.prefix_store.PrefixKvStore`` under ``model_id``."""
+        r = next((x for x in self.running if x.rid == rid), None)
+        if r is None or r.seq < 0 or self.runner is None:
+            raise KeyError(f"request {rid} is not running on the device")
+        if self.seqs.is_swapped(r.seq):
+            raise RuntimeError(f"request {rid} is swapped out")
+        toks = (r.prompt_ids + r.output_ids)[: self.seqs.num_tokens(r.seq)]
+        torch.cuda.current_stream(self.runner.device).synchronize()
+        return store.store(model_id, self.runner.kv, list(self.seqs.block_table(r.seq)), toks, scheme)
+
+    def restore_prefix(self, model_id: str, store) -> int:
+        """Load ``model_id``'s stored prefix into the prefix cache (whole blocks); returns the
+        tokens cached. Lossy schemes make later outputs differ from a fresh prefill."""
+        if self.runner is None or self.prefix_cache is None:
+            raise RuntimeError("restoring a stored prefix needs a device engine with prefix caching")
+        seq, toks, blocks = store.restore(model_id, self.runner.kv, self.seqs)
+        try:
+            bs = self.runner.block_size
+            n_full = len(toks) // bs
+            self.prefix_cache.insert(toks[: n_full * bs], blocks[:n_full])
+        finally:
+            self.seqs.free_sequence(seq)
+        return n_full * self.runner.block_size
+
     # ------------------------------------------------------------------ embeddings
     def embed(self, ids: list[int]) -> list[float]:
         """Mean-pooled final-norm hidden state of a prompt (``/v1/embeddings``).
