@@ -22,7 +22,7 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
-from .tp import TPGroup
+from .tp import COMM, TPGroup
 
 MAX_PEERS = 8
 DEFAULT_TIMEOUT_S = 2.0
@@ -97,12 +97,14 @@ class PeerComm:
     def push_gemv(self, w: ops.QWeight, xq, xds, B: int, err=None):
         """Row-parallel decode GEMV whose epilogue pushes the partial to every rank."""
         ops.gemv(w, xq, xds, B, ops.EPI_PEER_PUSH, ld_out=w.N, push_meta=self.push_meta, err=err)
+        COMM.record("peer_push", B * w.N * 4 * (self.world - 1))
         self.pending = True
 
     def push(self, src: torch.Tensor, B: int):
         """Push an fp32 partial [B, N] computed by another kernel."""
         ops.require_ext().peer_push(self.push_meta, src, B, src.shape[1], src.stride(0))
         ops.count_launch()
+        COMM.record("peer_push", B * src.shape[1] * 4 * (self.world - 1))
         self.pending = True
 
     # ----------------------------------------------------------------- consumer side

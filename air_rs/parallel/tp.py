@@ -16,6 +16,43 @@ import torch
 import torch.distributed as dist
 
 
+class CommStats:
+    """Calls and payload bytes per collective kind, process-wide. Payload bytes are what one
+    rank contributes: the partial it all-reduces, the shard it all-gathers, the rows it pushes
+    to each peer. Collectives inside a CUDA graph are recorded once at capture and added per
+    replay by the runner (``snapshot`` / ``since`` / ``add``)."""
+
+    def __init__(self):
+        self.calls: dict[str, int] = {}
+        self.bytes: dict[str, int] = {}
+
+    def record(self, kind: str, nbytes: int, calls: int = 1):
+        self.calls[kind] = self.calls.get(kind, 0) + calls
+        self.bytes[kind] = self.bytes.get(kind, 0) + int(nbytes)
+
+    def snapshot(self) -> dict[str, tuple[int, int]]:
+        return {k: (self.calls[k], self.bytes[k]) for k in self.calls if self.calls[k] or self.bytes[k]}
+
+    def since(self, snap: dict[str, tuple[int, int]]) -> dict[str, tuple[int, int]]:
+        now = self.snapshot()
+        return {k: (c - snap.get(k, (0, 0))[0], b - snap.get(k, (0, 0))[1]) for k, (c, b) in now.items()
+                if (c, b) != snap.get(k, (0, 0))}
+
+    def add(self, delta: dict[str, tuple[int, int]], sign: int = 1):
+        for k, (c, b) in delta.items():
+            self.record(k, sign * b, sign * c)
+
+    def totals(self) -> tuple[int, int]:
+        return sum(self.calls.values()), sum(self.bytes.values())
+
+    def reset(self):
+        self.calls.clear()
+        self.bytes.clear()
+
+
+COMM = CommStats()
+
+
 class TPGroup:
     def __init__(self, group=None):
         self.group = group
@@ -26,6 +63,7 @@ class TPGroup:
     def all_reduce_add(self, partial: torch.Tensor, x: torch.Tensor):
         """x += sum over ranks of partial (fp32)."""
         dist.all_reduce(partial, group=self.group)
+        COMM.record("all_reduce", partial.numel() * partial.element_size())
         x.add_(partial)
 
     def all_gather_vocab(self, local: torch.Tensor, full: torch.Tensor) -> torch.Tensor:
@@ -36,7 +74,8 @@ class TPGroup:
         if self._gather_buf is None or self._gather_buf.numel() < n:
             self._gather_buf = torch.empty(n, dtype=local.dtype, device=local.device)
         buf = self._gather_buf[:n].view(W, B, Vl)
-        dist.all_gather_into_tensor(buf, local.contiguous(), group=self.group)
+        dist.all_gather_into_tensor(buf.view(W * B, Vl), local.contiguous(), group=self.group)
+        COMM.record("all_gather", local.numel() * local.element_size())
         V = full.shape[1]
         full.copy_(buf.permute(1, 0, 2).reshape(B, W * Vl)[:, :V])
         return full

@@ -342,6 +342,9 @@ class Engine:
         device time of the last / average decode step, collective bytes per step."""
         out = {"running": len(self.running), "waiting": len(self.waiting), "swapped": len(self.swapped),
                "decode_steps": self.step_count, "preemptions": getattr(self.metrics, "preemptions", 0)}
+        from ..parallel.tp import COMM
+        calls, nbytes = COMM.totals()
+        out.update(collective_calls_total=calls, collective_bytes_total=nbytes)
         if self.runner is None:
             return out
         alloc = self.seqs.allocator

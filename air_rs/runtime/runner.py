@@ -15,6 +15,7 @@ from dataclasses import dataclass
 import torch
 
 from .. import ops
+from ..parallel.tp import COMM
 from ..models.config import ModelConfig
 from ..models.llama import LlamaWeights
 from ..utils import trace
@@ -130,6 +131,7 @@ class ModelRunner:
         self.inputs: dict[int, StepInputs] = {}
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_launches: dict[int, int] = {}
+        self.graph_comm: dict[int, dict] = {}      # collective calls / bytes per replay
         self._prefill_ws: dict[str, torch.Tensor] = {}
         self.streamer = None
         self.expert_cache = None
@@ -424,13 +426,17 @@ class ModelRunner:
             del saved
             g = torch.cuda.CUDAGraph()
             c0 = ops.launch_count()
+            m0 = COMM.snapshot()
             with torch.cuda.graph(g):
                 self._decode_body(B)
             self.graph_launches[B] = ops.launch_count() - c0
             ops.count_launch(-(ops.launch_count() - c0))  # capture itself runs nothing
+            self.graph_comm[B] = COMM.since(m0)
+            COMM.add(self.graph_comm[B], sign=-1)
             self.graphs[B] = g
         g.replay()
         ops.count_launch(self.graph_launches[B])
+        COMM.add(self.graph_comm[B])
         return self.inputs[B]
 
     # ------------------------------------------------------------------ prefill

@@ -242,3 +242,34 @@ def test_engine_snapshot_restore_hits_prefix_cache(tmp_path):
     out = eng2.generate_ids([prompt], SamplingParams(max_tokens=6, temperature=0.0, ignore_eos=True))
     assert eng2.prefix_cache.stats().hit_tokens >= 64
     assert out == ref
+
+
+# ---------------------------------------------------------------- collective accounting
+def test_comm_stats_record_capture_and_replay(tmp_path):
+    import torch.distributed as dist
+    from air_rs.parallel.tp import COMM, CommStats, TPGroup
+    s = CommStats()
+    s.record("all_reduce", 100)
+    snap = s.snapshot()
+    s.record("all_reduce", 50)
+    s.record("peer_push", 8, calls=2)
+    d = s.since(snap)
+    assert d == {"all_reduce": (1, 50), "peer_push": (2, 8)}
+    s.add(d, sign=-1)                       # undo a capture ...
+    assert s.snapshot() == snap
+    s.add(d)                                # ... and add it once per replay
+    s.add(d)
+    assert s.totals() == (1 + 2 + 4, 100 + 100 + 16)
+    store = dist.FileStore(str(tmp_path / "fs"), 1)
+    dist.init_process_group("gloo", store=store, rank=0, world_size=1)
+    try:
+        COMM.reset()
+        tp = TPGroup()
+        x = torch.zeros(2, 8)
+        tp.all_reduce_add(torch.ones(2, 8), x)
+        full = torch.zeros(2, 10)
+        tp.all_gather_vocab(torch.ones(2, 10), full)
+        assert COMM.snapshot() == {"all_reduce": (1, 64), "all_gather": (1, 80)}
+    finally:
+        dist.destroy_process_group()
+        COMM.reset()
