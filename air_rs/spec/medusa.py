@@ -36,9 +36,26 @@ class MedusaHeads:
         self.n_heads = n_heads
 
     @classmethod
-    def load(cls, path: str, device="cuda") -> "MedusaHeads":
-        sd = torch.load(path, map_location="cpu")
-        ws = [sd[k] for k in sorted(sd) if k.startswith("head")]
+    def load(cls, path: str, device="cuda", fingerprint: bytes | None = None,
+             hidden: int | None = None) -> "MedusaHeads":
+        """Heads from a state dict; a ``<path>.draft.json`` manifest next to it, when present,
+        must match ``fingerprint`` (the target checkpoint's, ``parallel.pd.gguf_fingerprint``)
+        and ``hidden``, and the heads must match the manifest."""
+        import json
+        import os
+        sd = torch.load(path, map_location="cpu", weights_only=True)
+        keys = sorted((k for k in sd if k.startswith("head")), key=lambda k: int(k[4:]))
+        ws = [sd[k] for k in keys]
+        man_path = path + ".draft.json"
+        if os.path.exists(man_path):
+            with open(man_path) as f:
+                man = json.load(f)
+            if fingerprint is not None and man.get("target_fingerprint") not in (None, bytes(fingerprint).hex()):
+                raise ValueError(f"{path}: draft heads were trained for another target ({man.get('target_name')!r})")
+            if man.get("n_heads") != len(ws) or any(tuple(w.shape) != (man["hidden"], man["hidden"]) for w in ws):
+                raise ValueError(f"{path}: heads do not match their manifest")
+        if hidden is not None and any(tuple(w.shape) != (hidden, hidden) for w in ws):
+            raise ValueError(f"{path}: heads are not {hidden} x {hidden}")
         obj = cls.__new__(cls)
         obj.W = [w.to(device, torch.float32) for w in ws]
         obj.n_heads = len(ws)
@@ -46,6 +63,18 @@ class MedusaHeads:
 
     def state_dict(self) -> dict:
         return {f"head{i}": w.cpu() for i, w in enumerate(self.W)}
+
+    def save(self, path: str, fingerprint: bytes | None = None, target_name: str = "") -> str:
+        """State dict at ``path`` plus the ``<path>.draft.json`` manifest (kind, head count,
+        hidden size, target checkpoint fingerprint and name); returns the manifest path."""
+        import json
+        torch.save(self.state_dict(), path)
+        man = {"kind": "medusa", "n_heads": self.n_heads, "hidden": int(self.W[0].shape[0]),
+               "target_fingerprint": None if fingerprint is None else bytes(fingerprint).hex(),
+               "target_name": target_name}
+        with open(path + ".draft.json", "w") as f:
+            json.dump(man, f, indent=1)
+        return path + ".draft.json"
 
     def logits(self, h: torch.Tensor, lm_head_fn) -> list[torch.Tensor]:
         """h [S, H] final-norm hidden -> per head [S, V] logits."""

@@ -132,3 +132,23 @@ def test_oracle_hook_observes_and_masks_ffn():
     m.ffn_hook = None
     m.reset()
     assert torch.equal(m.forward(ids, 0), dense)
+
+
+def test_medusa_heads_manifest_sidecar(tmp_path):
+    from air_rs.spec.medusa import MedusaHeads
+    h = MedusaHeads(16, n_heads=11, device="cpu", seed=2)
+    p = str(tmp_path / "heads.pt")
+    man = h.save(p, fingerprint=b"\x07" * 32, target_name="llama-3-8b")
+    assert man.endswith(".draft.json")
+    back = MedusaHeads.load(p, device="cpu", fingerprint=b"\x07" * 32, hidden=16)
+    assert back.n_heads == 11 and all(torch.equal(a, b) for a, b in zip(h.W, back.W))   # head10 after head9
+    with pytest.raises(ValueError, match="another target"):
+        MedusaHeads.load(p, device="cpu", fingerprint=b"\x08" * 32)
+    with pytest.raises(ValueError, match="not 32 x 32"):
+        MedusaHeads.load(p, device="cpu", hidden=32)
+    import json
+    m = json.load(open(man))
+    m["n_heads"] = 3
+    json.dump(m, open(man, "w"))
+    with pytest.raises(ValueError, match="manifest"):
+        MedusaHeads.load(p, device="cpu")
