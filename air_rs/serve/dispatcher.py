@@ -154,6 +154,7 @@ class EngineDispatcher(Dispatcher):
                     self.errors += 1
                     for r in list(eng.running) + list(eng.waiting) + list(getattr(eng, "swapped", [])):
                         cb = getattr(r, "_on_done", None)
+                        r._on_done = None          # reported here; _reap must not report it again
                         eng.abort(r.rid)
                         if cb:
                             cb(FinishReason.ERROR, str(e))
@@ -222,11 +223,17 @@ class EngineDispatcher(Dispatcher):
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
 
+        def post(item):
+            try:
+                loop.call_soon_threadsafe(q.put_nowait, item)
+            except RuntimeError:           # the client's loop has closed (client went away)
+                pass
+
         def push(chunk):
-            loop.call_soon_threadsafe(q.put_nowait, chunk)
+            post(chunk)
 
         def done(reason, err):
-            loop.call_soon_threadsafe(q.put_nowait, TokenChunk(finish_reason=reason, error=err))
+            post(TokenChunk(finish_reason=reason, error=err))
 
         self._submit.put(("gen", config, push, done))
         while True:

@@ -8,10 +8,11 @@ the reference's council verifier accepted by a hash of the token ids.
 
 * ``MedusaDecoder``: K extra heads on the target's own final hidden state. Head k maps the
   hidden h_t of the last accepted position to logits for token t+1+k through a residual
-  SiLU block and the target's LM head (``lm(h + silu(W_k h))``); the draft tree takes the
+  SwiGLU block and the target's LM head (``lm(h + silu(h W1^T) * (h W2^T))``); the draft tree takes the
   top-c tokens of each head as the children of every node of the previous depth (cumulative
   probability order, capped node count). Heads are random-initialised here (no trained
-  checkpoints offline) and load from a ``.pt`` state dict.
+  checkpoints offline) and load from the reference's GGUF tensors ``mtp_head.{i}.weight0/1``
+  or from a ``.pt`` state dict with a ``.draft.json`` manifest.
 * ``CouncilDecoder`` (``--council``, ``--epsilon``): several voter drafts (draft engines)
   propose the next token; the council extends a draft chain only while the voters agree —
   the Jensen-Shannon divergence of their distributions is at most epsilon — with the
@@ -29,56 +30,116 @@ from .speculative import MAX_TREE_NODES, SpeculativeDecoder, _Seq
 
 
 class MedusaHeads:
+    """K draft heads, each one residual SwiGLU block on the final hidden state:
+    ``h' = h + silu(h W1^T) * (h W2^T)``, then the target's LM head (reference
+    ``src/medusa_heads.rs:71-94``). Weights are [hidden, hidden] pairs; random init uses
+    N(0, 1/hidden) like the reference's bootstrap heads."""
+
     def __init__(self, hidden: int, n_heads: int = 3, device="cuda", seed: int = 0, dtype=torch.float32,
-                 init_scale: float = 0.02):
+                 init_scale: float | None = None):
         g = torch.Generator().manual_seed(seed)
-        self.W = [(torch.randn(hidden, hidden, generator=g) * init_scale).to(device, dtype) for _ in range(n_heads)]
+        sc = init_scale if init_scale is not None else 1.0 / math.sqrt(hidden)
+        mk = lambda: (torch.randn(hidden, hidden, generator=g) * sc).to(device, dtype)
+        self.W = [(mk(), mk()) for _ in range(n_heads)]
         self.n_heads = n_heads
+
+    @staticmethod
+    def _from_pairs(ws, device) -> "MedusaHeads":
+        obj = MedusaHeads.__new__(MedusaHeads)
+        obj.W = [(a.to(device, torch.float32), b.to(device, torch.float32)) for a, b in ws]
+        obj.n_heads = len(ws)
+        return obj
+
+    @classmethod
+    def from_gguf(cls, path: str, n_heads: int | None = None, device="cuda") -> "MedusaHeads":
+        """Native multi-token heads stored in a GGUF checkpoint as ``mtp_head.{i}.weight0`` (W1)
+        and ``mtp_head.{i}.weight1`` (W2), the names the reference loads
+        (``src/medusa_heads.rs:137-160``). Heads are read in index order until one is missing
+        (or ``n_heads`` are read); a file with none raises."""
+        from ..gguf import read_gguf
+        f = read_gguf(path)
+        try:
+            ws, i = [], 0
+            while (n_heads is None or i < n_heads) and f.has(f"mtp_head.{i}.weight0"):
+                if not f.has(f"mtp_head.{i}.weight1"):
+                    raise ValueError(f"{path}: mtp_head.{i}.weight1 is missing")
+                ws.append((f.dequantize(f"mtp_head.{i}.weight0").float(),
+                           f.dequantize(f"mtp_head.{i}.weight1").float()))
+                i += 1
+        finally:
+            f.close()
+        if not ws:
+            raise ValueError(f"{path}: no mtp_head.<i>.weight0/weight1 tensors")
+        if n_heads is not None and len(ws) < n_heads:
+            raise ValueError(f"{path}: {n_heads} heads requested, {len(ws)} present")
+        hid = ws[0][0].shape[0]
+        if any(tuple(t.shape) != (hid, hid) for pair in ws for t in pair):
+            raise ValueError(f"{path}: MTP heads are not square and equal-sized")
+        return cls._from_pairs(ws, device)
 
     @classmethod
     def load(cls, path: str, device="cuda", fingerprint: bytes | None = None,
              hidden: int | None = None) -> "MedusaHeads":
-        """Heads from a state dict; a ``<path>.draft.json`` manifest next to it, when present,
+        """Heads from a ``.gguf`` (``from_gguf``) or a torch state dict (keys ``head<i>.w1`` /
+        ``head<i>.w2``). A ``<path>.draft.json`` manifest next to a state dict, when present,
         must match ``fingerprint`` (the target checkpoint's, ``parallel.pd.gguf_fingerprint``)
         and ``hidden``, and the heads must match the manifest."""
         import json
         import os
+        import re
+        if path.endswith(".gguf"):
+            heads = cls.from_gguf(path, device=device)
+            if hidden is not None and heads.W[0][0].shape[0] != hidden:
+                raise ValueError(f"{path}: heads are not {hidden} x {hidden}")
+            return heads
         sd = torch.load(path, map_location="cpu", weights_only=True)
-        keys = sorted((k for k in sd if k.startswith("head")), key=lambda k: int(k[4:]))
-        ws = [sd[k] for k in keys]
+        idx = {}
+        for k in sd:
+            m = re.fullmatch(r"head(\d+)\.w([12])", k)
+            if m is None:
+                raise ValueError(f"{path}: unexpected key {k!r} (expected head<i>.w1 / head<i>.w2)")
+            idx.setdefault(int(m.group(1)), {})[m.group(2)] = sd[k]
+        if not idx or sorted(idx) != list(range(len(idx))) or any(len(v) != 2 for v in idx.values()):
+            raise ValueError(f"{path}: heads must be numbered 0..n-1, each with w1 and w2")
+        ws = [(idx[i]["1"], idx[i]["2"]) for i in range(len(idx))]
         man_path = path + ".draft.json"
         if os.path.exists(man_path):
             with open(man_path) as f:
                 man = json.load(f)
             if fingerprint is not None and man.get("target_fingerprint") not in (None, bytes(fingerprint).hex()):
                 raise ValueError(f"{path}: draft heads were trained for another target ({man.get('target_name')!r})")
-            if man.get("n_heads") != len(ws) or any(tuple(w.shape) != (man["hidden"], man["hidden"]) for w in ws):
+            if man.get("n_heads") != len(ws) or any(tuple(w.shape) != (man["hidden"], man["hidden"])
+                                                    for pair in ws for w in pair):
                 raise ValueError(f"{path}: heads do not match their manifest")
-        if hidden is not None and any(tuple(w.shape) != (hidden, hidden) for w in ws):
+        if hidden is not None and any(tuple(w.shape) != (hidden, hidden) for pair in ws for w in pair):
             raise ValueError(f"{path}: heads are not {hidden} x {hidden}")
-        obj = cls.__new__(cls)
-        obj.W = [w.to(device, torch.float32) for w in ws]
-        obj.n_heads = len(ws)
-        return obj
+        return cls._from_pairs(ws, device)
 
     def state_dict(self) -> dict:
-        return {f"head{i}": w.cpu() for i, w in enumerate(self.W)}
+        sd = {}
+        for i, (a, b) in enumerate(self.W):
+            sd[f"head{i}.w1"], sd[f"head{i}.w2"] = a.cpu(), b.cpu()
+        return sd
 
     def save(self, path: str, fingerprint: bytes | None = None, target_name: str = "") -> str:
         """State dict at ``path`` plus the ``<path>.draft.json`` manifest (kind, head count,
         hidden size, target checkpoint fingerprint and name); returns the manifest path."""
         import json
         torch.save(self.state_dict(), path)
-        man = {"kind": "medusa", "n_heads": self.n_heads, "hidden": int(self.W[0].shape[0]),
+        man = {"kind": "medusa", "n_heads": self.n_heads, "hidden": int(self.W[0][0].shape[0]),
                "target_fingerprint": None if fingerprint is None else bytes(fingerprint).hex(),
                "target_name": target_name}
         with open(path + ".draft.json", "w") as f:
             json.dump(man, f, indent=1)
         return path + ".draft.json"
 
+    def hidden(self, h: torch.Tensor) -> list[torch.Tensor]:
+        """h [S, H] -> per head the transformed hidden state [S, H]."""
+        return [h + torch.nn.functional.silu(h @ w1.t()) * (h @ w2.t()) for w1, w2 in self.W]
+
     def logits(self, h: torch.Tensor, lm_head_fn) -> list[torch.Tensor]:
         """h [S, H] final-norm hidden -> per head [S, V] logits."""
-        return [lm_head_fn(h + torch.nn.functional.silu(h @ w.t())) for w in self.W]
+        return [lm_head_fn(t) for t in self.hidden(h)]
 
 
 class MedusaDecoder(SpeculativeDecoder):

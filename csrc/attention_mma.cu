@@ -270,11 +270,8 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
 template <int G>
 void launch_g(const AttnArgs& a, cudaStream_t st) {
   const int smem = kWarpsM * 4 * kTile + kWarpsM * 16 * kD * 4;  // 64 KB tiles + 32 KB merge
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(paged_attn_mma_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  set_max_smem_per_device(paged_attn_mma_kernel<G>, smem, attr_done);
   dim3 grid(a.n_kv, a.n_rows, a.n_splits);
   paged_attn_mma_kernel<G><<<grid, kWarpsM * 32, smem, st>>>(
       a.q, (const __nv_bfloat16*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_heads, a.n_kv,

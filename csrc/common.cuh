@@ -19,6 +19,21 @@ enum ErrorCode : int {
   kErrBadArg = 3,
 };
 
+// Raise a kernel's dynamic shared-memory limit on the current device, once per device.
+// cudaFuncSetAttribute applies to the device that is current when it is called, so a
+// process that launches the same kernel on several GPUs must set it on each of them.
+// `done` is a per-kernel bitmask of the devices already set (devices 0..63).
+template <class Kernel>
+inline bool set_max_smem_per_device(Kernel kernel, int bytes, unsigned long long& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  const unsigned long long bit = 1ull << dev;
+  if (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  __atomic_fetch_or(&done, bit, __ATOMIC_ACQ_REL);
+  return true;
+}
+
 AIR_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -568,13 +568,9 @@ const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, con
   if (!encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)a.K, (uint64_t)a.T,
                  (uint64_t)ldx * 2, 64, NT, CU_TENSOR_MAP_SWIZZLE_128B))
     return "cuTensorMapEncodeTiled failed for the activation operand";
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemLaunch) !=
-        cudaSuccess)
-      return "cudaFuncSetAttribute(max dynamic smem) failed";
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (!set_max_smem_per_device(gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS>, C::kSmemLaunch, attr_done))
+    return "cudaFuncSetAttribute(max dynamic smem) failed";
   gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS><<<grid, (AT ? 96 : 64) + 32 * DQ, C::kSmemLaunch, st>>>(tw, tx, b);
   return nullptr;
 }

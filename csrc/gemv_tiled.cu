@@ -428,13 +428,9 @@ const char* launch_t(const GemvWeight& w, int N, int K, int B, const int8_t* xq,
     if (k < 2) k = 2;
     return (int)k;
   };
-  static size_t attr = 0;
-  if (attr == 0) {
-    if (cudaFuncSetAttribute(gemv_tiled_kernel<MAXB, DUAL, TPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             227 * 1024) != cudaSuccess)
-      return "gemv_tiled: cudaFuncSetAttribute failed";
-    attr = 227 * 1024;
-  }
+  static unsigned long long attr_done = 0;
+  if (!set_max_smem_per_device(gemv_tiled_kernel<MAXB, DUAL, TPR>, 227 * 1024, attr_done))
+    return "gemv_tiled: cudaFuncSetAttribute failed";
   int kper = kper_for(cap);
   int occ = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_tiled_kernel<MAXB, DUAL, TPR>, kRows * TPR,

@@ -41,7 +41,7 @@ int scratch_for_current_device(unsigned char** out) {
 extern "C" __attribute__((visibility("default"))) int air_gemv_q4k_noalloc(
     const void* w_tiled, int N, int K, int B, const int8_t* xq, const void* xds, float* out, int* err,
     cudaStream_t stream) {
-  if (!w_tiled || !xq || !xds || !out || N <= 0 || K <= 0 || K % 256 != 0 || B < 1 || B > 8)
+  if (!w_tiled || !xq || !xds || !out || !err || N <= 0 || K <= 0 || K % 256 != 0 || B < 1 || B > 8)
     return AIR_NOALLOC_BAD_ARGUMENT;
   // grid cap: as many CTAs as the static array has split-K partial slots for
   const int per_cta = (int)(air::gemv_tiled_workspace_floats(N, 1, air::kEpiStore) * sizeof(float));
@@ -49,17 +49,17 @@ extern "C" __attribute__((visibility("default"))) int air_gemv_q4k_noalloc(
   int splits = air::gemv_tiled_splits(N, K, air::kEpiStore);
   splits = splits < fit ? splits : fit;
   const size_t counters = air::gemv_tiled_counters(N);
-  const size_t ws_bytes = air::gemv_tiled_workspace_floats(N, splits, air::kEpiStore) * sizeof(float);
-  if (counters > kMaxCounters || kHeaderBytes + ws_bytes > AIR_NOALLOC_SCRATCH_BYTES) return AIR_NOALLOC_TOO_LARGE;
+  // The split count above is capped to what the array holds, so the partials always fit;
+  // the one real limit is the tile-counter header (N <= AIR_NOALLOC_MAX_N).
+  if (counters > kMaxCounters) return AIR_NOALLOC_TOO_LARGE;
 
   unsigned char* scratch = nullptr;
   const int st = scratch_for_current_device(&scratch);
   if (st != AIR_NOALLOC_OK) return st;
-  int* err_word = err ? err : reinterpret_cast<int*>(scratch);
   int* cnt = reinterpret_cast<int*>(scratch) + 1;
   float* ws = reinterpret_cast<float*>(scratch + kHeaderBytes);
   // The counters must start at zero; a previous call that gave up early could have left
-  // them raised. (The scratch err word is cleared with them; a caller's err is left alone.)
+  // them raised. The caller's err word is left alone (it accumulates across calls).
   if (cudaMemsetAsync(scratch, 0, (counters + 1) * sizeof(int), stream) != cudaSuccess) {
     cudaGetLastError();
     return AIR_NOALLOC_LAUNCH_FAILED;
@@ -70,7 +70,7 @@ extern "C" __attribute__((visibility("default"))) int air_gemv_q4k_noalloc(
   ep.mode = air::kEpiStore;
   ep.out_f32 = out;
   ep.ld_out = N;
-  ep.err = err_word;
+  ep.err = err;
   air::GemvTiledScratch sc{ws, cnt};
   const char* e = air::launch_gemv_tiled(w, N, K, B, xq, static_cast<const float2*>(xds), ep, sc, splits, stream);
   if (e != nullptr || cudaGetLastError() != cudaSuccess) return AIR_NOALLOC_LAUNCH_FAILED;
@@ -80,8 +80,8 @@ extern "C" __attribute__((visibility("default"))) int air_gemv_q4k_noalloc(
 extern "C" __attribute__((visibility("default"))) const char* air_noalloc_status_string(int status) {
   switch (status) {
     case AIR_NOALLOC_OK: return "ok";
-    case AIR_NOALLOC_BAD_ARGUMENT: return "bad argument (null pointer, B not in [1, 8], K not a multiple of 256, or N <= 0)";
-    case AIR_NOALLOC_TOO_LARGE: return "shape needs more split-K scratch than the 4 MiB static array holds";
+    case AIR_NOALLOC_BAD_ARGUMENT: return "bad argument (null pointer, err included; B not in [1, 8]; K not a multiple of 256; or N <= 0)";
+    case AIR_NOALLOC_TOO_LARGE: return "N above 2,097,024 (16383 tiles of 128 rows): more tile counters than the static array's header holds";
     case AIR_NOALLOC_SETUP_FAILED: return "could not resolve the scratch array's device address on the current device";
     case AIR_NOALLOC_LAUNCH_FAILED: return "kernel launch or scratch clear failed";
     default: return "unknown status";

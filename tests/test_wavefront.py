@@ -141,7 +141,7 @@ def test_medusa_heads_manifest_sidecar(tmp_path):
     man = h.save(p, fingerprint=b"\x07" * 32, target_name="llama-3-8b")
     assert man.endswith(".draft.json")
     back = MedusaHeads.load(p, device="cpu", fingerprint=b"\x07" * 32, hidden=16)
-    assert back.n_heads == 11 and all(torch.equal(a, b) for a, b in zip(h.W, back.W))   # head10 after head9
+    assert back.n_heads == 11 and all(torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]) for a, b in zip(h.W, back.W))   # head10 after head9
     with pytest.raises(ValueError, match="another target"):
         MedusaHeads.load(p, device="cpu", fingerprint=b"\x08" * 32)
     with pytest.raises(ValueError, match="not 32 x 32"):
@@ -151,4 +151,36 @@ def test_medusa_heads_manifest_sidecar(tmp_path):
     m["n_heads"] = 3
     json.dump(m, open(man, "w"))
     with pytest.raises(ValueError, match="manifest"):
+        MedusaHeads.load(p, device="cpu")
+
+
+def test_medusa_heads_math_and_gguf(tmp_path):
+    """Residual SwiGLU block h + silu(h W1^T) * (h W2^T) (reference src/medusa_heads.rs:89-94),
+    loaded from GGUF tensors mtp_head.{i}.weight0/weight1."""
+    import torch.nn.functional as F
+    from air_rs.gguf import GGMLType
+    from air_rs.gguf.writer import GGUFWriter
+    from air_rs.spec.medusa import MedusaHeads
+    g = torch.Generator().manual_seed(5)
+    pairs = [(torch.randn(16, 16, generator=g), torch.randn(16, 16, generator=g)) for _ in range(2)]
+    p = str(tmp_path / "mtp.gguf")
+    wr = GGUFWriter(p)
+    for i, (a, b) in enumerate(pairs):
+        wr.add_tensor(f"mtp_head.{i}.weight0", a.contiguous().view(torch.uint8).flatten(), (16, 16), GGMLType.F32)
+        wr.add_tensor(f"mtp_head.{i}.weight1", b.contiguous().view(torch.uint8).flatten(), (16, 16), GGMLType.F32)
+    wr.write()
+    heads = MedusaHeads.load(p, device="cpu", hidden=16)
+    assert heads.n_heads == 2
+    h = torch.randn(3, 16, generator=g)
+    for (a, b), t in zip(pairs, heads.hidden(h)):
+        torch.testing.assert_close(t, h + F.silu(h @ a.t()) * (h @ b.t()))
+    with pytest.raises(ValueError, match="requested"):
+        MedusaHeads.from_gguf(p, n_heads=3, device="cpu")
+
+
+def test_medusa_heads_bad_keys(tmp_path):
+    from air_rs.spec.medusa import MedusaHeads
+    p = str(tmp_path / "bad.pt")
+    torch.save({"head_norm": torch.zeros(4)}, p)
+    with pytest.raises(ValueError, match="unexpected key"):
         MedusaHeads.load(p, device="cpu")

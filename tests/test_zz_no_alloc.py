@@ -64,5 +64,6 @@ def test_noalloc_rejects_bad_shapes():
     p = dummy.data_ptr()
     assert fn(p, 128, 300, 1, p, p, p, None, None) == 1      # K not a multiple of 256
     assert fn(p, 128, 256, 9, p, p, p, None, None) == 1      # batch above 8
-    rc = fn(p, 1 << 22, 1 << 16, 8, p, p, p, None, None)     # workspace beyond 4 MiB
+    assert fn(p, 128, 256, 1, p, p, p, None, None) == 1      # err word is required
+    rc = fn(p, 16384 * 128, 256, 8, p, p, p, p, None)        # N one tile above the counter header
     assert rc == 2, msg(rc).decode()
