@@ -14,7 +14,7 @@ import torch
 
 from . import QWeight, require_ext, FMT_BF16, FMT_Q4K, count_launch
 
-GEMM_STORE_F32, GEMM_STORE_BF16, GEMM_RESIDUAL = 0, 1, 2
+GEMM_STORE_F32, GEMM_STORE_BF16, GEMM_RESIDUAL, GEMM_PEER_PUSH = 0, 1, 2, 3
 
 
 def _baseline_forced() -> bool:
@@ -67,15 +67,20 @@ def workspace(device) -> _Workspace:
 
 def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, residual: bool = False,
            splits: int | None = None, err: torch.Tensor | None = None,
-           dbg: torch.Tensor | None = None, row_count: torch.Tensor | None = None) -> torch.Tensor:
+           dbg: torch.Tensor | None = None, row_count: torch.Tensor | None = None,
+           push_meta: torch.Tensor | None = None) -> torch.Tensor:
     """out = x @ W^T (or out += x @ W^T when residual, out fp32). ``row_count`` (device int32)
-    limits the tensor-core path to the first rows (token tiles past it exit at once)."""
+    limits the tensor-core path to the first rows (token tiles past it exit at once).
+    ``push_meta`` (a ``PeerComm`` push table): the epilogue stores the result into the
+    tensor-parallel peer receive buffers instead of ``out`` (tensor-core path only)."""
     T = x.shape[0]
     if T == 0:
         return out
     if tc_supported(w):
         ext = require_ext()
-        if residual:
+        if push_meta is not None:
+            mode = GEMM_PEER_PUSH
+        elif residual:
             mode = GEMM_RESIDUAL
         else:
             mode = GEMM_STORE_BF16 if out.dtype == torch.bfloat16 else GEMM_STORE_F32
@@ -86,9 +91,12 @@ def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, resid
                                                  ext.gemm_q_counters(w.N, T))
         if err is None:
             err = workspace(x.device).err
-        ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out, mode, s, ws, cnt, err, dbg, row_count)
+        ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out, mode, s, ws, cnt, err, dbg, row_count,
+                   push_meta)
         count_launch()
         return out
+    if push_meta is not None:
+        raise ValueError("peer-push GEMM epilogue needs the tensor-core path")
     if residual:
         tmp = linear_baseline(x, w, torch.empty(T, w.N, dtype=torch.float32, device=x.device), runner)
         out.add_(tmp)

@@ -214,8 +214,12 @@ class ModelRunner:
         happens in the next ``_norm`` (decode only)."""
         T = xin.shape[0]
         if peer is not None:
-            self.linear(xin, w, self.y[:T])
-            peer.push(self.y[:T], T)
+            from ..ops import gemm
+            if gemm.tc_supported(w):
+                peer.push_gemm(xin, w, self.y[:T], err=self.err)   # push from the GEMM epilogue
+            else:
+                self.linear(xin, w, self.y[:T])
+                peer.push(self.y[:T], T)
         elif tp:
             self.linear(xin, w, obuf[:T])
             self._residual_T(obuf[:T], T, x, tp)

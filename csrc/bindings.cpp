@@ -122,7 +122,8 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
   if (mode == air::kEpiPeerPush) {
     TORCH_CHECK(push_meta.has_value() && fmt == air::kFmtQ4K, "gemv peer push: Q4_K tiled weights and push meta");
     ep.push = peer_push_from_meta(*push_meta);
-    TORCH_CHECK(B * ld_out <= ep.push.slot_elems, "gemv peer push: output exceeds the receive slot");
+    TORCH_CHECK(N == ep.push.row_len && B * ep.push.row_len <= ep.push.slot_elems,
+                "gemv peer push: output [B, N] must fit the receive slot, N = its row length");
   }
   if (mode == air::kEpiResidual) TORCH_CHECK(ep.resid, "gemv residual: resid required");
   if (mode == air::kEpiQKVRope)

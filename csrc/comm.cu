@@ -15,6 +15,7 @@ constexpr int kMaxPer = 16;   // K <= 16 * 1024
 __device__ __forceinline__ float wait_tagged(const uint2* p, uint32_t tag, int64_t timeout_ns, bool& timed_out) {
   uint2 v = ld_tagged(p);
   if (v.y == tag) return __uint_as_float(v.x);
+  if (timed_out) return 0.f;          // an earlier wait of this thread already gave up
   const uint64_t t0 = sm100::global_ns();
   for (uint32_t it = 1;; ++it) {
     v = ld_tagged(p);
@@ -26,41 +27,74 @@ __device__ __forceinline__ float wait_tagged(const uint2* p, uint32_t tag, int64
   }
 }
 
-// Grid (1, B): one CTA per row, so the reduced row can be held in registers between the
-// sum-of-squares pass and the quantisation pass (no other CTA reads x meanwhile).
-__global__ void __launch_bounds__(kThreads)
-reduce_rmsnorm_quant_kernel(PeerReduce r, float* __restrict__ x, const float* __restrict__ w, float w_offset,
-                            int K, float eps, int8_t* __restrict__ q, float2* __restrict__ ds,
-                            __nv_bfloat16* __restrict__ y_out) {
+// Grid (1, B, n_local): one CTA per (row, rank), so the reduced row can be held in registers
+// between the sum-of-squares pass and the quantisation pass. In two-shot mode a CTA first
+// reduces its rank's columns of the row and all-gathers them, then waits for the rest of
+// the row from the other owners; every CTA of every rank is resident at once (B * n_local
+// <= 2 * 148 is checked by the host), so these cross-CTA waits always make progress.
+template <bool TWO>
+__global__ void __launch_bounds__(kThreads) tp_reduce_norm_kernel(const __grid_constant__ TPReduceArgs a) {
   pdl_trigger();   // a dependent GEMV may start streaming its weights now
   __shared__ float red[32];
-  const int b = blockIdx.y, t = threadIdx.x;
-  const int e = *(volatile const int*)r.epoch;
+  const TPReduceRank& R = a.r[blockIdx.z];
+  const int b = blockIdx.y, t = threadIdx.x, K = a.K;
+  const int e = *(volatile const int*)R.epoch;
   const uint32_t tag = (uint32_t)e + 1u;
-  const uint2* base = r.data + (int64_t)(e & 1) * r.world * r.slot_elems + (int64_t)b * K;
+  const int par = e & 1;
   bool timed_out = false;
-  // ---- x += sum of partials (each element waits for its tag); sum of squares ----
+  float* xr = R.x + (size_t)b * K;
   float v[kMaxPer];
   float ss = 0.f;
-  float* xr = x + (size_t)b * K;
-#pragma unroll
-  for (int j = 0; j < kMaxPer; ++j) {
-    const int i = j * kThreads + t;
-    v[j] = 0.f;
-    if (i < K) {
+  if (TWO) {
+    // ---- reduce-scatter half: this rank's columns [c0, c1) of row b ----
+    const int64_t S = a.shard;
+    const int c0 = (int)(R.rank * S);
+    const int c1 = min(K, (int)(c0 + S));
+    const uint2* rs = R.rs + (int64_t)par * a.world * a.slot_elems + (int64_t)b * S;
+    const int64_t ag_off = (int64_t)par * a.slot_elems + (int64_t)b * K;
+    for (int i = c0 + t; i < c1; i += kThreads) {
       float s = xr[i];
-      for (int src = 0; src < r.world; ++src)
-        s += wait_tagged(base + (int64_t)src * r.slot_elems + i, tag, r.timeout_ns, timed_out);
-      xr[i] = s;
-      v[j] = s;
-      ss += s * s;
+      for (int src = 0; src < a.world; ++src)
+        s += wait_tagged(rs + (int64_t)src * a.slot_elems + (i - c0), tag, a.timeout_ns, timed_out);
+#pragma unroll
+      for (int d = 0; d < kMaxPeers; ++d)
+        if (d < a.world) st_tagged(R.ag_peer[d] + ag_off + i, s, tag);
+    }
+    // ---- all-gather half: the whole row from its owners (local memory) ----
+    const uint2* ag = R.ag + ag_off;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+      const int i = j * kThreads + t;
+      v[j] = 0.f;
+      if (i < K) {
+        const float s = wait_tagged(ag + i, tag, a.timeout_ns, timed_out);
+        xr[i] = s;
+        v[j] = s;
+        ss += s * s;
+      }
+    }
+  } else {
+    // ---- one-shot: x += sum of every rank's whole partial ----
+    const uint2* base = R.rs + (int64_t)par * a.world * a.slot_elems + (int64_t)b * K;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+      const int i = j * kThreads + t;
+      v[j] = 0.f;
+      if (i < K) {
+        float s = xr[i];
+        for (int src = 0; src < a.world; ++src)
+          s += wait_tagged(base + (int64_t)src * a.slot_elems + i, tag, a.timeout_ns, timed_out);
+        xr[i] = s;
+        v[j] = s;
+        ss += s * s;
+      }
     }
   }
-  if (timed_out) set_error(r.err, kErrTimeout);
+  if (timed_out) set_error(R.err, kErrTimeout);
   float scale = 1.f;
-  if (w) {
+  if (a.w) {
     ss = block_sum(ss, red);
-    scale = rsqrtf(ss / (float)K + eps);
+    scale = rsqrtf(ss / (float)K + a.eps);
   }
   const int lane = t & 31;
 #pragma unroll
@@ -68,26 +102,26 @@ reduce_rmsnorm_quant_kernel(PeerReduce r, float* __restrict__ x, const float* __
     const int i = j * kThreads + t;
     if (j * kThreads >= K) break;          // uniform across the CTA
     float y = v[j] * scale;
-    if (w && i < K) y *= (w[i] + w_offset);
-    if (i < K && y_out) y_out[(size_t)b * K + i] = f2bf(y);
-    if (q) {
+    if (a.w && i < K) y *= (a.w[i] + a.w_offset);
+    if (i < K && R.y_bf16) static_cast<__nv_bfloat16*>(R.y_bf16)[(size_t)b * K + i] = f2bf(y);
+    if (R.q) {
       // a warp covers 32 consecutive elements = one Q8A group (K % 32 == 0)
       const float amax = warp_max(i < K ? fabsf(y) : 0.f);
       const float d = amax / 127.f;
       int qi = (d > 0.f && i < K) ? __float2int_rn(y / d) : 0;
       qi = max(-127, min(127, qi));
-      if (i < K) q[(size_t)b * K + i] = (int8_t)qi;
+      if (i < K) R.q[(size_t)b * K + i] = (int8_t)qi;
       const int s = warp_sum_i(qi);
-      if (lane == 0 && i < K) ds[(size_t)b * (K / 32) + i / 32] = make_float2(d, d * (float)s);
+      if (lane == 0 && i < K) R.ds[(size_t)b * (K / 32) + i / 32] = make_float2(d, d * (float)s);
     }
   }
-  // ---- the last CTA advances the epoch (every CTA read it before arriving) ----
+  // ---- the rank's last CTA advances its epoch (every CTA read it before arriving) ----
   __syncthreads();
   if (t == 0) {
     __threadfence();
-    if (atomicAdd(r.done, 1) == (int)gridDim.y - 1) {
-      *r.done = 0;
-      *r.epoch = e + 1;
+    if (atomicAdd(R.done, 1) == (int)gridDim.y - 1) {
+      *R.done = 0;
+      *R.epoch = e + 1;
       __threadfence();
     }
   }
@@ -99,16 +133,18 @@ peer_push_kernel(PeerPush p, const float* __restrict__ src, int B, int N, int64_
   const int64_t n = (int64_t)B * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t b = i / N, c = i % N;
-    peer_store(p, e, b * ld + c, __ldcg(src + b * ld + c));
+    peer_store(p, e, b, c, __ldcg(src + b * ld + c));
   }
 }
 
 }  // namespace
 
-void launch_reduce_rmsnorm_quant(const PeerReduce& r, float* x, const float* w, float w_offset, int B, int K,
-                                 float eps, int8_t* q, float2* ds, void* y_bf16, cudaStream_t st) {
-  reduce_rmsnorm_quant_kernel<<<dim3(1, B), kThreads, 0, st>>>(r, x, w, w_offset, K, eps, q, ds,
-                                                              (__nv_bfloat16*)y_bf16);
+void launch_tp_reduce_norm(const TPReduceArgs& a, cudaStream_t st) {
+  const dim3 grid(1, a.B, a.n_local);
+  if (a.shard > 0)
+    tp_reduce_norm_kernel<true><<<grid, kThreads, 0, st>>>(a);
+  else
+    tp_reduce_norm_kernel<false><<<grid, kThreads, 0, st>>>(a);
 }
 
 void launch_peer_push(const PeerPush& p, const float* src, int B, int N, int64_t ld, cudaStream_t st) {

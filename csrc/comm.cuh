@@ -23,12 +23,22 @@ AIR_DEVICE uint2 ld_tagged(const uint2* p) {
   return v;
 }
 
-// Store one partial-sum element, tagged epoch + 1, into slot (parity, this rank) of every
-// rank's buffer. The peer loop is unrolled over the compile-time maximum so the pointer
-// table stays in the parameter space.
-AIR_DEVICE void peer_store(const PeerPush& p, int epoch, int64_t idx, float v) {
-  const int64_t off = ((int64_t)(epoch & 1) * p.world + p.rank) * p.slot_elems + idx;
+// Store element (b, c) of a partial, tagged epoch + 1, into region (parity, this rank) of
+// the receive buffers: every rank's (one-shot) or the owner's of column c (two-shot). The
+// peer loop is unrolled over the compile-time maximum so the pointer table stays in the
+// parameter space.
+AIR_DEVICE void peer_store(const PeerPush& p, int epoch, int64_t b, int64_t c, float v) {
+  const int64_t region = ((int64_t)(epoch & 1) * p.world + p.rank) * p.slot_elems;
   const uint32_t tag = (uint32_t)epoch + 1u;
+  if (p.shard > 0) {
+    const int o = (int)(c / p.shard);
+    const int64_t cl = c - (int64_t)o * p.shard;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r == o) st_tagged(p.data[r] + region + b * p.shard + cl, v, tag);
+    return;
+  }
+  const int64_t off = region + b * p.row_len + c;
 #pragma unroll
   for (int r = 0; r < kMaxPeers; ++r)
     if (r < p.world) st_tagged(p.data[r] + off, v, tag);

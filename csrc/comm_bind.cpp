@@ -3,12 +3,14 @@
 // export/import between the ranks' processes, and the producer/consumer launches.
 //
 // Pointer tables travel as int64 CPU tensors ("meta"):
-//   push meta  : data[8], epoch, slot_elems, world, rank
-//   reduce meta: data, epoch, done, err, slot_elems, world, timeout_ns
+//   push meta  : data[8], epoch, slot_elems, world, rank, row_len, shard
+//   reduce meta: rs, ag, ag_peer[8], epoch, done, err, slot_elems, world, rank, timeout_ns, shard
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cstring>
+#include <vector>
+#include <torch/csrc/utils/pybind.h>
 
 #include "comm.h"
 
@@ -62,32 +64,80 @@ bool enable_peer_access(int64_t device, int64_t peer) {
 
 void ipc_close(int64_t ptr) { ck(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)), "cudaIpcCloseMemHandle"); }
 
-void reduce_rmsnorm_quant(const Tensor& meta, Tensor x, optional<Tensor> w, double w_offset, double eps, int64_t B,
-                          int64_t K, optional<Tensor> q, optional<Tensor> ds, optional<Tensor> y_bf16) {
-  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 7, "reduce meta");
-  TORCH_CHECK(K % 32 == 0 && K <= 16384, "reduce_rmsnorm_quant: K must be a multiple of 32, <= 16384");
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat && x.is_contiguous(), "x must be contiguous fp32 CUDA");
+// reduce meta: rs, ag, ag_peer[8], epoch, done, err, slot_elems, world, rank, timeout_ns, shard
+air::TPReduceRank reduce_rank_from_meta(const Tensor& meta, int64_t* slot, int* world, int64_t* timeout,
+                                        int64_t* shard) {
+  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 18, "reduce meta");
   const int64_t* m = meta.data_ptr<int64_t>();
-  air::PeerReduce r{};
-  r.data = reinterpret_cast<const uint2*>(m[0]);
-  r.epoch = reinterpret_cast<int*>(m[1]);
-  r.done = reinterpret_cast<int*>(m[2]);
-  r.err = reinterpret_cast<int*>(m[3]);
-  r.slot_elems = m[4];
-  r.world = (int)m[5];
-  r.timeout_ns = m[6];
-  TORCH_CHECK(B * K <= r.slot_elems, "reduce_rmsnorm_quant: B*K exceeds the receive slot");
+  air::TPReduceRank r{};
+  r.rs = reinterpret_cast<const uint2*>(m[0]);
+  r.ag = reinterpret_cast<const uint2*>(m[1]);
+  for (int i = 0; i < air::kMaxPeers; ++i) r.ag_peer[i] = reinterpret_cast<uint2*>(m[2 + i]);
+  r.epoch = reinterpret_cast<int*>(m[10]);
+  r.done = reinterpret_cast<int*>(m[11]);
+  r.err = reinterpret_cast<int*>(m[12]);
+  *slot = m[13];
+  *world = (int)m[14];
+  r.rank = (int)m[15];
+  *timeout = m[16];
+  *shard = m[17];
+  return r;
+}
+
+// x[b] += sum of the ranks' partials, then RMSNorm (+ Q8A / bf16 outputs). One meta (and one
+// x / q / ds / y) per rank handled by this launch: a real TP group passes one; the
+// single-GPU emulation of a group passes all of them, so the two-shot exchange between ranks
+// happens inside one launch.
+void tp_reduce_norm(const std::vector<Tensor>& metas, const std::vector<Tensor>& xs, optional<Tensor> w,
+                    double w_offset, double eps, int64_t B, int64_t K, const std::vector<optional<Tensor>>& qs,
+                    const std::vector<optional<Tensor>>& dss, const std::vector<optional<Tensor>>& ys,
+                    bool two_shot) {
+  const int n = (int)metas.size();
+  TORCH_CHECK(n >= 1 && n <= air::kMaxPeers && (int)xs.size() == n, "tp_reduce_norm: 1..8 ranks, one x each");
+  TORCH_CHECK(qs.empty() || (int)qs.size() == n, "tp_reduce_norm: q per rank");
+  TORCH_CHECK(dss.empty() || (int)dss.size() == n, "tp_reduce_norm: ds per rank");
+  TORCH_CHECK(ys.empty() || (int)ys.size() == n, "tp_reduce_norm: y per rank");
+  TORCH_CHECK(K % 32 == 0 && K <= 16384, "tp_reduce_norm: K must be a multiple of 32, <= 16384");
+  // two-shot CTAs wait for the other ranks' CTAs of the same launch (emulated group) or of
+  // the peers' launches: every CTA must be resident at once (one 1024-thread CTA per SM)
+  TORCH_CHECK(B >= 1 && (!two_shot || B * n <= 148), "tp_reduce_norm: two-shot needs B x ranks-in-launch <= 148");
   auto p = [](const optional<Tensor>& t) { return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr; };
-  air::launch_reduce_rmsnorm_quant(r, x.data_ptr<float>(), static_cast<const float*>(p(w)), (float)w_offset,
-                                   (int)B, (int)K, (float)eps, static_cast<int8_t*>(p(q)), static_cast<float2*>(p(ds)),
-                                   p(y_bf16), at::cuda::getCurrentCUDAStream());
-  ck(cudaGetLastError(), "reduce_rmsnorm_quant");
+  air::TPReduceArgs a{};
+  a.n_local = n;
+  for (int i = 0; i < n; ++i) {
+    int64_t slot, timeout, shard;
+    int world;
+    a.r[i] = reduce_rank_from_meta(metas[i], &slot, &world, &timeout, &shard);
+    a.slot_elems = slot;
+    a.world = world;
+    a.timeout_ns = timeout;
+    a.shard = two_shot ? shard : 0;
+    TORCH_CHECK(B * K <= slot, "tp_reduce_norm: B*K exceeds the receive slot");
+    TORCH_CHECK(!two_shot || (shard > 0 && shard % 32 == 0 && shard * world >= K),
+                "tp_reduce_norm: two-shot needs a positive shard, a multiple of 32, covering K");
+    const Tensor& x = xs[i];
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat && x.is_contiguous() && x.numel() >= B * K,
+                "x must be contiguous fp32 CUDA [B, K]");
+    a.r[i].x = x.data_ptr<float>();
+    a.r[i].q = qs.empty() ? nullptr : static_cast<int8_t*>(p(qs[i]));
+    a.r[i].ds = dss.empty() ? nullptr : static_cast<float2*>(p(dss[i]));
+    a.r[i].y_bf16 = ys.empty() ? nullptr : p(ys[i]);
+    TORCH_CHECK((a.r[i].q == nullptr) == (a.r[i].ds == nullptr), "tp_reduce_norm: q and ds go together");
+  }
+  a.w = static_cast<const float*>(p(w));
+  a.w_offset = (float)w_offset;
+  a.eps = (float)eps;
+  a.B = (int)B;
+  a.K = (int)K;
+  air::launch_tp_reduce_norm(a, at::cuda::getCurrentCUDAStream());
+  ck(cudaGetLastError(), "tp_reduce_norm");
 }
 
 }  // namespace
 
+// push meta: data[8], epoch, slot_elems, world, rank, row_len, shard
 air::PeerPush peer_push_from_meta(const Tensor& meta) {
-  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 12, "push meta");
+  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 14, "push meta");
   const int64_t* m = meta.data_ptr<int64_t>();
   air::PeerPush p{};
   for (int i = 0; i < air::kMaxPeers; ++i) p.data[i] = reinterpret_cast<uint2*>(m[i]);
@@ -95,7 +145,11 @@ air::PeerPush peer_push_from_meta(const Tensor& meta) {
   p.slot_elems = m[9];
   p.world = (int)m[10];
   p.rank = (int)m[11];
+  p.row_len = m[12];
+  p.shard = m[13];
   TORCH_CHECK(p.world >= 1 && p.world <= air::kMaxPeers && p.rank >= 0 && p.rank < p.world, "push meta: world/rank");
+  TORCH_CHECK(p.row_len > 0 && p.shard >= 0 && (p.shard == 0 || p.shard * p.world >= p.row_len),
+              "push meta: row length / shard");
   return p;
 }
 
@@ -106,11 +160,11 @@ void register_comm(pybind11::module_& m) {
   m.def("ipc_close", &ipc_close);
   m.def("enable_peer_access", &enable_peer_access);
   m.def("peer_buffer_bytes", [](int64_t w, int64_t s) { return air::peer_buffer_bytes((int)w, s); });
-  m.def("reduce_rmsnorm_quant", &reduce_rmsnorm_quant);
+  m.def("tp_reduce_norm", &tp_reduce_norm);
   m.def("peer_push", [](const Tensor& meta, const Tensor& src, int64_t B, int64_t N, int64_t ld) {
     TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kFloat, "peer_push: fp32 CUDA source");
     const air::PeerPush p = peer_push_from_meta(meta);
-    TORCH_CHECK(B * ld <= p.slot_elems, "peer_push: B*ld exceeds the receive slot");
+    TORCH_CHECK(N == p.row_len && B * p.row_len <= p.slot_elems, "peer_push: [B, N] must fit the receive slot, N = row length");
     air::launch_peer_push(p, src.data_ptr<float>(), (int)B, (int)N, ld, at::cuda::getCurrentCUDAStream());
     ck(cudaGetLastError(), "peer_push");
   });

@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "sm100.cuh"
 #include "gemm_tc.h"
+#include "comm.cuh"
 #include <stdlib.h>
 #include <string.h>
 
@@ -501,6 +502,15 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         } else {
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = 0.f;
+        }
+        if (a.mode == kGemmPeerPush) {
+          const int ep = *(volatile const int*)a.push.epoch;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int n = n0 + 16 * j + e;
+            if (n < a.T && mg < a.N) peer_store(a.push, ep, n, mg, v[e]);
+          }
+          continue;
         }
 #pragma unroll
         for (int e = 0; e < 16; ++e) {

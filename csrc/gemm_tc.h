@@ -6,7 +6,9 @@
 
 namespace air {
 
-enum GemmMode : int { kGemmStoreF32 = 0, kGemmStoreBF16 = 1, kGemmResidualF32 = 2 };
+// kGemmPeerPush: the output is a tensor-parallel partial, stored from the epilogue into the
+// peer receive buffers (PeerPush protocol, comm.h) instead of `out`.
+enum GemmMode : int { kGemmStoreF32 = 0, kGemmStoreBF16 = 1, kGemmResidualF32 = 2, kGemmPeerPush = 3 };
 
 struct GemmArgs {
   int N, K, T;          // weight rows, reduction length, tokens
@@ -22,6 +24,7 @@ struct GemmArgs {
   int wsplit;           // raw weight tile copy split into this many bulk copies (filled in)
   const int* row_count; // optional device count of valid token rows: token tiles at or past it
                         // exit at once (routed-expert GEMMs launched for a capacity)
+  PeerPush push;        // kGemmPeerPush destinations
        // optional per-phase clock64 stamps of CTA (0,0,0) (profiling aid)
 };
 

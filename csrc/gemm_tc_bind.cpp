@@ -5,16 +5,20 @@
 using at::Tensor;
 using c10::optional;
 
+air::PeerPush peer_push_from_meta(const Tensor& meta);
+
 namespace {
 
 void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, int64_t N, int64_t K,
             Tensor x, Tensor out, int64_t mode, int64_t splits, optional<Tensor> ws,
             optional<Tensor> counters, optional<Tensor> err, optional<Tensor> dbg,
-            optional<Tensor> row_count) {
+            optional<Tensor> row_count, optional<Tensor> push_meta) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2, "gemm_q: x must be 2-D bf16 CUDA");
   TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "gemm_q: rows must be contiguous");
   TORCH_CHECK(x.size(1) == K, "gemm_q: x has ", x.size(1), " columns, expected K=", K);
-  if (mode == air::kGemmStoreBF16) {
+  if (mode == air::kGemmPeerPush) {
+    TORCH_CHECK(push_meta.has_value(), "gemm_q peer push: push meta required");
+  } else if (mode == air::kGemmStoreBF16) {
     TORCH_CHECK(out.scalar_type() == at::kBFloat16, "gemm_q: out must be bf16");
   } else {
     TORCH_CHECK(out.scalar_type() == at::kFloat, "gemm_q: out must be f32");
@@ -39,6 +43,11 @@ void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, i
   a.err = err->data_ptr<int>();
   a.dbg = dbg.has_value() ? (long long*)dbg->data_ptr<int64_t>() : nullptr;
   a.row_count = row_count.has_value() ? row_count->data_ptr<int>() : nullptr;
+  if (mode == air::kGemmPeerPush) {
+    a.push = peer_push_from_meta(*push_meta);
+    TORCH_CHECK(a.N == a.push.row_len && (int64_t)a.T * a.push.row_len <= a.push.slot_elems,
+                "gemm_q peer push: output [T, N] must fit the receive slot with N = its row length");
+  }
   const char* e = air::launch_gemm_q((int)fmt, w.data_ptr(), row_bytes, x.data_ptr(), x.stride(0), a,
                                      at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(e == nullptr, e ? e : "");

@@ -233,7 +233,7 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
       const int e = *(volatile const int*)ep.push.epoch;
 #pragma unroll
       for (int b = 0; b < MAXB; ++b)
-        if ((b % TPR) == c4 && b < nB) peer_store(ep.push, e, (int64_t)b * ep.ld_out + row, acc[0][b]);
+        if ((b % TPR) == c4 && b < nB) peer_store(ep.push, e, b, row, acc[0][b]);
       return;
     }
 #pragma unroll

@@ -24,17 +24,23 @@ enum GemvEpilogue : int {
 
 constexpr int kMaxPeers = 8;
 
-// Producer side of the fused tensor-parallel all-reduce. Every rank owns one receive
-// buffer, mapped into every peer process: data [2 parities][world][slot_elems] of 8-byte
-// (value, tag) pairs. A producer writes each element of its [B, ld] partial into slot
-// (parity, its rank) of every rank's buffer as ONE 8-byte store carrying tag = epoch + 1,
-// so a reader that sees the tag also sees the value (no fence, no separate flag: the
-// "low-latency" protocol). `epoch` is the local collective counter, advanced by the
-// consumer (reduce_rmsnorm_quant) once all of its CTAs have read it.
+// Producer side of the fused tensor-parallel all-reduce (protocol in comm.h). Every rank
+// owns one receive buffer, mapped into every peer process, of 8-byte (value, tag) elements
+// carrying tag = epoch + 1, so a reader that sees the tag also sees the value (no fence, no
+// separate flag). Its first region is [2 parities][world][slot_elems]; a producer writes
+// element (b, c) of its [B, row_len] partial into region (parity, its rank) of
+//   * one-shot (shard == 0): EVERY rank's buffer, at b * row_len + c;
+//   * two-shot (shard > 0): only the buffer of the rank that owns column c
+//     (owner = c / shard), at b * shard + c % shard: a reduce-scatter, each element
+//     crossing NVLink once to one rank.
+// `epoch` is the local collective counter, advanced by the consumer once all of its CTAs
+// have read it.
 struct PeerPush {
   uint2* data[kMaxPeers];     // per destination rank: its receive buffer (mapped here)
   const int* epoch;           // this rank's collective counter
   int64_t slot_elems;
+  int64_t row_len;            // columns of one partial row (the hidden size)
+  int64_t shard;              // two-shot: columns owned per rank (0 = one-shot)
   int world, rank;
 };
 

@@ -1,8 +1,10 @@
 """Fused tensor-parallel all-reduce kernels (peer push + reduce-RMSNorm-quant).
 
 Ranks are emulated on one GPU with ``PeerComm.local_group``: every rank's receive buffer is
-a local allocation, and the producers (which never wait) run before the consumers, so no
-launch ever waits on another launch that has not finished."""
+a local allocation, the producers (which never wait) run before the consumers, and all
+ranks' consumers run as CTAs of one launch (``reduce_norm_group``), so no launch ever waits
+on another launch. Both data paths are covered: one-shot (every partial to every rank) and
+two-shot (reduce-scatter to the column owners, then all-gather of the reduced values)."""
 import pytest
 import torch
 
@@ -20,19 +22,20 @@ def _norm_ref(x, w, eps=1e-5):
 
 def _consume(comms, xs, w, B, K):
     outs = []
-    for c, x in zip(comms, xs):
-        xq = torch.zeros(B, K, dtype=torch.int8, device=DEV)
-        xds = torch.zeros(B, K // 32, 2, dtype=torch.float32, device=DEV)
-        y = torch.zeros(B, K, dtype=torch.bfloat16, device=DEV)
-        c.reduce_norm(x, w, 1e-5, xq, xds, y, B)
-        outs.append((xq, xds, y))
+    for _ in comms:
+        outs.append((torch.zeros(B, K, dtype=torch.int8, device=DEV),
+                     torch.zeros(B, K // 32, 2, dtype=torch.float32, device=DEV),
+                     torch.zeros(B, K, dtype=torch.bfloat16, device=DEV)))
+    PeerComm.reduce_norm_group(comms, xs, w, 1e-5, [o[0] for o in outs], [o[1] for o in outs],
+                               [o[2] for o in outs], B)
     return outs
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_push_reduce_rounds(world):
-    B, K = 5, 1024
-    comms = PeerComm.local_group(world, max_rows=8, hidden=K, device=DEV)
+@pytest.mark.parametrize("world,B,K", [(2, 5, 1024), (4, 5, 1024), (8, 5, 1024),
+                                       (4, 12, 1024), (8, 16, 4096), (8, 10, 1056), (3, 9, 2048)])
+def test_push_reduce_rounds(world, B, K):
+    comms = PeerComm.local_group(world, max_rows=16, hidden=K, device=DEV)
+    assert comms[0].two_shot(B) == (world > 2 and B >= 9)
     g = torch.Generator().manual_seed(world)
     w = (torch.rand(K, generator=g) + 0.5).to(DEV)
     x0 = torch.randn(B, K, generator=g).to(DEV)
@@ -55,10 +58,14 @@ def test_push_reduce_rounds(world):
         assert int(c.epoch.item()) == 3
 
 
-def test_gemv_epilogue_push_matches_store():
+@pytest.mark.parametrize("world,two_shot", [(2, False), (4, True), (8, True)])
+def test_gemv_epilogue_push_matches_store(world, two_shot):
     """Row-parallel Q4_K GEMV with the push epilogue == per-rank partials summed."""
-    world, B, H, Kr = 2, 3, 512, 1024
+    B, H, Kr = 3, 512, 1024
     comms = PeerComm.local_group(world, max_rows=8, hidden=H, device=DEV)
+    for c in comms:
+        c.two_shot_min_rows = 1 if two_shot else 1000
+    assert comms[0].two_shot(B) == two_shot
     g = torch.Generator().manual_seed(0)
     ws = [ops.QWeight.from_raw(quantize(torch.randn(H, Kr, generator=g) * 0.02, GGMLType.Q4_K),
                                GGMLType.Q4_K, H, Kr, DEV) for _ in range(world)]
@@ -114,8 +121,7 @@ def test_graph_replay_advances_epochs():
         with torch.cuda.graph(g, stream=s):
             for c, p in zip(comms, parts):
                 c.push(p, B)
-            for c, x in zip(comms, xs):
-                c.reduce_norm(x, w, 1e-5, None, None, None, B)
+            PeerComm.reduce_norm_group(comms, xs, w, 1e-5, B=B)
     torch.cuda.current_stream().wait_stream(s)
     for x in xs:
         x.zero_()
@@ -127,3 +133,38 @@ def test_graph_replay_advances_epochs():
         torch.testing.assert_close(x, 5 * total, rtol=1e-5, atol=1e-4)
         assert int(c.epoch.item()) == 5
         c.check()
+
+
+@pytest.mark.parametrize("world,T", [(2, 24), (4, 32), (8, 16)])   # T x world <= 148 (one launch)
+def test_gemm_epilogue_push_matches_store(world, T):
+    """Row-parallel tcgen05 GEMM (Q4_K) whose epilogue pushes into the peer buffers: the
+    reduced residual equals the sum of the per-rank GEMM outputs (fp32 reference of the
+    same products, computed with the store epilogue)."""
+    from air_rs.ops import gemm
+    H, Kr = 1024, 2048
+    comms = PeerComm.local_group(world, max_rows=T, hidden=H, device=DEV)
+    g = torch.Generator().manual_seed(world)
+    ws = [ops.QWeight.from_raw(quantize(torch.randn(H, Kr, generator=g) * 0.02, GGMLType.Q4_K),
+                               GGMLType.Q4_K, H, Kr, DEV) for _ in range(world)]
+    acts = [(torch.randn(T, Kr, generator=g)).to(DEV, torch.bfloat16) for _ in range(world)]
+    x0 = torch.randn(T, H, generator=g).to(DEV)
+    ref = x0.clone()
+    for w, a in zip(ws, acts):
+        out = torch.zeros(T, H, device=DEV)
+        gemm.linear(a, w, out)
+        ref += out
+        # the store epilogue agrees with an fp32 PyTorch product of the dequantised weight
+        r32 = a.float() @ w.dequantize_bf16().float().t()
+        # A is rounded to bf16 after the GGUF scale math (same bound as the GEMM tests)
+        torch.testing.assert_close(out, r32, rtol=2e-2, atol=1e-2 * float(r32.abs().max()))
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    dummy = torch.zeros(T, H, device=DEV)
+    for c, w, a in zip(comms, ws, acts):
+        c.push_gemm(a, w, dummy, err=err)
+    xs = [x0.clone() for _ in range(world)]
+    _consume(comms, xs, torch.ones(H, device=DEV), T, H)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for c, x in zip(comms, xs):
+        c.check()
+        torch.testing.assert_close(x, ref, rtol=1e-4, atol=1e-4)

@@ -1,8 +1,9 @@
-"""Tensor parallelism across GPUs: fused peer-memory all-reduce vs the NCCL all-reduce.
+"""Tensor parallelism across GPUs: fused peer-memory all-reduce vs the NCCL all-reduce vs
+the unsharded model, compared on the logits of every decode step.
 
-Runs ``tests/workers/tp_worker.py`` under torch.distributed.run on 2 GPUs (skipped with
-fewer). NVLS stays off so the test has no multicast objects."""
-import json
+Runs ``tests/workers/tp_worker.py`` under torch.distributed.run on 2, 4 and 8 GPUs (each
+skipped with fewer GPUs). NVLS stays off so the test has no multicast objects. At 4 and 8
+GPUs the batch-16 runs take the two-shot (reduce-scatter + all-gather) path."""
 import os
 import subprocess
 import sys
@@ -17,23 +18,44 @@ def _n_gpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-@pytest.mark.skipif(_n_gpus() < 2, reason="needs 2 GPUs")
-def test_fused_allreduce_matches_nccl(tmp_path):
-    out = tmp_path / "tp.json"
+def _compare(a, b, rel):
+    """Max |logit difference| / logit spread over the rows and steps where both runs have
+    produced the same tokens so far (a greedy near-tie can part two runs; after that the
+    contexts differ and the logits are not comparable)."""
+    (ta, la), (tb, lb) = a, b
+    worst, compared = 0.0, 0
+    for s in range(min(la.shape[0], lb.shape[0])):
+        for r in range(la.shape[1]):
+            if ta[r][:s + 1] != tb[r][:s + 1]:
+                continue
+            spread = float(la[s, r].max() - la[s, r].min())
+            worst = max(worst, float((la[s, r] - lb[s, r]).abs().max()) / spread)
+            compared += 1
+    assert compared >= la.shape[1], compared           # at least every row's first step
+    assert worst <= rel, worst
+    return worst
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_logits_match_nccl_and_single_gpu(tmp_path, world):
+    if _n_gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = tmp_path / "tp.pt"
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=os.getcwd())
     worker = os.path.join(os.path.dirname(__file__), "workers", "tp_worker.py")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29533", worker, str(out)]
-    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr=127.0.0.1", f"--master-port={29533 + world}", worker, str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    res = json.loads(out.read_text())
-    for pre, B in [(p, b) for p in ("", "moe_") for b in (4, 16)]:
-        a, b = res[f"{pre}nccl_B{B}"], res[f"{pre}ours_B{B}"]
-        # the first two tokens (prefill + first fused decode step) agree for every sequence;
-        # later ones may part at fp32 summation-order near-ties of a random model
-        assert all(x[:2] == y[:2] for x, y in zip(a, b)), (pre, a, b)
-        same = sum(x == y for x, y in zip(a, b))
-        assert same >= 0.75 * len(a), (pre, same, len(a))
-        single = res[f"{pre or 'dense_'}single_B{B}"]
-        # TP / EP against the unsharded model: first token from the same prefill math
-        assert sum(x[:1] == y[:1] for x, y in zip(single, b)) >= 0.75 * len(b), (pre, single, b)
+    res = torch.load(out, weights_only=False)
+    report = {}
+    for name in ("dense", "moe"):
+        for B in (4, 16):
+            single, nccl, ours = (res[f"{name}_{k}_B{B}"] for k in ("single", "nccl", "ours"))
+            # fused vs NCCL: the same shards and kernels, only the all-reduce differs (fp32
+            # sums in another order)
+            report[f"{name} B{B} ours~nccl"] = _compare(ours, nccl, 1e-3)
+            # TP vs the unsharded model: quantised activations are grouped per shard, and the
+            # unsharded decode takes other kernels (fused-norm GEMV chain)
+            report[f"{name} B{B} ours~single"] = _compare(ours, single, 2e-2)
+    print(report)
