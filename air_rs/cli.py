@@ -197,7 +197,17 @@ def cmd_serve(args) -> int:
     from .serve.dispatcher import EngineDispatcher
     core = _engine(args, max_batch=args.max_num_seqs)
     name = args.model_name or os.path.splitext(os.path.basename(args.model))[0]
-    d = EngineDispatcher(core, name)
+    if args.tp > 1:
+        # one HTTP front end on rank 0; the other ranks mirror its engine loop (one port)
+        import torch.distributed as dist
+        from .serve.distributed import DistributedDispatcher
+        ctl = dist.new_group(backend="gloo")
+        d = DistributedDispatcher(core, name, group=ctl)
+        if d.rank != 0:
+            d.serve_follower()
+            return 0
+    else:
+        d = EngineDispatcher(core, name)
     safety = None
     if args.content_safety:
         from .safety import ContentSafetyGate
@@ -210,8 +220,11 @@ def cmd_serve(args) -> int:
     app = create_app(d, name, api_keys=keys, chat_format=args.chat_template,
                      reasoning_format=args.reasoning_format, tool_call_parser=args.tool_call_parser,
                      safety=safety, modelfile=mf)
-    uvicorn.run(app, host=args.host, port=args.port, ssl_certfile=args.tls_cert, ssl_keyfile=args.tls_key,
-                log_level="info")
+    try:
+        uvicorn.run(app, host=args.host, port=args.port, ssl_certfile=args.tls_cert, ssl_keyfile=args.tls_key,
+                    log_level="info")
+    finally:
+        d.shutdown()          # under --tp this also releases the follower ranks
     return 0
 
 

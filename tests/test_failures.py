@@ -71,3 +71,24 @@ def test_server_fails_requests_on_engine_error_and_keeps_serving():
         assert d.errors == 1 and not eng.running and not eng.waiting
     finally:
         d.shutdown()
+
+
+def test_multi_rank_serving_mirrors_rank0(tmp_path):
+    """serve --tp N design on gloo ranks: rank 0 answers concurrent HTTP requests, the
+    follower mirrors every admission and step, and both generate the same tokens."""
+    import json
+    import subprocess
+    import sys
+    out = tmp_path / "serve"
+    worker = os.path.join(os.path.dirname(__file__), "workers", "serve_worker.py")
+    env = dict(os.environ, PYTHONPATH=os.getcwd())
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29561", worker, str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    r0 = json.loads(open(f"{out}.0").read())
+    r1 = json.loads(open(f"{out}.1").read())
+    assert r0["embed_ok"]
+    assert all(code == 200 and n == 5 + int(i) for i, (code, _, n) in r0["texts"].items()), r0["texts"]
+    assert len(r0["history"]) == 4 and r0["history"] == r1["history"]
+    assert r0["ticks"] == r1["ticks"]
