@@ -84,6 +84,22 @@ class ModelConfig:
     eos_token_id: int = 2
     bos_token_id: int = 1
     extra: dict[str, Any] = field(default_factory=dict)
+    # per-architecture tensor layout (reference src/model.rs:326-360, src/weight_streamer.rs:215-250):
+    qkv_bias: bool = False        # blk.N.attn_{q,k,v}.bias (Qwen2)
+    norm_bias: bool = False       # blk.N.{attn,ffn}_norm.bias, output_norm.bias (Falcon LayerNorm)
+    fused_qkv: bool = False       # blk.N.attn_qkv.weight = [q; k; v] rows (Phi-3)
+    fused_gate_up: bool = False   # blk.N.ffn_up.weight = [gate; up] rows, no ffn_gate (Phi-3)
+
+    def detect_layout(self, tensor_names) -> "ModelConfig":
+        """Set the layout flags from a checkpoint's tensor names (biases and fused tensors are
+        optional per file, so metadata alone does not say)."""
+        names = set(tensor_names)
+        self.qkv_bias = "blk.0.attn_q.bias" in names
+        self.norm_bias = "blk.0.attn_norm.bias" in names
+        self.fused_qkv = "blk.0.attn_qkv.weight" in names and "blk.0.attn_q.weight" not in names
+        self.fused_gate_up = ("blk.0.ffn_gate.weight" not in names and "blk.0.ffn_up.weight" in names
+                              and self.ffn_type in (FfnType.SWIGLU, FfnType.GEGLU))
+        return self
 
     @property
     def q_dim(self) -> int:
@@ -149,7 +165,9 @@ class ModelConfig:
             from .archs.hybrid import HybridAttentionRouter
             extra["attention_layout"] = HybridAttentionRouter.gemma4(
                 n_layers, int(sw), int(pattern)).windows()
-        return cls(n_layers=n_layers, n_heads=n_heads, n_kv_heads=n_kv, hidden_dim=hidden,
+        return cls(qkv_bias=variant == ModelVariant.QWEN2, norm_bias=variant == ModelVariant.FALCON,
+                   fused_qkv=variant == ModelVariant.PHI3, fused_gate_up=variant == ModelVariant.PHI3,
+                   n_layers=n_layers, n_heads=n_heads, n_kv_heads=n_kv, hidden_dim=hidden,
                    intermediate_dim=inter, vocab_size=int(vocab), rope_theta=rope,
                    context_length=ctx, rms_norm_eps=float(eps), head_dim=head_dim, arch=arch,
                    variant=variant, norm_type=norm, ffn_type=ffn,
@@ -219,5 +237,26 @@ def tiny_moe() -> ModelConfig:
                        variant=ModelVariant.MISTRAL, n_experts=4, moe_top_k=2)
 
 
-PRESETS = {"tiny": tiny_llama, "tiny-moe": tiny_moe, "llama3-8b": llama3_8b, "llama3-70b": llama3_70b,
+def tiny_variant(arch: str) -> ModelConfig:
+    """Tiny model of an architecture variant (tests): qwen2 (q/k/v biases), gemma (Gemma
+    RMSNorm + GeGLU), falcon (LayerNorm with biases + dense GELU MLP), phi3 (fused attn_qkv and
+    gate|up tensors)."""
+    v = ModelVariant.from_arch(arch)
+    c = tiny_llama()
+    c.arch, c.variant = arch, v
+    c.intermediate_dim = 512
+    if v == ModelVariant.QWEN2:
+        c.qkv_bias = True
+    elif v == ModelVariant.GEMMA:
+        c.norm_type, c.ffn_type = NormType.GEMMA_RMS, FfnType.GEGLU
+    elif v == ModelVariant.FALCON:
+        c.norm_type, c.ffn_type, c.norm_bias = NormType.LAYER, FfnType.DENSE, True
+    elif v == ModelVariant.PHI3:
+        c.fused_qkv = c.fused_gate_up = True
+    return c
+
+
+PRESETS = {"tiny": tiny_llama, "tiny-qwen2": lambda: tiny_variant("qwen2"),
+           "tiny-gemma": lambda: tiny_variant("gemma"), "tiny-falcon": lambda: tiny_variant("falcon"),
+           "tiny-phi3": lambda: tiny_variant("phi3"), "tiny-moe": tiny_moe, "llama3-8b": llama3_8b, "llama3-70b": llama3_70b,
            "mixtral-8x7b": mixtral_8x7b, "draft-1b": draft_1b}

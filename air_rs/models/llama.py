@@ -40,6 +40,10 @@ class LayerWeights:
     experts_gu: list = field(default_factory=list)
     experts_down: list = field(default_factory=list)
     expert_ids: list = field(default_factory=list)   # global ids of the local experts
+    # architecture variants (reference src/model.rs:326-360)
+    qkv_bias: torch.Tensor | None = None    # [q|k|v] rows of this rank, f32 (Qwen2)
+    attn_norm_b: torch.Tensor | None = None  # LayerNorm biases (Falcon)
+    ffn_norm_b: torch.Tensor | None = None
 
     @property
     def w_gate(self) -> ops.QWeight:
@@ -52,7 +56,7 @@ class LayerWeights:
 
 def layer_tensors(lw: "LayerWeights") -> list:
     """Every tensor of a layer in a fixed order (weights data/scales, norms, router)."""
-    out = [lw.attn_norm, lw.ffn_norm]
+    out = [lw.attn_norm, lw.ffn_norm] + [t for t in (lw.qkv_bias, lw.attn_norm_b, lw.ffn_norm_b) if t is not None]
     qws = [lw.wqkv, lw.wo] + ([lw.wgu, lw.wdown] if lw.wgu is not None else []) + list(lw.experts_gu) + \
         list(lw.experts_down)
     for q in qws:
@@ -95,6 +99,7 @@ class LlamaWeights:
         pending: dict[str, tuple] = {}
         self.layers: list[LayerWeights | None] = [None] * (self.layer_range[1] - self.layer_range[0])
         self.embd = self.out_norm = self.lm_head = None
+        self.out_norm_b = None
         for name, raw, qt, shape in records:
             pending[name] = (raw, GGMLType(qt), tuple(shape))
             self._try_build(pending)
@@ -130,6 +135,8 @@ class LlamaWeights:
             self.embd = self._lin_full(*p["token_embd.weight"])
         if self.out_norm is None and "output_norm.weight" in p:
             self.out_norm = self._vec(*p.pop("output_norm.weight"))
+        if self.out_norm_b is None and "output_norm.bias" in p:
+            self.out_norm_b = self._vec(*p.pop("output_norm.bias"))
         if self.lm_head is None and "output.weight" in p:
             raw, qt, shape = p.pop("output.weight")
             self.lm_head = self._shard_rows_tp(raw, qt, shape)
@@ -142,11 +149,17 @@ class LlamaWeights:
             if self.layers[i - l0] is not None:
                 continue
             pre = f"blk.{i}."
-            need = ["attn_norm.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight",
-                    "attn_output.weight", "ffn_norm.weight"]
+            need = ["attn_norm.weight", "attn_output.weight", "ffn_norm.weight"]
+            need += ["attn_qkv.weight"] if cfg.fused_qkv else ["attn_q.weight", "attn_k.weight", "attn_v.weight"]
+            if cfg.qkv_bias:
+                need += ["attn_q.bias", "attn_k.bias", "attn_v.bias"]
+            if cfg.norm_bias:
+                need += ["attn_norm.bias", "ffn_norm.bias"]
             if cfg.n_experts:
                 need += ["ffn_gate_inp.weight", "ffn_gate_exps.weight", "ffn_up_exps.weight",
                          "ffn_down_exps.weight"]
+            elif cfg.ffn_type == FfnType.DENSE or cfg.fused_gate_up:
+                need += ["ffn_up.weight", "ffn_down.weight"]
             else:
                 need += ["ffn_gate.weight", "ffn_up.weight", "ffn_down.weight"]
             if not all(pre + n in p for n in need):
@@ -173,13 +186,22 @@ class LlamaWeights:
         hd = cfg.head_dim
         nh_l, nkv_l = cfg.n_heads // tp, max(1, cfg.n_kv_heads // tp)
         kv_rank = rk * nkv_l // max(1, nkv_l) if cfg.n_kv_heads >= tp else rk * cfg.n_kv_heads // tp
-        q = self._lin_rows(*g["attn_q.weight"], rk * nh_l * hd, (rk + 1) * nh_l * hd)
+        q0, q1 = rk * nh_l * hd, (rk + 1) * nh_l * hd
         if cfg.n_kv_heads >= tp:
             k0 = rk * nkv_l * hd
         else:  # replicate KV heads across ranks that share them
             k0 = (rk * cfg.n_kv_heads // tp) * hd
-        k = self._lin_rows(*g["attn_k.weight"], k0, k0 + nkv_l * hd)
-        v = self._lin_rows(*g["attn_v.weight"], k0, k0 + nkv_l * hd)
+        k1 = k0 + nkv_l * hd
+        if cfg.fused_qkv:    # Phi-3: rows [q; k; v] of one tensor
+            raw, qt, shp = g["attn_qkv.weight"]
+            qd, kd = cfg.q_dim, cfg.kv_dim
+            q = self._lin_rows(raw, qt, shp, q0, q1)
+            k = self._lin_rows(raw, qt, shp, qd + k0, qd + k1)
+            v = self._lin_rows(raw, qt, shp, qd + kd + k0, qd + kd + k1)
+        else:
+            q = self._lin_rows(*g["attn_q.weight"], q0, q1)
+            k = self._lin_rows(*g["attn_k.weight"], k0, k1)
+            v = self._lin_rows(*g["attn_v.weight"], k0, k1)
         del kv_rank
         wqkv = ops.QWeight.cat([q, k, v])
         if tp == 1:
@@ -188,6 +210,11 @@ class LlamaWeights:
             wo = self._lin_cols(*g["attn_output.weight"], rk * nh_l * hd, (rk + 1) * nh_l * hd)
         lw = LayerWeights(self._vec(*g["attn_norm.weight"]), wqkv, wo, self._vec(*g["ffn_norm.weight"]),
                           None, None)
+        if cfg.qkv_bias:
+            bq, bk, bv = (self._vec(*g[f"attn_{n}.bias"]) for n in "qkv")
+            lw.qkv_bias = torch.cat([bq[q0:q1], bk[k0:k1], bv[k0:k1]]).contiguous()
+        if cfg.norm_bias:
+            lw.attn_norm_b, lw.ffn_norm_b = self._vec(*g["attn_norm.bias"]), self._vec(*g["ffn_norm.bias"])
         F = cfg.intermediate_dim
         Fl = F // tp
         if cfg.n_experts:
@@ -214,9 +241,21 @@ class LlamaWeights:
                 dn = ops.QWeight.from_raw(dr[e], dq, cfg.hidden_dim, F, xdev)
                 lw.experts_gu.append(gu.to_device(None, pin=True) if pin else gu)
                 lw.experts_down.append(dn.to_device(None, pin=True) if pin else dn)
+        elif cfg.ffn_type == FfnType.DENSE:
+            # Falcon: up -> GELU -> down; wgu holds only the up rows (no gate)
+            lw.wgu = self._lin_rows(*g["ffn_up.weight"], rk * Fl, (rk + 1) * Fl)
+            if tp == 1:
+                lw.wdown = self._lin_full(*g["ffn_down.weight"])
+            else:
+                lw.wdown = self._lin_cols(*g["ffn_down.weight"], rk * Fl, (rk + 1) * Fl)
         else:
-            gate = self._lin_rows(*g["ffn_gate.weight"], rk * Fl, (rk + 1) * Fl)
-            up = self._lin_rows(*g["ffn_up.weight"], rk * Fl, (rk + 1) * Fl)
+            if cfg.fused_gate_up:   # Phi-3: ffn_up = [gate; up]
+                raw, qt, shp = g["ffn_up.weight"]
+                gate = self._lin_rows(raw, qt, shp, rk * Fl, (rk + 1) * Fl)
+                up = self._lin_rows(raw, qt, shp, F + rk * Fl, F + (rk + 1) * Fl)
+            else:
+                gate = self._lin_rows(*g["ffn_gate.weight"], rk * Fl, (rk + 1) * Fl)
+                up = self._lin_rows(*g["ffn_up.weight"], rk * Fl, (rk + 1) * Fl)
             lw.wgu = ops.QWeight.cat([gate, up])
             if tp == 1:
                 lw.wdown = self._lin_full(*g["ffn_down.weight"])

@@ -17,28 +17,49 @@ from .config import ModelConfig, FfnType
 
 
 def tensor_specs(cfg: ModelConfig, qtype: GGMLType) -> Iterator[tuple[str, tuple[int, ...], GGMLType, bool]]:
-    """(name, row-major shape, type, is_norm) in canonical order."""
+    """(name, row-major shape, type, kind) in canonical order; kind is False for weights,
+    True for norm weights (ones) and "bias" for biases (small random)."""
     H, V = cfg.hidden_dim, cfg.vocab_size
     yield "token_embd.weight", (V, H), qtype, False
+    F = cfg.intermediate_dim
     for i in range(cfg.n_layers):
         p = f"blk.{i}."
         yield p + "attn_norm.weight", (H,), GGMLType.F32, True
-        yield p + "attn_q.weight", (cfg.q_dim, H), qtype, False
-        yield p + "attn_k.weight", (cfg.kv_dim, H), qtype, False
-        yield p + "attn_v.weight", (cfg.kv_dim, H), qtype, False
+        if cfg.norm_bias:
+            yield p + "attn_norm.bias", (H,), GGMLType.F32, "bias"
+        if cfg.fused_qkv:
+            yield p + "attn_qkv.weight", (cfg.q_dim + 2 * cfg.kv_dim, H), qtype, False
+        else:
+            yield p + "attn_q.weight", (cfg.q_dim, H), qtype, False
+            yield p + "attn_k.weight", (cfg.kv_dim, H), qtype, False
+            yield p + "attn_v.weight", (cfg.kv_dim, H), qtype, False
+        if cfg.qkv_bias:
+            yield p + "attn_q.bias", (cfg.q_dim,), GGMLType.F32, "bias"
+            yield p + "attn_k.bias", (cfg.kv_dim,), GGMLType.F32, "bias"
+            yield p + "attn_v.bias", (cfg.kv_dim,), GGMLType.F32, "bias"
         yield p + "attn_output.weight", (H, cfg.q_dim), qtype, False
         yield p + "ffn_norm.weight", (H,), GGMLType.F32, True
+        if cfg.norm_bias:
+            yield p + "ffn_norm.bias", (H,), GGMLType.F32, "bias"
         if cfg.n_experts > 0:
-            E, F = cfg.n_experts, cfg.intermediate_dim
+            E = cfg.n_experts
             yield p + "ffn_gate_inp.weight", (E, H), GGMLType.F32, False
             yield p + "ffn_gate_exps.weight", (E, F, H), qtype, False
             yield p + "ffn_up_exps.weight", (E, F, H), qtype, False
             yield p + "ffn_down_exps.weight", (E, H, F), qtype, False
+        elif cfg.ffn_type == FfnType.DENSE:
+            yield p + "ffn_up.weight", (F, H), qtype, False
+            yield p + "ffn_down.weight", (H, F), qtype, False
+        elif cfg.fused_gate_up:
+            yield p + "ffn_up.weight", (2 * F, H), qtype, False
+            yield p + "ffn_down.weight", (H, F), qtype, False
         else:
-            yield p + "ffn_gate.weight", (cfg.intermediate_dim, H), qtype, False
-            yield p + "ffn_up.weight", (cfg.intermediate_dim, H), qtype, False
-            yield p + "ffn_down.weight", (H, cfg.intermediate_dim), qtype, False
+            yield p + "ffn_gate.weight", (F, H), qtype, False
+            yield p + "ffn_up.weight", (F, H), qtype, False
+            yield p + "ffn_down.weight", (H, F), qtype, False
     yield "output_norm.weight", (H,), GGMLType.F32, True
+    if cfg.norm_bias:
+        yield "output_norm.bias", (H,), GGMLType.F32, "bias"
     yield "output.weight", (V, H), qtype, False
 
 
@@ -62,7 +83,10 @@ def random_tensors(cfg: ModelConfig, qtype: GGMLType = GGMLType.Q8_0, seed: int 
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     for name, shape, qt, is_norm in tensor_specs(cfg, GGMLType(qtype)):
-        if is_norm:
+        if is_norm == "bias":
+            x = torch.randn(shape, generator=gen, device=device) * std
+            raw = x.contiguous().view(torch.uint8).reshape(1, -1)
+        elif is_norm:
             raw = torch.ones(shape, dtype=torch.float32, device=device).view(torch.uint8).reshape(1, -1)
         elif qt == GGMLType.F32:
             x = torch.randn(shape, generator=gen, device=device) * std

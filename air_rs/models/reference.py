@@ -21,7 +21,7 @@ import torch
 
 from ..gguf import GGMLType
 from ..gguf.quants import dequantize, unpack_k4_scales
-from .config import ModelConfig
+from .config import FfnType, ModelConfig, NormType
 
 
 def _round_away(x: torch.Tensor) -> torch.Tensor:
@@ -93,6 +93,11 @@ class OracleLayer:
     w_down: tuple | None
     router: torch.Tensor | None = None          # [E, H] f32
     experts: list | None = None                 # per expert (gate, up, down) raw tuples
+    bq: torch.Tensor | None = None              # q/k/v projection biases (Qwen2)
+    bk: torch.Tensor | None = None
+    bv: torch.Tensor | None = None
+    attn_norm_b: torch.Tensor | None = None     # LayerNorm biases (Falcon)
+    ffn_norm_b: torch.Tensor | None = None
 
 
 class OracleModel:
@@ -108,20 +113,45 @@ class OracleModel:
             raw, qt, shape = tensors[name]
             return (raw, qt, shape[0])
 
+        def lin_rows(name, r0, r1):
+            raw, qt, shape = tensors[name]
+            return (raw.reshape(shape[0], -1)[r0:r1], qt, r1 - r0)
+
         def vec(name):
             raw, qt, shape = tensors[name]
             return dequantize(raw.reshape(1, -1), qt).reshape(-1).half()
+
+        def vec32(name):
+            if name not in tensors:
+                return None
+            raw, qt, shape = tensors[name]
+            return dequantize(raw.reshape(1, -1), qt).reshape(-1).float()
 
         self.embd = dequantize(tensors["token_embd.weight"][0], tensors["token_embd.weight"][1]).half()
         self.layers = []
         for i in range(cfg.n_layers):
             p = f"blk.{i}."
             moe = cfg.n_experts > 0
-            L = OracleLayer(
-                vec(p + "attn_norm.weight"), lin(p + "attn_q.weight"), lin(p + "attn_k.weight"),
-                lin(p + "attn_v.weight"), lin(p + "attn_output.weight"), vec(p + "ffn_norm.weight"),
-                None if moe else lin(p + "ffn_gate.weight"), None if moe else lin(p + "ffn_up.weight"),
-                None if moe else lin(p + "ffn_down.weight"))
+            qd, kd = cfg.q_dim, cfg.kv_dim
+            if cfg.fused_qkv:      # Phi-3: one [q; k; v] tensor
+                wq, wk, wv = (lin_rows(p + "attn_qkv.weight", a, b) for a, b in
+                              ((0, qd), (qd, qd + kd), (qd + kd, qd + 2 * kd)))
+            else:
+                wq, wk, wv = lin(p + "attn_q.weight"), lin(p + "attn_k.weight"), lin(p + "attn_v.weight")
+            F = cfg.intermediate_dim
+            if moe:
+                wg = wu = wd = None
+            elif cfg.ffn_type == FfnType.DENSE:      # Falcon: up -> GELU -> down
+                wg, wu, wd = None, lin(p + "ffn_up.weight"), lin(p + "ffn_down.weight")
+            elif cfg.fused_gate_up:                  # Phi-3: ffn_up = [gate; up]
+                wg, wu = lin_rows(p + "ffn_up.weight", 0, F), lin_rows(p + "ffn_up.weight", F, 2 * F)
+                wd = lin(p + "ffn_down.weight")
+            else:
+                wg, wu, wd = lin(p + "ffn_gate.weight"), lin(p + "ffn_up.weight"), lin(p + "ffn_down.weight")
+            L = OracleLayer(vec(p + "attn_norm.weight"), wq, wk, wv, lin(p + "attn_output.weight"),
+                            vec(p + "ffn_norm.weight"), wg, wu, wd)
+            L.bq, L.bk, L.bv = vec32(p + "attn_q.bias"), vec32(p + "attn_k.bias"), vec32(p + "attn_v.bias")
+            L.attn_norm_b, L.ffn_norm_b = vec32(p + "attn_norm.bias"), vec32(p + "ffn_norm.bias")
             if moe:
                 E, F, H = cfg.n_experts, cfg.intermediate_dim, cfg.hidden_dim
                 rr, rq, _ = tensors[p + "ffn_gate_inp.weight"]
@@ -134,6 +164,7 @@ class OracleModel:
                                    for nm in ("gate", "up", "down")) for e in range(E)]
             self.layers.append(L)
         self.out_norm = vec("output_norm.weight")
+        self.out_norm_b = vec32("output_norm.bias")
         self.lm_head = lin("output.weight" if "output.weight" in tensors else "token_embd.weight")
         hd = cfg.head_dim
         self.inv_freq = 1.0 / torch.pow(torch.tensor(float(cfg.rope_theta)),
@@ -144,7 +175,7 @@ class OracleModel:
 
     @classmethod
     def from_gguf(cls, g) -> "OracleModel":
-        cfg = ModelConfig.from_gguf_metadata(g.metadata)
+        cfg = ModelConfig.from_gguf_metadata(g.metadata).detect_layout(g.tensors)
         tensors = {n: (g.raw(n), t.qtype, t.torch_shape) for n, t in g.tensors.items()}
         return cls(cfg, tensors)
 
@@ -163,6 +194,26 @@ class OracleModel:
         xf = x.float()
         y = xf / torch.sqrt((xf * xf).mean(-1, keepdim=True) + eps)
         return (y * w.float()).to(x.dtype)
+
+    def norm(self, x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None) -> torch.Tensor:
+        """Per-architecture norm (reference src/model.rs:400-416, src/ops.rs:49-90): RMSNorm,
+        Gemma RMSNorm (weight + 1) or LayerNorm (mean subtracted, optional bias), in F32."""
+        cfg = self.cfg
+        xf = x.float()
+        if cfg.norm_type == NormType.LAYER:
+            c = xf - xf.mean(-1, keepdim=True)
+            y = c / torch.sqrt((c * c).mean(-1, keepdim=True) + cfg.rms_norm_eps) * w.float()
+        else:
+            wf = w.float() + (1.0 if cfg.norm_type == NormType.GEMMA_RMS else 0.0)
+            y = xf / torch.sqrt((xf * xf).mean(-1, keepdim=True) + cfg.rms_norm_eps) * wf
+        if b is not None:
+            y = y + b
+        return y.to(x.dtype)
+
+    @staticmethod
+    def gelu(x: torch.Tensor) -> torch.Tensor:
+        """GELU, tanh form (reference src/ops.rs:103-119)."""
+        return 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x * x * x)))
 
     def rope(self, x: torch.Tensor, start: int) -> torch.Tensor:
         # x [S, H, D] f32, NeoX half split
@@ -192,10 +243,13 @@ class OracleModel:
         S = x.shape[0]
         nh, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         for li, L in enumerate(self.layers):
-            h = self.rms_norm(x, L.attn_norm, cfg.rms_norm_eps).float()
-            q = qmatmul(h, L.wq[0], L.wq[1], L.wq[2]).reshape(S, nh, hd)
-            k = qmatmul(h, L.wk[0], L.wk[1], L.wk[2]).reshape(S, nkv, hd)
-            v = qmatmul(h, L.wv[0], L.wv[1], L.wv[2]).reshape(S, nkv, hd)
+            h = self.norm(x, L.attn_norm, L.attn_norm_b).float()
+            q = qmatmul(h, L.wq[0], L.wq[1], L.wq[2])
+            k = qmatmul(h, L.wk[0], L.wk[1], L.wk[2])
+            v = qmatmul(h, L.wv[0], L.wv[1], L.wv[2])
+            if L.bq is not None:        # Qwen2 q/k/v biases, before RoPE
+                q, k, v = q + L.bq, k + L.bk, v + L.bv
+            q, k, v = q.reshape(S, nh, hd), k.reshape(S, nkv, hd), v.reshape(S, nkv, hd)
             q = self.rope(q, start_pos)
             k = self.rope(k, start_pos)
             if self.k_cache[li] is not None:
@@ -206,18 +260,22 @@ class OracleModel:
             attn = attention_reference(q, k, v, causal=S > 1, window=self.windows[li])
             o = qmatmul(attn.reshape(S, nh * hd), L.wo[0], L.wo[1], L.wo[2]).to(x.dtype)
             x = x + o
-            h = self.rms_norm(x, L.ffn_norm, cfg.rms_norm_eps).float()
+            h = self.norm(x, L.ffn_norm, L.ffn_norm_b).float()
             if L.router is not None:
                 dn = self.moe_ffn(h, L).to(x.dtype)
             else:
-                g = qmatmul(h, L.w_gate[0], L.w_gate[1], L.w_gate[2])
                 u = qmatmul(h, L.w_up[0], L.w_up[1], L.w_up[2])
-                a = g / (1.0 + torch.exp(-g)) * u
+                if L.w_gate is None:                                  # dense GELU MLP (Falcon)
+                    a = self.gelu(u)
+                else:
+                    g = qmatmul(h, L.w_gate[0], L.w_gate[1], L.w_gate[2])
+                    act = self.gelu(g) if cfg.ffn_type == FfnType.GEGLU else g / (1.0 + torch.exp(-g))
+                    a = act * u
                 if self.ffn_hook is not None:      # sparsity predictors: observe / mask neurons
                     a = self.ffn_hook(li, h, a)
                 dn = qmatmul(a, L.w_down[0], L.w_down[1], L.w_down[2]).to(x.dtype)
             x = x + dn
-        x = self.rms_norm(x, self.out_norm, cfg.rms_norm_eps)
+        x = self.norm(x, self.out_norm, self.out_norm_b)
         if getattr(self, "_want_hidden", False):
             self._hidden = x.float()
         last = x[-1:].float()

@@ -199,12 +199,18 @@ class QWeight:
         return out
 
 
+ACT_SILU, ACT_GELU = 0, 1
+
+
 def rmsnorm_quant(x: torch.Tensor | None, w: torch.Tensor | None, eps: float, q: torch.Tensor | None,
                   ds: torch.Tensor | None, y_bf16: torch.Tensor | None = None,
-                  x_bf16: torch.Tensor | None = None, w_offset: float = 0.0):
+                  x_bf16: torch.Tensor | None = None, w_offset: float = 0.0,
+                  bias: torch.Tensor | None = None, layer: bool = False):
+    """y = norm(x) * (w + w_offset) (+ bias), quantised to Q8A (q, ds) and/or bf16. norm is
+    RMSNorm, or LayerNorm (mean subtracted) when ``layer``; w None: y = x."""
     src = x if x is not None else x_bf16
     B, K = src.shape
-    require_ext().rmsnorm_quant(x, x_bf16, w, w_offset, eps, B, K, q, ds, y_bf16)
+    require_ext().rmsnorm_quant(x, x_bf16, w, w_offset, eps, B, K, q, ds, y_bf16, bias, int(layer))
     count_launch()
 
 
@@ -213,7 +219,7 @@ def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EP
          rope_cs=None, positions=None, slots=None, kv=None, q_out=None, n_heads=0, n_kv=0,
          head_dim=0, block_size=0, rot_dim=0, err=None, push_meta=None, out_q=None, out_ds=None,
          norm_w=None, norm_offset: float = 0.0, ss_out=None, ss_in=None, norm_k: int = 0,
-         eps: float = 0.0):
+         eps: float = 0.0, act: int = 0):
     """Decode GEMV (batch <= 8) with a fused epilogue ``mode``.
 
     Fused RMSNorm chain (tiled Q4_K): a residual GEMV given ``norm_w`` also writes the next
@@ -234,7 +240,7 @@ def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EP
              out_bf16, ld, resid, None if w2 is None else w2.data,
              None if w2 is None else w2.scales, rope_cs, positions, slots, kv, q_out,
              n_heads, n_kv, head_dim, block_size, rot_dim or head_dim, err, splits, ws, cnt, push_meta,
-             out_q, out_ds, norm_w, norm_offset, ss_out, ss_in, norm_k, eps)
+             out_q, out_ds, norm_w, norm_offset, ss_out, ss_in, norm_k, eps, act)
     count_launch()
 
 
@@ -289,16 +295,20 @@ def embed(w: QWeight, ids: torch.Tensor, out_f32=None, out_bf16=None, mult: floa
 
 
 def rope_kv(qkv, T, rope_cs, positions, slots, kv, q_out, *, n_heads, n_kv, head_dim, block_size,
-            rot_dim=None, err=None):
+            rot_dim=None, err=None, bias=None):
+    """RoPE on q and k (+ an optional q|k|v projection bias first), q to ``q_out``, k and v
+    into the paged cache."""
     require_ext().rope_kv(qkv, T, rope_cs, positions, slots, kv, q_out, n_heads, n_kv, head_dim,
-                          block_size, rot_dim or head_dim, err)
+                          block_size, rot_dim or head_dim, err, bias)
     count_launch()
 
 
-def swiglu(gu, T, F, out_bf16=None, out_f32=None, ld_out: int | None = None, up_off: int | None = None):
-    """out[t, j] = silu(gu[t, j]) * gu[t, up_off + j] for j < F (out row stride ld_out)."""
+def swiglu(gu, T, F, out_bf16=None, out_f32=None, ld_out: int | None = None, up_off: int | None = None,
+           act: int = ACT_SILU):
+    """out[t, j] = act(gu[t, j]) * gu[t, up_off + j] for j < F (out row stride ld_out);
+    ``up_off=-1``: out = act(gu[t, j]) (dense GELU MLP). act: ACT_SILU or ACT_GELU (tanh form)."""
     require_ext().swiglu(gu, T, F, up_off if up_off is not None else F, ld_out if ld_out is not None else F,
-                         out_bf16, out_f32)
+                         out_bf16, out_f32, act)
     count_launch()
 
 

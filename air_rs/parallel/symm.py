@@ -154,25 +154,26 @@ class PeerComm:
 
     # ----------------------------------------------------------------- consumer side
     def reduce_norm(self, x, w, eps: float, xq=None, xds=None, y_bf16=None, B: int | None = None,
-                    w_offset: float = 0.0):
-        """x += sum of all ranks' pushed partials, then RMSNorm (+ Q8A quantisation)."""
+                    w_offset: float = 0.0, bias=None, layer: bool = False):
+        """x += sum of all ranks' pushed partials, then RMSNorm / LayerNorm (+ Q8A quantisation)."""
         B = B if B is not None else x.shape[0]
         K = x.shape[1]
         ops.require_ext().tp_reduce_norm([self.reduce_meta], [x], w, w_offset, eps, B, K,
                                          [xq] if xq is not None else [], [xds] if xds is not None else [],
-                                         [y_bf16] if y_bf16 is not None else [], self.two_shot(B))
+                                         [y_bf16] if y_bf16 is not None else [], self.two_shot(B),
+                                         bias, int(layer))
         ops.count_launch()
         self.pending = False
 
     @staticmethod
     def reduce_norm_group(comms: list["PeerComm"], xs, w, eps: float, xqs=None, xdss=None, ys=None,
-                          B: int | None = None, w_offset: float = 0.0):
+                          B: int | None = None, w_offset: float = 0.0, bias=None, layer: bool = False):
         """Every rank's ``reduce_norm`` of a ``local_group`` in one launch (one GPU)."""
         B = B if B is not None else xs[0].shape[0]
         K = xs[0].shape[1]
         ops.require_ext().tp_reduce_norm([c.reduce_meta for c in comms], list(xs), w, w_offset, eps, B, K,
                                          list(xqs or []), list(xdss or []), list(ys or []),
-                                         comms[0].two_shot(B))
+                                         comms[0].two_shot(B), bias, int(layer))
         ops.count_launch()
         for c in comms:
             c.pending = False

@@ -93,7 +93,7 @@ def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None
     """``resident="auto"``: keep everything in HBM when it fits under the VRAM cap, else
     stream layers or serve MoE experts from host memory (``runtime.residency.plan_model``)."""
     g = read_gguf(path)
-    cfg = ModelConfig.from_gguf_metadata(g.metadata)
+    cfg = ModelConfig.from_gguf_metadata(g.metadata).detect_layout(g.tensors)
     tok = Tokenizer.from_gguf_metadata(g.metadata)
     if device is None:
         device = "cuda" if torch.cuda.is_available() else "cpu"

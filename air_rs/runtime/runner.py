@@ -123,8 +123,20 @@ class ModelRunner:
         self.qkv_b = torch.zeros(B, self.qkv_dim, dtype=bf16, device=dev)
         self.attn_b = torch.zeros(B, self.nh * self.hd, dtype=bf16, device=dev)
         l0 = weights.layers[0]
+        # architecture variant (reference src/model.rs:400-416, :623-660): norm kind, gate
+        # activation, dense (ungated) MLP, q/k/v biases
+        from ..models.config import FfnType, NormType
+        self.norm_layer = cfg.norm_type == NormType.LAYER
+        self.norm_off = 1.0 if cfg.norm_type == NormType.GEMMA_RMS else 0.0
+        self.act = ops.ACT_GELU if cfg.ffn_type in (FfnType.GEGLU, FfnType.DENSE) else ops.ACT_SILU
+        self.dense_ffn = cfg.ffn_type == FfnType.DENSE and not cfg.n_experts
+        self.qkv_bias = l0.qkv_bias is not None
         self.gu_w = l0.wgu.N if l0.wgu is not None else 2 * self.F   # gate|up GEMM width
-        self.up_off = l0.wgu.parts[1][0] if l0.wgu is not None else self.F
+        if self.dense_ffn:
+            self.up_off = -1           # the "gate|up" GEMM output is the up projection alone
+        else:
+            self.up_off = l0.wgu.parts[1][0] if l0.wgu is not None else self.F
+        self.qkv_f = torch.zeros(B, self.qkv_dim, dtype=f32, device=dev) if self.qkv_bias else None
         self.gu_b = torch.zeros(B, self.gu_w, dtype=bf16, device=dev)
         self.h_b = torch.zeros(B, self.Fp, dtype=bf16, device=dev)
         self.o_b = torch.zeros(B, self.H, dtype=bf16, device=dev)
@@ -250,12 +262,30 @@ class ModelRunner:
         else:
             ops.gemv(w, xq, xds, B, ops.EPI_RESIDUAL, resid=x)
 
-    def _norm(self, x, w, B: int, xq=None, xds=None, y_bf16=None, peer=None):
-        """RMSNorm(+quant) of the residual stream; first completes a pending peer reduce."""
+    def _norm(self, x, w, B: int, xq=None, xds=None, y_bf16=None, peer=None, bias=None):
+        """The architecture's norm (+quant) of the residual stream; first completes a pending
+        peer reduce."""
+        eps = self.cfg.rms_norm_eps
         if peer is not None and peer.pending:
-            peer.reduce_norm(x[:B], w, self.cfg.rms_norm_eps, xq, xds, y_bf16, B)
+            peer.reduce_norm(x[:B], w, eps, xq, xds, y_bf16, B, w_offset=self.norm_off, bias=bias,
+                             layer=self.norm_layer)
         else:
-            ops.rmsnorm_quant(x[:B], w, self.cfg.rms_norm_eps, xq, xds, y_bf16=y_bf16)
+            ops.rmsnorm_quant(x[:B], w, eps, xq, xds, y_bf16=y_bf16, w_offset=self.norm_off, bias=bias,
+                              layer=self.norm_layer)
+
+    def _qkv_rope(self, lw, xq, xds, B, kv, si):
+        """Decode QKV GEMV + RoPE + paged KV write (fused epilogue; with q/k/v biases the
+        GEMV stores and the token-parallel RoPE kernel adds the bias first)."""
+        if self.qkv_bias:
+            ops.gemv(lw.wqkv, xq, xds, B, ops.EPI_STORE, out_f32=self.qkv_f[:B])
+            ops.rope_kv(self.qkv_f[:B], B, self.rope_cs, si.positions, si.slots, kv, self.q[:B],
+                        n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd, block_size=self.block_size,
+                        rot_dim=self.rot_dim, err=self.err, bias=lw.qkv_bias)
+            return
+        ops.gemv(lw.wqkv, xq, xds, B, ops.EPI_QKV_ROPE, rope_cs=self.rope_cs,
+                 positions=si.positions, slots=si.slots, kv=kv, q_out=self.q[:B],
+                 n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
+                 block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int):
@@ -272,17 +302,14 @@ class ModelRunner:
             lw = self._layer(li)
             kv = self.kv[li]
             if gemv_path:
-                self._norm(x, lw.attn_norm, B, xq, xds, peer=peer)
-                ops.gemv(lw.wqkv, xq, xds, B, ops.EPI_QKV_ROPE, rope_cs=self.rope_cs,
-                         positions=si.positions, slots=si.slots, kv=kv, q_out=self.q[:B],
-                         n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
-                         block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
+                self._norm(x, lw.attn_norm, B, xq, xds, peer=peer, bias=lw.attn_norm_b)
+                self._qkv_rope(lw, xq, xds, B, kv, si)
             else:
-                self._norm(x, lw.attn_norm, B, y_bf16=self.xn_b[:B], peer=peer)
+                self._norm(x, lw.attn_norm, B, y_bf16=self.xn_b[:B], peer=peer, bias=lw.attn_norm_b)
                 self.linear(self.xn_b[:B], lw.wqkv, self.qkv_b[:B])
                 ops.rope_kv(self.qkv_b[:B], B, self.rope_cs, si.positions, si.slots, kv, self.q[:B],
                             n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
-                            block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
+                            block_size=self.block_size, rot_dim=self.rot_dim, err=self.err, bias=lw.qkv_bias)
             ops.paged_attention(self.q[:B], kv, si.block_tables, si.ctx_len, self.attn[:B],
                                 n_rows=B, n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
                                 block_size=self.block_size, n_splits=ns if gemv_path else max(2, ns),
@@ -293,11 +320,12 @@ class ModelRunner:
             if gemv_path:
                 self._row_parallel(lw.wo, xq, xds, B, x, peer)
                 # MoE layers also need the bf16 normalised row for the router
-                self._norm(x, lw.ffn_norm, B, xq, xds, y_bf16=self.xn_b[:B] if lw.wgu is None else None, peer=peer)
+                self._norm(x, lw.ffn_norm, B, xq, xds, y_bf16=self.xn_b[:B] if lw.wgu is None else None, peer=peer,
+                           bias=lw.ffn_norm_b)
                 self._ffn_gemv(lw, B, x, xq, xds, tp, peer)
             else:
                 self._proj_into_residual(self.attn_b[:B], lw.wo, x, self.o_b, tp, peer)
-                self._norm(x, lw.ffn_norm, B, y_bf16=self.xn_b[:B], peer=peer)
+                self._norm(x, lw.ffn_norm, B, y_bf16=self.xn_b[:B], peer=peer, bias=lw.ffn_norm_b)
                 self._ffn_gemm(lw, B, x, tp, peer)
             self._layer_done(li)
         self._head(B, x, xq, xds, gemv_path, peer)
@@ -310,6 +338,7 @@ class ModelRunner:
             w = self.w
             self._fused_ok = (self.tp_size == 1 and self.hd == 128 and q4(w.lm_head) and
                               os.environ.get("AIR_FUSED_NORM", "1") != "0" and
+                              not self.norm_layer and not self.dense_ffn and not self.qkv_bias and
                               all(lw.wgu is not None and q4(lw.wqkv) and q4(lw.wo) and q4(lw.w_gate) and
                                   q4(lw.wdown) for lw in w.layers))
         return self._fused_ok and self.streamer is None
@@ -328,7 +357,7 @@ class ModelRunner:
         # i.e. after the previous consumer has finished reading it
         ss = self.ss[:B]
         ops.embed(w.embd, si.ids, out_f32=x, err=self.err, n=B)
-        ops.rmsnorm_quant(x, w.layers[0].attn_norm, eps, xa, xda)
+        ops.rmsnorm_quant(x, w.layers[0].attn_norm, eps, xa, xda, w_offset=self.norm_off)
         ns = self.n_splits(B)
         L = len(w.layers)
         for li in range(L):
@@ -345,12 +374,12 @@ class ModelRunner:
                                 part_o=self.part_o, part_ml=self.part_ml, out_q=aq, out_ds=ads,
                                 err=self.err, window=self.layer_window[li])
             ops.gemv(lw.wo, aq, ads, B, ops.EPI_RESIDUAL, resid=x, norm_w=lw.ffn_norm, out_q=xa, out_ds=xda,
-                     ss_out=ss)
+                     ss_out=ss, norm_offset=self.norm_off)
             ops.gemv(lw.w_gate, xa, xda, B, ops.EPI_SWIGLU, w2=lw.w_up, ld_out=self.Fp, out_q=hq, out_ds=hds,
-                     ss_in=ss, norm_k=H, eps=eps)
+                     ss_in=ss, norm_k=H, eps=eps, act=self.act)
             nxt = w.layers[li + 1].attn_norm if li + 1 < L else w.out_norm
             ops.gemv(lw.wdown, hq, hds, B, ops.EPI_RESIDUAL, resid=x, norm_w=nxt, out_q=xa, out_ds=xda,
-                     ss_out=ss)
+                     ss_out=ss, norm_offset=self.norm_off)
         ops.gemv(w.lm_head, xa, xda, B, ops.EPI_STORE, out_f32=self.logits[:B], ss_in=ss, norm_k=H, eps=eps)
         ops.sample(self.logits[:B], si.tokens, counts=self.counts, count_row=si.count_row, mask=si.mask,
                    temperature=si.temperature, penalty=si.penalty, top_k=si.top_k, top_p=si.top_p,
@@ -370,13 +399,22 @@ class ModelRunner:
             from ..parallel import moe
             moe.moe_ffn_decode(self, lw, B, x, xq, xds, peer)
             return
+        if self.dense_ffn:
+            # dense GELU MLP: up GEMV, GELU, quantise, down
+            ops.gemv(lw.wgu, xq, xds, B, ops.EPI_STORE, out_f32=self.h[:B], ld_out=self.Fp)
+            ops.swiglu(self.h[:B], B, self.F, out_f32=self.h[:B], ld_out=self.Fp, up_off=-1, act=self.act)
+            ops.rmsnorm_quant(self.h[:B], None, 0.0, xq, xds)
+            self._row_parallel(lw.wdown, xq, xds, B, x, peer)
+            return
         if lw.w_gate.fmt == ops.FMT_Q4K:
-            # SwiGLU product quantised in the GEMV epilogue (no separate quant kernel)
+            # gated product quantised in the GEMV epilogue (no separate quant kernel)
             hq, hds = self.hq[:B], self.hds[:B]
-            ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, ld_out=self.Fp, out_q=hq, out_ds=hds)
+            ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, ld_out=self.Fp, out_q=hq, out_ds=hds,
+                     act=self.act)
             self._row_parallel(lw.wdown, hq, hds, B, x, peer)
             return
-        ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, out_f32=self.h[:B], ld_out=self.Fp)
+        ops.gemv(lw.w_gate, xq, xds, B, ops.EPI_SWIGLU, w2=lw.w_up, out_f32=self.h[:B], ld_out=self.Fp,
+                 act=self.act)
         ops.rmsnorm_quant(self.h[:B], None, 0.0, xq, xds)
         self._row_parallel(lw.wdown, xq, xds, B, x, peer)
 
@@ -386,16 +424,17 @@ class ModelRunner:
             moe.moe_ffn_gemm(self, lw, B, x, peer)
             return
         self.linear(self.xn_b[:B], lw.wgu, self.gu_b[:B])
-        ops.swiglu(self.gu_b[:B], B, self.F, out_bf16=self.h_b[:B], ld_out=self.Fp, up_off=self.up_off)
+        ops.swiglu(self.gu_b[:B], B, self.F, out_bf16=self.h_b[:B], ld_out=self.Fp, up_off=self.up_off,
+                   act=self.act)
         self._proj_into_residual(self.h_b[:B], lw.wdown, x, self.o_b, tp, peer)
 
     def _head(self, B, x, xq, xds, gemv_path, peer=None):
         w, si = self.w, self.inputs[B]
         if gemv_path:
-            self._norm(x, w.out_norm, B, xq, xds, peer=peer)
+            self._norm(x, w.out_norm, B, xq, xds, peer=peer, bias=w.out_norm_b)
             ops.gemv(w.lm_head, xq, xds, B, ops.EPI_STORE, out_f32=self.logits[:B])
         else:
-            self._norm(x, w.out_norm, B, y_bf16=self.xn_b[:B], peer=peer)
+            self._norm(x, w.out_norm, B, y_bf16=self.xn_b[:B], peer=peer, bias=w.out_norm_b)
             self.linear(self.xn_b[:B], w.lm_head, self.logits[:B])
         logits = self.logits[:B]
         if self.tp_size > 1:
@@ -496,23 +535,26 @@ class ModelRunner:
                 _sp.__enter__()
             lw = self._layer(li)
             kv = self.kv[li]
-            ops.rmsnorm_quant(x, lw.attn_norm, eps, None, None, y_bf16=xn)
+            ops.rmsnorm_quant(x, lw.attn_norm, eps, None, None, y_bf16=xn, bias=lw.attn_norm_b,
+                              w_offset=self.norm_off, layer=self.norm_layer)
             self.linear(xn, lw.wqkv, qkv)
             ops.rope_kv(qkv, T, self.rope_cs, positions, slots, kv, q, n_heads=self.nh, n_kv=self.nkv,
-                        head_dim=self.hd, block_size=self.block_size, rot_dim=self.rot_dim, err=self.err)
+                        head_dim=self.hd, block_size=self.block_size, rot_dim=self.rot_dim, err=self.err,
+                        bias=lw.qkv_bias)
             ops.paged_attention(q, kv, block_tables, ctx, attn, n_rows=T, n_heads=self.nh,
                                 n_kv=self.nkv, head_dim=self.hd, block_size=self.block_size,
                                 row_seq=row_seq, n_splits=1, err=self.err,
                                 window=self.layer_window[li], tree_base=tree_base, tree_mask=tree_mask)
             attn_b.copy_(attn)
             self._proj_into_residual(attn_b, lw.wo, x, o, tp)
-            ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=xn)
+            ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=xn, bias=lw.ffn_norm_b,
+                              w_offset=self.norm_off, layer=self.norm_layer)
             if lw.wgu is None:
                 from ..parallel import moe
                 moe.moe_ffn_prefill(self, lw, T, x, xn)
             else:
                 self.linear(xn, lw.wgu, gu)
-                ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp, up_off=self.up_off)
+                ops.swiglu(gu, T, self.F, out_bf16=hb, ld_out=self.Fp, up_off=self.up_off, act=self.act)
                 self._proj_into_residual(hb, lw.wdown, x, o, tp)
             self._layer_done(li)
             if _sp is not None:
@@ -521,11 +563,13 @@ class ModelRunner:
             return x.clone()
         if return_hidden:  # final-norm hidden states of every row (embeddings)
             hn = self._ws("hn", (T, self.H), bf16)
-            ops.rmsnorm_quant(x, w.out_norm, eps, None, None, y_bf16=hn)
+            ops.rmsnorm_quant(x, w.out_norm, eps, None, None, y_bf16=hn, bias=w.out_norm_b,
+                              w_offset=self.norm_off, layer=self.norm_layer)
             return hn.float()
         xl = x.index_select(0, last_rows.long())
         xs = self._ws("xs", (S, self.H), bf16)
-        ops.rmsnorm_quant(xl, w.out_norm, eps, None, None, y_bf16=xs)
+        ops.rmsnorm_quant(xl, w.out_norm, eps, None, None, y_bf16=xs, bias=w.out_norm_b,
+                          w_offset=self.norm_off, layer=self.norm_layer)
         logits = self._ws("logits", (S, self.V_l), f32)
         self.linear(xs, w.lm_head, logits)
         if tp:

@@ -47,9 +47,10 @@ void post_launch(const char* what) {
 
 void rmsnorm_quant(optional<Tensor> x, optional<Tensor> x_bf16, optional<Tensor> w, double w_offset,
                    double eps, int64_t B, int64_t K, optional<Tensor> q, optional<Tensor> ds,
-                   optional<Tensor> y_bf16) {
+                   optional<Tensor> y_bf16, optional<Tensor> bias, int64_t layer) {
   TORCH_CHECK(K % 32 == 0, "rmsnorm_quant: K must be a multiple of 32");
-  air::launch_rmsnorm_quant(ptr<float>(x), ptr(x_bf16), ptr<float>(w), (float)w_offset, (int)B,
+  air::launch_rmsnorm_quant(ptr<float>(x), ptr(x_bf16), ptr<float>(w), (float)w_offset, ptr<float>(bias),
+                            (int)layer, (int)B,
                             (int)K, (float)eps, ptr<int8_t>(q), ptr<float2>(ds), ptr(y_bf16), stream());
   post_launch("rmsnorm_quant");
 }
@@ -63,7 +64,7 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
           int64_t block_size, int64_t rot_dim, optional<Tensor> err, int64_t splits,
           optional<Tensor> ws, optional<Tensor> counters, optional<Tensor> push_meta,
           optional<Tensor> out_q, optional<Tensor> out_ds, optional<Tensor> norm_w, double norm_offset,
-          optional<Tensor> ss_out, optional<Tensor> ss_in, int64_t norm_k, double eps) {
+          optional<Tensor> ss_out, optional<Tensor> ss_in, int64_t norm_k, double eps, int64_t act) {
   check_cuda(data, "gemv weight");
   TORCH_CHECK(B >= 1 && B <= 8, "gemv: batch must be in [1, 8]");
   TORCH_CHECK(K % 32 == 0, "gemv: K must be a multiple of 32");
@@ -88,6 +89,7 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
   ep.block_size = (int)block_size;
   ep.rot_dim = (int)rot_dim;
   ep.err = ptr<int>(err);
+  ep.act = (int)act;
   if (mode == air::kEpiSwiGLU) TORCH_CHECK(ep.w2.data, "gemv swiglu: w2 required");
   if (norm_w.has_value()) {
     TORCH_CHECK(mode == air::kEpiResidual && fmt == air::kFmtQ4K && out_q.has_value() && out_ds.has_value() &&
@@ -233,19 +235,19 @@ void dequant(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, 
 
 void rope_kv(Tensor qkv, int64_t T, Tensor rope_cs, Tensor positions, Tensor slots, Tensor kv,
              Tensor q_out, int64_t n_heads, int64_t n_kv, int64_t head_dim, int64_t block_size,
-             int64_t rot_dim, optional<Tensor> err) {
+             int64_t rot_dim, optional<Tensor> err, optional<Tensor> bias) {
   air::RopeKvArgs a{ptr<float2>(rope_cs), ptr<int>(positions), ptr<int64_t>(slots), kv.data_ptr(),
                     ptr<float>(q_out), (int)n_heads, (int)n_kv, (int)head_dim, (int)block_size,
-                    (int)rot_dim, kv.size(0), ptr<int>(err)};
+                    (int)rot_dim, kv.size(0), ptr<int>(err), ptr<float>(bias)};
   air::launch_rope_kv(qkv.data_ptr(), qkv.scalar_type() == at::kBFloat16, (int)T, a, stream());
   post_launch("rope_kv");
 }
 
 void swiglu(Tensor gu, int64_t T, int64_t F, int64_t up_off, int64_t ld_out, optional<Tensor> out_bf16,
-            optional<Tensor> out_f32) {
+            optional<Tensor> out_f32, int64_t act) {
   air::launch_swiglu(gu.data_ptr(), gu.scalar_type() == at::kBFloat16, (int)T, (int)F, gu.stride(0), up_off,
                      ld_out, ptr(out_bf16),
-                     ptr<float>(out_f32), stream());
+                     ptr<float>(out_f32), (int)act, stream());
   post_launch("swiglu");
 }
 

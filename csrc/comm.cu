@@ -91,8 +91,18 @@ __global__ void __launch_bounds__(kThreads) tp_reduce_norm_kernel(const __grid_c
     }
   }
   if (timed_out) set_error(R.err, kErrTimeout);
-  float scale = 1.f;
+  float scale = 1.f, mean = 0.f;
   if (a.w) {
+    if (a.layer) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kMaxPer; ++j) s += v[j];      // zero beyond K
+      mean = block_sum(s, red) / (float)K;
+      ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kMaxPer; ++j)
+        if (j * kThreads + t < K) ss += (v[j] - mean) * (v[j] - mean);
+    }
     ss = block_sum(ss, red);
     scale = rsqrtf(ss / (float)K + a.eps);
   }
@@ -101,8 +111,9 @@ __global__ void __launch_bounds__(kThreads) tp_reduce_norm_kernel(const __grid_c
   for (int j = 0; j < kMaxPer; ++j) {
     const int i = j * kThreads + t;
     if (j * kThreads >= K) break;          // uniform across the CTA
-    float y = v[j] * scale;
+    float y = (v[j] - mean) * scale;
     if (a.w && i < K) y *= (a.w[i] + a.w_offset);
+    if (a.bias && i < K) y += a.bias[i];
     if (i < K && R.y_bf16) static_cast<__nv_bfloat16*>(R.y_bf16)[(size_t)b * K + i] = f2bf(y);
     if (R.q) {
       // a warp covers 32 consecutive elements = one Q8A group (K % 32 == 0)

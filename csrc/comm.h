@@ -50,8 +50,10 @@ struct TPReduceArgs {
   int64_t slot_elems;
   int64_t shard;              // two-shot columns per rank (0 = one-shot)
   int64_t timeout_ns;
-  const float* w;             // RMSNorm weight [K] (null: no normalisation)
+  const float* w;             // norm weight [K] (null: no normalisation)
   float w_offset;
+  const float* bias;          // optional norm bias [K]
+  int layer;                  // 1: LayerNorm (mean subtracted), 0: RMSNorm
   float eps;
   int B, K;
 };

@@ -91,7 +91,7 @@ air::TPReduceRank reduce_rank_from_meta(const Tensor& meta, int64_t* slot, int* 
 void tp_reduce_norm(const std::vector<Tensor>& metas, const std::vector<Tensor>& xs, optional<Tensor> w,
                     double w_offset, double eps, int64_t B, int64_t K, const std::vector<optional<Tensor>>& qs,
                     const std::vector<optional<Tensor>>& dss, const std::vector<optional<Tensor>>& ys,
-                    bool two_shot) {
+                    bool two_shot, optional<Tensor> bias, int64_t layer) {
   const int n = (int)metas.size();
   TORCH_CHECK(n >= 1 && n <= air::kMaxPeers && (int)xs.size() == n, "tp_reduce_norm: 1..8 ranks, one x each");
   TORCH_CHECK(qs.empty() || (int)qs.size() == n, "tp_reduce_norm: q per rank");
@@ -126,6 +126,8 @@ void tp_reduce_norm(const std::vector<Tensor>& metas, const std::vector<Tensor>&
   }
   a.w = static_cast<const float*>(p(w));
   a.w_offset = (float)w_offset;
+  a.bias = static_cast<const float*>(p(bias));
+  a.layer = (int)layer;
   a.eps = (float)eps;
   a.B = (int)B;
   a.K = (int)K;

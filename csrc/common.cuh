@@ -34,6 +34,14 @@ inline bool set_max_smem_per_device(Kernel kernel, int bytes, unsigned long long
   return true;
 }
 
+// Gate activation of the gated FFNs: 0 = SiLU (SwiGLU), 1 = GELU, tanh form (GeGLU / dense
+// GELU MLP; reference src/ops.rs:103-119: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))).
+enum GateAct : int { kActSilu = 0, kActGelu = 1 };
+AIR_DEVICE float gate_act(float x, int act) {
+  if (act == kActGelu) return 0.5f * x * (1.f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+  return x / (1.f + __expf(-x));
+}
+
 AIR_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -232,7 +232,7 @@ gemv_kernel(GemvWeight w, int N, int K, int nB, const int8_t* __restrict__ xq,
     for (int b = 0; b < MAXB; ++b) {
       if (b < nB && lane == b) {
         const float g = acc[0][b], u = acc[1][b];
-        const float s = g / (1.f + __expf(-g));
+        const float s = gate_act(g, ep.act);
         const size_t o = (size_t)b * ep.ld_out + task;
         if (ep.out_f32) ep.out_f32[o] = s * u;
         if (ep.out_bf16) static_cast<__nv_bfloat16*>(ep.out_bf16)[o] = f2bf(s * u);

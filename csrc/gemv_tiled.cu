@@ -190,7 +190,7 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
       for (int b = 0; b < MAXB; ++b) {
         if (b >= nB) break;
         float v = 0.f;
-        if (row < N) v = acc[0][b] / (1.f + __expf(-acc[0][b])) * acc[1][b];
+        if (row < N) v = gate_act(acc[0][b], ep.act) * acc[1][b];
         if (ep.out_f32) { if (row < N) ep.out_f32[(size_t)b * ep.ld_out + row] = v; }
         const float amax = warp_max(fabsf(v));
         const float dq = amax / 127.f;
@@ -241,7 +241,7 @@ gemv_tiled_kernel(const uint8_t* __restrict__ w1, const uint8_t* __restrict__ w2
       if ((b % TPR) != c4 || b >= nB) continue;
       const size_t o = (size_t)b * ep.ld_out + row;
       float v = acc[0][b];
-      if (DUAL) v = v / (1.f + __expf(-v)) * acc[W - 1][b];
+      if (DUAL) v = gate_act(v, ep.act) * acc[W - 1][b];
       if (ep.mode == kEpiResidual) {
         ep.resid[o] += v;
       } else {

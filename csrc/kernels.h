@@ -85,14 +85,17 @@ struct GemvEpiParams {
   const float* ss_in;
   int norm_k;
   float eps;
+  int act;                    // kEpiSwiGLU gate activation (GateAct): SiLU or GELU (GeGLU)
 };
 
 // x: activations quantised by rmsnorm_quant (int8 [B,K] + float2 [B,K/32]).
 void launch_gemv(const GemvWeight& w, int N, int K, int B, const int8_t* xq, const float2* xds,
                  const GemvEpiParams& ep, cudaStream_t st);
 
+// layer = 0: RMSNorm, y = x * rsqrt(mean(x^2) + eps) * (w + w_offset) (+ bias);
+// layer = 1: LayerNorm, y = (x - mean) * rsqrt(var + eps) * (w + w_offset) (+ bias).
 void launch_rmsnorm_quant(const float* x, const void* x_bf16, const float* w, float w_offset,
-                          int B, int K, float eps, int8_t* q, float2* ds, void* y_bf16,
-                          cudaStream_t st);
+                          const float* bias, int layer, int B, int K, float eps, int8_t* q, float2* ds,
+                          void* y_bf16, cudaStream_t st);
 
 }  // namespace air

@@ -90,6 +90,10 @@ __global__ void rope_kv_kernel(const TIn* __restrict__ qkv, int T, RopeKvArgs a)
   float x0, x1;
   if constexpr (sizeof(TIn) == 4) { x0 = row[i]; x1 = row[i + half]; }
   else { x0 = bf2f(row[i]); x1 = bf2f(row[i + half]); }
+  if (a.bias) {   // q/k/v projection bias (Qwen2), added before RoPE
+    x0 += a.bias[(size_t)head * a.head_dim + i];
+    x1 += a.bias[(size_t)head * a.head_dim + i + half];
+  }
   const bool is_v = head >= a.n_heads + a.n_kv;
   const int rh = a.rot_dim / 2;
   if (!is_v && i < rh) {
@@ -115,18 +119,19 @@ __global__ void rope_kv_kernel(const TIn* __restrict__ qkv, int T, RopeKvArgs a)
   base[i + half] = f2bf(x1);
 }
 
-// out[t, j] = silu(gu[t, j]) * gu[t, F + j]   (gate/up concatenated along columns)
+// out[t, j] = act(gu[t, j]) * gu[t, up_off + j]   (gate/up concatenated along columns);
+// up_off < 0: out = act(gu[t, j]) (dense GELU MLP, no gate)
 template <typename TIn>
 __global__ void swiglu_kernel(const TIn* __restrict__ gu, int T, int F, int64_t ld_in, int64_t up_off,
                               int64_t ld_out,
-                              __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
+                              __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32, int act) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)T * F) return;
   const int64_t t = idx / F, j = idx % F;
-  float g, u;
-  if constexpr (sizeof(TIn) == 4) { g = gu[t * ld_in + j]; u = gu[t * ld_in + up_off + j]; }
-  else { g = bf2f(gu[t * ld_in + j]); u = bf2f(gu[t * ld_in + up_off + j]); }
-  const float v = g / (1.f + __expf(-g)) * u;
+  float g, u = 1.f;
+  if constexpr (sizeof(TIn) == 4) { g = gu[t * ld_in + j]; if (up_off >= 0) u = gu[t * ld_in + up_off + j]; }
+  else { g = bf2f(gu[t * ld_in + j]); if (up_off >= 0) u = bf2f(gu[t * ld_in + up_off + j]); }
+  const float v = gate_act(g, act) * u;
   if (out_bf16) out_bf16[t * ld_out + j] = f2bf(v);
   if (out_f32) out_f32[t * ld_out + j] = v;
 }
@@ -165,12 +170,12 @@ void launch_rope_kv(const void* qkv, bool bf16_in, int T, const RopeKvArgs& a, c
 }
 
 void launch_swiglu(const void* gu, bool bf16_in, int T, int F, int64_t ld_in, int64_t up_off,
-                   int64_t ld_out, void* out_bf16, float* out_f32, cudaStream_t st) {
+                   int64_t ld_out, void* out_bf16, float* out_f32, int act, cudaStream_t st) {
   const int64_t n = (int64_t)T * F;
   if (n <= 0) return;
   const unsigned grid = (unsigned)((n + 255) / 256);
-  if (bf16_in) swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, out_f32);
-  else swiglu_kernel<float><<<grid, 256, 0, st>>>((const float*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, out_f32);
+  if (bf16_in) swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, out_f32, act);
+  else swiglu_kernel<float><<<grid, 256, 0, st>>>((const float*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, out_f32, act);
 }
 
 void launch_residual_add(float* resid, const void* y, bool bf16_in, int64_t n, cudaStream_t st) {

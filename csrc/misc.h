@@ -14,6 +14,7 @@ struct RopeKvArgs {
   int n_heads, n_kv, head_dim, block_size, rot_dim;
   int64_t num_blocks;
   int* err;
+  const float* bias;       // optional [(n_heads + 2 n_kv) * head_dim] q|k|v bias, added before RoPE
 };
 
 void launch_embed(int fmt, const void* table, const void* scales, int64_t row_bytes, int K,
@@ -23,7 +24,7 @@ void launch_dequant(int fmt, const void* w, const void* scales, int64_t row_byte
                     void* out, cudaStream_t st);
 void launch_rope_kv(const void* qkv, bool bf16_in, int T, const RopeKvArgs& a, cudaStream_t st);
 void launch_swiglu(const void* gu, bool bf16_in, int T, int F, int64_t ld_in, int64_t up_off,
-                   int64_t ld_out, void* out_bf16, float* out_f32, cudaStream_t st);
+                   int64_t ld_out, void* out_bf16, float* out_f32, int act, cudaStream_t st);
 void launch_residual_add(float* resid, const void* y, bool bf16_in, int64_t n, cudaStream_t st);
 
 }  // namespace air

@@ -83,7 +83,7 @@ def test_multi_rank_serving_mirrors_rank0(tmp_path):
     worker = os.path.join(os.path.dirname(__file__), "workers", "serve_worker.py")
     env = dict(os.environ, PYTHONPATH=os.getcwd())
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29561", worker, str(out)]
+           "--master-addr=127.0.0.1", "--master-port=29597", worker, str(out)]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     r0 = json.loads(open(f"{out}.0").read())
