@@ -69,6 +69,8 @@ def build_parser() -> argparse.ArgumentParser:
     g.add_argument("--seed", type=int, default=0)
 
     s = sub.add_parser("serve", help="OpenAI-compatible HTTP server")
+    s.add_argument("--dp", type=int, default=1,
+                   help="Data-parallel replicas: one full model per GPU (cuda:0..N-1) behind one endpoint")
     _common(s, serve=True)
     s.add_argument("-P", "--port", type=int, default=8080)
     s.add_argument("-H", "--host", default="127.0.0.1")
@@ -195,6 +197,8 @@ def cmd_serve(args) -> int:
     import uvicorn
     from .serve.app import create_app
     from .serve.dispatcher import EngineDispatcher
+    if getattr(args, "dp", 1) > 1 and args.device is None:
+        args.device = "cuda:0"
     core = _engine(args, max_batch=args.max_num_seqs)
     name = args.model_name or os.path.splitext(os.path.basename(args.model))[0]
     if args.tp > 1:
@@ -206,6 +210,14 @@ def cmd_serve(args) -> int:
         if d.rank != 0:
             d.serve_follower()
             return 0
+    elif getattr(args, "dp", 1) > 1:
+        # data-parallel replicas: one engine per GPU, least-in-flight routing
+        from .serve.replicas import ReplicaRouter
+        reps = [EngineDispatcher(core, name)]
+        for i in range(1, args.dp):
+            reps.append(EngineDispatcher(_engine(argparse.Namespace(**{**vars(args), "device": f"cuda:{i}"}),
+                                                 max_batch=args.max_num_seqs), name))
+        d = ReplicaRouter(reps, name)
     else:
         d = EngineDispatcher(core, name)
     safety = None

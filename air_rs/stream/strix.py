@@ -244,3 +244,84 @@ class ResidencyScheduler:
             if t.layer == current_layer:
                 t.last_access = self.step
         return load, evict
+
+
+# ---------------------------------------------------------------------------------------
+# Memory budget (native) and cold boot (reference src/strix/arena.rs, src/strix/ram_pool.rs,
+# src/strix/cold_boot.rs)
+# ---------------------------------------------------------------------------------------
+
+def vram_arena(total_bytes: int, safety_margin: int = 0):
+    """The native first-fit VRAM budget arena (``air_rs._host.VramArena``): offsets within a
+    budget, alignment, coalescing on free, and a round-robin ring of prefetch flight slots."""
+    from .. import _host
+    return _host.VramArena(total_bytes, safety_margin)
+
+
+def ram_pool(max_bytes: int):
+    """The native host staging-buffer pool (``air_rs._host.RamPool``), power-of-two classes."""
+    from .. import _host
+    return _host.RamPool(max_bytes)
+
+
+@dataclass
+class ColdBootStep:
+    name: str
+    target: str          # "pinned" | "hot" | "warm" | "cold"
+    phase: int
+    size_bytes: int
+
+
+@dataclass
+class ColdBootPlan:
+    steps: list
+    phase_bytes: dict    # phase -> bytes
+    skipped: int
+
+    @property
+    def total_transfer_bytes(self) -> int:
+        """Bytes moved at boot: phases 1-3 (pin, first layers hot, the rest staged in RAM)."""
+        return sum(self.phase_bytes.get(p, 0) for p in (1, 2, 3))
+
+    @property
+    def critical_path_bytes(self) -> int:
+        """Bytes that must land before the first token: phases 1 and 2."""
+        return sum(self.phase_bytes.get(p, 0) for p in (1, 2))
+
+    def estimate_seconds(self, mb_per_s: float) -> float:
+        return float("inf") if mb_per_s <= 0 else self.total_transfer_bytes / 2**20 / mb_per_s
+
+    def estimate_ttft_seconds(self, mb_per_s: float) -> float:
+        return float("inf") if mb_per_s <= 0 else self.critical_path_bytes / 2**20 / mb_per_s
+
+
+def plan_cold_boot(tensors, prefetch_window: int) -> ColdBootPlan:
+    """Order a model's first load by tensor class (reference ``src/strix/cold_boot.rs:76-170``).
+
+    ``tensors``: iterable of (name, TensorClass, layer or None, size_bytes). Phase 1 pins
+    class A (embeddings, norms, LM head); phase 2 makes class-B layers below
+    ``prefetch_window`` hot in HBM, in layer order; phase 3 stages the other class-B layers
+    in host RAM (warm); phase 4 leaves class C on disk (cold); class D is skipped."""
+    steps, pb, skipped = [], {}, 0
+    items = list(tensors)
+
+    def add(name, target, phase, size):
+        steps.append(ColdBootStep(name, target, phase, size))
+        pb[phase] = pb.get(phase, 0) + size
+
+    for name, tc, layer, size in items:
+        if tc == TensorClass.A:
+            add(name, "pinned", 1, size)
+    b = sorted((x for x in items if x[1] == TensorClass.B),
+               key=lambda x: x[2] if x[2] is not None else 1 << 60)
+    for name, tc, layer, size in b:
+        if layer is not None and layer < prefetch_window:
+            add(name, "hot", 2, size)
+        else:
+            add(name, "warm", 3, size)
+    for name, tc, layer, size in items:
+        if tc == TensorClass.C:
+            add(name, "cold", 4, size)
+        elif tc == TensorClass.D:
+            skipped += 1
+    return ColdBootPlan(steps, pb, skipped)

@@ -1,4 +1,4 @@
-"""The native host runtime (paged-KV bookkeeping) built with AddressSanitizer and
+"""The native host runtime (paged-KV bookkeeping, VRAM arena, RAM pool) built with AddressSanitizer and
 UndefinedBehaviorSanitizer, driven through random operation sequences in a child process:
 a heap error or undefined behaviour aborts the child, and every sequence must return all of
 its blocks to the pool when freed."""
@@ -39,6 +39,25 @@ for seed in range(4):
     for s in live:
         m.free_sequence(s)
     assert m.allocator.num_free_blocks() == 24, m.allocator.num_free_blocks()
+for seed in range(4):
+    random.seed(seed)
+    a = _host.VramArena(1 << 20, 4096)
+    held = []
+    for i in range(3000):
+        if held and random.random() < 0.45:
+            a.free(held.pop(random.randrange(len(held))))
+        else:
+            x = a.allocate(random.randint(1, 50000), random.choice([1, 256, 4096]))
+            if x is not None:
+                held.append(x)
+    for x in held:
+        a.free(x)
+    assert a.used == 0 and a.fragment_count() == 1 and a.largest_free() == a.usable
+    pool = _host.RamPool(1 << 18)
+    bufs = [pool.acquire(random.randint(1, 70000)) for _ in range(64)]
+    for b in bufs:
+        memoryview(b)[:len(b)] = b"x" * len(b)
+        pool.release(b)
 print("clean")
 """
 
@@ -52,7 +71,7 @@ def _lib(name):
 def test_host_runtime_under_asan_ubsan(tmp_path):
     import pybind11
     out = tmp_path / ("_host" + sysconfig.get_config_var("EXT_SUFFIX"))
-    src = [os.path.join(ROOT, "csrc", "host", f) for f in ("host_kv.cpp", "module.cpp")]
+    src = [os.path.join(ROOT, "csrc", "host", f) for f in ("host_kv.cpp", "arena.cpp", "module.cpp")]
     cmd = ["g++", "-shared", "-fPIC", "-O1", "-g", "-fsanitize=address,undefined", "-fno-omit-frame-pointer",
            "-std=c++17", "-DAIR_HOST_NO_TORCH", "-I" + pybind11.get_include(),
            "-I" + sysconfig.get_paths()["include"], *src, "-o", str(out)]

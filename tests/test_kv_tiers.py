@@ -159,3 +159,47 @@ def test_engine_prefix_cache_and_preemption():
         assert len(o) == 64
         _check_near_argmax(oracle, [cfg.bos_token_id] + p, o, penalty=1.0)
     assert eng.seqs.allocator.num_used_blocks() == 0
+
+
+def test_tri_attention_scores_match_definition():
+    """TriAttention (reference src/tri_attention.rs:17-28, 93-129): sinks score 1, the rest is
+    the min-max normalised blend of the scaled head-mean cosine and the RoPE phase term."""
+    import math
+    import torch
+    from air_rs.kv.tri_attention import ALPHA, SINK_COUNT, TriScorer, TriAttentionTierManager
+    from air_rs.kv.tiers import KvTier, TierBudget
+    H, D, S = 4, 64, 40
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(H * D, generator=g)
+    k = torch.randn(S, H, D, generator=g)
+    sc = TriScorer(D, H, 10000.0)
+    got = sc.score(q, k)
+    # per-position loop, straight from the definition
+    freqs = [1.0 / 10000.0 ** (2 * i / D) for i in range(D // 2)]
+    raw = []
+    for p in range(S):
+        if p < SINK_COUNT:
+            raw.append(1.0)
+            continue
+        sims = []
+        for h in range(H):
+            qh, kh = q[h * D:(h + 1) * D], k[p, h]
+            c = float(qh @ kh) * D ** -0.25 / (float(qh.norm()) * float(kh.norm()))
+            sims.append(max(-1.0, min(1.0, c)))
+        ph = (sum(math.cos(f * p) for f in freqs) / len(freqs) + 1) / 2
+        raw.append(max(0.0, min(1.0, ALPHA * sum(sims) / H + (1 - ALPHA) * ph)))
+    lo, hi = min(raw[SINK_COUNT:]), max(raw[SINK_COUNT:])
+    ref = raw[:SINK_COUNT] + [(r - lo) / (hi - lo) for r in raw[SINK_COUNT:]]
+    torch.testing.assert_close(got, torch.tensor(ref), rtol=1e-4, atol=1e-5)
+    m = TriScorer.keep_mask(got, 10)
+    assert int(m.sum()) == 10 and bool(m[:SINK_COUNT].all())
+    assert int(TriScorer.keep_mask(got, 1).sum()) == SINK_COUNT + 1      # minimum budget
+    # as a tier manager: the lowest-scoring active positions are demoted first
+    mgr = TriAttentionTierManager(TierBudget(pinned_max=4, active_max=30, warm_max=100), sc)
+    for p in range(S):
+        mgr.add_token(p)
+    mgr.update_scores(q, k)
+    mgr.enforce_budgets()
+    warm = sorted(p for p, e in mgr.entries.items() if e.tier == KvTier.WARM)
+    expect = sorted(sorted(range(S), key=lambda p: (float(got[p]), p))[:S - 30])
+    assert warm == expect

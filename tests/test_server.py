@@ -106,3 +106,49 @@ def test_engine_dispatcher_cpu(tmp_path):
         assert len(e) == 256
     finally:
         d.shutdown()
+
+
+def test_replica_router_balances_and_skips_failed_replica():
+    """Data-parallel replicas: least-in-flight routing with round robin on ties, and a
+    replica that raises before streaming is skipped for the next one."""
+    import asyncio
+    from air_rs.serve.dispatcher import GenerateConfig, TokenChunk
+    from air_rs.serve.replicas import ReplicaRouter
+
+    class Slow(MockDispatcher):
+        async def generate(self, config):
+            await asyncio.sleep(0.01)
+            async for c in super().generate(config):
+                yield c
+
+    class Broken(MockDispatcher):
+        async def generate(self, config):
+            raise RuntimeError("GPU lost")
+            yield
+
+    reps = [Slow("m", ["a"]), Slow("m", ["b"]), Slow("m", ["c"])]
+    router = ReplicaRouter(reps, "m")
+
+    async def one(i):
+        return [c async for c in router.generate(GenerateConfig(prompt=str(i), max_tokens=4))]
+
+    async def many():
+        return await asyncio.gather(*(one(i) for i in range(6)))
+
+    outs = asyncio.run(many())
+    assert sorted(o[0].text for o in outs) == ["a", "a", "b", "b", "c", "c"]
+    assert router.served == [2, 2, 2] and router.in_flight == [0, 0, 0]
+    r2 = ReplicaRouter([Broken("m"), MockDispatcher("m", ["ok"])], "m")
+    for _ in range(3):
+        out = asyncio.run(_collect(r2))
+        assert out[0].text == "ok" and out[-1].finish_reason == "stop"
+    dead = ReplicaRouter([Broken("m")], "m")
+    assert asyncio.run(_collect(dead))[-1].error.startswith("all replicas failed")
+    client = TestClient(create_app(ReplicaRouter([MockDispatcher("m"), MockDispatcher("m")], "m"), "m"))
+    r = client.post("/v1/completions", json={"prompt": "x", "max_tokens": 8})
+    assert r.json()["choices"][0]["text"] == "Hello, world!"
+
+
+async def _collect(router):
+    from air_rs.serve.dispatcher import GenerateConfig
+    return [c async for c in router.generate(GenerateConfig(prompt="p", max_tokens=4))]

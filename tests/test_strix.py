@@ -68,3 +68,51 @@ def test_gguf_read_parallel_matches_memory_map(tmp_path):
     assert set(bufs) == set(g.tensors)
     for n in g.tensors:
         assert torch.equal(bufs[n], g.raw(n)), n
+
+
+def test_native_vram_arena_and_ram_pool():
+    """Native STRIX budget arena (reference src/strix/arena.rs) and RAM pool (ram_pool.rs)."""
+    from air_rs.stream.strix import ram_pool, vram_arena
+    a = vram_arena(1 << 20, 4096)
+    assert a.usable == (1 << 20) - 4096 and a.available == a.usable
+    x = a.allocate(1000, 256)
+    y = a.allocate(5000, 4096)
+    assert x.offset == 0 and y.offset % 4096 == 0 and y.offset >= 1000
+    assert a.used == 6000 and a.fragment_count() == 2          # the alignment gap stays free
+    a.free(x)
+    a.free(y)
+    assert a.used == 0 and a.fragment_count() == 1 and a.largest_free() == a.usable
+    with pytest.raises(ValueError):
+        a.free(y)                                                 # double free is caught
+    assert a.allocate(a.usable + 1, 1) is None                    # out of budget
+    a.register_flight_slots(3, 65536, 4096)
+    order = [a.next_flight_slot().index for _ in range(5)]
+    assert order == [0, 1, 2, 0, 1]
+    s = a.flight_slots[2]
+    s.timeline_value = 7
+    assert a.flight_slots[2].timeline_value == 7
+    p = ram_pool(1 << 16)
+    b = p.acquire(5000)
+    assert len(b) == 5000 and b.capacity == 8192
+    mv = memoryview(b)
+    mv[:4] = b"abcd"
+    addr = b.address
+    del mv
+    assert p.release(b) and p.pool_bytes == 8192
+    c = p.acquire(6000)                                           # same class: recycled storage
+    assert c.address == addr and p.recycled_count == 1 and p.pool_bytes == 0
+    big = p.acquire(1 << 17)
+    assert not p.release(big)                                     # above the cap: freed
+
+
+def test_cold_boot_plan_phases():
+    """Cold boot order (reference src/strix/cold_boot.rs:76-170)."""
+    from air_rs.stream.strix import TensorClass, plan_cold_boot
+    ts = [("output.weight", TensorClass.A, None, 100), ("blk.3.w", TensorClass.B, 3, 10),
+          ("blk.0.w", TensorClass.B, 0, 10), ("blk.1.w", TensorClass.B, 1, 10),
+          ("draft.w", TensorClass.C, None, 7), ("expert.9", TensorClass.D, 5, 3)]
+    plan = plan_cold_boot(ts, prefetch_window=2)
+    assert [(s.name, s.phase) for s in plan.steps] == [
+        ("output.weight", 1), ("blk.0.w", 2), ("blk.1.w", 2), ("blk.3.w", 3), ("draft.w", 4)]
+    assert plan.skipped == 1 and plan.critical_path_bytes == 120 and plan.total_transfer_bytes == 130
+    assert abs(plan.estimate_ttft_seconds(120 / 2**20) - 1.0) < 1e-9
