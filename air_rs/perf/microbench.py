@@ -5,6 +5,9 @@
 and as a replayed graph, device time per step from CUDA events plus host time per step, and
 the number of kernels in the step.
 
+``--op prefill`` lists the kernels of one ``--batch``-token prefill (default 512) the same
+way, then its CUDA-event time (the device part of TTFT).
+
 ``--op step`` lists the kernels of one graph-replayed decode step (CUPTI through
 ``torch.profiler``: count and device time per kernel over 10 steps) at ``--batch`` rows of
 ``--ctx`` context tokens, then the CUDA-event time per step.
@@ -198,9 +201,42 @@ def profile_step(preset: str, B: int, ctx: int, dev) -> str:
     return table + f"\n{preset} decode B={B} ctx={ctx}: {a.elapsed_time(b) / 20:.3f} ms/step (CUDA events, graph replay)"
 
 
+def profile_prefill(preset: str, T: int, dev) -> str:
+    """Kernels of one T-token prefill (prompt -> first token): CUPTI through torch.profiler,
+    count and device time per kernel over 3 prefills, then the CUDA-event time of one."""
+    from torch.profiler import ProfilerActivity, profile
+    from ..runtime.builder import random_engine
+    from ..runtime.engine import SamplingParams
+    eng = random_engine(preset, device=dev, max_batch=8, max_model_len=T + 64, num_blocks=8 * ((T + 64) // 16 + 2))
+
+    def one(i):
+        eng.add_request([(7 * i + j) % 200 + 3 for j in range(T)],
+                        SamplingParams(max_tokens=1, temperature=0.0, ignore_eos=True))
+        eng._prefill(eng._admit())
+
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for i in range(3):
+            one(10 + i)
+        torch.cuda.synchronize()
+    table = prof.key_averages().table(sort_by="cuda_time_total", row_limit=25, max_name_column_width=80)
+    ts = []
+    for i in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        one(20 + i)
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ts.sort()
+    return table + f"\n{preset} prefill T={T}: {ts[len(ts) // 2]:.3f} ms median of 5 (CUDA events)"
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--op", default="all", choices=["all", "gemv", "gemm", "attn", "norm", "graph", "step"])
+    ap.add_argument("--op", default="all", choices=["all", "gemv", "gemm", "attn", "norm", "graph", "step", "prefill"])
     ap.add_argument("--preset", default="llama3-8b")
     ap.add_argument("--name", default=None, choices=list(SHAPES))
     ap.add_argument("--batch", type=int, default=None)
@@ -240,6 +276,8 @@ def main(argv=None):
 
     if a.op == "step":
         print(profile_step(a.preset, a.batch or 1, a.ctx, dev), flush=True)
+    if a.op == "prefill":
+        print(profile_prefill(a.preset, a.batch or 512, dev), flush=True)
     if a.op == "graph":
         for B in ([a.batch] if a.batch else [1, 64]):
             r = bench_graph(a.preset, B, a.iters, dev)

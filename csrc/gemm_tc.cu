@@ -58,15 +58,19 @@ struct Cfg {
   static constexpr int kAbufs = AT ? (kTmemCols - kATmemCol) / (32 * kUA) : NA;
   static_assert(!AT || kAbufs >= 2, "TMEM: not enough room for two A buffers");
   static_assert(kAbufs <= 4, "A buffer barriers");
-  static_assert(kStages >= 2, "not enough shared memory for two stages");
+  static_assert(AT || kStages >= 2, "not enough shared memory for two stages");
   // AT: decoupled rings — raw weight tiles (streamed from HBM, as many in flight as fit) and
   // activation tiles (L2-resident, a short ring), each with its own producer warp
-  static constexpr int kXStage = kChunks * kBChunk;
-  static constexpr int kXStages = (NT >= 64 || CPS == 2) ? 2 : 3;
+  // activation ring in 64-wide K chunks (NT rows x 128 B each): the MMA frees a chunk as
+  // soon as its four K16 steps are issued, so a few chunks keep the tensor pipe fed and the
+  // rest of shared memory holds raw weight tiles in flight
+  static constexpr int kXStage = kBChunk;
+  static constexpr int kXStages = NT >= 256 ? 3 : (NT >= 128 ? 4 : (CPS == 2 ? 4 : 8));
   static constexpr int kBudgetAT = CPS == 2 ? 112 * 1024 - 2048 : kBudget;
   static constexpr int kWStagesRaw = (kBudgetAT - kXStages * kXStage) / kRawTile;
   static constexpr int kWStages = kWStagesRaw > 12 ? 12 : kWStagesRaw;
   static constexpr int kSmemAT = 1024 + kWStages * kRawTile + kXStages * kXStage + 1024;
+  static_assert(!AT || kWStages >= 2, "not enough shared memory for two raw weight stages");
   static constexpr int kFirstDq = AT ? 3 : 2;       // first dequant/epilogue warp
   static constexpr int kSmemLaunch = AT ? kSmemAT : kSmem;
 };
@@ -74,8 +78,8 @@ struct Cfg {
 struct Bars {
   uint64_t full[12];
   uint64_t empty[12];
-  uint64_t xfull[4];
-  uint64_t xempty[4];
+  uint64_t xfull[8];
+  uint64_t xempty[8];
   uint64_t afull[4];
   uint64_t aempty[4];
   uint64_t done;
@@ -177,14 +181,17 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
     // ------------------------------------------------------------ producers (AT)
     // warp 0: raw weight tiles into the deep ring; warp 2: activation tiles into the short ring
     if (lane == 0) {
+      // items: one raw weight tile per K stage (warp 0), one 64-wide activation chunk per
+      // quarter stage (warp 2)
       const bool wprod = warp == 0;
       const int S = wprod ? C::kWStages : C::kXStages;
       uint64_t* fullb = wprod ? bars->full : bars->xfull;
       uint64_t* emptyb = wprod ? bars->empty : bars->xempty;
       uint8_t* ring = wprod ? stages : stages + C::kWStages * kRawTile;
       const uint32_t bytes = wprod ? kRawTile : C::kXStage;
+      const int items = wprod ? nk : 4 * nk;
       int issued = 0;
-      for (int i = 0; i < nk; ++i) {
+      for (int i = 0; i < items; ++i) {
         const int s = i % S;
         if (i >= S && !mbar_wait(&emptyb[s], ((i / S) - 1) & 1, a.err)) {
           set_error(a.err, kErrTimeout);
@@ -195,17 +202,14 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         uint8_t* st = ring + s * bytes;
         if (dbg && wprod && i < 32) dbg[i] = clock64();
         mbar_expect_tx(&fullb[s], bytes);
-        const int kb = kb0 + i;
         if (wprod) {
           // the tile as a.wsplit back-to-back bulk copies (more requests in flight per CTA)
-          const uint8_t* src = a.wq + ((size_t)blockIdx.x * ksteps + kb) * kRawTile;
+          const uint8_t* src = a.wq + ((size_t)blockIdx.x * ksteps + kb0 + i) * kRawTile;
           const int np = a.wsplit > 0 ? a.wsplit : 1;
           const uint32_t piece = kRawTile / np;
           for (int p = 0; p < np; ++p) bulk_load(st + p * piece, src + p * piece, piece, &fullb[s]);
         } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            tma_load_2d(st + c * C::kBChunk, &tm_x, &fullb[s], kb * 256 + 64 * c, n0);
+          tma_load_2d(st, &tm_x, &fullb[s], (kb0 + i / 4) * 256 + 64 * (i % 4), n0);
         }
         issued = i + 1;
       }
@@ -253,9 +257,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
         if constexpr (AT) {
-          const int xs = i % C::kXStages;
-          if (!mbar_wait(&bars->xfull[xs], (i / C::kXStages) & 1, a.err)) { ok = false; break; }
-          uint8_t* xst = stages + C::kWStages * kRawTile + xs * C::kXStage;
+          uint8_t* xring = stages + C::kWStages * kRawTile;
           for (int u = 0; u < C::kUPS && ok; ++u) {
             const int g = i * C::kUPS + u;
             const int ab = g % C::kAbufs;
@@ -266,7 +268,11 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
 #pragma unroll
             for (int cu = 0; cu < C::kUA; ++cu) {
               const int c = u * C::kUA + cu;
-              const uint64_t bd = sw128_desc(xst + c * C::kBChunk);
+              const int gx = 4 * i + c;                 // activation chunk
+              const int xs = gx % C::kXStages;
+              if (!mbar_wait(&bars->xfull[xs], (gx / C::kXStages) & 1, a.err)) { ok = false; break; }
+              tc_fence_after();
+              const uint64_t bd = sw128_desc(xring + xs * C::kXStage);
 #pragma unroll
               for (int k = 0; k < 4; ++k) {  // K16 steps: 8 TMEM columns of A, +32 B of B
                 const int j = (4 * c + k) % NACC;       // interleaved accumulators
@@ -274,11 +280,12 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
                 if (dmode != 2)
                   mma_bf16_ts(tmem + C::kAccW * j, ta + 32 * cu + 8 * k, bd + 2 * k, idesc, acc);
               }
+              mma_commit(&bars->xempty[xs]);            // chunk read once these MMAs retire
             }
+            if (!ok) break;
             mma_commit(&bars->aempty[ab]);
           }
           if (!ok) break;
-          mma_commit(&bars->xempty[xs]);
           continue;
         }
         const int s = i % C::kStages;
@@ -601,7 +608,10 @@ template <int NT, int FMT>
 const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
                      dim3 grid, cudaStream_t st) {
   constexpr int NA = (FMT == kFmtQ4K && NT == 128) ? 2 : 4;
-  if constexpr (FMT == kFmtQ4K) {
+  if constexpr (FMT == kFmtQ4K && NT >= 256) {
+    // 256-token tiles: A in TMEM only (one 256-column accumulator + two A stage buffers)
+    return launch_na<NT, FMT, NA, 8, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
+  } else if constexpr (FMT == kFmtQ4K) {
     const int p = a_path();
     if (p == 0) {
       constexpr int NACC = NT <= 64 ? 4 : 2;
@@ -616,8 +626,10 @@ const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, cons
       return launch_na<NT, FMT, NA, 8, true, NACC>(a, w, w_row_bytes, x, ldx, grid, st);
     }
     if (p == 2) return launch_na<NT, FMT, NA, 16>(a, w, w_row_bytes, x, ldx, grid, st);
+    return launch_na<NT, FMT, NA, 8>(a, w, w_row_bytes, x, ldx, grid, st);
+  } else {
+    return launch_na<NT, FMT, NA, 8>(a, w, w_row_bytes, x, ldx, grid, st);
   }
-  return launch_na<NT, FMT, NA, 8>(a, w, w_row_bytes, x, ldx, grid, st);
 }
 
 }  // namespace
@@ -626,7 +638,9 @@ int gemm_q_token_tile(int T) {
   if (T <= 16) return 16;
   if (T <= 32) return 32;
   if (T <= 64) return 64;
-  return 128;
+  if (T <= 128) return 128;
+  const char* e = getenv("AIR_GEMM_NT256");
+  return (e && e[0] == '0') ? 128 : 256;
 }
 
 int gemm_q_splits(int N, int K, int T, int fmt) {
@@ -641,11 +655,28 @@ int gemm_q_splits(int N, int K, int T, int fmt) {
   const bool cps2 = fmt == kFmtQ4K && nt <= 64 && a_path() == 0 && !(c2 && atoi(c2) == 1);
   const int wave = w ? atoi(w) : 148;   // 2 x 148 for the two-CTA variant measured slower on split shapes
   (void)cps2;
-  int s = wave / tiles;
-  s = s < 1 ? 1 : s;
   const char* mk = getenv("AIR_GEMM_MINK");
   const int mink = mk ? atoi(mk) : 2;                     // K-steps per split at least
   const int max_s = ksteps / mink > 0 ? ksteps / mink : 1;
+  if (nt >= 128) {
+    // one CTA per SM: time ~ waves x (tile math / s + partial traffic), in units of one
+    // tile's math. A partial last wave costs a whole wave. Writing and re-reading a tile's
+    // fp32 partial (2 x 128 x nt x 4 B at an SM's share of HBM, ~43 GB/s) against its math
+    // (2 x 128 x nt x K FLOP at an SM's share of the tensor peak, ~9.5 TFLOP/s) is ~884 / K.
+    int best = 1;
+    double best_cost = 1e30;
+    for (int s = 1; s <= max_s && s <= 16; ++s) {
+      const double waves = (double)((s * tiles + wave - 1) / wave);
+      const double cost = waves * (1.0 / s + (s > 1 ? 884.0 / K : 0.0));
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = s;
+      }
+    }
+    return best;
+  }
+  int s = wave / tiles;
+  s = s < 1 ? 1 : s;
   return s > max_s ? max_s : s;
 }
 
@@ -688,14 +719,16 @@ const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const voi
       case 16: return launch_t<16, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
       case 32: return launch_t<32, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
       case 64: return launch_t<64, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
-      default: return launch_t<128, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 128: return launch_t<128, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
+      default: return launch_t<256, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
     }
   }
   switch (nt) {
     case 16: return launch_t<16, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
     case 32: return launch_t<32, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
     case 64: return launch_t<64, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
-    default: return launch_t<128, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
+    case 128: return launch_t<128, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
+    default: return launch_t<256, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
   }
 }
 

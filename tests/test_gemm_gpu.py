@@ -21,7 +21,9 @@ def _w(N, K, qt, seed):
 @pytest.mark.parametrize("qt", [GGMLType.Q4_K, GGMLType.BF16])
 @pytest.mark.parametrize("N,K,T,splits", [(128, 256, 1, 1), (384, 512, 5, 1), (256, 1024, 64, None),
                                           (256, 2048, 64, 4), (512, 1024, 200, None), (4096, 4096, 16, None),
-                                          (200, 512, 33, None), (1456, 256, 33, 1)])
+                                          (200, 512, 33, None), (1456, 256, 33, 1),
+                                          (1024, 2048, 512, None), (384, 1024, 300, 3),
+                                          (256, 512, 129, 1)])     # 256-token tiles
 def test_gemm_q_store(qt, N, K, T, splits):
     w, wd = _w(N, K, qt, 1)
     g = torch.Generator().manual_seed(2)
