@@ -25,8 +25,8 @@ def _common(p: argparse.ArgumentParser, serve: bool = False):
                    help="S.L.I.P.: keep layer weights in pinned host memory and stream them per forward")
     p.add_argument("--tp", type=int, default=1, help="Tensor-parallel GPUs (default: 1)")
     p.add_argument("--gds", action="store_true",
-                   help="Read weights with parallel direct reads into pinned buffers (no GPUDirect Storage "
-                        "driver on this platform)")
+                   help="Read weights with GPUDirect Storage (cuFile) straight into HBM; falls back to "
+                        "parallel reads into pinned buffers when cuFile is unavailable")
     p.add_argument("--enable-auto-tool-choice", action="store_true")
     p.add_argument("--tool-call-parser", default=None,
                    help="llama3_json | hermes | mistral | deepseekv3")
@@ -130,7 +130,7 @@ def _engine(args, max_batch=64):
                             prefix_cache=getattr(args, "enable_prefix_caching", False) or ec.prefix_cache,
                             kv_swap=ec.kv_swap, pressure_control=ec.pressure_control, secure_kv=ec.secure_kv,
                             admission=ec.admission,
-                            parallel_read=getattr(args, "gds", False))
+                            gds=getattr(args, "gds", False))
 
 
 def cmd_generate(args) -> int:

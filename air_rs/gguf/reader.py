@@ -116,6 +116,31 @@ class GGUFFile:
             raise OSError(f"{len(names) - len(out)} tensors of {self.path} were not read")
         return out
 
+    def read_gds(self, device, names=None) -> dict:
+        """Tensors read with GPUDirect Storage (cuFile) straight into device memory, one
+        uint8 ``[rows, row_bytes]`` CUDA tensor each, globals first then layer by layer
+        (reference ``src/strix/gpu_direct.rs:540-640``). Raises ``OSError`` when cuFile is
+        not usable here (see ``gds_available``); callers fall back to ``read_parallel``."""
+        from .. import ops
+        ext = ops.require_ext()
+        if not ext.gds_available():
+            raise OSError(f"GPUDirect Storage unavailable: {ext.gds_error()}")
+        names = list(self.tensors) if names is None else list(names)
+        order = lambda n: (1, int(n.split(".")[1])) if n.startswith("blk.") else (0, 0)
+        rd = ext.GdsReader(self.path)
+        out = {}
+        try:
+            for n in sorted(names, key=order):
+                t = self.tensors[n]
+                buf = torch.empty(t.nbytes, dtype=torch.uint8, device=device)
+                got = rd.read(buf, t.offset, t.nbytes, 0)
+                if got != t.nbytes:
+                    raise OSError(f"short cuFile read of {n}: {got} of {t.nbytes} bytes")
+                out[n] = buf.view(t.rows, t.nbytes // t.rows)
+        finally:
+            rd.close()
+        return out
+
     def dequantize(self, name: str) -> torch.Tensor:
         from .quants import dequantize
         t = self.tensors[name]

@@ -89,7 +89,7 @@ def random_engine(preset: str | ModelConfig = "tiny", qtype: GGMLType = GGMLType
 
 def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None, tp=None,
                      num_blocks=None, seed=0, resident: bool | str = True, expert_slots: int | None = None,
-                     parallel_read: bool = False, **kw) -> Engine:
+                     parallel_read: bool = False, gds: bool = False, **kw) -> Engine:
     """``resident="auto"``: keep everything in HBM when it fits under the VRAM cap, else
     stream layers or serve MoE experts from host memory (``runtime.residency.plan_model``)."""
     g = read_gguf(path)
@@ -111,8 +111,16 @@ def engine_from_gguf(path: str, *, device=None, max_batch=64, max_model_len=None
         resident, stream_slots = plan.resident, plan.stream_slots
         expert_slots = expert_slots or plan.expert_slots
         resident_layers = plan.resident_layers
-    if parallel_read:
+    bufs = None
+    if gds and resident is True:
+        # GPUDirect Storage: file -> HBM without a host copy; threaded pread when unavailable
+        try:
+            bufs = g.read_gds(device)
+        except OSError:
+            bufs = None
+    if bufs is None and (parallel_read or gds):
         bufs = g.read_parallel()
+    if bufs is not None:
         recs = ((n, bufs[n], t.qtype, t.torch_shape) for n, t in g.tensors.items())
     else:
         recs = ((n, g.raw(n), t.qtype, t.torch_shape) for n, t in g.tensors.items())

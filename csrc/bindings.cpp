@@ -16,6 +16,7 @@
 
 void register_gemm_tc(pybind11::module_& m);
 void register_comm(pybind11::module_& m);
+void register_gds(pybind11::module_& m);
 void register_kv_push(pybind11::module_& m);
 void register_ssm(pybind11::module_& m);
 air::PeerPush peer_push_from_meta(const at::Tensor& meta);
@@ -323,4 +324,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_kv_push(m);
   register_ssm(m);
   register_comm(m);
+  register_gds(m);
 }

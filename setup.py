@@ -22,6 +22,7 @@ ext = CUDAExtension(
     name="air_rs._C",
     sources=sources(),
     include_dirs=[os.path.join(HERE, "csrc")],
+    libraries=["dl"],        # libcufile is dlopen'ed at run time (GPUDirect Storage reads)
     extra_compile_args={
         "cxx": ["-O3", "-std=c++17"],
         "nvcc": ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
