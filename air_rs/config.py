@@ -34,7 +34,7 @@ class EngineConfig:
     max_batch: int = 64                 # concurrent decode rows (CUDA-graph buckets up to here)
     max_num_seqs: int = 256
     max_model_len: int | None = None
-    prefill_chunk: int = 512
+    prefill_chunk: int = 2048
     max_prefill_tokens: int = 8192
     cuda_graph_batch_sizes: tuple[int, ...] = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
     resident: bool = True               # False: stream layers from pinned host memory

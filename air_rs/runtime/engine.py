@@ -4,8 +4,9 @@ The reference serves one request at a time with batch 1 (``src/scheduler.rs:36-1
 ``src/inference_step.rs:19-184``) and keeps its Orca/Sarathi scheduler as unused
 bookkeeping (``src/continuous_batch.rs``). Here the scheduler drives real batched steps:
 waiting requests are admitted while KV blocks and batch slots allow, prompts are
-prefilled in token-budgeted chunks (``prefill_chunk`` = 512 like the reference's
-``PREFILL_CHUNK_SIZE``), and every step decodes all running sequences in one CUDA-graph
+prefilled in token-budgeted chunks (``prefill_chunk``, 2048 tokens by default: a prompt up to
+that length is one GEMM pass over the weights; the reference's ``PREFILL_CHUNK_SIZE`` is 512),
+and every step decodes all running sequences in one CUDA-graph
 replay of the bucket that fits them. Output processing is pipelined: step k+1 is
 launched before step k's tokens are read back, so the host never idles the GPU.
 
@@ -79,7 +80,7 @@ class Engine:
     """Batched generation over a ``ModelRunner`` (GPU) or the CPU oracle."""
 
     def __init__(self, cfg: ModelConfig, runner=None, tokenizer=None, *, oracle=None,
-                 max_batch: int = 64, prefill_chunk: int = 512, max_prefill_tokens: int = 8192,
+                 max_batch: int = 64, prefill_chunk: int = 2048, max_prefill_tokens: int = 8192,
                  add_bos: bool = True, eos_id: int | None = None, prefix_cache: bool = False,
                  prefix_cache_blocks: int | None = None, kv_swap: bool = True,
                  cuda_graph_batch_sizes: tuple[int, ...] = BUCKETS, pressure_control: bool = False,

@@ -294,6 +294,11 @@ template <int D, int G>
 void launch_dg(const AttnArgs& a, cudaStream_t st) {
   dim3 grid(a.n_kv, a.n_rows, a.n_splits);
   static const bool simt = getenv("AIR_ATTN_SIMT") != nullptr;
+  static const bool per_row = getenv("AIR_PREFILL_ATTN_PER_ROW") != nullptr;
+  // prefill rows (a block-table row per query row) of 16 or more: the query-tiled kernel
+  if (D == 128 && !simt && !per_row && a.rows.row_seq != nullptr && a.n_rows >= 16 &&
+      launch_prefill_attention(a, st))
+    return;
   if (!(D == 128 && !simt && launch_paged_attention_mma(a, st)))
   paged_attn_kernel<D, G><<<grid, kWarps * 32, 0, st>>>(
       a.q, (const __nv_bfloat16*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_heads, a.n_kv,

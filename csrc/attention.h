@@ -35,5 +35,8 @@ struct AttnArgs {
 bool launch_paged_attention(const AttnArgs& a, cudaStream_t st);
 // tensor-core main pass (head_dim 128, group <= 8); false if the shape is not covered
 bool launch_paged_attention_mma(const AttnArgs& a, cudaStream_t st);
+// query-tiled prefill pass (head_dim 128, no tree rows, one split, no Q8A output): 16 query
+// rows of one KV head per CTA share every K/V tile; false if the shape is not covered
+bool launch_prefill_attention(const AttnArgs& a, cudaStream_t st);
 
 }  // namespace air

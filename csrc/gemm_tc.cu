@@ -61,11 +61,12 @@ struct Cfg {
   static_assert(AT || kStages >= 2, "not enough shared memory for two stages");
   // AT: decoupled rings — raw weight tiles (streamed from HBM, as many in flight as fit) and
   // activation tiles (L2-resident, a short ring), each with its own producer warp
-  // activation ring in 64-wide K chunks (NT rows x 128 B each): the MMA frees a chunk as
-  // soon as its four K16 steps are issued, so a few chunks keep the tensor pipe fed and the
-  // rest of shared memory holds raw weight tiles in flight
-  static constexpr int kXStage = kBChunk;
-  static constexpr int kXStages = NT >= 256 ? 3 : (NT >= 128 ? 4 : (CPS == 2 ? 4 : 8));
+  // activation ring: one item per K stage (four 64-wide chunks) for token tiles up to 128;
+  // 256-token tiles stage single chunks (a whole stage would be 128 KB), and the MMA frees a
+  // chunk as soon as its four K16 steps are issued
+  static constexpr int kXC = NT >= 256 ? 1 : 4;                 // 64-wide chunks per X item
+  static constexpr int kXStage = kXC * kBChunk;
+  static constexpr int kXStages = NT >= 256 ? 3 : ((NT >= 64 || CPS == 2) ? 2 : 3);
   static constexpr int kBudgetAT = CPS == 2 ? 112 * 1024 - 2048 : kBudget;
   static constexpr int kWStagesRaw = (kBudgetAT - kXStages * kXStage) / kRawTile;
   static constexpr int kWStages = kWStagesRaw > 12 ? 12 : kWStagesRaw;
@@ -189,7 +190,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       uint64_t* emptyb = wprod ? bars->empty : bars->xempty;
       uint8_t* ring = wprod ? stages : stages + C::kWStages * kRawTile;
       const uint32_t bytes = wprod ? kRawTile : C::kXStage;
-      const int items = wprod ? nk : 4 * nk;
+      const int items = wprod ? nk : nk * (4 / C::kXC);
       int issued = 0;
       for (int i = 0; i < items; ++i) {
         const int s = i % S;
@@ -209,7 +210,11 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
           const uint32_t piece = kRawTile / np;
           for (int p = 0; p < np; ++p) bulk_load(st + p * piece, src + p * piece, piece, &fullb[s]);
         } else {
-          tma_load_2d(st, &tm_x, &fullb[s], (kb0 + i / 4) * 256 + 64 * (i % 4), n0);
+#pragma unroll
+          for (int c = 0; c < C::kXC; ++c) {
+            const int ch = i * C::kXC + c;              // chunk index along K
+            tma_load_2d(st + c * C::kBChunk, &tm_x, &fullb[s], (kb0 + ch / 4) * 256 + 64 * (ch % 4), n0);
+          }
         }
         issued = i + 1;
       }
@@ -268,11 +273,14 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
 #pragma unroll
             for (int cu = 0; cu < C::kUA; ++cu) {
               const int c = u * C::kUA + cu;
-              const int gx = 4 * i + c;                 // activation chunk
+              const int gc = 4 * i + c;                 // activation chunk
+              const int gx = gc / C::kXC;               // its X ring item
               const int xs = gx % C::kXStages;
-              if (!mbar_wait(&bars->xfull[xs], (gx / C::kXStages) & 1, a.err)) { ok = false; break; }
-              tc_fence_after();
-              const uint64_t bd = sw128_desc(xring + xs * C::kXStage);
+              if (gc % C::kXC == 0) {
+                if (!mbar_wait(&bars->xfull[xs], (gx / C::kXStages) & 1, a.err)) { ok = false; break; }
+                tc_fence_after();
+              }
+              const uint64_t bd = sw128_desc(xring + xs * C::kXStage + (gc % C::kXC) * C::kBChunk);
 #pragma unroll
               for (int k = 0; k < 4; ++k) {  // K16 steps: 8 TMEM columns of A, +32 B of B
                 const int j = (4 * c + k) % NACC;       // interleaved accumulators
@@ -280,7 +288,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
                 if (dmode != 2)
                   mma_bf16_ts(tmem + C::kAccW * j, ta + 32 * cu + 8 * k, bd + 2 * k, idesc, acc);
               }
-              mma_commit(&bars->xempty[xs]);            // chunk read once these MMAs retire
+              if (gc % C::kXC == C::kXC - 1) mma_commit(&bars->xempty[xs]);   // item read once these retire
             }
             if (!ok) break;
             mma_commit(&bars->aempty[ab]);

@@ -247,6 +247,41 @@ def test_paged_prefill_causal_and_tree():
     torch.testing.assert_close(out2.cpu(), ref2, rtol=2e-3, atol=2e-3)
 
 
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
+@pytest.mark.parametrize("window", [0, 50])
+def test_query_tiled_prefill_attention(G, window):
+    """The query-tiled prefill kernel (16 rows per CTA, shared K/V tiles) against dense fp32
+    attention: three sequences whose chunks straddle 16-row tiles (mixed-sequence tiles),
+    chunked prefill (queries start mid-sequence), GQA groups 1-8, sliding window."""
+    nkv, d, bs = 2, 128, 16
+    nh = nkv * G
+    lens = [75, 130, 33]          # total keys per sequence
+    qlen = [40, 130, 21]          # the last qlen tokens of each are this step's queries
+    kv, bt, dense = _paged_setup(lens, nkv, d, bs, seed=7)
+    rows_seq, ctx = [], []
+    for s_, (L, n) in enumerate(zip(lens, qlen)):
+        rows_seq += [s_] * n
+        ctx += list(range(L - n + 1, L + 1))
+    T = len(rows_seq)
+    q = torch.randn(T, nh, d, generator=torch.Generator().manual_seed(11))
+    out = torch.zeros(T, nh, d, device=DEV)
+    ops.paged_attention(q.to(DEV), kv.to(DEV), bt.to(DEV), torch.tensor(ctx, dtype=torch.int32, device=DEV), out,
+                        n_rows=T, n_heads=nh, n_kv=nkv, head_dim=d, block_size=bs,
+                        row_seq=torch.tensor(rows_seq, dtype=torch.int32, device=DEV), window=window)
+    torch.cuda.synchronize()
+    r = 0
+    for s_, (L, n) in enumerate(zip(lens, qlen)):
+        k, v = dense[s_]
+        mask = torch.zeros(n, L, dtype=torch.bool)
+        for i in range(n):
+            c = L - n + 1 + i
+            lo = max(0, c - window) if window else 0
+            mask[i, lo:c] = True
+        ref = attention_reference(q[r:r + n], k, v, causal=False, mask=mask)
+        torch.testing.assert_close(out[r:r + n].cpu(), ref, rtol=1e-2, atol=8e-3)
+        r += n
+
+
 def test_sampler_greedy_penalty_and_topk():
     B, V = 3, 50000
     g = torch.Generator().manual_seed(0)

@@ -13,7 +13,7 @@ from air_rs.utils import trace
 # ---------------------------------------------------------------- config
 def test_engine_config_defaults_and_env():
     c = EngineConfig()
-    assert c.block_size == 16 and c.max_num_seqs == 256 and c.prefill_chunk == 512
+    assert c.block_size == 16 and c.max_num_seqs == 256 and c.prefill_chunk == 2048
     c = EngineConfig.from_env({"AIR_MAX_BATCH": "128", "AIR_PREFIX_CACHE": "yes", "AIR_VRAM_FRACTION": "0.5",
                                "AIR_NUM_BLOCKS": "none", "AIR_CUDA_GRAPH_BATCH_SIZES": "1,2,8",
                                "AIR_PRESET": "tiny", "AIR_EXPERT_SLOTS": "4"}, tp=2)
