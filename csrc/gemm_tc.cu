@@ -33,6 +33,10 @@ using namespace sm100;
 
 constexpr int kRawRowBytes = 144;           // one Q4_K super-block of one row
 constexpr int kRawTile = 128 * kRawRowBytes; // 18432 B (multiple of 1024)
+// Q8_0 stage of 128 rows x 256 weights: the int8 codes as two 128-byte-wide SW128 TMA boxes
+// (16 KB each) plus the eight f16 block scales per row (one 16-byte box row): 34 KB
+constexpr int kQ8Half = 128 * 128;
+constexpr int kQ8Tile = 2 * kQ8Half + 128 * 16;
 constexpr int kATile = 128 * 128;            // 128 rows x 64 bf16
 
 template <int NT, int FMT, int NA, bool AT, int NACC = 1, int CPS = 1>
@@ -64,13 +68,15 @@ struct Cfg {
   // activation ring: one item per K stage (four 64-wide chunks) for token tiles up to 128;
   // 256-token tiles stage single chunks (a whole stage would be 128 KB), and the MMA frees a
   // chunk as soon as its four K16 steps are issued
-  static constexpr int kXC = NT >= 256 ? 1 : 4;                 // 64-wide chunks per X item
+  // (Q8_0 weight tiles are twice the Q4_K size: the two-CTA decode variant stages chunks too)
+  static constexpr int kXC = (NT >= 256 || (FMT == kFmtQ8_0 && CPS == 2)) ? 1 : 4;   // chunks per X item
   static constexpr int kXStage = kXC * kBChunk;
-  static constexpr int kXStages = NT >= 256 ? 3 : ((NT >= 64 || CPS == 2) ? 2 : 3);
+  static constexpr int kXStages = kXC == 1 ? (NT >= 256 ? 3 : 4) : ((NT >= 64 || CPS == 2) ? 2 : 3);
+  static constexpr int kWTile = FMT == kFmtQ8_0 ? kQ8Tile : kRawTile;   // one raw weight stage
   static constexpr int kBudgetAT = CPS == 2 ? 112 * 1024 - 2048 : kBudget;
-  static constexpr int kWStagesRaw = (kBudgetAT - kXStages * kXStage) / kRawTile;
+  static constexpr int kWStagesRaw = (kBudgetAT - kXStages * kXStage) / kWTile;
   static constexpr int kWStages = kWStagesRaw > 12 ? 12 : kWStagesRaw;
-  static constexpr int kSmemAT = 1024 + kWStages * kRawTile + kXStages * kXStage + 1024;
+  static constexpr int kSmemAT = 1024 + kWStages * kWTile + kXStages * kXStage + 1024;
   static_assert(!AT || kWStages >= 2, "not enough shared memory for two raw weight stages");
   static constexpr int kFirstDq = AT ? 3 : 2;       // first dequant/epilogue warp
   static constexpr int kSmemLaunch = AT ? kSmemAT : kSmem;
@@ -118,9 +124,9 @@ __device__ __forceinline__ uint32_t q4_pair(uint32_t t, __nv_bfloat162 s, __nv_b
 template <int NT, int FMT, int NA, int DQ, bool AT, int NACC, int CPS>
 __global__ void __launch_bounds__((AT ? 96 : 64) + 32 * DQ, CPS)
 gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-              GemmArgs a) {
+              const __grid_constant__ CUtensorMap tm_s, GemmArgs a) {
   using C = Cfg<NT, FMT, NA, AT, NACC, CPS>;
-  static_assert(!AT || FMT == kFmtQ4K, "A-in-TMEM path: Q4_K only");
+  static_assert(!AT || FMT == kFmtQ4K || FMT == kFmtQ8_0, "A-in-TMEM path: Q4_K and Q8_0");
   // routed-expert GEMMs: token tiles beyond the device row count do nothing (uniform per CTA,
   // before any barrier, TMEM allocation or copy)
   if (a.row_count != nullptr && (int)blockIdx.y * NT >= __ldg(a.row_count)) return;
@@ -129,13 +135,13 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   uint8_t* stages = smem;
   uint8_t* abuf = stages + C::kStages * C::kStageBytes;
   // AT lays out [weight ring][activation ring] instead; the barriers follow whichever layout
-  Bars* bars = reinterpret_cast<Bars*>(AT ? stages + C::kWStages * kRawTile + C::kXStages * C::kXStage
+  Bars* bars = reinterpret_cast<Bars*>(AT ? stages + C::kWStages * C::kWTile + C::kXStages * C::kXStage
                                           : abuf + C::kABuf);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * 128, n0 = blockIdx.y * NT;
   const int split = blockIdx.z, splits = gridDim.z;
-  const int ksteps = FMT == kFmtQ4K ? a.K / 256 : a.K / 64;
+  const int ksteps = (FMT == kFmtQ4K || FMT == kFmtQ8_0) ? a.K / 256 : a.K / 64;
   const int kper = (ksteps + splits - 1) / splits;
   const int kb0 = split * kper;
   const int nk = max(0, min(ksteps, kb0 + kper) - kb0);
@@ -166,6 +172,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   }
   if (warp == 0 && lane == 0) {
     if (FMT != kFmtQ4K) prefetch_tmap(&tm_w);
+    if (FMT == kFmtQ8_0) prefetch_tmap(&tm_s);
     prefetch_tmap(&tm_x);
   }
   if (warp == 1) tmem_alloc(&bars->tmem, C::kTmemCols);
@@ -188,8 +195,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       const int S = wprod ? C::kWStages : C::kXStages;
       uint64_t* fullb = wprod ? bars->full : bars->xfull;
       uint64_t* emptyb = wprod ? bars->empty : bars->xempty;
-      uint8_t* ring = wprod ? stages : stages + C::kWStages * kRawTile;
-      const uint32_t bytes = wprod ? kRawTile : C::kXStage;
+      uint8_t* ring = wprod ? stages : stages + C::kWStages * C::kWTile;
+      const uint32_t bytes = wprod ? C::kWTile : C::kXStage;
       const int items = wprod ? nk : nk * (4 / C::kXC);
       int issued = 0;
       for (int i = 0; i < items; ++i) {
@@ -203,7 +210,13 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         uint8_t* st = ring + s * bytes;
         if (dbg && wprod && i < 32) dbg[i] = clock64();
         mbar_expect_tx(&fullb[s], bytes);
-        if (wprod) {
+        if (wprod && FMT == kFmtQ8_0) {
+          // codes [rows m0.., K kb*256..] as two SW128 boxes, then the rows' eight block scales
+          const int kb = kb0 + i;
+          tma_load_2d(st, &tm_w, &fullb[s], kb * 256, m0);
+          tma_load_2d(st + kQ8Half, &tm_w, &fullb[s], kb * 256 + 128, m0);
+          tma_load_2d(st + 2 * kQ8Half, &tm_s, &fullb[s], kb * 8, m0);
+        } else if (wprod) {
           // the tile as a.wsplit back-to-back bulk copies (more requests in flight per CTA)
           const uint8_t* src = a.wq + ((size_t)blockIdx.x * ksteps + kb0 + i) * kRawTile;
           const int np = a.wsplit > 0 ? a.wsplit : 1;
@@ -262,7 +275,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
         if constexpr (AT) {
-          uint8_t* xring = stages + C::kWStages * kRawTile;
+          uint8_t* xring = stages + C::kWStages * C::kWTile;
           for (int u = 0; u < C::kUPS && ok; ++u) {
             const int g = i * C::kUPS + u;
             const int ab = g % C::kAbufs;
@@ -355,10 +368,14 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         const int s = i % C::kWStages;
         if (!mbar_wait(&bars->full[s], (i / C::kWStages) & 1, a.err)) { ok = false; break; }
         if (dbg && threadIdx.x == 32 * C::kFirstDq && i < 64) dbg[96 + i] = clock64();
-        const uint8_t* rb = stages + s * kRawTile + r * kRawRowBytes;
-        const uint32_t hdr = *reinterpret_cast<const uint32_t*>(rb);
-        const float d = __half2float(__ushort_as_half((unsigned short)(hdr & 0xFFFF)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr >> 16)));
+        const uint8_t* rb = stages + s * C::kWTile + r * kRawRowBytes;
+        float d = 0.f, dmin = 0.f;
+        if constexpr (FMT == kFmtQ4K) {
+          const uint32_t hdr = *reinterpret_cast<const uint32_t*>(rb);
+          d = __half2float(__ushort_as_half((unsigned short)(hdr & 0xFFFF)));
+          dmin = __half2float(__ushort_as_half((unsigned short)(hdr >> 16)));
+        }
+        const uint8_t* q8 = stages + s * C::kWTile;     // Q8_0: [2 SW128 halves][scales]
         const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + C::kATmemCol + 16 * h;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -367,23 +384,43 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
           if (c % C::kUA == 0 && g >= C::kAbufs &&
               !mbar_wait(&bars->aempty[ab], ((g / C::kAbufs) - 1) & 1, a.err)) { ok = false; break; }
           const uint32_t ta = tlane + 32 * C::kUA * ab - 32 * (c / C::kUA) * C::kUA;
-          int sc, mn;
-          q4k_scale_min(rb + 4, 2 * c + h, sc, mn);
-          const __nv_bfloat162 sv = __float2bfloat162_rn(d * (float)sc);
-          const __nv_bfloat162 mv = __float2bfloat162_rn(-dmin * (float)mn);
-          const uint4 qa = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
-          const uint4 qb = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
-          uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
           uint32_t o[16];
+          if constexpr (FMT == kFmtQ8_0) {
+            // block 2c + h of the stage: 32 codes = two 16-byte chunks of row r's SW128 half
+            const uint8_t* row = q8 + (c >> 1) * kQ8Half + r * 128;
+            const int j0 = 4 * (c & 1) + 2 * h;
+            const uint4 qa = *reinterpret_cast<const uint4*>(row + ((j0 ^ (r & 7)) << 4));
+            const uint4 qb = *reinterpret_cast<const uint4*>(row + (((j0 + 1) ^ (r & 7)) << 4));
+            const float dq = __half2float(*reinterpret_cast<const __half*>(q8 + 2 * kQ8Half + r * 16 + (2 * c + h) * 2));
+            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t wk = h ? (w[k] >> 4) & 0x0F0F0F0Fu : w[k] & 0x0F0F0F0Fu;
+            for (int k = 0; k < 8; ++k) {
+              const int32_t v = (int32_t)w[k];
+              const float f0 = (float)(int8_t)(v & 0xFF), f1 = (float)(int8_t)((v >> 8) & 0xFF);
+              const float f2 = (float)(int8_t)((v >> 16) & 0xFF), f3 = (float)(int8_t)(v >> 24);
+              __nv_bfloat162 b0 = __floats2bfloat162_rn(f0 * dq, f1 * dq);
+              __nv_bfloat162 b1 = __floats2bfloat162_rn(f2 * dq, f3 * dq);
+              o[2 * k] = *reinterpret_cast<uint32_t*>(&b0);
+              o[2 * k + 1] = *reinterpret_cast<uint32_t*>(&b1);
+            }
+          } else {
+            int sc, mn;
+            q4k_scale_min(rb + 4, 2 * c + h, sc, mn);
+            const __nv_bfloat162 sv = __float2bfloat162_rn(d * (float)sc);
+            const __nv_bfloat162 mv = __float2bfloat162_rn(-dmin * (float)mn);
+            const uint4 qa = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
+            const uint4 qb = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
+            uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const uint32_t v = __byte_perm(wk, 0x43434343u, e ? 0x4342 : 0x4140);
-              __nv_bfloat162 bv = *reinterpret_cast<const __nv_bfloat162*>(&v);
-              bv = __hfma2(__hsub2(bv, c128), sv, mv);
-              o[2 * k + e] = *reinterpret_cast<uint32_t*>(&bv);
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t wk = h ? (w[k] >> 4) & 0x0F0F0F0Fu : w[k] & 0x0F0F0F0Fu;
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const uint32_t v = __byte_perm(wk, 0x43434343u, e ? 0x4342 : 0x4140);
+                __nv_bfloat162 bv = *reinterpret_cast<const __nv_bfloat162*>(&v);
+                bv = __hfma2(__hsub2(bv, c128), sv, mv);
+                o[2 * k + e] = *reinterpret_cast<uint32_t*>(&bv);
+              }
             }
           }
           if (dmode != 1) tmem_st16(ta + 32 * c, o);
@@ -579,13 +616,21 @@ template <int NT, int FMT, int NA, int DQ, bool AT = false, int NACC = 1, int CP
 const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
                       dim3 grid, cudaStream_t st) {
   using C = Cfg<NT, FMT, NA, AT, NACC, CPS>;
-  CUtensorMap tw, tx;
+  CUtensorMap tw, tx, ts;
   bool ok;
   GemmArgs b = a;
   b.wq = static_cast<const uint8_t*>(w);
+  memset(&ts, 0, sizeof(ts));
   if (FMT == kFmtQ4K) {
     memset(&tw, 0, sizeof(tw));  // unused: the tiled Q4_K operand is fetched with bulk copies
     ok = true;
+  } else if (FMT == kFmtQ8_0) {
+    // int8 codes [N, K] in 128-byte-wide SW128 boxes; f16 scales [N, K/32], 8 per row per stage
+    ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)w_row_bytes,
+                   128, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         a.wscales != nullptr &&
+         encode_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.wscales, (uint64_t)(a.K / 32), (uint64_t)a.N,
+                   (uint64_t)(a.K / 32) * 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
   } else
     ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, (uint64_t)a.K, (uint64_t)a.N,
                    (uint64_t)w_row_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -596,7 +641,7 @@ const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, con
   static unsigned long long attr_done = 0;
   if (!set_max_smem_per_device(gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS>, C::kSmemLaunch, attr_done))
     return "cudaFuncSetAttribute(max dynamic smem) failed";
-  gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS><<<grid, (AT ? 96 : 64) + 32 * DQ, C::kSmemLaunch, st>>>(tw, tx, b);
+  gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS><<<grid, (AT ? 96 : 64) + 32 * DQ, C::kSmemLaunch, st>>>(tw, tx, ts, b);
   return nullptr;
 }
 
@@ -635,6 +680,15 @@ const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, cons
     }
     if (p == 2) return launch_na<NT, FMT, NA, 16>(a, w, w_row_bytes, x, ldx, grid, st);
     return launch_na<NT, FMT, NA, 8>(a, w, w_row_bytes, x, ldx, grid, st);
+  } else if constexpr (FMT == kFmtQ8_0) {
+    // Q8_0: A (dequantised codes x block scale) in TMEM, as the default Q4_K path
+    if constexpr (NT >= 256) {
+      return launch_na<NT, FMT, 4, 8, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
+    } else if constexpr (NT <= 64) {
+      return launch_na<NT, FMT, 4, 8, true, 1, 2>(a, w, w_row_bytes, x, ldx, grid, st);
+    } else {
+      return launch_na<NT, FMT, 4, 8, true, 2>(a, w, w_row_bytes, x, ldx, grid, st);
+    }
   } else {
     return launch_na<NT, FMT, NA, 8>(a, w, w_row_bytes, x, ldx, grid, st);
   }
@@ -654,7 +708,7 @@ int gemm_q_token_tile(int T) {
 int gemm_q_splits(int N, int K, int T, int fmt) {
   const int nt = gemm_q_token_tile(T);
   const int tiles = ((N + 127) / 128) * ((T + nt - 1) / nt);
-  const int ksteps = fmt == kFmtQ4K ? K / 256 : K / 64;
+  const int ksteps = fmt == kFmtBF16 ? K / 64 : K / 256;
   // as many K splits as fit in ONE wave (a partial second wave costs a whole wave of time);
   // the decode variant runs two CTAs per SM, so its wave is 2 x 148 CTAs. More than one wave
   // of tiles already fills the machine.
@@ -714,8 +768,11 @@ const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const voi
                           const GemmArgs& a_in, cudaStream_t st) {
   GemmArgs a = a_in;
   a.wsplit = wsplit();
-  if (a.K % (fmt == kFmtQ4K ? 256 : 64)) return "gemm_q: K must be a multiple of 256 (Q4_K) or 64 (bf16)";
-  if (fmt != kFmtQ4K && fmt != kFmtBF16) return "gemm_q: weight format not supported by the tensor-core path";
+  if (a.K % (fmt == kFmtBF16 ? 64 : 256)) return "gemm_q: K must be a multiple of 256 (Q4_K, Q8_0) or 64 (bf16)";
+  if (fmt != kFmtQ4K && fmt != kFmtBF16 && fmt != kFmtQ8_0)
+    return "gemm_q: weight format not supported by the tensor-core path";
+  if (fmt == kFmtQ8_0 && (a.wscales == nullptr || reinterpret_cast<uintptr_t>(a.wscales) % 16))
+    return "gemm_q: Q8_0 needs 16-byte aligned f16 block scales";
   if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16 || w_row_bytes % 16 ||
       (ldx * 2) % 16)
     return "gemm_q: operands must be 16-byte aligned with 16-byte-multiple row strides";
@@ -729,6 +786,15 @@ const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const voi
       case 64: return launch_t<64, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
       case 128: return launch_t<128, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
       default: return launch_t<256, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
+    }
+  }
+  if (fmt == kFmtQ8_0) {
+    switch (nt) {
+      case 16: return launch_t<16, kFmtQ8_0>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 32: return launch_t<32, kFmtQ8_0>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 64: return launch_t<64, kFmtQ8_0>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 128: return launch_t<128, kFmtQ8_0>(a, w, w_row_bytes, x, ldx, grid, st);
+      default: return launch_t<256, kFmtQ8_0>(a, w, w_row_bytes, x, ldx, grid, st);
     }
   }
   switch (nt) {

@@ -25,6 +25,7 @@ struct GemmArgs {
   const int* row_count; // optional device count of valid token rows: token tiles at or past it
                         // exit at once (routed-expert GEMMs launched for a capacity)
   PeerPush push;        // kGemmPeerPush destinations
+  const void* wscales;  // Q8_0: f16 block scales [N, K/32] (the codes are the weight pointer)
        // optional per-phase clock64 stamps of CTA (0,0,0) (profiling aid)
 };
 

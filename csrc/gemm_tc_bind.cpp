@@ -43,6 +43,7 @@ void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, i
   a.err = err->data_ptr<int>();
   a.dbg = dbg.has_value() ? (long long*)dbg->data_ptr<int64_t>() : nullptr;
   a.row_count = row_count.has_value() ? row_count->data_ptr<int>() : nullptr;
+  a.wscales = (scales.has_value() && scales->defined()) ? scales->data_ptr() : nullptr;
   if (mode == air::kGemmPeerPush) {
     a.push = peer_push_from_meta(*push_meta);
     TORCH_CHECK(a.N == a.push.row_len && (int64_t)a.T * a.push.row_len <= a.push.slot_elems,
