@@ -4,8 +4,9 @@ names mapped to the GGUF ones (``model.layers.N.self_attn.q_proj.weight`` ->
 ``blk.N.attn_q.weight`` ...), Mixtral experts stacked into ``ffn_*_exps``, and matrices
 quantised on the way in (on the device given, chunk by chunk) to the requested GGUF type.
 
-Block-scaled fp8 weights (E4M3 codes with a ``weight_scale_inv`` per 128 x 128 tile) are
-expanded with their scales first. Attention projections are kept in Hugging Face order: its rotary embedding rotates the two
+Block-scaled fp8 weights (E4M3 codes with a ``weight_scale_inv`` per 128 x 128 tile) are kept
+as fp8 when the requested type is ``FP8_E4M3_B128`` (codes unchanged, the tile multiplier per
+row block), else expanded with their scales first. Attention projections are kept in Hugging Face order: its rotary embedding rotates the two
 halves of each head, which is the rotation the kernels apply, so no permutation is needed.
 """
 from __future__ import annotations
@@ -124,6 +125,13 @@ def hf_records(path: str, qtype: GGMLType = GGMLType.Q4_K, device="cpu", cfg: Mo
                 continue                      # rotary caches, biases of other families ...
             gname = f"blk.{mm.group(1)}.{_LAYER[mm.group(2)]}"
         x = src[name]()
+        if (x.dtype == torch.float8_e4m3fn and qtype == GGMLType.FP8_E4M3_B128 and x.dim() == 2
+                and x.shape[1] % 128 == 0 and name[: -len("weight")] + "weight_scale_inv" in src):
+            # keep block-scaled fp8 as fp8: codes unchanged, tile multipliers per 128-row block
+            from ..gguf.quants import fp8_b128_from_tiles
+            raw = fp8_b128_from_tiles(x, src[name[: -len("weight")] + "weight_scale_inv"]()).to(device)
+            yield gname, raw, GGMLType.FP8_E4M3_B128, tuple(x.shape)
+            continue
         if x.dtype in (torch.float8_e4m3fn, torch.float8_e5m2):
             # block-scaled fp8 checkpoints store the tile multipliers beside the weight
             sname = name[: -len("weight")] + "weight_scale_inv"

@@ -63,6 +63,10 @@ class GGMLType(enum.IntEnum):
     TQ1_0 = 34
     TQ2_0 = 35
     MXFP4 = 39
+    # internal, never written to GGUF files: block-scaled FP8 weights, one f32 multiplier
+    # then 128 E4M3 codes per block of 128 weights along K (132 bytes). Block-scaled fp8
+    # checkpoints (128 x 128 tile scales) map onto it exactly, one tile row at a time.
+    FP8_E4M3_B128 = 1001
 
 
 QK_K = 256
@@ -101,6 +105,7 @@ BLOCK_GEOMETRY: dict[GGMLType, tuple[int, int]] = {
     GGMLType.TQ1_0: (256, 54),
     GGMLType.TQ2_0: (256, 66),
     GGMLType.MXFP4: (32, 17),
+    GGMLType.FP8_E4M3_B128: (128, 132),
 }
 
 

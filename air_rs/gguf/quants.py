@@ -321,6 +321,35 @@ def dequantize_iq4_xs(raw: torch.Tensor) -> torch.Tensor:
     return _flat(v.reshape(*b.shape[:-1], 256))
 
 
+def quantize_fp8_b128(x: torch.Tensor) -> torch.Tensor:
+    """[..., K] -> blocks of [f32 multiplier | 128 E4M3 codes]; each block's absmax maps to
+    448, the E4M3 maximum."""
+    xf = x.float()
+    b = xf.reshape(*xf.shape[:-1], xf.shape[-1] // 128, 128)
+    s = (b.abs().amax(-1, keepdim=True) / 448.0).clamp_min(1e-12)
+    codes = (b / s).to(torch.float8_e4m3fn).view(torch.uint8)
+    raw = torch.cat([s.contiguous().view(torch.uint8), codes], -1)
+    return raw.reshape(*xf.shape[:-1], -1)
+
+
+def fp8_b128_from_tiles(codes: torch.Tensor, scale_inv: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """A block-scaled fp8 checkpoint tensor (E4M3 codes [N, K], multipliers per block x block
+    tile) in the FP8_E4M3_B128 layout, codes unchanged (exact)."""
+    N, K = codes.shape
+    if K % 128 or block != 128:
+        raise ValueError("FP8_E4M3_B128 needs K % 128 == 0 and 128 x 128 tiles")
+    s = scale_inv.float().repeat_interleave(block, 0)[:N].reshape(N, K // 128, 1)
+    c = codes.contiguous().view(torch.uint8).reshape(N, K // 128, 128)
+    return torch.cat([s.contiguous().view(torch.uint8), c], -1).reshape(N, -1)
+
+
+def dequantize_fp8_b128(raw: torch.Tensor) -> torch.Tensor:
+    b = raw.reshape(*raw.shape[:-1], raw.shape[-1] // 132, 132)
+    s = b[..., :4].contiguous().view(torch.float32)
+    v = b[..., 4:].contiguous().view(torch.float8_e4m3fn).float() * s
+    return v.reshape(*raw.shape[:-1], -1)
+
+
 def _dense(dtype):
     def f(raw: torch.Tensor) -> torch.Tensor:
         n = torch.tensor([], dtype=dtype).element_size()
@@ -345,6 +374,7 @@ DEQUANT = {
     GGMLType.Q8_K: dequantize_q8_k,
     GGMLType.IQ4_NL: dequantize_iq4_nl,
     GGMLType.IQ4_XS: dequantize_iq4_xs,
+    GGMLType.FP8_E4M3_B128: dequantize_fp8_b128,
 }
 
 QUANT = {
@@ -354,6 +384,7 @@ QUANT = {
     GGMLType.Q8_0: quantize_q8_0,
     GGMLType.Q4_K: quantize_q4_k,
     GGMLType.Q6_K: quantize_q6_k,
+    GGMLType.FP8_E4M3_B128: quantize_fp8_b128,
 }
 
 

@@ -132,7 +132,12 @@ class LlamaWeights:
     def _try_build(self, p: dict, final: bool = False):
         cfg = self.cfg
         if self.embd is None and "token_embd.weight" in p:
-            self.embd = self._lin_full(*p["token_embd.weight"])
+            raw, qt, shape = p["token_embd.weight"]
+            if qt == GGMLType.FP8_E4M3_B128:
+                # the embedding gather reads GGUF block formats; keep the table as Q8_0
+                from ..gguf.quants import quantize_q8_0
+                raw, qt = quantize_q8_0(dequantize(raw.reshape(shape[0], -1), qt)), GGMLType.Q8_0
+            self.embd = self._lin_full(raw, qt, shape)
         if self.out_norm is None and "output_norm.weight" in p:
             self.out_norm = self._vec(*p.pop("output_norm.weight"))
         if self.out_norm_b is None and "output_norm.bias" in p:

@@ -17,7 +17,8 @@ from ..gguf.quants import dequantize
 _EXT = None
 _EXT_ERR: Exception | None = None
 
-FMT_Q4K, FMT_Q8_0, FMT_BF16 = 0, 1, 2
+FMT_Q4K, FMT_Q8_0, FMT_BF16, FMT_FP8 = 0, 1, 2, 3
+GEMV_FMTS = (FMT_Q4K, FMT_Q8_0, FMT_BF16)   # formats the decode GEMVs read
 
 # Number of our kernels launched (eager launches + kernels inside replayed CUDA graphs).
 _LAUNCHES = [0]
@@ -103,7 +104,9 @@ class QWeight:
     FMT_Q4K keeps the GGUF Q4_K blocks (144 B per 256 weights) byte-for-byte but groups
     them as [N/128 tiles][K/256][128 rows][144 B], so a 128-row x 256-weight tile is one
     contiguous 18 KB copy for the TMA engine (rows padded to whole tiles). FMT_Q8_0 splits
-    the 34-byte GGUF block into int8 codes + f16 scales (row-major). FMT_BF16 is dense bf16
+    the 34-byte GGUF block into int8 codes + f16 scales (row-major). FMT_FP8 holds block-scaled
+    E4M3 codes [N, K] + one f32 multiplier per row and 128-wide K block (tensor-core GEMM
+    only). FMT_BF16 is dense bf16
     (F16/BF16/F32 checkpoints and K-quants without a fused kernel are expanded to it).
     ``parts`` records the row offsets of concatenated weights (e.g. gate|up), which start
     on tile boundaries for Q4_K.
@@ -158,6 +161,12 @@ class QWeight:
         raw = raw.reshape(N, -1)
         if qtype == GGMLType.Q4_K:
             return cls(FMT_Q4K, _q4k_tile(raw.to(device), N, K), None, N, K, qtype, ((0, N),))
+        if qtype == GGMLType.FP8_E4M3_B128:
+            # E4M3 codes [N, K] (uint8) + one f32 multiplier per row and 128-wide K block
+            b = raw.to(device).reshape(N, K // 128, 132)
+            scales = b[..., 0:4].contiguous().view(torch.float32).reshape(N, K // 128)
+            codes = b[..., 4:].contiguous().reshape(N, K)
+            return cls(FMT_FP8, codes, scales.contiguous(), N, K, qtype, ((0, N),))
         if qtype == GGMLType.Q8_0:
             b = raw.to(device).reshape(N, K // 32, 34)
             scales = b[..., 0:2].contiguous().view(torch.float16).reshape(N, K // 32)

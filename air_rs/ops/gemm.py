@@ -1,7 +1,7 @@
 """GEMM entry point of the prefill / large-batch path.
 
-``linear`` runs the tcgen05 dequant-fused GEMM (``air_rs._C.gemm_q``) for Q4_K, Q8_0 and
-bf16 weights; split-K partials go to a per-device workspace owned here (allocated once, before
+``linear`` runs the tcgen05 dequant-fused GEMM (``air_rs._C.gemm_q``) for Q4_K, Q8_0,
+block-scaled FP8 and bf16 weights; split-K partials go to a per-device workspace owned here (allocated once, before
 any CUDA-graph capture, and grown only outside capture). The ``baseline`` implementation
 (dequantise to a bf16 scratch with our kernel, then a library matmul) exists as the
 comparison arm (``AIR_GEMM_IMPL=baseline``) and for formats without a fused kernel.
@@ -12,7 +12,7 @@ import os
 
 import torch
 
-from . import QWeight, require_ext, FMT_BF16, FMT_Q4K, FMT_Q8_0, count_launch
+from . import QWeight, require_ext, FMT_BF16, FMT_FP8, FMT_Q4K, FMT_Q8_0, count_launch
 
 GEMM_STORE_F32, GEMM_STORE_BF16, GEMM_RESIDUAL, GEMM_PEER_PUSH = 0, 1, 2, 3
 
@@ -28,6 +28,8 @@ def tc_supported(w: QWeight) -> bool:
         return w.K % 256 == 0 and w.data.dim() == 4
     if w.fmt == FMT_BF16:
         return w.K % 64 == 0
+    if w.fmt == FMT_FP8:
+        return w.K % 256 == 0 and w.scales is not None
     if w.fmt == FMT_Q8_0:
         # int8 codes + f16 block scales fed by TMA; the scale rows must be 16-byte strides
         return w.K % 256 == 0 and w.scales is not None and os.environ.get("AIR_GEMM_Q8", "1") != "0"

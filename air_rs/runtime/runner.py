@@ -137,6 +137,11 @@ class ModelRunner:
         else:
             self.up_off = l0.wgu.parts[1][0] if l0.wgu is not None else self.F
         self.qkv_f = torch.zeros(B, self.qkv_dim, dtype=f32, device=dev) if self.qkv_bias else None
+        # decode GEMVs read Q4_K / Q8_0 / bf16; other formats (block-scaled FP8) decode on the
+        # tensor-core GEMM path at every batch size
+        fmts = [q.fmt for lw in weights.layers for q in (lw.wqkv, lw.wo, lw.wgu, lw.wdown) if q is not None]
+        fmts += [q.fmt for lw in weights.layers for q in lw.experts_gu + lw.experts_down] + [weights.lm_head.fmt]
+        self.gemv_ok = all(f in ops.GEMV_FMTS for f in fmts)
         self.gu_b = torch.zeros(B, self.gu_w, dtype=bf16, device=dev)
         self.h_b = torch.zeros(B, self.Fp, dtype=bf16, device=dev)
         self.o_b = torch.zeros(B, self.H, dtype=bf16, device=dev)
@@ -289,12 +294,12 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int):
-        if B <= GEMV_MAX_B and self.fused_norm_ok():
+        if B <= GEMV_MAX_B and self.gemv_ok and self.fused_norm_ok():
             return self._decode_fused(B)
         cfg, w, si = self.cfg, self.w, self.inputs[B]
         x, xq, xds = self.x[:B], self.xq[:B], self.xds[:B]
         ops.embed(w.embd, si.ids, out_f32=x, err=self.err, n=B)
-        gemv_path = B <= GEMV_MAX_B
+        gemv_path = B <= GEMV_MAX_B and self.gemv_ok
         ns = self.n_splits(B)
         tp = self.tp_size > 1
         peer = self._peer(B)

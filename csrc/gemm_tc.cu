@@ -18,6 +18,7 @@
 // src/ops.rs:594-611 via candle-core's CUDA quantized matmul).
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_fp8.h>
 #include "common.cuh"
 #include "sm100.cuh"
 #include "gemm_tc.h"
@@ -69,10 +70,11 @@ struct Cfg {
   // 256-token tiles stage single chunks (a whole stage would be 128 KB), and the MMA frees a
   // chunk as soon as its four K16 steps are issued
   // (Q8_0 weight tiles are twice the Q4_K size: the two-CTA decode variant stages chunks too)
-  static constexpr int kXC = (NT >= 256 || (FMT == kFmtQ8_0 && CPS == 2)) ? 1 : 4;   // chunks per X item
+  static constexpr int kXC = (NT >= 256 || (FMT != kFmtQ4K && CPS == 2)) ? 1 : 4;   // chunks per X item
   static constexpr int kXStage = kXC * kBChunk;
   static constexpr int kXStages = kXC == 1 ? (NT >= 256 ? 3 : 4) : ((NT >= 64 || CPS == 2) ? 2 : 3);
-  static constexpr int kWTile = FMT == kFmtQ8_0 ? kQ8Tile : kRawTile;   // one raw weight stage
+  // one raw weight stage: Q4_K tile / Q8_0 codes + scales / FP8 codes (scales read directly)
+  static constexpr int kWTile = FMT == kFmtQ8_0 ? kQ8Tile : (FMT == kFmtFP8 ? 2 * kQ8Half : kRawTile);
   static constexpr int kBudgetAT = CPS == 2 ? 112 * 1024 - 2048 : kBudget;
   static constexpr int kWStagesRaw = (kBudgetAT - kXStages * kXStage) / kWTile;
   static constexpr int kWStages = kWStagesRaw > 12 ? 12 : kWStagesRaw;
@@ -126,7 +128,7 @@ __global__ void __launch_bounds__((AT ? 96 : 64) + 32 * DQ, CPS)
 gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
               const __grid_constant__ CUtensorMap tm_s, GemmArgs a) {
   using C = Cfg<NT, FMT, NA, AT, NACC, CPS>;
-  static_assert(!AT || FMT == kFmtQ4K || FMT == kFmtQ8_0, "A-in-TMEM path: Q4_K and Q8_0");
+  static_assert(!AT || FMT == kFmtQ4K || FMT == kFmtQ8_0 || FMT == kFmtFP8, "A-in-TMEM path: Q4_K, Q8_0, FP8");
   // routed-expert GEMMs: token tiles beyond the device row count do nothing (uniform per CTA,
   // before any barrier, TMEM allocation or copy)
   if (a.row_count != nullptr && (int)blockIdx.y * NT >= __ldg(a.row_count)) return;
@@ -141,7 +143,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * 128, n0 = blockIdx.y * NT;
   const int split = blockIdx.z, splits = gridDim.z;
-  const int ksteps = (FMT == kFmtQ4K || FMT == kFmtQ8_0) ? a.K / 256 : a.K / 64;
+  const int ksteps = FMT == kFmtBF16 ? a.K / 64 : a.K / 256;
   const int kper = (ksteps + splits - 1) / splits;
   const int kb0 = split * kper;
   const int nk = max(0, min(ksteps, kb0 + kper) - kb0);
@@ -210,12 +212,12 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         uint8_t* st = ring + s * bytes;
         if (dbg && wprod && i < 32) dbg[i] = clock64();
         mbar_expect_tx(&fullb[s], bytes);
-        if (wprod && FMT == kFmtQ8_0) {
-          // codes [rows m0.., K kb*256..] as two SW128 boxes, then the rows' eight block scales
+        if (wprod && (FMT == kFmtQ8_0 || FMT == kFmtFP8)) {
+          // codes [rows m0.., K kb*256..] as two SW128 boxes; Q8_0 then the rows' eight scales
           const int kb = kb0 + i;
           tma_load_2d(st, &tm_w, &fullb[s], kb * 256, m0);
           tma_load_2d(st + kQ8Half, &tm_w, &fullb[s], kb * 256 + 128, m0);
-          tma_load_2d(st + 2 * kQ8Half, &tm_s, &fullb[s], kb * 8, m0);
+          if (FMT == kFmtQ8_0) tma_load_2d(st + 2 * kQ8Half, &tm_s, &fullb[s], kb * 8, m0);
         } else if (wprod) {
           // the tile as a.wsplit back-to-back bulk copies (more requests in flight per CTA)
           const uint8_t* src = a.wq + ((size_t)blockIdx.x * ksteps + kb0 + i) * kRawTile;
@@ -385,7 +387,30 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
               !mbar_wait(&bars->aempty[ab], ((g / C::kAbufs) - 1) & 1, a.err)) { ok = false; break; }
           const uint32_t ta = tlane + 32 * C::kUA * ab - 32 * (c / C::kUA) * C::kUA;
           uint32_t o[16];
-          if constexpr (FMT == kFmtQ8_0) {
+          if constexpr (FMT == kFmtFP8) {
+            // 32 E4M3 codes of row r (two 16-byte chunks of its SW128 half) x the f32 multiplier
+            // of K block (kb * 256 + 64 c) / 128
+            const uint8_t* row = q8 + (c >> 1) * kQ8Half + r * 128;
+            const int j0 = 4 * (c & 1) + 2 * h;
+            const uint4 qa = *reinterpret_cast<const uint4*>(row + ((j0 ^ (r & 7)) << 4));
+            const uint4 qb = *reinterpret_cast<const uint4*>(row + (((j0 + 1) ^ (r & 7)) << 4));
+            const int grow = m0 + r;
+            const float dq = grow < a.N ? __ldg(static_cast<const float*>(a.wscales) +
+                                               (size_t)grow * (a.K / 128) + (kb0 + i) * 2 + (c >> 1))
+                                        : 0.f;
+            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(
+                    (__nv_fp8x2_storage_t)((w[k] >> (16 * e)) & 0xFFFF), __NV_E4M3);
+                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+                __nv_bfloat162 b = __floats2bfloat162_rn(v.x * dq, v.y * dq);
+                o[2 * k + e] = *reinterpret_cast<uint32_t*>(&b);
+              }
+            }
+          } else if constexpr (FMT == kFmtQ8_0) {
             // block 2c + h of the stage: 32 codes = two 16-byte chunks of row r's SW128 half
             const uint8_t* row = q8 + (c >> 1) * kQ8Half + r * 128;
             const int j0 = 4 * (c & 1) + 2 * h;
@@ -631,6 +656,11 @@ const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, con
          a.wscales != nullptr &&
          encode_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.wscales, (uint64_t)(a.K / 32), (uint64_t)a.N,
                    (uint64_t)(a.K / 32) * 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else if (FMT == kFmtFP8) {
+    // E4M3 codes [N, K] as Q8_0's; the f32 multipliers are read by the dequant warps
+    ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)w_row_bytes,
+                   128, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         a.wscales != nullptr;
   } else
     ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, (uint64_t)a.K, (uint64_t)a.N,
                    (uint64_t)w_row_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -680,8 +710,8 @@ const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, cons
     }
     if (p == 2) return launch_na<NT, FMT, NA, 16>(a, w, w_row_bytes, x, ldx, grid, st);
     return launch_na<NT, FMT, NA, 8>(a, w, w_row_bytes, x, ldx, grid, st);
-  } else if constexpr (FMT == kFmtQ8_0) {
-    // Q8_0: A (dequantised codes x block scale) in TMEM, as the default Q4_K path
+  } else if constexpr (FMT == kFmtQ8_0 || FMT == kFmtFP8) {
+    // Q8_0 / FP8: A (dequantised codes x block scale) in TMEM, as the default Q4_K path
     if constexpr (NT >= 256) {
       return launch_na<NT, FMT, 4, 8, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
     } else if constexpr (NT <= 64) {
@@ -769,10 +799,10 @@ const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const voi
   GemmArgs a = a_in;
   a.wsplit = wsplit();
   if (a.K % (fmt == kFmtBF16 ? 64 : 256)) return "gemm_q: K must be a multiple of 256 (Q4_K, Q8_0) or 64 (bf16)";
-  if (fmt != kFmtQ4K && fmt != kFmtBF16 && fmt != kFmtQ8_0)
+  if (fmt != kFmtQ4K && fmt != kFmtBF16 && fmt != kFmtQ8_0 && fmt != kFmtFP8)
     return "gemm_q: weight format not supported by the tensor-core path";
-  if (fmt == kFmtQ8_0 && (a.wscales == nullptr || reinterpret_cast<uintptr_t>(a.wscales) % 16))
-    return "gemm_q: Q8_0 needs 16-byte aligned f16 block scales";
+  if ((fmt == kFmtQ8_0 || fmt == kFmtFP8) && (a.wscales == nullptr || reinterpret_cast<uintptr_t>(a.wscales) % 16))
+    return "gemm_q: Q8_0 / FP8 need 16-byte aligned block scales";
   if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(x) % 16 || w_row_bytes % 16 ||
       (ldx * 2) % 16)
     return "gemm_q: operands must be 16-byte aligned with 16-byte-multiple row strides";
@@ -786,6 +816,15 @@ const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const voi
       case 64: return launch_t<64, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
       case 128: return launch_t<128, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
       default: return launch_t<256, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
+    }
+  }
+  if (fmt == kFmtFP8) {
+    switch (nt) {
+      case 16: return launch_t<16, kFmtFP8>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 32: return launch_t<32, kFmtFP8>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 64: return launch_t<64, kFmtFP8>(a, w, w_row_bytes, x, ldx, grid, st);
+      case 128: return launch_t<128, kFmtFP8>(a, w, w_row_bytes, x, ldx, grid, st);
+      default: return launch_t<256, kFmtFP8>(a, w, w_row_bytes, x, ldx, grid, st);
     }
   }
   if (fmt == kFmtQ8_0) {

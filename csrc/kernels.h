@@ -11,6 +11,7 @@ enum WeightFormat : int {
   kFmtQ4K = 0,    // raw GGUF Q4_K blocks, [N, K/256*144] bytes
   kFmtQ8_0 = 1,   // repacked Q8_0: int8 qs [N, K] + f16 scales [N, K/32]
   kFmtBF16 = 2,   // dense bf16 [N, K]
+  kFmtFP8 = 3,    // E4M3 codes [N, K] + f32 multiplier per row and 128-wide K block (GEMM only)
 };
 
 enum GemvEpilogue : int {

@@ -1,6 +1,7 @@
 // Token-parallel kernels of the prefill / batched path: embedding gather with on-the-fly
 // dequant (K1), RoPE + paged KV write for GEMM outputs (K4/K5), SwiGLU activation,
 // residual add, and GGUF block -> bf16 dequant (K17).
+#include <cuda_fp8.h>
 #include "common.cuh"
 #include "misc.h"
 
@@ -36,6 +37,17 @@ AIR_DEVICE void dequant32(int fmt, const uint8_t* base, int64_t r, int64_t row_b
     const float d = __half2float(static_cast<const __half*>(scales_row)[k0 >> 5]);
 #pragma unroll
     for (int l = 0; l < 32; ++l) f[l] = d * q[l];
+  } else if (fmt == kFmtFP8) {
+    // E4M3 codes; one f32 multiplier per row and 128-wide K block
+    const float d = static_cast<const float*>(scales)[r * (K / 128) + (k0 >> 7)];
+#pragma unroll
+    for (int l = 0; l < 32; l += 2) {
+      const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(
+          *reinterpret_cast<const __nv_fp8x2_storage_t*>(row + k0 + l), __NV_E4M3);
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&h));
+      f[l] = v.x * d;
+      f[l + 1] = v.y * d;
+    }
   } else {
     const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(row) + k0;
 #pragma unroll

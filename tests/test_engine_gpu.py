@@ -38,7 +38,7 @@ def _check_near_argmax(oracle, prompt, toks, penalty=1.1, tol=0.15):
     return worst
 
 
-@pytest.mark.parametrize("qt", [GGMLType.Q8_0, GGMLType.Q4_K])
+@pytest.mark.parametrize("qt", [GGMLType.Q8_0, GGMLType.Q4_K, GGMLType.FP8_E4M3_B128])
 def test_engine_gemv_path_matches_oracle(qt):
     cfg, oracle, runner = _models(qt)
     eng = Engine(cfg, runner, max_batch=8)

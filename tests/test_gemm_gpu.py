@@ -18,7 +18,7 @@ def _w(N, K, qt, seed):
     return ops.QWeight.from_raw(raw, qt, N, K, DEV), wd
 
 
-@pytest.mark.parametrize("qt", [GGMLType.Q4_K, GGMLType.Q8_0, GGMLType.BF16])
+@pytest.mark.parametrize("qt", [GGMLType.Q4_K, GGMLType.Q8_0, GGMLType.FP8_E4M3_B128, GGMLType.BF16])
 @pytest.mark.parametrize("N,K,T,splits", [(128, 256, 1, 1), (384, 512, 5, 1), (256, 1024, 64, None),
                                           (256, 2048, 64, 4), (512, 1024, 200, None), (4096, 4096, 16, None),
                                           (200, 512, 33, None), (1456, 256, 33, 1),

@@ -125,3 +125,24 @@ def test_iq4_formats_against_definition():
     sh = int(raw[0, 2]) | (int(raw[0, 3]) << 8)
     ls = (int(raw[0, 4]) & 0xF) | ((sh & 3) << 4)
     assert float(out[0]) == (ls - 32) * float(IQ4_NL_VALUES[int(raw[0, 8]) & 0xF])
+
+
+def test_fp8_b128_block_format():
+    """Block-scaled FP8 (internal type FP8_E4M3_B128: f32 multiplier + 128 E4M3 codes per
+    block): round trip within E4M3's relative step, and a 128 x 128-tile fp8 checkpoint maps
+    onto it with its codes unchanged (exact)."""
+    import torch
+    from air_rs.gguf import GGMLType, dequantize, quantize
+    from air_rs.gguf.quants import fp8_b128_from_tiles
+    from air_rs.quant.fp8 import block_dequantize_fp8, block_quantize_fp8
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(6, 384, generator=g)
+    raw = quantize(x, GGMLType.FP8_E4M3_B128)
+    assert raw.shape == (6, 3 * 132)
+    y = dequantize(raw, GGMLType.FP8_E4M3_B128)
+    blk = x.reshape(6, 3, 128).abs().amax(-1, keepdim=True)
+    assert float(((y - x).reshape(6, 3, 128).abs() / blk).max()) <= 1 / 14 + 1e-6   # half an E4M3 step at 448
+    w = torch.randn(256, 384, generator=g)
+    codes, s_inv = block_quantize_fp8(w)
+    r2 = fp8_b128_from_tiles(codes, s_inv)
+    torch.testing.assert_close(dequantize(r2, GGMLType.FP8_E4M3_B128), block_dequantize_fp8(codes, s_inv))
