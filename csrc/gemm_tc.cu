@@ -129,9 +129,16 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
               const __grid_constant__ CUtensorMap tm_s, GemmArgs a) {
   using C = Cfg<NT, FMT, NA, AT, NACC, CPS>;
   static_assert(!AT || FMT == kFmtQ4K || FMT == kFmtQ8_0 || FMT == kFmtFP8, "A-in-TMEM path: Q4_K, Q8_0, FP8");
+  // Programmatic dependent launch: this grid may start while the previous kernel finishes.
+  // Set-up, the weight stream (read-only), the dequantisation and the MMAs run ahead; the
+  // activation producer and the epilogue (the only readers of activations / scratch and the
+  // only global writers) wait for the previous grid first (griddepcontrol.wait), as does
+  // everything when a device row count gates the tiles.
+  if (a.row_count != nullptr) pdl_wait();
+  pdl_trigger();
   // routed-expert GEMMs: token tiles beyond the device row count do nothing (uniform per CTA,
   // before any barrier, TMEM allocation or copy)
-  if (a.row_count != nullptr && (int)blockIdx.y * NT >= __ldg(a.row_count)) return;
+  if (a.row_count != nullptr && (int)blockIdx.y * NT >= *(volatile const int*)a.row_count) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -200,6 +207,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       uint8_t* ring = wprod ? stages : stages + C::kWStages * C::kWTile;
       const uint32_t bytes = wprod ? C::kWTile : C::kXStage;
       const int items = wprod ? nk : nk * (4 / C::kXC);
+      if (!wprod) pdl_wait();                          // activations come from the previous kernel
       int issued = 0;
       for (int i = 0; i < items; ++i) {
         const int s = i % S;
@@ -239,6 +247,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   } else if (!AT && warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
+      pdl_wait();                                      // the stages carry activations
       const uint32_t tx = C::kStageBytes;
       int issued = 0;
       for (int i = 0; i < nk; ++i) {
@@ -528,6 +537,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
       }
     }
     // ------------------------------------------------------------ epilogue
+    pdl_wait();                                        // epilogue: scratch and output writes
     const bool done_ok = mbar_wait(&bars->done, 0, a.err);
     if (dbg && threadIdx.x == 32 * C::kFirstDq) dbg[224] = clock64();
     tc_fence_after();
@@ -637,6 +647,16 @@ bool encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64_t
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// AIR_PDL=0 turns programmatic dependent launch off (for the GEMVs too).
+bool gemm_pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("AIR_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 template <int NT, int FMT, int NA, int DQ, bool AT = false, int NACC = 1, int CPS = 1>
 const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
                       dim3 grid, cudaStream_t st) {
@@ -671,7 +691,18 @@ const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, con
   static unsigned long long attr_done = 0;
   if (!set_max_smem_per_device(gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS>, C::kSmemLaunch, attr_done))
     return "cudaFuncSetAttribute(max dynamic smem) failed";
-  gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS><<<grid, (AT ? 96 : 64) + 32 * DQ, C::kSmemLaunch, st>>>(tw, tx, ts, b);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3((AT ? 96 : 64) + 32 * DQ);
+  cfg.dynamicSmemBytes = C::kSmemLaunch;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = gemm_pdl_enabled() ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS>, tw, tx, ts, b) != cudaSuccess)
+    return "gemm_q: launch failed";
   return nullptr;
 }
 

@@ -137,6 +137,7 @@ template <typename TIn>
 __global__ void swiglu_kernel(const TIn* __restrict__ gu, int T, int F, int64_t ld_in, int64_t up_off,
                               int64_t ld_out,
                               __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32, int act) {
+  pdl_trigger();   // the down GEMM that follows may start streaming its weights
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)T * F) return;
   const int64_t t = idx / F, j = idx % F;
