@@ -14,6 +14,7 @@
 #include <fcntl.h>
 #include <unistd.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -34,6 +35,13 @@ CuFileApi& api() {
   static CuFileApi a;
   static std::once_flag once;
   std::call_once(once, [] {
+    // Off unless AIR_CUFILE=1: on the B200 pool used for testing (no nvidia-fs driver) a
+    // cuFile read in compatibility mode did not return, so nothing here runs by default.
+    const char* en = getenv("AIR_CUFILE");
+    if (!(en && en[0] == '1')) {
+      a.error = "cuFile disabled (set AIR_CUFILE=1 to enable)";
+      return;
+    }
     void* h = dlopen("libcufile.so.0", RTLD_NOW | RTLD_LOCAL);
     if (!h) h = dlopen("libcufile.so", RTLD_NOW | RTLD_LOCAL);
     if (!h) {
