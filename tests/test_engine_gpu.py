@@ -100,7 +100,9 @@ def test_fused_norm_decode_chain_matches_unfused(B):
         eng = Engine(cfg, rn, max_batch=8)
         outs[fused] = eng.generate_ids(prompts, SamplingParams(max_tokens=16, temperature=0.0, ignore_eos=True))
         rn.check_errors()
-    for p, o in zip(prompts, outs[True]):
-        _check_near_argmax(oracle, [cfg.bos_token_id] + p, o)
-    same = sum(a == b for x, y in zip(outs[True], outs[False]) for a, b in zip(x, y))
-    assert same >= 0.9 * sum(len(x) for x in outs[True])
+    # both chains decode near the oracle's argmax at every step (teacher forcing); their
+    # token streams may part at a near-tie of the random model, after which they differ
+    for fused in (True, False):
+        for p, o in zip(prompts, outs[fused]):
+            _check_near_argmax(oracle, [cfg.bos_token_id] + p, o)
+    assert all(x[0] == y[0] for x, y in zip(outs[True], outs[False]))   # first decode step
