@@ -149,6 +149,28 @@ __global__ void swiglu_kernel(const TIn* __restrict__ gu, int T, int F, int64_t 
   if (out_f32) out_f32[t * ld_out + j] = v;
 }
 
+// bf16 in / bf16 out, 8 columns per thread (16-byte loads and stores): F, ld_in, up_off and
+// ld_out multiples of 8 with 16-byte aligned rows
+__global__ void swiglu_bf16x8_kernel(const __nv_bfloat16* __restrict__ gu, int T, int F, int64_t ld_in,
+                                     int64_t up_off, int64_t ld_out, __nv_bfloat16* __restrict__ out, int act) {
+  pdl_trigger();
+  const int F8 = F / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)T * F8) return;
+  const int64_t t = idx / F8, j = (idx % F8) * 8;
+  float g[8], u[8];
+  bf16x8_to_f32(*reinterpret_cast<const uint4*>(gu + t * ld_in + j), g);
+  if (up_off >= 0) {
+    bf16x8_to_f32(*reinterpret_cast<const uint4*>(gu + t * ld_in + up_off + j), u);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) u[e] = 1.f;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) g[e] = gate_act(g[e], act) * u[e];
+  *reinterpret_cast<uint4*>(out + t * ld_out + j) = f32_to_bf16x8(g);
+}
+
 template <typename TIn>
 __global__ void residual_add_kernel(float* __restrict__ resid, const TIn* __restrict__ y, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -186,6 +208,15 @@ void launch_swiglu(const void* gu, bool bf16_in, int T, int F, int64_t ld_in, in
                    int64_t ld_out, void* out_bf16, float* out_f32, int act, cudaStream_t st) {
   const int64_t n = (int64_t)T * F;
   if (n <= 0) return;
+  const bool vec = bf16_in && out_bf16 && !out_f32 && F % 8 == 0 && ld_in % 8 == 0 && ld_out % 8 == 0 &&
+                   (up_off < 0 || up_off % 8 == 0) && reinterpret_cast<uintptr_t>(gu) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(out_bf16) % 16 == 0;
+  if (vec) {
+    const int64_t n8 = (int64_t)T * (F / 8);
+    swiglu_bf16x8_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, st>>>(
+        (const __nv_bfloat16*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, act);
+    return;
+  }
   const unsigned grid = (unsigned)((n + 255) / 256);
   if (bf16_in) swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, out_f32, act);
   else swiglu_kernel<float><<<grid, 256, 0, st>>>((const float*)gu, T, F, ld_in, up_off, ld_out, (__nv_bfloat16*)out_bf16, out_f32, act);

@@ -324,3 +324,20 @@ def test_embed_and_dequant():
         torch.testing.assert_close(out.cpu(), wd[ids.cpu().long()], rtol=1e-5, atol=1e-6)
         bf = w.dequantize_bf16()
         torch.testing.assert_close(bf.float().cpu(), wd, rtol=1e-2, atol=1e-4)
+
+
+@pytest.mark.parametrize("act,up", [(0, True), (1, True), (1, False)])
+@pytest.mark.parametrize("F", [688, 1024])
+def test_swiglu_kernel_matches_fp32(act, up, F):
+    """Gated activation kernel (SiLU / GELU-tanh gate, or ungated GELU) against fp32 PyTorch;
+    F = 1024 takes the 8-wide vector path, 688 the scalar one."""
+    import torch.nn.functional as Fn
+    T = 37
+    g = torch.Generator().manual_seed(F + act)
+    gu = torch.randn(T, 2 * F, generator=g).bfloat16()
+    out = torch.zeros(T, F, dtype=torch.bfloat16, device=DEV)
+    ops.swiglu(gu.to(DEV), T, F, out_bf16=out, ld_out=F, up_off=F if up else -1, act=act)
+    a = gu[:, :F].float()
+    gate = Fn.silu(a) if act == 0 else Fn.gelu(a, approximate="tanh")
+    ref = gate * (gu[:, F:].float() if up else 1.0)
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=1e-2, atol=1e-2)
