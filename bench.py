@@ -75,7 +75,23 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def mark(self, start: bool):
+        """Bracket the timed region; the summary keeps the samples inside it (plus the nearest
+        one on each side when the region is shorter than the 200 ms sampling period)."""
+        if start:
+            # wait (up to 3 s) for the first sample so the sampler is running before timing
+            t0 = time.monotonic()
+            while self.proc is not None and not self.lines and time.monotonic() - t0 < 3.0:
+                time.sleep(0.02)
+            self.t_start = time.monotonic()
+        else:
+            self.t_end = time.monotonic()
+            t0 = time.monotonic()
+            while self.proc is not None and time.monotonic() - t0 < 0.5 and \
+                    not any(t >= self.t_end for t, _ in self.lines):
+                time.sleep(0.02)
 
     def __exit__(self, *a):
         if self.proc is not None:
@@ -88,7 +104,16 @@ class ClockSampler:
     def summary(self) -> dict:
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        ts, te = getattr(self, "t_start", None), getattr(self, "t_end", None)
+        lines = self.lines
+        if ts is not None and te is not None and lines:
+            inside = [l for t, l in lines if ts <= t <= te]
+            before = [l for t, l in lines if t < ts][-1:]
+            after = [l for t, l in lines if t > te][:1]
+            lines = inside + before + after
+        else:
+            lines = [l for _, l in lines]
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -228,16 +253,18 @@ def main():
             for r in batch:
                 r.output_ids.append(0)  # the token sampled on the device; ids stay there
 
-    run_steps(W)
-    ops.reset_launch_count()
-    barrier()
     from air_rs.ops import launch_count
     with ClockSampler(local) as clk:
+        run_steps(W)
+        clk.mark(start=True)          # the sampler has produced a sample before timing starts
+        ops.reset_launch_count()
+        barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         run_steps(K)
         e1.record()
         barrier()
+        clk.mark(start=False)
     ms = e0.elapsed_time(e1)
     launches = launch_count()
     rn.check_errors()
