@@ -742,6 +742,8 @@ const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, cons
         const int cps = c2 ? atoi(c2) : (ctas <= 148 ? 1 : 2);
         if (cps == 1 && !(e && atoi(e) == 8))
           return launch_na<NT, FMT, NA, 16, true, NACC>(a, w, w_row_bytes, x, ldx, grid, st);
+        if (cps != 1 && e && atoi(e) == 16)   // two CTAs per SM with 16 dequant warps each (trial)
+          return launch_na<NT, FMT, NA, 16, true, 1, 2>(a, w, w_row_bytes, x, ldx, grid, st);
         if (cps != 1) return launch_na<NT, FMT, NA, 8, true, 1, 2>(a, w, w_row_bytes, x, ldx, grid, st);
       }
       if (e && atoi(e) == 16) return launch_na<NT, FMT, NA, 16, true, NACC>(a, w, w_row_bytes, x, ldx, grid, st);
