@@ -32,6 +32,13 @@ from ..gguf import GGMLType
 
 SHAPES = {"qkv": (6144, 4096), "o": (4096, 4096), "gateup": (28672, 4096), "down": (4096, 14336),
           "lm": (128256, 4096)}
+
+
+def tp_shapes(tp: int) -> dict:
+    """One rank's shard of each projection under tensor parallelism: QKV / gate|up / LM head
+    split by output rows, O / down by input columns."""
+    return {"qkv": (6144 // tp, 4096), "o": (4096, 4096 // tp), "gateup": (28672 // tp, 4096),
+            "down": (4096, 14336 // tp), "lm": (128256 // tp, 4096)}
 L2_BYTES = 126e6
 
 
@@ -114,8 +121,8 @@ def bench_gemm(name: str, T: int, iters: int, dev):
     return us, nbytes + T * K * 2 + T * N * 2, 2.0 * N * K * T
 
 
-def bench_attn(B: int, ctx: int, iters: int, dev):
-    nkv, nh, d, bs = 8, 32, 128, 16
+def bench_attn(B: int, ctx: int, iters: int, dev, tp: int = 1):
+    nkv, nh, d, bs = 8 // tp, 32 // tp, 128, 16
     nblk = B * ((ctx + bs - 1) // bs)
     copies = max(1, int(4 * L2_BYTES // (nblk * 2 * nkv * bs * d * 2)) + 1)
     kvs = [torch.randn(nblk, 2, nkv, bs, d, device=dev).bfloat16() for _ in range(copies)]
@@ -242,8 +249,11 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=640)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--tp", type=int, default=1, help="shapes of one rank's shard under tensor parallelism")
     a = ap.parse_args(argv)
     dev = torch.device("cuda")
+    if a.tp > 1:
+        SHAPES.update(tp_shapes(a.tp))
     bw, fl, tag = peaks()
     names = [a.name] if a.name else list(SHAPES)
 
@@ -263,7 +273,7 @@ def main(argv=None):
                 line("gemm", f"{n} N={SHAPES[n][0]} K={SHAPES[n][1]} T={T}", us, nb, f)
     if a.op in ("all", "attn"):
         for B in ([a.batch] if a.batch else [1, 64]):
-            us, nb, f = bench_attn(B, a.ctx, a.iters, dev)
+            us, nb, f = bench_attn(B, a.ctx, a.iters, dev, a.tp)
             line("attn", f"decode B={B} ctx={a.ctx}", us, nb, f)
     if a.op in ("all", "norm"):
         for K, B in [(4096, 1), (4096, 64), (14336, 8)]:

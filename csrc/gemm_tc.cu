@@ -724,6 +724,8 @@ const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, cons
   constexpr int NA = (FMT == kFmtQ4K && NT == 128) ? 2 : 4;
   if constexpr (FMT == kFmtQ4K && NT >= 256) {
     // 256-token tiles: A in TMEM only (one 256-column accumulator + two A stage buffers)
+    const char* e = getenv("AIR_GEMM_PREFILL_DQ");
+    if (e && atoi(e) == 16) return launch_na<NT, FMT, NA, 16, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
     return launch_na<NT, FMT, NA, 8, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
   } else if constexpr (FMT == kFmtQ4K) {
     const int p = a_path();
