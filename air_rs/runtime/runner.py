@@ -278,6 +278,21 @@ class ModelRunner:
             ops.rmsnorm_quant(x[:B], w, eps, xq, xds, y_bf16=y_bf16, w_offset=self.norm_off, bias=bias,
                               layer=self.norm_layer)
 
+    def _qkv_gemm_rope(self, xin, lw, qkv_buf, positions, slots, kv, q_out):
+        """QKV projection on the GEMM path + RoPE + paged KV write: in the tcgen05 GEMM epilogue
+        (head_dim 128), else a separate token-parallel kernel."""
+        from ..ops import gemm
+        T = xin.shape[0]
+        if self.hd == 128 and gemm.tc_supported(lw.wqkv) and os.environ.get("AIR_GEMM_ROPE", "1") != "0":
+            rope = dict(cs=self.rope_cs, positions=positions, slots=slots, kv=kv, q_out=q_out, bias=lw.qkv_bias,
+                        n_heads=self.nh, n_kv=self.nkv, block_size=self.block_size, rot_dim=self.rot_dim)
+            gemm.linear(xin, lw.wqkv, qkv_buf, self, err=self.err, rope=rope)
+            return
+        self.linear(xin, lw.wqkv, qkv_buf)
+        ops.rope_kv(qkv_buf, T, self.rope_cs, positions, slots, kv, q_out, n_heads=self.nh, n_kv=self.nkv,
+                    head_dim=self.hd, block_size=self.block_size, rot_dim=self.rot_dim, err=self.err,
+                    bias=lw.qkv_bias)
+
     def _qkv_rope(self, lw, xq, xds, B, kv, si):
         """Decode QKV GEMV + RoPE + paged KV write (fused epilogue; with q/k/v biases the
         GEMV stores and the token-parallel RoPE kernel adds the bias first)."""
@@ -311,10 +326,7 @@ class ModelRunner:
                 self._qkv_rope(lw, xq, xds, B, kv, si)
             else:
                 self._norm(x, lw.attn_norm, B, y_bf16=self.xn_b[:B], peer=peer, bias=lw.attn_norm_b)
-                self.linear(self.xn_b[:B], lw.wqkv, self.qkv_b[:B])
-                ops.rope_kv(self.qkv_b[:B], B, self.rope_cs, si.positions, si.slots, kv, self.q[:B],
-                            n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
-                            block_size=self.block_size, rot_dim=self.rot_dim, err=self.err, bias=lw.qkv_bias)
+                self._qkv_gemm_rope(self.xn_b[:B], lw, self.qkv_b[:B], si.positions, si.slots, kv, self.q[:B])
             ops.paged_attention(self.q[:B], kv, si.block_tables, si.ctx_len, self.attn[:B],
                                 n_rows=B, n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
                                 block_size=self.block_size, n_splits=ns if gemv_path else max(2, ns),
@@ -542,10 +554,7 @@ class ModelRunner:
             kv = self.kv[li]
             ops.rmsnorm_quant(x, lw.attn_norm, eps, None, None, y_bf16=xn, bias=lw.attn_norm_b,
                               w_offset=self.norm_off, layer=self.norm_layer)
-            self.linear(xn, lw.wqkv, qkv)
-            ops.rope_kv(qkv, T, self.rope_cs, positions, slots, kv, q, n_heads=self.nh, n_kv=self.nkv,
-                        head_dim=self.hd, block_size=self.block_size, rot_dim=self.rot_dim, err=self.err,
-                        bias=lw.qkv_bias)
+            self._qkv_gemm_rope(xn, lw, qkv, positions, slots, kv, q)
             ops.paged_attention(q, kv, block_tables, ctx, attn, n_rows=T, n_heads=self.nh,
                                 n_kv=self.nkv, head_dim=self.hd, block_size=self.block_size,
                                 row_seq=row_seq, n_splits=1, err=self.err,

@@ -590,6 +590,49 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = 0.f;
         }
+        if (a.mode == kGemmQkvRope) {
+          // exchange through shared memory (the consumed stage ring): row m needs row m ^ 64
+          // of the same head for the rotation; the four warps of this column group hold all
+          // 128 rows of the tile
+          float* xb = reinterpret_cast<float*>(stages) + jh * 128 * 16;
+          const GemmRope& R = a.rope;
+          const int head = blockIdx.x;                 // 128-row tile = one head
+          const bool is_v = head >= R.n_heads + R.n_kv;
+          const int i = m & 63;
+          const int rh = R.rot_dim / 2;
+          const float bself = R.bias ? R.bias[mg] : 0.f, bpart = R.bias ? R.bias[mg ^ 64] : 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) xb[m * 16 + e] = v[e];
+          asm volatile("bar.sync %0, 128;" ::"r"(2 + jh) : "memory");
+#pragma unroll 4
+          for (int e = 0; e < 16; ++e) {
+            const int n = n0 + 16 * j + e;
+            float y = v[e] + bself;
+            if (n < a.T && !is_v && i < rh) {
+              const float p = xb[(m ^ 64) * 16 + e] + bpart;
+              const float2 cs = R.cs[(size_t)R.positions[n] * rh + i];
+              y = m < 64 ? y * cs.x - p * cs.y : p * cs.y + y * cs.x;
+            }
+            if (n >= a.T) continue;
+            if (head < R.n_heads) {
+              R.q_out[((size_t)n * R.n_heads + head) * 128 + m] = y;
+              continue;
+            }
+            const int64_t slot = R.slots[n];
+            if (slot < 0) continue;
+            const int64_t blk = slot / R.block_size, off = slot % R.block_size;
+            if (blk >= R.num_blocks) {
+              set_error(a.err, kErrBounds);
+              continue;
+            }
+            const int kvh = is_v ? head - R.n_heads - R.n_kv : head - R.n_heads;
+            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(R.kv) +
+                ((((size_t)blk * 2 + (is_v ? 1 : 0)) * R.n_kv + kvh) * R.block_size + off) * 128 + m;
+            *dst = f2bf(y);
+          }
+          asm volatile("bar.sync %0, 128;" ::"r"(2 + jh) : "memory");   // xb is reused next
+          continue;
+        }
         if (a.mode == kGemmPeerPush) {
           const int ep = *(volatile const int*)a.push.epoch;
 #pragma unroll
@@ -724,9 +767,11 @@ const char* launch_t(const GemmArgs& a, const void* w, int64_t w_row_bytes, cons
   constexpr int NA = (FMT == kFmtQ4K && NT == 128) ? 2 : 4;
   if constexpr (FMT == kFmtQ4K && NT >= 256) {
     // 256-token tiles: A in TMEM only (one 256-column accumulator + two A stage buffers)
+    // 16 dequantising warps (AIR_GEMM_PREFILL_DQ=8 for 8): 4-18 % faster on the Llama-3-8B
+    // shapes at T = 512
     const char* e = getenv("AIR_GEMM_PREFILL_DQ");
-    if (e && atoi(e) == 16) return launch_na<NT, FMT, NA, 16, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
-    return launch_na<NT, FMT, NA, 8, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
+    if (e && atoi(e) == 8) return launch_na<NT, FMT, NA, 8, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
+    return launch_na<NT, FMT, NA, 16, true, 1>(a, w, w_row_bytes, x, ldx, grid, st);
   } else if constexpr (FMT == kFmtQ4K) {
     const int p = a_path();
     if (p == 0) {

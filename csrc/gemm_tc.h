@@ -8,7 +8,22 @@ namespace air {
 
 // kGemmPeerPush: the output is a tensor-parallel partial, stored from the epilogue into the
 // peer receive buffers (PeerPush protocol, comm.h) instead of `out`.
-enum GemmMode : int { kGemmStoreF32 = 0, kGemmStoreBF16 = 1, kGemmResidualF32 = 2, kGemmPeerPush = 3 };
+// kGemmQkvRope: the output rows are [q heads | k heads | v heads] of head_dim 128 (one head per
+// 128-row tile); the epilogue adds the optional bias, applies NeoX RoPE to q and k, writes q
+// (fp32) and k, v into the paged KV cache (bf16) instead of `out`.
+enum GemmMode : int { kGemmStoreF32 = 0, kGemmStoreBF16 = 1, kGemmResidualF32 = 2, kGemmPeerPush = 3,
+                      kGemmQkvRope = 4 };
+
+struct GemmRope {
+  const float2* cs;        // [max_pos, rot_dim / 2] (cos, sin)
+  const int* positions;    // [T]
+  const int64_t* slots;    // [T] paged-cache slot (block * block_size + offset); < 0 = skip
+  void* kv;                // layer [num_blocks, 2, n_kv, block_size, 128] bf16
+  float* q_out;            // [T, n_heads, 128]
+  const float* bias;       // optional [(n_heads + 2 n_kv) * 128]
+  int n_heads, n_kv, block_size, rot_dim;
+  int64_t num_blocks;
+};
 
 struct GemmArgs {
   int N, K, T;          // weight rows, reduction length, tokens
@@ -26,6 +41,7 @@ struct GemmArgs {
                         // exit at once (routed-expert GEMMs launched for a capacity)
   PeerPush push;        // kGemmPeerPush destinations
   const void* wscales;  // Q8_0: f16 block scales [N, K/32] (the codes are the weight pointer)
+  GemmRope rope;        // kGemmQkvRope
        // optional per-phase clock64 stamps of CTA (0,0,0) (profiling aid)
 };
 

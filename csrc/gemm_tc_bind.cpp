@@ -12,12 +12,24 @@ namespace {
 void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, int64_t N, int64_t K,
             Tensor x, Tensor out, int64_t mode, int64_t splits, optional<Tensor> ws,
             optional<Tensor> counters, optional<Tensor> err, optional<Tensor> dbg,
-            optional<Tensor> row_count, optional<Tensor> push_meta) {
+            optional<Tensor> row_count, optional<Tensor> push_meta, optional<Tensor> rope_cs,
+            optional<Tensor> positions, optional<Tensor> slots, optional<Tensor> kv, optional<Tensor> q_out,
+            optional<Tensor> qkv_bias, int64_t n_heads, int64_t n_kv, int64_t block_size, int64_t rot_dim) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2, "gemm_q: x must be 2-D bf16 CUDA");
   TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "gemm_q: rows must be contiguous");
   TORCH_CHECK(x.size(1) == K, "gemm_q: x has ", x.size(1), " columns, expected K=", K);
   if (mode == air::kGemmPeerPush) {
     TORCH_CHECK(push_meta.has_value(), "gemm_q peer push: push meta required");
+  } else if (mode == air::kGemmQkvRope) {
+    TORCH_CHECK(rope_cs.has_value() && positions.has_value() && slots.has_value() && kv.has_value() &&
+                    q_out.has_value(), "gemm_q qkv rope: rope table, positions, slots, kv and q_out required");
+    TORCH_CHECK(N == (n_heads + 2 * n_kv) * 128 && rot_dim > 0 && rot_dim <= 128 && rot_dim % 2 == 0,
+                "gemm_q qkv rope: N must be (n_heads + 2 n_kv) x 128 (head_dim 128)");
+    TORCH_CHECK(kv->scalar_type() == at::kBFloat16 && kv->is_contiguous() && q_out->is_contiguous() &&
+                    q_out->scalar_type() == at::kFloat && positions->numel() >= x.size(0) &&
+                    slots->numel() >= x.size(0) && slots->scalar_type() == at::kLong,
+                "gemm_q qkv rope: bf16 contiguous kv, fp32 q_out, int64 slots covering the rows");
+    TORCH_CHECK(!qkv_bias.has_value() || qkv_bias->numel() >= N, "gemm_q qkv rope: bias too short");
   } else if (mode == air::kGemmStoreBF16) {
     TORCH_CHECK(out.scalar_type() == at::kBFloat16, "gemm_q: out must be bf16");
   } else {
@@ -44,6 +56,19 @@ void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, i
   a.dbg = dbg.has_value() ? (long long*)dbg->data_ptr<int64_t>() : nullptr;
   a.row_count = row_count.has_value() ? row_count->data_ptr<int>() : nullptr;
   a.wscales = (scales.has_value() && scales->defined()) ? scales->data_ptr() : nullptr;
+  if (mode == air::kGemmQkvRope) {
+    a.rope.cs = static_cast<const float2*>(rope_cs->data_ptr());
+    a.rope.positions = positions->data_ptr<int>();
+    a.rope.slots = slots->data_ptr<int64_t>();
+    a.rope.kv = kv->data_ptr();
+    a.rope.q_out = q_out->data_ptr<float>();
+    a.rope.bias = qkv_bias.has_value() ? qkv_bias->data_ptr<float>() : nullptr;
+    a.rope.n_heads = (int)n_heads;
+    a.rope.n_kv = (int)n_kv;
+    a.rope.block_size = (int)block_size;
+    a.rope.rot_dim = (int)rot_dim;
+    a.rope.num_blocks = kv->size(0);
+  }
   if (mode == air::kGemmPeerPush) {
     a.push = peer_push_from_meta(*push_meta);
     TORCH_CHECK(a.N == a.push.row_len && (int64_t)a.T * a.push.row_len <= a.push.slot_elems,
