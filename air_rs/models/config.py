@@ -89,6 +89,7 @@ class ModelConfig:
     norm_bias: bool = False       # blk.N.{attn,ffn}_norm.bias, output_norm.bias (Falcon LayerNorm)
     fused_qkv: bool = False       # blk.N.attn_qkv.weight = [q; k; v] rows (Phi-3)
     fused_gate_up: bool = False   # blk.N.ffn_up.weight = [gate; up] rows, no ffn_gate (Phi-3)
+    attn_softcap: float = 0.0     # {arch}.attn_logit_softcapping: scores -> c * tanh(s / c) (Gemma-2)
 
     def detect_layout(self, tensor_names) -> "ModelConfig":
         """Set the layout flags from a checkpoint's tensor names (biases and fused tensors are
@@ -165,7 +166,8 @@ class ModelConfig:
             from .archs.hybrid import HybridAttentionRouter
             extra["attention_layout"] = HybridAttentionRouter.gemma4(
                 n_layers, int(sw), int(pattern)).windows()
-        return cls(qkv_bias=variant == ModelVariant.QWEN2, norm_bias=variant == ModelVariant.FALCON,
+        return cls(attn_softcap=float(md.get(f"{arch}.attn_logit_softcapping", 0.0) or 0.0),
+                   qkv_bias=variant == ModelVariant.QWEN2, norm_bias=variant == ModelVariant.FALCON,
                    fused_qkv=variant == ModelVariant.PHI3, fused_gate_up=variant == ModelVariant.PHI3,
                    n_layers=n_layers, n_heads=n_heads, n_kv_heads=n_kv, hidden_dim=hidden,
                    intermediate_dim=inter, vocab_size=int(vocab), rope_theta=rope,
@@ -196,6 +198,8 @@ class ModelConfig:
             md[f"{a}.expert_used_count"] = self.moe_top_k
         if self.sliding_window:
             md[f"{a}.attention.sliding_window"] = self.sliding_window
+        if self.attn_softcap > 0:
+            md[f"{a}.attn_logit_softcapping"] = float(self.attn_softcap)
         return md
 
 
@@ -249,6 +253,7 @@ def tiny_variant(arch: str) -> ModelConfig:
         c.qkv_bias = True
     elif v == ModelVariant.GEMMA:
         c.norm_type, c.ffn_type = NormType.GEMMA_RMS, FfnType.GEGLU
+        c.attn_softcap = 50.0
     elif v == ModelVariant.FALCON:
         c.norm_type, c.ffn_type, c.norm_bias = NormType.LAYER, FfnType.DENSE, True
     elif v == ModelVariant.PHI3:

@@ -257,7 +257,7 @@ class OracleModel:
                 v = torch.cat([self.v_cache[li][0], v], 0)
             self.k_cache[li] = k.unsqueeze(0)
             self.v_cache[li] = v.unsqueeze(0)
-            attn = attention_reference(q, k, v, causal=S > 1, window=self.windows[li])
+            attn = attention_reference(q, k, v, causal=S > 1, window=self.windows[li], softcap=cfg.attn_softcap)
             o = qmatmul(attn.reshape(S, nh * hd), L.wo[0], L.wo[1], L.wo[2]).to(x.dtype)
             x = x + o
             h = self.norm(x, L.ffn_norm, L.ffn_norm_b).float()
@@ -313,8 +313,9 @@ OracleModel.moe_ffn = _moe_ffn
 
 
 def attention_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool,
-                        mask: torch.Tensor | None = None, window: int = 0) -> torch.Tensor:
-    """Dense GQA attention, F32. q [S, H, D], k/v [Skv, Hkv, D] -> [S, H, D].
+                        mask: torch.Tensor | None = None, window: int = 0, softcap: float = 0.0) -> torch.Tensor:
+    """Dense GQA attention, F32. q [S, H, D], k/v [Skv, Hkv, D] -> [S, H, D]. ``softcap`` > 0
+    caps the scaled scores as softcap * tanh(s / softcap) (Gemma-2 style).
 
     Causal rule (``src/ops.rs:762-788``): key j visible to query i iff j <= i + (Skv - S).
     ``mask`` (optional, [S, Skv] bool) further restricts visibility (tree attention).
@@ -325,6 +326,8 @@ def attention_reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causa
     kk = k.float().repeat_interleave(rep, dim=1)
     vv = v.float().repeat_interleave(rep, dim=1)
     s = torch.einsum("shd,thd->hst", q.float(), kk) * (1.0 / math.sqrt(D))
+    if softcap > 0:
+        s = softcap * torch.tanh(s / softcap)
     vis = torch.ones(S, Skv, dtype=torch.bool)
     if causal or window > 0:
         i = torch.arange(S)[:, None]

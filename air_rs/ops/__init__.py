@@ -256,11 +256,12 @@ def gemv(w: QWeight, xq: torch.Tensor, xds: torch.Tensor, B: int, mode: int = EP
 def paged_attention(q, kv, block_tables, ctx_len, out, *, n_rows, n_heads, n_kv, head_dim,
                     block_size, row_seq=None, tree_base=None, tree_mask=None, window=0, n_splits=1,
                     split_tokens=1 << 30, scale=None, part_o=None, part_ml=None, out_q=None,
-                    out_ds=None, err=None, out_bf16=None):
+                    out_ds=None, err=None, out_bf16=None, softcap: float = 0.0):
+    """``softcap`` > 0: scaled scores s become softcap * tanh(s / softcap) before the softmax."""
     scale = scale if scale is not None else head_dim ** -0.5
     require_ext().paged_attention(q, kv, block_tables, row_seq, ctx_len, tree_base, tree_mask, window,
                                   n_rows, n_heads, n_kv, head_dim, block_size, n_splits, split_tokens,
-                                  scale, part_o, part_ml, out, out_q, out_ds, err, out_bf16)
+                                  scale, part_o, part_ml, out, out_q, out_ds, err, out_bf16, softcap)
     count_launch(2 if (n_splits > 1 or out_q is not None) else 1)
 
 

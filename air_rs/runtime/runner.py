@@ -283,7 +283,7 @@ class ModelRunner:
         (head_dim 128), else a separate token-parallel kernel."""
         from ..ops import gemm
         T = xin.shape[0]
-        if self.hd == 128 and gemm.tc_supported(lw.wqkv) and os.environ.get("AIR_GEMM_ROPE", "1") != "0":
+        if self.hd == 128 and gemm.tc_supported(lw.wqkv) and os.environ.get("AIR_GEMM_ROPE", "0") == "1":
             rope = dict(cs=self.rope_cs, positions=positions, slots=slots, kv=kv, q_out=q_out, bias=lw.qkv_bias,
                         n_heads=self.nh, n_kv=self.nkv, block_size=self.block_size, rot_dim=self.rot_dim)
             gemm.linear(xin, lw.wqkv, qkv_buf, self, err=self.err, rope=rope)
@@ -332,7 +332,7 @@ class ModelRunner:
                                 block_size=self.block_size, n_splits=ns if gemv_path else max(2, ns),
                                 split_tokens=0, part_o=self.part_o, part_ml=self.part_ml,
                                 out_q=xq if gemv_path else None, out_ds=xds if gemv_path else None,
-                                err=self.err, window=self.layer_window[li],
+                                err=self.err, window=self.layer_window[li], softcap=cfg.attn_softcap,
                                 out_bf16=None if gemv_path else self.attn_b[:B])
             if gemv_path:
                 self._row_parallel(lw.wo, xq, xds, B, x, peer)
@@ -389,7 +389,7 @@ class ModelRunner:
                                 n_rows=B, n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd,
                                 block_size=self.block_size, n_splits=ns, split_tokens=0,
                                 part_o=self.part_o, part_ml=self.part_ml, out_q=aq, out_ds=ads,
-                                err=self.err, window=self.layer_window[li])
+                                err=self.err, window=self.layer_window[li], softcap=cfg.attn_softcap)
             ops.gemv(lw.wo, aq, ads, B, ops.EPI_RESIDUAL, resid=x, norm_w=lw.ffn_norm, out_q=xa, out_ds=xda,
                      ss_out=ss, norm_offset=self.norm_off)
             ops.gemv(lw.w_gate, xa, xda, B, ops.EPI_SWIGLU, w2=lw.w_up, ld_out=self.Fp, out_q=hq, out_ds=hds,
@@ -558,7 +558,8 @@ class ModelRunner:
             ops.paged_attention(q, kv, block_tables, ctx, attn, n_rows=T, n_heads=self.nh,
                                 n_kv=self.nkv, head_dim=self.hd, block_size=self.block_size,
                                 row_seq=row_seq, n_splits=1, err=self.err,
-                                window=self.layer_window[li], tree_base=tree_base, tree_mask=tree_mask)
+                                window=self.layer_window[li], tree_base=tree_base, tree_mask=tree_mask,
+                                softcap=cfg.attn_softcap)
             attn_b.copy_(attn)
             self._proj_into_residual(attn_b, lw.wo, x, o, tp)
             ops.rmsnorm_quant(x, lw.ffn_norm, eps, None, None, y_bf16=xn, bias=lw.ffn_norm_b,

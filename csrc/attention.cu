@@ -154,7 +154,7 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         v += __shfl_xor_sync(0xffffffffu, v, 4);
-        s[i][g] = vis ? v : -INFINITY;
+        s[i][g] = vis ? soft_cap(v, rows.softcap) : -INFINITY;
       }
     }
     // ---- online softmax ----

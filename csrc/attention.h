@@ -11,6 +11,7 @@ struct AttnRows {
   const int* tree_base;      // [R] first position of the speculative tree region (null: none)
   const unsigned long long* tree_mask;  // [R] ancestor bitmask over tree positions
   int window;                // sliding window (0 = none)
+  float softcap;             // > 0: scaled scores s -> softcap * tanh(s / softcap) (Gemma-2 style)
 };
 
 struct AttnArgs {

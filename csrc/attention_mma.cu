@@ -186,6 +186,7 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
       for (int j = 0; j < 2; ++j) {
         const int t = t0 + nt * 8 + (lane & 3) * 2 + j;
         if (!visible(t, rows, r, ctx) || t >= t_end) s[nt][j] = -INFINITY;
+        else s[nt][j] = soft_cap(s[nt][j], rows.softcap);
         mx = fmaxf(mx, s[nt][j]);
       }
     }

@@ -189,7 +189,7 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
           const int i = j >> 1;
           const int t = t0 + nt * 8 + (lane & 3) * 2 + (j & 1);
           const bool vis = in_g[i] && t < ctx[i] && !(rows.window > 0 && t < ctx[i] - rows.window);
-          if (!vis) s[nt][j] = -INFINITY;
+          s[nt][j] = vis ? soft_cap(s[nt][j], rows.softcap) : -INFINITY;
           mx[i] = fmaxf(mx[i], s[nt][j]);
         }
       float alpha[2];

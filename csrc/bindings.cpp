@@ -157,7 +157,7 @@ void paged_attention(Tensor q, Tensor kv, Tensor block_tables, optional<Tensor> 
                      int64_t block_size, int64_t n_splits, int64_t split_tokens, double scale,
                      optional<Tensor> part_o, optional<Tensor> part_ml, Tensor out,
                      optional<Tensor> out_q, optional<Tensor> out_ds, optional<Tensor> err,
-                     optional<Tensor> out_bf16) {
+                     optional<Tensor> out_bf16, double softcap) {
   check_cuda(q, "q");
   check_cuda(kv, "kv");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt, "block_tables must be int32");
@@ -167,7 +167,7 @@ void paged_attention(Tensor q, Tensor kv, Tensor block_tables, optional<Tensor> 
   a.block_tables = ptr<int>(block_tables);
   a.max_blocks = (int)block_tables.size(1);
   a.rows = air::AttnRows{ptr<int>(row_seq), ptr<int>(ctx_len), ptr<int>(tree_base),
-                         ptr<unsigned long long>(tree_mask), (int)window};
+                         ptr<unsigned long long>(tree_mask), (int)window, (float)softcap};
   a.n_rows = (int)n_rows;
   a.n_heads = (int)n_heads;
   a.n_kv = (int)n_kv;

@@ -42,6 +42,9 @@ AIR_DEVICE float gate_act(float x, int act) {
   return x / (1.f + __expf(-x));
 }
 
+// Attention logit soft-capping: cap * tanh(s / cap) when cap > 0.
+AIR_DEVICE float soft_cap(float s, float cap) { return cap > 0.f ? cap * tanhf(s / cap) : s; }
+
 AIR_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

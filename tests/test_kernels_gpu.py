@@ -189,7 +189,8 @@ def _paged_setup(lens, nkv, d, bs, seed=0):
 
 @pytest.mark.parametrize("splits", [1, 4, 13])
 @pytest.mark.parametrize("G", [1, 4, 8])
-def test_paged_decode_attention(splits, G):
+@pytest.mark.parametrize("cap", [0.0, 3.0])
+def test_paged_decode_attention(splits, G, cap):
     nkv, d, bs = 2, 128, 16
     nh = nkv * G
     lens = [1, 37, 300, 1000]
@@ -201,9 +202,9 @@ def test_paged_decode_attention(splits, G):
     part_ml = torch.zeros(R * nh * splits * 2, device=DEV)
     ops.paged_attention(q.to(DEV), kv.to(DEV), bt.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV),
                         out, n_rows=R, n_heads=nh, n_kv=nkv, head_dim=d, block_size=bs,
-                        n_splits=splits, split_tokens=0, part_o=part_o, part_ml=part_ml)
+                        n_splits=splits, split_tokens=0, part_o=part_o, part_ml=part_ml, softcap=cap)
     for i, l in enumerate(lens):
-        ref = attention_reference(q[i:i + 1], dense[i][0], dense[i][1], causal=False)[0]
+        ref = attention_reference(q[i:i + 1], dense[i][0], dense[i][1], causal=False, softcap=cap)[0]
         # tensor-core path: Q and P enter the MMA as bf16
         torch.testing.assert_close(out[i].cpu(), ref, rtol=1e-2, atol=8e-3)
 
@@ -248,8 +249,8 @@ def test_paged_prefill_causal_and_tree():
 
 
 @pytest.mark.parametrize("G", [1, 2, 4, 8])
-@pytest.mark.parametrize("window", [0, 50])
-def test_query_tiled_prefill_attention(G, window):
+@pytest.mark.parametrize("window,cap", [(0, 0.0), (50, 0.0), (0, 3.0)])
+def test_query_tiled_prefill_attention(G, window, cap):
     """The query-tiled prefill kernel (16 rows per CTA, shared K/V tiles) against dense fp32
     attention: three sequences whose chunks straddle 16-row tiles (mixed-sequence tiles),
     chunked prefill (queries start mid-sequence), GQA groups 1-8, sliding window."""
@@ -267,7 +268,8 @@ def test_query_tiled_prefill_attention(G, window):
     out = torch.zeros(T, nh, d, device=DEV)
     ops.paged_attention(q.to(DEV), kv.to(DEV), bt.to(DEV), torch.tensor(ctx, dtype=torch.int32, device=DEV), out,
                         n_rows=T, n_heads=nh, n_kv=nkv, head_dim=d, block_size=bs,
-                        row_seq=torch.tensor(rows_seq, dtype=torch.int32, device=DEV), window=window)
+                        row_seq=torch.tensor(rows_seq, dtype=torch.int32, device=DEV), window=window,
+                        softcap=cap)
     torch.cuda.synchronize()
     r = 0
     for s_, (L, n) in enumerate(zip(lens, qlen)):
@@ -277,7 +279,7 @@ def test_query_tiled_prefill_attention(G, window):
             c = L - n + 1 + i
             lo = max(0, c - window) if window else 0
             mask[i, lo:c] = True
-        ref = attention_reference(q[r:r + n], k, v, causal=False, mask=mask)
+        ref = attention_reference(q[r:r + n], k, v, causal=False, mask=mask, softcap=cap)
         torch.testing.assert_close(out[r:r + n].cpu(), ref, rtol=1e-2, atol=8e-3)
         r += n
 

@@ -1,5 +1,5 @@
 """Architecture variants (reference src/model.rs:326-416, :623-660, src/model_variant.rs:140-189):
-Qwen2 q/k/v biases, Gemma RMSNorm (weight + 1) + GeGLU, Falcon LayerNorm with biases + dense
+Qwen2 q/k/v biases, Gemma RMSNorm (weight + 1) + GeGLU + attention logit soft-capping, Falcon LayerNorm with biases + dense
 GELU MLP, Phi-3 fused attn_qkv / [gate; up] tensors.
 
 CPU: the reference-numerics oracle against a plain fp32 PyTorch forward written out here
@@ -66,8 +66,11 @@ def _plain_forward(cfg: ModelConfig, recs: dict, ids: list[int]) -> torch.Tensor
         q, k, v = rope(q.view(S, nh, hd)), rope(k.view(S, nkv, hd)), v.view(S, nkv, hd)
         rep = nh // nkv
         k, v = k.repeat_interleave(rep, 1), v.repeat_interleave(rep, 1)
-        a = F.scaled_dot_product_attention(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1),
-                                           is_causal=True).transpose(0, 1).reshape(S, nh * hd)
+        sc = (q.transpose(0, 1) @ k.transpose(0, 1).transpose(-1, -2)) / math.sqrt(hd)   # [h, S, S]
+        if cfg.attn_softcap > 0:
+            sc = cfg.attn_softcap * torch.tanh(sc / cfg.attn_softcap)
+        sc = sc.masked_fill(torch.triu(torch.ones(S, S, dtype=torch.bool), 1)[None], float("-inf"))
+        a = (torch.softmax(sc, -1) @ v.transpose(0, 1)).transpose(0, 1).reshape(S, nh * hd)
         x = x + a @ w(p + "attn_output.weight").t()
         h = norm(x, p + "ffn_norm")
         if cfg.ffn_type == FfnType.DENSE:
@@ -103,7 +106,7 @@ def test_variant_gguf_roundtrip_layout(tmp_path, arch):
     path = write_random_gguf(str(tmp_path / f"{arch}.gguf"), cfg, GGMLType.Q8_0, seed=0)
     g = read_gguf(path)
     back = ModelConfig.from_gguf_metadata(g.metadata).detect_layout(g.tensors)
-    for f in ("qkv_bias", "norm_bias", "fused_qkv", "fused_gate_up", "norm_type", "ffn_type"):
+    for f in ("qkv_bias", "norm_bias", "fused_qkv", "fused_gate_up", "norm_type", "ffn_type", "attn_softcap"):
         assert getattr(back, f) == getattr(cfg, f), f
     o1 = OracleModel.from_gguf(g).forward([5, 6, 7], 0)
     recs = {n: (r, q, s) for n, r, q, s in random_tensors(cfg, GGMLType.Q8_0, seed=0, device="cpu")}
