@@ -14,7 +14,7 @@ import torch
 
 from . import QWeight, require_ext, FMT_BF16, FMT_FP8, FMT_Q4K, FMT_Q8_0, count_launch
 
-GEMM_STORE_F32, GEMM_STORE_BF16, GEMM_RESIDUAL, GEMM_PEER_PUSH, GEMM_QKV_ROPE = 0, 1, 2, 3, 4
+GEMM_STORE_F32, GEMM_STORE_BF16, GEMM_RESIDUAL, GEMM_PEER_PUSH = 0, 1, 2, 3
 
 
 def _baseline_forced() -> bool:
@@ -73,22 +73,17 @@ def workspace(device) -> _Workspace:
 def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, residual: bool = False,
            splits: int | None = None, err: torch.Tensor | None = None,
            dbg: torch.Tensor | None = None, row_count: torch.Tensor | None = None,
-           push_meta: torch.Tensor | None = None, rope: dict | None = None) -> torch.Tensor:
+           push_meta: torch.Tensor | None = None) -> torch.Tensor:
     """out = x @ W^T (or out += x @ W^T when residual, out fp32). ``row_count`` (device int32)
     limits the tensor-core path to the first rows (token tiles past it exit at once).
     ``push_meta`` (a ``PeerComm`` push table): the epilogue stores the result into the
-    tensor-parallel peer receive buffers instead of ``out`` (tensor-core path only).
-    ``rope`` (dict: cs, positions, slots, kv, q_out, bias, n_heads, n_kv, block_size, rot_dim):
-    the rows are q|k|v heads of head_dim 128; the epilogue adds the bias, applies RoPE and
-    writes q to ``q_out`` and k, v into the paged cache (``out`` is not written)."""
+    tensor-parallel peer receive buffers instead of ``out`` (tensor-core path only)."""
     T = x.shape[0]
     if T == 0:
         return out
     if tc_supported(w):
         ext = require_ext()
-        if rope is not None:
-            mode = GEMM_QKV_ROPE
-        elif push_meta is not None:
+        if push_meta is not None:
             mode = GEMM_PEER_PUSH
         elif residual:
             mode = GEMM_RESIDUAL
@@ -101,15 +96,12 @@ def linear(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None, *, resid
                                                  ext.gemm_q_counters(w.N, T))
         if err is None:
             err = workspace(x.device).err
-        r = rope or {}
         ext.gemm_q(w.fmt, w.data, w.scales, w.row_bytes, w.N, w.K, x, out, mode, s, ws, cnt, err, dbg, row_count,
-                   push_meta, r.get("cs"), r.get("positions"), r.get("slots"), r.get("kv"), r.get("q_out"),
-                   r.get("bias"), r.get("n_heads", 0), r.get("n_kv", 0), r.get("block_size", 0),
-                   r.get("rot_dim", 0))
+                   push_meta)
         count_launch()
         return out
-    if push_meta is not None or rope is not None:
-        raise ValueError("peer-push / RoPE GEMM epilogues need the tensor-core path")
+    if push_meta is not None:
+        raise ValueError("peer-push GEMM epilogue needs the tensor-core path")
     if residual:
         tmp = linear_baseline(x, w, torch.empty(T, w.N, dtype=torch.float32, device=x.device), runner)
         out.add_(tmp)
@@ -133,4 +125,22 @@ def linear_baseline(x: torch.Tensor, w: QWeight, out: torch.Tensor, runner=None)
         torch.matmul(x, wt.t(), out=out)
     else:
         out.copy_(torch.matmul(x, wt.t()))
+    return out
+
+
+def linear_grouped(x: torch.Tensor, ws: list, out: torch.Tensor, row_counts: torch.Tensor, rows: int,
+                   err: torch.Tensor | None = None) -> torch.Tensor:
+    """One tcgen05 launch over up to 8 weights of one shape (routed experts): group g computes
+    out[g*rows : g*rows + row_counts[g]] = x[same rows] @ W_g^T (row_counts on the device;
+    token tiles past a group's count exit at once)."""
+    if not ws:
+        return out
+    w0 = ws[0]
+    if any(w.fmt != w0.fmt or w.N != w0.N or w.K != w0.K or w.row_bytes != w0.row_bytes for w in ws):
+        raise ValueError("grouped GEMM: weights must share format and shape")
+    if err is None:
+        err = workspace(x.device).err
+    require_ext().gemm_q_grouped(w0.fmt, [w.data for w in ws], [w.scales for w in ws], w0.row_bytes, w0.N, w0.K,
+                                 x, rows, out, row_counts, err)
+    count_launch()
     return out

@@ -8,10 +8,13 @@ has no host round trip and stays CUDA-graph capturable.
 * Decode GEMV path (B <= 8): each local expert's SwiGLU FFN runs over the batch with the
   fused GEMV kernels (weights are read once either way) and ``moe_combine`` adds
   ``cw[:, e] * y_e`` (zero-weight rows skipped).
-* Batched / prefill path: per local expert, ``moe_select`` lists the tokens routed to it,
-  ``moe_gather`` packs their rows, the tcgen05 GEMMs run on that group only (token tiles past
-  the device-side count exit at once — launches keep a fixed shape), and ``moe_scatter``
-  adds the weighted outputs back.
+* Batched / prefill path: up to eight local experts at a time, ``moe_select_grouped`` lists
+  each expert's tokens, ``moe_gather_grouped`` packs their rows into one buffer (expert g at
+  rows g*T..), ONE grouped tcgen05 GEMM runs gate|up for every expert of the group and one
+  runs down (token tiles past an expert's device-side count exit at once — fixed launch
+  shapes, graph capturable), SwiGLU runs over the packed rows, and ``moe_scatter_grouped``
+  adds each token's weighted expert outputs in expert order. Per-expert launches remain for
+  host-resident experts (expert cache) and formats without a tensor-core kernel.
 
 Expert parallelism: under TP the experts are spread over the ranks (expert e on rank
 e % tp) while attention stays tensor parallel, so every rank holds every token's
@@ -85,7 +88,58 @@ def moe_ffn_decode(rn, lw, B, x, xq, xds, peer=None):
         _finish(rn, B, x, acc, peer)
 
 
-def _ffn_tokens(rn, lw, T, x, xn, bufs, peer=None):
+GROUP = 8      # experts per grouped launch (the GEMM's group limit)
+
+
+def _grouped_ok(rn, lw) -> bool:
+    """All local experts resident and on the tensor-core GEMM: one launch per group of 8."""
+    import os
+    from ..ops import gemm
+    if getattr(rn, "expert_cache", None) is not None or os.environ.get("AIR_MOE_GROUPED", "1") == "0":
+        return False
+    ws = list(lw.experts_gu) + list(lw.experts_down)
+    return bool(ws) and all(gemm.tc_supported(w) for w in ws)
+
+
+def _ffn_tokens_grouped(rn, lw, T, x, xn, cw, acc, alloc, prefix):
+    """Routed experts in groups of up to GROUP: grouped select / gather, one grouped GEMM for
+    gate|up and one for down over every expert of the group, SwiGLU over the packed rows, and
+    a grouped scatter that adds each token's expert outputs in a fixed order."""
+    from ..ops import gemm
+    ext = ops.require_ext()
+    ids = _ids(lw)
+    gid_cache = getattr(lw, "_group_ids", None)
+    if gid_cache is None:
+        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("MoE group ids must be staged before CUDA-graph capture")
+        gid_cache = lw._group_ids = [torch.tensor(ids[i:i + GROUP], dtype=torch.int32, device=rn.device)
+                                     for i in range(0, len(ids), GROUP)]
+    G = min(GROUP, len(ids))
+    # decode buffers are sized once for the largest batch (a captured graph keeps pointers)
+    cap = rn.max_batch if prefix == "moe_d_" else T
+    idx = alloc(prefix + "gidx", (G * cap,), torch.int32)
+    wts = alloc(prefix + "gwts", (G * cap,), torch.float32)
+    pos = alloc(prefix + "gpos", (G * cap,), torch.int32)
+    cnt = alloc(prefix + "gcnt", (G,), torch.int32)
+    xg = alloc(prefix + "gxg", (G * cap, rn.H), torch.bfloat16)
+    gu_buf = alloc(prefix + "ggu", (G * cap, rn.gu_w), torch.bfloat16)
+    h_buf = alloc(prefix + "gh", (G * cap, rn.Fp), torch.bfloat16)
+    y_buf = alloc(prefix + "gy", (G * cap, rn.H), torch.float32)
+    up_off = lw.experts_gu[0].parts[1][0]
+    for c, gids in enumerate(gid_cache):
+        g = gids.numel()
+        gu_w = lw.experts_gu[c * GROUP:c * GROUP + g]
+        dn_w = lw.experts_down[c * GROUP:c * GROUP + g]
+        ext.moe_select_grouped(cw[:T], gids, T, idx, wts, cnt, pos)
+        ext.moe_gather_grouped(xn[:T], idx, cnt, g, T, xg)
+        gemm.linear_grouped(xg, gu_w, gu_buf, cnt, T, err=rn.err)
+        ops.swiglu(gu_buf[:g * T], g * T, rn.F, out_bf16=h_buf[:g * T], ld_out=rn.Fp, up_off=up_off, act=rn.act)
+        gemm.linear_grouped(h_buf, dn_w, y_buf, cnt, T, err=rn.err)
+        ext.moe_scatter_grouped(acc[:T], y_buf, pos, wts, g, T)
+        ops.count_launch(3)
+
+
+def _ffn_tokens(rn, lw, T, x, xn, bufs, peer=None, alloc=None, prefix=""):
     ext = ops.require_ext()
     E = rn.cfg.n_experts
     cw, idx, wts, cnt, xg, gu_buf, h_buf, y_buf = (bufs[k] for k in ("cw", "idx", "wts", "cnt", "xg", "gu", "h", "y"))
@@ -95,6 +149,11 @@ def _ffn_tokens(rn, lw, T, x, xn, bufs, peer=None):
     acc = bufs["part"] if ep else x
     if ep:
         acc[:T].zero_()
+    if alloc is not None and _grouped_ok(rn, lw):
+        _ffn_tokens_grouped(rn, lw, T, x, xn, cw, acc, alloc, prefix)
+        if ep:
+            _finish(rn, T, x, acc, peer)
+        return
     for j, (gu, dn, e) in enumerate(_experts(rn, lw, cw, T)):
         c = cnt[j:j + 1]
         ext.moe_select(cw[:T], e, T, idx, wts, c)
@@ -123,10 +182,12 @@ def _bufs(rn, T, prefix, alloc):
 
 def moe_ffn_gemm(rn, lw, B, x, peer=None):
     """Batched decode (GEMM path): input is ``rn.xn_b[:B]`` (bf16, normalised)."""
-    bufs = _bufs(rn, rn.max_batch, "moe_d_", lambda n, s, d: _ensure(rn, n, s, d))
-    _ffn_tokens(rn, lw, B, x, rn.xn_b, bufs, peer)
+    alloc = lambda n, s, d: _ensure(rn, n, s, d)
+    bufs = _bufs(rn, rn.max_batch, "moe_d_", alloc)
+    _ffn_tokens(rn, lw, B, x, rn.xn_b, bufs, peer, alloc=alloc, prefix="moe_d_")
 
 
 def moe_ffn_prefill(rn, lw, T, x, xn):
-    bufs = _bufs(rn, T, "moe_p_", lambda n, s, d: rn._ws(n, s, d, zero=(n.endswith("h"))))
-    _ffn_tokens(rn, lw, T, x, xn, bufs, None)
+    alloc = lambda n, s, d: rn._ws(n, s, d, zero=(n.endswith("h")))
+    bufs = _bufs(rn, T, "moe_p_", alloc)
+    _ffn_tokens(rn, lw, T, x, xn, bufs, None, alloc=alloc, prefix="moe_p_")

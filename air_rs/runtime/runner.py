@@ -279,15 +279,10 @@ class ModelRunner:
                               layer=self.norm_layer)
 
     def _qkv_gemm_rope(self, xin, lw, qkv_buf, positions, slots, kv, q_out):
-        """QKV projection on the GEMM path + RoPE + paged KV write: in the tcgen05 GEMM epilogue
-        (head_dim 128), else a separate token-parallel kernel."""
-        from ..ops import gemm
+        """QKV projection on the GEMM path, then RoPE + paged KV write (token-parallel kernel;
+        folding it into the GEMM epilogue measured slower, the epilogue is serial after the
+        main loop while this kernel overlaps the next launch under PDL)."""
         T = xin.shape[0]
-        if self.hd == 128 and gemm.tc_supported(lw.wqkv) and os.environ.get("AIR_GEMM_ROPE", "0") == "1":
-            rope = dict(cs=self.rope_cs, positions=positions, slots=slots, kv=kv, q_out=q_out, bias=lw.qkv_bias,
-                        n_heads=self.nh, n_kv=self.nkv, block_size=self.block_size, rot_dim=self.rot_dim)
-            gemm.linear(xin, lw.wqkv, qkv_buf, self, err=self.err, rope=rope)
-            return
         self.linear(xin, lw.wqkv, qkv_buf)
         ops.rope_kv(qkv_buf, T, self.rope_cs, positions, slots, kv, q_out, n_heads=self.nh, n_kv=self.nkv,
                     head_dim=self.hd, block_size=self.block_size, rot_dim=self.rot_dim, err=self.err,

@@ -282,6 +282,34 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                             (int)E, (int)T, (int)x.size(1), stream());
     post_launch("moe_combine");
   });
+  m.def("moe_select_grouped", [](Tensor cw, Tensor experts, int64_t T, Tensor idx, Tensor wts, Tensor count,
+                                  Tensor pos) {
+    const int G = (int)experts.numel();
+    TORCH_CHECK(cw.is_cuda() && cw.scalar_type() == torch::kFloat && cw.dim() == 2, "moe_select_grouped: cw [T, E]");
+    TORCH_CHECK(experts.is_cuda() && experts.scalar_type() == torch::kInt && idx.numel() >= G * T &&
+                    wts.numel() >= G * T && count.numel() >= G && pos.numel() >= G * T,
+                "moe_select_grouped: buffers of G * T rows");
+    air::launch_moe_select_grouped(cw.data_ptr<float>(), experts.data_ptr<int>(), G, (int)cw.size(1), (int)T,
+                                   idx.data_ptr<int>(), wts.data_ptr<float>(), count.data_ptr<int>(),
+                                   pos.data_ptr<int>(), stream());
+    post_launch("moe_select_grouped");
+  });
+  m.def("moe_gather_grouped", [](Tensor x, Tensor idx, Tensor count, int64_t G, int64_t T, Tensor xg) {
+    const int64_t H = x.size(1);
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16 && xg.scalar_type() == at::kBFloat16 && H % 8 == 0 &&
+                    x.stride(0) % 8 == 0 && xg.size(1) == H && xg.size(0) >= G * T && xg.is_contiguous(),
+                "moe_gather_grouped: bf16 rows");
+    air::launch_moe_gather_grouped(x.data_ptr(), x.stride(0), (int)H, idx.data_ptr<int>(), count.data_ptr<int>(),
+                                   (int)G, (int)T, xg.data_ptr(), stream());
+    post_launch("moe_gather_grouped");
+  });
+  m.def("moe_scatter_grouped", [](Tensor out, Tensor y, Tensor pos, Tensor wts, int64_t G, int64_t T) {
+    TORCH_CHECK(out.scalar_type() == torch::kFloat && y.scalar_type() == torch::kFloat && out.is_contiguous() &&
+                    y.size(0) >= G * T && y.stride(1) == 1, "moe_scatter_grouped: fp32 out / y");
+    air::launch_moe_scatter_grouped(out.data_ptr<float>(), y.data_ptr<float>(), y.stride(0), (int)out.size(1),
+                                    pos.data_ptr<int>(), wts.data_ptr<float>(), (int)G, (int)T, stream());
+    post_launch("moe_scatter_grouped");
+  });
   m.def("moe_select", [](Tensor cw, int64_t e, int64_t T, Tensor idx, Tensor wts, Tensor count) {
     TORCH_CHECK(cw.is_cuda() && cw.scalar_type() == torch::kFloat && cw.dim() == 2, "moe_select: cw [T, E] fp32");
     TORCH_CHECK(idx.numel() >= T && wts.numel() >= T && count.numel() >= 1, "moe_select: buffers");

@@ -84,6 +84,12 @@ struct Cfg {
   static constexpr int kSmemLaunch = AT ? kSmemAT : kSmem;
 };
 
+// Per-group weight tensor maps of a grouped launch (unused otherwise).
+struct GroupMaps {
+  CUtensorMap w[kGemmMaxGroups];
+  CUtensorMap s[kGemmMaxGroups];
+};
+
 struct Bars {
   uint64_t full[12];
   uint64_t empty[12];
@@ -125,8 +131,9 @@ __device__ __forceinline__ uint32_t q4_pair(uint32_t t, __nv_bfloat162 s, __nv_b
 
 template <int NT, int FMT, int NA, int DQ, bool AT, int NACC, int CPS>
 __global__ void __launch_bounds__((AT ? 96 : 64) + 32 * DQ, CPS)
-gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
-              const __grid_constant__ CUtensorMap tm_s, GemmArgs a) {
+gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_x,
+              const __grid_constant__ CUtensorMap tm_s0, const __grid_constant__ GroupMaps gm,
+              const __grid_constant__ GemmArgs a) {
   using C = Cfg<NT, FMT, NA, AT, NACC, CPS>;
   static_assert(!AT || FMT == kFmtQ4K || FMT == kFmtQ8_0 || FMT == kFmtFP8, "A-in-TMEM path: Q4_K, Q8_0, FP8");
   // Programmatic dependent launch: this grid may start while the previous kernel finishes.
@@ -136,9 +143,19 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
   // everything when a device row count gates the tiles.
   if (a.row_count != nullptr) pdl_wait();
   pdl_trigger();
+  // grouped launch: this CTA's group (routed expert), its token tile and row range
+  const bool grouped = a.groups > 0;
+  const int grp = grouped ? (int)blockIdx.y / a.tiles_per_group : 0;
+  const int ty = grouped ? (int)blockIdx.y % a.tiles_per_group : (int)blockIdx.y;
+  const int rowbase = grouped ? grp * a.group_rows : 0;     // first x / out row of the group
+  const int T_lim = grouped ? a.group_rows : a.T;           // rows of this group
+  const CUtensorMap& tm_w = grouped ? gm.w[grp] : tm_w0;
+  const CUtensorMap& tm_s = grouped ? gm.s[grp] : tm_s0;
+  const uint8_t* wq = grouped ? a.wq_g[grp] : a.wq;
+  const float* wscales_f = static_cast<const float*>(grouped ? a.wscales_g[grp] : a.wscales);
   // routed-expert GEMMs: token tiles beyond the device row count do nothing (uniform per CTA,
   // before any barrier, TMEM allocation or copy)
-  if (a.row_count != nullptr && (int)blockIdx.y * NT >= *(volatile const int*)a.row_count) return;
+  if (a.row_count != nullptr && ty * NT >= *(volatile const int*)(a.row_count + grp)) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -148,7 +165,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
                                           : abuf + C::kABuf);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * 128, n0 = blockIdx.y * NT;
+  const int m0 = blockIdx.x * 128, n0 = ty * NT;   // n0: first token row within the group
   const int split = blockIdx.z, splits = gridDim.z;
   const int ksteps = FMT == kFmtBF16 ? a.K / 64 : a.K / 256;
   const int kper = (ksteps + splits - 1) / splits;
@@ -228,7 +245,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
           if (FMT == kFmtQ8_0) tma_load_2d(st + 2 * kQ8Half, &tm_s, &fullb[s], kb * 8, m0);
         } else if (wprod) {
           // the tile as a.wsplit back-to-back bulk copies (more requests in flight per CTA)
-          const uint8_t* src = a.wq + ((size_t)blockIdx.x * ksteps + kb0 + i) * kRawTile;
+          const uint8_t* src = wq + ((size_t)blockIdx.x * ksteps + kb0 + i) * kRawTile;
           const int np = a.wsplit > 0 ? a.wsplit : 1;
           const uint32_t piece = kRawTile / np;
           for (int p = 0; p < np; ++p) bulk_load(st + p * piece, src + p * piece, piece, &fullb[s]);
@@ -236,7 +253,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
 #pragma unroll
           for (int c = 0; c < C::kXC; ++c) {
             const int ch = i * C::kXC + c;              // chunk index along K
-            tma_load_2d(st + c * C::kBChunk, &tm_x, &fullb[s], (kb0 + ch / 4) * 256 + 64 * (ch % 4), n0);
+            tma_load_2d(st + c * C::kBChunk, &tm_x, &fullb[s], (kb0 + ch / 4) * 256 + 64 * (ch % 4), rowbase + n0);
           }
         }
         issued = i + 1;
@@ -264,13 +281,13 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
         const int kb = kb0 + i;
         if (FMT == kFmtQ4K) {
           // tiled Q4_K: the 128-row x 256-weight tile is 18 KB contiguous -> one bulk copy
-          bulk_load(st, a.wq + ((size_t)blockIdx.x * ksteps + kb) * kRawTile, kRawTile, &bars->full[s]);
+          bulk_load(st, wq + ((size_t)blockIdx.x * ksteps + kb) * kRawTile, kRawTile, &bars->full[s]);
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            tma_load_2d(st + kRawTile + c * C::kBChunk, &tm_x, &bars->full[s], kb * 256 + 64 * c, n0);
+            tma_load_2d(st + kRawTile + c * C::kBChunk, &tm_x, &bars->full[s], kb * 256 + 64 * c, rowbase + n0);
         } else {
           tma_load_2d(st, &tm_w, &bars->full[s], kb * 64, m0);
-          tma_load_2d(st + kATile, &tm_x, &bars->full[s], kb * 64, n0);
+          tma_load_2d(st + kATile, &tm_x, &bars->full[s], kb * 64, rowbase + n0);
         }
         issued = i + 1;
       }
@@ -404,7 +421,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
             const uint4 qa = *reinterpret_cast<const uint4*>(row + ((j0 ^ (r & 7)) << 4));
             const uint4 qb = *reinterpret_cast<const uint4*>(row + (((j0 + 1) ^ (r & 7)) << 4));
             const int grow = m0 + r;
-            const float dq = grow < a.N ? __ldg(static_cast<const float*>(a.wscales) +
+            const float dq = grow < a.N ? __ldg(wscales_f +
                                                (size_t)grow * (a.K / 128) + (kb0 + i) * 2 + (c >> 1))
                                         : 0.f;
             const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
@@ -590,49 +607,6 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] = 0.f;
         }
-        if (a.mode == kGemmQkvRope) {
-          // exchange through shared memory (the consumed stage ring): row m needs row m ^ 64
-          // of the same head for the rotation; the four warps of this column group hold all
-          // 128 rows of the tile
-          float* xb = reinterpret_cast<float*>(stages) + jh * 128 * 16;
-          const GemmRope& R = a.rope;
-          const int head = blockIdx.x;                 // 128-row tile = one head
-          const bool is_v = head >= R.n_heads + R.n_kv;
-          const int i = m & 63;
-          const int rh = R.rot_dim / 2;
-          const float bself = R.bias ? R.bias[mg] : 0.f, bpart = R.bias ? R.bias[mg ^ 64] : 0.f;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) xb[m * 16 + e] = v[e];
-          asm volatile("bar.sync %0, 128;" ::"r"(2 + jh) : "memory");
-#pragma unroll 4
-          for (int e = 0; e < 16; ++e) {
-            const int n = n0 + 16 * j + e;
-            float y = v[e] + bself;
-            if (n < a.T && !is_v && i < rh) {
-              const float p = xb[(m ^ 64) * 16 + e] + bpart;
-              const float2 cs = R.cs[(size_t)R.positions[n] * rh + i];
-              y = m < 64 ? y * cs.x - p * cs.y : p * cs.y + y * cs.x;
-            }
-            if (n >= a.T) continue;
-            if (head < R.n_heads) {
-              R.q_out[((size_t)n * R.n_heads + head) * 128 + m] = y;
-              continue;
-            }
-            const int64_t slot = R.slots[n];
-            if (slot < 0) continue;
-            const int64_t blk = slot / R.block_size, off = slot % R.block_size;
-            if (blk >= R.num_blocks) {
-              set_error(a.err, kErrBounds);
-              continue;
-            }
-            const int kvh = is_v ? head - R.n_heads - R.n_kv : head - R.n_heads;
-            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(R.kv) +
-                ((((size_t)blk * 2 + (is_v ? 1 : 0)) * R.n_kv + kvh) * R.block_size + off) * 128 + m;
-            *dst = f2bf(y);
-          }
-          asm volatile("bar.sync %0, 128;" ::"r"(2 + jh) : "memory");   // xb is reused next
-          continue;
-        }
         if (a.mode == kGemmPeerPush) {
           const int ep = *(volatile const int*)a.push.epoch;
 #pragma unroll
@@ -645,8 +619,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ 
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int n = n0 + 16 * j + e;
-          if (n < a.T && mg < a.N) {
-            const size_t o = (size_t)n * a.ldo + mg;
+          if (n < T_lim && mg < a.N) {
+            const size_t o = (size_t)(rowbase + n) * a.ldo + mg;
             if (a.mode == kGemmStoreF32) static_cast<float*>(a.out)[o] = v[e];
             else if (a.mode == kGemmStoreBF16) static_cast<__nv_bfloat16*>(a.out)[o] = f2bf(v[e]);
             else static_cast<float*>(a.out)[o] += v[e];
@@ -705,28 +679,33 @@ const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, con
                       dim3 grid, cudaStream_t st) {
   using C = Cfg<NT, FMT, NA, AT, NACC, CPS>;
   CUtensorMap tw, tx, ts;
+  thread_local GroupMaps gmaps;  // host staging of the per-group maps (copied into the launch)
   bool ok;
   GemmArgs b = a;
   b.wq = static_cast<const uint8_t*>(w);
-  memset(&ts, 0, sizeof(ts));
-  if (FMT == kFmtQ4K) {
-    memset(&tw, 0, sizeof(tw));  // unused: the tiled Q4_K operand is fetched with bulk copies
-    ok = true;
-  } else if (FMT == kFmtQ8_0) {
-    // int8 codes [N, K] in 128-byte-wide SW128 boxes; f16 scales [N, K/32], 8 per row per stage
-    ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)w_row_bytes,
-                   128, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
-         a.wscales != nullptr &&
-         encode_2d(&ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.wscales, (uint64_t)(a.K / 32), (uint64_t)a.N,
-                   (uint64_t)(a.K / 32) * 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
-  } else if (FMT == kFmtFP8) {
-    // E4M3 codes [N, K] as Q8_0's; the f32 multipliers are read by the dequant warps
-    ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)w_row_bytes,
-                   128, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
-         a.wscales != nullptr;
-  } else
-    ok = encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, (uint64_t)a.K, (uint64_t)a.N,
-                   (uint64_t)w_row_bytes, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  // the weight operand's tensor maps: Q8_0 int8 codes [N, K] in 128-byte-wide SW128 boxes plus
+  // f16 scales [N, K/32] (8 per row per stage); FP8 codes like Q8_0's (multipliers are read by
+  // the dequant warps); bf16 [N, K]; the tiled Q4_K operand is fetched with bulk copies
+  auto encode_w = [&](const void* wp, const void* sp, CUtensorMap* m, CUtensorMap* ms) -> bool {
+    memset(m, 0, sizeof(*m));
+    memset(ms, 0, sizeof(*ms));
+    if (FMT == kFmtQ4K) return true;
+    if (FMT == kFmtQ8_0)
+      return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, wp, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)w_row_bytes,
+                       128, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
+             sp != nullptr &&
+             encode_2d(ms, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sp, (uint64_t)(a.K / 32), (uint64_t)a.N,
+                       (uint64_t)(a.K / 32) * 2, 8, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (FMT == kFmtFP8)
+      return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, wp, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)w_row_bytes,
+                       128, 128, CU_TENSOR_MAP_SWIZZLE_128B) &&
+             sp != nullptr;
+    return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, wp, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)w_row_bytes,
+                     64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  ok = encode_w(w, a.wscales, &tw, &ts);
+  memset(&gmaps, 0, sizeof(gmaps));
+  for (int g = 0; g < a.groups && ok; ++g) ok = encode_w(a.wq_g[g], a.wscales_g[g], &gmaps.w[g], &gmaps.s[g]);
   if (!ok) return "cuTensorMapEncodeTiled failed for the weight operand";
   if (!encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)a.K, (uint64_t)a.T,
                  (uint64_t)ldx * 2, 64, NT, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -744,7 +723,7 @@ const char* launch_na(const GemmArgs& a, const void* w, int64_t w_row_bytes, con
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = gemm_pdl_enabled() ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS>, tw, tx, ts, b) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, gemm_q_kernel<NT, FMT, NA, DQ, AT, NACC, CPS>, tw, tx, ts, gmaps, b) != cudaSuccess)
     return "gemm_q: launch failed";
   return nullptr;
 }
@@ -882,6 +861,9 @@ static int wsplit() {
   return v;
 }
 
+const char* launch_gemm_q_tiles(int fmt, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
+                                const GemmArgs& a, int nt, dim3 grid, cudaStream_t st);
+
 const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
                           const GemmArgs& a_in, cudaStream_t st) {
   GemmArgs a = a_in;
@@ -897,6 +879,13 @@ const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const voi
   const int nt = gemm_q_token_tile(a.T);
   dim3 grid((a.N + 127) / 128, (a.T + nt - 1) / nt, a.splits);
   if (a.splits > 1 && (!a.ws || !a.counters)) return "gemm_q: split-K needs workspace and counters";
+  a.groups = 0;
+  return launch_gemm_q_tiles(fmt, w, w_row_bytes, x, ldx, a, nt, grid, st);
+}
+
+// Dispatch on format and token tile (checks done by the callers).
+const char* launch_gemm_q_tiles(int fmt, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
+                                const GemmArgs& a, int nt, dim3 grid, cudaStream_t st) {
   if (fmt == kFmtQ4K) {
     switch (nt) {
       case 16: return launch_t<16, kFmtQ4K>(a, w, w_row_bytes, x, ldx, grid, st);
@@ -931,6 +920,38 @@ const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const voi
     case 128: return launch_t<128, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
     default: return launch_t<256, kFmtBF16>(a, w, w_row_bytes, x, ldx, grid, st);
   }
+}
+
+const char* launch_gemm_q_grouped(int fmt, const void* const* w, const void* const* scales, int G,
+                                  int64_t w_row_bytes, const void* x, int64_t ldx, int rows, const GemmArgs& a_in,
+                                  cudaStream_t st) {
+  if (G < 1 || G > kGemmMaxGroups) return "gemm_q grouped: 1..8 groups";
+  if (a_in.mode != kGemmStoreF32 && a_in.mode != kGemmStoreBF16) return "gemm_q grouped: store modes only";
+  if (a_in.splits > 1) return "gemm_q grouped: no split-K";
+  GemmArgs a = a_in;
+  a.wsplit = wsplit();
+  if (a.K % (fmt == kFmtBF16 ? 64 : 256)) return "gemm_q grouped: K must be a multiple of 256 (64 for bf16)";
+  if (fmt != kFmtQ4K && fmt != kFmtBF16 && fmt != kFmtQ8_0 && fmt != kFmtFP8)
+    return "gemm_q grouped: weight format not supported";
+  if (reinterpret_cast<uintptr_t>(x) % 16 || w_row_bytes % 16 || (ldx * 2) % 16 || rows < 1)
+    return "gemm_q grouped: operands must be 16-byte aligned with 16-byte-multiple row strides";
+  for (int g = 0; g < G; ++g)
+    if ((fmt == kFmtQ8_0 || fmt == kFmtFP8) &&
+        (!scales || !scales[g] || reinterpret_cast<uintptr_t>(scales[g]) % 16))
+      return "gemm_q grouped: Q8_0 / FP8 need 16-byte aligned block scales";
+  a.groups = G;
+  a.group_rows = rows;
+  a.T = G * rows;
+  const int nt = gemm_q_token_tile(rows);
+  a.tiles_per_group = (rows + nt - 1) / nt;
+  for (int g = 0; g < G; ++g) {
+    a.wq_g[g] = static_cast<const uint8_t*>(w[g]);
+    a.wscales_g[g] = scales ? scales[g] : nullptr;
+    if (reinterpret_cast<uintptr_t>(w[g]) % 16) return "gemm_q grouped: 16-byte aligned weights";
+  }
+  // the token-tile size follows the per-group rows; the grid covers every group's tiles
+  a.wscales = a.wscales_g[0];
+  return launch_gemm_q_tiles(fmt, w[0], w_row_bytes, x, ldx, a, nt, dim3((a.N + 127) / 128, G * a.tiles_per_group, 1), st);
 }
 
 }  // namespace air

@@ -8,22 +8,10 @@ namespace air {
 
 // kGemmPeerPush: the output is a tensor-parallel partial, stored from the epilogue into the
 // peer receive buffers (PeerPush protocol, comm.h) instead of `out`.
-// kGemmQkvRope: the output rows are [q heads | k heads | v heads] of head_dim 128 (one head per
-// 128-row tile); the epilogue adds the optional bias, applies NeoX RoPE to q and k, writes q
-// (fp32) and k, v into the paged KV cache (bf16) instead of `out`.
-enum GemmMode : int { kGemmStoreF32 = 0, kGemmStoreBF16 = 1, kGemmResidualF32 = 2, kGemmPeerPush = 3,
-                      kGemmQkvRope = 4 };
+enum GemmMode : int { kGemmStoreF32 = 0, kGemmStoreBF16 = 1, kGemmResidualF32 = 2, kGemmPeerPush = 3 };
 
-struct GemmRope {
-  const float2* cs;        // [max_pos, rot_dim / 2] (cos, sin)
-  const int* positions;    // [T]
-  const int64_t* slots;    // [T] paged-cache slot (block * block_size + offset); < 0 = skip
-  void* kv;                // layer [num_blocks, 2, n_kv, block_size, 128] bf16
-  float* q_out;            // [T, n_heads, 128]
-  const float* bias;       // optional [(n_heads + 2 n_kv) * 128]
-  int n_heads, n_kv, block_size, rot_dim;
-  int64_t num_blocks;
-};
+constexpr int kGemmMaxGroups = 8;
+
 
 struct GemmArgs {
   int N, K, T;          // weight rows, reduction length, tokens
@@ -41,7 +29,12 @@ struct GemmArgs {
                         // exit at once (routed-expert GEMMs launched for a capacity)
   PeerPush push;        // kGemmPeerPush destinations
   const void* wscales;  // Q8_0: f16 block scales [N, K/32] (the codes are the weight pointer)
-  GemmRope rope;        // kGemmQkvRope
+  // Grouped launch (routed experts): blockIdx.y = group * tiles_per_group + token tile; group g
+  // reads weight g (wq_g / wscales_g / its tensor maps) and rows [g * group_rows, + group_rows)
+  // of x and out, limited by row_count[g]. groups == 0: one weight, rows [0, T).
+  int groups, group_rows, tiles_per_group;
+  const uint8_t* wq_g[kGemmMaxGroups];
+  const void* wscales_g[kGemmMaxGroups];
        // optional per-phase clock64 stamps of CTA (0,0,0) (profiling aid)
 };
 
@@ -49,6 +42,11 @@ int gemm_q_token_tile(int T);
 int gemm_q_splits(int N, int K, int T, int fmt);
 size_t gemm_q_workspace_floats(int N, int K, int T, int fmt, int splits);
 size_t gemm_q_counters(int N, int T);
+// Grouped launch: G <= kGemmMaxGroups weights of one shape, x [G * rows, K], out [G * rows, N];
+// row_count[g] (device) limits group g. Store modes only.
+const char* launch_gemm_q_grouped(int fmt, const void* const* w, const void* const* scales, int G,
+                                  int64_t w_row_bytes, const void* x, int64_t ldx, int rows, const GemmArgs& a,
+                                  cudaStream_t st);
 // Returns nullptr on success, else an error message (nothing was launched).
 const char* launch_gemm_q(int fmt, const void* w, int64_t w_row_bytes, const void* x, int64_t ldx,
                           const GemmArgs& a, cudaStream_t st);

@@ -1,5 +1,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <vector>
+#include <torch/csrc/utils/pybind.h>
 #include "gemm_tc.h"
 
 using at::Tensor;
@@ -12,24 +14,12 @@ namespace {
 void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, int64_t N, int64_t K,
             Tensor x, Tensor out, int64_t mode, int64_t splits, optional<Tensor> ws,
             optional<Tensor> counters, optional<Tensor> err, optional<Tensor> dbg,
-            optional<Tensor> row_count, optional<Tensor> push_meta, optional<Tensor> rope_cs,
-            optional<Tensor> positions, optional<Tensor> slots, optional<Tensor> kv, optional<Tensor> q_out,
-            optional<Tensor> qkv_bias, int64_t n_heads, int64_t n_kv, int64_t block_size, int64_t rot_dim) {
+            optional<Tensor> row_count, optional<Tensor> push_meta) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2, "gemm_q: x must be 2-D bf16 CUDA");
   TORCH_CHECK(x.stride(1) == 1 && out.stride(1) == 1, "gemm_q: rows must be contiguous");
   TORCH_CHECK(x.size(1) == K, "gemm_q: x has ", x.size(1), " columns, expected K=", K);
   if (mode == air::kGemmPeerPush) {
     TORCH_CHECK(push_meta.has_value(), "gemm_q peer push: push meta required");
-  } else if (mode == air::kGemmQkvRope) {
-    TORCH_CHECK(rope_cs.has_value() && positions.has_value() && slots.has_value() && kv.has_value() &&
-                    q_out.has_value(), "gemm_q qkv rope: rope table, positions, slots, kv and q_out required");
-    TORCH_CHECK(N == (n_heads + 2 * n_kv) * 128 && rot_dim > 0 && rot_dim <= 128 && rot_dim % 2 == 0,
-                "gemm_q qkv rope: N must be (n_heads + 2 n_kv) x 128 (head_dim 128)");
-    TORCH_CHECK(kv->scalar_type() == at::kBFloat16 && kv->is_contiguous() && q_out->is_contiguous() &&
-                    q_out->scalar_type() == at::kFloat && positions->numel() >= x.size(0) &&
-                    slots->numel() >= x.size(0) && slots->scalar_type() == at::kLong,
-                "gemm_q qkv rope: bf16 contiguous kv, fp32 q_out, int64 slots covering the rows");
-    TORCH_CHECK(!qkv_bias.has_value() || qkv_bias->numel() >= N, "gemm_q qkv rope: bias too short");
   } else if (mode == air::kGemmStoreBF16) {
     TORCH_CHECK(out.scalar_type() == at::kBFloat16, "gemm_q: out must be bf16");
   } else {
@@ -56,19 +46,6 @@ void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, i
   a.dbg = dbg.has_value() ? (long long*)dbg->data_ptr<int64_t>() : nullptr;
   a.row_count = row_count.has_value() ? row_count->data_ptr<int>() : nullptr;
   a.wscales = (scales.has_value() && scales->defined()) ? scales->data_ptr() : nullptr;
-  if (mode == air::kGemmQkvRope) {
-    a.rope.cs = static_cast<const float2*>(rope_cs->data_ptr());
-    a.rope.positions = positions->data_ptr<int>();
-    a.rope.slots = slots->data_ptr<int64_t>();
-    a.rope.kv = kv->data_ptr();
-    a.rope.q_out = q_out->data_ptr<float>();
-    a.rope.bias = qkv_bias.has_value() ? qkv_bias->data_ptr<float>() : nullptr;
-    a.rope.n_heads = (int)n_heads;
-    a.rope.n_kv = (int)n_kv;
-    a.rope.block_size = (int)block_size;
-    a.rope.rot_dim = (int)rot_dim;
-    a.rope.num_blocks = kv->size(0);
-  }
   if (mode == air::kGemmPeerPush) {
     a.push = peer_push_from_meta(*push_meta);
     TORCH_CHECK(a.N == a.push.row_len && (int64_t)a.T * a.push.row_len <= a.push.slot_elems,
@@ -81,10 +58,44 @@ void gemm_q(int64_t fmt, Tensor w, optional<Tensor> scales, int64_t row_bytes, i
   TORCH_CHECK(ce == cudaSuccess, "gemm_q launch: ", cudaGetErrorString(ce));
 }
 
+// Grouped GEMM over G <= 8 weights of one shape (routed experts): x [G * rows, K] bf16,
+// out [G * rows, N] (f32 or bf16), row_counts [G] int32 on the device.
+void gemm_q_grouped(int64_t fmt, std::vector<Tensor> ws, std::vector<optional<Tensor>> scales, int64_t row_bytes,
+                    int64_t N, int64_t K, Tensor x, int64_t rows, Tensor out, Tensor row_counts, Tensor err) {
+  const int G = (int)ws.size();
+  TORCH_CHECK(G >= 1 && G <= air::kGemmMaxGroups, "gemm_q_grouped: 1..8 weights");
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(0) >= G * rows &&
+                  x.size(1) == K && x.stride(1) == 1, "gemm_q_grouped: x must be bf16 [G * rows, K]");
+  TORCH_CHECK(out.size(0) >= G * rows && out.size(1) >= N && out.stride(1) == 1, "gemm_q_grouped: out [G * rows, N]");
+  TORCH_CHECK(row_counts.is_cuda() && row_counts.scalar_type() == at::kInt && row_counts.numel() >= G,
+              "gemm_q_grouped: int32 row counts per group");
+  const void* wp[air::kGemmMaxGroups] = {};
+  const void* sp[air::kGemmMaxGroups] = {};
+  for (int g = 0; g < G; ++g) {
+    wp[g] = ws[g].data_ptr();
+    sp[g] = (g < (int)scales.size() && scales[g].has_value()) ? scales[g]->data_ptr() : nullptr;
+  }
+  air::GemmArgs a{};
+  a.N = (int)N;
+  a.K = (int)K;
+  a.mode = out.scalar_type() == at::kBFloat16 ? air::kGemmStoreBF16 : air::kGemmStoreF32;
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.splits = 1;
+  a.err = err.data_ptr<int>();
+  a.row_count = row_counts.data_ptr<int>();
+  const char* e = air::launch_gemm_q_grouped((int)fmt, wp, sp, G, row_bytes, x.data_ptr(), x.stride(0), (int)rows, a,
+                                             at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(e == nullptr, e ? e : "");
+  cudaError_t ce = cudaGetLastError();
+  TORCH_CHECK(ce == cudaSuccess, "gemm_q_grouped launch: ", cudaGetErrorString(ce));
+}
+
 }  // namespace
 
 void register_gemm_tc(pybind11::module_& m) {
   m.def("gemm_q", &gemm_q);
+  m.def("gemm_q_grouped", &gemm_q_grouped);
   m.def("gemm_q_splits", [](int64_t N, int64_t K, int64_t T, int64_t fmt) {
     return air::gemm_q_splits((int)N, (int)K, (int)T, (int)fmt);
   });

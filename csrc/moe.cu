@@ -127,7 +127,98 @@ __global__ void moe_scatter_kernel(float* __restrict__ out, const float* __restr
   for (int k = threadIdx.x; k < H; k += blockDim.x) o[k] += w * yr[k];
 }
 
+// Grouped variants over G local experts: group g covers rows [g * T, g * T + T) of the
+// packed buffers. One CTA per group lists its expert's tokens in token order (idx, wts,
+// count[g]) and records each token's packed row (pos[g * T + t], -1 when not routed).
+__global__ void __launch_bounds__(1024)
+moe_select_grouped_kernel(const float* __restrict__ cw, const int* __restrict__ experts, int E, int T,
+                          int* __restrict__ idx, float* __restrict__ wts, int* __restrict__ count,
+                          int* __restrict__ pos) {
+  __shared__ int warp_tot[32];
+  __shared__ int base;
+  const int g = blockIdx.x, e = experts[g];
+  if (threadIdx.x == 0) base = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int* gidx = idx + (int64_t)g * T;
+  float* gwts = wts + (int64_t)g * T;
+  int* gpos = pos + (int64_t)g * T;
+  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    const float w = t < T ? cw[(int64_t)t * E + e] : 0.f;
+    const bool sel = w > 0.f;
+    const unsigned m = __ballot_sync(0xffffffffu, sel);
+    if (lane == 0) warp_tot[warp] = __popc(m);
+    __syncthreads();
+    int off = base;
+    for (int k = 0; k < warp; ++k) off += warp_tot[k];
+    if (t < T) gpos[t] = -1;
+    if (sel) {
+      const int p = off + __popc(m & ((1u << lane) - 1));
+      gidx[p] = t;
+      gwts[p] = w;
+      gpos[t] = p;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int s = 0;
+      for (int k = 0; k < (int)(blockDim.x >> 5); ++k) s += warp_tot[k];
+      base += s;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) count[g] = base;
+}
+
+// Grid (T, G): packed row i < count[g] of group g = x[idx[g * T + i]].
+__global__ void moe_gather_grouped_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int H,
+                                          const int* __restrict__ idx, const int* __restrict__ count, int T,
+                                          __nv_bfloat16* __restrict__ xg) {
+  const int i = blockIdx.x, g = blockIdx.y;
+  if (i >= __ldg(count + g)) return;
+  const uint4* s = reinterpret_cast<const uint4*>(x + (int64_t)idx[(int64_t)g * T + i] * ldx);
+  uint4* d = reinterpret_cast<uint4*>(xg + ((int64_t)g * T + i) * H);
+  for (int k = threadIdx.x; k < H / 8; k += blockDim.x) d[k] = s[k];
+}
+
+// Grid (ceil(H / 256), T): out[t] += sum over groups g in order of wts * y[packed row of t in
+// g] (a fixed order, so the sum does not depend on scheduling).
+__global__ void moe_scatter_grouped_kernel(float* __restrict__ out, const float* __restrict__ y, int64_t ldy, int H,
+                                           const int* __restrict__ pos, const float* __restrict__ wts, int G,
+                                           int T) {
+  const int t = blockIdx.y, h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= H) return;
+  float acc = 0.f;
+  bool any = false;
+  for (int g = 0; g < G; ++g) {
+    const int p = pos[(int64_t)g * T + t];
+    if (p < 0) continue;
+    const int64_t row = (int64_t)g * T + p;
+    acc += wts[row] * y[row * ldy + h];
+    any = true;
+  }
+  if (any) out[(int64_t)t * H + h] += acc;
+}
+
 }  // namespace
+
+void launch_moe_select_grouped(const float* cw, const int* experts, int G, int E, int T, int* idx, float* wts,
+                               int* count, int* pos, cudaStream_t st) {
+  moe_select_grouped_kernel<<<G, 1024, 0, st>>>(cw, experts, E, T, idx, wts, count, pos);
+}
+
+void launch_moe_gather_grouped(const void* x, int64_t ldx, int H, const int* idx, const int* count, int G, int T,
+                               void* xg, cudaStream_t st) {
+  if (T <= 0) return;
+  moe_gather_grouped_kernel<<<dim3(T, G), 128, 0, st>>>((const __nv_bfloat16*)x, ldx, H, idx, count, T,
+                                                        (__nv_bfloat16*)xg);
+}
+
+void launch_moe_scatter_grouped(float* out, const float* y, int64_t ldy, int H, const int* pos, const float* wts,
+                                int G, int T, cudaStream_t st) {
+  if (T <= 0) return;
+  moe_scatter_grouped_kernel<<<dim3((H + 255) / 256, T), 256, 0, st>>>(out, y, ldy, H, pos, wts, G, T);
+}
 
 void launch_moe_select(const float* cw, int e, int E, int T, int* idx, float* wts, int* count, cudaStream_t st) {
   moe_select_kernel<<<1, 1024, 0, st>>>(cw, e, E, T, idx, wts, count);

@@ -25,4 +25,14 @@ void launch_moe_gather(const void* x, int64_t ldx, int H, const int* idx, const 
 void launch_moe_scatter(float* out, const float* y, int64_t ldy, int H, const int* idx, const float* wts,
                         const int* count, int cap, cudaStream_t st);
 
+// Grouped over G local experts (ids in `experts`, device int32): packed buffers of G * T rows,
+// group g at rows [g * T, g * T + T). pos[g * T + t] = packed row of token t in group g or -1.
+// The scatter sums every group's weighted output per token in group order.
+void launch_moe_select_grouped(const float* cw, const int* experts, int G, int E, int T, int* idx, float* wts,
+                               int* count, int* pos, cudaStream_t st);
+void launch_moe_gather_grouped(const void* x, int64_t ldx, int H, const int* idx, const int* count, int G, int T,
+                               void* xg, cudaStream_t st);
+void launch_moe_scatter_grouped(float* out, const float* y, int64_t ldy, int H, const int* pos, const float* wts,
+                                int G, int T, cudaStream_t st);
+
 }  // namespace air

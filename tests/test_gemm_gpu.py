@@ -51,37 +51,3 @@ def test_gemm_q_residual_and_repeat():
     for i in range(3):  # the split-K counters must reset themselves between calls
         gemm.linear(x.to(DEV), w, resid, residual=True)
     torch.testing.assert_close(resid.cpu(), 1 + 3 * ref, rtol=2e-2, atol=3e-2 * float(ref.abs().max()))
-
-
-@pytest.mark.parametrize("T,rot,bias", [(40, 128, False), (300, 128, True), (17, 64, False)])
-def test_gemm_qkv_rope_epilogue_matches_separate_kernel(T, rot, bias):
-    """QKV GEMM whose epilogue adds the bias, applies RoPE and writes q and the paged K/V,
-    against the same GEMM storing bf16 followed by the token-parallel RoPE/KV kernel."""
-    nh, nkv, hd, bs = 4, 2, 128, 16
-    N, K = (nh + 2 * nkv) * hd, 512
-    w, _ = _w(N, K, GGMLType.Q4_K, 7)
-    g = torch.Generator().manual_seed(T)
-    x = torch.randn(T, K, generator=g).bfloat16().to(DEV)
-    cs = ops.rope_table(1024, rot, 10000.0, DEV)
-    pos = torch.randint(0, 1000, (T,), generator=g, dtype=torch.int32).to(DEV)
-    nblk = (T + bs - 1) // bs + 2
-    slots = torch.randperm(nblk * bs, generator=g)[:T].to(torch.int64)
-    slots[::7] = -1                                              # rows without a cache slot
-    slots = slots.to(DEV)
-    b = (torch.randn(N, generator=g) * 0.1).to(DEV) if bias else None
-    kv_a = torch.zeros(nblk, 2, nkv, bs, hd, dtype=torch.bfloat16, device=DEV)
-    kv_b = torch.zeros_like(kv_a)
-    q_a = torch.zeros(T, nh, hd, device=DEV)
-    q_b = torch.zeros_like(q_a)
-    err = torch.zeros(1, dtype=torch.int32, device=DEV)
-    qkv = torch.zeros(T, N, dtype=torch.bfloat16, device=DEV)
-    gemm.linear(x, w, qkv, err=err, rope=dict(cs=cs, positions=pos, slots=slots, kv=kv_a, q_out=q_a, bias=b,
-                                               n_heads=nh, n_kv=nkv, block_size=bs, rot_dim=rot))
-    gemm.linear(x, w, qkv, err=err)
-    ops.rope_kv(qkv, T, cs, pos, slots, kv_b, q_b, n_heads=nh, n_kv=nkv, head_dim=hd, block_size=bs,
-                rot_dim=rot, err=err, bias=b)
-    torch.cuda.synchronize()
-    assert int(err.item()) == 0
-    scale = float(q_b.abs().max())
-    torch.testing.assert_close(q_a, q_b, rtol=2e-2, atol=1e-2 * scale)
-    torch.testing.assert_close(kv_a.float(), kv_b.float(), rtol=2e-2, atol=1e-2 * scale)

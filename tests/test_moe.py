@@ -118,3 +118,33 @@ def test_grouped_gemm_row_count_limits_work():
     gemm.linear(x, w, part, row_count=torch.tensor([40], dtype=torch.int32, device="cuda"))
     torch.testing.assert_close(part[:40], full[:40])
     assert torch.all(part[256:] == 7.0)     # token tiles (256 rows at T=300) past the count did nothing
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt,E", [(GGMLType.Q4_K, 4), (GGMLType.Q8_0, 10)])
+def test_grouped_expert_ffn_matches_per_expert_launches(monkeypatch, qt, E):
+    """The grouped routed-expert path (grouped select / gather, one grouped GEMM per
+    projection for up to 8 experts, grouped scatter) against one launch chain per expert."""
+    from air_rs.models.config import tiny_moe
+    from air_rs.parallel import moe
+    from air_rs.runtime.builder import build_runner
+    cfg = tiny_moe()
+    cfg.n_experts = E
+    recs = list(random_tensors(cfg, qt, seed=4, device="cpu"))
+    rn = build_runner(cfg, iter(recs), device="cuda", max_batch=16, max_model_len=256, num_blocks=64)
+    lw = rn.w.layers[0]
+    assert moe._grouped_ok(rn, lw)
+    g = torch.Generator().manual_seed(E)
+    T = 37
+    xn = (torch.randn(T, cfg.hidden_dim, generator=g)).to("cuda", torch.bfloat16)
+    x0 = torch.randn(T, cfg.hidden_dim, generator=g).cuda()
+    outs = {}
+    for grouped in ("1", "0"):
+        monkeypatch.setenv("AIR_MOE_GROUPED", grouped)
+        x = x0.clone()
+        moe.moe_ffn_prefill(rn, lw, T, x, xn)
+        torch.cuda.synchronize()
+        outs[grouped] = x
+    rn.check_errors()
+    torch.testing.assert_close(outs["1"], outs["0"], rtol=1e-4, atol=1e-4)
+    assert not torch.equal(outs["1"], x0)
