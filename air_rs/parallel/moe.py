@@ -65,7 +65,12 @@ def _finish(rn, T, x, partial, peer):
 
 def moe_ffn_decode(rn, lw, B, x, xq, xds, peer=None):
     """GEMV path (B <= 8). Expects ``rn.xn_b[:B]`` = normalised input (bf16) and xq/xds its
-    quantised form."""
+    quantised form. With resident tensor-core experts the grouped GEMM path runs instead:
+    experts no token picked exit before reading a byte of their weights (a per-expert GEMV
+    chain would stream every expert), so a batch-1 step reads top_k of n_experts."""
+    if _grouped_ok(rn, lw):
+        moe_ffn_gemm(rn, lw, B, x, peer)
+        return
     ext = ops.require_ext()
     E = rn.cfg.n_experts
     cw = _ensure(rn, "moe_cw", (rn.max_batch, E), torch.float32)

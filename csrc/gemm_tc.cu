@@ -143,16 +143,17 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__
   // everything when a device row count gates the tiles.
   if (a.row_count != nullptr) pdl_wait();
   pdl_trigger();
-  // grouped launch: this CTA's group (routed expert), its token tile and row range
-  const bool grouped = a.groups > 0;
-  const int grp = grouped ? (int)blockIdx.y / a.tiles_per_group : 0;
-  const int ty = grouped ? (int)blockIdx.y % a.tiles_per_group : (int)blockIdx.y;
-  const int rowbase = grouped ? grp * a.group_rows : 0;     // first x / out row of the group
-  const int T_lim = grouped ? a.group_rows : a.T;           // rows of this group
-  const CUtensorMap& tm_w = grouped ? gm.w[grp] : tm_w0;
-  const CUtensorMap& tm_s = grouped ? gm.s[grp] : tm_s0;
-  const uint8_t* wq = grouped ? a.wq_g[grp] : a.wq;
-  const float* wscales_f = static_cast<const float*>(grouped ? a.wscales_g[grp] : a.wscales);
+  // grouped launch: this CTA's group (routed expert) and token tile; the per-group weight
+  // pointers, tensor maps and row range are looked up where they are used (GROUP_* below),
+  // so they hold no registers across the kernel
+  const int grp = a.groups > 0 ? (int)blockIdx.y / a.tiles_per_group : 0;
+  const int ty = a.groups > 0 ? (int)blockIdx.y % a.tiles_per_group : (int)blockIdx.y;
+#define GROUP_ROWBASE (a.groups > 0 ? grp * a.group_rows : 0)
+#define GROUP_TLIM (a.groups > 0 ? a.group_rows : a.T)
+#define GROUP_WQ (a.groups > 0 ? a.wq_g[grp] : a.wq)
+#define GROUP_TMW (a.groups > 0 ? &gm.w[grp] : &tm_w0)
+#define GROUP_TMS (a.groups > 0 ? &gm.s[grp] : &tm_s0)
+#define GROUP_WSCALES static_cast<const float*>(a.groups > 0 ? a.wscales_g[grp] : a.wscales)
   // routed-expert GEMMs: token tiles beyond the device row count do nothing (uniform per CTA,
   // before any barrier, TMEM allocation or copy)
   if (a.row_count != nullptr && ty * NT >= *(volatile const int*)(a.row_count + grp)) return;
@@ -197,8 +198,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    if (FMT != kFmtQ4K) prefetch_tmap(&tm_w);
-    if (FMT == kFmtQ8_0) prefetch_tmap(&tm_s);
+    if (FMT != kFmtQ4K) prefetch_tmap(GROUP_TMW);
+    if (FMT == kFmtQ8_0) prefetch_tmap(GROUP_TMS);
     prefetch_tmap(&tm_x);
   }
   if (warp == 1) tmem_alloc(&bars->tmem, C::kTmemCols);
@@ -240,12 +241,12 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__
         if (wprod && (FMT == kFmtQ8_0 || FMT == kFmtFP8)) {
           // codes [rows m0.., K kb*256..] as two SW128 boxes; Q8_0 then the rows' eight scales
           const int kb = kb0 + i;
-          tma_load_2d(st, &tm_w, &fullb[s], kb * 256, m0);
-          tma_load_2d(st + kQ8Half, &tm_w, &fullb[s], kb * 256 + 128, m0);
-          if (FMT == kFmtQ8_0) tma_load_2d(st + 2 * kQ8Half, &tm_s, &fullb[s], kb * 8, m0);
+          tma_load_2d(st, GROUP_TMW, &fullb[s], kb * 256, m0);
+          tma_load_2d(st + kQ8Half, GROUP_TMW, &fullb[s], kb * 256 + 128, m0);
+          if (FMT == kFmtQ8_0) tma_load_2d(st + 2 * kQ8Half, GROUP_TMS, &fullb[s], kb * 8, m0);
         } else if (wprod) {
           // the tile as a.wsplit back-to-back bulk copies (more requests in flight per CTA)
-          const uint8_t* src = wq + ((size_t)blockIdx.x * ksteps + kb0 + i) * kRawTile;
+          const uint8_t* src = GROUP_WQ + ((size_t)blockIdx.x * ksteps + kb0 + i) * kRawTile;
           const int np = a.wsplit > 0 ? a.wsplit : 1;
           const uint32_t piece = kRawTile / np;
           for (int p = 0; p < np; ++p) bulk_load(st + p * piece, src + p * piece, piece, &fullb[s]);
@@ -253,7 +254,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__
 #pragma unroll
           for (int c = 0; c < C::kXC; ++c) {
             const int ch = i * C::kXC + c;              // chunk index along K
-            tma_load_2d(st + c * C::kBChunk, &tm_x, &fullb[s], (kb0 + ch / 4) * 256 + 64 * (ch % 4), rowbase + n0);
+            tma_load_2d(st + c * C::kBChunk, &tm_x, &fullb[s], (kb0 + ch / 4) * 256 + 64 * (ch % 4), GROUP_ROWBASE + n0);
           }
         }
         issued = i + 1;
@@ -281,13 +282,13 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__
         const int kb = kb0 + i;
         if (FMT == kFmtQ4K) {
           // tiled Q4_K: the 128-row x 256-weight tile is 18 KB contiguous -> one bulk copy
-          bulk_load(st, wq + ((size_t)blockIdx.x * ksteps + kb) * kRawTile, kRawTile, &bars->full[s]);
+          bulk_load(st, GROUP_WQ + ((size_t)blockIdx.x * ksteps + kb) * kRawTile, kRawTile, &bars->full[s]);
 #pragma unroll
           for (int c = 0; c < 4; ++c)
-            tma_load_2d(st + kRawTile + c * C::kBChunk, &tm_x, &bars->full[s], kb * 256 + 64 * c, rowbase + n0);
+            tma_load_2d(st + kRawTile + c * C::kBChunk, &tm_x, &bars->full[s], kb * 256 + 64 * c, GROUP_ROWBASE + n0);
         } else {
-          tma_load_2d(st, &tm_w, &bars->full[s], kb * 64, m0);
-          tma_load_2d(st + kATile, &tm_x, &bars->full[s], kb * 64, rowbase + n0);
+          tma_load_2d(st, GROUP_TMW, &bars->full[s], kb * 64, m0);
+          tma_load_2d(st + kATile, &tm_x, &bars->full[s], kb * 64, GROUP_ROWBASE + n0);
         }
         issued = i + 1;
       }
@@ -421,7 +422,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__
             const uint4 qa = *reinterpret_cast<const uint4*>(row + ((j0 ^ (r & 7)) << 4));
             const uint4 qb = *reinterpret_cast<const uint4*>(row + (((j0 + 1) ^ (r & 7)) << 4));
             const int grow = m0 + r;
-            const float dq = grow < a.N ? __ldg(wscales_f +
+            const float dq = grow < a.N ? __ldg(GROUP_WSCALES +
                                                (size_t)grow * (a.K / 128) + (kb0 + i) * 2 + (c >> 1))
                                         : 0.f;
             const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
@@ -619,8 +620,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int n = n0 + 16 * j + e;
-          if (n < T_lim && mg < a.N) {
-            const size_t o = (size_t)(rowbase + n) * a.ldo + mg;
+          if (n < GROUP_TLIM && mg < a.N) {
+            const size_t o = (size_t)(GROUP_ROWBASE + n) * a.ldo + mg;
             if (a.mode == kGemmStoreF32) static_cast<float*>(a.out)[o] = v[e];
             else if (a.mode == kGemmStoreBF16) static_cast<__nv_bfloat16*>(a.out)[o] = f2bf(v[e]);
             else static_cast<float*>(a.out)[o] += v[e];
@@ -637,6 +638,12 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__
     tmem_dealloc(tmem, C::kTmemCols);
   }
 }
+#undef GROUP_ROWBASE
+#undef GROUP_TLIM
+#undef GROUP_WQ
+#undef GROUP_TMW
+#undef GROUP_TMS
+#undef GROUP_WSCALES
 
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
