@@ -37,6 +37,8 @@ def _common(p: argparse.ArgumentParser, serve: bool = False):
     p.add_argument("--enable-prefix-caching", action="store_true")
     p.add_argument("--kv-swap", action="store_true", help="Enable the pinned host KV tier")
     p.add_argument("--kv-swap-block-kb", type=int, default=64)
+    p.add_argument("--kv-dtype", default=None, choices=("bf16", "fp8"),
+                   help="Paged KV pool precision: bf16 (default) or fp8 (E4M3 + a scale per token and head)")
     p.add_argument("--ternary", "--bitnet", dest="ternary", action="store_true")
     p.add_argument("--ternary-cdsc", action="store_true")
     p.add_argument("--device", default=None, help="cuda | cpu (default: cuda when available)")
@@ -130,7 +132,8 @@ def _engine(args, max_batch=64):
                             prefix_cache=getattr(args, "enable_prefix_caching", False) or ec.prefix_cache,
                             kv_swap=ec.kv_swap, pressure_control=ec.pressure_control, secure_kv=ec.secure_kv,
                             admission=ec.admission,
-                            gds=getattr(args, "gds", False))
+                            gds=getattr(args, "gds", False),
+                            kv_dtype=getattr(args, "kv_dtype", None) or ec.kv_dtype)
 
 
 def cmd_generate(args) -> int:

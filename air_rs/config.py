@@ -30,6 +30,7 @@ class EngineConfig:
     pp: int = 1
     ep: bool = False                    # experts spread over the TP ranks
     block_size: int = 16                # KV block (tokens)
+    kv_dtype: str = "bf16"              # paged KV pool: bf16 | fp8 (E4M3 + per-row scale)
     num_blocks: int | None = None       # KV pool size; default: what the VRAM guard allows
     max_batch: int = 64                 # concurrent decode rows (CUDA-graph buckets up to here)
     max_num_seqs: int = 256
@@ -81,6 +82,8 @@ class EngineConfig:
             raise ValueError("vram_fraction must be in (0, 1]")
         if self.admission not in ("fifo", "priority", "arb"):
             raise ValueError("admission must be fifo, priority or arb")
+        if self.kv_dtype not in ("bf16", "fp8"):
+            raise ValueError("kv_dtype must be 'bf16' or 'fp8'")
         if self.allreduce not in ("peer", "nccl"):
             raise ValueError("allreduce must be 'peer' or 'nccl'")
         if self.stream_slots < 2:
@@ -112,13 +115,14 @@ class EngineConfig:
             return engine_from_gguf(self.model, device=self.device, max_batch=self.max_batch,
                                     max_model_len=self.max_model_len, tp=tp, num_blocks=self.num_blocks,
                                     seed=self.seed, resident=self.resident, expert_slots=self.expert_slots,
+                                    kv_dtype=self.kv_dtype,
                                     **{k: v for k, v in self.engine_kwargs().items() if k != "max_batch"})
         if self.preset is None:
             raise ValueError("EngineConfig needs a model path or a preset")
         return random_engine(self.preset, GGMLType[self.qtype], seed=self.seed,
                              device=self.device or "cuda", max_batch=self.max_batch,
                              max_model_len=self.max_model_len or 4096, tp=tp, num_blocks=self.num_blocks,
-                             expert_slots=self.expert_slots,
+                             expert_slots=self.expert_slots, kv_dtype=self.kv_dtype,
                              **{k: v for k, v in self.engine_kwargs().items() if k != "max_batch"})
 
 

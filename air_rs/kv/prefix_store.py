@@ -72,6 +72,9 @@ class PrefixEntry:
 
 
 def _encode(blocks: torch.Tensor, scheme: CompressionScheme) -> dict:
+    if blocks.dtype == torch.uint8:
+        # fp8 pool rows (E4M3 codes + scale) are already compressed: kept byte for byte
+        return {"kv": blocks.clone()}
     if scheme == CompressionScheme.BF16:
         return {"kv": blocks.to(torch.bfloat16).clone()}
     if scheme == CompressionScheme.F16:
@@ -121,6 +124,8 @@ class PrefixKvStore:
         need = (len(tokens) + bs - 1) // bs
         if not tokens or need > len(blocks):
             raise ValueError(f"{len(tokens)} tokens need {need} blocks, {len(blocks)} given")
+        if kv.dtype == torch.uint8 and scheme != CompressionScheme.BF16:
+            raise ValueError("an fp8 KV pool is stored as is (scheme BF16 = raw rows)")
         if scheme == CompressionScheme.Q8 and kv.shape[-1] % 32:
             raise ValueError("Q8 needs a head dim that is a multiple of 32")
         idx = torch.tensor(blocks[:need], dtype=torch.long, device=kv.device)

@@ -391,9 +391,11 @@ class DecodeNode:
 class KvPushLink:
     """Device-side prefill->decode KV copy into a (possibly peer / IPC-mapped) decode pool."""
 
-    def __init__(self, dst_kv_ptr: int, dst_shape: tuple, flags_ptr: int, device, timeout_s: float = 2.0):
+    def __init__(self, dst_kv_ptr: int, dst_shape: tuple, flags_ptr: int, device, timeout_s: float = 2.0,
+                 elem_size: int = 2):
         self.dst = dst_kv_ptr
-        self.dst_shape = dst_shape                   # (L, nb, 2, nkv, bs, d)
+        self.dst_shape = dst_shape                   # (L, nb, 2, nkv, bs, row elements)
+        self.elem_size = elem_size                   # 2: bf16 pool, 1: fp8 pool (uint8 rows)
         self.flags = flags_ptr
         self.device = torch.device(device)
         self.timeout_s = timeout_s
@@ -401,8 +403,8 @@ class KvPushLink:
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     @staticmethod
-    def block_bytes(shape) -> int:
-        n = 2
+    def block_bytes(shape, elem_size: int = 2) -> int:
+        n = elem_size
         for d in shape[2:]:
             n *= d
         return n
@@ -413,11 +415,12 @@ class KvPushLink:
         ext = ops.require_ext()
         self.tag += 1
         L, nb = self.dst_shape[0], self.dst_shape[1]
-        bb = self.block_bytes(self.dst_shape)
+        bb = self.block_bytes(self.dst_shape, self.elem_size)
         assert tuple(src_kv.shape[2:]) == tuple(self.dst_shape[2:]) and src_kv.shape[0] == L
+        assert src_kv.element_size() == self.elem_size, "prefill and decode pools differ in KV dtype"
         sb = torch.tensor(src_blocks, dtype=torch.int32, device=src_kv.device)
         db = torch.tensor(dst_blocks, dtype=torch.int32, device=src_kv.device)
-        ext.kv_push(src_kv.data_ptr(), src_kv.stride(0) * 2, src_kv.shape[1], self.dst, nb * bb, nb, bb, L,
+        ext.kv_push(src_kv.data_ptr(), src_kv.stride(0) * self.elem_size, src_kv.shape[1], self.dst, nb * bb, nb, bb, L,
                     sb, db, self.flags, nb, self.tag, self.err)
         ops.count_launch()
         return self.tag
@@ -451,7 +454,7 @@ class PdPair:
         nb = decode.runner.kv.shape[1]
         self.flags = torch.zeros(decode.runner.kv.shape[0], nb, dtype=torch.int32, device=dd)
         self.link = KvPushLink(decode.runner.kv.data_ptr(), tuple(decode.runner.kv.shape), self.flags.data_ptr(),
-                               pd_, timeout_s)
+                               pd_, timeout_s, elem_size=decode.runner.kv.element_size())
         self.timeout_s = timeout_s
         self.metrics = TransferMetrics()
 
@@ -491,7 +494,7 @@ class PdPair:
                 raise KvTransferError("corrupt", f"decode blocks differ from prefill blocks "
                                                  f"({int((a_ != b_).sum())} elements)")
         self.metrics.record_transfer(len(src_blocks) * d.runner.kv.shape[0] * KvPushLink.block_bytes(
-            tuple(d.runner.kv.shape)), time.perf_counter() - t0)
+            tuple(d.runner.kv.shape), d.runner.kv.element_size()), time.perf_counter() - t0)
         with torch.cuda.device(p.runner.device):
             p.abort(rid)               # the prefill side's copy is no longer needed
         return dr.rid

@@ -49,9 +49,12 @@ class ModelRunner:
     def __init__(self, cfg: ModelConfig, weights: LlamaWeights, *, num_blocks: int,
                  block_size: int = 16, max_batch: int = 64, max_model_len: int = 4096,
                  max_seqs: int = 256, max_prefill_tokens: int = 8192, device="cuda", tp=None,
-                 seed: int = 0, use_gemm_kernel: bool = True, kv_alloc=None):
+                 seed: int = 0, use_gemm_kernel: bool = True, kv_alloc=None, kv_dtype: str = "bf16"):
         """``kv_alloc(nbytes) -> uint8 CUDA tensor`` supplies the KV pool's memory (e.g. a
-        cudaMalloc'd buffer exported over CUDA IPC for prefill->decode KV pushes)."""
+        cudaMalloc'd buffer exported over CUDA IPC for prefill->decode KV pushes).
+        ``kv_dtype``: "bf16" pool rows of head_dim values, or "fp8": uint8 rows of head_dim
+        E4M3 codes + f32 scale + padding (written by the RoPE/KV kernel, read by every
+        attention kernel; reference: the Q8_0 KV option of src/kv_cache.rs:54-92)."""
         self.cfg, self.w = cfg, weights
         self.device = torch.device(device)
         self.tp = tp
@@ -75,15 +78,23 @@ class ModelRunner:
         self.use_gemm_kernel = use_gemm_kernel
         dev = self.device
         L = len(weights.layers)          # this pipeline stage's layers
-        kv_shape = (L, num_blocks, 2, self.nkv, block_size, self.hd)
+        from .builder import kv_row_bytes
+        self.kv_dtype = kv_dtype
+        self.kv_fp8 = kv_dtype == "fp8"
+        row_b = kv_row_bytes(self.hd, kv_dtype)
+        if self.kv_fp8 and self.hd % 64:
+            raise ValueError("fp8 KV needs head_dim a multiple of 64")
+        kv_t = torch.uint8 if self.kv_fp8 else torch.bfloat16
+        esz = 1 if self.kv_fp8 else 2
+        kv_shape = (L, num_blocks, 2, self.nkv, block_size, row_b // esz)
         if kv_alloc is None:
-            self.kv = torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev)
+            self.kv = torch.zeros(kv_shape, dtype=kv_t, device=dev)
         else:
             n = 1
             for d_ in kv_shape:
                 n *= d_
-            self._kv_buf = kv_alloc(2 * n)
-            self.kv = self._kv_buf[: 2 * n].view(torch.bfloat16).view(kv_shape)
+            self._kv_buf = kv_alloc(esz * n)
+            self.kv = self._kv_buf[: esz * n].view(kv_t).view(kv_shape)
         rot = self.hd if cfg.partial_rope_factor is None else int(self.hd * cfg.partial_rope_factor)
         self.rot_dim = rot
         self.rope_cs = ops.rope_table(max_model_len + 64, rot, cfg.rope_theta, dev)
@@ -136,7 +147,8 @@ class ModelRunner:
             self.up_off = -1           # the "gate|up" GEMM output is the up projection alone
         else:
             self.up_off = l0.wgu.parts[1][0] if l0.wgu is not None else self.F
-        self.qkv_f = torch.zeros(B, self.qkv_dim, dtype=f32, device=dev) if self.qkv_bias else None
+        self.qkv_f = (torch.zeros(B, self.qkv_dim, dtype=f32, device=dev)
+                      if self.qkv_bias or self.kv_fp8 else None)
         # decode GEMVs read Q4_K / Q8_0 / bf16; other formats (block-scaled FP8) decode on the
         # tensor-core GEMM path at every batch size
         fmts = [q.fmt for lw in weights.layers for q in (lw.wqkv, lw.wo, lw.wgu, lw.wdown) if q is not None]
@@ -291,7 +303,8 @@ class ModelRunner:
     def _qkv_rope(self, lw, xq, xds, B, kv, si):
         """Decode QKV GEMV + RoPE + paged KV write (fused epilogue; with q/k/v biases the
         GEMV stores and the token-parallel RoPE kernel adds the bias first)."""
-        if self.qkv_bias:
+        if self.qkv_f is not None:
+            # q/k/v biases, or an fp8 pool (the per-row E4M3 scale needs the whole head row)
             ops.gemv(lw.wqkv, xq, xds, B, ops.EPI_STORE, out_f32=self.qkv_f[:B])
             ops.rope_kv(self.qkv_f[:B], B, self.rope_cs, si.positions, si.slots, kv, self.q[:B],
                         n_heads=self.nh, n_kv=self.nkv, head_dim=self.hd, block_size=self.block_size,
@@ -351,6 +364,7 @@ class ModelRunner:
             self._fused_ok = (self.tp_size == 1 and self.hd == 128 and q4(w.lm_head) and
                               os.environ.get("AIR_FUSED_NORM", "1") != "0" and
                               not self.norm_layer and not self.dense_ffn and not self.qkv_bias and
+                              not self.kv_fp8 and
                               all(lw.wgu is not None and q4(lw.wqkv) and q4(lw.wo) and q4(lw.w_gate) and
                                   q4(lw.wdown) for lw in w.layers))
         return self._fused_ok and self.streamer is None

@@ -9,9 +9,11 @@
 // (src/flash_decode.rs:70-176) on the paged layout of src/paged_attention.rs (block 16),
 // with causal / sliding-window / tree-ancestor visibility (src/ops.rs:762-845).
 //
-// KV layer layout: [num_blocks, 2 (K,V), n_kv, block_size, head_dim] bf16.
+// KV layer layout: [num_blocks, 2 (K,V), n_kv, block_size, row]: a row is head_dim bf16, or
+// (F8) head_dim E4M3 codes + f32 scale + padding (kv_f8.cuh).
 #include "common.cuh"
 #include "attention.h"
+#include "kv_f8.cuh"
 #include <stdlib.h>
 
 namespace air {
@@ -40,10 +42,10 @@ AIR_DEVICE bool key_visible(int t, const AttnRows& rows, int r, int ctx) {
   return true;
 }
 
-// D = head dim; G = query heads per KV head (GQA group).
-template <int D, int G>
+// D = head dim; G = query heads per KV head (GQA group); F8: fp8 pool rows.
+template <int D, int G, bool F8>
 __global__ void __launch_bounds__(kWarps * 32)
-paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kv,
+paged_attn_kernel(const float* __restrict__ q, const uint8_t* __restrict__ kv,
                   const int* __restrict__ block_tables, int max_blocks, AttnRows rows,
                   int n_heads, int n_kv, int block_size, int64_t num_blocks, int n_splits,
                   int split_tokens, float scale, float* __restrict__ part_o,
@@ -82,7 +84,8 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
     for (int j = 0; j < DL; ++j) acc[g][j] = 0.f;
   }
   const int* bt = block_tables + (size_t)seq * max_blocks;
-  const size_t head_stride = (size_t)block_size * D;              // one head of one block
+  constexpr size_t kRowB = F8 ? kv_f8_row_bytes(D) : D * 2;        // bytes per (token, head) row
+  const size_t head_stride = (size_t)block_size * kRowB;           // one head of one block
   const size_t kv_stride = (size_t)n_kv * head_stride;             // K -> V
   const size_t blk_stride = 2 * kv_stride;
 
@@ -92,11 +95,13 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
     // ---- issue every K and V load of this 32-token chunk before any math ----
     uint4 kreg[kNI][KU];
     uint2 vreg[kNI][4];   // [i][gg]: V slice of token c0 + 4i + gg
+    float ksc[kNI], vsc[kNI][4];   // F8 row scales
     bool kval[kNI];
 #pragma unroll
     for (int i = 0; i < kNI; ++i) {
       const int t = c0 + 4 * i + grp;
       kval[i] = false;
+      ksc[i] = 0.f;
 #pragma unroll
       for (int u = 0; u < KU; ++u) kreg[i][u] = make_uint4(0, 0, 0, 0);
       if (t < t_end) {
@@ -105,10 +110,20 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
           set_error(err, kErrBounds);
         } else {
           kval[i] = true;
-          const uint4* kp = reinterpret_cast<const uint4*>(
-              kv + (size_t)b * blk_stride + h * head_stride + (size_t)(t % block_size) * D + gl * (D / 8));
+          const uint8_t* rp = kv + (size_t)b * blk_stride + h * head_stride + (size_t)(t % block_size) * kRowB;
+          if constexpr (F8) {
+            if constexpr (D == 128) {
+              kreg[i][0] = __ldg(reinterpret_cast<const uint4*>(rp + gl * 16));
+            } else {
+              const uint2 c = __ldg(reinterpret_cast<const uint2*>(rp + gl * 8));
+              kreg[i][0] = make_uint4(c.x, c.y, 0u, 0u);
+            }
+            ksc[i] = __ldg(reinterpret_cast<const float*>(rp + D));
+          } else {
+            const uint4* kp = reinterpret_cast<const uint4*>(rp + gl * (D / 8) * 2);
 #pragma unroll
-          for (int u = 0; u < KU; ++u) kreg[i][u] = __ldg(kp + u);
+            for (int u = 0; u < KU; ++u) kreg[i][u] = __ldg(kp + u);
+          }
         }
       }
     }
@@ -118,13 +133,21 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
       for (int gg = 0; gg < 4; ++gg) {
         const int t = c0 + 4 * i + gg;
         vreg[i][gg] = make_uint2(0, 0);
+        vsc[i][gg] = 0.f;
         if (t < t_end) {
           const int b = bt[t / block_size];
           if (b >= 0 && b < num_blocks) {
-            const __nv_bfloat16* vp = kv + (size_t)b * blk_stride + kv_stride + h * head_stride +
-                                      (size_t)(t % block_size) * D + lane * DL;
-            if (DL == 4) vreg[i][gg] = __ldg(reinterpret_cast<const uint2*>(vp));
-            else vreg[i][gg].x = *reinterpret_cast<const uint32_t*>(vp);
+            const uint8_t* rp = kv + (size_t)b * blk_stride + kv_stride + h * head_stride +
+                                (size_t)(t % block_size) * kRowB;
+            if constexpr (F8) {
+              if (DL == 4) vreg[i][gg].x = __ldg(reinterpret_cast<const uint32_t*>(rp + lane * DL));
+              else vreg[i][gg].x = __ldg(reinterpret_cast<const uint16_t*>(rp + lane * DL));
+              vsc[i][gg] = __ldg(reinterpret_cast<const float*>(rp + D));
+            } else {
+              const __nv_bfloat16* vp = reinterpret_cast<const __nv_bfloat16*>(rp) + lane * DL;
+              if (DL == 4) vreg[i][gg] = __ldg(reinterpret_cast<const uint2*>(vp));
+              else vreg[i][gg].x = *reinterpret_cast<const uint32_t*>(vp);
+            }
           }
         }
       }
@@ -138,14 +161,32 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
       float part[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) part[g] = 0.f;
+      if constexpr (F8) {
+        constexpr int NE = D / 8;           // codes of this lane: 16 (D 128) or 8 (D 64)
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&kreg[i][0]);
+        float kf[NE];
 #pragma unroll
-      for (int u = 0; u < KU; ++u) {
-        float kf[8];
-        bf16x8_to_f32(kreg[i][u], kf);
+        for (int e = 0; e < NE; e += 2) {
+          const float2 f = e4m3x2_to_f2(w[e >> 2] >> (8 * (e & 3)));
+          kf[e] = f.x;
+          kf[e + 1] = f.y;
+        }
 #pragma unroll
         for (int g = 0; g < G; ++g) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) part[g] += kf[e] * q_s[g][gl * (D / 8) + u * 8 + e];
+          for (int e = 0; e < NE; ++e) part[g] += kf[e] * q_s[g][gl * NE + e];
+          part[g] *= ksc[i];
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < KU; ++u) {
+          float kf[8];
+          bf16x8_to_f32(kreg[i][u], kf);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) part[g] += kf[e] * q_s[g][gl * (D / 8) + u * 8 + e];
+          }
         }
       }
 #pragma unroll
@@ -189,9 +230,15 @@ paged_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__
 #pragma unroll
         for (int g = 0; g < G; ++g) pv[g] = __shfl_sync(0xffffffffu, p[i][g], gg * 8);
         float vf[4];
-        const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&vreg[i][gg]);
-        const float2 a0 = __bfloat1622float2(hh[0]), a1 = __bfloat1622float2(hh[1]);
-        vf[0] = a0.x; vf[1] = a0.y; vf[2] = a1.x; vf[3] = a1.y;
+        if constexpr (F8) {
+          const float2 a0 = e4m3x2_to_f2(vreg[i][gg].x), a1 = e4m3x2_to_f2(vreg[i][gg].x >> 16);
+          const float sv = vsc[i][gg];
+          vf[0] = a0.x * sv; vf[1] = a0.y * sv; vf[2] = a1.x * sv; vf[3] = a1.y * sv;
+        } else {
+          const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&vreg[i][gg]);
+          const float2 a0 = __bfloat1622float2(hh[0]), a1 = __bfloat1622float2(hh[1]);
+          vf[0] = a0.x; vf[1] = a0.y; vf[2] = a1.x; vf[3] = a1.y;
+        }
 #pragma unroll
         for (int g = 0; g < G; ++g) {
 #pragma unroll
@@ -300,10 +347,13 @@ void launch_dg(const AttnArgs& a, cudaStream_t st) {
       launch_prefill_attention(a, st))
     return;
   if (!(D == 128 && !simt && launch_paged_attention_mma(a, st)))
-  paged_attn_kernel<D, G><<<grid, kWarps * 32, 0, st>>>(
-      a.q, (const __nv_bfloat16*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_heads, a.n_kv,
-      a.block_size, a.num_blocks, a.n_splits, a.split_tokens, a.scale, a.part_o, a.part_ml,
-      a.out, a.err);
+  {
+    auto kern = a.kv_fp8 ? paged_attn_kernel<D, G, true> : paged_attn_kernel<D, G, false>;
+    kern<<<grid, kWarps * 32, 0, st>>>(
+        a.q, (const uint8_t*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_heads, a.n_kv,
+        a.block_size, a.num_blocks, a.n_splits, a.split_tokens, a.scale, a.part_o, a.part_ml,
+        a.out, a.err);
+  }
   if (a.n_splits > 1) {
     attn_merge_kernel<D><<<dim3(a.n_heads, a.n_rows), D, 0, st>>>(
         a.part_o, a.part_ml, a.n_heads, a.n_splits, a.out, a.out_q, a.out_ds, (__nv_bfloat16*)a.out_bf16);

@@ -16,7 +16,9 @@ struct AttnRows {
 
 struct AttnArgs {
   const float* q;            // [R, n_heads, head_dim] (RoPE applied, unscaled)
-  const void* kv;            // layer [num_blocks, 2, n_kv, block_size, head_dim] bf16
+  const void* kv;            // layer [num_blocks, 2, n_kv, block_size, row]: head_dim bf16, or
+                             // (kv_fp8) head_dim E4M3 codes + f32 scale + 12 B padding
+  int kv_fp8;
   const int* block_tables;   // [n_seqs, max_blocks]
   int max_blocks;
   AttnRows rows;

@@ -8,8 +8,14 @@
 // cp.async into an XOR-swizzled shared buffer (double buffered) and feeds the MMAs with
 // ldmatrix (.trans for V). The S accumulators are reused directly as the P operand
 // (FlashAttention-2 register layout).
+//
+// F8 (fp8 KV pool, kv_f8.cuh): the cp.async ring holds the raw 144-byte rows (codes + scale);
+// before its MMAs a warp converts its chunk to f16 (exact for E4M3) in one swizzled K|V tile
+// pair, runs the same MMAs in f16, multiplies each key's score by its K scale and each key's
+// softmax weight by its V scale.
 #include "common.cuh"
 #include "attention.h"
+#include "kv_f8.cuh"
 
 namespace air {
 
@@ -20,6 +26,11 @@ constexpr int kRow = kD * 2;           // bytes per K/V row
 constexpr int kKeys = 16;              // keys per warp chunk
 constexpr int kWarpsM = 4;
 constexpr int kTile = kKeys * kRow;    // 4 KB: one K or V chunk
+constexpr int kF8Row = kv_f8_row_bytes(kD);     // 144 B fp8 row
+constexpr int kF8Tile = kKeys * kF8Row;          // 2304 B: one raw fp8 K or V chunk
+// shared bytes per warp: 2 stages x (K, V) bf16 tiles, or one f16 tile pair + 2 raw fp8 stages
+template <bool F8>
+__host__ __device__ constexpr int warp_bytes() { return F8 ? 2 * kTile + 4 * kF8Tile : 4 * kTile; }
 
 AIR_DEVICE uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -49,9 +60,30 @@ AIR_DEVICE void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uin
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+AIR_DEVICE void mma16816_h(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
 AIR_DEVICE uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+AIR_DEVICE uint32_t pack_h16(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <bool F8>
+AIR_DEVICE void mma_kv(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (F8) mma16816_h(c, a, b0, b1);
+  else mma16816(c, a, b0, b1);
+}
+template <bool F8>
+AIR_DEVICE uint32_t pack_kv(float lo, float hi) {
+  if constexpr (F8) return pack_h16(lo, hi);
+  else return pack_bf16(lo, hi);
 }
 
 AIR_DEVICE bool visible(int t, const AttnRows& rows, int r, int ctx) {
@@ -68,9 +100,9 @@ AIR_DEVICE bool visible(int t, const AttnRows& rows, int r, int ctx) {
   return true;
 }
 
-template <int G>
+template <int G, bool F8>
 __global__ void __launch_bounds__(kWarpsM * 32)
-paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kv,
+paged_attn_mma_kernel(const float* __restrict__ q, const uint8_t* __restrict__ kv,
                       const int* __restrict__ block_tables, int max_blocks, AttnRows rows, int n_heads,
                       int n_kv, int block_size, int64_t num_blocks, int n_splits, int split_tokens,
                       float scale, float* __restrict__ part_o, float2* __restrict__ part_ml,
@@ -79,7 +111,7 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
   extern __shared__ __align__(128) uint8_t smem[];
   // per warp: 2 stages x (K tile + V tile)
   __shared__ float red_m[kWarpsM][16], red_l[kWarpsM][16];
-  float* red_o = reinterpret_cast<float*>(smem + kWarpsM * 4 * kTile);  // [warps][16][128]
+  float* red_o = reinterpret_cast<float*>(smem + kWarpsM * warp_bytes<F8>());  // [warps][16][128]
 
   const int h = blockIdx.x, r = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -109,39 +141,47 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
             x0 = qp[0] * scale;
             x1 = qp[1] * scale;
           }
-          qa[kk][half + 2 * kh] = pack_bf16(x0, x1);
+          qa[kk][half + 2 * kh] = pack_kv<F8>(x0, x1);
         }
       }
     }
   }
 
   const int* bt = block_tables + (size_t)seq * max_blocks;
-  const size_t head_stride = (size_t)block_size * kD;
+  constexpr int kRowB = F8 ? kF8Row : kRow;
+  constexpr int kChunks = kRowB / 16;                 // 16-byte chunks per row: 16 or 9
+  const size_t head_stride = (size_t)block_size * kRowB;
   const size_t kv_stride = (size_t)n_kv * head_stride;
   const size_t blk_stride = 2 * kv_stride;
-  const uint32_t wbase = smem_addr(smem) + warp * 4 * kTile;  // [stage][K|V]
+  const uint32_t wbase = smem_addr(smem) + warp * warp_bytes<F8>();  // bf16: [stage][K|V]
+  uint8_t* const wgen = smem + warp * warp_bytes<F8>();
+  // F8: raw rows of stage sidx at wbase + 2 kTile + sidx * 2 kF8Tile (K, then V)
 
   // issue the cp.async loads of one 16-key chunk starting at key t0 into stage sidx
   auto load_chunk = [&](int t0, int sidx) {
-    const uint32_t kb = wbase + sidx * 2 * kTile, vb = kb + kTile;
+    const uint32_t kb = F8 ? wbase + 2 * kTile + sidx * 2 * kF8Tile : wbase + sidx * 2 * kTile;
+    const uint32_t vb = kb + (F8 ? kF8Tile : kTile);
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {              // 16 keys x 16 chunks = 256 x 16 B per tile
+    for (int it = 0; it < (kKeys * kChunks + 31) / 32; ++it) {
       const int idx = it * 32 + lane;
-      const int key = idx >> 4, c = idx & 15;
+      if (kKeys * kChunks % 32 != 0 && idx >= kKeys * kChunks) continue;
+      const int key = idx / kChunks, c = idx % kChunks;
       const int t = t0 + key;
       bool ok = t < t_end;
-      const __nv_bfloat16* src = kv;
+      const uint8_t* src = kv;
       if (ok) {
         const int b = bt[t / block_size];
         if (b < 0 || b >= num_blocks) {
           set_error(err, kErrBounds);
           ok = false;
         } else {
-          src = kv + (size_t)b * blk_stride + h * head_stride + (size_t)(t % block_size) * kD + c * 8;
+          src = kv + (size_t)b * blk_stride + h * head_stride + (size_t)(t % block_size) * kRowB + c * 16;
         }
       }
-      cp_async16(swz(kb, key, c), src, ok);
-      cp_async16(swz(vb, key, c), ok ? src + kv_stride : kv, ok);
+      const uint32_t dk = F8 ? kb + key * kF8Row + c * 16 : swz(kb, key, c);
+      const uint32_t dv = F8 ? vb + key * kF8Row + c * 16 : swz(vb, key, c);
+      cp_async16(dk, src, ok);
+      cp_async16(dv, ok ? src + kv_stride : kv, ok);
     }
     cp_commit();
   };
@@ -162,7 +202,33 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
     if (more) load_chunk(t0 + stride, sidx ^ 1);
     if (more) cp_wait<1>(); else cp_wait<0>();
     __syncwarp();
-    const uint32_t kb = wbase + sidx * 2 * kTile, vb = kb + kTile;
+    const uint32_t kb = F8 ? wbase : wbase + sidx * 2 * kTile, vb = kb + kTile;
+    float ksc[2][2], vsc[2][2];   // F8: scales of this lane's keys (lane&3)*2 + {0,1} (+8)
+    if constexpr (F8) {
+      const uint8_t* raw = wgen + 2 * kTile + sidx * 2 * kF8Tile;
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {              // 16 keys x 8 code chunks, K and V
+        const int u = it * 32 + lane, key = u >> 3, cc = u & 7;
+#pragma unroll
+        for (int kvi = 0; kvi < 2; ++kvi) {
+          const uint4 c = *reinterpret_cast<const uint4*>(raw + kvi * kF8Tile + key * kF8Row + cc * 16);
+          uint4 lo, hi;
+          e4m3x16_to_h16(c, lo, hi);
+          const uint32_t tb = kvi ? vb : kb;
+          *reinterpret_cast<uint4*>(wgen + (swz(tb, key, 2 * cc) - wbase)) = lo;
+          *reinterpret_cast<uint4*>(wgen + (swz(tb, key, 2 * cc + 1) - wbase)) = hi;
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int key = nt * 8 + (lane & 3) * 2 + j;
+          ksc[nt][j] = *reinterpret_cast<const float*>(raw + key * kF8Row + kD);
+          vsc[nt][j] = *reinterpret_cast<const float*>(raw + kF8Tile + key * kF8Row + kD);
+        }
+      __syncwarp();
+    }
     // ---- S = Q K^T for 16 keys: two n8 tiles ----
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -174,8 +240,8 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
         const int c = 2 * (kk + (mi >> 1)) + (mi & 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(swz(kb, key, c), b0, b1, b2, b3);
-        mma16816(s[nt], qa[kk], b0, b1);
-        mma16816(s[nt], qa[kk + 1], b2, b3);
+        mma_kv<F8>(s[nt], qa[kk], b0, b1);
+        mma_kv<F8>(s[nt], qa[kk + 1], b2, b3);
       }
     }
     // ---- mask + online softmax for head row lane/4 (keys (lane&3)*2 + {0,1} (+8)) ----
@@ -185,6 +251,7 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int t = t0 + nt * 8 + (lane & 3) * 2 + j;
+        if constexpr (F8) s[nt][j] *= ksc[nt][j];
         if (!visible(t, rows, r, ctx) || t >= t_end) s[nt][j] = -INFINITY;
         else s[nt][j] = soft_cap(s[nt][j], rows.softcap);
         mx = fmaxf(mx, s[nt][j]);
@@ -213,9 +280,14 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
     }
     // P as the A operand: rows 8..15 (padding heads) are zero
     uint32_t pa[4];
-    pa[0] = pack_bf16(p[0][0], p[0][1]);
+    if constexpr (F8) {
+      pa[0] = pack_h16(p[0][0] * vsc[0][0], p[0][1] * vsc[0][1]);
+      pa[2] = pack_h16(p[1][0] * vsc[1][0], p[1][1] * vsc[1][1]);
+    } else {
+      pa[0] = pack_bf16(p[0][0], p[0][1]);
+      pa[2] = pack_bf16(p[1][0], p[1][1]);
+    }
     pa[1] = 0u;
-    pa[2] = pack_bf16(p[1][0], p[1][1]);
     pa[3] = 0u;
     // ---- O += P V: 16 n8 tiles over the 128 dims ----
 #pragma unroll
@@ -225,8 +297,8 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
       const int c = nd + (mi >> 1);
       uint32_t b0, b1, b2, b3;
       ldsm_x4_t(swz(vb, key, c), b0, b1, b2, b3);
-      mma16816(o[nd], pa, b0, b1);
-      mma16816(o[nd + 1], pa, b2, b3);
+      mma_kv<F8>(o[nd], pa, b0, b1);
+      mma_kv<F8>(o[nd + 1], pa, b2, b3);
     }
     __syncwarp();
   }
@@ -268,15 +340,22 @@ paged_attn_mma_kernel(const float* __restrict__ q, const __nv_bfloat16* __restri
   }
 }
 
+template <int G, bool F8>
+void launch_gf(const AttnArgs& a, cudaStream_t st) {
+  // bf16: 64 KB tiles + 32 KB merge; F8: 68 KB tiles + 32 KB merge
+  const int smem = kWarpsM * warp_bytes<F8>() + kWarpsM * 16 * kD * 4;
+  static unsigned long long attr_done = 0;
+  set_max_smem_per_device(paged_attn_mma_kernel<G, F8>, smem, attr_done);
+  dim3 grid(a.n_kv, a.n_rows, a.n_splits);
+  paged_attn_mma_kernel<G, F8><<<grid, kWarpsM * 32, smem, st>>>(
+      a.q, (const uint8_t*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_heads, a.n_kv,
+      a.block_size, a.num_blocks, a.n_splits, a.split_tokens, a.scale, a.part_o, a.part_ml, a.out, a.err);
+}
+
 template <int G>
 void launch_g(const AttnArgs& a, cudaStream_t st) {
-  const int smem = kWarpsM * 4 * kTile + kWarpsM * 16 * kD * 4;  // 64 KB tiles + 32 KB merge
-  static unsigned long long attr_done = 0;
-  set_max_smem_per_device(paged_attn_mma_kernel<G>, smem, attr_done);
-  dim3 grid(a.n_kv, a.n_rows, a.n_splits);
-  paged_attn_mma_kernel<G><<<grid, kWarpsM * 32, smem, st>>>(
-      a.q, (const __nv_bfloat16*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_heads, a.n_kv,
-      a.block_size, a.num_blocks, a.n_splits, a.split_tokens, a.scale, a.part_o, a.part_ml, a.out, a.err);
+  if (a.kv_fp8) launch_gf<G, true>(a, st);
+  else launch_gf<G, false>(a, st);
 }
 
 }  // namespace

@@ -13,8 +13,13 @@
 // handled as consecutive groups: the CTA runs the key loop once per group against that
 // group's block table with the other rows masked. Speculative-tree rows keep the per-row
 // kernel. Reference: flash-attention prefill in src/ops.rs:458-508 (GQA at :514-568).
+//
+// F8 (fp8 KV pool, kv_f8.cuh): the cp.async ring holds raw 144-byte rows; after each tile
+// lands the CTA converts it to one f16 K|V tile pair (exact), runs the MMAs in f16 and applies
+// the per-key K scale to the scores and the V scale to the softmax weights.
 #include "common.cuh"
 #include "attention.h"
+#include "kv_f8.cuh"
 
 namespace air {
 
@@ -25,6 +30,11 @@ constexpr int kRow = kD * 2;            // bytes per K/V row
 constexpr int kQT = 16;                 // query rows per CTA
 constexpr int kKT = 64;                 // keys per tile
 constexpr int kTileBytes = kKT * kRow;  // 16 KB (K or V)
+constexpr int kF8Row = kv_f8_row_bytes(kD);   // 144 B
+constexpr int kF8Tile = kKT * kF8Row;          // 9 KB raw fp8 K or V tile
+// bf16: 2 stages x (K, V); F8: one f16 (K, V) pair + 2 raw stages x (K, V)
+template <bool F8>
+__host__ __device__ constexpr int smem_bytes() { return F8 ? 2 * kTileBytes + 4 * kF8Tile : 4 * kTileBytes; }
 
 AIR_DEVICE uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 AIR_DEVICE uint32_t swz(uint32_t base, int t, int c) { return base + t * kRow + ((c ^ (t & 7)) << 4); }
@@ -51,14 +61,32 @@ AIR_DEVICE void mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+AIR_DEVICE void mma_h(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <bool F8>
+AIR_DEVICE void mmak(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (F8) mma_h(c, a, b0, b1);
+  else mma(c, a, b0, b1);
+}
+template <bool F8>
 AIR_DEVICE uint32_t pk(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+  if constexpr (F8) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
 }
 
-template <int G>
+template <int G, bool F8>
 __global__ void __launch_bounds__(G * 32)
-prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict__ kv,
+prefill_attn_kernel(const float* __restrict__ q, const uint8_t* __restrict__ kv,
                     const int* __restrict__ block_tables, int max_blocks, AttnRows rows, int R, int n_heads,
                     int n_kv, int block_size, int64_t num_blocks, float scale, float* __restrict__ out,
                     __nv_bfloat16* __restrict__ out_bf16, int* err) {
@@ -93,10 +121,12 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
             x0 = qp[0] * scale;
             x1 = qp[1] * scale;
           }
-          qa[kk][half + 2 * kh] = pk(x0, x1);
+          qa[kk][half + 2 * kh] = pk<F8>(x0, x1);
         }
   }
-  const size_t head_stride = (size_t)block_size * kD;
+  constexpr int kRowB = F8 ? kF8Row : kRow;
+  constexpr int kChunks = kRowB / 16;
+  const size_t head_stride = (size_t)block_size * kRowB;
   const size_t kv_stride = (size_t)n_kv * head_stride;
   const size_t blk_stride = 2 * kv_stride;
   const uint32_t sbase = saddr(smem);
@@ -128,23 +158,24 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
     }
 
     auto load_tile = [&](int t0, int stage) {
-      const uint32_t kb = sbase + stage * 2 * kTileBytes, vb = kb + kTileBytes;
-      for (int idx = threadIdx.x; idx < kKT * 16; idx += G * 32) {
-        const int key = idx >> 4, c = idx & 15;
+      const uint32_t kb = F8 ? sbase + 2 * kTileBytes + stage * 2 * kF8Tile : sbase + stage * 2 * kTileBytes;
+      const uint32_t vb = kb + (F8 ? kF8Tile : kTileBytes);
+      for (int idx = threadIdx.x; idx < kKT * kChunks; idx += G * 32) {
+        const int key = idx / kChunks, c = idx % kChunks;
         const int t = t0 + key;
         bool ok = t < kmax;
-        const __nv_bfloat16* src = kv;
+        const uint8_t* src = kv;
         if (ok) {
           const int b = bt[t / block_size];
           if (b < 0 || b >= num_blocks) {
             set_error(err, kErrBounds);
             ok = false;
           } else {
-            src = kv + (size_t)b * blk_stride + h * head_stride + (size_t)(t % block_size) * kD + c * 8;
+            src = kv + (size_t)b * blk_stride + h * head_stride + (size_t)(t % block_size) * kRowB + c * 16;
           }
         }
-        cp16(swz(kb, key, c), src, ok);
-        cp16(swz(vb, key, c), ok ? src + kv_stride : kv, ok);
+        cp16(F8 ? kb + key * kF8Row + c * 16 : swz(kb, key, c), src, ok);
+        cp16(F8 ? vb + key * kF8Row + c * 16 : swz(vb, key, c), ok ? src + kv_stride : kv, ok);
       }
       cp_commit();
     };
@@ -163,7 +194,20 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
       if (more) load_tile(t0 + kKT, stage ^ 1);
       if (more) cp_wait<1>(); else cp_wait<0>();
       __syncthreads();
-      const uint32_t kb = sbase + stage * 2 * kTileBytes, vb = kb + kTileBytes;
+      const uint32_t kb = F8 ? sbase : sbase + stage * 2 * kTileBytes, vb = kb + kTileBytes;
+      const uint8_t* raw = smem + 2 * kTileBytes + stage * 2 * kF8Tile;   // F8 only
+      if constexpr (F8) {
+        for (int u = threadIdx.x; u < 2 * kKT * 8; u += G * 32) {   // (K|V) x 64 keys x 8 chunks
+          const int kvi = u / (kKT * 8), key = (u / 8) % kKT, cc = u % 8;
+          const uint4 c = *reinterpret_cast<const uint4*>(raw + kvi * kF8Tile + key * kF8Row + cc * 16);
+          uint4 lo, hi;
+          e4m3x16_to_h16(c, lo, hi);
+          const uint32_t tb = kvi ? vb : kb;
+          *reinterpret_cast<uint4*>(smem + (swz(tb, key, 2 * cc) - sbase)) = lo;
+          *reinterpret_cast<uint4*>(smem + (swz(tb, key, 2 * cc + 1) - sbase)) = hi;
+        }
+        __syncthreads();
+      }
       // ---- S = Q K^T: 16 rows x 64 keys ----
       float s[8][4];
 #pragma unroll
@@ -176,8 +220,8 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
           const int c = 2 * (kk + (mi >> 1)) + (mi & 1);
           uint32_t b0, b1, b2, b3;
           ldsm4(swz(kb, key, c), b0, b1, b2, b3);
-          mma(s[nt], qa[kk], b0, b1);
-          mma(s[nt], qa[kk + 1], b2, b3);
+          mmak<F8>(s[nt], qa[kk], b0, b1);
+          mmak<F8>(s[nt], qa[kk + 1], b2, b3);
         }
       }
       // ---- mask + online softmax (rows qr[0], qr[1]) ----
@@ -189,6 +233,8 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
           const int i = j >> 1;
           const int t = t0 + nt * 8 + (lane & 3) * 2 + (j & 1);
           const bool vis = in_g[i] && t < ctx[i] && !(rows.window > 0 && t < ctx[i] - rows.window);
+          if constexpr (F8)
+            s[nt][j] *= *reinterpret_cast<const float*>(raw + (nt * 8 + (lane & 3) * 2 + (j & 1)) * kF8Row + kD);
           s[nt][j] = vis ? soft_cap(s[nt][j], rows.softcap) : -INFINITY;
           mx[i] = fmaxf(mx[i], s[nt][j]);
         }
@@ -228,10 +274,24 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
 #pragma unroll
       for (int kt = 0; kt < 4; ++kt) {
         uint32_t pa[4];
-        pa[0] = pk(s[2 * kt][0], s[2 * kt][1]);
-        pa[1] = pk(s[2 * kt][2], s[2 * kt][3]);
-        pa[2] = pk(s[2 * kt + 1][0], s[2 * kt + 1][1]);
-        pa[3] = pk(s[2 * kt + 1][2], s[2 * kt + 1][3]);
+        if constexpr (F8) {
+          float vs[2][2];     // V scales of keys kt*16 + {0, 8} + (lane&3)*2 + {0, 1}
+#pragma unroll
+          for (int x = 0; x < 2; ++x)
+#pragma unroll
+            for (int y = 0; y < 2; ++y)
+              vs[x][y] = *reinterpret_cast<const float*>(
+                  raw + kF8Tile + ((2 * kt + x) * 8 + (lane & 3) * 2 + y) * kF8Row + kD);
+          pa[0] = pk<F8>(s[2 * kt][0] * vs[0][0], s[2 * kt][1] * vs[0][1]);
+          pa[1] = pk<F8>(s[2 * kt][2] * vs[0][0], s[2 * kt][3] * vs[0][1]);
+          pa[2] = pk<F8>(s[2 * kt + 1][0] * vs[1][0], s[2 * kt + 1][1] * vs[1][1]);
+          pa[3] = pk<F8>(s[2 * kt + 1][2] * vs[1][0], s[2 * kt + 1][3] * vs[1][1]);
+        } else {
+          pa[0] = pk<F8>(s[2 * kt][0], s[2 * kt][1]);
+          pa[1] = pk<F8>(s[2 * kt][2], s[2 * kt][3]);
+          pa[2] = pk<F8>(s[2 * kt + 1][0], s[2 * kt + 1][1]);
+          pa[3] = pk<F8>(s[2 * kt + 1][2], s[2 * kt + 1][3]);
+        }
 #pragma unroll
         for (int nd = 0; nd < 16; nd += 2) {
           const int mi = lane >> 3;
@@ -239,8 +299,8 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
           const int c = nd + (mi >> 1);
           uint32_t b0, b1, b2, b3;
           ldsm4t(swz(vb, key, c), b0, b1, b2, b3);
-          mma(o[nd], pa, b0, b1);
-          mma(o[nd + 1], pa, b2, b3);
+          mmak<F8>(o[nd], pa, b0, b1);
+          mmak<F8>(o[nd + 1], pa, b2, b3);
         }
       }
       __syncthreads();      // every warp is done with this stage before it is refilled
@@ -268,15 +328,21 @@ prefill_attn_kernel(const float* __restrict__ q, const __nv_bfloat16* __restrict
   }
 }
 
+template <int G, bool F8>
+void launch_gf(const AttnArgs& a, cudaStream_t st) {
+  constexpr int smem = smem_bytes<F8>();    // 64 KB (bf16) / 68 KB (F8)
+  static unsigned long long attr_done = 0;
+  set_max_smem_per_device(prefill_attn_kernel<G, F8>, smem, attr_done);
+  dim3 grid(a.n_kv, (a.n_rows + kQT - 1) / kQT);
+  prefill_attn_kernel<G, F8><<<grid, G * 32, smem, st>>>(
+      a.q, (const uint8_t*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_rows, a.n_heads, a.n_kv,
+      a.block_size, a.num_blocks, a.scale, a.out, (__nv_bfloat16*)a.out_bf16, a.err);
+}
+
 template <int G>
 void launch_g(const AttnArgs& a, cudaStream_t st) {
-  constexpr int smem = 2 * 2 * kTileBytes;    // 64 KB
-  static unsigned long long attr_done = 0;
-  set_max_smem_per_device(prefill_attn_kernel<G>, smem, attr_done);
-  dim3 grid(a.n_kv, (a.n_rows + kQT - 1) / kQT);
-  prefill_attn_kernel<G><<<grid, G * 32, smem, st>>>(
-      a.q, (const __nv_bfloat16*)a.kv, a.block_tables, a.max_blocks, a.rows, a.n_rows, a.n_heads, a.n_kv,
-      a.block_size, a.num_blocks, a.scale, a.out, (__nv_bfloat16*)a.out_bf16, a.err);
+  if (a.kv_fp8) launch_gf<G, true>(a, st);
+  else launch_gf<G, false>(a, st);
 }
 
 }  // namespace

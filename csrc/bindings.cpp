@@ -132,6 +132,9 @@ void gemv(int64_t fmt, Tensor data, optional<Tensor> scales, int64_t row_bytes, 
   if (mode == air::kEpiQKVRope)
     TORCH_CHECK(ep.kv_cache && ep.q_out && ep.rope_cs && ep.positions && ep.slots,
                 "gemv qkv: rope/kv/q buffers required");
+  if (mode == air::kEpiQKVRope && kv)
+    TORCH_CHECK(kv->scalar_type() == at::kBFloat16, "gemv qkv: the fused KV write needs a bf16 pool "
+                "(fp8 pools take the rope_kv kernel)");
   if (fmt == air::kFmtQ4K) TORCH_CHECK(data.dim() == 4, "gemv q4k: expects the tiled device layout");
   // the tiled kernel handles every Q4_K case except the QKV epilogue of head_dim != 128
   if (fmt == air::kFmtQ4K && !(mode == air::kEpiQKVRope && head_dim != 128)) {
@@ -164,6 +167,12 @@ void paged_attention(Tensor q, Tensor kv, Tensor block_tables, optional<Tensor> 
   air::AttnArgs a{};
   a.q = ptr<float>(q);
   a.kv = kv.data_ptr();
+  a.kv_fp8 = kv.scalar_type() == at::kByte ? 1 : 0;
+  if (a.kv_fp8) {
+    TORCH_CHECK(kv.size(-1) == head_dim + 16, "paged_attention: fp8 KV rows are head_dim + 16 bytes");
+  } else {
+    TORCH_CHECK(kv.scalar_type() == at::kBFloat16, "paged_attention: KV pool is bf16 or uint8 (fp8 rows)");
+  }
   a.block_tables = ptr<int>(block_tables);
   a.max_blocks = (int)block_tables.size(1);
   a.rows = air::AttnRows{ptr<int>(row_seq), ptr<int>(ctx_len), ptr<int>(tree_base),
@@ -239,7 +248,12 @@ void rope_kv(Tensor qkv, int64_t T, Tensor rope_cs, Tensor positions, Tensor slo
              int64_t rot_dim, optional<Tensor> err, optional<Tensor> bias) {
   air::RopeKvArgs a{ptr<float2>(rope_cs), ptr<int>(positions), ptr<int64_t>(slots), kv.data_ptr(),
                     ptr<float>(q_out), (int)n_heads, (int)n_kv, (int)head_dim, (int)block_size,
-                    (int)rot_dim, kv.size(0), ptr<int>(err), ptr<float>(bias)};
+                    (int)rot_dim, kv.size(0), ptr<int>(err), ptr<float>(bias),
+                    kv.scalar_type() == at::kByte ? 1 : 0};
+  if (a.kv_fp8) {
+    TORCH_CHECK(kv.size(-1) == head_dim + 16 && head_dim % 64 == 0 && head_dim <= 512,
+                "rope_kv: fp8 KV rows are head_dim + 16 bytes, head_dim a multiple of 64 (<= 512)");
+  }
   air::launch_rope_kv(qkv.data_ptr(), qkv.scalar_type() == at::kBFloat16, (int)T, a, stream());
   post_launch("rope_kv");
 }

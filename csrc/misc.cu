@@ -4,6 +4,7 @@
 #include <cuda_fp8.h>
 #include "common.cuh"
 #include "misc.h"
+#include "kv_f8.cuh"
 
 namespace air {
 
@@ -131,6 +132,80 @@ __global__ void rope_kv_kernel(const TIn* __restrict__ qkv, int T, RopeKvArgs a)
   base[i + half] = f2bf(x1);
 }
 
+// fp8 KV pool variant: one warp per (token, head) row, so the row's absmax (the E4M3 scale)
+// is a warp reduction. Q rows are written as in rope_kv_kernel; K and V rows as E4M3 codes
+// plus the f32 scale (kv_f8.cuh). head_dim is a multiple of 64 (one pair of rotated halves
+// per lane per step).
+template <typename TIn>
+__global__ void __launch_bounds__(256) rope_kv_f8_kernel(const TIn* __restrict__ qkv, int T, RopeKvArgs a) {
+  const int heads = a.n_heads + 2 * a.n_kv;
+  const int64_t rowi = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (rowi >= (int64_t)T * heads) return;
+  const int head = rowi % heads;
+  const int t = rowi / heads;
+  const int D = a.head_dim, half = D / 2, rh = a.rot_dim / 2;
+  constexpr int kMaxPairs = 8;             // head_dim <= 512
+  const int np = half / 32;
+  const TIn* row = qkv + (size_t)t * heads * D + (size_t)head * D;
+  const bool is_v = head >= a.n_heads + a.n_kv;
+  float x0[kMaxPairs], x1[kMaxPairs];
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxPairs; ++j) {
+    if (j >= np) break;
+    const int i = lane + 32 * j;
+    float u0, u1;
+    if constexpr (sizeof(TIn) == 4) { u0 = row[i]; u1 = row[i + half]; }
+    else { u0 = bf2f(row[i]); u1 = bf2f(row[i + half]); }
+    if (a.bias) {
+      u0 += a.bias[(size_t)head * D + i];
+      u1 += a.bias[(size_t)head * D + i + half];
+    }
+    if (!is_v && i < rh) {
+      const float2 cs = a.rope_cs[(size_t)a.positions[t] * rh + i];
+      const float y0 = u0 * cs.x - u1 * cs.y, y1 = u0 * cs.y + u1 * cs.x;
+      u0 = y0;
+      u1 = y1;
+    }
+    x0[j] = u0;
+    x1[j] = u1;
+    amax = fmaxf(amax, fmaxf(fabsf(u0), fabsf(u1)));
+  }
+  if (head < a.n_heads) {
+    float* q = a.q_out + ((size_t)t * a.n_heads + head) * D;
+#pragma unroll
+    for (int j = 0; j < kMaxPairs; ++j) {
+      if (j >= np) break;
+      q[lane + 32 * j] = x0[j];
+      q[lane + 32 * j + half] = x1[j];
+    }
+    return;
+  }
+  const int64_t slot = a.slots[t];
+  if (slot < 0) return;
+  const int64_t blk = slot / a.block_size, off = slot % a.block_size;
+  if (blk >= a.num_blocks) {
+    if (lane == 0) set_error(a.err, kErrBounds);
+    return;
+  }
+  amax = warp_max(amax);
+  const float s = amax / kE4M3Max;
+  const float inv = s > 0.f ? 1.f / s : 0.f;
+  const int kvh = is_v ? head - a.n_heads - a.n_kv : head - a.n_heads;
+  const int rb = kv_f8_row_bytes(D);
+  uint8_t* base = static_cast<uint8_t*>(a.kv_cache) +
+      ((((size_t)blk * 2 + (is_v ? 1 : 0)) * a.n_kv + kvh) * a.block_size + off) * rb;
+#pragma unroll
+  for (int j = 0; j < kMaxPairs; ++j) {
+    if (j >= np) break;
+    const uint16_t c = f2_to_e4m3x2(x0[j] * inv, x1[j] * inv);
+    base[lane + 32 * j] = (uint8_t)(c & 0xFF);
+    base[lane + 32 * j + half] = (uint8_t)(c >> 8);
+  }
+  if (lane < 4) reinterpret_cast<float*>(base + D)[lane] = lane == 0 ? s : 0.f;
+}
+
 // out[t, j] = act(gu[t, j]) * gu[t, up_off + j]   (gate/up concatenated along columns);
 // up_off < 0: out = act(gu[t, j]) (dense GELU MLP, no gate)
 template <typename TIn>
@@ -199,6 +274,13 @@ void launch_dequant(int fmt, const void* w, const void* scales, int64_t row_byte
 void launch_rope_kv(const void* qkv, bool bf16_in, int T, const RopeKvArgs& a, cudaStream_t st) {
   const int64_t n = (int64_t)T * (a.n_heads + 2 * a.n_kv) * (a.head_dim / 2);
   if (n <= 0) return;
+  if (a.kv_fp8) {
+    const int64_t rows = (int64_t)T * (a.n_heads + 2 * a.n_kv);
+    const unsigned g8 = (unsigned)((rows + 7) / 8);
+    if (bf16_in) rope_kv_f8_kernel<__nv_bfloat16><<<g8, 256, 0, st>>>((const __nv_bfloat16*)qkv, T, a);
+    else rope_kv_f8_kernel<float><<<g8, 256, 0, st>>>((const float*)qkv, T, a);
+    return;
+  }
   const unsigned grid = (unsigned)((n + 255) / 256);
   if (bf16_in) rope_kv_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)qkv, T, a);
   else rope_kv_kernel<float><<<grid, 256, 0, st>>>((const float*)qkv, T, a);

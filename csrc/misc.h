@@ -15,6 +15,7 @@ struct RopeKvArgs {
   int64_t num_blocks;
   int* err;
   const float* bias;       // optional [(n_heads + 2 n_kv) * head_dim] q|k|v bias, added before RoPE
+  int kv_fp8;              // 1: the pool rows are E4M3 codes + f32 scale (kv_f8.cuh)
 };
 
 void launch_embed(int fmt, const void* table, const void* scales, int64_t row_bytes, int K,
