@@ -276,6 +276,28 @@ def sample(logits, out_tokens, *, counts=None, count_row=None, mask=None, temper
     count_launch(3 if step is not None else 2)
 
 
+def sample_partial(logits, part, *, v_off: int, V_total: int, counts=None, count_row=None, mask=None,
+                   penalty=None, B=None, V=None, nch=None):
+    """Greedy partial pass over a vocabulary shard (columns [v_off, v_off + V) of V_total):
+    per 1024-column chunk the penalised, masked max and its global index -> part
+    [B, nch, 4] (nch >= sampler_chunks(V); chunks past V hold (-inf, INT_MAX))."""
+    B = B if B is not None else logits.shape[0]
+    V = V if V is not None else logits.shape[1]
+    nch = nch if nch is not None else sampler_chunks(logits.shape[1])
+    require_ext().sampler_partial(logits, B, V, nch, v_off, V_total, counts, count_row, mask, penalty, part)
+    count_launch()
+
+
+def sample_greedy_merge(part_all, out_tokens, *, W: int, B: int, nch: int, out_prob=None, step=None):
+    """Argmax over all ranks' gathered partials [W, B, nch, 4] (lowest index on ties)."""
+    require_ext().sampler_greedy_merge(part_all, W, B, nch, out_tokens, out_prob, step)
+    count_launch(2 if step is not None else 1)
+
+
+def sampler_chunks(V: int) -> int:
+    return int(require_ext().sampler_chunks(V))
+
+
 _SAMPLER_PART: dict = {}
 
 

@@ -80,6 +80,12 @@ class TPGroup:
         full.copy_(buf.permute(1, 0, 2).reshape(B, W * Vl)[:, :V])
         return full
 
+    def all_gather_flat(self, local: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Contiguous ``local`` of every rank -> ``out`` = [W * local.numel()] in rank order."""
+        dist.all_gather_into_tensor(out, local.contiguous(), group=self.group)
+        COMM.record("all_gather", local.numel() * local.element_size())
+        return out
+
     def broadcast_obj(self, obj, src: int = 0):
         lst = [obj]
         dist.broadcast_object_list(lst, src=src, group=self.group)

@@ -121,11 +121,16 @@ def bench_gemm(name: str, T: int, iters: int, dev):
     return us, nbytes + T * K * 2 + T * N * 2, 2.0 * N * K * T
 
 
-def bench_attn(B: int, ctx: int, iters: int, dev, tp: int = 1):
+def bench_attn(B: int, ctx: int, iters: int, dev, tp: int = 1, kv_dtype: str = "bf16"):
     nkv, nh, d, bs = 8 // tp, 32 // tp, 128, 16
     nblk = B * ((ctx + bs - 1) // bs)
-    copies = max(1, int(4 * L2_BYTES // (nblk * 2 * nkv * bs * d * 2)) + 1)
-    kvs = [torch.randn(nblk, 2, nkv, bs, d, device=dev).bfloat16() for _ in range(copies)]
+    row = d * 2 if kv_dtype == "bf16" else d + 16
+    copies = max(1, int(4 * L2_BYTES // (nblk * 2 * nkv * bs * row)) + 1)
+    if kv_dtype == "fp8":
+        from ..kv.fp8 import quantize_rows
+        kvs = [quantize_rows(torch.randn(nblk, 2, nkv, bs, d, device=dev)) for _ in range(copies)]
+    else:
+        kvs = [torch.randn(nblk, 2, nkv, bs, d, device=dev).bfloat16() for _ in range(copies)]
     bt = torch.arange(nblk, dtype=torch.int32, device=dev).view(B, -1)
     q = torch.randn(B, nh, d, device=dev)
     out = torch.zeros(B, nh, d, device=dev)
@@ -140,7 +145,7 @@ def bench_attn(B: int, ctx: int, iters: int, dev, tp: int = 1):
                             block_size=bs, n_splits=ns, split_tokens=0, part_o=po, part_ml=pm)
         i[0] += 1
     us = ev_time(f, iters)
-    return us, B * ctx * 2 * nkv * d * 2, 4.0 * B * nh * ctx * d
+    return us, B * ctx * 2 * nkv * row, 4.0 * B * nh * ctx * d
 
 
 def bench_graph(preset: str, B: int, iters: int, dev) -> dict:
@@ -248,6 +253,7 @@ def main(argv=None):
     ap.add_argument("--name", default=None, choices=list(SHAPES))
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=640)
+    ap.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tp", type=int, default=1, help="shapes of one rank's shard under tensor parallelism")
     a = ap.parse_args(argv)
@@ -273,8 +279,8 @@ def main(argv=None):
                 line("gemm", f"{n} N={SHAPES[n][0]} K={SHAPES[n][1]} T={T}", us, nb, f)
     if a.op in ("all", "attn"):
         for B in ([a.batch] if a.batch else [1, 64]):
-            us, nb, f = bench_attn(B, a.ctx, a.iters, dev, a.tp)
-            line("attn", f"decode B={B} ctx={a.ctx}", us, nb, f)
+            us, nb, f = bench_attn(B, a.ctx, a.iters, dev, a.tp, a.kv_dtype)
+            line("attn", f"decode B={B} ctx={a.ctx} kv={a.kv_dtype}", us, nb, f)
     if a.op in ("all", "norm"):
         for K, B in [(4096, 1), (4096, 64), (14336, 8)]:
             x = torch.randn(B, K, device=dev)

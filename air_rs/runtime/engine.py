@@ -551,6 +551,7 @@ class Engine:
             si.ids.copy_(i32[3 * B:], non_blocking=True)
             h2d += B * 4
             p["members"] = key
+            p["greedy"] = all(q.temperature <= 1e-6 for q in prs)
         elif self.seqs_changed_blocks(batch):
             self.seqs.fill_table(seqs, st["tab"])
             si.block_tables.copy_(st["tab"], non_blocking=True)
@@ -564,7 +565,7 @@ class Engine:
             for m in rn.inputs.values():
                 m.mask.fill_(-1)
             self._mask_dirty = False
-        rn.decode(B, use_graph=True)
+        rn.decode(B, use_graph=True, greedy=p.get("greedy", False))
         st["tok"].copy_(si.tokens, non_blocking=True)
         ev = torch.cuda.Event()
         ev.record()

@@ -20,7 +20,9 @@ from ..models.config import ModelConfig
 from ..models.llama import LlamaWeights
 from ..utils import trace
 
-GEMV_MAX_B = 8
+# decode batches up to this size run the int8-activation GEMV chain; larger ones the
+# tensor-core GEMM (AIR_GEMV_MAX_B overrides, e.g. to compare the two at one batch size)
+GEMV_MAX_B = max(1, min(8, int(os.environ.get("AIR_GEMV_MAX_B", "8"))))
 
 
 def _dev_param(x, dtype, device):
@@ -126,6 +128,15 @@ class ModelRunner:
         self.y = torch.zeros(B, self.H, dtype=f32, device=dev)
         self.logits = torch.zeros(B, self.V_l, dtype=f32, device=dev)
         self.logits_full = self.logits if tp_size == 1 else torch.zeros(B, self.V, dtype=f32, device=dev)
+        # greedy steps under TP: per-rank partial argmax pass, all-gather of the partials
+        # ([W, B, chunks] float4) instead of the [B, V] logits, device merge
+        self.vocab_greedy = (tp_size > 1 and self.V_l < self.V and self.V_l % 32 == 0 and
+                             os.environ.get("AIR_VOCAB_GREEDY", "0") == "1")
+        self.head_greedy = False          # set per step by decode(greedy=...)
+        if self.vocab_greedy:
+            self.vnch = ops.sampler_chunks(self.V_l)
+            self.vpart = torch.zeros(B * self.vnch * 4, dtype=f32, device=dev)
+            self.vpart_all = torch.zeros(tp_size * B * self.vnch * 4, dtype=f32, device=dev)
         self.max_splits = 32
         self.part_o = torch.zeros(B * self.nh * self.max_splits * self.hd, dtype=f32, device=dev)
         self.part_ml = torch.zeros(B * self.nh * self.max_splits * 2, dtype=f32, device=dev)
@@ -158,9 +169,10 @@ class ModelRunner:
         self.h_b = torch.zeros(B, self.Fp, dtype=bf16, device=dev)
         self.o_b = torch.zeros(B, self.H, dtype=bf16, device=dev)
         self.inputs: dict[int, StepInputs] = {}
-        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
-        self.graph_launches: dict[int, int] = {}
-        self.graph_comm: dict[int, dict] = {}      # collective calls / bytes per replay
+        # keyed by (bucket, greedy head): greedy steps under TP capture the partial-merge head
+        self.graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: dict[tuple, int] = {}
+        self.graph_comm: dict[tuple, dict] = {}      # collective calls / bytes per replay
         self._prefill_ws: dict[str, torch.Tensor] = {}
         self.streamer = None
         self.expert_cache = None
@@ -463,6 +475,9 @@ class ModelRunner:
             self._norm(x, w.out_norm, B, y_bf16=self.xn_b[:B], peer=peer, bias=w.out_norm_b)
             self.linear(self.xn_b[:B], w.lm_head, self.logits[:B])
         logits = self.logits[:B]
+        if self.tp_size > 1 and self.head_greedy and self.vocab_greedy:
+            self._head_greedy_tp(B, si)
+            return
         if self.tp_size > 1:
             logits = self.tp.all_gather_vocab(self.logits[:B], self.logits_full[:B])
         ops.sample(logits, si.tokens, counts=self.counts, count_row=si.count_row, mask=si.mask,
@@ -471,13 +486,36 @@ class ModelRunner:
         ops.count_tokens(self.counts, si.tokens, n=B, count_row=si.count_row)
         si.ids.copy_(si.tokens)
 
-    def decode(self, B: int, use_graph: bool = True):
-        """Runs one decode step for the first B rows of the bucket-B inputs."""
+    def _head_greedy_tp(self, B: int, si: StepInputs):
+        """Vocabulary-parallel greedy sampling: this rank's penalised, masked argmax per
+        1024-column chunk of its logit shard, one all-gather of [B, chunks] float4 partials
+        (B x 126 x 16 bytes per rank at V = 128K, TP 8; the logits are B x 64 KB), and the
+        argmax merge on every rank. Same tokens as the whole-vocabulary sampler at
+        temperature 0 (lowest index on ties). Reference: the sampler's greedy branch
+        (src/sampler.rs:83-120) over logits gathered to one device."""
+        W, r, nch = self.tp_size, self.tp.rank, self.vnch
+        v_off = r * self.V_l
+        valid = max(0, min(self.V_l, self.V - v_off))
+        part = self.vpart[:B * nch * 4]
+        ops.sample_partial(self.logits[:B], part, v_off=v_off, V_total=self.V, counts=self.counts,
+                           count_row=si.count_row, mask=si.mask, penalty=si.penalty, B=B, V=valid, nch=nch)
+        allp = self.vpart_all[:W * B * nch * 4]
+        self.tp.all_gather_flat(part, allp)
+        ops.sample_greedy_merge(allp, si.tokens, W=W, B=B, nch=nch, out_prob=si.probs, step=self.step_ctr)
+        ops.count_tokens(self.counts, si.tokens, n=B, count_row=si.count_row)
+        si.ids.copy_(si.tokens)
+
+    def decode(self, B: int, use_graph: bool = True, greedy: bool = False):
+        """Runs one decode step for the first B rows of the bucket-B inputs. ``greedy``: every
+        row samples at temperature 0 (lets a TP step merge per-rank argmax partials instead
+        of gathering the logits)."""
         self.step_inputs(B)
+        self.head_greedy = bool(greedy) and self.vocab_greedy
         if not use_graph or self.streamer is not None or self.expert_cache is not None:
             self._decode_body(B)
             return self.inputs[B]
-        g = self.graphs.get(B)
+        key = (B, self.head_greedy)
+        g = self.graphs.get(key)
         if g is None:
             # The warm-up run (lazy init outside capture) mutates step state: sampled ids,
             # penalty counts, the Philox step counter. Snapshot and restore it so the first
@@ -498,14 +536,14 @@ class ModelRunner:
             m0 = COMM.snapshot()
             with torch.cuda.graph(g):
                 self._decode_body(B)
-            self.graph_launches[B] = ops.launch_count() - c0
+            self.graph_launches[key] = ops.launch_count() - c0
             ops.count_launch(-(ops.launch_count() - c0))  # capture itself runs nothing
-            self.graph_comm[B] = COMM.since(m0)
-            COMM.add(self.graph_comm[B], sign=-1)
-            self.graphs[B] = g
+            self.graph_comm[key] = COMM.since(m0)
+            COMM.add(self.graph_comm[key], sign=-1)
+            self.graphs[key] = g
         g.replay()
-        ops.count_launch(self.graph_launches[B])
-        COMM.add(self.graph_comm[B])
+        ops.count_launch(self.graph_launches[key])
+        COMM.add(self.graph_comm[key])
         return self.inputs[B]
 
     # ------------------------------------------------------------------ prefill

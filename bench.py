@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--ttft-runs", type=int, default=5)
     ap.add_argument("--b1-steps", type=int, default=64, help="timed batch-1 decode steps (0 = skip)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"],
+                    help="paged KV pool precision (bf16 default; fp8 = E4M3 rows + per-row scale)")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="TP all-reduce: fused peer-memory push/reduce, or NCCL (baseline arm)")
     return ap.parse_args()
@@ -169,7 +171,8 @@ def main():
     max_len = P + 1 + W + max(K, args.b1_steps) + 8 + (K + 8 if not args.no_e2e else 0)
     qt = GGMLType[args.quant]
     t0 = time.time()
-    eng = random_engine(args.model, qt, seed=0, device=dev, max_batch=B, max_model_len=max_len + 64, tp=tp)
+    eng = random_engine(args.model, qt, seed=0, device=dev, max_batch=B, max_model_len=max_len + 64, tp=tp,
+                        kv_dtype=args.kv_dtype)
     rn = eng.runner
     torch.cuda.synchronize()
     build_s = time.time() - t0
@@ -312,6 +315,7 @@ def main():
             "data": "synthetic: uniform-random 512-token prompts; random-init N(0,0.02) weights quantised to Q4_K on device",
             "config": {"model": f"{args.model} ({args.quant})", "global_batch": B, "seq_len": P,
                        "decode_tokens_timed": K, "parallelism": f"tp{world}", "kv_block": rn.block_size,
+                       "kv_dtype": args.kv_dtype,
                        "l2": "inputs larger than L2 (4.6 GB weights + KV per step); no flush",
                        "gemm": "baseline" if args.impl == "baseline" else "ours",
                        "tp_allreduce": ("none" if world == 1 else

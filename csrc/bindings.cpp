@@ -220,6 +220,36 @@ void sampler(Tensor logits, int64_t B, int64_t V, optional<Tensor> counts, optio
   post_launch("sampler");
 }
 
+// partial pass over a vocabulary shard: columns [v_off, v_off + V) of a V_total vocabulary
+void sampler_partial(Tensor logits, int64_t B, int64_t V, int64_t nch, int64_t v_off, int64_t V_total,
+                     optional<Tensor> counts, optional<Tensor> count_row, optional<Tensor> mask,
+                     optional<Tensor> penalty, Tensor part) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(v_off % 32 == 0 && v_off + V <= V_total, "sampler_partial: shard [v_off, v_off+V) of V_total, v_off % 32 == 0");
+  TORCH_CHECK(nch >= air::sampler_chunks((int)V) && nch > 0, "sampler_partial: nch < sampler_chunks(V)");
+  TORCH_CHECK(part.dtype() == torch::kFloat32 && part.is_contiguous() && (size_t)part.numel() >= (size_t)B * nch * 4,
+              "sampler_partial: part must be float32 [B * nch * 4]");
+  air::SamplerArgs a{ptr<uint8_t>(counts), ptr<int>(count_row), ptr<uint32_t>(mask), nullptr,
+                     ptr<float>(penalty), nullptr, nullptr, 0ull, nullptr, nullptr, nullptr};
+  a.part = reinterpret_cast<float4*>(part.data_ptr<float>());
+  a.v_off = (int)v_off;
+  a.v_total = (int)V_total;
+  air::launch_sampler_partial(ptr<float>(logits), (int)B, (int)V, (int)nch, logits.stride(0), a, stream());
+  post_launch("sampler_partial");
+}
+
+void sampler_greedy_merge(Tensor part_all, int64_t W, int64_t B, int64_t nch, Tensor out_tokens,
+                          optional<Tensor> out_prob, optional<Tensor> step) {
+  check_cuda(part_all, "part_all");
+  TORCH_CHECK(part_all.dtype() == torch::kFloat32 && part_all.is_contiguous() &&
+                  (size_t)part_all.numel() >= (size_t)W * B * nch * 4,
+              "sampler_greedy_merge: part_all must be float32 [W, B, nch, 4]");
+  air::launch_sampler_greedy_merge(reinterpret_cast<const float4*>(part_all.data_ptr<float>()), (int)W, (int)B,
+                                   (int)nch, ptr<int>(out_tokens), ptr<float>(out_prob), ptr<long long>(step),
+                                   stream());
+  post_launch("sampler_greedy_merge");
+}
+
 void count_tokens(Tensor counts, Tensor tokens, int64_t n, int64_t per_row,
                   optional<Tensor> count_row) {
   air::launch_count_tokens(ptr<uint8_t>(counts), (int)counts.size(1), ptr<int>(tokens), (int)n,
@@ -355,6 +385,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_tiled_counters", [](int64_t N) { return (int64_t)air::gemv_tiled_counters((int)N); });
   m.def("paged_attention", &paged_attention);
   m.def("sampler", &sampler);
+  m.def("sampler_partial", &sampler_partial);
+  m.def("sampler_greedy_merge", &sampler_greedy_merge);
   m.def("sampler_chunks", [](int64_t V) { return (int64_t)air::sampler_chunks((int)V); });
   m.def("count_tokens", &count_tokens);
   m.def("embed", &embed);

@@ -50,9 +50,10 @@ struct RowView {
 
 AIR_DEVICE RowView row_view(const float* logits, int V, int64_t ld, const SamplerArgs& a, int row) {
   RowView r;
+  const int vt = a.v_total > 0 ? a.v_total : V;   // counts / mask row width
   r.lg = logits + (size_t)row * ld;
-  r.cnt = a.counts ? a.counts + (size_t)(a.count_row ? a.count_row[row] : row) * V : nullptr;
-  r.mask = a.allow_mask ? a.allow_mask + (size_t)row * ((V + 31) / 32) : nullptr;
+  r.cnt = a.counts ? a.counts + (size_t)(a.count_row ? a.count_row[row] : row) * vt + a.v_off : nullptr;
+  r.mask = a.allow_mask ? a.allow_mask + (size_t)row * ((vt + 31) / 32) + a.v_off / 32 : nullptr;
   r.pen = a.rep_penalty ? a.rep_penalty[row] : 1.f;
   return r;
 }
@@ -100,7 +101,30 @@ sampler_partial_kernel(const float* __restrict__ logits, int V, int64_t ld, Samp
     __syncthreads();
     z = block_sum(z, red);
   }
-  if (threadIdx.x == 0) a.part[(size_t)row * nch + chunk] = make_float4(best, __int_as_float(besti), z, 0.f);
+  if (threadIdx.x == 0)
+    a.part[(size_t)row * nch + chunk] =
+        make_float4(best, __int_as_float(besti == 0x7fffffff ? besti : besti + a.v_off), z, 0.f);
+}
+
+// one warp per row: argmax over the W x nch gathered partials (global indices)
+__global__ void sampler_greedy_merge_kernel(const float4* __restrict__ part, int W, int B, int nch,
+                                            int* __restrict__ out_tokens, float* __restrict__ out_prob) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= B) return;
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int j = lane; j < W * nch; j += 32) {
+    const int w = j / nch, c = j % nch;
+    const float4 p = part[((size_t)w * B + row) * nch + c];
+    argmax_merge(best, besti, p.x, __float_as_int(p.y));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_merge(best, besti, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, besti, o));
+  if (lane == 0) {
+    out_tokens[row] = besti == 0x7fffffff ? 0 : besti;
+    if (out_prob) out_prob[row] = 1.f;
+  }
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -320,6 +344,18 @@ void launch_sampler(const float* logits, int B, int V, int64_t ld, const Sampler
 }
 
 int sampler_chunks(int V) { return (V + kChunk - 1) / kChunk; }
+
+void launch_sampler_partial(const float* logits, int B, int V, int nch, int64_t ld, const SamplerArgs& a,
+                            cudaStream_t st) {
+  // nch >= chunks of V: the layout's chunk count (chunks past V write (-inf, INT_MAX))
+  sampler_partial_kernel<<<dim3(nch, B), kPartThreads, 0, st>>>(logits, V, ld, a, nch);
+}
+
+void launch_sampler_greedy_merge(const float4* part_all, int W, int B, int nch, int* out_tokens,
+                                 float* out_prob, long long* step, cudaStream_t st) {
+  sampler_greedy_merge_kernel<<<(B + 7) / 8, 256, 0, st>>>(part_all, W, B, nch, out_tokens, out_prob);
+  if (step) bump_step_kernel<<<1, 1, 0, st>>>(step);
+}
 
 void launch_count_tokens(uint8_t* counts, int V, const int* tokens, int n, int per_row,
                          const int* count_row, cudaStream_t st) {
