@@ -49,14 +49,27 @@ def main(out_path: str):
             prompts = [torch.randint(3, cfg.vocab_size, (int(l),), generator=g).tolist()
                        for l in torch.randint(5, 40, (B,), generator=g)]
             sp = SamplingParams(max_tokens=STEPS, temperature=0.0, repetition_penalty=1.0, ignore_eos=True)
-            for impl in ("nccl", "ours"):
-                tp = maybe_fused_tp(tp0, impl=impl, max_rows=B, hidden=cfg.hidden_dim, device=dev)
+            for impl in ("nccl", "ours", "ours_vg"):
+                # ours_vg: the vocabulary-parallel greedy head (per-rank argmax partials are
+                # gathered, not the logits): tokens only
+                os.environ["AIR_VOCAB_GREEDY"] = "1" if impl == "ours_vg" else "0"
+                tp = maybe_fused_tp(tp0, impl="nccl" if impl == "nccl" else "ours", max_rows=B,
+                                    hidden=cfg.hidden_dim, device=dev)
                 eng = random_engine(cfg, seed=3, device=dev, max_batch=B, max_model_len=256, tp=tp)
-                res[f"{name}_{impl}_B{B}"] = decode_with_logits(eng, prompts, sp)
+                if impl == "ours_vg":
+                    assert eng.runner.vocab_greedy
+                    rids = [eng.add_request(p, sp) for p in prompts]
+                    while eng.has_unfinished():
+                        eng.step()
+                    eng.runner.check_errors()
+                    res[f"{name}_{impl}_B{B}"] = [eng.finished[r].output_ids for r in rids]
+                else:
+                    res[f"{name}_{impl}_B{B}"] = decode_with_logits(eng, prompts, sp)
+                os.environ.pop("AIR_VOCAB_GREEDY", None)
                 torch.cuda.synchronize()
                 torch.distributed.barrier()
                 eng.runner.graphs.clear()
-                if impl == "ours":
+                if impl != "nccl":
                     tp.peer.close()
                 del eng
                 torch.cuda.empty_cache()
