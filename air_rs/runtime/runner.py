@@ -20,9 +20,12 @@ from ..models.config import ModelConfig
 from ..models.llama import LlamaWeights
 from ..utils import trace
 
-# decode batches up to this size run the int8-activation GEMV chain; larger ones the
-# tensor-core GEMM (AIR_GEMV_MAX_B overrides, e.g. to compare the two at one batch size)
-GEMV_MAX_B = max(1, min(8, int(os.environ.get("AIR_GEMV_MAX_B", "8"))))
+# The int8-activation GEMV chain serves decode batches up to GEMV_LIMIT_B (its buffers are
+# sized for that); by default only up to GEMV_MAX_B, above which the tensor-core GEMM step is
+# faster (Llama-3-8B Q4_K on B200: B=4 3.63 vs 4.30 ms per step, B=8 3.65 vs 7.88 ms).
+# AIR_GEMV_MAX_B overrides; ModelRunner.gemv_max_b per runner.
+GEMV_LIMIT_B = 8
+GEMV_MAX_B = max(1, min(GEMV_LIMIT_B, int(os.environ.get("AIR_GEMV_MAX_B", "2"))))
 
 
 def _dev_param(x, dtype, device):
@@ -118,7 +121,8 @@ class ModelRunner:
         self.q = torch.zeros(B, self.nh, self.hd, dtype=f32, device=dev)
         self.attn = torch.zeros(B, self.nh * self.hd, dtype=f32, device=dev)
         self.h = torch.zeros(B, self.Fp, dtype=f32, device=dev)
-        gb = min(B, GEMV_MAX_B)
+        gb = min(B, GEMV_LIMIT_B)
+        self.gemv_max_b = GEMV_MAX_B
         self.hq = torch.zeros(gb, self.Fp, dtype=i8, device=dev)          # SwiGLU output, Q8A
         self.hds = torch.zeros(gb, self.Fp // 32, 2, dtype=f32, device=dev)
         # fused-norm decode chain: attention output (Q8A) and per-32-row sums of squares
@@ -329,12 +333,12 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ decode
     def _decode_body(self, B: int):
-        if B <= GEMV_MAX_B and self.gemv_ok and self.fused_norm_ok():
+        if B <= self.gemv_max_b and self.gemv_ok and self.fused_norm_ok():
             return self._decode_fused(B)
         cfg, w, si = self.cfg, self.w, self.inputs[B]
         x, xq, xds = self.x[:B], self.xq[:B], self.xds[:B]
         ops.embed(w.embd, si.ids, out_f32=x, err=self.err, n=B)
-        gemv_path = B <= GEMV_MAX_B and self.gemv_ok
+        gemv_path = B <= self.gemv_max_b and self.gemv_ok
         ns = self.n_splits(B)
         tp = self.tp_size > 1
         peer = self._peer(B)

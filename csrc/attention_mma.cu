@@ -100,8 +100,16 @@ AIR_DEVICE bool visible(int t, const AttnRows& rows, int r, int ctx) {
   return true;
 }
 
+// merge buffer [warps][16][128] f32 (32 KB), aliased onto the tile ring after the key loop
+constexpr int kMergeBytes = kWarpsM * 16 * kD * 4;
+template <bool F8>
+__host__ __device__ constexpr int smem_total() {
+  return kWarpsM * warp_bytes<F8>() > kMergeBytes ? kWarpsM * warp_bytes<F8>() : kMergeBytes;
+}
+
+// three CTAs (12 warps) per SM: 64 KB (bf16) / 68 KB (F8) of shared memory each
 template <int G, bool F8>
-__global__ void __launch_bounds__(kWarpsM * 32)
+__global__ void __launch_bounds__(kWarpsM * 32, 3)
 paged_attn_mma_kernel(const float* __restrict__ q, const uint8_t* __restrict__ kv,
                       const int* __restrict__ block_tables, int max_blocks, AttnRows rows, int n_heads,
                       int n_kv, int block_size, int64_t num_blocks, int n_splits, int split_tokens,
@@ -111,7 +119,7 @@ paged_attn_mma_kernel(const float* __restrict__ q, const uint8_t* __restrict__ k
   extern __shared__ __align__(128) uint8_t smem[];
   // per warp: 2 stages x (K tile + V tile)
   __shared__ float red_m[kWarpsM][16], red_l[kWarpsM][16];
-  float* red_o = reinterpret_cast<float*>(smem + kWarpsM * warp_bytes<F8>());  // [warps][16][128]
+  float* red_o = reinterpret_cast<float*>(smem);  // [warps][16][128], over the tiles once the loop is done
 
   const int h = blockIdx.x, r = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -303,6 +311,7 @@ paged_attn_mma_kernel(const float* __restrict__ q, const uint8_t* __restrict__ k
     __syncwarp();
   }
   cp_wait<0>();
+  __syncthreads();     // every warp is done with its tiles before red_o overwrites them
 
   // ---- merge the 4 warps (head rows < G) ----
   const int hr = lane >> 2;
@@ -342,8 +351,8 @@ paged_attn_mma_kernel(const float* __restrict__ q, const uint8_t* __restrict__ k
 
 template <int G, bool F8>
 void launch_gf(const AttnArgs& a, cudaStream_t st) {
-  // bf16: 64 KB tiles + 32 KB merge; F8: 68 KB tiles + 32 KB merge
-  const int smem = kWarpsM * warp_bytes<F8>() + kWarpsM * 16 * kD * 4;
+  // bf16: 64 KB tiles; F8: 68 KB tiles (the merge buffer reuses them)
+  const int smem = smem_total<F8>();
   static unsigned long long attr_done = 0;
   set_max_smem_per_device(paged_attn_mma_kernel<G, F8>, smem, attr_done);
   dim3 grid(a.n_kv, a.n_rows, a.n_splits);

@@ -96,6 +96,7 @@ def test_fused_norm_decode_chain_matches_unfused(B):
     for fused in (True, False):
         rn = build_runner(cfg, iter(recs), device="cuda", max_batch=8, max_model_len=256, num_blocks=256)
         rn._fused_ok = fused
+        rn.gemv_max_b = 8                 # the GEMV chains at every batch size of the test
         assert rn.fused_norm_ok() == fused
         eng = Engine(cfg, rn, max_batch=8)
         outs[fused] = eng.generate_ids(prompts, SamplingParams(max_tokens=16, temperature=0.0, ignore_eos=True))

@@ -175,6 +175,7 @@ def test_engine_fp8_kv_matches_oracle():
     runner = build_runner(cfg, iter(recs), device="cuda", max_batch=16, max_model_len=512, num_blocks=256,
                           kv_dtype="fp8")
     assert runner.kv.dtype == torch.uint8 and runner.kv.shape[-1] == cfg.head_dim + 16
+    runner.gemv_max_b = 8                 # decode through the GEMV -> rope_kv path
     eng = Engine(cfg, runner, max_batch=16)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (32, 50, 7)]
@@ -182,3 +183,9 @@ def test_engine_fp8_kv_matches_oracle():
     for p, o in zip(prompts, outs):
         assert len(o) == 16
         _check_near_argmax(oracle, [cfg.bos_token_id] + p, o, tol=0.2)
+    runner.gemv_max_b = 1                 # and through the tensor-core GEMM step
+    runner.graphs.clear()
+    outs = eng.generate_ids(prompts, SamplingParams(max_tokens=16, temperature=0.0, ignore_eos=True))
+    for p, o in zip(prompts, outs):
+        _check_near_argmax(oracle, [cfg.bos_token_id] + p, o, tol=0.2)
+    runner.check_errors()

@@ -58,6 +58,7 @@ def test_moe_engine_matches_oracle(qt):
     recs = list(random_tensors(cfg, qt, seed=0, device="cpu"))
     oracle = OracleModel(cfg, {n: (r, q, s) for n, r, q, s in recs})
     runner = build_runner(cfg, iter(recs), device="cuda", max_batch=16, max_model_len=512, num_blocks=512)
+    runner.gemv_max_b = 8                 # 3 rows: the GEMV path; 12 rows: the GEMM path
     eng = Engine(cfg, runner, max_batch=16)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, cfg.vocab_size, (int(n),), generator=g).tolist() for n in (20, 33, 9)]

@@ -56,6 +56,7 @@ def main(out_path: str):
                 tp = maybe_fused_tp(tp0, impl="nccl" if impl == "nccl" else "ours", max_rows=B,
                                     hidden=cfg.hidden_dim, device=dev)
                 eng = random_engine(cfg, seed=3, device=dev, max_batch=B, max_model_len=256, tp=tp)
+                eng.runner.gemv_max_b = 8         # B=4: the GEMV chain; B=16: the GEMM step
                 if impl == "ours_vg":
                     assert eng.runner.vocab_greedy
                     rids = [eng.add_request(p, sp) for p in prompts]
@@ -75,6 +76,7 @@ def main(out_path: str):
                 torch.cuda.empty_cache()
             if tp0.rank == 0:     # the same model on one GPU (no TP / EP)
                 eng = random_engine(cfg, seed=3, device=dev, max_batch=B, max_model_len=256)
+                eng.runner.gemv_max_b = 8
                 res[f"{name}_single_B{B}"] = decode_with_logits(eng, prompts, sp)
                 del eng
                 torch.cuda.empty_cache()
