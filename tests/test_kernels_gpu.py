@@ -84,6 +84,39 @@ def test_rmsnorm_quant_matches():
     torch.testing.assert_close(xds[..., 1], s)
 
 
+@pytest.mark.parametrize("B,K", [(5, 4096), (37, 4096), (20, 2560), (16, 8192)])
+@pytest.mark.parametrize("mode", ["rms", "layer_bias", "bf16_in", "no_w"])
+def test_rmsnorm_quant_row_and_slice_kernels(B, K, mode):
+    """Both launch shapes (B < 16: row slices over several CTAs; B >= 16: one CTA per row held
+    in registers) against fp32 RMSNorm / LayerNorm (+ weight offset, bias) and the Q8A rule."""
+    g = torch.Generator().manual_seed(B + K)
+    x = torch.randn(B, K, generator=g) * 2 + (0.7 if mode == "layer_bias" else 0.0)
+    w = torch.rand(K, generator=g) + 0.5
+    bias = torch.randn(K, generator=g) * 0.1 if mode == "layer_bias" else None
+    xq = torch.empty(B, K, dtype=torch.int8, device=DEV)
+    xds = torch.empty(B, K // 32, 2, dtype=torch.float32, device=DEV)
+    y = torch.empty(B, K, dtype=torch.bfloat16, device=DEV)
+    kw = dict(y_bf16=y, bias=bias.to(DEV) if bias is not None else None, layer=mode == "layer_bias",
+              w_offset=1.0 if mode == "rms" else 0.0)
+    if mode == "bf16_in":
+        x = x.bfloat16().float()
+        ops.rmsnorm_quant(None, w.to(DEV), 1e-5, xq, xds, x_bf16=x.bfloat16().to(DEV), **kw)
+    else:
+        ops.rmsnorm_quant(x.to(DEV), None if mode == "no_w" else w.to(DEV), 1e-5, xq, xds, **kw)
+    if mode == "no_w":
+        ref = x
+    elif mode == "layer_bias":
+        c = x - x.mean(-1, keepdim=True)
+        ref = c / torch.sqrt((c * c).mean(-1, keepdim=True) + 1e-5) * w + bias
+    else:
+        ref = x / torch.sqrt((x * x).mean(-1, keepdim=True) + 1e-5) * (w + kw["w_offset"])
+    torch.testing.assert_close(y.float().cpu(), ref, rtol=1e-2, atol=1e-2)
+    deq = (xq.float().reshape(B, -1, 32) * xds[..., 0:1]).reshape(B, K).cpu()
+    torch.testing.assert_close(deq, _quant_act_ref(ref), rtol=0, atol=float(ref.abs().max()) / 120)
+    s = xq.float().reshape(B, -1, 32).sum(-1) * xds[..., 0]
+    torch.testing.assert_close(xds[..., 1], s)
+
+
 def test_gemv_residual_and_swiglu():
     B, H, F = 2, 512, 768
     wg, wgd = _qw(F, H, GGMLType.Q4_K, 3)
