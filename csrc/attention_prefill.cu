@@ -85,7 +85,7 @@ AIR_DEVICE uint32_t pk(float lo, float hi) {
 }
 
 template <int G, bool F8>
-__global__ void __launch_bounds__(G * 32)
+__global__ void __launch_bounds__(G * 32, G == 4 ? 3 : 1)
 prefill_attn_kernel(const float* __restrict__ q, const uint8_t* __restrict__ kv,
                     const int* __restrict__ block_tables, int max_blocks, AttnRows rows, int R, int n_heads,
                     int n_kv, int block_size, int64_t num_blocks, float scale, float* __restrict__ out,
