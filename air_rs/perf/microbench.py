@@ -106,16 +106,33 @@ def bench_gemv(name: str, B: int, iters: int, dev):
     return us, nbytes, 2.0 * N * K * B
 
 
-def bench_gemm(name: str, T: int, iters: int, dev):
+def _fp8_weights(N: int, K: int, dev, min_bytes: float = 4 * L2_BYTES):
+    """Random block-scaled FP8 weights (E4M3 codes + f32 multiplier per 128-wide block)."""
+    one = N * K + N * (K // 128) * 4
+    copies = max(1, int(min_bytes // one) + 1)
+    ws = []
+    for _ in range(copies):
+        codes = torch.randn(N, K, device=dev).to(torch.float8_e4m3fn).view(torch.uint8)
+        sc = torch.rand(N, K // 128, device=dev) * 0.01
+        ws.append(ops.QWeight(ops.FMT_FP8, codes, sc, N, K, GGMLType.FP8_E4M3_B128))
+    return ws, one
+
+
+def bench_gemm(name: str, T: int, iters: int, dev, wfmt: str = "q4k"):
+    """wfmt: q4k (dequant-fused GEMM), fp8 (FP8 codes dequantised to bf16 in the GEMM), fp8mma
+    (W8A8: activation quantisation + the kind::f8f6f4 kernel)."""
     from ..ops import gemm
     N, K = SHAPES[name]
-    ws, nbytes = _q4k_weights(N, K, dev)
+    ws, nbytes = _q4k_weights(N, K, dev) if wfmt == "q4k" else _fp8_weights(N, K, dev)
     x = torch.randn(T, K, device=dev).bfloat16()
     out = torch.zeros(T, N, device=dev, dtype=torch.bfloat16)
     i = [0]
 
     def f():
-        gemm.linear(x, ws[i[0] % len(ws)], out)
+        if wfmt == "fp8mma":
+            gemm.linear_fp8(x, ws[i[0] % len(ws)], out)
+        else:
+            gemm.linear(x, ws[i[0] % len(ws)], out)
         i[0] += 1
     us = ev_time(f, iters)
     return us, nbytes + T * K * 2 + T * N * 2, 2.0 * N * K * T
@@ -255,6 +272,7 @@ def main(argv=None):
     ap.add_argument("--ctx", type=int, default=640)
     ap.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--wfmt", default="q4k", choices=["q4k", "fp8", "fp8mma"], help="GEMM weight format / path")
     ap.add_argument("--tp", type=int, default=1, help="shapes of one rank's shard under tensor parallelism")
     a = ap.parse_args(argv)
     dev = torch.device("cuda")
@@ -275,8 +293,8 @@ def main(argv=None):
     if a.op in ("all", "gemm"):
         for n in names:
             for T in ([a.batch] if a.batch else [16, 64, 512]):
-                us, nb, f = bench_gemm(n, T, a.iters, dev)
-                line("gemm", f"{n} N={SHAPES[n][0]} K={SHAPES[n][1]} T={T}", us, nb, f)
+                us, nb, f = bench_gemm(n, T, a.iters, dev, a.wfmt)
+                line("gemm", f"{a.wfmt} {n} N={SHAPES[n][0]} K={SHAPES[n][1]} T={T}", us, nb, f)
     if a.op in ("all", "attn"):
         for B in ([a.batch] if a.batch else [1, 64]):
             us, nb, f = bench_attn(B, a.ctx, a.iters, dev, a.tp, a.kv_dtype)

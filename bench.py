@@ -312,7 +312,7 @@ def main():
             "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": round(tok_s / BASELINE_TOK_S, 2) if B == 1 else None, "dtype": "bf16",
-            "data": "synthetic: uniform-random 512-token prompts; random-init N(0,0.02) weights quantised to Q4_K on device",
+            "data": f"synthetic: uniform-random {P}-token prompts; random-init N(0,0.02) weights quantised to {args.quant} on device",
             "config": {"model": f"{args.model} ({args.quant})", "global_batch": B, "seq_len": P,
                        "decode_tokens_timed": K, "parallelism": f"tp{world}", "kv_block": rn.block_size,
                        "kv_dtype": args.kv_dtype,

@@ -117,6 +117,17 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f8f6f4 (8-bit floats in, f32 accumulate);
+// K per instruction is 32 (32 bytes of each operand row).
+__device__ __forceinline__ void mma_f8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // 32 lanes x 16 columns of 32-bit stores: thread i of the warp writes lane (base_lane + i).
 // Asynchronous: tmem_wait_st() before the data is handed to the MMA.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -163,6 +174,13 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4)                       // D format f32
        | (1u << 7)                       // A format bf16
        | (1u << 10)                      // B format bf16
+       | ((uint32_t)(N >> 3) << 17)      // N / 8
+       | ((uint32_t)(M >> 4) << 24);     // M / 16
+}
+
+// Instruction descriptor: kind::f8f6f4, A = B = E4M3 (format code 0), D = f32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4)                       // D format f32
        | ((uint32_t)(N >> 3) << 17)      // N / 8
        | ((uint32_t)(M >> 4) << 24);     // M / 16
 }

@@ -49,6 +49,12 @@ def test_engine_gemv_path_matches_oracle(qt):
     _check_near_argmax(oracle, [cfg.bos_token_id] + prompt, out)
 
 
+def test_engine_fp8_dequant_path_matches_oracle(monkeypatch):
+    """FP8 weights with bf16 activations (AIR_FP8_MMA=0: weights dequantised inside the GEMM)."""
+    monkeypatch.setenv("AIR_FP8_MMA", "0")
+    test_engine_gemv_path_matches_oracle(GGMLType.FP8_E4M3_B128)
+
+
 def test_engine_batched_gemm_path_and_pipelining():
     cfg, oracle, runner = _models(GGMLType.Q4_K, max_batch=16)
     eng = Engine(cfg, runner, max_batch=16)

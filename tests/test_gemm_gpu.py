@@ -24,7 +24,8 @@ def _w(N, K, qt, seed):
                                           (200, 512, 33, None), (1456, 256, 33, 1),
                                           (1024, 2048, 512, None), (384, 1024, 300, 3),
                                           (256, 512, 129, 1)])     # 256-token tiles
-def test_gemm_q_store(qt, N, K, T, splits):
+def test_gemm_q_store(qt, N, K, T, splits, monkeypatch):
+    monkeypatch.setenv("AIR_FP8_MMA", "0")   # FP8: the dequantising path (W8A8 has its own tests)
     w, wd = _w(N, K, qt, 1)
     assert gemm.tc_supported(w)          # the tcgen05 kernel, not the library fallback
     g = torch.Generator().manual_seed(2)
