@@ -193,8 +193,12 @@ class FusedTP(TPGroup):
 
 
 def maybe_fused_tp(tp, impl: str = "ours", max_rows: int = 64, hidden: int | None = None, device=None):
-    """Wrap an NCCL TPGroup with the peer-memory all-reduce (impl "ours"); "nccl" keeps NCCL."""
+    """Wrap an NCCL TPGroup with the peer-memory all-reduce (impl "ours") or the NVLink SHARP
+    multicast all-reduce (impl "nvls", ``air_rs.parallel.nvls``); "nccl" keeps NCCL."""
     if tp is None or impl == "nccl" or hidden is None:
         return tp
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if impl == "nvls":
+        from .nvls import NvlsComm
+        return FusedTP(tp, NvlsComm.create(tp, max_rows, hidden, dev))
     return FusedTP(tp, PeerComm.create(tp, max_rows, hidden, dev))

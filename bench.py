@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"],
                     help="paged KV pool precision (bf16 default; fp8 = E4M3 rows + per-row scale)")
-    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl", "nvls"],
                     help="TP all-reduce: fused peer-memory push/reduce, or NCCL (baseline arm)")
     return ap.parse_args()
 
@@ -164,7 +164,8 @@ def main():
         from air_rs.parallel.symm import maybe_fused_tp
         from air_rs.models.config import PRESETS
         ar_nccl = args.impl == "baseline" or args.allreduce == "nccl"
-        tp = maybe_fused_tp(tp, impl="nccl" if ar_nccl else "ours", max_rows=args.batch,
+        tp = maybe_fused_tp(tp, impl="nccl" if ar_nccl else ("nvls" if args.allreduce == "nvls" else "ours"),
+                            max_rows=args.batch,
                             hidden=PRESETS[args.model]().hidden_dim, device=dev)
 
     B, P, K, W = args.batch, args.prompt_len, args.steps, args.warmup
@@ -320,7 +321,8 @@ def main():
                        "gemm": "baseline" if args.impl == "baseline" else "ours",
                        "tp_allreduce": ("none" if world == 1 else
                                         "nccl" if (args.impl == "baseline" or args.allreduce == "nccl")
-                                        else "fused peer-memory push/reduce")},
+                                        else "NVLS multimem.ld_reduce (fused with the norm)"
+                                        if args.allreduce == "nvls" else "fused peer-memory push/reduce")},
             "p50_ttft_ms": round(ttft_ms, 3),
             "batch1": b1,
             "clocks": clk.summary(),

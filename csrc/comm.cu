@@ -27,13 +27,29 @@ __device__ __forceinline__ float wait_tagged(const uint2* p, uint32_t tag, int64
   }
 }
 
+// NVLink SHARP loads: the sum over every rank of the fp32 value(s) at multicast address p.
+__device__ __forceinline__ float mm_ld_reduce(const float* p) {
+  float v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 mm_ld_reduce4(const float* p) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p) : "memory");
+  return v;
+}
+constexpr int kNvlsRowMax = 8192;   // rows up to this width are loaded 16 bytes at a time
+
 // Grid (1, B, n_local): one CTA per (row, rank), so the reduced row can be held in registers
 // between the sum-of-squares pass and the quantisation pass. In two-shot mode a CTA first
 // reduces its rank's columns of the row and all-gathers them, then waits for the rest of
 // the row from the other owners; every CTA of every rank is resident at once (B * n_local
 // <= 2 * 148 is checked by the host), so these cross-CTA waits always make progress.
-template <bool TWO>
+// MODE 0: one-shot, 1: two-shot, 2: NVLS (multimem.ld_reduce over the symmetric buffer).
+template <int MODE>
 __global__ void __launch_bounds__(kThreads) tp_reduce_norm_kernel(const __grid_constant__ TPReduceArgs a) {
+  constexpr bool TWO = MODE == 1;
   pdl_trigger();   // a dependent GEMV may start streaming its weights now
   __shared__ float red[32];
   const TPReduceRank& R = a.r[blockIdx.z];
@@ -68,6 +84,52 @@ __global__ void __launch_bounds__(kThreads) tp_reduce_norm_kernel(const __grid_c
       v[j] = 0.f;
       if (i < K) {
         const float s = wait_tagged(ag + i, tag, a.timeout_ns, timed_out);
+        xr[i] = s;
+        v[j] = s;
+        ss += s * s;
+      }
+    }
+  } else if (MODE == 2) {
+    // ---- NVLS: row b's arrival flag to every rank, wait for all, then one switch-reduced
+    // load per element (the producers' stores completed with their kernels) ----
+    __shared__ int late;
+    if (t == 0) late = 0;
+    __syncthreads();
+    if (t < a.world) {
+      __threadfence_system();
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        if (r == t) st_release_sys(R.flags_peer[r] + (int64_t)b * a.world + R.rank, (int)tag);
+      const int* f = R.flags + (int64_t)b * a.world + t;
+      if ((int)(ld_acquire_sys(f) - (int)tag) < 0) {
+        const uint64_t t0 = sm100::global_ns();
+        for (uint32_t it = 1;; ++it) {
+          if ((int)(ld_acquire_sys(f) - (int)tag) >= 0) break;
+          if ((it & 31) == 0 && sm100::global_ns() - t0 > (uint64_t)a.timeout_ns) {
+            timed_out = true;
+            atomicExch(&late, 1);
+            break;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    const float* mrow = R.mc + (int64_t)b * K;
+    // 16-byte switch loads into shared memory (4x fewer NVLS requests than scalar ones), then
+    // the strided register layout the norm and the Q8A epilogue use
+    __shared__ float4 srow[MODE == 2 ? kNvlsRowMax / 4 : 1];
+    const bool vec = K <= kNvlsRowMax && !late;
+    if (vec) {
+      for (int i4 = t; i4 < K / 4; i4 += kThreads) srow[i4] = mm_ld_reduce4(mrow + 4 * i4);
+      __syncthreads();
+    }
+    const float* srf = reinterpret_cast<const float*>(srow);
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+      const int i = j * kThreads + t;
+      v[j] = 0.f;
+      if (i < K) {
+        const float s = xr[i] + (late ? 0.f : (vec ? srf[i] : mm_ld_reduce(mrow + i)));
         xr[i] = s;
         v[j] = s;
         ss += s * s;
@@ -152,10 +214,12 @@ peer_push_kernel(PeerPush p, const float* __restrict__ src, int B, int N, int64_
 
 void launch_tp_reduce_norm(const TPReduceArgs& a, cudaStream_t st) {
   const dim3 grid(1, a.B, a.n_local);
-  if (a.shard > 0)
-    tp_reduce_norm_kernel<true><<<grid, kThreads, 0, st>>>(a);
+  if (a.nvls)
+    tp_reduce_norm_kernel<2><<<grid, kThreads, 0, st>>>(a);
+  else if (a.shard > 0)
+    tp_reduce_norm_kernel<1><<<grid, kThreads, 0, st>>>(a);
   else
-    tp_reduce_norm_kernel<false><<<grid, kThreads, 0, st>>>(a);
+    tp_reduce_norm_kernel<0><<<grid, kThreads, 0, st>>>(a);
 }
 
 void launch_peer_push(const PeerPush& p, const float* src, int B, int N, int64_t ld, cudaStream_t st) {

@@ -20,6 +20,11 @@
 //     waits for its whole row there and normalises. Two hops, 2 (world - 1) / world x the
 //     partial's bytes out of each rank: best for large batches at 4 and 8 GPUs.
 // No NCCL call, and every wait is on local memory.
+// A third path (TPReduceArgs::nvls) uses NVLink SHARP: each producer stores its fp32 partial
+// into its own slot of a multicast-bound symmetric buffer (plain local stores); the consumer
+// CTA of row b raises row b's arrival flag on every rank, waits for every rank's flag, and
+// reads the row with multimem.ld_reduce, so the NVSwitch returns the sum of all ranks' partials:
+// one load per element, no per-rank partial crosses NVLink more than once.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -41,6 +46,12 @@ struct TPReduceRank {
   float2* ds;                 //   and its (d, d * sum) per 32 [B, K / 32]
   void* y_bf16;               // optional bf16 output [B, K]
   int rank;
+  // NVLS mode: multicast address of this collective's partial region [rows][K] f32 (every
+  // rank's copy, reduced by the switch on load), and the row arrival flags [rows][world]
+  // of this rank (local) and of every rank (mapped here)
+  const float* mc;
+  int* flags;
+  int* flags_peer[kMaxPeers];
 };
 
 struct TPReduceArgs {
@@ -56,6 +67,7 @@ struct TPReduceArgs {
   int layer;                  // 1: LayerNorm (mean subtracted), 0: RMSNorm
   float eps;
   int B, K;
+  int nvls;                   // 1: partials in symmetric memory, summed by multimem.ld_reduce
 };
 
 // x[b, :] += sum over ranks of their partials; then y = x * rsqrt(mean(x^2) + eps) *

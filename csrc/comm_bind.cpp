@@ -135,6 +135,49 @@ void tp_reduce_norm(const std::vector<Tensor>& metas, const std::vector<Tensor>&
   ck(cudaGetLastError(), "tp_reduce_norm");
 }
 
+// NVLS consumer of one rank. meta (int64, CPU): multicast partial region, local flags,
+// flags of ranks 0..7 (mapped here), epoch, done, err, world, rank, timeout_ns, slot_elems.
+void tp_reduce_norm_nvls(const Tensor& meta, const Tensor& x, optional<Tensor> w, double w_offset, double eps,
+                         int64_t B, int64_t K, optional<Tensor> q, optional<Tensor> ds, optional<Tensor> y,
+                         optional<Tensor> bias, int64_t layer) {
+  TORCH_CHECK(meta.device().is_cpu() && meta.scalar_type() == torch::kLong && meta.numel() >= 17, "nvls meta");
+  const int64_t* m = meta.data_ptr<int64_t>();
+  TORCH_CHECK(K % 32 == 0 && K <= 16384 && B >= 1 && B * K <= m[16], "tp_reduce_norm_nvls: B x K must fit the slot");
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat && x.is_contiguous() && x.numel() >= B * K,
+              "x must be contiguous fp32 CUDA [B, K]");
+  TORCH_CHECK(m[0] != 0 && m[0] % 16 == 0, "tp_reduce_norm_nvls: multicast address");
+  auto p = [](const optional<Tensor>& t) { return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr; };
+  air::TPReduceArgs a{};
+  a.n_local = 1;
+  a.nvls = 1;
+  a.world = (int)m[13];
+  TORCH_CHECK(a.world >= 1 && a.world <= air::kMaxPeers && m[14] >= 0 && m[14] < a.world, "nvls meta: world/rank");
+  a.timeout_ns = m[15];
+  a.slot_elems = m[16];
+  air::TPReduceRank& r = a.r[0];
+  r.mc = reinterpret_cast<const float*>(m[0]);
+  r.flags = reinterpret_cast<int*>(m[1]);
+  for (int i = 0; i < air::kMaxPeers; ++i) r.flags_peer[i] = reinterpret_cast<int*>(m[2 + i]);
+  r.epoch = reinterpret_cast<int*>(m[10]);
+  r.done = reinterpret_cast<int*>(m[11]);
+  r.err = reinterpret_cast<int*>(m[12]);
+  r.rank = (int)m[14];
+  r.x = x.data_ptr<float>();
+  r.q = static_cast<int8_t*>(p(q));
+  r.ds = static_cast<float2*>(p(ds));
+  r.y_bf16 = p(y);
+  TORCH_CHECK((r.q == nullptr) == (r.ds == nullptr), "tp_reduce_norm_nvls: q and ds go together");
+  a.w = static_cast<const float*>(p(w));
+  a.w_offset = (float)w_offset;
+  a.bias = static_cast<const float*>(p(bias));
+  a.layer = (int)layer;
+  a.eps = (float)eps;
+  a.B = (int)B;
+  a.K = (int)K;
+  air::launch_tp_reduce_norm(a, at::cuda::getCurrentCUDAStream());
+  ck(cudaGetLastError(), "tp_reduce_norm_nvls");
+}
+
 }  // namespace
 
 // push meta: data[8], epoch, slot_elems, world, rank, row_len, shard
@@ -163,6 +206,7 @@ void register_comm(pybind11::module_& m) {
   m.def("enable_peer_access", &enable_peer_access);
   m.def("peer_buffer_bytes", [](int64_t w, int64_t s) { return air::peer_buffer_bytes((int)w, s); });
   m.def("tp_reduce_norm", &tp_reduce_norm);
+  m.def("tp_reduce_norm_nvls", &tp_reduce_norm_nvls);
   m.def("peer_push", [](const Tensor& meta, const Tensor& src, int64_t B, int64_t N, int64_t ld) {
     TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kFloat, "peer_push: fp32 CUDA source");
     const air::PeerPush p = peer_push_from_meta(meta);
