@@ -538,7 +538,13 @@ class ModelRunner:
             g = torch.cuda.CUDAGraph()
             c0 = ops.launch_count()
             m0 = COMM.snapshot()
-            with torch.cuda.graph(g):
+            # capture on a stream of this runner's device: torch.cuda.graph's default capture
+            # stream is created once per process on whichever device was current then, and
+            # entering it switches the current device, so a second GPU in the same process
+            # (an in-process prefill/decode pair) would record its kernels on the first GPU
+            if getattr(self, "_capture_stream", None) is None:
+                self._capture_stream = torch.cuda.Stream(self.device)
+            with torch.cuda.graph(g, stream=self._capture_stream):
                 self._decode_body(B)
             self.graph_launches[key] = ops.launch_count() - c0
             ops.count_launch(-(ops.launch_count() - c0))  # capture itself runs nothing

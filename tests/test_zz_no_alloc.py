@@ -31,31 +31,45 @@ def _lib():
     return fn, msg
 
 
-@pytest.mark.parametrize("N,K,B", [(4096, 4096, 1), (1000, 2048, 3), (6144, 4096, 8)])
-def test_noalloc_gemv_matches_library_path(N, K, B):
+def _check_on(dev, N, K, B):
     from air_rs import ops
     from air_rs.gguf import GGMLType, quantize
 
     fn, msg = _lib()
     g = torch.Generator().manual_seed(N + K + B)
-    w = ops.QWeight.from_raw(quantize(torch.randn(N, K, generator=g) * 0.02, GGMLType.Q4_K),
-                             GGMLType.Q4_K, N, K, "cuda")
-    x = torch.randn(B, K, generator=g).cuda()
-    xq = torch.empty(B, K, dtype=torch.int8, device="cuda")
-    xds = torch.empty(B, K // 32, 2, dtype=torch.float32, device="cuda")
-    ops.rmsnorm_quant(x, None, 0.0, xq, xds)
-    ref = torch.zeros(B, N, device="cuda")
-    ops.gemv(w, xq, xds, B, ops.EPI_STORE, out_f32=ref)
-    err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    stream = torch.cuda.current_stream().cuda_stream
-    for _ in range(2):
-        out = torch.full((B, N), float("nan"), device="cuda")
-        rc = fn(w.data.data_ptr(), N, K, B, xq.data_ptr(), xds.data_ptr(), out.data_ptr(), err.data_ptr(),
-                stream)
-        assert rc == 0, msg(rc).decode()
-        torch.cuda.synchronize()
-        assert int(err.item()) == 0
-        torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-5)
+    with torch.cuda.device(dev):
+        w = ops.QWeight.from_raw(quantize(torch.randn(N, K, generator=g) * 0.02, GGMLType.Q4_K),
+                                 GGMLType.Q4_K, N, K, dev)
+        x = torch.randn(B, K, generator=g).to(dev)
+        xq = torch.empty(B, K, dtype=torch.int8, device=dev)
+        xds = torch.empty(B, K // 32, 2, dtype=torch.float32, device=dev)
+        ops.rmsnorm_quant(x, None, 0.0, xq, xds)
+        ref = torch.zeros(B, N, device=dev)
+        ops.gemv(w, xq, xds, B, ops.EPI_STORE, out_f32=ref)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        for _ in range(2):
+            out = torch.full((B, N), float("nan"), device=dev)
+            rc = fn(w.data.data_ptr(), N, K, B, xq.data_ptr(), xds.data_ptr(), out.data_ptr(), err.data_ptr(),
+                    stream)
+            assert rc == 0, msg(rc).decode()
+            torch.cuda.synchronize(dev)
+            assert int(err.item()) == 0
+            torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("N,K,B", [(4096, 4096, 1), (1000, 2048, 3), (6144, 4096, 8)])
+def test_noalloc_gemv_matches_library_path(N, K, B):
+    _check_on("cuda:0", N, K, B)
+
+
+def test_noalloc_gemv_second_device():
+    """The scratch array and the kernels' shared-memory limit are set up per device: a call on
+    the second GPU of the process (after calls on the first) resolves its own copy."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _check_on("cuda:0", 6144, 4096, 8)
+    _check_on("cuda:1", 6144, 4096, 8)
 
 
 def test_noalloc_rejects_bad_shapes():
